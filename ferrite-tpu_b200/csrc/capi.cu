@@ -1,0 +1,175 @@
+// Library plumbing behind the C ABI: thread-local last-error string, version,
+// device status word, per-device SM count cache, host-side fault injection and
+// TMA descriptor encoding (through the driver entry point, so the library needs
+// no link-time dependency on libcuda).
+#include <cudaTypedefs.h>
+
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace ferrite {
+
+namespace {
+thread_local std::string t_last_error;
+std::mutex g_mu;
+int g_sm_count[64] = {0};
+PFN_cuTensorMapEncodeTiled_v12000 g_encode_tiled = nullptr;
+}  // namespace
+
+void set_error(const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+}
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return code;
+}
+
+int current_device() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return dev;
+}
+
+int num_sms(int device) {
+  if (device < 0 || device >= 64) return 148;
+  int v = __atomic_load_n(&g_sm_count[device], __ATOMIC_ACQUIRE);
+  if (v > 0) return v;
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) !=
+          cudaSuccess ||
+      n <= 0)
+    n = 148;
+  __atomic_store_n(&g_sm_count[device], n, __ATOMIC_RELEASE);
+  return n;
+}
+
+int injected_fault(const char* op) {
+  const char* env = std::getenv("FERRITE_FAULT_INJECT");
+  if (env == nullptr || *env == '\0') return 0;
+  std::string list(env);
+  if (list == "all")
+    return fail(FERRITE_INJECTED_FAULT, "%s: injected fault (FERRITE_FAULT_INJECT=all)", op);
+  size_t start = 0;
+  while (start <= list.size()) {
+    size_t end = list.find(',', start);
+    if (end == std::string::npos) end = list.size();
+    if (list.compare(start, end - start, op) == 0)
+      return fail(FERRITE_INJECTED_FAULT, "%s: injected fault (FERRITE_FAULT_INJECT)", op);
+    start = end + 1;
+  }
+  return 0;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess)
+    return fail(FERRITE_LAUNCH_FAILED, "%s: launch failed: %s", what,
+                cudaGetErrorString(e));
+  return FERRITE_OK;
+}
+
+static int load_encoder() {
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (g_encode_tiled) return FERRITE_OK;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn,
+                                          cudaEnableDefault, &q);
+  if (e != cudaSuccess || fn == nullptr || q != cudaDriverEntryPointSuccess)
+    return fail(FERRITE_LAUNCH_FAILED,
+                "cuTensorMapEncodeTiled unavailable from the driver");
+  g_encode_tiled = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return FERRITE_OK;
+}
+
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
+                 int elem_bytes, uint64_t inner, uint64_t outer,
+                 uint64_t row_stride_bytes, uint32_t box_inner,
+                 uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+  if (int rc = load_encoder()) return rc;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
+    return fail(FERRITE_BAD_ALIGNMENT, "TMA base %p is not 16-byte aligned", base);
+  if (row_stride_bytes % 16 != 0)
+    return fail(FERRITE_BAD_ALIGNMENT,
+                "TMA row stride %llu bytes is not a multiple of 16",
+                (unsigned long long)row_stride_bytes);
+  if ((box_inner * (uint32_t)elem_bytes) % 16 != 0)
+    return fail(FERRITE_BAD_ALIGNMENT, "TMA box inner extent not 16-byte multiple");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode_tiled(map, dtype, 2, const_cast<void*>(base), dims,
+                              strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(FERRITE_BAD_SHAPE,
+                "cuTensorMapEncodeTiled failed (%d): dims %llu x %llu stride %llu "
+                "box %u x %u",
+                (int)r, (unsigned long long)inner, (unsigned long long)outer,
+                (unsigned long long)row_stride_bytes, box_inner, box_outer);
+  return FERRITE_OK;
+}
+
+int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
+                 int elem_bytes, uint64_t d0, uint64_t d1, uint64_t d2,
+                 uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0,
+                 uint32_t box1, uint32_t box2, CUtensorMapSwizzle swizzle) {
+  if (int rc = load_encoder()) return rc;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
+    return fail(FERRITE_BAD_ALIGNMENT, "TMA base %p is not 16-byte aligned", base);
+  if (stride1_bytes % 16 != 0 || stride2_bytes % 16 != 0)
+    return fail(FERRITE_BAD_ALIGNMENT, "TMA strides must be multiples of 16 bytes");
+  if ((box0 * (uint32_t)elem_bytes) % 16 != 0)
+    return fail(FERRITE_BAD_ALIGNMENT, "TMA box inner extent not 16-byte multiple");
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+  cuuint32_t box[3] = {box0, box1, box2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode_tiled(map, dtype, 3, const_cast<void*>(base), dims,
+                              strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(FERRITE_BAD_SHAPE, "cuTensorMapEncodeTiled (3d) failed (%d)", (int)r);
+  return FERRITE_OK;
+}
+
+}  // namespace ferrite
+
+extern "C" {
+
+const char* ferrite_last_error(void) { return ferrite::t_last_error.c_str(); }
+
+const char* ferrite_version(void) { return "ferrite_b200 0.1.0 sm_100a"; }
+
+int ferrite_device_status(void* stream, int clear) {
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess)
+    return ferrite::fail(FERRITE_LAUNCH_FAILED, "stream sync failed: %s",
+                         cudaGetErrorString(e));
+  int v = 0;
+  for (int st : {ferrite::status_gemm(clear), ferrite::status_attention(clear)})
+    if (v == 0 && st != 0) v = st;
+  if (v != 0)
+    return ferrite::fail(v, "device reported status %d (a bounded wait expired)", v);
+  return FERRITE_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,350 @@
+// RMSNorm backward kernels (dh and the deterministic dw reduction) and their
+// C-ABI entry points.
+#include "rmsnorm_common.cuh"
+
+namespace ferrite {
+namespace norm {
+
+// ---------------------------------------------------------------------------
+// backward
+// ---------------------------------------------------------------------------
+
+template <typename T, typename TW, bool HAS_DH, int VPT, int TPR, int CTA>
+__global__ void __launch_bounds__(CTA)
+    rmsnorm_bwd_kernel(const T* __restrict__ h, const TW* __restrict__ w,
+                       const T* __restrict__ dy, const T* __restrict__ dh_direct,
+                       T* __restrict__ dh, float* __restrict__ partial,
+                       int64_t rows, int dim, float eps) {
+  constexpr int VE = Vec<T>::N;
+  constexpr int RPC = CTA / TPR;
+  __shared__ float red[CTA / 32 * 2 + 2];
+  const int t = threadIdx.x % TPR;
+  const int grp = threadIdx.x / TPR;
+  const int nvec = dim / VE;
+  const float inv_dim = 1.0f / (float)dim;
+
+  float dwp[VPT][VE];
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+#pragma unroll
+    for (int j = 0; j < VE; ++j) dwp[i][j] = 0.f;
+  }
+
+  const int64_t groups_total = (int64_t)gridDim.x * RPC;
+  // Every thread of the CTA runs the same number of iterations (the shared
+  // reduction needs all of them); rows past the end are masked.
+  const int64_t iters = (rows + groups_total - 1) / groups_total;
+  for (int64_t it = 0; it < iters; ++it) {
+    const int64_t row = it * groups_total + (int64_t)blockIdx.x * RPC + grp;
+    const bool active = row < rows;
+    const int64_t base = row * (int64_t)dim;
+    float hv[VPT][VE], gv[VPT][VE];
+    float s2[2] = {0.f, 0.f};  // sum h^2, sum dy*w*h
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int vi = i * TPR + t;
+      if (active && vi < nvec) {
+        const int64_t e = base + (int64_t)vi * VE;
+        Vec<T>::to_f(ld_stream_v4(h + e), hv[i]);
+        Vec<T>::to_f(ld_stream_v4(dy + e), gv[i]);
+        float wv[VE];
+        load_w<TW, VE>(w, (int64_t)vi * VE, wv);  // L1-resident
+#pragma unroll
+        for (int j = 0; j < VE; ++j) {
+          s2[0] = fmaf(hv[i][j], hv[i][j], s2[0]);
+          s2[1] = fmaf(gv[i][j] * wv[j], hv[i][j], s2[1]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < VE; ++j) hv[i][j] = gv[i][j] = 0.f;
+      }
+    }
+    if constexpr (TPR > 32) {
+      row_reduce<TPR, 2>(s2, red);
+    } else {
+      row_reduce<TPR, 2>(s2, nullptr);
+    }
+    const float inv = rsqrtf(s2[0] * inv_dim + eps);
+    // mean(g * xhat) = inv * mean(dy*w*h)
+    const float c = inv * s2[1] * inv_dim;
+    if (active) {
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int vi = i * TPR + t;
+        if (vi < nvec) {
+          const int64_t e = base + (int64_t)vi * VE;
+          float dd[VE];
+          if constexpr (HAS_DH) Vec<T>::to_f(ld_stream_v4(dh_direct + e), dd);
+          float wv[VE];
+          load_w<TW, VE>(w, (int64_t)vi * VE, wv);
+          float o[VE];
+#pragma unroll
+          for (int j = 0; j < VE; ++j) {
+            const float xhat = hv[i][j] * inv;
+            const float g = gv[i][j] * wv[j];
+            dwp[i][j] = fmaf(gv[i][j], xhat, dwp[i][j]);
+            float v = inv * (g - xhat * c);
+            if constexpr (HAS_DH) v += dd[j];
+            o[j] = v;
+          }
+          st_v4(dh + e, Vec<T>::from_f(o));
+        }
+      }
+    }
+  }
+
+  // Combine the RPC row groups of this CTA (fixed order), then write the CTA's
+  // partial dw row.
+  if constexpr (RPC > 1) {
+    extern __shared__ float dwsm[];  // [RPC][dim]
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int vi = i * TPR + t;
+      if (vi < nvec) {
+#pragma unroll
+        for (int j = 0; j < VE; ++j) dwsm[grp * dim + vi * VE + j] = dwp[i][j];
+      }
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < dim; e += CTA) {
+      float s = 0.f;
+      for (int g = 0; g < RPC; ++g) s += dwsm[g * dim + e];
+      partial[(int64_t)blockIdx.x * dim + e] = s;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int vi = i * TPR + t;
+      if (vi < nvec) {
+        float* p = partial + (int64_t)blockIdx.x * dim + (int64_t)vi * VE;
+#pragma unroll
+        for (int j = 0; j < VE; j += 4)
+          *reinterpret_cast<float4*>(p + j) =
+              make_float4(dwp[i][j], dwp[i][j + 1], dwp[i][j + 2], dwp[i][j + 3]);
+      }
+    }
+  }
+}
+
+template <typename T, typename TW, bool HAS_DH>
+__global__ void __launch_bounds__(256)
+    rmsnorm_bwd_scalar(const T* __restrict__ h, const TW* __restrict__ w,
+                       const T* __restrict__ dy, const T* __restrict__ dh_direct,
+                       T* __restrict__ dh, float* __restrict__ partial,
+                       int64_t rows, int dim, float eps) {
+  // Persistent grid; each warp walks rows, each lane owns columns lane+32k.
+  // partial layout: [gridDim.x * 8][dim] (one row per warp).
+  const int lane = threadIdx.x & 31;
+  const int wib = threadIdx.x >> 5;
+  const int64_t gw = (int64_t)blockIdx.x * 8 + wib;
+  const int64_t nw = (int64_t)gridDim.x * 8;
+  float* my = partial + gw * dim;
+  for (int j = lane; j < dim; j += 32) my[j] = 0.f;
+  const float inv_dim = 1.0f / (float)dim;
+  for (int64_t row = gw; row < rows; row += nw) {
+    const int64_t base = row * (int64_t)dim;
+    float a = 0.f, b = 0.f;
+    for (int j = lane; j < dim; j += 32) {
+      const float hv = DT<T>::to_f(h[base + j]);
+      const float g = DT<T>::to_f(dy[base + j]) * DT<TW>::to_f(w[j]);
+      a = fmaf(hv, hv, a);
+      b = fmaf(g, hv, b);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      a += __shfl_xor_sync(0xffffffffu, a, off);
+      b += __shfl_xor_sync(0xffffffffu, b, off);
+    }
+    const float inv = rsqrtf(a * inv_dim + eps);
+    const float c = inv * b * inv_dim;
+    for (int j = lane; j < dim; j += 32) {
+      const float hv = DT<T>::to_f(h[base + j]);
+      const float dyv = DT<T>::to_f(dy[base + j]);
+      const float xhat = hv * inv;
+      const float g = dyv * DT<TW>::to_f(w[j]);
+      float v = inv * (g - xhat * c);
+      if constexpr (HAS_DH) v += DT<T>::to_f(dh_direct[base + j]);
+      dh[base + j] = DT<T>::from_f(v);
+      my[j] = fmaf(dyv, xhat, my[j]);
+    }
+  }
+}
+
+// dw[e] = sum_p partial[p][e], fixed summation order.
+template <typename TW>
+__global__ void __launch_bounds__(256)
+    dw_reduce_kernel(const float* __restrict__ partial, TW* __restrict__ dw,
+                     int nparts, int dim) {
+  const int e = blockIdx.x * 256 + threadIdx.x;
+  if (e >= dim) return;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  int p = 0;
+  for (; p + 4 <= nparts; p += 4) {
+    s0 += partial[(int64_t)p * dim + e];
+    s1 += partial[(int64_t)(p + 1) * dim + e];
+    s2 += partial[(int64_t)(p + 2) * dim + e];
+    s3 += partial[(int64_t)(p + 3) * dim + e];
+  }
+  for (; p < nparts; ++p) s0 += partial[(int64_t)p * dim + e];
+  dw[e] = DT<TW>::from_f((s0 + s1) + (s2 + s3));
+}
+
+// Persistent grid of the backward kernel and the resulting partial count.
+struct BwdPlan {
+  Cfg c;
+  int grid;
+  int nparts;  // rows of the partial-sum workspace
+  int smem;    // dynamic shared memory bytes
+};
+
+// Backward CTA size: at least 512 threads so that one CTA keeps enough loads in
+// flight and the persistent grid (and with it the dw partial workspace) stays
+// small.
+constexpr int bwd_cta(int tpr) { return tpr >= 512 ? tpr : 512; }
+
+template <typename T, typename TW, bool HAS_DH, int VPT, int TPR>
+static void* bwd_kernel_ptr() {
+  return (void*)rmsnorm_bwd_kernel<T, TW, HAS_DH, VPT, TPR, bwd_cta(TPR)>;
+}
+
+template <typename T, typename TW, bool HAS_DH, int VPT>
+static void* bwd_ptr_tpr(int tpr) {
+#define BWD_CASE(N)                                                              \
+  case N:                                                                        \
+    if constexpr ((VPT == 1) || (VPT == 2 && N >= 64) || (VPT == 4 && N >= 256)) \
+      return bwd_kernel_ptr<T, TW, HAS_DH, VPT, N>();                            \
+    break;
+  switch (tpr) {
+    BWD_CASE(4) BWD_CASE(8) BWD_CASE(16) BWD_CASE(32) BWD_CASE(64) BWD_CASE(128)
+    BWD_CASE(256) BWD_CASE(512) BWD_CASE(1024)
+  }
+#undef BWD_CASE
+  return nullptr;
+}
+
+template <typename T, typename TW, bool HAS_DH>
+static void* bwd_ptr(const Cfg& c) {
+  switch (c.vpt) {
+    case 1: return bwd_ptr_tpr<T, TW, HAS_DH, 1>(c.tpr);
+    case 2: return bwd_ptr_tpr<T, TW, HAS_DH, 2>(c.tpr);
+    case 4: return bwd_ptr_tpr<T, TW, HAS_DH, 4>(c.tpr);
+  }
+  return nullptr;
+}
+
+template <typename T, typename TW, bool HAS_DH>
+static BwdPlan plan_bwd(int64_t rows, int64_t dim, const void* const* ptrs,
+                        int nptr, int device) {
+  BwdPlan p{};
+  p.c = pick(dim, sizeof(T), ptrs, nptr, true);
+  const int sms = num_sms(device);
+  if (p.c.vec) {
+    const int CTA = bwd_cta(p.c.tpr);
+    const int RPC = CTA / p.c.tpr;
+    p.smem = RPC > 1 ? RPC * (int)dim * 4 : 0;
+    void* k = bwd_ptr<T, TW, HAS_DH>(p.c);
+    int occ = 0;
+    if (k == nullptr || p.smem > 200 * 1024) {
+      p.c.vec = false;
+    } else {
+      if (p.smem > 48 * 1024)
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, p.smem);
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, CTA, p.smem) !=
+              cudaSuccess ||
+          occ < 1)
+        occ = 1;
+      occ = std::min(occ, env_int("FERRITE_RMSNORM_BWD_CTAS_PER_SM", occ));
+      occ = std::max(1, std::min(occ, 4));
+      const int64_t groups = (rows + RPC - 1) / RPC;
+      p.grid = (int)std::max<int64_t>(1, std::min<int64_t>(groups, (int64_t)sms * occ));
+      p.nparts = p.grid;
+    }
+  }
+  if (!p.c.vec) {
+    p.grid = (int)std::max<int64_t>(1, std::min<int64_t>((rows + 7) / 8, sms));
+    p.nparts = p.grid * 8;
+    p.smem = 0;
+  }
+  return p;
+}
+
+template <typename T, typename TW, bool HAS_DH>
+static int run_bwd(cudaStream_t s, const void* h, const void* w, const void* dy,
+                   const void* dhd, void* dh, void* dw, void* ws,
+                   size_t ws_bytes, int64_t rows, int64_t dim, float eps) {
+  const int dev = current_device();
+  const void* ptrs[5] = {h, dy, HAS_DH ? dhd : nullptr, dh, w};
+  BwdPlan p = plan_bwd<T, TW, HAS_DH>(rows, dim, ptrs, 5, dev);
+  const size_t need = (size_t)p.nparts * (size_t)dim * sizeof(float);
+  if (ws == nullptr || ws_bytes < need)
+    return fail(FERRITE_WORKSPACE_TOO_SMALL,
+                "rmsnorm_bwd: workspace %zu bytes < %zu needed", ws_bytes, need);
+  if ((reinterpret_cast<uintptr_t>(ws) & 15u) != 0)
+    return fail(FERRITE_BAD_ALIGNMENT, "rmsnorm_bwd: workspace not 16-byte aligned");
+  if (p.c.vec) {
+    void* k = bwd_ptr<T, TW, HAS_DH>(p.c);
+    const int CTA = bwd_cta(p.c.tpr);
+    int dimi = (int)dim;
+    const T* hp = (const T*)h;
+    const TW* wp = (const TW*)w;
+    const T* dyp = (const T*)dy;
+    const T* dhdp = (const T*)dhd;
+    T* dhp = (T*)dh;
+    float* part = (float*)ws;
+    void* args[] = {&hp, &wp, &dyp, &dhdp, &dhp, &part, &rows, &dimi, &eps};
+    cudaError_t e = cudaLaunchKernel(k, dim3(p.grid), dim3(CTA), args, p.smem, s);
+    if (e != cudaSuccess)
+      return fail(FERRITE_LAUNCH_FAILED, "rmsnorm_bwd: %s", cudaGetErrorString(e));
+  } else {
+    rmsnorm_bwd_scalar<T, TW, HAS_DH><<<p.grid, 256, 0, s>>>(
+        (const T*)h, (const TW*)w, (const T*)dy, (const T*)dhd, (T*)dh,
+        (float*)ws, rows, (int)dim, eps);
+  }
+  if (int rc = check_launch("rmsnorm_bwd")) return rc;
+  dw_reduce_kernel<TW><<<(unsigned)((dim + 255) / 256), 256, 0, s>>>(
+      (const float*)ws, (TW*)dw, p.nparts, (int)dim);
+  return check_launch("rmsnorm_dw_reduce");
+}
+
+}  // namespace norm
+}  // namespace ferrite
+
+using namespace ferrite;
+using namespace ferrite::norm;
+
+extern "C" {
+
+size_t ferrite_rmsnorm_bwd_workspace_size(int64_t rows, int64_t dim) {
+  if (dim <= 0) return 16;
+  return (size_t)max_parts(rows, current_device()) * (size_t)dim * sizeof(float);
+}
+
+int ferrite_rmsnorm_bwd(void* stream, const void* h, const void* w,
+                        const void* dy, const void* dh_direct, void* dh,
+                        void* dw, void* workspace, size_t workspace_bytes,
+                        int64_t rows, int64_t dim, float eps, int dtype,
+                        int w_dtype) {
+  if (int rc = check_common("rmsnorm_bwd", rows, dim, dtype, w_dtype)) return rc;
+  if (!h || !w || !dy || !dh || !dw)
+    return fail(FERRITE_BAD_SHAPE, "rmsnorm_bwd: null pointer");
+  cudaStream_t s = (cudaStream_t)stream;
+  if (rows == 0) {
+    cudaError_t e = cudaMemsetAsync(dw, 0, dim * (w_dtype == FERRITE_F32 ? 4 : 2), s);
+    return e == cudaSuccess ? FERRITE_OK
+                            : fail(FERRITE_LAUNCH_FAILED, "rmsnorm_bwd: memset");
+  }
+  const bool has = dh_direct != nullptr;
+#define CALL(T, TW)                                                                  \
+  (has ? run_bwd<T, TW, true>(s, h, w, dy, dh_direct, dh, dw, workspace,             \
+                              workspace_bytes, rows, dim, eps)                       \
+       : run_bwd<T, TW, false>(s, h, w, dy, dh_direct, dh, dw, workspace,            \
+                               workspace_bytes, rows, dim, eps))
+  if (dtype == FERRITE_BF16 && w_dtype == FERRITE_F32) return CALL(__nv_bfloat16, float);
+  if (dtype == FERRITE_BF16 && w_dtype == FERRITE_BF16) return CALL(__nv_bfloat16, __nv_bfloat16);
+  if (dtype == FERRITE_F32 && w_dtype == FERRITE_F32) return CALL(float, float);
+  if (dtype == FERRITE_F16 && w_dtype == FERRITE_F32) return CALL(__half, float);
+#undef CALL
+  return fail(FERRITE_UNSUPPORTED_DTYPE, "rmsnorm_bwd: dtype");
+}
+
+}  // extern "C"

@@ -1,0 +1,197 @@
+"""Causal flash attention (forward, dK/dV, dQ) on B200, with a custom backward.
+
+Drop-in for the reference's ``ferrite.kernels.flash_attention``
+(src/ferrite/kernels/flash_attention.py): same public names (``BlockSizes``
+:49-62, ``flash_attention`` :356-367, ``flash_attention_reference`` :370-380,
+``attention_flops`` :383-390, ``MASK_VALUE`` :44), same validation
+(``_validate`` :336-353, raising ``ValueError``), same numerics contract:
+
+* scores ``s = scale * q k^T`` in f32, causal mask with the finite
+  ``MASK_VALUE``, online softmax with f32 row statistics, output normalised once
+  after the last key block, ``lse = m + log(l)`` kept for the backward;
+* ``P`` is rounded to the input dtype before ``P @ V`` (:114), ``P`` and ``dS``
+  before the backward products (:210-211, :234), and the scale is applied to
+  dK / dQ at the end (:220, :243);
+* backward = FlashAttention-2 recompute from ``lse`` and
+  ``delta = rowsum(dO * O)`` (:326-330) in two kernels without atomics: dK/dV with
+  one CTA per key tile sweeping query tiles, dQ with one CTA per query tile
+  sweeping key tiles.
+
+The reference's ``jax.custom_vjp`` (:315-333) becomes a ``torch.autograd.Function``
+whose residuals are ``(q, k, v, out, lse)``; ``lse`` and ``delta`` are compact f32
+``[b, h, s]`` tensors instead of the reference's lane-replicated ``[b, h, s, 128]``
+(that layout is internal to the residuals, so callers see no difference).
+Block sizes are validated exactly as in the reference; the kernels tile
+internally (128 x 128 on the tensor cores).
+"""
+
+from __future__ import annotations
+
+import dataclasses
+import math
+
+import numpy as np
+import torch
+
+from ferrite import _native as nat
+from ferrite import platform
+
+NUM_LANES = platform.LANES
+# Large negative finite value instead of -inf so masked rows never produce inf - inf.
+MASK_VALUE = -0.7 * float(np.finfo(np.float32).max)
+
+
+@dataclasses.dataclass(frozen=True)
+class BlockSizes:
+    """Tile sizes. ``block_q`` is a multiple of 8, ``block_k`` a multiple of 128."""
+
+    block_q: int = 128
+    block_k: int = 128
+    block_q_bwd: int = 128
+    block_k_bwd: int = 128
+
+    @classmethod
+    def for_device(cls) -> "BlockSizes":
+        t = platform.default_tile()
+        return cls(t, t, t, t)
+
+
+def _on_or_below_diag(qi: int, bq: int, ki: int, bk: int) -> bool:
+    """True when block (qi, ki) has at least one unmasked (col <= row) entry (:65-67)."""
+    return (qi + 1) * bq - 1 >= ki * bk
+
+
+def _validate(q, k, v, causal, bs: BlockSizes):
+    if not (q.ndim == 4 and k.shape == v.shape and q.shape[:2] == k.shape[:2] and q.shape[3] == k.shape[3]):
+        raise ValueError(f"expected q,k,v as [b,h,s,d] with matching b,h,d; got {tuple(q.shape)} {tuple(k.shape)} {tuple(v.shape)}")
+    if q.dtype != k.dtype or q.dtype != v.dtype:
+        raise ValueError("q, k, v must share a dtype")
+    d = q.shape[3]
+    if d % NUM_LANES and d > NUM_LANES:
+        raise ValueError(f"head_dim must be <= {NUM_LANES} or a multiple of it; got {d}")
+    if causal and q.shape[2] != k.shape[2]:
+        raise ValueError("causal attention needs equal q and k sequence lengths")
+    for name, blk, dim, mult in [
+        ("block_q", bs.block_q, q.shape[2], platform.SUBLANES),
+        ("block_k", bs.block_k, k.shape[2], NUM_LANES),
+        ("block_q_bwd", bs.block_q_bwd, q.shape[2], platform.SUBLANES),
+        ("block_k_bwd", bs.block_k_bwd, k.shape[2], NUM_LANES),
+    ]:
+        if blk % mult or dim % blk:
+            raise ValueError(f"{name}={blk} must be a multiple of {mult} and divide the sequence length {dim}")
+
+
+def _forward(q, k, v, causal: bool, scale: float, bs: BlockSizes):
+    nat.require_cuda(q, k, v)
+    b, h, sq, d = q.shape
+    sk = k.shape[2]
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    out = torch.empty_like(q)
+    lse = torch.empty((b, h, sq), dtype=torch.float32, device=q.device)
+    nat.check(
+        nat.lib().ferrite_attn_fwd(
+            nat.stream_ptr(q.device), q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), lse.data_ptr(),
+            b, h, sq, sk, d, scale, int(causal), bs.block_q, bs.block_k, nat.dtype_code(q.dtype),
+        )
+    )
+    return out, lse
+
+
+def _backward(q, k, v, out, lse, do, causal: bool, scale: float, bs: BlockSizes):
+    nat.require_cuda(q, k, v, out, lse, do)
+    b, h, sq, d = q.shape
+    sk = k.shape[2]
+    do = do.to(q.dtype).contiguous()
+    lib = nat.lib()
+    s = nat.stream_ptr(q.device)
+    code = nat.dtype_code(q.dtype)
+    delta = torch.empty((b, h, sq), dtype=torch.float32, device=q.device)
+    nat.check(lib.ferrite_attn_bwd_prep(s, do.data_ptr(), out.data_ptr(), delta.data_ptr(), b, h, sq, d, code))
+    dq = torch.empty_like(q)
+    dk = torch.empty_like(k)
+    dv = torch.empty_like(v)
+    nat.check(
+        lib.ferrite_attn_bwd_dkv(
+            s, q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), lse.data_ptr(), delta.data_ptr(),
+            dk.data_ptr(), dv.data_ptr(), b, h, sq, sk, d, scale, int(causal), bs.block_q_bwd, bs.block_k_bwd, code,
+        )
+    )
+    nat.check(
+        lib.ferrite_attn_bwd_dq(
+            s, q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), lse.data_ptr(), delta.data_ptr(),
+            dq.data_ptr(), b, h, sq, sk, d, scale, int(causal), bs.block_q_bwd, bs.block_k_bwd, code,
+        )
+    )
+    return dq, dk, dv
+
+
+class _Flash(torch.autograd.Function):
+    """custom_vjp of ``_flash`` (flash_attention.py:315-333)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, causal, scale, bs):
+        out, lse = _forward(q, k, v, causal, scale, bs)
+        ctx.save_for_backward(q, k, v, out, lse)
+        ctx.causal, ctx.scale, ctx.bs = causal, scale, bs
+        return out
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, out, lse = ctx.saved_tensors
+        dq, dk, dv = _backward(q, k, v, out, lse, do, ctx.causal, ctx.scale, ctx.bs)
+        return dq, dk, dv, None, None, None
+
+
+def flash_attention(q, k, v, *, causal: bool = True, scale: float | None = None, block_sizes: BlockSizes | None = None):
+    """Memory-efficient attention ``softmax(q k^T * scale) v`` with exact numerics.
+
+    Differentiable through autograd (custom backward kernels).  Shapes
+    ``[batch, heads, seq, head_dim]``; sequence lengths must be multiples of the
+    block sizes (pad upstream if needed).
+    """
+    bs = block_sizes or BlockSizes()
+    _validate(q, k, v, causal, bs)
+    if scale is None:
+        scale = 1.0 / math.sqrt(q.shape[-1])
+    return _Flash.apply(q, k, v, bool(causal), float(scale), bs)
+
+
+def flash_forward_with_lse(q, k, v, *, causal: bool = True, scale: float | None = None, block_sizes: BlockSizes | None = None):
+    """Forward only, returning ``(out, lse)`` (lse f32 ``[b, h, s]``); no autograd."""
+    bs = block_sizes or BlockSizes()
+    _validate(q, k, v, causal, bs)
+    if scale is None:
+        scale = 1.0 / math.sqrt(q.shape[-1])
+    return _forward(q, k, v, bool(causal), float(scale), bs)
+
+
+def flash_backward(q, k, v, out, lse, do, *, causal: bool = True, scale: float | None = None, block_sizes: BlockSizes | None = None):
+    """Backward only: ``(dq, dk, dv)`` from the forward residuals and ``dO``."""
+    bs = block_sizes or BlockSizes()
+    _validate(q, k, v, causal, bs)
+    if scale is None:
+        scale = 1.0 / math.sqrt(q.shape[-1])
+    return _backward(q, k, v, out, lse, do, bool(causal), float(scale), bs)
+
+
+def flash_attention_reference(q, k, v, *, causal: bool = True, scale: float | None = None):
+    """Materialised-scores reference in f32, same contract as :func:`flash_attention` (:370-380)."""
+    if scale is None:
+        scale = 1.0 / math.sqrt(q.shape[-1])
+    s = torch.einsum("bhqd,bhkd->bhqk", q.float(), k.float()) * scale
+    if causal:
+        sq, sk = q.shape[2], k.shape[2]
+        mask = torch.tril(torch.ones((sq, sk), dtype=torch.bool, device=q.device), diagonal=sk - sq)
+        s = torch.where(mask, s, torch.tensor(MASK_VALUE, dtype=s.dtype, device=s.device))
+    p = torch.softmax(s, dim=-1)
+    return torch.einsum("bhqk,bhkd->bhqd", p, v.float()).to(q.dtype)
+
+
+def attention_flops(b: int, h: int, sq: int, sk: int, d: int, *, causal: bool, backward: bool = False) -> int:
+    """Tensor-core FLOPs for one forward (and optionally backward) pass, counting skipped blocks as free (:383-390)."""
+    frac = 0.5 if causal else 1.0
+    fwd = 4 * b * h * sq * sk * d * frac  # QK^T and PV, 2 flops per MAC
+    if not backward:
+        return int(fwd)
+    # backward recomputes S (1 matmul) and does dP, dV, dK, dQ (4 matmuls) = 5 matmuls vs 2 in forward
+    return int(fwd * 2.5)

@@ -1,0 +1,105 @@
+"""Matmul with an f32 accumulator on B200, with a custom backward.
+
+Drop-in for the reference's ``ferrite.kernels.matmul`` (src/ferrite/kernels/matmul.py):
+``matmul`` (:110-126), ``matmul_reference`` (:129-131), ``matmul_flops``
+(:134-135).  Same contract: any ``[M, K] @ [K, N]`` shape, f32 accumulation,
+``out_dtype`` defaulting to ``x.dtype``, ``ValueError`` for non-2-D operands or
+mismatched K (:53-54) and for block sizes that are not multiples of (8, 128, 128)
+(:46-47).  The VJP (:99-104) computes ``dX = G Y^T`` and ``dY = X^T G`` through
+the same native GEMM, but as transposed-operand calls (no materialised
+transposes; the reference transposes in XLA first).
+
+Ragged shapes need no padding copies (the reference pads to the block grid,
+:58-63): the TMA loads zero-fill out-of-range tiles and the epilogue masks the
+stores.  bf16/f16 operands run on tcgen05 tensor cores; f32 operands run the
+exact-f32 path, matching ``dot_precision`` (_compat.py:17-26).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from ferrite import _native as nat
+from ferrite import platform
+
+
+def _pick_blocks(m: int, n: int, k: int, bm, bn, bk):
+    """Validate caller block sizes like the reference (:41-49); the kernel tiles internally."""
+    for name, b, mult in (("bm", bm, platform.SUBLANES), ("bn", bn, platform.LANES), ("bk", bk, platform.LANES)):
+        if b is not None and b % mult:
+            raise ValueError(f"blocks must be multiples of ({platform.SUBLANES}, {platform.LANES}); got bm={bm} bn={bn} bk={bk}")
+    return bm, bn, bk
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, *, trans_a: bool = False, trans_b: bool = False, out_dtype=None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``op(a) @ op(b)`` through ``ferrite_gemm``; ``op`` transposes the stored 2-D tensor.
+
+    ``a`` is stored ``[M, K]`` (or ``[K, M]`` with ``trans_a``), ``b`` is stored
+    ``[K, N]`` (or ``[N, K]`` with ``trans_b``).  Row strides other than the
+    packed ones are honoured (``a.stride(0)``), the inner stride must be 1.
+    """
+    nat.require_cuda(a, b)
+    if a.dtype != b.dtype:
+        raise ValueError(f"operands must share a dtype, got {a.dtype} and {b.dtype}")
+    if a.stride(1) != 1:
+        a = a.contiguous()
+    if b.stride(1) != 1:
+        b = b.contiguous()
+    m, ka = (a.shape[1], a.shape[0]) if trans_a else (a.shape[0], a.shape[1])
+    kb, n = (b.shape[1], b.shape[0]) if trans_b else (b.shape[0], b.shape[1])
+    if ka != kb:
+        raise ValueError(f"inner dimensions differ: {ka} vs {kb}")
+    out_dtype = out_dtype or a.dtype
+    if out is None:
+        out = torch.empty((m, n), dtype=out_dtype, device=a.device)
+    nat.check(
+        nat.lib().ferrite_gemm(
+            nat.stream_ptr(a.device), a.data_ptr(), b.data_ptr(), out.data_ptr(), m, n, ka,
+            a.stride(0), b.stride(0), out.stride(0), int(trans_a), int(trans_b),
+            nat.dtype_code(a.dtype), nat.dtype_code(out.dtype),
+        )
+    )
+    return out
+
+
+class _Matmul(torch.autograd.Function):
+    """custom_vjp of ``_matmul_vjp`` (matmul.py:89-107)."""
+
+    @staticmethod
+    def forward(ctx, x, y, out_dtype):
+        ctx.save_for_backward(x, y)
+        return gemm(x, y, out_dtype=out_dtype)
+
+    @staticmethod
+    def backward(ctx, g):
+        x, y = ctx.saved_tensors
+        dx = dy = None
+        if ctx.needs_input_grad[0]:
+            dx = gemm(g.to(x.dtype), y, trans_b=True, out_dtype=x.dtype)  # G @ Y^T
+        if ctx.needs_input_grad[1]:
+            dy = gemm(x, g.to(y.dtype), trans_a=True, out_dtype=y.dtype)  # X^T @ G
+        return dx, dy, None
+
+
+def matmul(x: torch.Tensor, y: torch.Tensor, *, block_m: int | None = None, block_n: int | None = None, block_k: int | None = None, out_dtype=None) -> torch.Tensor:
+    """``x @ y`` for 2-D ``x: [M, K]`` and ``y: [K, N]`` on the B200 GEMM kernels.
+
+    Any shape is accepted (ragged edges are handled in-kernel); differentiable:
+    the backward runs the transposed products through the same kernel.
+    """
+    if x.ndim != 2 or y.ndim != 2 or x.shape[1] != y.shape[0]:
+        raise ValueError(f"expected [M,K] @ [K,N], got {tuple(x.shape)} @ {tuple(y.shape)}")
+    _pick_blocks(x.shape[0], y.shape[1], x.shape[1], block_m, block_n, block_k)
+    if x.dtype != y.dtype:
+        ct = torch.promote_types(x.dtype, y.dtype)
+        x, y = x.to(ct), y.to(ct)
+    return _Matmul.apply(x, y, out_dtype or x.dtype)
+
+
+def matmul_reference(x: torch.Tensor, y: torch.Tensor, *, out_dtype=None) -> torch.Tensor:
+    """Plain-torch baseline with the same numerics contract (f32 accumulation, :129-131)."""
+    return torch.matmul(x.float(), y.float()).to(out_dtype or x.dtype)
+
+
+def matmul_flops(m: int, n: int, k: int) -> int:
+    return 2 * m * n * k

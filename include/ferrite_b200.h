@@ -1,0 +1,159 @@
+/*
+ * ferrite_b200.h -- C ABI of the B200 (sm_100a) kernels behind ferrite's three
+ * hot-path operators: causal flash attention (forward, delta prep, dK/dV, dQ),
+ * fused residual-add + RMSNorm (forward and backward) and the blocked matmul.
+ *
+ * Conventions shared by every entry point
+ *   - All tensor arguments are DEVICE pointers, row-major, densely packed unless a
+ *     leading-dimension argument says otherwise.  Nothing is allocated, freed or
+ *     synchronised: work is enqueued on `stream` (a cudaStream_t passed as void*,
+ *     NULL = legacy default stream) and the call returns.
+ *   - Return value: FERRITE_OK (0) or one of the ferrite_status codes below.  On a
+ *     non-zero return nothing was launched and ferrite_last_error() describes why
+ *     (thread-local string).
+ *   - dtype codes: FERRITE_F32, FERRITE_BF16, FERRITE_F16 (storage types; all
+ *     statistics and accumulators are f32).
+ *   - Kernels that wait on an mbarrier bound every wait; a wait that runs out sets
+ *     a device-side status word that ferrite_device_status() reads back as
+ *     FERRITE_DEVICE_TIMEOUT.
+ *
+ * Each declaration names the reference interface it replaces (file:line inside
+ * anxnd2211/ferrite-tpu).  In the reference every one of these is a
+ * `pl.pallas_call` (or an XLA fusion) inside a `jax.custom_vjp`.
+ */
+#ifndef FERRITE_B200_H_
+#define FERRITE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(FERRITE_BUILD) && defined(__GNUC__)
+#define FERRITE_API __attribute__((visibility("default")))
+#else
+#define FERRITE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  FERRITE_OK = 0,
+  FERRITE_BAD_SHAPE = 1,         /* a size, stride or block argument is invalid   */
+  FERRITE_UNSUPPORTED_DTYPE = 2, /* dtype combination not implemented            */
+  FERRITE_LAUNCH_FAILED = 3,     /* cudaGetLastError() after the launch           */
+  FERRITE_DEVICE_TIMEOUT = 4,    /* a bounded device-side wait expired            */
+  FERRITE_BAD_ALIGNMENT = 5,     /* a pointer/stride breaks a TMA or vector rule  */
+  FERRITE_WORKSPACE_TOO_SMALL = 6,
+  FERRITE_INJECTED_FAULT = 7     /* host-side fault injection (FERRITE_FAULT_INJECT) */
+} ferrite_status;
+
+typedef enum { FERRITE_F32 = 0, FERRITE_BF16 = 1, FERRITE_F16 = 2 } ferrite_dtype;
+
+/* ---- library / error plumbing ------------------------------------------------ */
+
+/* Human-readable description of the last non-zero status on this host thread. */
+FERRITE_API const char* ferrite_last_error(void);
+/* Library version string, e.g. "ferrite_b200 0.1.0 sm_100a". */
+FERRITE_API const char* ferrite_version(void);
+/* Synchronises `stream`, then returns the device status word of the current device
+ * (FERRITE_OK or FERRITE_DEVICE_TIMEOUT) and, if `clear` != 0, resets it. */
+FERRITE_API int ferrite_device_status(void* stream, int clear);
+
+/* ---- fused residual-add + RMSNorm ------------------------------------------- */
+
+/* y = x * rsqrt(mean(x^2) + eps) * w over the last axis of x[rows, dim].
+ * x, y: dtype `dtype`; w: dtype `w_dtype` (f32 or bf16); statistics in f32.
+ * Replaces ferrite_rmsnorm: rmsnorm.py:46-49 (_rmsnorm_kernel) via _call
+ * rmsnorm.py:77-110 with n_out=1. */
+FERRITE_API int ferrite_rmsnorm_fwd(void* stream, const void* x, const void* w, void* y,
+                        int64_t rows, int64_t dim, float eps, int dtype,
+                        int w_dtype);
+
+/* h = x + r (f32, stored rounded to dtype); y = h * rsqrt(mean(h^2)+eps) * w,
+ * computed from the UNROUNDED f32 h.  Replaces ferrite_add_rmsnorm:
+ * rmsnorm.py:52-56 (_add_rmsnorm_kernel) via _call rmsnorm.py:77-110, n_out=2. */
+FERRITE_API int ferrite_add_rmsnorm_fwd(void* stream, const void* x, const void* r,
+                            const void* w, void* h, void* y, int64_t rows,
+                            int64_t dim, float eps, int dtype, int w_dtype);
+
+/* Bytes of scratch ferrite_rmsnorm_bwd needs for (rows, dim): per-CTA f32
+ * partial sums of dw, reduced deterministically by a second kernel. */
+FERRITE_API size_t ferrite_rmsnorm_bwd_workspace_size(int64_t rows, int64_t dim);
+
+/* RMSNorm backward from the saved (rounded) input h:
+ *   inv = rsqrt(mean(h^2)+eps), xhat = h*inv, g = dy*w,
+ *   dh  = inv * (g - xhat * mean(g*xhat)) [+ dh_direct],   dw = sum_rows dy*xhat.
+ * dh_direct may be NULL (plain rmsnorm).  dh has dtype `dtype`, dw has `w_dtype`.
+ * Replaces the XLA backward of the reference: rmsnorm.py:159-166
+ * (_rmsnorm_bwd_math), rmsnorm.py:148-153 (_add_norm_bwd: returns dh twice) and
+ * rmsnorm.py:128-131 (_norm_bwd). */
+FERRITE_API int ferrite_rmsnorm_bwd(void* stream, const void* h, const void* w,
+                        const void* dy, const void* dh_direct, void* dh,
+                        void* dw, void* workspace, size_t workspace_bytes,
+                        int64_t rows, int64_t dim, float eps, int dtype,
+                        int w_dtype);
+
+/* ---- matmul ---------------------------------------------------------------- */
+
+/* C[M,N] = op(A)[M,K] @ op(B)[K,N] with an f32 accumulator, cast to c_dtype.
+ *   trans_a = 0: A stored [M,K] (row stride lda);  1: A stored [K,M] (stride lda)
+ *   trans_b = 0: B stored [K,N] (row stride ldb);  1: B stored [N,K] (stride ldb)
+ * C stored [M,N] with row stride ldc.  ab_dtype is the operand dtype (both the
+ * same); bf16/f16 run on tcgen05 tensor cores (kind::f16, f32 accumulator in
+ * TMEM); f32 runs an exact-f32 CUDA-core path (the Precision.HIGHEST contract).
+ * Any M, N, K >= 1 is accepted (ragged edges are zero-filled by TMA, no padding
+ * copies).  Replaces ferrite_matmul: matmul.py:27-38 (_matmul_kernel) via
+ * _matmul_impl matmul.py:52-86; the transposed forms serve the VJP
+ * matmul.py:99-104 without materialised transposes. */
+FERRITE_API int ferrite_gemm(void* stream, const void* a, const void* b, void* c,
+                 int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
+                 int64_t ldc, int trans_a, int trans_b, int ab_dtype,
+                 int c_dtype);
+
+/* ---- causal flash attention ------------------------------------------------ */
+
+/* Shapes: q [b, h, sq, d], k/v [b, h, sk, d], all of dtype `dtype`, densely
+ * packed.  lse/delta are f32 [b, h, sq] (the reference keeps them
+ * lane-replicated as [b, h, sq, 128]; that layout is internal to its custom_vjp
+ * residuals, so the compact one is a drop-in).  block_q/block_k are the caller's
+ * BlockSizes; the kernels validate them exactly like _validate
+ * (flash_attention.py:336-353) and tile internally. */
+
+/* o = softmax(scale * q k^T [causal mask]) v, lse = m + log(l).
+ * Replaces ferrite_flash_attention_fwd: flash_attention.py:91-127
+ * (_fwd_kernel) via _flash_forward flash_attention.py:130-175. */
+FERRITE_API int ferrite_attn_fwd(void* stream, const void* q, const void* k, const void* v,
+                     void* o, float* lse, int64_t b, int64_t h, int64_t sq,
+                     int64_t sk, int64_t d, float scale, int causal,
+                     int block_q, int block_k, int dtype);
+
+/* delta[b,h,s] = sum_d dO*O in f32.  Replaces the XLA fusion at
+ * flash_attention.py:328-329 (_flash_bwd). */
+FERRITE_API int ferrite_attn_bwd_prep(void* stream, const void* dout, const void* out,
+                          float* delta, int64_t b, int64_t h, int64_t s,
+                          int64_t d, int dtype);
+
+/* dK = scale * sum_q dS^T Q, dV = sum_q P^T dO (no atomics; one CTA per key
+ * tile).  Replaces ferrite_flash_attention_bwd_dkv: flash_attention.py:197-221
+ * with the grid of flash_attention.py:253-279. */
+FERRITE_API int ferrite_attn_bwd_dkv(void* stream, const void* q, const void* k,
+                         const void* v, const void* dout, const float* lse,
+                         const float* delta, void* dk, void* dv, int64_t b,
+                         int64_t h, int64_t sq, int64_t sk, int64_t d,
+                         float scale, int causal, int block_q, int block_k,
+                         int dtype);
+
+/* dQ = scale * sum_k dS K (no atomics; one CTA per query tile).  Replaces
+ * ferrite_flash_attention_bwd_dq: flash_attention.py:224-243 with the grid of
+ * flash_attention.py:281-306. */
+FERRITE_API int ferrite_attn_bwd_dq(void* stream, const void* q, const void* k,
+                        const void* v, const void* dout, const float* lse,
+                        const float* delta, void* dq, int64_t b, int64_t h,
+                        int64_t sq, int64_t sk, int64_t d, float scale,
+                        int causal, int block_q, int block_k, int dtype);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FERRITE_B200_H_ */

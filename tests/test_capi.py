@@ -1,0 +1,147 @@
+"""CPU checks of the C-ABI library and the host-side API logic (no GPU compute).
+
+* the shared library loads and exports every entry point ``include/*.h`` declares,
+  with the signatures the ctypes binding uses;
+* host-side validation returns the documented status codes before touching a
+  device (bad shapes / dtypes, host fault injection);
+* the Python API raises the reference's ``ValueError``s and refuses CPU tensors
+  (no fallback path).
+"""
+
+import ctypes
+import glob
+import os
+import re
+
+import pytest
+import torch
+
+from ferrite import _native as nat
+from ferrite.kernels.flash_attention import BlockSizes, attention_flops, flash_attention
+from ferrite.kernels.matmul import matmul, matmul_flops
+from ferrite.kernels.rmsnorm import rmsnorm
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared_symbols() -> set[str]:
+    names = set()
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        txt = open(h).read()
+        txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+        names |= set(re.findall(r"FERRITE_API\s+[\w\s\*]+?\b(ferrite_\w+)\s*\(", txt))
+    return names
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = nat.lib()
+    declared = _declared_symbols()
+    assert len(declared) >= 12, declared
+    for name in declared:
+        assert hasattr(lib, name), name
+    assert declared <= set(nat.SIGNATURES), declared - set(nat.SIGNATURES)
+    assert "sm_100a" in nat.version()
+
+
+def test_library_is_built_for_sm100a_only():
+    out = os.popen(f"cuobjdump --list-elf {nat.LIB_PATH} 2>/dev/null").read()
+    if not out:
+        pytest.skip("cuobjdump unavailable")
+    assert "sm_100a" in out
+    assert "sm_90" not in out and "sm_80" not in out
+
+
+def test_status_codes_without_a_gpu():
+    lib = nat.lib()
+    # negative rows -> BAD_SHAPE, before any CUDA call
+    rc = lib.ferrite_rmsnorm_fwd(None, 1, 1, 1, -1, 4096, 1e-6, nat.BF16, nat.F32)
+    assert rc == nat.BAD_SHAPE and "bad shape" in nat.last_error()
+    rc = lib.ferrite_add_rmsnorm_fwd(None, 1, 1, 1, 1, 1, 8, 4096, 1e-6, 7, nat.F32)
+    assert rc == nat.UNSUPPORTED_DTYPE
+    rc = lib.ferrite_rmsnorm_bwd(None, 1, 1, 1, None, 1, 1, 1, 16, 8, 0, 1e-6, nat.BF16, nat.F32)
+    assert rc == nat.BAD_SHAPE
+    with pytest.raises(nat.FerriteError) as e:
+        nat.check(nat.UNSUPPORTED_DTYPE)
+    assert e.value.status == nat.UNSUPPORTED_DTYPE
+
+
+def test_host_fault_injection(monkeypatch):
+    lib = nat.lib()
+    monkeypatch.setenv("FERRITE_FAULT_INJECT", "rmsnorm_fwd,add_rmsnorm_fwd")
+    rc = lib.ferrite_rmsnorm_fwd(None, 1, 1, 1, 8, 4096, 1e-6, nat.BF16, nat.F32)
+    assert rc == nat.INJECTED_FAULT and "injected" in nat.last_error()
+    monkeypatch.setenv("FERRITE_FAULT_INJECT", "all")
+    assert lib.ferrite_rmsnorm_bwd(None, 1, 1, 1, None, 1, 1, 1, 16, 8, 8, 1e-6, nat.BF16, nat.F32) == nat.INJECTED_FAULT
+    monkeypatch.delenv("FERRITE_FAULT_INJECT")
+
+
+def test_last_error_is_thread_local():
+    import threading
+
+    lib = nat.lib()
+    lib.ferrite_rmsnorm_fwd(None, 1, 1, 1, -1, 8, 1e-6, nat.BF16, nat.F32)
+    seen = []
+
+    def other():
+        seen.append(nat.last_error())
+
+    t = threading.Thread(target=other)
+    t.start()
+    t.join()
+    assert seen == [""]
+    assert "bad shape" in nat.last_error()
+
+
+def test_workspace_query_is_bounded():
+    lib = nat.lib()
+    ws = lib.ferrite_rmsnorm_bwd_workspace_size(8192, 4096)
+    assert 0 < ws <= 8192 * 4096 * 4
+    assert lib.ferrite_rmsnorm_bwd_workspace_size(1, 128) >= 8 * 128 * 4 or lib.ferrite_rmsnorm_bwd_workspace_size(1, 128) >= 128 * 4
+
+
+# ---------------------------------------------------------------- Python API validation
+
+
+def test_rmsnorm_validation_errors():
+    x = torch.zeros(4, 64)
+    with pytest.raises(ValueError):
+        rmsnorm(x, torch.ones(63))
+    with pytest.raises(ValueError):
+        rmsnorm(x, torch.ones(64), residual=torch.zeros(4, 32))
+    with pytest.raises(ValueError):
+        rmsnorm(x, torch.ones(64), block_rows=12)
+
+
+def test_cpu_tensors_are_refused_not_computed():
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        rmsnorm(torch.zeros(4, 64), torch.ones(64))
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        matmul(torch.zeros(8, 8), torch.zeros(8, 8))
+    q = torch.zeros(1, 1, 128, 64)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        flash_attention(q, q, q)
+
+
+def test_flash_attention_validation_errors():
+    q = torch.zeros(1, 1, 256, 128)
+    with pytest.raises(ValueError):
+        flash_attention(q, q, q, block_sizes=BlockSizes(block_k=100))
+    with pytest.raises(ValueError):
+        flash_attention(q, q[:, :, :128], q[:, :, :128], causal=True)
+    with pytest.raises(ValueError):
+        flash_attention(q, q, q.to(torch.bfloat16))
+    with pytest.raises(ValueError):
+        flash_attention(torch.zeros(1, 1, 256, 200), torch.zeros(1, 1, 256, 200), torch.zeros(1, 1, 256, 200))
+
+
+def test_matmul_validation_errors():
+    x = torch.zeros(128, 128)
+    with pytest.raises(ValueError):
+        matmul(x, x, block_n=100)
+    with pytest.raises(ValueError):
+        matmul(x, torch.zeros(64, 8))
+
+
+def test_flop_formulas():
+    assert matmul_flops(256, 256, 256) == 2 * 256**3
+    assert attention_flops(2, 4, 512, 512, 64, causal=True) * 3.5 == pytest.approx(9.395e8, rel=1e-3)

@@ -1,0 +1,138 @@
+"""GPU parity of the fused add+RMSNorm kernels (forward and backward) against the
+oracle, the committed golden fixtures and the reference's own test cases
+(tests/test_rmsnorm.py of anxnd2211/ferrite-tpu, re-pointed at the CUDA path).
+
+Tolerances: the reference's (1e-5 f32 forward, 1e-4 f32 gradients, 1e-2 / 2e-2
+bf16 h / y) and the north star's max-abs 2e-2 on bf16 outputs and gradients.
+"""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from ferrite import _native as nat
+from ferrite.kernels.rmsnorm import rmsnorm, rmsnorm_backward, rmsnorm_reference
+from helpers import BF16, load_arrays, max_abs, normal, to_numpy, to_torch
+from oracle import rmsnorm as on
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+@pytest.mark.parametrize("shape", [(4, 64, 256), (300, 384), (2, 8, 128)])
+def test_forward_matches_reference(rng, shape):
+    """test_rmsnorm.py:9-14 (f32, 1e-5)."""
+    x = normal(rng, shape)
+    w = (1.0 + 0.1 * rng.standard_normal(shape[-1])).astype(np.float32)
+    y = rmsnorm(to_torch(x), to_torch(w))
+    np.testing.assert_allclose(to_numpy(y), on.rmsnorm_fwd(x, w), atol=1e-5, rtol=1e-5)
+    np.testing.assert_allclose(to_numpy(y), to_numpy(rmsnorm_reference(to_torch(x), to_torch(w))), atol=1e-5, rtol=1e-5)
+
+
+def test_fused_residual_forward(rng):
+    """test_rmsnorm.py:17-25 (bf16, bf16 weight)."""
+    x, r = normal(rng, (2, 256, 256), BF16), normal(rng, (2, 256, 256), BF16)
+    w = np.ones(256, BF16)
+    h, y = rmsnorm(to_torch(x), to_torch(w), residual=to_torch(r))
+    h_ref, y_ref = on.add_rmsnorm_fwd(x, r, w)
+    assert h.dtype == torch.bfloat16
+    np.testing.assert_allclose(to_numpy(h).astype(np.float32), h_ref.astype(np.float32), atol=1e-2, rtol=1e-2)
+    np.testing.assert_allclose(to_numpy(y).astype(np.float32), y_ref.astype(np.float32), atol=2e-2, rtol=2e-2)
+
+
+def test_gradients_match_reference(rng):
+    """test_rmsnorm.py:28-44 (f32 fused gradients, 1e-4)."""
+    x, r = normal(rng, (64, 256)), normal(rng, (64, 256))
+    w = (1.0 + 0.1 * rng.standard_normal(256)).astype(np.float32)
+    cot = normal(rng, (64, 256))
+    xt, rt, wt = (to_torch(a).requires_grad_(True) for a in (x, r, w))
+    h, y = rmsnorm(xt, wt, residual=rt)
+    ct = to_torch(cot)
+    (torch.sum(y * ct) + torch.sum(h * ct.flip(0))).backward()
+    h_ref, _ = on.add_rmsnorm_fwd(x, r, w)
+    dh, dw = on.rmsnorm_bwd(h_ref, w, cot, cot[::-1].copy())
+    for got, ref in ((xt.grad, dh), (rt.grad, dh), (wt.grad, dw)):
+        np.testing.assert_allclose(to_numpy(got), ref, atol=1e-4, rtol=1e-4)
+
+
+def test_plain_gradient(rng):
+    """test_rmsnorm.py:47-53 (f32, 1e-5) against torch autograd of the reference."""
+    x = normal(rng, (32, 128))
+    xt, wt = to_torch(x).requires_grad_(True), torch.ones(128, device="cuda", requires_grad=True)
+    torch.sum(torch.tanh(rmsnorm(xt, wt))).backward()
+    xr, wr = to_torch(x).requires_grad_(True), torch.ones(128, device="cuda", requires_grad=True)
+    torch.sum(torch.tanh(rmsnorm_reference(xr, wr))).backward()
+    np.testing.assert_allclose(to_numpy(xt.grad), to_numpy(xr.grad), atol=1e-5, rtol=1e-5)
+    np.testing.assert_allclose(to_numpy(wt.grad), to_numpy(wr.grad), atol=1e-5, rtol=1e-5)
+
+
+def test_golden_fixtures():
+    g = load_arrays(os.path.join(GOLDEN, "add_rmsnorm_bf16_16x4096.npz"))
+    h, y = rmsnorm(to_torch(g["x"]), to_torch(g["w"]), residual=to_torch(g["r"]))
+    assert np.array_equal(to_numpy(h).view(np.uint16), g["h"].view(np.uint16))  # x+r rounding is exact
+    assert max_abs(y, g["y"]) <= 2e-2
+    dh, dw = rmsnorm_backward(to_torch(g["h"]), to_torch(g["w"]), to_torch(g["dy"]), to_torch(g["dh_direct"]), 1e-6)
+    assert max_abs(dh, g["dh"]) <= 2e-2
+    np.testing.assert_allclose(to_numpy(dw), g["dw"], rtol=1e-4, atol=1e-3)
+    g = load_arrays(os.path.join(GOLDEN, "rmsnorm_f32_40x384.npz"))
+    y = rmsnorm(to_torch(g["x"]), to_torch(g["w"]))
+    np.testing.assert_allclose(to_numpy(y), g["y"], atol=1e-5, rtol=1e-5)
+    dx, dw = rmsnorm_backward(to_torch(g["x"]), to_torch(g["w"]), to_torch(g["dy"]), None, 1e-6)
+    np.testing.assert_allclose(to_numpy(dx), g["dx"], atol=1e-5, rtol=1e-5)
+    np.testing.assert_allclose(to_numpy(dw), g["dw"], atol=1e-4, rtol=1e-5)
+
+
+@pytest.mark.parametrize("rows,dim", [(8192, 4096), (1, 4096), (7, 4096), (33, 1000), (5, 8), (3, 24), (1024, 8192), (64, 32768)])
+def test_add_rmsnorm_fwd_bwd_vs_oracle(rows, dim):
+    """BASELINE config (8192 x 4096 bf16) plus ragged / odd / tiny / long rows."""
+    rng = np.random.default_rng(rows * 7 + dim)
+    x, r = normal(rng, (rows, dim), BF16), normal(rng, (rows, dim), BF16)
+    w = (1.0 + 0.1 * rng.standard_normal(dim)).astype(np.float32)
+    dy, dhd = normal(rng, (rows, dim), BF16), normal(rng, (rows, dim), BF16)
+    h, y = rmsnorm(to_torch(x), to_torch(w), residual=to_torch(r))
+    h_ref, y_ref = on.add_rmsnorm_fwd(x, r, w)
+    assert np.array_equal(to_numpy(h).view(np.uint16), h_ref.view(np.uint16))
+    assert max_abs(y, y_ref) <= 2e-2
+    # bf16 y: at most one ulp apart from the oracle
+    yg, yr = to_numpy(y).astype(np.float32), y_ref.astype(np.float32)
+    assert np.all(np.abs(yg - yr) <= np.abs(yr) * 2**-7 + 1e-6)
+    dh, dw = rmsnorm_backward(to_torch(h_ref), to_torch(w), to_torch(dy), to_torch(dhd), 1e-6)
+    dh_ref, dw_ref = on.rmsnorm_bwd(h_ref, w, dy, dhd)
+    assert max_abs(dh, dh_ref) <= 2e-2
+    np.testing.assert_allclose(to_numpy(dw), dw_ref, rtol=2e-4, atol=2e-3 * np.sqrt(rows / 64 + 1))
+
+
+def test_backward_is_deterministic():
+    rng = np.random.default_rng(5)
+    h = to_torch(normal(rng, (4096, 4096), BF16))
+    w = to_torch((1.0 + 0.1 * rng.standard_normal(4096)).astype(np.float32))
+    dy = to_torch(normal(rng, (4096, 4096), BF16))
+    a = rmsnorm_backward(h, w, dy, None, 1e-6)
+    b = rmsnorm_backward(h, w, dy, None, 1e-6)
+    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+
+
+def test_misaligned_views_take_the_scalar_path():
+    rng = np.random.default_rng(3)
+    base = to_torch(normal(rng, (65, 257), np.float32))
+    x = base[1:, 1:]  # not 16-byte aligned rows; the API makes it contiguous
+    w = torch.ones(256, device="cuda")
+    y = rmsnorm(x, w)
+    np.testing.assert_allclose(to_numpy(y), on.rmsnorm_fwd(to_numpy(x.contiguous()), to_numpy(w)), atol=1e-5, rtol=1e-5)
+    # unaligned raw pointer straight into the C ABI (scalar path)
+    xs = base.reshape(-1)[1 : 1 + 64 * 256].reshape(64, 256)
+    ys = torch.empty(64, 256, device="cuda")
+    nat.check(nat.lib().ferrite_rmsnorm_fwd(nat.stream_ptr(), xs.data_ptr(), w.data_ptr(), ys.data_ptr(), 64, 256, 1e-6, nat.F32, nat.F32))
+    np.testing.assert_allclose(to_numpy(ys), on.rmsnorm_fwd(to_numpy(xs), to_numpy(w)), atol=1e-5, rtol=1e-5)
+
+
+def test_zero_rows_is_a_no_op():
+    x = torch.empty(0, 4096, dtype=torch.bfloat16, device="cuda")
+    w = torch.ones(4096, device="cuda")
+    assert rmsnorm(x, w).shape == (0, 4096)
+
+
+def test_device_status_clean():
+    nat.device_status(clear=True)
