@@ -1,4 +1,527 @@
-// placeholder; replaced by the tcgen05 GEMM
+// Matmul with an f32 accumulator for sm_100a.
+//
+// bf16/f16 operands: persistent, warp-specialised tcgen05 kernel.
+//   * warp 0 (one elected lane) issues TMA loads of A and B tiles into a ring of
+//     STAGES shared-memory slots (128-byte swizzle, no padding copies: ragged
+//     edges are zero-filled by TMA);
+//   * warp 1 owns the TMEM allocation and (one lane) issues tcgen05.mma
+//     (M=128, N=BN, K=16, kind::f16) into an f32 accumulator in TMEM; every slot
+//     is released with tcgen05.commit -> mbarrier, every finished tile with a
+//     commit to the accumulator's "full" barrier;
+//   * warps 2-5 are the epilogue: tcgen05.ld the accumulator (two TMEM buffers,
+//     so the epilogue of tile i overlaps the main loop of tile i+1), convert,
+//     and store with row/column masks.
+//   Operands may be K-major or MN-major in global memory (the transpose flags
+//   of the C ABI); the MN-major case uses MN-major shared-memory layouts and the
+//   instruction descriptor's transpose bits instead of materialised transposes.
+//
+// f32 operands (the reference's Precision.HIGHEST contract, _compat.py:17-26)
+// and shapes TMA cannot describe (row strides not a multiple of 16 bytes, tiny
+// dimensions) run a register-tiled CUDA-core kernel that accumulates in f32 with
+// FFMA: exact f32 products, no reduced-precision passes.
+//
+// Reference: src/ferrite/kernels/matmul.py of anxnd2211/ferrite-tpu
+// (_matmul_kernel :27-38, _matmul_impl :52-86, VJP :99-104).
+#include <algorithm>
+#include <cstdlib>
+
 #include "common.cuh"
-namespace ferrite { FERRITE_DEFINE_STATUS_READER(status_gemm) }
-extern "C" int ferrite_gemm(void*, const void*, const void*, void*, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int, int, int, int) { return ferrite::fail(FERRITE_UNSUPPORTED_DTYPE, "gemm: not built yet"); }
+
+namespace ferrite {
+FERRITE_DEFINE_STATUS_READER(status_gemm)
+
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // 64 x 16-bit = 128 bytes: one swizzle row
+constexpr int kThreads = 192;
+
+template <int BN>
+struct Smem {
+  static constexpr int kStages = BN == 256 ? 4 : 6;
+  static constexpr int kABytes = BM * BK * 2;  // 16 KiB
+  static constexpr int kBBytes = BN * BK * 2;  // 16 or 32 KiB
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTileBytes = kStages * kStageBytes;
+  // barriers: full[S], empty[S], acc_full[2], acc_empty[2]; then tmem base, abort
+  static constexpr int kBarBytes = (2 * kStages + 4) * 8 + 16;
+  static constexpr int kTotal = 1024 /*alignment slack*/ + kTileBytes + kBarBytes;
+};
+
+struct Params {
+  int m, n, k;
+  int64_t ldc;
+  void* c;
+  int tiles_m, tiles_n, k_blocks;
+  int group_m;  // raster: groups of group_m M-tiles sweep all N-tiles
+};
+
+template <typename TC>
+__device__ __forceinline__ void store_row32(TC* __restrict__ c, int64_t ldc, int row,
+                                            int col0, int m, int n, const uint32_t (&r)[32],
+                                            bool vec_ok) {
+  if (row >= m) return;
+  TC* dst = c + (int64_t)row * ldc + col0;
+  if (vec_ok && col0 + 32 <= n) {
+    if constexpr (sizeof(TC) == 2) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        uint4 v;
+        if constexpr (std::is_same<TC, __nv_bfloat16>::value) {
+          v.x = pack_bf16x2(__uint_as_float(r[j]), __uint_as_float(r[j + 1]));
+          v.y = pack_bf16x2(__uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+          v.z = pack_bf16x2(__uint_as_float(r[j + 4]), __uint_as_float(r[j + 5]));
+          v.w = pack_bf16x2(__uint_as_float(r[j + 6]), __uint_as_float(r[j + 7]));
+        } else {
+          v.x = pack_f16x2(__uint_as_float(r[j]), __uint_as_float(r[j + 1]));
+          v.y = pack_f16x2(__uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+          v.z = pack_f16x2(__uint_as_float(r[j + 4]), __uint_as_float(r[j + 5]));
+          v.w = pack_f16x2(__uint_as_float(r[j + 6]), __uint_as_float(r[j + 7]));
+        }
+        *reinterpret_cast<uint4*>(dst + j) = v;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4)
+        *reinterpret_cast<uint4*>(dst + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (col0 + j < n) dst[j] = DT<TC>::from_f(__uint_as_float(r[j]));
+  }
+}
+
+__device__ __forceinline__ void tile_coords(int t, const Params& p, int& mb, int& nb) {
+  const int per_group = p.group_m * p.tiles_n;
+  const int g = t / per_group;
+  const int first_m = g * p.group_m;
+  const int gm = min(p.group_m, p.tiles_m - first_m);
+  const int r = t - g * per_group;
+  mb = first_m + r % gm;
+  nb = r / gm;
+}
+
+// A_MN: A stored [K][M] (MN-major); B_MN: B stored [K][N] (MN-major).
+template <int BN, bool A_MN, bool B_MN, bool BF16, typename TC>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a,
+                   const __grid_constant__ CUtensorMap tma_b, const Params p) {
+  using S = Smem<BN>;
+  constexpr int STAGES = S::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* tiles = smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kTileBytes);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_tiles = p.tiles_m * p.tiles_n;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+    }
+    *abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tma_a);
+    tma_prefetch_desc(&tma_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 2 * BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        int mb, nb;
+        tile_coords(t, p, mb, nb);
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, abort, 1)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = tiles + s * S::kStageBytes;
+          uint8_t* sb = sa + S::kABytes;
+          mbar_arrive_expect_tx(&full[s], S::kStageBytes);
+          if constexpr (A_MN) {
+            tma_load_2d(sa, &tma_a, &full[s], mb * BM, kb * BK);
+            tma_load_2d(sa + 8192, &tma_a, &full[s], mb * BM + 64, kb * BK);
+          } else {
+            tma_load_2d(sa, &tma_a, &full[s], kb * BK, mb * BM);
+          }
+          if constexpr (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(sb + j * 8192, &tma_b, &full[s], nb * BN + j * 64, kb * BK);
+          } else {
+            tma_load_2d(sb, &tma_b, &full[s], kb * BK, nb * BN);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_f16(BM, BN, BF16, A_MN, B_MN);
+      int it = 0, local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
+        const int buf = local & 1;
+        const uint32_t aph = (local >> 1) & 1;
+        if (!mbar_wait(&acc_empty[buf], aph ^ 1, abort, 2)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, abort, 3)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(tiles + s * S::kStageBytes);
+          const uint32_t sb = sa + S::kABytes;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = A_MN ? make_sdesc(sa + kk * 2048, 8192, 1024)
+                                     : make_sdesc(sa + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? make_sdesc(sb + kk * 2048, 8192, 1024)
+                                     : make_sdesc(sb + kk * 32, 16, 1024);
+            tc_mma_f16_ss(d_tmem, ad, bd, idesc, (kb | kk) != 0);
+          }
+          tc_commit(&empty[s]);  // slot free once these MMAs retire
+        }
+        tc_commit(&acc_full[buf]);  // accumulator ready for the epilogue
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_in_tile = q * 32 + lane;
+    TC* c = reinterpret_cast<TC*>(p.c);
+    const bool vec_ok = ((reinterpret_cast<uintptr_t>(c) & 15u) == 0) &&
+                        ((p.ldc * (int64_t)sizeof(TC)) % 16 == 0);
+    int local = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+      int mb, nb;
+      tile_coords(t, p, mb, nb);
+      const int buf = local & 1;
+      const uint32_t aph = (local >> 1) & 1;
+      if (!mbar_wait(&acc_full[buf], aph, abort, 4)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
+      const int row = mb * BM + row_in_tile;
+#pragma unroll 1
+      for (int cc = 0; cc < BN / 32; ++cc) {
+        uint32_t r[32];
+        tmem_ld32(tbase + cc * 32, r);
+        tmem_wait_ld();
+        store_row32<TC>(c, p.ldc, row, nb * BN + cc * 32, p.m, p.n, r, vec_ok);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+  }
+
+  // ------------------------------------------------------------ teardown
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// CUDA-core path: exact f32 accumulation, any strides / transposes / dtypes.
+// 128x128 CTA tile, 256 threads, 8x8 register micro-tile, K step 16.
+// ---------------------------------------------------------------------------
+
+constexpr int SB_M = 128, SB_N = 128, SB_K = 16;
+
+template <typename TA>
+__device__ __forceinline__ float ld_elem(const TA* p, int64_t idx) {
+  return DT<TA>::to_f(p[idx]);
+}
+
+template <typename TA, typename TC>
+__global__ void __launch_bounds__(256)
+    gemm_simt_kernel(const TA* __restrict__ a, const TA* __restrict__ b, TC* __restrict__ c,
+                     int m, int n, int k, int64_t lda, int64_t ldb, int64_t ldc,
+                     int trans_a, int trans_b) {
+  __shared__ float As[2][SB_K][SB_M + 4];
+  __shared__ float Bs[2][SB_K][SB_N + 4];
+  const int tid = threadIdx.x;
+  const int m0 = blockIdx.y * SB_M, n0 = blockIdx.x * SB_N;
+  const int tr = tid / 16, tc = tid % 16;  // 16 x 16 threads, 8x8 each
+
+  auto load_tile = [&](int buf, int k0) {
+    // A tile: SB_M x SB_K elements = 2048, 8 per thread.
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = tid + i * 256;
+      int mm, kk;
+      if (trans_a) {  // stored [K][M]: consecutive threads along M
+        mm = e % SB_M;
+        kk = e / SB_M;
+      } else {  // stored [M][K]: consecutive threads along K
+        kk = e % SB_K;
+        mm = e / SB_K;
+      }
+      const int gm = m0 + mm, gk = k0 + kk;
+      float v = 0.f;
+      if (gm < m && gk < k)
+        v = ld_elem(a, trans_a ? (int64_t)gk * lda + gm : (int64_t)gm * lda + gk);
+      As[buf][kk][mm] = v;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = tid + i * 256;
+      int nn, kk;
+      if (trans_b) {  // stored [N][K]
+        kk = e % SB_K;
+        nn = e / SB_K;
+      } else {  // stored [K][N]
+        nn = e % SB_N;
+        kk = e / SB_N;
+      }
+      const int gn = n0 + nn, gk = k0 + kk;
+      float v = 0.f;
+      if (gn < n && gk < k)
+        v = ld_elem(b, trans_b ? (int64_t)gn * ldb + gk : (int64_t)gk * ldb + gn);
+      Bs[buf][kk][nn] = v;
+    }
+  };
+
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+
+  const int kt = (k + SB_K - 1) / SB_K;
+  load_tile(0, 0);
+  __syncthreads();
+  for (int t = 0; t < kt; ++t) {
+    const int cur = t & 1;
+    if (t + 1 < kt) load_tile(cur ^ 1, (t + 1) * SB_K);
+#pragma unroll
+    for (int kk = 0; kk < SB_K; ++kk) {
+      float av[8], bv[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        av[i] = As[cur][kk][tr * 4 + i];
+        av[4 + i] = As[cur][kk][64 + tr * 4 + i];
+        bv[i] = Bs[cur][kk][tc * 4 + i];
+        bv[4 + i] = Bs[cur][kk][64 + tc * 4 + i];
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int gm = m0 + (i < 4 ? tr * 4 + i : 64 + tr * 4 + (i - 4));
+    if (gm >= m) continue;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int gn = n0 + (j < 4 ? tc * 4 + j : 64 + tc * 4 + (j - 4));
+      if (gn < n) c[(int64_t)gm * ldc + gn] = DT<TC>::from_f(acc[i][j]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host
+// ---------------------------------------------------------------------------
+
+static int env_int(const char* name, int dflt) {
+  const char* s = std::getenv(name);
+  return (s && *s) ? std::atoi(s) : dflt;
+}
+
+template <typename TA, typename TC>
+static int launch_simt(cudaStream_t s, const void* a, const void* b, void* c, int64_t m,
+                       int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc,
+                       int ta, int tb) {
+  dim3 grid((unsigned)((n + SB_N - 1) / SB_N), (unsigned)((m + SB_M - 1) / SB_M));
+  if (grid.y > 65535) return fail(FERRITE_BAD_SHAPE, "gemm: M too large for the CUDA-core path");
+  gemm_simt_kernel<TA, TC><<<grid, 256, 0, s>>>((const TA*)a, (const TA*)b, (TC*)c, (int)m,
+                                                 (int)n, (int)k, lda, ldb, ldc, ta, tb);
+  return check_launch("gemm_simt");
+}
+
+template <int BN, bool A_MN, bool B_MN, bool BF16, typename TC>
+static int launch_tc(cudaStream_t s, const CUtensorMap& ta, const CUtensorMap& tb,
+                     const Params& p, int grid) {
+  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, BF16, TC>;
+  const int smem = Smem<BN>::kTotal;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess)
+    return fail(FERRITE_LAUNCH_FAILED, "gemm: smem attribute: %s", cudaGetErrorString(e));
+  kern<<<grid, kThreads, smem, s>>>(ta, tb, p);
+  return check_launch("gemm_tc");
+}
+
+template <int BN, bool BF16, typename TC>
+static int dispatch_major(cudaStream_t s, bool a_mn, bool b_mn, const CUtensorMap& ta,
+                          const CUtensorMap& tb, const Params& p, int grid) {
+  if (!a_mn && !b_mn) return launch_tc<BN, false, false, BF16, TC>(s, ta, tb, p, grid);
+  if (!a_mn && b_mn) return launch_tc<BN, false, true, BF16, TC>(s, ta, tb, p, grid);
+  if (a_mn && !b_mn) return launch_tc<BN, true, false, BF16, TC>(s, ta, tb, p, grid);
+  return launch_tc<BN, true, true, BF16, TC>(s, ta, tb, p, grid);
+}
+
+template <bool BF16, typename TC>
+static int run_tc(cudaStream_t s, const void* a, const void* b, void* c, int64_t m,
+                  int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int trans_a,
+                  int trans_b) {
+  const int dev = current_device();
+  const int sms = num_sms(dev);
+  // B tile width: 256 unless that leaves most SMs idle.
+  const int64_t tiles256 = ((m + BM - 1) / BM) * ((n + 255) / 256);
+  int BN = (tiles256 >= sms || n <= 128) ? 256 : 128;
+  if (n <= 128) BN = 128;
+  const int forced = env_int("FERRITE_GEMM_BN", 0);
+  if (forced == 128 || forced == 256) BN = forced;
+  if (n < BN) BN = 128;
+
+  const CUtensorMapDataType dt = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap ta, tb;
+  const bool a_mn = trans_a != 0;  // A stored [K][M]
+  const bool b_mn = trans_b == 0;  // B stored [K][N] is MN-major for the MMA
+  int rc;
+  if (a_mn)
+    rc = make_tmap_2d(&ta, a, dt, 2, (uint64_t)m, (uint64_t)k, (uint64_t)lda * 2, 64, 64,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+  else
+    rc = make_tmap_2d(&ta, a, dt, 2, (uint64_t)k, (uint64_t)m, (uint64_t)lda * 2, 64, 128,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  if (b_mn)
+    rc = make_tmap_2d(&tb, b, dt, 2, (uint64_t)n, (uint64_t)k, (uint64_t)ldb * 2, 64, 64,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+  else
+    rc = make_tmap_2d(&tb, b, dt, 2, (uint64_t)k, (uint64_t)n, (uint64_t)ldb * 2, 64,
+                      (uint32_t)BN, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+
+  Params p;
+  p.m = (int)m;
+  p.n = (int)n;
+  p.k = (int)k;
+  p.ldc = ldc;
+  p.c = c;
+  p.tiles_m = (int)((m + BM - 1) / BM);
+  p.tiles_n = (int)((n + BN - 1) / BN);
+  p.k_blocks = (int)((k + BK - 1) / BK);
+  p.group_m = std::max(1, std::min(env_int("FERRITE_GEMM_GROUP_M", 16), p.tiles_m));
+  const int tiles = p.tiles_m * p.tiles_n;
+  const int grid = std::min(tiles, sms);
+  if (BN == 256) return dispatch_major<256, BF16, TC>(s, a_mn, b_mn, ta, tb, p, grid);
+  return dispatch_major<128, BF16, TC>(s, a_mn, b_mn, ta, tb, p, grid);
+}
+
+// True when every operand satisfies the TMA rules and the tile shapes fit.
+static bool tc_eligible(const void* a, const void* b, int64_t m, int64_t n, int64_t k,
+                        int64_t lda, int64_t ldb, int trans_a, int trans_b) {
+  if (env_int("FERRITE_GEMM_FORCE_SIMT", 0)) return false;
+  if ((reinterpret_cast<uintptr_t>(a) & 15u) || (reinterpret_cast<uintptr_t>(b) & 15u)) return false;
+  if ((lda * 2) % 16 || (ldb * 2) % 16) return false;
+  // Keep every TMA box inside the tensor extent along each dimension.
+  if (m < BM || n < 128 || k < BK) return false;
+  (void)trans_a;
+  (void)trans_b;
+  if (m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff) return false;
+  return true;
+}
+
+}  // namespace gemm
+}  // namespace ferrite
+
+using namespace ferrite;
+using namespace ferrite::gemm;
+
+extern "C" int ferrite_gemm(void* stream, const void* a, const void* b, void* c, int64_t m,
+                            int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc,
+                            int trans_a, int trans_b, int ab_dtype, int c_dtype) {
+  if (int rc = injected_fault("gemm")) return rc;
+  if (m < 0 || n < 0 || k < 0)
+    return fail(FERRITE_BAD_SHAPE, "gemm: negative size m=%lld n=%lld k=%lld", (long long)m,
+                (long long)n, (long long)k);
+  const int64_t a_rows = trans_a ? k : m, a_cols = trans_a ? m : k;
+  const int64_t b_rows = trans_b ? n : k, b_cols = trans_b ? k : n;
+  if (lda < std::max<int64_t>(1, a_cols) || ldb < std::max<int64_t>(1, b_cols) ||
+      ldc < std::max<int64_t>(1, n))
+    return fail(FERRITE_BAD_SHAPE, "gemm: leading dimension too small (lda=%lld ldb=%lld ldc=%lld)",
+                (long long)lda, (long long)ldb, (long long)ldc);
+  (void)a_rows;
+  (void)b_rows;
+  if (ab_dtype != FERRITE_F32 && ab_dtype != FERRITE_BF16 && ab_dtype != FERRITE_F16)
+    return fail(FERRITE_UNSUPPORTED_DTYPE, "gemm: operand dtype %d", ab_dtype);
+  if (c_dtype != FERRITE_F32 && c_dtype != FERRITE_BF16 && c_dtype != FERRITE_F16)
+    return fail(FERRITE_UNSUPPORTED_DTYPE, "gemm: output dtype %d", c_dtype);
+  if (m == 0 || n == 0) return FERRITE_OK;
+  if (!a || !b || !c) return fail(FERRITE_BAD_SHAPE, "gemm: null pointer");
+  cudaStream_t s = (cudaStream_t)stream;
+  if (k == 0) {
+    // C = 0 (row by row to honour ldc)
+    const size_t es = c_dtype == FERRITE_F32 ? 4 : 2;
+    cudaError_t e = cudaMemset2DAsync(c, ldc * es, 0, n * es, m, s);
+    return e == cudaSuccess ? FERRITE_OK : fail(FERRITE_LAUNCH_FAILED, "gemm: memset");
+  }
+
+  if (ab_dtype != FERRITE_F32 && tc_eligible(a, b, m, n, k, lda, ldb, trans_a, trans_b)) {
+    const bool bf = ab_dtype == FERRITE_BF16;
+    if (bf) {
+      if (c_dtype == FERRITE_BF16) return run_tc<true, __nv_bfloat16>(s, a, b, c, m, n, k, lda, ldb, ldc, trans_a, trans_b);
+      if (c_dtype == FERRITE_F32) return run_tc<true, float>(s, a, b, c, m, n, k, lda, ldb, ldc, trans_a, trans_b);
+      return run_tc<true, __half>(s, a, b, c, m, n, k, lda, ldb, ldc, trans_a, trans_b);
+    }
+    if (c_dtype == FERRITE_BF16) return run_tc<false, __nv_bfloat16>(s, a, b, c, m, n, k, lda, ldb, ldc, trans_a, trans_b);
+    if (c_dtype == FERRITE_F32) return run_tc<false, float>(s, a, b, c, m, n, k, lda, ldb, ldc, trans_a, trans_b);
+    return run_tc<false, __half>(s, a, b, c, m, n, k, lda, ldb, ldc, trans_a, trans_b);
+  }
+#define SIMT(TA, TC) launch_simt<TA, TC>(s, a, b, c, m, n, k, lda, ldb, ldc, trans_a, trans_b)
+  if (ab_dtype == FERRITE_F32) {
+    if (c_dtype == FERRITE_F32) return SIMT(float, float);
+    if (c_dtype == FERRITE_BF16) return SIMT(float, __nv_bfloat16);
+    return SIMT(float, __half);
+  }
+  if (ab_dtype == FERRITE_BF16) {
+    if (c_dtype == FERRITE_F32) return SIMT(__nv_bfloat16, float);
+    if (c_dtype == FERRITE_BF16) return SIMT(__nv_bfloat16, __nv_bfloat16);
+    return SIMT(__nv_bfloat16, __half);
+  }
+  if (c_dtype == FERRITE_F32) return SIMT(__half, float);
+  if (c_dtype == FERRITE_BF16) return SIMT(__half, __nv_bfloat16);
+  return SIMT(__half, __half);
+#undef SIMT
+}

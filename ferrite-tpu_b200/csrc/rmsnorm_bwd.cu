@@ -325,14 +325,14 @@ int ferrite_rmsnorm_bwd(void* stream, const void* h, const void* w,
                         int64_t rows, int64_t dim, float eps, int dtype,
                         int w_dtype) {
   if (int rc = check_common("rmsnorm_bwd", rows, dim, dtype, w_dtype)) return rc;
-  if (!h || !w || !dy || !dh || !dw)
-    return fail(FERRITE_BAD_SHAPE, "rmsnorm_bwd: null pointer");
   cudaStream_t s = (cudaStream_t)stream;
+  if (!dw) return fail(FERRITE_BAD_SHAPE, "rmsnorm_bwd: null dw");
   if (rows == 0) {
     cudaError_t e = cudaMemsetAsync(dw, 0, dim * (w_dtype == FERRITE_F32 ? 4 : 2), s);
     return e == cudaSuccess ? FERRITE_OK
                             : fail(FERRITE_LAUNCH_FAILED, "rmsnorm_bwd: memset");
   }
+  if (!h || !w || !dy || !dh) return fail(FERRITE_BAD_SHAPE, "rmsnorm_bwd: null pointer");
   const bool has = dh_direct != nullptr;
 #define CALL(T, TW)                                                                  \
   (has ? run_bwd<T, TW, true>(s, h, w, dy, dh_direct, dh, dw, workspace,             \

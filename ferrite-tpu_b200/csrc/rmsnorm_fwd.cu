@@ -154,8 +154,8 @@ int ferrite_rmsnorm_fwd(void* stream, const void* x, const void* w, void* y,
                         int64_t rows, int64_t dim, float eps, int dtype,
                         int w_dtype) {
   if (int rc = check_common("rmsnorm_fwd", rows, dim, dtype, w_dtype)) return rc;
-  if (!x || !w || !y) return fail(FERRITE_BAD_SHAPE, "rmsnorm_fwd: null pointer");
   if (rows == 0) return FERRITE_OK;
+  if (!x || !w || !y) return fail(FERRITE_BAD_SHAPE, "rmsnorm_fwd: null pointer");
   cudaStream_t s = (cudaStream_t)stream;
 #define CALL(T, TW, ADD) run_fwd<T, TW, ADD>(s, x, nullptr, w, nullptr, y, rows, dim, eps)
   if (dtype == FERRITE_BF16 && w_dtype == FERRITE_F32) return CALL(__nv_bfloat16, float, false);
@@ -170,9 +170,9 @@ int ferrite_add_rmsnorm_fwd(void* stream, const void* x, const void* r,
                             const void* w, void* h, void* y, int64_t rows,
                             int64_t dim, float eps, int dtype, int w_dtype) {
   if (int rc = check_common("add_rmsnorm_fwd", rows, dim, dtype, w_dtype)) return rc;
+  if (rows == 0) return FERRITE_OK;
   if (!x || !r || !w || !h || !y)
     return fail(FERRITE_BAD_SHAPE, "add_rmsnorm_fwd: null pointer");
-  if (rows == 0) return FERRITE_OK;
   cudaStream_t s = (cudaStream_t)stream;
 #define CALL(T, TW, ADD) run_fwd<T, TW, ADD>(s, x, r, w, h, y, rows, dim, eps)
   if (dtype == FERRITE_BF16 && w_dtype == FERRITE_F32) return CALL(__nv_bfloat16, float, true);
