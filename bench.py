@@ -65,26 +65,37 @@ def _host_cores() -> int:
 
 
 class ClockSampler:
-    """Samples nvidia-smi clocks/throttle reasons in the background during the timed region."""
+    """Samples nvidia-smi clocks and throttle reasons in the background during the
+    timed region (the profiling recipe's query), for the GPU this rank drives."""
 
-    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+    FIELDS = (
+        "index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+        "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+        "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+    )
 
-    def __init__(self, index: int):
-        self.index = index
+    def __init__(self, device: torch.device):
+        self.bus = None
+        try:
+            props = torch.cuda.get_device_properties(device)
+            self.bus = int(getattr(props, "pci_bus_id"))
+        except Exception:  # noqa: BLE001
+            pass
         self.proc = None
         self.lines: list[str] = []
+        self.err = ""
         self._t = None
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True,
             )
             self._t = threading.Thread(target=self._read, daemon=True)
             self._t.start()
-        except (OSError, FileNotFoundError):
-            self.proc = None
+        except OSError as e:
+            self.proc, self.err = None, str(e)
         return self
 
     def _read(self):
@@ -95,33 +106,40 @@ class ClockSampler:
         if self.proc is not None:
             self.proc.terminate()
             try:
-                self.proc.wait(timeout=5)
+                _, err = self.proc.communicate(timeout=5)
+                self.err = (err or "")[:200]
             except subprocess.TimeoutExpired:
                 self.proc.kill()
         if self._t is not None:
             self._t.join(timeout=2)
+
+    def _mine(self, parts) -> bool:
+        if self.bus is None:
+            return True
+        try:
+            return int(parts[1].split(":")[1], 16) == self.bus
+        except (IndexError, ValueError):
+            return True
 
     def summary(self) -> dict:
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.lines:
             parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10 or not self._mine(parts):
                 continue
             try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
+                sm.append(float(parts[2]))
+                mx = float(parts[3])
             except ValueError:
                 continue
-            for name, val in zip(names, parts[5:9]):
+            for name, val in zip(names, parts[6:10]):
                 if val.lower() == "active":
                     reasons.add(name)
-        return {
-            "sm_mhz": statistics.median(sm) if sm else None,
-            "sm_max_mhz": mx,
-            "reasons": sorted(reasons),
-            "samples": len(sm),
-        }
+        out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        if not sm and self.err:
+            out["error"] = self.err
+        return out
 
 
 def _load_traffic(kernel: str):
@@ -227,7 +245,7 @@ class NormWorkload:
 # ----------------------------------------------------------------------------- CPU baseline / reference arm
 
 
-def cpu_norm_baseline(sample_rows: int = 1024, repeats: int = 3, threads: int | None = None) -> dict:
+def cpu_norm_baseline(sample_rows: int = 8192, repeats: int = 5, threads: int | None = None) -> dict:
     """Time the oracle restatement (numpy, f32 statistics) of add+RMSNorm fwd+bwd on
     ``sample_rows`` x 4096 bf16 rows, split over ``threads`` host threads."""
     import concurrent.futures as cf
@@ -302,7 +320,7 @@ def run_ours(args, ws, rank, local):
 
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    with ClockSampler(dev) as clk:
         start.record()
         for i in range(args.steps):
             one_step(i, evs[i])
@@ -437,7 +455,7 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["norm"], default="norm")
-    ap.add_argument("--cpu-rows", type=int, default=1024, help="rows in the bounded CPU-baseline sample")
+    ap.add_argument("--cpu-rows", type=int, default=8192, help="rows in the bounded CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)  # timing rule: at least 3 untimed warm-up steps

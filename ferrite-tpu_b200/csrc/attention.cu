@@ -1,9 +1,765 @@
-// placeholder; replaced by the tcgen05 attention kernels
+// Causal flash attention for sm_100a: forward, delta prep, dK/dV and dQ.
+//
+// Tensor-core path (bf16/f16, head_dim 64 or 128, sk a multiple of 128): one CTA
+// per (128-row query tile, batch*head), warp-specialised:
+//   warp 0      TMA producer: Q once, then K/V tiles into a 2-slot ring; fully
+//               masked causal tiles are never requested (the KV loop stops at
+//               the diagonal), so they cost neither TMA traffic nor MMA time;
+//   warp 1      MMA issuer (one lane): S = Q K^T into one of two TMEM S buffers
+//               (SS form, both operands K-major), then O_j = P_j V_j into one of
+//               two TMEM PV buffers (P from shared memory, V MN-major), each
+//               completion published with tcgen05.commit -> mbarrier;
+//   warps 2-5   softmax warpgroup, one thread per query row (TMEM lane): reads S
+//               with tcgen05.ld, keeps the running max m and sum l in f32,
+//               writes P = exp(s - m) rounded to the input dtype into shared
+//               memory in the 128-byte-swizzled K-major layout the MMA reads,
+//               and folds each P_j V_j into an f32 register accumulator with the
+//               online-softmax rescale acc = acc * alpha + P_j V_j.  The output is
+//               normalised once at the end and lse = m + log(l) is written.
+// The S(j+1) MMA overlaps the softmax of tile j, and the P_j V_j MMA overlaps
+// the softmax of tile j+1 (the accumulator update lags one tile).
+//
+// Reference numerics (src/ferrite/kernels/flash_attention.py): scores
+// scale * q k^T in f32 (:103-105), finite MASK_VALUE on the causal diagonal
+// tile (:44, :80-83), online softmax with f32 statistics (:108-115), P rounded
+// to v.dtype before P V (:114), normalise once after the last key block and
+// lse = m + log l (:122-127).  Exponentials are evaluated as exp2 of
+// log2(e)-prescaled scores (the same function up to f32 rounding).
+//
+// Everything else (f32 inputs, other head dims, ragged sequence lengths) runs
+// a CUDA-core path with the same blockwise semantics: one warp per query (or
+// key) row, blocks of 32 keys (queries).
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
+
 #include "common.cuh"
-namespace ferrite { FERRITE_DEFINE_STATUS_READER(status_attention) }
-extern "C" {
-int ferrite_attn_fwd(void*, const void*, const void*, const void*, void*, float*, int64_t, int64_t, int64_t, int64_t, int64_t, float, int, int, int, int) { return ferrite::fail(FERRITE_UNSUPPORTED_DTYPE, "attn: not built yet"); }
-int ferrite_attn_bwd_prep(void*, const void*, const void*, float*, int64_t, int64_t, int64_t, int64_t, int) { return ferrite::fail(FERRITE_UNSUPPORTED_DTYPE, "attn: not built yet"); }
-int ferrite_attn_bwd_dkv(void*, const void*, const void*, const void*, const void*, const float*, const float*, void*, void*, int64_t, int64_t, int64_t, int64_t, int64_t, float, int, int, int, int) { return ferrite::fail(FERRITE_UNSUPPORTED_DTYPE, "attn: not built yet"); }
-int ferrite_attn_bwd_dq(void*, const void*, const void*, const void*, const void*, const float*, const float*, void*, int64_t, int64_t, int64_t, int64_t, int64_t, float, int, int, int, int) { return ferrite::fail(FERRITE_UNSUPPORTED_DTYPE, "attn: not built yet"); }
+
+namespace ferrite {
+FERRITE_DEFINE_STATUS_READER(status_attention)
+
+namespace attn {
+
+constexpr float kMaskValue = -0.7f * 3.40282346638528859812e+38f;  // -0.7 * FLT_MAX
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+// ===========================================================================
+// delta = rowsum(dO * O) (flash_attention.py:328)
+// ===========================================================================
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+    bwd_prep_kernel(const T* __restrict__ dout, const T* __restrict__ out,
+                    float* __restrict__ delta, int64_t rows, int d) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const T* a = dout + row * d;
+  const T* b = out + row * d;
+  float s = 0.f;
+  for (int j = lane; j < d; j += 32) s = fmaf(DT<T>::to_f(a[j]), DT<T>::to_f(b[j]), s);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (lane == 0) delta[row] = s;
 }
+
+// ===========================================================================
+// CUDA-core path (any dtype, head_dim <= 256)
+// ===========================================================================
+
+constexpr int kSimtMaxD = 256;
+constexpr int kSimtWarps = 4;  // rows per CTA
+
+template <typename T>
+__device__ __forceinline__ float round_to(float v) {
+  return DT<T>::to_f(DT<T>::from_f(v));
+}
+
+// Forward: one warp per query row; keys in blocks of 32 (lane j owns key j of
+// the block for the scores, and d/32 output dims for the accumulator).
+template <typename T>
+__global__ void __launch_bounds__(kSimtWarps * 32)
+    simt_fwd_kernel(const T* __restrict__ q, const T* __restrict__ k,
+                    const T* __restrict__ v, T* __restrict__ o, float* __restrict__ lse,
+                    int sq, int sk, int d, float scale, int causal) {
+  __shared__ float qs[kSimtWarps][kSimtMaxD];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t bh = blockIdx.y;
+  const int row = blockIdx.x * kSimtWarps + warp;
+  const bool active = row < sq;
+  const T* qr = q + (bh * sq + (active ? row : 0)) * (int64_t)d;
+  const T* kb = k + bh * sk * (int64_t)d;
+  const T* vb = v + bh * sk * (int64_t)d;
+  for (int j = lane; j < d; j += 32) qs[warp][j] = DT<T>::to_f(qr[j]);
+  __syncwarp();
+  constexpr int DPL = kSimtMaxD / 32;  // output dims per lane (max)
+  float acc[DPL];
+#pragma unroll
+  for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
+  float m = -INFINITY, l = 0.f;
+  const int kend = causal ? min(sk, row + 1 + (sk - sq)) : sk;
+  for (int k0 = 0; active && k0 < kend; k0 += 32) {
+    const int key = k0 + lane;
+    float s = kMaskValue;
+    if (key < sk) {
+      const T* kr = kb + (int64_t)key * d;
+      float dot = 0.f;
+      for (int j = 0; j < d; ++j) dot = fmaf(qs[warp][j], DT<T>::to_f(kr[j]), dot);
+      s = dot * scale;
+      if (causal && key > row + (sk - sq)) s = kMaskValue;
+    }
+    float bm = s;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, off));
+    const float m_new = fmaxf(m, bm);
+    float p = (key < sk) ? expf(s - m_new) : 0.f;
+    const float alpha = expf(m - m_new);
+    float ps = p;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+    l = alpha * l + ps;
+    m = m_new;
+    const float pr = round_to<T>(p);
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) acc[i] *= alpha;
+    for (int jj = 0; jj < 32; ++jj) {
+      const float pj = __shfl_sync(0xffffffffu, pr, jj);
+      const int kk = k0 + jj;
+      if (kk >= sk) break;
+      const T* vr = vb + (int64_t)kk * d;
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) {
+        const int dd = lane + 32 * i;
+        if (dd < d) acc[i] = fmaf(pj, DT<T>::to_f(vr[dd]), acc[i]);
+      }
+    }
+  }
+  if (!active) return;
+  const float inv = 1.0f / l;
+  T* orow = o + (bh * sq + row) * (int64_t)d;
+#pragma unroll
+  for (int i = 0; i < DPL; ++i) {
+    const int dd = lane + 32 * i;
+    if (dd < d) orow[dd] = DT<T>::from_f(acc[i] * inv);
+  }
+  if (lane == 0) lse[bh * sq + row] = m + logf(l);
+}
+
+// dQ: one warp per query row, keys in blocks of 32.
+template <typename T>
+__global__ void __launch_bounds__(kSimtWarps * 32)
+    simt_bwd_dq_kernel(const T* __restrict__ q, const T* __restrict__ k,
+                       const T* __restrict__ v, const T* __restrict__ dout,
+                       const float* __restrict__ lse, const float* __restrict__ delta,
+                       T* __restrict__ dq, int sq, int sk, int d, float scale, int causal) {
+  __shared__ float qs[kSimtWarps][kSimtMaxD];
+  __shared__ float ds_[kSimtWarps][kSimtMaxD];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t bh = blockIdx.y;
+  const int row = blockIdx.x * kSimtWarps + warp;
+  if (row >= sq) return;
+  const T* qr = q + (bh * sq + row) * (int64_t)d;
+  const T* dor = dout + (bh * sq + row) * (int64_t)d;
+  for (int j = lane; j < d; j += 32) {
+    qs[warp][j] = DT<T>::to_f(qr[j]);
+    ds_[warp][j] = DT<T>::to_f(dor[j]);
+  }
+  __syncwarp();
+  const float lr = lse[bh * sq + row], dl = delta[bh * sq + row];
+  const T* kb = k + bh * sk * (int64_t)d;
+  const T* vb = v + bh * sk * (int64_t)d;
+  constexpr int DPL = kSimtMaxD / 32;
+  float acc[DPL];
+#pragma unroll
+  for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
+  const int kend = causal ? min(sk, row + 1 + (sk - sq)) : sk;
+  for (int k0 = 0; k0 < kend; k0 += 32) {
+    const int key = k0 + lane;
+    float dsv = 0.f;
+    if (key < sk) {
+      const T* kr = kb + (int64_t)key * d;
+      const T* vr = vb + (int64_t)key * d;
+      float sdot = 0.f, pdot = 0.f;
+      for (int j = 0; j < d; ++j) {
+        sdot = fmaf(qs[warp][j], DT<T>::to_f(kr[j]), sdot);
+        pdot = fmaf(ds_[warp][j], DT<T>::to_f(vr[j]), pdot);
+      }
+      float s = sdot * scale;
+      if (causal && key > row + (sk - sq)) s = kMaskValue;
+      const float p = expf(s - lr);
+      dsv = round_to<T>(p * (pdot - dl));
+    }
+    for (int jj = 0; jj < 32; ++jj) {
+      const float dj = __shfl_sync(0xffffffffu, dsv, jj);
+      const int kk = k0 + jj;
+      if (kk >= sk) break;
+      const T* kr = kb + (int64_t)kk * d;
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) {
+        const int dd = lane + 32 * i;
+        if (dd < d) acc[i] = fmaf(dj, DT<T>::to_f(kr[dd]), acc[i]);
+      }
+    }
+  }
+  T* out = dq + (bh * sq + row) * (int64_t)d;
+#pragma unroll
+  for (int i = 0; i < DPL; ++i) {
+    const int dd = lane + 32 * i;
+    if (dd < d) out[dd] = DT<T>::from_f(acc[i] * scale);
+  }
+}
+
+// dK, dV: one warp per key row, queries in blocks of 32.
+template <typename T>
+__global__ void __launch_bounds__(kSimtWarps * 32)
+    simt_bwd_dkv_kernel(const T* __restrict__ q, const T* __restrict__ k,
+                        const T* __restrict__ v, const T* __restrict__ dout,
+                        const float* __restrict__ lse, const float* __restrict__ delta,
+                        T* __restrict__ dk, T* __restrict__ dv, int sq, int sk, int d,
+                        float scale, int causal) {
+  __shared__ float ks[kSimtWarps][kSimtMaxD];
+  __shared__ float vs[kSimtWarps][kSimtMaxD];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t bh = blockIdx.y;
+  const int key = blockIdx.x * kSimtWarps + warp;
+  if (key >= sk) return;
+  const T* kr = k + (bh * sk + key) * (int64_t)d;
+  const T* vr = v + (bh * sk + key) * (int64_t)d;
+  for (int j = lane; j < d; j += 32) {
+    ks[warp][j] = DT<T>::to_f(kr[j]);
+    vs[warp][j] = DT<T>::to_f(vr[j]);
+  }
+  __syncwarp();
+  const T* qb = q + bh * sq * (int64_t)d;
+  const T* db = dout + bh * sq * (int64_t)d;
+  constexpr int DPL = kSimtMaxD / 32;
+  float ak[DPL], av[DPL];
+#pragma unroll
+  for (int i = 0; i < DPL; ++i) ak[i] = av[i] = 0.f;
+  const int qstart = causal ? max(0, key - (sk - sq)) : 0;
+  for (int q0 = qstart - (qstart % 32); q0 < sq; q0 += 32) {
+    const int qi = q0 + lane;
+    float pv = 0.f, dsv = 0.f;
+    if (qi < sq && qi >= qstart) {
+      const T* qr = qb + (int64_t)qi * d;
+      const T* dr = db + (int64_t)qi * d;
+      float sdot = 0.f, pdot = 0.f;
+      for (int j = 0; j < d; ++j) {
+        sdot = fmaf(DT<T>::to_f(qr[j]), ks[warp][j], sdot);
+        pdot = fmaf(DT<T>::to_f(dr[j]), vs[warp][j], pdot);
+      }
+      float s = sdot * scale;
+      if (causal && key > qi + (sk - sq)) s = kMaskValue;
+      const float p = expf(s - lse[bh * sq + qi]);
+      pv = round_to<T>(p);
+      dsv = round_to<T>(p * (pdot - delta[bh * sq + qi]));
+    }
+    for (int jj = 0; jj < 32; ++jj) {
+      const float pj = __shfl_sync(0xffffffffu, pv, jj);
+      const float dj = __shfl_sync(0xffffffffu, dsv, jj);
+      const int qq = q0 + jj;
+      if (qq >= sq) break;
+      const T* qr = qb + (int64_t)qq * d;
+      const T* dr = db + (int64_t)qq * d;
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) {
+        const int dd = lane + 32 * i;
+        if (dd < d) {
+          av[i] = fmaf(pj, DT<T>::to_f(dr[dd]), av[i]);
+          ak[i] = fmaf(dj, DT<T>::to_f(qr[dd]), ak[i]);
+        }
+      }
+    }
+  }
+  T* okr = dk + (bh * sk + key) * (int64_t)d;
+  T* ovr = dv + (bh * sk + key) * (int64_t)d;
+#pragma unroll
+  for (int i = 0; i < DPL; ++i) {
+    const int dd = lane + 32 * i;
+    if (dd < d) {
+      okr[dd] = DT<T>::from_f(ak[i] * scale);
+      ovr[dd] = DT<T>::from_f(av[i]);
+    }
+  }
+}
+
+// ===========================================================================
+// Tensor-core forward
+// ===========================================================================
+
+constexpr int TQ = 128;  // query rows per CTA (TMEM lanes)
+constexpr int TK = 128;  // keys per KV tile
+constexpr int kFwdThreads = 192;
+
+template <int D>
+struct FwdSmem {
+  static constexpr int kChunks = D / 64;         // 128-byte swizzle chunks along d
+  static constexpr int kQBytes = TQ * D * 2;     // Q tile (K-major)
+  static constexpr int kKBytes = TK * D * 2;     // K tile (K-major)
+  static constexpr int kVBytes = TK * D * 2;     // V tile (MN-major for the B operand)
+  static constexpr int kStageBytes = kKBytes + kVBytes;
+  static constexpr int kPBytes = TQ * TK * 2;    // P tile (K-major, 2 chunks of 64 keys)
+  static constexpr int kQOff = 0;
+  static constexpr int kKVOff = kQOff + kQBytes;
+  static constexpr int kPOff = kKVOff + 2 * kStageBytes;
+  static constexpr int kBarOff = kPOff + kPBytes;
+  // q_full, kv_full[2], kv_empty[2], s_full[2], s_free[2], p_full, p_free,
+  // pv_full[2], pv_free[2]  = 15 barriers; then tmem slot + abort flag
+  static constexpr int kNumBars = 15;
+  static constexpr int kTotal = 1024 + kBarOff + kNumBars * 8 + 16;
+  // TMEM columns: S0, S1 (128 each), PV0, PV1 (D each)
+  static constexpr int kTmemCols = 512;
+};
+
+struct FwdParams {
+  int sq, sk, bh;
+  float scale_log2;  // scale * log2(e)
+  int causal;
+  void* o;
+  float* lse;
+  int nq_tiles;
+};
+
+// Byte offset of element (row, col) of a [rows x 64] bf16 K-major tile stored
+// with the 128-byte swizzle (16-byte granule index XOR row % 8).
+__device__ __forceinline__ uint32_t swz128(int row, int col_granule) {
+  return (uint32_t)(row * 128 + ((col_granule ^ (row & 7)) << 4));
+}
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kFwdThreads, 1)
+    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq,
+                       const __grid_constant__ CUtensorMap tk,
+                       const __grid_constant__ CUtensorMap tv, const FwdParams p) {
+  using L = FwdSmem<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = bars + 3;
+  uint64_t* s_full = bars + 5;
+  uint64_t* s_free = bars + 7;
+  uint64_t* p_full = bars + 9;
+  uint64_t* p_free = bars + 10;
+  uint64_t* pv_full = bars + 11;
+  uint64_t* pv_free = bars + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kNumBars);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Heaviest (last) query tiles first: causal work grows with the tile index.
+  const int qt = p.nq_tiles - 1 - (int)blockIdx.x;
+  const int bh = blockIdx.y;
+  const int q0 = qt * TQ;
+  // KV tiles this query tile needs (causal: up to and including the diagonal).
+  int n_kv = (p.sk + TK - 1) / TK;
+  if (p.causal) {
+    const int last_key = min(p.sk - 1, q0 + TQ - 1 + (p.sk - p.sq));
+    n_kv = last_key < 0 ? 0 : last_key / TK + 1;
+  }
+
+  if (threadIdx.x == 0) {
+    // arrival counts: 1 for TMA / tcgen05.commit, 4 for the softmax warps
+    mbar_init(q_full, 1);
+    mbar_init(p_full, 4);
+    mbar_init(p_free, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
+      mbar_init(&pv_full[i], 1);
+      mbar_init(&pv_free[i], 4);
+    }
+    *abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t t_s[2] = {tmem, tmem + 128};
+  const uint32_t t_pv[2] = {tmem + 256, tmem + 256 + D};
+
+  if (warp == 0) {
+    if (lane == 0 && n_kv > 0) {
+      tma_prefetch_desc(&tq);
+      tma_prefetch_desc(&tk);
+      tma_prefetch_desc(&tv);
+      uint8_t* sq_ = smem + L::kQOff;
+      mbar_arrive_expect_tx(q_full, L::kQBytes);
+#pragma unroll
+      for (int c = 0; c < L::kChunks; ++c)
+        tma_load_3d(sq_ + c * (TQ * 128), &tq, q_full, c * 64, q0, bh);
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, abort, 10)) break;
+        uint8_t* sk_ = smem + L::kKVOff + s * L::kStageBytes;
+        uint8_t* sv_ = sk_ + L::kKBytes;
+        mbar_arrive_expect_tx(&kv_full[s], L::kStageBytes);
+#pragma unroll
+        for (int c = 0; c < L::kChunks; ++c) {
+          tma_load_3d(sk_ + c * (TK * 128), &tk, &kv_full[s], c * 64, j * TK, bh);
+          tma_load_3d(sv_ + c * (TK * 128), &tv, &kv_full[s], c * 64, j * TK, bh);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && n_kv > 0) {
+      constexpr uint32_t idesc_s = make_idesc_f16(TQ, TK, BF16, false, false);
+      constexpr uint32_t idesc_o = make_idesc_f16(TQ, D, BF16, false, true);
+      const uint32_t sq_ = smem_u32(smem + L::kQOff);
+      const uint32_t sp_ = smem_u32(smem + L::kPOff);
+      bool ok = mbar_wait(q_full, 0, abort, 11);
+      auto issue_s = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait(&kv_full[s], (j >> 1) & 1, abort, 12)) return false;
+        if (!mbar_wait(&s_free[s], ((j >> 1) & 1) ^ 1, abort, 13)) return false;
+        tc_fence_after();
+        const uint32_t sk_ = smem_u32(smem + L::kKVOff + s * L::kStageBytes);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * (TQ * 128) + (kk & 3) * 32;
+          tc_mma_f16_ss(t_s[s], make_sdesc(sq_ + off, 16, 1024),
+                        make_sdesc(sk_ + (kk >> 2) * (TK * 128) + (kk & 3) * 32, 16, 1024),
+                        idesc_s, kk != 0);
+        }
+        tc_commit(&s_full[s]);
+        return true;
+      };
+      auto issue_pv = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait(p_full, j & 1, abort, 14)) return false;
+        if (!mbar_wait(&pv_free[s], ((j >> 1) & 1) ^ 1, abort, 15)) return false;
+        tc_fence_after();
+        const uint32_t sv_ = smem_u32(smem + L::kKVOff + s * L::kStageBytes + L::kKBytes);
+#pragma unroll
+        for (int kk = 0; kk < TK / 16; ++kk) {
+          const uint32_t aoff = (kk >> 2) * (TQ * 128) + (kk & 3) * 32;
+          // V tile: MN-major, d chunks of 64 at TK*128 bytes, 16 keys per step
+          tc_mma_f16_ss(t_pv[s], make_sdesc(sp_ + aoff, 16, 1024),
+                        make_sdesc(sv_ + kk * 2048, TK * 128, 1024), idesc_o, kk != 0);
+        }
+        tc_commit(&pv_full[s]);
+        tc_commit(p_free);
+        tc_commit(&kv_empty[s]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; ok && j < n_kv; ++j) {
+        if (j + 1 < n_kv) ok = issue_s(j + 1);
+        if (ok) ok = issue_pv(j);
+      }
+    }
+  } else {
+    // ------------------------------------------------ softmax warpgroup
+    const int qw = warp & 3;
+    const int r = qw * 32 + lane;  // query row within the tile == TMEM lane
+    const int qrow = q0 + r;
+    const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
+    uint8_t* sp = smem + L::kPOff;
+    float acc[D];
+#pragma unroll
+    for (int i = 0; i < D; ++i) acc[i] = 0.f;
+    float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
+    bool ok = n_kv > 0;
+    const int diag_shift = p.sk - p.sq;  // causal: key <= qrow + diag_shift
+
+    auto fold_pv = [&](int j, float alpha) -> bool {
+      const int s = j & 1;
+      if (!mbar_wait(&pv_full[s], (j >> 1) & 1, abort, 16)) return false;
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < D / 16; ++c) {
+        uint32_t v[16];
+        tmem_ld16(t_pv[s] + lane_off + c * 16, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[c * 16 + i] = fmaf(acc[c * 16 + i], alpha, __uint_as_float(v[i]));
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&pv_free[s]);
+      return true;
+    };
+
+    for (int j = 0; ok && j < n_kv; ++j) {
+      const int s = j & 1;
+      if (!mbar_wait(&s_full[s], (j >> 1) & 1, abort, 17)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const bool diag = p.causal && (j * TK + TK - 1 > q0 + diag_shift);
+      // pass 1: row max of the scaled scores (log2 domain)
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < TK / 16; ++c) {
+        uint32_t v[16];
+        tmem_ld16(t_s[s] + lane_off + c * 16, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float x = __uint_as_float(v[i]) * p.scale_log2;
+          if (diag && (j * TK + c * 16 + i > qrow + diag_shift)) x = kMaskValue;
+          mx = fmaxf(mx, x);
+        }
+      }
+      const float m_new = fmaxf(m, mx);
+      const float alpha = exp2f(m - m_new);
+      // P slot free once the previous P V MMA has read it
+      if (j > 0 && !mbar_wait(p_free, (j - 1) & 1, abort, 18)) {
+        ok = false;
+        break;
+      }
+      // pass 2: p = exp2(x - m_new), rounded to the input dtype, into smem
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < TK / 16; ++c) {
+        uint32_t v[16];
+        tmem_ld16(t_s[s] + lane_off + c * 16, v);
+        tmem_wait_ld();
+        uint32_t packed[8];
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) {
+          float x0 = __uint_as_float(v[i]) * p.scale_log2;
+          float x1 = __uint_as_float(v[i + 1]) * p.scale_log2;
+          if (diag) {
+            if (j * TK + c * 16 + i > qrow + diag_shift) x0 = kMaskValue;
+            if (j * TK + c * 16 + i + 1 > qrow + diag_shift) x1 = kMaskValue;
+          }
+          const float p0 = exp2f(x0 - m_new);
+          const float p1 = exp2f(x1 - m_new);
+          rs += p0 + p1;
+          packed[i / 2] = BF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
+        }
+        // 16 keys = 2 granules of chunk c/4 (64 keys per 128-byte row)
+        uint8_t* chunk = sp + (c >> 2) * (TQ * 128);
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          const int granule = (c & 3) * 2 + g;
+          *reinterpret_cast<uint4*>(chunk + swz128(r, granule)) =
+              make_uint4(packed[g * 4], packed[g * 4 + 1], packed[g * 4 + 2], packed[g * 4 + 3]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[s]);  // S buffer may be overwritten
+      fence_proxy_async_smem();                // P visible to the tensor core
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+      l = alpha * l + rs;
+      m = m_new;
+      // fold the previous tile's P V (overlaps this tile's P V MMA)
+      if (j > 0 && !fold_pv(j - 1, alpha_prev)) {
+        ok = false;
+        break;
+      }
+      alpha_prev = alpha;
+    }
+    if (ok && n_kv > 0) ok = fold_pv(n_kv - 1, alpha_prev);
+    if (ok && qrow < p.sq) {
+      const float inv = 1.0f / l;
+      typedef typename std::conditional<BF16, __nv_bfloat16, __half>::type T;
+      T* orow = reinterpret_cast<T*>(p.o) + ((int64_t)bh * p.sq + qrow) * D;
+#pragma unroll
+      for (int i = 0; i < D; i += 8) {
+        uint4 v;
+        if constexpr (BF16) {
+          v.x = pack_bf16x2(acc[i] * inv, acc[i + 1] * inv);
+          v.y = pack_bf16x2(acc[i + 2] * inv, acc[i + 3] * inv);
+          v.z = pack_bf16x2(acc[i + 4] * inv, acc[i + 5] * inv);
+          v.w = pack_bf16x2(acc[i + 6] * inv, acc[i + 7] * inv);
+        } else {
+          v.x = pack_f16x2(acc[i] * inv, acc[i + 1] * inv);
+          v.y = pack_f16x2(acc[i + 2] * inv, acc[i + 3] * inv);
+          v.z = pack_f16x2(acc[i + 4] * inv, acc[i + 5] * inv);
+          v.w = pack_f16x2(acc[i + 6] * inv, acc[i + 7] * inv);
+        }
+        *reinterpret_cast<uint4*>(orow + i) = v;
+      }
+      p.lse[(int64_t)bh * p.sq + qrow] = (m + log2f(l)) * kLn2;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, L::kTmemCols);
+  }
+}
+
+// ===========================================================================
+// host
+// ===========================================================================
+
+static int env_int(const char* name, int dflt) {
+  const char* s = std::getenv(name);
+  return (s && *s) ? std::atoi(s) : dflt;
+}
+
+static int validate(const char* op, int64_t b, int64_t h, int64_t sq, int64_t sk,
+                    int64_t d, int causal, int block_q, int block_k, int dtype) {
+  if (b <= 0 || h <= 0 || sq <= 0 || sk <= 0 || d <= 0)
+    return fail(FERRITE_BAD_SHAPE, "%s: non-positive shape", op);
+  if (d % 128 && d > 128)
+    return fail(FERRITE_BAD_SHAPE, "%s: head_dim must be <= 128 or a multiple of it; got %lld", op, (long long)d);
+  if (d > kSimtMaxD) return fail(FERRITE_BAD_SHAPE, "%s: head_dim %lld > %d unsupported", op, (long long)d, kSimtMaxD);
+  if (causal && sq != sk)
+    return fail(FERRITE_BAD_SHAPE, "%s: causal attention needs equal q and k sequence lengths", op);
+  if (block_q <= 0 || block_q % 8 || sq % block_q)
+    return fail(FERRITE_BAD_SHAPE, "%s: block_q=%d must be a multiple of 8 and divide %lld", op, block_q, (long long)sq);
+  if (block_k <= 0 || block_k % 128 || sk % block_k)
+    return fail(FERRITE_BAD_SHAPE, "%s: block_k=%d must be a multiple of 128 and divide %lld", op, block_k, (long long)sk);
+  if (dtype != FERRITE_F32 && dtype != FERRITE_BF16 && dtype != FERRITE_F16)
+    return fail(FERRITE_UNSUPPORTED_DTYPE, "%s: dtype %d", op, dtype);
+  if (b * h > 65535) return fail(FERRITE_BAD_SHAPE, "%s: batch*heads > 65535", op);
+  if (sq > (1 << 24) || sk > (1 << 24)) return fail(FERRITE_BAD_SHAPE, "%s: sequence too long", op);
+  return injected_fault(op);
+}
+
+static bool tc_fwd_ok(int64_t d, int64_t sk, int dtype) {
+  if (env_int("FERRITE_ATTN_FORCE_SIMT", 0)) return false;
+  return dtype != FERRITE_F32 && (d == 64 || d == 128) && sk % TK == 0;
+}
+
+template <int D, bool BF16>
+static int launch_fwd_tc(cudaStream_t s, const void* q, const void* k, const void* v,
+                         void* o, float* lse, int64_t bh, int64_t sq, int64_t sk,
+                         float scale, int causal) {
+  using L = FwdSmem<D>;
+  const CUtensorMapDataType dt = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap tq, tk, tv;
+  int rc = make_tmap_3d(&tq, q, dt, 2, D, (uint64_t)sq, (uint64_t)bh, D * 2, (uint64_t)sq * D * 2,
+                        64, TQ, 1, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc)
+    rc = make_tmap_3d(&tk, k, dt, 2, D, (uint64_t)sk, (uint64_t)bh, D * 2,
+                      (uint64_t)sk * D * 2, 64, TK, 1, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc)
+    rc = make_tmap_3d(&tv, v, dt, 2, D, (uint64_t)sk, (uint64_t)bh, D * 2,
+                      (uint64_t)sk * D * 2, 64, TK, 1, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  FwdParams p;
+  p.sq = (int)sq;
+  p.sk = (int)sk;
+  p.bh = (int)bh;
+  p.scale_log2 = scale * kLog2e;
+  p.causal = causal;
+  p.o = o;
+  p.lse = lse;
+  p.nq_tiles = (int)((sq + TQ - 1) / TQ);
+  auto kern = attn_fwd_tc_kernel<D, BF16>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+  if (e != cudaSuccess) return fail(FERRITE_LAUNCH_FAILED, "attn_fwd: smem attr: %s", cudaGetErrorString(e));
+  dim3 grid(p.nq_tiles, (unsigned)bh);
+  kern<<<grid, kFwdThreads, L::kTotal, s>>>(tq, tk, tv, p);
+  return check_launch("attn_fwd_tc");
+}
+
+template <typename T>
+static int launch_fwd_simt(cudaStream_t s, const void* q, const void* k, const void* v,
+                           void* o, float* lse, int64_t bh, int64_t sq, int64_t sk,
+                           int64_t d, float scale, int causal) {
+  dim3 grid((unsigned)((sq + kSimtWarps - 1) / kSimtWarps), (unsigned)bh);
+  simt_fwd_kernel<T><<<grid, kSimtWarps * 32, 0, s>>>((const T*)q, (const T*)k, (const T*)v,
+                                                       (T*)o, lse, (int)sq, (int)sk, (int)d,
+                                                       scale, causal);
+  return check_launch("attn_fwd_simt");
+}
+
+}  // namespace attn
+}  // namespace ferrite
+
+using namespace ferrite;
+using namespace ferrite::attn;
+
+extern "C" {
+
+int ferrite_attn_fwd(void* stream, const void* q, const void* k, const void* v, void* o,
+                     float* lse, int64_t b, int64_t h, int64_t sq, int64_t sk, int64_t d,
+                     float scale, int causal, int block_q, int block_k, int dtype) {
+  if (int rc = validate("attn_fwd", b, h, sq, sk, d, causal, block_q, block_k, dtype)) return rc;
+  if (!q || !k || !v || !o || !lse) return fail(FERRITE_BAD_SHAPE, "attn_fwd: null pointer");
+  cudaStream_t s = (cudaStream_t)stream;
+  const int64_t bh = b * h;
+  if (tc_fwd_ok(d, sk, dtype)) {
+    const bool bf = dtype == FERRITE_BF16;
+    if (d == 64) return bf ? launch_fwd_tc<64, true>(s, q, k, v, o, lse, bh, sq, sk, scale, causal)
+                           : launch_fwd_tc<64, false>(s, q, k, v, o, lse, bh, sq, sk, scale, causal);
+    return bf ? launch_fwd_tc<128, true>(s, q, k, v, o, lse, bh, sq, sk, scale, causal)
+              : launch_fwd_tc<128, false>(s, q, k, v, o, lse, bh, sq, sk, scale, causal);
+  }
+  if (dtype == FERRITE_F32) return launch_fwd_simt<float>(s, q, k, v, o, lse, bh, sq, sk, d, scale, causal);
+  if (dtype == FERRITE_BF16) return launch_fwd_simt<__nv_bfloat16>(s, q, k, v, o, lse, bh, sq, sk, d, scale, causal);
+  return launch_fwd_simt<__half>(s, q, k, v, o, lse, bh, sq, sk, d, scale, causal);
+}
+
+int ferrite_attn_bwd_prep(void* stream, const void* dout, const void* out, float* delta,
+                          int64_t b, int64_t h, int64_t s_, int64_t d, int dtype) {
+  if (int rc = injected_fault("attn_bwd_prep")) return rc;
+  if (b <= 0 || h <= 0 || s_ <= 0 || d <= 0) return fail(FERRITE_BAD_SHAPE, "attn_bwd_prep: shape");
+  if (!dout || !out || !delta) return fail(FERRITE_BAD_SHAPE, "attn_bwd_prep: null pointer");
+  cudaStream_t s = (cudaStream_t)stream;
+  const int64_t rows = b * h * s_;
+  const unsigned grid = (unsigned)((rows + 7) / 8);
+  if (dtype == FERRITE_F32)
+    bwd_prep_kernel<float><<<grid, 256, 0, s>>>((const float*)dout, (const float*)out, delta, rows, (int)d);
+  else if (dtype == FERRITE_BF16)
+    bwd_prep_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)dout, (const __nv_bfloat16*)out, delta, rows, (int)d);
+  else if (dtype == FERRITE_F16)
+    bwd_prep_kernel<__half><<<grid, 256, 0, s>>>((const __half*)dout, (const __half*)out, delta, rows, (int)d);
+  else
+    return fail(FERRITE_UNSUPPORTED_DTYPE, "attn_bwd_prep: dtype %d", dtype);
+  return check_launch("attn_bwd_prep");
+}
+
+int ferrite_attn_bwd_dkv(void* stream, const void* q, const void* k, const void* v,
+                         const void* dout, const float* lse, const float* delta, void* dk,
+                         void* dv, int64_t b, int64_t h, int64_t sq, int64_t sk, int64_t d,
+                         float scale, int causal, int block_q, int block_k, int dtype) {
+  if (int rc = validate("attn_bwd_dkv", b, h, sq, sk, d, causal, block_q, block_k, dtype)) return rc;
+  if (!q || !k || !v || !dout || !lse || !delta || !dk || !dv)
+    return fail(FERRITE_BAD_SHAPE, "attn_bwd_dkv: null pointer");
+  cudaStream_t s = (cudaStream_t)stream;
+  const int64_t bh = b * h;
+  dim3 grid((unsigned)((sk + kSimtWarps - 1) / kSimtWarps), (unsigned)bh);
+#define DKV(T)                                                                                  \
+  simt_bwd_dkv_kernel<T><<<grid, kSimtWarps * 32, 0, s>>>(                                      \
+      (const T*)q, (const T*)k, (const T*)v, (const T*)dout, lse, delta, (T*)dk, (T*)dv,        \
+      (int)sq, (int)sk, (int)d, scale, causal)
+  if (dtype == FERRITE_F32) DKV(float);
+  else if (dtype == FERRITE_BF16) DKV(__nv_bfloat16);
+  else DKV(__half);
+#undef DKV
+  return check_launch("attn_bwd_dkv_simt");
+}
+
+int ferrite_attn_bwd_dq(void* stream, const void* q, const void* k, const void* v,
+                        const void* dout, const float* lse, const float* delta, void* dq,
+                        int64_t b, int64_t h, int64_t sq, int64_t sk, int64_t d, float scale,
+                        int causal, int block_q, int block_k, int dtype) {
+  if (int rc = validate("attn_bwd_dq", b, h, sq, sk, d, causal, block_q, block_k, dtype)) return rc;
+  if (!q || !k || !v || !dout || !lse || !delta || !dq)
+    return fail(FERRITE_BAD_SHAPE, "attn_bwd_dq: null pointer");
+  cudaStream_t s = (cudaStream_t)stream;
+  const int64_t bh = b * h;
+  dim3 grid((unsigned)((sq + kSimtWarps - 1) / kSimtWarps), (unsigned)bh);
+#define DQ(T)                                                                                    \
+  simt_bwd_dq_kernel<T><<<grid, kSimtWarps * 32, 0, s>>>(                                        \
+      (const T*)q, (const T*)k, (const T*)v, (const T*)dout, lse, delta, (T*)dq, (int)sq,        \
+      (int)sk, (int)d, scale, causal)
+  if (dtype == FERRITE_F32) DQ(float);
+  else if (dtype == FERRITE_BF16) DQ(__nv_bfloat16);
+  else DQ(__half);
+#undef DQ
+  return check_launch("attn_bwd_dq_simt");
+}
+
+}  // extern "C"

@@ -9,8 +9,13 @@ namespace norm {
 // backward
 // ---------------------------------------------------------------------------
 
+// Persistent backward.  Each row group walks rows r0, r0 + G, ... (G = row
+// groups in the grid).  The next row's h, dy and dh_direct are loaded as raw
+// 16-byte vectors before the current row is reduced, so one row's loads are
+// always in flight while the previous row is reduced and written; the weight
+// dw partial stays in registers for the whole kernel.
 template <typename T, typename TW, bool HAS_DH, int VPT, int TPR, int CTA>
-__global__ void __launch_bounds__(CTA)
+__global__ void __launch_bounds__(CTA, CTA <= 512 ? 2 : 1)
     rmsnorm_bwd_kernel(const T* __restrict__ h, const TW* __restrict__ w,
                        const T* __restrict__ dy, const T* __restrict__ dh_direct,
                        T* __restrict__ dh, float* __restrict__ partial,
@@ -29,34 +34,53 @@ __global__ void __launch_bounds__(CTA)
 #pragma unroll
     for (int j = 0; j < VE; ++j) dwp[i][j] = 0.f;
   }
+  // The weight slice is re-read from L1 every row (16 KiB, shared by all rows).
+  auto weights = [&](int i, float (&wv)[VE]) {
+    const int vi = i * TPR + t;
+    if (vi < nvec) {
+      load_w<TW, VE>(w, (int64_t)vi * VE, wv);
+    } else {
+#pragma unroll
+      for (int j = 0; j < VE; ++j) wv[j] = 0.f;
+    }
+  };
 
   const int64_t groups_total = (int64_t)gridDim.x * RPC;
-  // Every thread of the CTA runs the same number of iterations (the shared
-  // reduction needs all of them); rows past the end are masked.
+  const int64_t first = (int64_t)blockIdx.x * RPC + grp;
+  // Every thread runs the same number of iterations (the shared reduction needs
+  // all of them); rows past the end are masked.
   const int64_t iters = (rows + groups_total - 1) / groups_total;
-  for (int64_t it = 0; it < iters; ++it) {
-    const int64_t row = it * groups_total + (int64_t)blockIdx.x * RPC + grp;
-    const bool active = row < rows;
-    const int64_t base = row * (int64_t)dim;
-    float hv[VPT][VE], gv[VPT][VE];
-    float s2[2] = {0.f, 0.f};  // sum h^2, sum dy*w*h
+  uint4 ch[VPT], cg[VPT], cd[VPT];  // current row, raw
+  uint4 nh[VPT], ng[VPT], nd[VPT];  // next row, raw
+  auto load_row = [&](int64_t row, uint4 (&rh)[VPT], uint4 (&rg)[VPT], uint4 (&rd)[VPT]) {
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const int vi = i * TPR + t;
-      if (active && vi < nvec) {
-        const int64_t e = base + (int64_t)vi * VE;
-        Vec<T>::to_f(ld_stream_v4(h + e), hv[i]);
-        Vec<T>::to_f(ld_stream_v4(dy + e), gv[i]);
-        float wv[VE];
-        load_w<TW, VE>(w, (int64_t)vi * VE, wv);  // L1-resident
-#pragma unroll
-        for (int j = 0; j < VE; ++j) {
-          s2[0] = fmaf(hv[i][j], hv[i][j], s2[0]);
-          s2[1] = fmaf(gv[i][j] * wv[j], hv[i][j], s2[1]);
-        }
+      if (row < rows && vi < nvec) {
+        const int64_t e = row * (int64_t)dim + (int64_t)vi * VE;
+        rh[i] = ld_stream_v4(h + e);
+        rg[i] = ld_stream_v4(dy + e);
+        if constexpr (HAS_DH) rd[i] = ld_stream_v4(dh_direct + e);
       } else {
+        rh[i] = rg[i] = rd[i] = make_uint4(0, 0, 0, 0);
+      }
+    }
+  };
+  load_row(first, ch, cg, cd);
+  for (int64_t it = 0; it < iters; ++it) {
+    const int64_t row = first + it * groups_total;
+    if (it + 1 < iters) load_row(row + groups_total, nh, ng, nd);
+    float s2[2] = {0.f, 0.f};  // sum h^2, sum dy*w*h
 #pragma unroll
-        for (int j = 0; j < VE; ++j) hv[i][j] = gv[i][j] = 0.f;
+    for (int i = 0; i < VPT; ++i) {
+      float hv[VE], gv[VE], wv[VE];
+      Vec<T>::to_f(ch[i], hv);
+      Vec<T>::to_f(cg[i], gv);
+      weights(i, wv);
+#pragma unroll
+      for (int j = 0; j < VE; ++j) {
+        s2[0] = fmaf(hv[j], hv[j], s2[0]);
+        s2[1] = fmaf(gv[j] * wv[j], hv[j], s2[1]);
       }
     }
     if constexpr (TPR > 32) {
@@ -67,29 +91,33 @@ __global__ void __launch_bounds__(CTA)
     const float inv = rsqrtf(s2[0] * inv_dim + eps);
     // mean(g * xhat) = inv * mean(dy*w*h)
     const float c = inv * s2[1] * inv_dim;
-    if (active) {
+    if (row < rows) {
 #pragma unroll
       for (int i = 0; i < VPT; ++i) {
         const int vi = i * TPR + t;
         if (vi < nvec) {
-          const int64_t e = base + (int64_t)vi * VE;
-          float dd[VE];
-          if constexpr (HAS_DH) Vec<T>::to_f(ld_stream_v4(dh_direct + e), dd);
-          float wv[VE];
-          load_w<TW, VE>(w, (int64_t)vi * VE, wv);
-          float o[VE];
+          float hv[VE], gv[VE], dd[VE], o[VE], wv[VE];
+          Vec<T>::to_f(ch[i], hv);
+          Vec<T>::to_f(cg[i], gv);
+          weights(i, wv);
+          if constexpr (HAS_DH) Vec<T>::to_f(cd[i], dd);
 #pragma unroll
           for (int j = 0; j < VE; ++j) {
-            const float xhat = hv[i][j] * inv;
-            const float g = gv[i][j] * wv[j];
-            dwp[i][j] = fmaf(gv[i][j], xhat, dwp[i][j]);
-            float v = inv * (g - xhat * c);
+            const float xhat = hv[j] * inv;
+            dwp[i][j] = fmaf(gv[j], xhat, dwp[i][j]);
+            float v = inv * (gv[j] * wv[j] - xhat * c);
             if constexpr (HAS_DH) v += dd[j];
             o[j] = v;
           }
-          st_v4(dh + e, Vec<T>::from_f(o));
+          st_v4(dh + row * (int64_t)dim + (int64_t)vi * VE, Vec<T>::from_f(o));
         }
       }
+    }
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      ch[i] = nh[i];
+      cg[i] = ng[i];
+      cd[i] = nd[i];
     }
   }
 
@@ -170,23 +198,33 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// dw[e] = sum_p partial[p][e], fixed summation order.
+// dw[e] = sum_p partial[p][e] in a fixed order (bitwise deterministic).  A CTA
+// owns 32 columns; its 8 warps each sum every 8th partial row (coalesced 128-byte
+// rows), then warp 0 adds the 8 results in order.
 template <typename TW>
 __global__ void __launch_bounds__(256)
     dw_reduce_kernel(const float* __restrict__ partial, TW* __restrict__ dw,
                      int nparts, int dim) {
-  const int e = blockIdx.x * 256 + threadIdx.x;
-  if (e >= dim) return;
-  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-  int p = 0;
-  for (; p + 4 <= nparts; p += 4) {
-    s0 += partial[(int64_t)p * dim + e];
-    s1 += partial[(int64_t)(p + 1) * dim + e];
-    s2 += partial[(int64_t)(p + 2) * dim + e];
-    s3 += partial[(int64_t)(p + 3) * dim + e];
+  __shared__ float sm[8][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int e = blockIdx.x * 32 + tx;
+  float s0 = 0.f, s1 = 0.f;
+  if (e < dim) {
+    int p = ty;
+    for (; p + 8 < nparts; p += 16) {
+      s0 += partial[(int64_t)p * dim + e];
+      s1 += partial[(int64_t)(p + 8) * dim + e];
+    }
+    if (p < nparts) s0 += partial[(int64_t)p * dim + e];
   }
-  for (; p < nparts; ++p) s0 += partial[(int64_t)p * dim + e];
-  dw[e] = DT<TW>::from_f((s0 + s1) + (s2 + s3));
+  sm[ty][tx] = s0 + s1;
+  __syncthreads();
+  if (ty == 0 && e < dim) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += sm[k][tx];
+    dw[e] = DT<TW>::from_f(t);
+  }
 }
 
 // Persistent grid of the backward kernel and the resulting partial count.
@@ -301,7 +339,7 @@ static int run_bwd(cudaStream_t s, const void* h, const void* w, const void* dy,
         (float*)ws, rows, (int)dim, eps);
   }
   if (int rc = check_launch("rmsnorm_bwd")) return rc;
-  dw_reduce_kernel<TW><<<(unsigned)((dim + 255) / 256), 256, 0, s>>>(
+  dw_reduce_kernel<TW><<<(unsigned)((dim + 31) / 32), 256, 0, s>>>(
       (const float*)ws, (TW*)dw, p.nparts, (int)dim);
   return check_launch("rmsnorm_dw_reduce");
 }

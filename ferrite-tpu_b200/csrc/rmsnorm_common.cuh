@@ -146,7 +146,7 @@ static Cfg pick(int64_t dim, int elem, const void* const* ptrs, int nptr,
   for (int i = 0; i < nptr; ++i)
     if (ptrs[i] && (reinterpret_cast<uintptr_t>(ptrs[i]) & 15u)) return c;
   const int64_t nvec = dim / ve;
-  int pref = env_int(bwd ? "FERRITE_RMSNORM_BWD_VPT" : "FERRITE_RMSNORM_VPT", 2);
+  int pref = bwd ? env_int("FERRITE_RMSNORM_BWD_VPT", 1) : env_int("FERRITE_RMSNORM_VPT", 2);
   if (pref != 1 && pref != 2 && pref != 4) pref = 2;
   const int order[3][3] = {{1, 2, 4}, {2, 4, 1}, {4, 2, 1}};
   const int* ord = order[pref == 1 ? 0 : (pref == 2 ? 1 : 2)];
