@@ -137,8 +137,9 @@ class ClockSampler:
                 if val.lower() == "active":
                     reasons.add(name)
         out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
-        if not sm and self.err:
-            out["error"] = self.err
+        if not sm:
+            out["error"] = self.err or "no parsable samples"
+            out["raw"] = self.lines[:2]
         return out
 
 

@@ -597,6 +597,361 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 }
 
 // ===========================================================================
+// Tensor-core backward: one kernel template for dK/dV and for dQ
+// ===========================================================================
+//
+// A CTA keeps a 128-row "stationary" pair X1, X2 in shared memory and sweeps
+// 64-row "streaming" tiles Y1, Y2 (2-slot TMA ring):
+//   dK/dV (IS_DKV): X1 = K, X2 = V (128 keys);  Y1 = Q, Y2 = dO (64 queries)
+//   dQ            : X1 = Q, X2 = dO (128 queries); Y1 = K, Y2 = V (64 keys)
+// Per streaming tile (warp 1, one lane, kind::f16, f32 accumulators in TMEM):
+//   T1 = X1 Y1^T   (dK/dV: S^T;  dQ: S)      128 x 64, two TMEM buffers
+//   T2 = X2 Y2^T   (dK/dV: dP^T; dQ: dP)     128 x 64, two TMEM buffers
+// then the elementwise warpgroup (one thread per X row = TMEM lane) forms
+//   P = exp(scale*S - lse) (causal mask with the finite MASK_VALUE),
+//   dS = P * (dP - delta),
+// rounds both to the input dtype (flash_attention.py:210-211, :234) into
+// 128-byte-swizzled K-major shared tiles, and warp 1 accumulates
+//   dK/dV: dV += P^T dO, dK += dS^T Q      (B operands = the same Y tiles read
+//   dQ   : dQ += dS K                        MN-major: no transposed copies)
+// After the last tile the warpgroup scales dK / dQ by `scale`
+// (flash_attention.py:220, :243) and stores.  No atomics: each CTA owns its
+// output rows (grids of flash_attention.py:253-306).
+
+constexpr int BX = 128;  // stationary rows
+constexpr int BY = 64;   // streaming rows
+constexpr int kBwdThreads = 192;
+
+template <int D>
+struct BwdSmem {
+  static constexpr int kChunks = D / 64;
+  static constexpr int kXBytes = BX * D * 2;  // one stationary tile
+  static constexpr int kYBytes = BY * D * 2;  // one streaming tile
+  static constexpr int kStageBytes = 2 * kYBytes;
+  static constexpr int kEBytes = BX * BY * 2;  // one P or dS tile (bf16)
+  static constexpr int kX1Off = 0;
+  static constexpr int kX2Off = kXBytes;
+  static constexpr int kYOff = 2 * kXBytes;
+  static constexpr int kEOff = kYOff + 2 * kStageBytes;  // [buf][P, dS]
+  static constexpr int kStatOff = kEOff + 2 * 2 * kEBytes;  // per-warp lse/delta (4 x 128 floats)
+  static constexpr int kBarOff = kStatOff + 4 * 128 * 4;
+  // x_full, y_full[2], y_empty[2], t_full[2], t_free[2], e_full[2], e_free[2], acc_full
+  static constexpr int kNumBars = 14;
+  static constexpr int kTotal = 1024 + kBarOff + kNumBars * 8 + 16;
+};
+
+struct BwdParams {
+  int sq, sk;
+  float scale;
+  float scale_log2;
+  int causal;
+  const float* lse;
+  const float* delta;
+  void* out0;  // dK/dV: dK; dQ: dQ
+  void* out1;  // dK/dV: dV
+  int n_x_tiles;
+};
+
+template <int D, bool BF16, bool IS_DKV>
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tx1, const __grid_constant__ CUtensorMap tx2,
+                       const __grid_constant__ CUtensorMap ty1, const __grid_constant__ CUtensorMap ty2,
+                       const BwdParams p) {
+  using L = BwdSmem<D>;
+  typedef typename std::conditional<BF16, __nv_bfloat16, __half>::type T;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* x_full = bars + 0;
+  uint64_t* y_full = bars + 1;
+  uint64_t* y_empty = bars + 3;
+  uint64_t* t_full = bars + 5;
+  uint64_t* t_free = bars + 7;
+  uint64_t* e_full = bars + 9;
+  uint64_t* e_free = bars + 11;
+  uint64_t* acc_full = bars + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kNumBars);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int xt = p.n_x_tiles - 1 - (int)blockIdx.x;  // heaviest tiles first
+  const int bh = blockIdx.y;
+  const int x0 = xt * BX;
+  const int x_len = IS_DKV ? p.sk : p.sq;  // rows of the stationary operand
+  const int y_len = IS_DKV ? p.sq : p.sk;  // rows of the streaming operand
+  const int diag_shift = p.sk - p.sq;      // causal: key <= query + diag_shift
+  // Streaming tiles [j0, j1) this CTA needs.
+  int j0 = 0, j1 = (y_len + BY - 1) / BY;
+  if (p.causal) {
+    if (IS_DKV) {
+      const int q_first = max(0, x0 - diag_shift);  // first query that sees key x0
+      j0 = q_first / BY;
+    } else {
+      const int last_key = min(p.sk - 1, x0 + BX - 1 + diag_shift);
+      j1 = last_key < 0 ? 0 : last_key / BY + 1;
+    }
+  }
+  const int n_y = max(0, j1 - j0);
+
+  if (threadIdx.x == 0) {
+    mbar_init(x_full, 1);
+    mbar_init(acc_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&y_full[i], 1);
+      mbar_init(&y_empty[i], 1);
+      mbar_init(&t_full[i], 1);
+      mbar_init(&t_free[i], 4);
+      mbar_init(&e_full[i], 4);
+      mbar_init(&e_free[i], 1);
+    }
+    *abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // TMEM columns: T1[2] at 0/64, T2[2] at 128/192, acc0 at 256, acc1 at 256 + D
+  const uint32_t t_t1[2] = {tmem, tmem + 64};
+  const uint32_t t_t2[2] = {tmem + 128, tmem + 192};
+  const uint32_t t_acc0 = tmem + 256;
+  const uint32_t t_acc1 = tmem + 256 + D;
+
+  if (warp == 0) {
+    if (lane == 0 && n_y > 0) {
+      tma_prefetch_desc(&tx1);
+      tma_prefetch_desc(&tx2);
+      tma_prefetch_desc(&ty1);
+      tma_prefetch_desc(&ty2);
+      mbar_arrive_expect_tx(x_full, 2 * L::kXBytes);
+#pragma unroll
+      for (int c = 0; c < L::kChunks; ++c) {
+        tma_load_3d(smem + L::kX1Off + c * (BX * 128), &tx1, x_full, c * 64, x0, bh);
+        tma_load_3d(smem + L::kX2Off + c * (BX * 128), &tx2, x_full, c * 64, x0, bh);
+      }
+      for (int i = 0; i < n_y; ++i) {
+        const int s = i & 1;
+        if (!mbar_wait(&y_empty[s], ((i >> 1) & 1) ^ 1, abort, 20)) break;
+        uint8_t* y1 = smem + L::kYOff + s * L::kStageBytes;
+        uint8_t* y2 = y1 + L::kYBytes;
+        mbar_arrive_expect_tx(&y_full[s], L::kStageBytes);
+        const int yrow = (j0 + i) * BY;
+#pragma unroll
+        for (int c = 0; c < L::kChunks; ++c) {
+          tma_load_3d(y1 + c * (BY * 128), &ty1, &y_full[s], c * 64, yrow, bh);
+          tma_load_3d(y2 + c * (BY * 128), &ty2, &y_full[s], c * 64, yrow, bh);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && n_y > 0) {
+      constexpr uint32_t idesc_t = make_idesc_f16(BX, BY, BF16, false, false);
+      constexpr uint32_t idesc_a = make_idesc_f16(BX, D, BF16, false, true);
+      const uint32_t sx1 = smem_u32(smem + L::kX1Off);
+      const uint32_t sx2 = smem_u32(smem + L::kX2Off);
+      bool ok = mbar_wait(x_full, 0, abort, 21);
+      auto issue_t = [&](int i) -> bool {
+        const int s = i & 1;
+        if (!mbar_wait(&y_full[s], (i >> 1) & 1, abort, 22)) return false;
+        if (!mbar_wait(&t_free[s], ((i >> 1) & 1) ^ 1, abort, 23)) return false;
+        tc_fence_after();
+        const uint32_t sy1 = smem_u32(smem + L::kYOff + s * L::kStageBytes);
+        const uint32_t sy2 = sy1 + L::kYBytes;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t xo = (kk >> 2) * (BX * 128) + (kk & 3) * 32;
+          const uint32_t yo = (kk >> 2) * (BY * 128) + (kk & 3) * 32;
+          tc_mma_f16_ss(t_t1[s], make_sdesc(sx1 + xo, 16, 1024), make_sdesc(sy1 + yo, 16, 1024), idesc_t, kk != 0);
+          tc_mma_f16_ss(t_t2[s], make_sdesc(sx2 + xo, 16, 1024), make_sdesc(sy2 + yo, 16, 1024), idesc_t, kk != 0);
+        }
+        tc_commit(&t_full[s]);
+        return true;
+      };
+      auto issue_acc = [&](int i) -> bool {
+        const int s = i & 1;
+        if (!mbar_wait(&e_full[s], (i >> 1) & 1, abort, 24)) return false;
+        tc_fence_after();
+        const uint32_t sy1 = smem_u32(smem + L::kYOff + s * L::kStageBytes);
+        const uint32_t sy2 = sy1 + L::kYBytes;
+        const uint32_t sP = smem_u32(smem + L::kEOff + s * 2 * L::kEBytes);
+        const uint32_t sdS = sP + L::kEBytes;
+#pragma unroll
+        for (int kk = 0; kk < BY / 16; ++kk) {
+          const uint32_t eo = kk * 32;            // K-major [128 x 64] tile, 16-col steps
+          const uint32_t yo = kk * 2048;          // MN-major Y: 16 rows per step
+          const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+          if constexpr (IS_DKV) {
+            // dV += P^T dO   (acc1),   dK += dS^T Q  (acc0)
+            tc_mma_f16_ss(t_acc1, make_sdesc(sP + eo, 16, 1024), make_sdesc(sy2 + yo, BY * 128, 1024), idesc_a, acc);
+            tc_mma_f16_ss(t_acc0, make_sdesc(sdS + eo, 16, 1024), make_sdesc(sy1 + yo, BY * 128, 1024), idesc_a, acc);
+          } else {
+            // dQ += dS K  (acc0)
+            tc_mma_f16_ss(t_acc0, make_sdesc(sdS + eo, 16, 1024), make_sdesc(sy1 + yo, BY * 128, 1024), idesc_a, acc);
+          }
+        }
+        tc_commit(&e_free[s]);
+        tc_commit(&y_empty[s]);
+        return true;
+      };
+      if (ok) ok = issue_t(0);
+      for (int i = 0; ok && i < n_y; ++i) {
+        if (i + 1 < n_y) ok = issue_t(i + 1);
+        if (ok) ok = issue_acc(i);
+      }
+      tc_commit(acc_full);
+    }
+  } else {
+    // ------------------------------------------------ elementwise warpgroup
+    const int qw = warp & 3;
+    const int r = qw * 32 + lane;  // stationary row == TMEM lane
+    const int xrow = x0 + r;
+    const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
+    float* stat = reinterpret_cast<float*>(smem + L::kStatOff) + qw * 128;  // [lse2 x64][delta x64]
+    // dQ: this row's statistics (rows past sq are masked below)
+    float row_lse2 = 0.f, row_delta = 0.f;
+    if (!IS_DKV && xrow < p.sq) {
+      row_lse2 = p.lse[(int64_t)bh * p.sq + xrow] * kLog2e;
+      row_delta = p.delta[(int64_t)bh * p.sq + xrow];
+    }
+    bool ok = n_y > 0;
+    for (int i = 0; ok && i < n_y; ++i) {
+      const int s = i & 1;
+      const int y0 = (j0 + i) * BY;
+      if constexpr (IS_DKV) {
+        // stage the 64 queries' lse (log2 domain) and delta for this warp
+        __syncwarp();
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int c = lane + 32 * h2;
+          const int qi = y0 + c;
+          const bool in = qi < p.sq;
+          stat[c] = in ? p.lse[(int64_t)bh * p.sq + qi] * kLog2e : 0.f;
+          stat[64 + c] = in ? p.delta[(int64_t)bh * p.sq + qi] : 0.f;
+        }
+        __syncwarp();
+      }
+      if (!mbar_wait(&t_full[s], (i >> 1) & 1, abort, 25)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (i >= 2 && !mbar_wait(&e_free[s], ((i >> 1) & 1) ^ 1, abort, 26)) {
+        ok = false;
+        break;
+      }
+      uint8_t* sP = smem + L::kEOff + s * 2 * L::kEBytes;
+      uint8_t* sdS = sP + L::kEBytes;
+#pragma unroll
+      for (int c16 = 0; c16 < BY / 16; ++c16) {
+        uint32_t a[16], b[16];
+        tmem_ld16(t_t1[s] + lane_off + c16 * 16, a);
+        tmem_ld16(t_t2[s] + lane_off + c16 * 16, b);
+        tmem_wait_ld();
+        uint32_t pp[8], dd[8];
+#pragma unroll
+        for (int e = 0; e < 16; e += 2) {
+          float pv[2], dv[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int c = c16 * 16 + e + u;  // streaming column
+            const int ycol = y0 + c;
+            int key, qry;
+            float l2, dl;
+            if constexpr (IS_DKV) {
+              key = xrow;
+              qry = ycol;
+              l2 = stat[c];
+              dl = stat[64 + c];
+            } else {
+              key = ycol;
+              qry = xrow;
+              l2 = row_lse2;
+              dl = row_delta;
+            }
+            float x = __uint_as_float(a[e + u]) * p.scale_log2;
+            const bool valid = qry < p.sq && !(p.causal && key > qry + diag_shift);
+            const float pr = valid ? exp2f(x - l2) : 0.f;
+            pv[u] = pr;
+            dv[u] = pr * (__uint_as_float(b[e + u]) - dl);
+          }
+          pp[e / 2] = BF16 ? pack_bf16x2(pv[0], pv[1]) : pack_f16x2(pv[0], pv[1]);
+          dd[e / 2] = BF16 ? pack_bf16x2(dv[0], dv[1]) : pack_f16x2(dv[0], dv[1]);
+        }
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          const int granule = c16 * 2 + g;
+          if constexpr (IS_DKV)
+            *reinterpret_cast<uint4*>(sP + swz128(r, granule)) = make_uint4(pp[g * 4], pp[g * 4 + 1], pp[g * 4 + 2], pp[g * 4 + 3]);
+          *reinterpret_cast<uint4*>(sdS + swz128(r, granule)) = make_uint4(dd[g * 4], dd[g * 4 + 1], dd[g * 4 + 2], dd[g * 4 + 3]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&t_free[s]);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&e_full[s]);
+    }
+    // epilogue: scaled accumulators -> global
+    if (ok && n_y > 0 && mbar_wait(acc_full, 0, abort, 27)) {
+      tc_fence_after();
+      const bool row_ok = xrow < x_len;
+      T* o0 = reinterpret_cast<T*>(p.out0) + ((int64_t)bh * x_len + xrow) * D;
+      T* o1 = IS_DKV ? reinterpret_cast<T*>(p.out1) + ((int64_t)bh * x_len + xrow) * D : nullptr;
+#pragma unroll
+      for (int c16 = 0; c16 < D / 16; ++c16) {
+        uint32_t a[16];
+        tmem_ld16(t_acc0 + lane_off + c16 * 16, a);
+        tmem_wait_ld();
+        if (row_ok) {
+          uint32_t pk[8];
+#pragma unroll
+          for (int e = 0; e < 16; e += 2) {
+            const float v0 = __uint_as_float(a[e]) * p.scale, v1 = __uint_as_float(a[e + 1]) * p.scale;
+            pk[e / 2] = BF16 ? pack_bf16x2(v0, v1) : pack_f16x2(v0, v1);
+          }
+          *reinterpret_cast<uint4*>(o0 + c16 * 16) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          *reinterpret_cast<uint4*>(o0 + c16 * 16 + 8) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        }
+        if constexpr (IS_DKV) {
+          tmem_ld16(t_acc1 + lane_off + c16 * 16, a);
+          tmem_wait_ld();
+          if (row_ok) {
+            uint32_t pk[8];
+#pragma unroll
+            for (int e = 0; e < 16; e += 2) {
+              pk[e / 2] = BF16 ? pack_bf16x2(__uint_as_float(a[e]), __uint_as_float(a[e + 1]))
+                               : pack_f16x2(__uint_as_float(a[e]), __uint_as_float(a[e + 1]));
+            }
+            *reinterpret_cast<uint4*>(o1 + c16 * 16) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            *reinterpret_cast<uint4*>(o1 + c16 * 16 + 8) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          }
+        }
+      }
+    } else if (ok && n_y == 0 && xrow < x_len) {
+      // no streaming tile reaches these rows (cannot happen for causal sq == sk): zeros
+      T* o0 = reinterpret_cast<T*>(p.out0) + ((int64_t)bh * x_len + xrow) * D;
+      for (int c = 0; c < D; ++c) o0[c] = DT<T>::from_f(0.f);
+      if constexpr (IS_DKV) {
+        T* o1 = reinterpret_cast<T*>(p.out1) + ((int64_t)bh * x_len + xrow) * D;
+        for (int c = 0; c < D; ++c) o1[c] = DT<T>::from_f(0.f);
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ===========================================================================
 // host
 // ===========================================================================
 
@@ -661,6 +1016,57 @@ static int launch_fwd_tc(cudaStream_t s, const void* q, const void* k, const voi
   dim3 grid(p.nq_tiles, (unsigned)bh);
   kern<<<grid, kFwdThreads, L::kTotal, s>>>(tq, tk, tv, p);
   return check_launch("attn_fwd_tc");
+}
+
+template <int D, bool BF16, bool IS_DKV>
+static int launch_bwd_tc(cudaStream_t s, const void* q, const void* k, const void* v,
+                         const void* dout, const float* lse, const float* delta, void* out0,
+                         void* out1, int64_t bh, int64_t sq, int64_t sk, float scale,
+                         int causal) {
+  using L = BwdSmem<D>;
+  const CUtensorMapDataType dt = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  // stationary pair (128-row boxes) and streaming pair (64-row boxes)
+  const void* x1 = IS_DKV ? k : q;
+  const void* x2 = IS_DKV ? v : dout;
+  const void* y1 = IS_DKV ? q : k;
+  const void* y2 = IS_DKV ? dout : v;
+  const int64_t xs = IS_DKV ? sk : sq, ys = IS_DKV ? sq : sk;
+  CUtensorMap tx1, tx2, ty1, ty2;
+  int rc = make_tmap_3d(&tx1, x1, dt, 2, D, (uint64_t)xs, (uint64_t)bh, D * 2, (uint64_t)xs * D * 2, 64, BX, 1, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc) rc = make_tmap_3d(&tx2, x2, dt, 2, D, (uint64_t)xs, (uint64_t)bh, D * 2, (uint64_t)xs * D * 2, 64, BX, 1, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc) rc = make_tmap_3d(&ty1, y1, dt, 2, D, (uint64_t)ys, (uint64_t)bh, D * 2, (uint64_t)ys * D * 2, 64, BY, 1, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc) rc = make_tmap_3d(&ty2, y2, dt, 2, D, (uint64_t)ys, (uint64_t)bh, D * 2, (uint64_t)ys * D * 2, 64, BY, 1, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  BwdParams p;
+  p.sq = (int)sq;
+  p.sk = (int)sk;
+  p.scale = scale;
+  p.scale_log2 = scale * kLog2e;
+  p.causal = causal;
+  p.lse = lse;
+  p.delta = delta;
+  p.out0 = out0;
+  p.out1 = out1;
+  p.n_x_tiles = (int)((xs + BX - 1) / BX);
+  auto kern = attn_bwd_tc_kernel<D, BF16, IS_DKV>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+  if (e != cudaSuccess) return fail(FERRITE_LAUNCH_FAILED, "attn_bwd: smem attr: %s", cudaGetErrorString(e));
+  dim3 grid(p.n_x_tiles, (unsigned)bh);
+  kern<<<grid, kBwdThreads, L::kTotal, s>>>(tx1, tx2, ty1, ty2, p);
+  return check_launch(IS_DKV ? "attn_bwd_dkv_tc" : "attn_bwd_dq_tc");
+}
+
+template <bool IS_DKV>
+static int dispatch_bwd_tc(cudaStream_t s, const void* q, const void* k, const void* v,
+                           const void* dout, const float* lse, const float* delta, void* out0,
+                           void* out1, int64_t bh, int64_t sq, int64_t sk, int64_t d,
+                           float scale, int causal, int dtype) {
+  const bool bf = dtype == FERRITE_BF16;
+  if (d == 64)
+    return bf ? launch_bwd_tc<64, true, IS_DKV>(s, q, k, v, dout, lse, delta, out0, out1, bh, sq, sk, scale, causal)
+              : launch_bwd_tc<64, false, IS_DKV>(s, q, k, v, dout, lse, delta, out0, out1, bh, sq, sk, scale, causal);
+  return bf ? launch_bwd_tc<128, true, IS_DKV>(s, q, k, v, dout, lse, delta, out0, out1, bh, sq, sk, scale, causal)
+            : launch_bwd_tc<128, false, IS_DKV>(s, q, k, v, dout, lse, delta, out0, out1, bh, sq, sk, scale, causal);
 }
 
 template <typename T>
@@ -729,6 +1135,8 @@ int ferrite_attn_bwd_dkv(void* stream, const void* q, const void* k, const void*
     return fail(FERRITE_BAD_SHAPE, "attn_bwd_dkv: null pointer");
   cudaStream_t s = (cudaStream_t)stream;
   const int64_t bh = b * h;
+  if (tc_fwd_ok(d, sk, dtype) && !env_int("FERRITE_ATTN_BWD_FORCE_SIMT", 0))
+    return dispatch_bwd_tc<true>(s, q, k, v, dout, lse, delta, dk, dv, bh, sq, sk, d, scale, causal, dtype);
   dim3 grid((unsigned)((sk + kSimtWarps - 1) / kSimtWarps), (unsigned)bh);
 #define DKV(T)                                                                                  \
   simt_bwd_dkv_kernel<T><<<grid, kSimtWarps * 32, 0, s>>>(                                      \
@@ -750,6 +1158,8 @@ int ferrite_attn_bwd_dq(void* stream, const void* q, const void* k, const void* 
     return fail(FERRITE_BAD_SHAPE, "attn_bwd_dq: null pointer");
   cudaStream_t s = (cudaStream_t)stream;
   const int64_t bh = b * h;
+  if (tc_fwd_ok(d, sk, dtype) && !env_int("FERRITE_ATTN_BWD_FORCE_SIMT", 0))
+    return dispatch_bwd_tc<false>(s, q, k, v, dout, lse, delta, dq, nullptr, bh, sq, sk, d, scale, causal, dtype);
   dim3 grid((unsigned)((sq + kSimtWarps - 1) / kSimtWarps), (unsigned)bh);
 #define DQ(T)                                                                                    \
   simt_bwd_dq_kernel<T><<<grid, kSimtWarps * 32, 0, s>>>(                                        \

@@ -199,30 +199,33 @@ __global__ void __launch_bounds__(256)
 }
 
 // dw[e] = sum_p partial[p][e] in a fixed order (bitwise deterministic).  A CTA
-// owns 32 columns; its 8 warps each sum every 8th partial row (coalesced 128-byte
-// rows), then warp 0 adds the 8 results in order.
+// owns 32 columns; its 32 warps each sum every 32nd partial row (coalesced
+// 128-byte rows, four independent loads in flight per thread), then warp 0 adds
+// the 32 warp results in order.
 template <typename TW>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(1024)
     dw_reduce_kernel(const float* __restrict__ partial, TW* __restrict__ dw,
                      int nparts, int dim) {
-  __shared__ float sm[8][33];
+  __shared__ float sm[32][33];
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const int e = blockIdx.x * 32 + tx;
-  float s0 = 0.f, s1 = 0.f;
+  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
   if (e < dim) {
     int p = ty;
-    for (; p + 8 < nparts; p += 16) {
-      s0 += partial[(int64_t)p * dim + e];
-      s1 += partial[(int64_t)(p + 8) * dim + e];
+    for (; p + 96 < nparts; p += 128) {
+      a0 += partial[(int64_t)p * dim + e];
+      a1 += partial[(int64_t)(p + 32) * dim + e];
+      a2 += partial[(int64_t)(p + 64) * dim + e];
+      a3 += partial[(int64_t)(p + 96) * dim + e];
     }
-    if (p < nparts) s0 += partial[(int64_t)p * dim + e];
+    for (; p < nparts; p += 32) a0 += partial[(int64_t)p * dim + e];
   }
-  sm[ty][tx] = s0 + s1;
+  sm[ty][tx] = (a0 + a1) + (a2 + a3);
   __syncthreads();
   if (ty == 0 && e < dim) {
     float t = 0.f;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) t += sm[k][tx];
+    for (int k = 0; k < 32; ++k) t += sm[k][tx];
     dw[e] = DT<TW>::from_f(t);
   }
 }
@@ -339,7 +342,7 @@ static int run_bwd(cudaStream_t s, const void* h, const void* w, const void* dy,
         (float*)ws, rows, (int)dim, eps);
   }
   if (int rc = check_launch("rmsnorm_bwd")) return rc;
-  dw_reduce_kernel<TW><<<(unsigned)((dim + 31) / 32), 256, 0, s>>>(
+  dw_reduce_kernel<TW><<<(unsigned)((dim + 31) / 32), 1024, 0, s>>>(
       (const float*)ws, (TW*)dw, p.nparts, (int)dim);
   return check_launch("rmsnorm_dw_reduce");
 }
