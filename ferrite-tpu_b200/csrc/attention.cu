@@ -287,42 +287,60 @@ __global__ void __launch_bounds__(kSimtWarps * 32)
 // ===========================================================================
 // Tensor-core forward
 // ===========================================================================
+//
+// One CTA = 256 query rows (two 128-row tiles Q0, Q1) of one (batch, head):
+//   warp 0       TMA: Q0, Q1 once; K/V tiles into a 2-slot ring.  Causal: only
+//                the KV tiles up to the block's diagonal are ever loaded.
+//   warp 1       MMA issuer (one lane), ping-pong over the two query tiles:
+//                  S_g = Q_g K_j^T                    (SS, f32 in TMEM)
+//                  O_g += P_g V_j                     (TS: P_g read from TMEM)
+//                in the order S0(0) S1(0) | PV0(j) S0(j+1) PV1(j) S1(j+1) | ...,
+//                so one group's softmax overlaps the other group's MMAs.
+//   warps 4-7    softmax group 0 (rows of Q0), warps 8-11 group 1 (Q1); one
+//                thread per row / TMEM lane.  Each tile: load the S row (128
+//                columns) into registers, row max in the log2 domain, and
+//                  p = 2^(s * scale * log2e - m)
+//                rounded to the input dtype and written back into the first 64
+//                S columns as packed pairs (the A operand of the next PV MMA).  O lives in TMEM: it is rescaled (ld, multiply, st)
+//                only when the running max grows by more than 2^8, otherwise p
+//                keeps using the stale max (l and O share it, so O / l is
+//                unchanged up to rounding).  After the last tile O / l is stored
+//                and lse = (m + log2 l) * ln 2.
+// TMEM: S0 [0,128), S1 [128,256), O0 [256, 256+D), O1 [256+D, 256+2D).
+// MMAs issued by one thread execute in issue order, so S_g(j+1) (which
+// overwrites the P_g(j) columns) is issued only after PV_g(j).
 
-constexpr int TQ = 128;  // query rows per CTA (TMEM lanes)
+constexpr int TQ = 128;  // query rows per tile (TMEM lanes)
 constexpr int TK = 128;  // keys per KV tile
-constexpr int kFwdThreads = 192;
+constexpr int kFwdThreads = 384;  // 12 warps
+constexpr float kRescaleLog2 = 8.0f;
 
 template <int D>
 struct FwdSmem {
-  static constexpr int kChunks = D / 64;         // 128-byte swizzle chunks along d
-  static constexpr int kQBytes = TQ * D * 2;     // Q tile (K-major)
-  static constexpr int kKBytes = TK * D * 2;     // K tile (K-major)
-  static constexpr int kVBytes = TK * D * 2;     // V tile (MN-major for the B operand)
+  static constexpr int kChunks = D / 64;      // 128-byte swizzle chunks along d
+  static constexpr int kQBytes = TQ * D * 2;  // one Q tile (K-major)
+  static constexpr int kKBytes = TK * D * 2;  // K tile (K-major)
+  static constexpr int kVBytes = TK * D * 2;  // V tile (MN-major for the B operand)
   static constexpr int kStageBytes = kKBytes + kVBytes;
-  static constexpr int kPBytes = TQ * TK * 2;    // P tile (K-major, 2 chunks of 64 keys)
-  static constexpr int kQOff = 0;
-  static constexpr int kKVOff = kQOff + kQBytes;
-  static constexpr int kPOff = kKVOff + 2 * kStageBytes;
-  static constexpr int kBarOff = kPOff + kPBytes;
-  // q_full, kv_full[2], kv_empty[2], s_full[2], s_free[2], p_full, p_free,
-  // pv_full[2], pv_free[2]  = 15 barriers; then tmem slot + abort flag
-  static constexpr int kNumBars = 15;
+  static constexpr int kQOff = 0;  // Q0, Q1
+  static constexpr int kKVOff = 2 * kQBytes;
+  static constexpr int kBarOff = kKVOff + 2 * kStageBytes;
+  // q_full, kv_full[2], kv_empty[2], s_full[2], p_full[2], pv_done[2]
+  static constexpr int kNumBars = 11;
   static constexpr int kTotal = 1024 + kBarOff + kNumBars * 8 + 16;
-  // TMEM columns: S0, S1 (128 each), PV0, PV1 (D each)
-  static constexpr int kTmemCols = 512;
 };
 
 struct FwdParams {
-  int sq, sk, bh;
+  int sq, sk;
   float scale_log2;  // scale * log2(e)
   int causal;
   void* o;
   float* lse;
-  int nq_tiles;
+  int nq_blocks;  // 256-row query blocks
 };
 
-// Byte offset of element (row, col) of a [rows x 64] bf16 K-major tile stored
-// with the 128-byte swizzle (16-byte granule index XOR row % 8).
+// Byte offset of 16-byte granule `col_granule` of row `row` in a [rows x 64]
+// 16-bit K-major tile stored with the 128-byte swizzle (granule ^= row % 8).
 __device__ __forceinline__ uint32_t swz128(int row, int col_granule) {
   return (uint32_t)(row * 128 + ((col_granule ^ (row & 7)) << 4));
 }
@@ -341,63 +359,55 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   uint64_t* kv_full = bars + 1;
   uint64_t* kv_empty = bars + 3;
   uint64_t* s_full = bars + 5;
-  uint64_t* s_free = bars + 7;
-  uint64_t* p_full = bars + 9;
-  uint64_t* p_free = bars + 10;
-  uint64_t* pv_full = bars + 11;
-  uint64_t* pv_free = bars + 13;
+  uint64_t* p_full = bars + 7;
+  uint64_t* pv_done = bars + 9;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kNumBars);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // Heaviest (last) query tiles first: causal work grows with the tile index.
-  const int qt = p.nq_tiles - 1 - (int)blockIdx.x;
+  // Heaviest (last) query blocks first: causal work grows with the index.
+  const int qb = p.nq_blocks - 1 - (int)blockIdx.x;
   const int bh = blockIdx.y;
-  const int q0 = qt * TQ;
-  // KV tiles this query tile needs (causal: up to and including the diagonal).
+  const int q0 = qb * 2 * TQ;
+  const int diag_shift = p.sk - p.sq;  // causal: key <= query + diag_shift
   int n_kv = (p.sk + TK - 1) / TK;
   if (p.causal) {
-    const int last_key = min(p.sk - 1, q0 + TQ - 1 + (p.sk - p.sq));
+    const int last_key = min(p.sk - 1, q0 + 2 * TQ - 1 + diag_shift);
     n_kv = last_key < 0 ? 0 : last_key / TK + 1;
   }
 
   if (threadIdx.x == 0) {
-    // arrival counts: 1 for TMA / tcgen05.commit, 4 for the softmax warps
     mbar_init(q_full, 1);
-    mbar_init(p_full, 4);
-    mbar_init(p_free, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 4);
-      mbar_init(&pv_full[i], 1);
-      mbar_init(&pv_free[i], 4);
+      mbar_init(&p_full[i], 4);  // one arrival per softmax warp of the group
+      mbar_init(&pv_done[i], 1);
     }
     *abort = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, L::kTmemCols);
+    tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t t_s[2] = {tmem, tmem + 128};
-  const uint32_t t_pv[2] = {tmem + 256, tmem + 256 + D};
-
   if (warp == 0) {
     if (lane == 0 && n_kv > 0) {
       tma_prefetch_desc(&tq);
       tma_prefetch_desc(&tk);
       tma_prefetch_desc(&tv);
-      uint8_t* sq_ = smem + L::kQOff;
-      mbar_arrive_expect_tx(q_full, L::kQBytes);
+      mbar_arrive_expect_tx(q_full, 2 * L::kQBytes);
 #pragma unroll
-      for (int c = 0; c < L::kChunks; ++c)
-        tma_load_3d(sq_ + c * (TQ * 128), &tq, q_full, c * 64, q0, bh);
+      for (int g = 0; g < 2; ++g)
+#pragma unroll
+        for (int c = 0; c < L::kChunks; ++c)
+          tma_load_3d(smem + L::kQOff + g * L::kQBytes + c * (TQ * 128), &tq, q_full, c * 64,
+                      q0 + g * TQ, bh);
       for (int j = 0; j < n_kv; ++j) {
         const int s = j & 1;
         if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, abort, 10)) break;
@@ -416,183 +426,178 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       constexpr uint32_t idesc_s = make_idesc_f16(TQ, TK, BF16, false, false);
       constexpr uint32_t idesc_o = make_idesc_f16(TQ, D, BF16, false, true);
       const uint32_t sq_ = smem_u32(smem + L::kQOff);
-      const uint32_t sp_ = smem_u32(smem + L::kPOff);
-      bool ok = mbar_wait(q_full, 0, abort, 11);
-      auto issue_s = [&](int j) -> bool {
-        const int s = j & 1;
-        if (!mbar_wait(&kv_full[s], (j >> 1) & 1, abort, 12)) return false;
-        if (!mbar_wait(&s_free[s], ((j >> 1) & 1) ^ 1, abort, 13)) return false;
-        tc_fence_after();
-        const uint32_t sk_ = smem_u32(smem + L::kKVOff + s * L::kStageBytes);
+      bool ok = mbar_wait(q_full, 0, abort, 11) && mbar_wait(&kv_full[0], 0, abort, 12);
+      auto issue_s = [&](int g, int j) {
+        const uint32_t sk_ = smem_u32(smem + L::kKVOff + (j & 1) * L::kStageBytes);
+        const uint32_t qa = sq_ + g * L::kQBytes;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * (TQ * 128) + (kk & 3) * 32;
-          tc_mma_f16_ss(t_s[s], make_sdesc(sq_ + off, 16, 1024),
-                        make_sdesc(sk_ + (kk >> 2) * (TK * 128) + (kk & 3) * 32, 16, 1024),
+          const uint32_t qo = (kk >> 2) * (TQ * 128) + (kk & 3) * 32;
+          const uint32_t ko = (kk >> 2) * (TK * 128) + (kk & 3) * 32;
+          tc_mma_f16_ss(tmem + g * 128, make_sdesc(qa + qo, 16, 1024), make_sdesc(sk_ + ko, 16, 1024),
                         idesc_s, kk != 0);
         }
-        tc_commit(&s_full[s]);
-        return true;
+        tc_commit(&s_full[g]);
       };
-      auto issue_pv = [&](int j) -> bool {
-        const int s = j & 1;
-        if (!mbar_wait(p_full, j & 1, abort, 14)) return false;
-        if (!mbar_wait(&pv_free[s], ((j >> 1) & 1) ^ 1, abort, 15)) return false;
-        tc_fence_after();
-        const uint32_t sv_ = smem_u32(smem + L::kKVOff + s * L::kStageBytes + L::kKBytes);
+      auto issue_pv = [&](int g, int j) {
+        const uint32_t sv_ = smem_u32(smem + L::kKVOff + (j & 1) * L::kStageBytes + L::kKBytes);
+        const uint32_t pa = tmem + g * 128;  // P_g: packed pairs in S columns [0, 64)
 #pragma unroll
-        for (int kk = 0; kk < TK / 16; ++kk) {
-          const uint32_t aoff = (kk >> 2) * (TQ * 128) + (kk & 3) * 32;
-          // V tile: MN-major, d chunks of 64 at TK*128 bytes, 16 keys per step
-          tc_mma_f16_ss(t_pv[s], make_sdesc(sp_ + aoff, 16, 1024),
-                        make_sdesc(sv_ + kk * 2048, TK * 128, 1024), idesc_o, kk != 0);
-        }
-        tc_commit(&pv_full[s]);
-        tc_commit(p_free);
-        tc_commit(&kv_empty[s]);
-        return true;
+        for (int kk = 0; kk < TK / 16; ++kk)
+          tc_mma_f16_ts(tmem + 256 + g * D, pa + kk * 8, make_sdesc(sv_ + kk * 2048, TK * 128, 1024),
+                        idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&pv_done[g]);
       };
-      if (ok) ok = issue_s(0);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
+      }
       for (int j = 0; ok && j < n_kv; ++j) {
-        if (j + 1 < n_kv) ok = issue_s(j + 1);
-        if (ok) ok = issue_pv(j);
+        const bool more = j + 1 < n_kv;
+        if (!mbar_wait(&p_full[0], j & 1, abort, 13)) break;
+        tc_fence_after();
+        issue_pv(0, j);
+        if (more) {
+          if (!mbar_wait(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort, 14)) break;
+          tc_fence_after();
+          issue_s(0, j + 1);
+        }
+        if (!mbar_wait(&p_full[1], j & 1, abort, 15)) break;
+        tc_fence_after();
+        issue_pv(1, j);
+        tc_commit(&kv_empty[j & 1]);  // K_j, V_j no longer read
+        if (more) issue_s(1, j + 1);
       }
     }
-  } else {
-    // ------------------------------------------------ softmax warpgroup
+  } else if (warp >= 4) {
+    // ------------------------------------------------ softmax groups
+    const int g = (warp - 4) >> 2;
     const int qw = warp & 3;
-    const int r = qw * 32 + lane;  // query row within the tile == TMEM lane
-    const int qrow = q0 + r;
+    const int r = qw * 32 + lane;  // row within the query tile == TMEM lane
+    const int qrow = q0 + g * TQ + r;
     const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
-    uint8_t* sp = smem + L::kPOff;
-    float acc[D];
-#pragma unroll
-    for (int i = 0; i < D; ++i) acc[i] = 0.f;
-    float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
+    const uint32_t t_s = tmem + lane_off + g * 128;
+    const uint32_t t_o = tmem + lane_off + 256 + g * D;
+    float m_used = -INFINITY, l = 0.f;
     bool ok = n_kv > 0;
-    const int diag_shift = p.sk - p.sq;  // causal: key <= qrow + diag_shift
-
-    auto fold_pv = [&](int j, float alpha) -> bool {
-      const int s = j & 1;
-      if (!mbar_wait(&pv_full[s], (j >> 1) & 1, abort, 16)) return false;
-      tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < D / 16; ++c) {
-        uint32_t v[16];
-        tmem_ld16(t_pv[s] + lane_off + c * 16, v);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 16; ++i) acc[c * 16 + i] = fmaf(acc[c * 16 + i], alpha, __uint_as_float(v[i]));
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&pv_free[s]);
-      return true;
-    };
-
     for (int j = 0; ok && j < n_kv; ++j) {
-      const int s = j & 1;
-      if (!mbar_wait(&s_full[s], (j >> 1) & 1, abort, 17)) {
+      if (!mbar_wait(&s_full[g], j & 1, abort, 16)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const bool diag = p.causal && (j * TK + TK - 1 > q0 + diag_shift);
+      const bool diag = p.causal && (j * TK + TK - 1 > q0 + g * TQ + diag_shift);
+      const int kmax = qrow + diag_shift - j * TK;  // columns > kmax are masked
       // pass 1: row max of the scaled scores (log2 domain)
       float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < TK / 16; ++c) {
-        uint32_t v[16];
-        tmem_ld16(t_s[s] + lane_off + c * 16, v);
+      {
+        uint32_t sv[TK];
+        tmem_ld32(t_s + 0, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        tmem_ld32(t_s + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+        tmem_ld32(t_s + 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[64]));
+        tmem_ld32(t_s + 96, *reinterpret_cast<uint32_t(*)[32]>(&sv[96]));
         tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float x = __uint_as_float(v[i]) * p.scale_log2;
-          if (diag && (j * TK + c * 16 + i > qrow + diag_shift)) x = kMaskValue;
+        for (int i = 0; i < TK; ++i) {
+          const float x = (diag && i > kmax) ? kMaskValue : __uint_as_float(sv[i]) * p.scale_log2;
           mx = fmaxf(mx, x);
         }
       }
-      const float m_new = fmaxf(m, mx);
-      const float alpha = exp2f(m - m_new);
-      // P slot free once the previous P V MMA has read it
-      if (j > 0 && !mbar_wait(p_free, (j - 1) & 1, abort, 18)) {
-        ok = false;
-        break;
+      const float m_new = fmaxf(m_used, mx);
+      const bool need = m_new > m_used + kRescaleLog2;
+      if (__any_sync(0xffffffffu, need)) {
+        const float alpha = need ? ex2_approx(m_used - m_new) : 1.0f;
+        if (j > 0) {
+          // O_g holds P V up to tile j-1: wait for it, then rescale in TMEM
+          if (!mbar_wait(&pv_done[g], (j - 1) & 1, abort, 17)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t ov[32];
+            tmem_ld32(t_o + c * 32, ov);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+            tmem_st32(t_o + c * 32, ov);
+          }
+          tmem_wait_st();
+        }
+        if (need) {
+          l *= alpha;
+          m_used = m_new;
+        }
       }
-      // pass 2: p = exp2(x - m_new), rounded to the input dtype, into smem
+      // pass 2, two halves of 64 keys: p = 2^(x - m) rounded to the input dtype,
+      // packed in pairs into S columns [0, 64) (already consumed).
       float rs = 0.f;
 #pragma unroll
-      for (int c = 0; c < TK / 16; ++c) {
-        uint32_t v[16];
-        tmem_ld16(t_s[s] + lane_off + c * 16, v);
+      for (int half = 0; half < 2; ++half) {
+        uint32_t sv[64];
+        tmem_ld32(t_s + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        tmem_ld32(t_s + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
         tmem_wait_ld();
-        uint32_t packed[8];
+        uint32_t pk[32];
 #pragma unroll
-        for (int i = 0; i < 16; i += 2) {
-          float x0 = __uint_as_float(v[i]) * p.scale_log2;
-          float x1 = __uint_as_float(v[i + 1]) * p.scale_log2;
-          if (diag) {
-            if (j * TK + c * 16 + i > qrow + diag_shift) x0 = kMaskValue;
-            if (j * TK + c * 16 + i + 1 > qrow + diag_shift) x1 = kMaskValue;
-          }
-          const float p0 = exp2f(x0 - m_new);
-          const float p1 = exp2f(x1 - m_new);
+        for (int i = 0; i < 64; i += 2) {
+          const int col = half * 64 + i;
+          const float x0 = (diag && col > kmax) ? kMaskValue : __uint_as_float(sv[i]) * p.scale_log2;
+          const float x1 = (diag && col + 1 > kmax) ? kMaskValue : __uint_as_float(sv[i + 1]) * p.scale_log2;
+          const float p0 = ex2_approx(x0 - m_used);
+          const float p1 = ex2_approx(x1 - m_used);
           rs += p0 + p1;
-          packed[i / 2] = BF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
+          pk[i / 2] = BF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
         }
-        // 16 keys = 2 granules of chunk c/4 (64 keys per 128-byte row)
-        uint8_t* chunk = sp + (c >> 2) * (TQ * 128);
-#pragma unroll
-        for (int g = 0; g < 2; ++g) {
-          const int granule = (c & 3) * 2 + g;
-          *reinterpret_cast<uint4*>(chunk + swz128(r, granule)) =
-              make_uint4(packed[g * 4], packed[g * 4 + 1], packed[g * 4 + 2], packed[g * 4 + 3]);
-        }
+        tmem_st32(t_s + half * 32, pk);
       }
+      l += rs;
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[s]);  // S buffer may be overwritten
-      fence_proxy_async_smem();                // P visible to the tensor core
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
-      l = alpha * l + rs;
-      m = m_new;
-      // fold the previous tile's P V (overlaps this tile's P V MMA)
-      if (j > 0 && !fold_pv(j - 1, alpha_prev)) {
-        ok = false;
-        break;
-      }
-      alpha_prev = alpha;
+      if (lane == 0) mbar_arrive(&p_full[g]);
     }
-    if (ok && n_kv > 0) ok = fold_pv(n_kv - 1, alpha_prev);
-    if (ok && qrow < p.sq) {
+    // epilogue: O / l -> global, lse
+    if (ok && n_kv > 0 && mbar_wait(&pv_done[g], (n_kv - 1) & 1, abort, 18)) {
+      tc_fence_after();
       const float inv = 1.0f / l;
       typedef typename std::conditional<BF16, __nv_bfloat16, __half>::type T;
       T* orow = reinterpret_cast<T*>(p.o) + ((int64_t)bh * p.sq + qrow) * D;
 #pragma unroll
-      for (int i = 0; i < D; i += 8) {
-        uint4 v;
-        if constexpr (BF16) {
-          v.x = pack_bf16x2(acc[i] * inv, acc[i + 1] * inv);
-          v.y = pack_bf16x2(acc[i + 2] * inv, acc[i + 3] * inv);
-          v.z = pack_bf16x2(acc[i + 4] * inv, acc[i + 5] * inv);
-          v.w = pack_bf16x2(acc[i + 6] * inv, acc[i + 7] * inv);
-        } else {
-          v.x = pack_f16x2(acc[i] * inv, acc[i + 1] * inv);
-          v.y = pack_f16x2(acc[i + 2] * inv, acc[i + 3] * inv);
-          v.z = pack_f16x2(acc[i + 4] * inv, acc[i + 5] * inv);
-          v.w = pack_f16x2(acc[i + 6] * inv, acc[i + 7] * inv);
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t ov[32];
+        tmem_ld32(t_o + c * 32, ov);
+        tmem_wait_ld();
+        if (qrow < p.sq) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint4 v;
+            const float* f = reinterpret_cast<const float*>(&ov[i]);
+            if constexpr (BF16) {
+              v.x = pack_bf16x2(f[0] * inv, f[1] * inv);
+              v.y = pack_bf16x2(f[2] * inv, f[3] * inv);
+              v.z = pack_bf16x2(f[4] * inv, f[5] * inv);
+              v.w = pack_bf16x2(f[6] * inv, f[7] * inv);
+            } else {
+              v.x = pack_f16x2(f[0] * inv, f[1] * inv);
+              v.y = pack_f16x2(f[2] * inv, f[3] * inv);
+              v.z = pack_f16x2(f[4] * inv, f[5] * inv);
+              v.w = pack_f16x2(f[6] * inv, f[7] * inv);
+            }
+            *reinterpret_cast<uint4*>(orow + c * 32 + i) = v;
+          }
         }
-        *reinterpret_cast<uint4*>(orow + i) = v;
       }
-      p.lse[(int64_t)bh * p.sq + qrow] = (m + log2f(l)) * kLn2;
+      if (qrow < p.sq) p.lse[(int64_t)bh * p.sq + qrow] = (m_used + log2f(l)) * kLn2;
     }
   }
 
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, L::kTmemCols);
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -1004,16 +1009,15 @@ static int launch_fwd_tc(cudaStream_t s, const void* q, const void* k, const voi
   FwdParams p;
   p.sq = (int)sq;
   p.sk = (int)sk;
-  p.bh = (int)bh;
   p.scale_log2 = scale * kLog2e;
   p.causal = causal;
   p.o = o;
   p.lse = lse;
-  p.nq_tiles = (int)((sq + TQ - 1) / TQ);
+  p.nq_blocks = (int)((sq + 2 * TQ - 1) / (2 * TQ));
   auto kern = attn_fwd_tc_kernel<D, BF16>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
   if (e != cudaSuccess) return fail(FERRITE_LAUNCH_FAILED, "attn_fwd: smem attr: %s", cudaGetErrorString(e));
-  dim3 grid(p.nq_tiles, (unsigned)bh);
+  dim3 grid(p.nq_blocks, (unsigned)bh);
   kern<<<grid, kFwdThreads, L::kTotal, s>>>(tq, tk, tv, p);
   return check_launch("attn_fwd_tc");
 }
