@@ -607,39 +607,41 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 //
 // A CTA keeps a 128-row "stationary" pair X1, X2 in shared memory and sweeps
 // 64-row "streaming" tiles Y1, Y2 (2-slot TMA ring):
-//   dK/dV (IS_DKV): X1 = K, X2 = V (128 keys);  Y1 = Q, Y2 = dO (64 queries)
+//   dK/dV (IS_DKV): X1 = K, X2 = V (128 keys);  Y1 = Q, Y2 = dO (64 queries),
+//                   plus the 64 queries' lse and delta (TMA, zero-filled past sq)
 //   dQ            : X1 = Q, X2 = dO (128 queries); Y1 = K, Y2 = V (64 keys)
-// Per streaming tile (warp 1, one lane, kind::f16, f32 accumulators in TMEM):
-//   T1 = X1 Y1^T   (dK/dV: S^T;  dQ: S)      128 x 64, two TMEM buffers
-//   T2 = X2 Y2^T   (dK/dV: dP^T; dQ: dP)     128 x 64, two TMEM buffers
-// then the elementwise warpgroup (one thread per X row = TMEM lane) forms
+// Per streaming tile i (warp 1, one lane, kind::f16, f32 accumulators in TMEM):
+//   T1 = X1 Y1^T   (dK/dV: S^T;  dQ: S)      128 x 64, TMEM buffer i % 2
+//   T2 = X2 Y2^T   (dK/dV: dP^T; dQ: dP)     128 x 64, TMEM buffer i % 2
+// Elementwise warpgroup i % 2 (warps 4-7 or 8-11, one thread per X row = TMEM
+// lane; the two groups ping-pong over the tiles) forms
 //   P = exp(scale*S - lse) (causal mask with the finite MASK_VALUE),
 //   dS = P * (dP - delta),
 // rounds both to the input dtype (flash_attention.py:210-211, :234) into
 // 128-byte-swizzled K-major shared tiles, and warp 1 accumulates
 //   dK/dV: dV += P^T dO, dK += dS^T Q      (B operands = the same Y tiles read
 //   dQ   : dQ += dS K                        MN-major: no transposed copies)
-// After the last tile the warpgroup scales dK / dQ by `scale`
-// (flash_attention.py:220, :243) and stores.  No atomics: each CTA owns its
+// After the last tile the two groups scale dK / dQ by `scale`
+// (flash_attention.py:220, :243) and store.  No atomics: each CTA owns its
 // output rows (grids of flash_attention.py:253-306).
 
 constexpr int BX = 128;  // stationary rows
 constexpr int BY = 64;   // streaming rows
-constexpr int kBwdThreads = 192;
+constexpr int kBwdThreads = 384;  // 12 warps
 
 template <int D>
 struct BwdSmem {
   static constexpr int kChunks = D / 64;
   static constexpr int kXBytes = BX * D * 2;  // one stationary tile
   static constexpr int kYBytes = BY * D * 2;  // one streaming tile
-  static constexpr int kStageBytes = 2 * kYBytes;
-  static constexpr int kEBytes = BX * BY * 2;  // one P or dS tile (bf16)
+  static constexpr int kStatBytes = 2 * BY * 4;  // lse, delta of the streaming rows
+  static constexpr int kStageBytes = 2 * kYBytes + 1024;  // Y1, Y2, stats (padded to 1 KiB)
+  static constexpr int kEBytes = BX * BY * 2;  // one P or dS tile (16-bit)
   static constexpr int kX1Off = 0;
   static constexpr int kX2Off = kXBytes;
   static constexpr int kYOff = 2 * kXBytes;
   static constexpr int kEOff = kYOff + 2 * kStageBytes;  // [buf][P, dS]
-  static constexpr int kStatOff = kEOff + 2 * 2 * kEBytes;  // per-warp lse/delta (4 x 128 floats)
-  static constexpr int kBarOff = kStatOff + 4 * 128 * 4;
+  static constexpr int kBarOff = kEOff + 2 * 2 * kEBytes;
   // x_full, y_full[2], y_empty[2], t_full[2], t_free[2], e_full[2], e_free[2], acc_full
   static constexpr int kNumBars = 14;
   static constexpr int kTotal = 1024 + kBarOff + kNumBars * 8 + 16;
@@ -650,7 +652,7 @@ struct BwdParams {
   float scale;
   float scale_log2;
   int causal;
-  const float* lse;
+  const float* lse;    // dQ: per-row statistics
   const float* delta;
   void* out0;  // dK/dV: dK; dQ: dQ
   void* out1;  // dK/dV: dV
@@ -661,6 +663,7 @@ template <int D, bool BF16, bool IS_DKV>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tx1, const __grid_constant__ CUtensorMap tx2,
                        const __grid_constant__ CUtensorMap ty1, const __grid_constant__ CUtensorMap ty2,
+                       const __grid_constant__ CUtensorMap tlse, const __grid_constant__ CUtensorMap tdelta,
                        const BwdParams p) {
   using L = BwdSmem<D>;
   typedef typename std::conditional<BF16, __nv_bfloat16, __half>::type T;
@@ -722,8 +725,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   // TMEM columns: T1[2] at 0/64, T2[2] at 128/192, acc0 at 256, acc1 at 256 + D
-  const uint32_t t_t1[2] = {tmem, tmem + 64};
-  const uint32_t t_t2[2] = {tmem + 128, tmem + 192};
   const uint32_t t_acc0 = tmem + 256;
   const uint32_t t_acc1 = tmem + 256 + D;
 
@@ -744,12 +745,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (!mbar_wait(&y_empty[s], ((i >> 1) & 1) ^ 1, abort, 20)) break;
         uint8_t* y1 = smem + L::kYOff + s * L::kStageBytes;
         uint8_t* y2 = y1 + L::kYBytes;
-        mbar_arrive_expect_tx(&y_full[s], L::kStageBytes);
+        mbar_arrive_expect_tx(&y_full[s], 2 * L::kYBytes + (IS_DKV ? L::kStatBytes : 0));
         const int yrow = (j0 + i) * BY;
 #pragma unroll
         for (int c = 0; c < L::kChunks; ++c) {
           tma_load_3d(y1 + c * (BY * 128), &ty1, &y_full[s], c * 64, yrow, bh);
           tma_load_3d(y2 + c * (BY * 128), &ty2, &y_full[s], c * 64, yrow, bh);
+        }
+        if constexpr (IS_DKV) {
+          float* st = reinterpret_cast<float*>(y2 + L::kYBytes);
+          tma_load_2d(st, &tlse, &y_full[s], yrow, bh);
+          tma_load_2d(st + BY, &tdelta, &y_full[s], yrow, bh);
         }
       }
     }
@@ -771,8 +777,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t xo = (kk >> 2) * (BX * 128) + (kk & 3) * 32;
           const uint32_t yo = (kk >> 2) * (BY * 128) + (kk & 3) * 32;
-          tc_mma_f16_ss(t_t1[s], make_sdesc(sx1 + xo, 16, 1024), make_sdesc(sy1 + yo, 16, 1024), idesc_t, kk != 0);
-          tc_mma_f16_ss(t_t2[s], make_sdesc(sx2 + xo, 16, 1024), make_sdesc(sy2 + yo, 16, 1024), idesc_t, kk != 0);
+          tc_mma_f16_ss(tmem + s * 64, make_sdesc(sx1 + xo, 16, 1024), make_sdesc(sy1 + yo, 16, 1024), idesc_t, kk != 0);
+          tc_mma_f16_ss(tmem + 128 + s * 64, make_sdesc(sx2 + xo, 16, 1024), make_sdesc(sy2 + yo, 16, 1024), idesc_t, kk != 0);
         }
         tc_commit(&t_full[s]);
         return true;
@@ -787,8 +793,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const uint32_t sdS = sP + L::kEBytes;
 #pragma unroll
         for (int kk = 0; kk < BY / 16; ++kk) {
-          const uint32_t eo = kk * 32;            // K-major [128 x 64] tile, 16-col steps
-          const uint32_t yo = kk * 2048;          // MN-major Y: 16 rows per step
+          const uint32_t eo = kk * 32;    // K-major [128 x 64] tile, 16-column steps
+          const uint32_t yo = kk * 2048;  // MN-major Y: 16 rows per step
           const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
           if constexpr (IS_DKV) {
             // dV += P^T dO   (acc1),   dK += dS^T Q  (acc0)
@@ -804,148 +810,133 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         return true;
       };
       if (ok) ok = issue_t(0);
+      if (ok && n_y > 1) ok = issue_t(1);
       for (int i = 0; ok && i < n_y; ++i) {
-        if (i + 1 < n_y) ok = issue_t(i + 1);
-        if (ok) ok = issue_acc(i);
+        ok = issue_acc(i);
+        if (ok && i + 2 < n_y) ok = issue_t(i + 2);
       }
       tc_commit(acc_full);
     }
-  } else {
-    // ------------------------------------------------ elementwise warpgroup
+  } else if (warp >= 4) {
+    // ------------------------------------------------ elementwise warpgroups
+    const int g = (warp - 4) >> 2;  // group g handles tiles i with i % 2 == g
     const int qw = warp & 3;
     const int r = qw * 32 + lane;  // stationary row == TMEM lane
     const int xrow = x0 + r;
     const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
-    float* stat = reinterpret_cast<float*>(smem + L::kStatOff) + qw * 128;  // [lse2 x64][delta x64]
+    const uint32_t t_t1 = tmem + lane_off + g * 64;
+    const uint32_t t_t2 = tmem + lane_off + 128 + g * 64;
     // dQ: this row's statistics (rows past sq are masked below)
     float row_lse2 = 0.f, row_delta = 0.f;
     if (!IS_DKV && xrow < p.sq) {
       row_lse2 = p.lse[(int64_t)bh * p.sq + xrow] * kLog2e;
       row_delta = p.delta[(int64_t)bh * p.sq + xrow];
     }
+    uint8_t* sP = smem + L::kEOff + g * 2 * L::kEBytes;
+    uint8_t* sdS = sP + L::kEBytes;
     bool ok = n_y > 0;
-    for (int i = 0; ok && i < n_y; ++i) {
-      const int s = i & 1;
+    for (int i = g; ok && i < n_y; i += 2) {
+      const int ph = (i >> 1) & 1;
       const int y0 = (j0 + i) * BY;
-      if constexpr (IS_DKV) {
-        // stage the 64 queries' lse (log2 domain) and delta for this warp
-        __syncwarp();
-#pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
-          const int c = lane + 32 * h2;
-          const int qi = y0 + c;
-          const bool in = qi < p.sq;
-          stat[c] = in ? p.lse[(int64_t)bh * p.sq + qi] * kLog2e : 0.f;
-          stat[64 + c] = in ? p.delta[(int64_t)bh * p.sq + qi] : 0.f;
-        }
-        __syncwarp();
-      }
-      if (!mbar_wait(&t_full[s], (i >> 1) & 1, abort, 25)) {
+      if (!mbar_wait(&t_full[g], ph, abort, 25)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      if (i >= 2 && !mbar_wait(&e_free[s], ((i >> 1) & 1) ^ 1, abort, 26)) {
+      uint32_t a[BY], b[BY];
+      tmem_ld32(t_t1, *reinterpret_cast<uint32_t(*)[32]>(&a[0]));
+      tmem_ld32(t_t1 + 32, *reinterpret_cast<uint32_t(*)[32]>(&a[32]));
+      tmem_ld32(t_t2, *reinterpret_cast<uint32_t(*)[32]>(&b[0]));
+      tmem_ld32(t_t2 + 32, *reinterpret_cast<uint32_t(*)[32]>(&b[32]));
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&t_free[g]);  // T buffer g may be overwritten
+      const float* st = nullptr;
+      if constexpr (IS_DKV) {
+        // the stage's lse / delta (already landed: T(i) was computed from this stage)
+        if (!mbar_wait(&y_full[g], ph, abort, 26)) {
+          ok = false;
+          break;
+        }
+        st = reinterpret_cast<const float*>(smem + L::kYOff + g * L::kStageBytes + 2 * L::kYBytes);
+      }
+      if (i >= 2 && !mbar_wait(&e_free[g], ph ^ 1, abort, 27)) {
         ok = false;
         break;
       }
-      uint8_t* sP = smem + L::kEOff + s * 2 * L::kEBytes;
-      uint8_t* sdS = sP + L::kEBytes;
 #pragma unroll
-      for (int c16 = 0; c16 < BY / 16; ++c16) {
-        uint32_t a[16], b[16];
-        tmem_ld16(t_t1[s] + lane_off + c16 * 16, a);
-        tmem_ld16(t_t2[s] + lane_off + c16 * 16, b);
-        tmem_wait_ld();
-        uint32_t pp[8], dd[8];
+      for (int c8 = 0; c8 < BY / 8; ++c8) {  // 8 columns = one 16-byte granule
+        uint32_t pp[4], dd[4];
 #pragma unroll
-        for (int e = 0; e < 16; e += 2) {
+        for (int e = 0; e < 8; e += 2) {
           float pv[2], dv[2];
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
-            const int c = c16 * 16 + e + u;  // streaming column
-            const int ycol = y0 + c;
+            const int c = c8 * 8 + e + u;  // streaming column
             int key, qry;
             float l2, dl;
             if constexpr (IS_DKV) {
               key = xrow;
-              qry = ycol;
-              l2 = stat[c];
-              dl = stat[64 + c];
+              qry = y0 + c;
+              l2 = st[c] * kLog2e;
+              dl = st[BY + c];
             } else {
-              key = ycol;
+              key = y0 + c;
               qry = xrow;
               l2 = row_lse2;
               dl = row_delta;
             }
-            float x = __uint_as_float(a[e + u]) * p.scale_log2;
             const bool valid = qry < p.sq && !(p.causal && key > qry + diag_shift);
-            const float pr = valid ? exp2f(x - l2) : 0.f;
+            const float pr = valid ? ex2_approx(fmaf(__uint_as_float(a[c]), p.scale_log2, -l2)) : 0.f;
             pv[u] = pr;
-            dv[u] = pr * (__uint_as_float(b[e + u]) - dl);
+            dv[u] = pr * (__uint_as_float(b[c]) - dl);
           }
           pp[e / 2] = BF16 ? pack_bf16x2(pv[0], pv[1]) : pack_f16x2(pv[0], pv[1]);
           dd[e / 2] = BF16 ? pack_bf16x2(dv[0], dv[1]) : pack_f16x2(dv[0], dv[1]);
         }
-#pragma unroll
-        for (int g = 0; g < 2; ++g) {
-          const int granule = c16 * 2 + g;
-          if constexpr (IS_DKV)
-            *reinterpret_cast<uint4*>(sP + swz128(r, granule)) = make_uint4(pp[g * 4], pp[g * 4 + 1], pp[g * 4 + 2], pp[g * 4 + 3]);
-          *reinterpret_cast<uint4*>(sdS + swz128(r, granule)) = make_uint4(dd[g * 4], dd[g * 4 + 1], dd[g * 4 + 2], dd[g * 4 + 3]);
-        }
+        if constexpr (IS_DKV)
+          *reinterpret_cast<uint4*>(sP + swz128(r, c8)) = make_uint4(pp[0], pp[1], pp[2], pp[3]);
+        *reinterpret_cast<uint4*>(sdS + swz128(r, c8)) = make_uint4(dd[0], dd[1], dd[2], dd[3]);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&t_free[s]);
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&e_full[s]);
+      if (lane == 0) mbar_arrive(&e_full[g]);
     }
-    // epilogue: scaled accumulators -> global
-    if (ok && n_y > 0 && mbar_wait(acc_full, 0, abort, 27)) {
+    // epilogue: dK/dV -> group 0 stores dK, group 1 stores dV; dQ -> column halves
+    if (ok && n_y > 0 && mbar_wait(acc_full, 0, abort, 28)) {
       tc_fence_after();
       const bool row_ok = xrow < x_len;
-      T* o0 = reinterpret_cast<T*>(p.out0) + ((int64_t)bh * x_len + xrow) * D;
-      T* o1 = IS_DKV ? reinterpret_cast<T*>(p.out1) + ((int64_t)bh * x_len + xrow) * D : nullptr;
-#pragma unroll
-      for (int c16 = 0; c16 < D / 16; ++c16) {
-        uint32_t a[16];
-        tmem_ld16(t_acc0 + lane_off + c16 * 16, a);
+      const int64_t orow = ((int64_t)bh * x_len + xrow) * D;
+      T* out = reinterpret_cast<T*>((IS_DKV && g == 1) ? p.out1 : p.out0) + orow;
+      const uint32_t src = (IS_DKV && g == 1) ? t_acc1 : t_acc0;
+      const float mul = (IS_DKV && g == 1) ? 1.0f : p.scale;
+      const int c_begin = IS_DKV ? 0 : g * (D / 2);
+      const int c_end = IS_DKV ? D : (g + 1) * (D / 2);
+      for (int c0 = c_begin; c0 < c_end; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(src + lane_off + c0, v);
         tmem_wait_ld();
         if (row_ok) {
-          uint32_t pk[8];
 #pragma unroll
-          for (int e = 0; e < 16; e += 2) {
-            const float v0 = __uint_as_float(a[e]) * p.scale, v1 = __uint_as_float(a[e + 1]) * p.scale;
-            pk[e / 2] = BF16 ? pack_bf16x2(v0, v1) : pack_f16x2(v0, v1);
-          }
-          *reinterpret_cast<uint4*>(o0 + c16 * 16) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-          *reinterpret_cast<uint4*>(o0 + c16 * 16 + 8) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-        }
-        if constexpr (IS_DKV) {
-          tmem_ld16(t_acc1 + lane_off + c16 * 16, a);
-          tmem_wait_ld();
-          if (row_ok) {
-            uint32_t pk[8];
-#pragma unroll
-            for (int e = 0; e < 16; e += 2) {
-              pk[e / 2] = BF16 ? pack_bf16x2(__uint_as_float(a[e]), __uint_as_float(a[e + 1]))
-                               : pack_f16x2(__uint_as_float(a[e]), __uint_as_float(a[e + 1]));
-            }
-            *reinterpret_cast<uint4*>(o1 + c16 * 16) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-            *reinterpret_cast<uint4*>(o1 + c16 * 16 + 8) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          for (int e = 0; e < 32; e += 8) {
+            uint4 w;
+            const float* f = reinterpret_cast<const float*>(&v[e]);
+            w.x = BF16 ? pack_bf16x2(f[0] * mul, f[1] * mul) : pack_f16x2(f[0] * mul, f[1] * mul);
+            w.y = BF16 ? pack_bf16x2(f[2] * mul, f[3] * mul) : pack_f16x2(f[2] * mul, f[3] * mul);
+            w.z = BF16 ? pack_bf16x2(f[4] * mul, f[5] * mul) : pack_f16x2(f[4] * mul, f[5] * mul);
+            w.w = BF16 ? pack_bf16x2(f[6] * mul, f[7] * mul) : pack_f16x2(f[6] * mul, f[7] * mul);
+            *reinterpret_cast<uint4*>(out + c0 + e) = w;
           }
         }
       }
     } else if (ok && n_y == 0 && xrow < x_len) {
-      // no streaming tile reaches these rows (cannot happen for causal sq == sk): zeros
-      T* o0 = reinterpret_cast<T*>(p.out0) + ((int64_t)bh * x_len + xrow) * D;
-      for (int c = 0; c < D; ++c) o0[c] = DT<T>::from_f(0.f);
-      if constexpr (IS_DKV) {
-        T* o1 = reinterpret_cast<T*>(p.out1) + ((int64_t)bh * x_len + xrow) * D;
-        for (int c = 0; c < D; ++c) o1[c] = DT<T>::from_f(0.f);
-      }
+      // no streaming tile reaches these rows (not reachable for causal sq == sk): zeros
+      const int64_t orow = ((int64_t)bh * x_len + xrow) * D;
+      T* out = reinterpret_cast<T*>((IS_DKV && g == 1) ? p.out1 : p.out0) + orow;
+      const int c_begin = IS_DKV ? 0 : g * (D / 2);
+      const int c_end = IS_DKV ? D : (g + 1) * (D / 2);
+      for (int c = c_begin; c < c_end; ++c) out[c] = DT<T>::from_f(0.f);
     }
   }
 
@@ -1040,6 +1031,10 @@ static int launch_bwd_tc(cudaStream_t s, const void* q, const void* k, const voi
   if (!rc) rc = make_tmap_3d(&tx2, x2, dt, 2, D, (uint64_t)xs, (uint64_t)bh, D * 2, (uint64_t)xs * D * 2, 64, BX, 1, CU_TENSOR_MAP_SWIZZLE_128B);
   if (!rc) rc = make_tmap_3d(&ty1, y1, dt, 2, D, (uint64_t)ys, (uint64_t)bh, D * 2, (uint64_t)ys * D * 2, 64, BY, 1, CU_TENSOR_MAP_SWIZZLE_128B);
   if (!rc) rc = make_tmap_3d(&ty2, y2, dt, 2, D, (uint64_t)ys, (uint64_t)bh, D * 2, (uint64_t)ys * D * 2, 64, BY, 1, CU_TENSOR_MAP_SWIZZLE_128B);
+  // lse / delta as [bh][sq] f32, 64-query boxes (zero-filled past sq)
+  CUtensorMap tl, td;
+  if (!rc) rc = make_tmap_2d(&tl, lse, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)sq, (uint64_t)bh, (uint64_t)sq * 4, BY, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (!rc) rc = make_tmap_2d(&td, delta, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)sq, (uint64_t)bh, (uint64_t)sq * 4, BY, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
   BwdParams p;
   p.sq = (int)sq;
@@ -1056,7 +1051,7 @@ static int launch_bwd_tc(cudaStream_t s, const void* q, const void* k, const voi
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
   if (e != cudaSuccess) return fail(FERRITE_LAUNCH_FAILED, "attn_bwd: smem attr: %s", cudaGetErrorString(e));
   dim3 grid(p.n_x_tiles, (unsigned)bh);
-  kern<<<grid, kBwdThreads, L::kTotal, s>>>(tx1, tx2, ty1, ty2, p);
+  kern<<<grid, kBwdThreads, L::kTotal, s>>>(tx1, tx2, ty1, ty2, tl, td, p);
   return check_launch(IS_DKV ? "attn_bwd_dkv_tc" : "attn_bwd_dq_tc");
 }
 
