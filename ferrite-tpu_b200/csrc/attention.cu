@@ -617,10 +617,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 // lane; the two groups ping-pong over the tiles) forms
 //   P = exp(scale*S - lse) (causal mask with the finite MASK_VALUE),
 //   dS = P * (dP - delta),
-// rounds both to the input dtype (flash_attention.py:210-211, :234) into
-// 128-byte-swizzled K-major shared tiles, and warp 1 accumulates
+// rounds both to the input dtype (flash_attention.py:210-211, :234) and writes
+// them back into the first 32 columns of T1 / T2 as packed pairs; warp 1 then
+// accumulates with TS-form MMAs (A read from TMEM)
 //   dK/dV: dV += P^T dO, dK += dS^T Q      (B operands = the same Y tiles read
 //   dQ   : dQ += dS K                        MN-major: no transposed copies)
+// MMAs issued by one thread run in issue order, so T(i+2) (which overwrites
+// those columns) is issued after the accumulation of tile i.  With P and dS in
+// TMEM the streaming ring has 4 slots, so TMA loads run two tiles ahead.
 // After the last tile the two groups scale dK / dQ by `scale`
 // (flash_attention.py:220, :243) and store.  No atomics: each CTA owns its
 // output rows (grids of flash_attention.py:253-306).
@@ -629,6 +633,8 @@ constexpr int BX = 128;  // stationary rows
 constexpr int BY = 64;   // streaming rows
 constexpr int kBwdThreads = 384;  // 12 warps
 
+constexpr int kYStages = 4;  // streaming TMA ring depth
+
 template <int D>
 struct BwdSmem {
   static constexpr int kChunks = D / 64;
@@ -636,14 +642,12 @@ struct BwdSmem {
   static constexpr int kYBytes = BY * D * 2;  // one streaming tile
   static constexpr int kStatBytes = 2 * BY * 4;  // lse, delta of the streaming rows
   static constexpr int kStageBytes = 2 * kYBytes + 1024;  // Y1, Y2, stats (padded to 1 KiB)
-  static constexpr int kEBytes = BX * BY * 2;  // one P or dS tile (16-bit)
   static constexpr int kX1Off = 0;
   static constexpr int kX2Off = kXBytes;
   static constexpr int kYOff = 2 * kXBytes;
-  static constexpr int kEOff = kYOff + 2 * kStageBytes;  // [buf][P, dS]
-  static constexpr int kBarOff = kEOff + 2 * 2 * kEBytes;
-  // x_full, y_full[2], y_empty[2], t_full[2], t_free[2], e_full[2], e_free[2], acc_full
-  static constexpr int kNumBars = 14;
+  static constexpr int kBarOff = kYOff + kYStages * kStageBytes;
+  // x_full, y_full[S], y_empty[S], t_full[2], e_full[2], acc_full
+  static constexpr int kNumBars = 2 * kYStages + 6;
   static constexpr int kTotal = 1024 + kBarOff + kNumBars * 8 + 16;
 };
 
@@ -673,12 +677,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* x_full = bars + 0;
   uint64_t* y_full = bars + 1;
-  uint64_t* y_empty = bars + 3;
-  uint64_t* t_full = bars + 5;
-  uint64_t* t_free = bars + 7;
-  uint64_t* e_full = bars + 9;
-  uint64_t* e_free = bars + 11;
-  uint64_t* acc_full = bars + 13;
+  uint64_t* y_empty = bars + 1 + kYStages;
+  uint64_t* t_full = bars + 1 + 2 * kYStages;
+  uint64_t* e_full = t_full + 2;
+  uint64_t* acc_full = e_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kNumBars);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -705,13 +707,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(x_full, 1);
     mbar_init(acc_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kYStages; ++i) {
       mbar_init(&y_full[i], 1);
       mbar_init(&y_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&t_full[i], 1);
-      mbar_init(&t_free[i], 4);
-      mbar_init(&e_full[i], 4);
-      mbar_init(&e_free[i], 1);
+      mbar_init(&e_full[i], 4);  // one arrival per elementwise warp of the group
     }
     *abort = 0;
     fence_mbar_init();
@@ -741,8 +743,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tma_load_3d(smem + L::kX2Off + c * (BX * 128), &tx2, x_full, c * 64, x0, bh);
       }
       for (int i = 0; i < n_y; ++i) {
-        const int s = i & 1;
-        if (!mbar_wait(&y_empty[s], ((i >> 1) & 1) ^ 1, abort, 20)) break;
+        const int s = i % kYStages;
+        if (!mbar_wait(&y_empty[s], ((i / kYStages) & 1) ^ 1, abort, 20)) break;
         uint8_t* y1 = smem + L::kYOff + s * L::kStageBytes;
         uint8_t* y2 = y1 + L::kYBytes;
         mbar_arrive_expect_tx(&y_full[s], 2 * L::kYBytes + (IS_DKV ? L::kStatBytes : 0));
@@ -767,9 +769,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const uint32_t sx2 = smem_u32(smem + L::kX2Off);
       bool ok = mbar_wait(x_full, 0, abort, 21);
       auto issue_t = [&](int i) -> bool {
-        const int s = i & 1;
-        if (!mbar_wait(&y_full[s], (i >> 1) & 1, abort, 22)) return false;
-        if (!mbar_wait(&t_free[s], ((i >> 1) & 1) ^ 1, abort, 23)) return false;
+        const int s = i % kYStages, b = i & 1;
+        if (!mbar_wait(&y_full[s], (i / kYStages) & 1, abort, 22)) return false;
         tc_fence_after();
         const uint32_t sy1 = smem_u32(smem + L::kYOff + s * L::kStageBytes);
         const uint32_t sy2 = sy1 + L::kYBytes;
@@ -777,35 +778,33 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t xo = (kk >> 2) * (BX * 128) + (kk & 3) * 32;
           const uint32_t yo = (kk >> 2) * (BY * 128) + (kk & 3) * 32;
-          tc_mma_f16_ss(tmem + s * 64, make_sdesc(sx1 + xo, 16, 1024), make_sdesc(sy1 + yo, 16, 1024), idesc_t, kk != 0);
-          tc_mma_f16_ss(tmem + 128 + s * 64, make_sdesc(sx2 + xo, 16, 1024), make_sdesc(sy2 + yo, 16, 1024), idesc_t, kk != 0);
+          tc_mma_f16_ss(tmem + b * 64, make_sdesc(sx1 + xo, 16, 1024), make_sdesc(sy1 + yo, 16, 1024), idesc_t, kk != 0);
+          tc_mma_f16_ss(tmem + 128 + b * 64, make_sdesc(sx2 + xo, 16, 1024), make_sdesc(sy2 + yo, 16, 1024), idesc_t, kk != 0);
         }
-        tc_commit(&t_full[s]);
+        tc_commit(&t_full[b]);
         return true;
       };
       auto issue_acc = [&](int i) -> bool {
-        const int s = i & 1;
-        if (!mbar_wait(&e_full[s], (i >> 1) & 1, abort, 24)) return false;
+        const int s = i % kYStages, b = i & 1;
+        if (!mbar_wait(&e_full[b], (i >> 1) & 1, abort, 24)) return false;
         tc_fence_after();
         const uint32_t sy1 = smem_u32(smem + L::kYOff + s * L::kStageBytes);
         const uint32_t sy2 = sy1 + L::kYBytes;
-        const uint32_t sP = smem_u32(smem + L::kEOff + s * 2 * L::kEBytes);
-        const uint32_t sdS = sP + L::kEBytes;
+        const uint32_t tP = tmem + b * 64;         // P (dK/dV only): T1 columns [0, 32)
+        const uint32_t tdS = tmem + 128 + b * 64;  // dS: T2 columns [0, 32)
 #pragma unroll
         for (int kk = 0; kk < BY / 16; ++kk) {
-          const uint32_t eo = kk * 32;    // K-major [128 x 64] tile, 16-column steps
           const uint32_t yo = kk * 2048;  // MN-major Y: 16 rows per step
           const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
           if constexpr (IS_DKV) {
             // dV += P^T dO   (acc1),   dK += dS^T Q  (acc0)
-            tc_mma_f16_ss(t_acc1, make_sdesc(sP + eo, 16, 1024), make_sdesc(sy2 + yo, BY * 128, 1024), idesc_a, acc);
-            tc_mma_f16_ss(t_acc0, make_sdesc(sdS + eo, 16, 1024), make_sdesc(sy1 + yo, BY * 128, 1024), idesc_a, acc);
+            tc_mma_f16_ts(t_acc1, tP + kk * 8, make_sdesc(sy2 + yo, BY * 128, 1024), idesc_a, acc);
+            tc_mma_f16_ts(t_acc0, tdS + kk * 8, make_sdesc(sy1 + yo, BY * 128, 1024), idesc_a, acc);
           } else {
             // dQ += dS K  (acc0)
-            tc_mma_f16_ss(t_acc0, make_sdesc(sdS + eo, 16, 1024), make_sdesc(sy1 + yo, BY * 128, 1024), idesc_a, acc);
+            tc_mma_f16_ts(t_acc0, tdS + kk * 8, make_sdesc(sy1 + yo, BY * 128, 1024), idesc_a, acc);
           }
         }
-        tc_commit(&e_free[s]);
         tc_commit(&y_empty[s]);
         return true;
       };
@@ -832,8 +831,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       row_lse2 = p.lse[(int64_t)bh * p.sq + xrow] * kLog2e;
       row_delta = p.delta[(int64_t)bh * p.sq + xrow];
     }
-    uint8_t* sP = smem + L::kEOff + g * 2 * L::kEBytes;
-    uint8_t* sdS = sP + L::kEBytes;
     bool ok = n_y > 0;
     for (int i = g; ok && i < n_y; i += 2) {
       const int ph = (i >> 1) & 1;
@@ -848,58 +845,49 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tmem_ld32(t_t1 + 32, *reinterpret_cast<uint32_t(*)[32]>(&a[32]));
       tmem_ld32(t_t2, *reinterpret_cast<uint32_t(*)[32]>(&b[0]));
       tmem_ld32(t_t2 + 32, *reinterpret_cast<uint32_t(*)[32]>(&b[32]));
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&t_free[g]);  // T buffer g may be overwritten
       const float* st = nullptr;
       if constexpr (IS_DKV) {
         // the stage's lse / delta (already landed: T(i) was computed from this stage)
-        if (!mbar_wait(&y_full[g], ph, abort, 26)) {
+        const int s = i % kYStages;
+        if (!mbar_wait(&y_full[s], (i / kYStages) & 1, abort, 26)) {
           ok = false;
           break;
         }
-        st = reinterpret_cast<const float*>(smem + L::kYOff + g * L::kStageBytes + 2 * L::kYBytes);
+        st = reinterpret_cast<const float*>(smem + L::kYOff + s * L::kStageBytes + 2 * L::kYBytes);
       }
-      if (i >= 2 && !mbar_wait(&e_free[g], ph ^ 1, abort, 27)) {
-        ok = false;
-        break;
-      }
+      tmem_wait_ld();
+      uint32_t pp[BY / 2], dd[BY / 2];
 #pragma unroll
-      for (int c8 = 0; c8 < BY / 8; ++c8) {  // 8 columns = one 16-byte granule
-        uint32_t pp[4], dd[4];
+      for (int e = 0; e < BY; e += 2) {
+        float pv[2], dv[2];
 #pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-          float pv[2], dv[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int c = c8 * 8 + e + u;  // streaming column
-            int key, qry;
-            float l2, dl;
-            if constexpr (IS_DKV) {
-              key = xrow;
-              qry = y0 + c;
-              l2 = st[c] * kLog2e;
-              dl = st[BY + c];
-            } else {
-              key = y0 + c;
-              qry = xrow;
-              l2 = row_lse2;
-              dl = row_delta;
-            }
-            const bool valid = qry < p.sq && !(p.causal && key > qry + diag_shift);
-            const float pr = valid ? ex2_approx(fmaf(__uint_as_float(a[c]), p.scale_log2, -l2)) : 0.f;
-            pv[u] = pr;
-            dv[u] = pr * (__uint_as_float(b[c]) - dl);
+        for (int u = 0; u < 2; ++u) {
+          const int c = e + u;  // streaming column
+          int key, qry;
+          float l2, dl;
+          if constexpr (IS_DKV) {
+            key = xrow;
+            qry = y0 + c;
+            l2 = st[c] * kLog2e;
+            dl = st[BY + c];
+          } else {
+            key = y0 + c;
+            qry = xrow;
+            l2 = row_lse2;
+            dl = row_delta;
           }
-          pp[e / 2] = BF16 ? pack_bf16x2(pv[0], pv[1]) : pack_f16x2(pv[0], pv[1]);
-          dd[e / 2] = BF16 ? pack_bf16x2(dv[0], dv[1]) : pack_f16x2(dv[0], dv[1]);
+          const bool valid = qry < p.sq && !(p.causal && key > qry + diag_shift);
+          const float pr = valid ? ex2_approx(fmaf(__uint_as_float(a[c]), p.scale_log2, -l2)) : 0.f;
+          pv[u] = pr;
+          dv[u] = pr * (__uint_as_float(b[c]) - dl);
         }
-        if constexpr (IS_DKV)
-          *reinterpret_cast<uint4*>(sP + swz128(r, c8)) = make_uint4(pp[0], pp[1], pp[2], pp[3]);
-        *reinterpret_cast<uint4*>(sdS + swz128(r, c8)) = make_uint4(dd[0], dd[1], dd[2], dd[3]);
+        pp[e / 2] = BF16 ? pack_bf16x2(pv[0], pv[1]) : pack_f16x2(pv[0], pv[1]);
+        dd[e / 2] = BF16 ? pack_bf16x2(dv[0], dv[1]) : pack_f16x2(dv[0], dv[1]);
       }
-      fence_proxy_async_smem();
+      if constexpr (IS_DKV) tmem_st32(t_t1, pp);
+      tmem_st32(t_t2, dd);
+      tmem_wait_st();
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&e_full[g]);
     }
