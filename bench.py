@@ -1,27 +1,39 @@
-"""Benchmark driver: one JSON line for the headline workload.
+"""Benchmark driver: one JSON line for one workload.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload norm|attn_small|attn_long|gemm]
+                    [--workload norm|attn|gemm|gpt|prefill]
 
-Default workload: fused residual-add + RMSNorm,
-forward + backward, x/residual bf16 [8192, 4096] ~ N(0,1), weight f32
-1 + 0.1 N(0,1), eps 1e-6, upstream grads bf16 ~ N(0,1).  One step =
-``add_rmsnorm_fwd`` on one buffer set + ``rmsnorm_bwd`` (dh and the
-deterministic dw reduction) on the other set's saved h; two buffer sets
-alternate so that every kernel streams operands that are not L2-resident
-(each set is 448 MiB, the L2 is 126 MB).  The metric is algorithmic HBM bytes
-(read x, r; write h, y; read h, dy, dh_direct; write dh; plus w and dw) per
-second, summed over ranks.
+Workloads (synthetic inputs, seeded):
 
-Multi-GPU (torchrun, one rank per GPU, NCCL): weak scaling.  Every rank
-normalises its own 8192-token shard; the only exchange is the real one of the
-backward, the all-reduce of the f32 dw partial (16 KiB) per step.  Timing is
-CUDA events on the launching stream between barriers + synchronize, max over
-ranks.
+* ``norm`` (default, configs[1]) -- fused residual-add + RMSNorm forward +
+  backward, x/residual bf16 [8192, 4096] ~ N(0,1), weight f32 1 + 0.1 N(0,1),
+  eps 1e-6, upstream grads bf16 ~ N(0,1).  One step = ``add_rmsnorm_fwd`` on one
+  buffer set + ``rmsnorm_bwd`` (dh and the deterministic dw reduction) on the
+  other set's saved h; the two 448 MiB sets alternate, so no kernel reads
+  L2-resident operands (L2 is 126 MB).  Metric: algorithmic HBM bytes / s.
+  Multi-GPU: weak scaling, every rank normalises its own 8192-token shard; the
+  only exchange is the backward's all-reduce of the f32 dw partial (16 KiB).
+* ``attn`` -- causal flash attention fwd + bwd, b8 h32 s8192 d128
+  bf16, heads sharded over ranks (strong scaling, no communication).  Metric:
+  algorithmic TFLOP/s (fwd + bwd = 3.5 x fwd, flash_attention.py:383-390).
+* ``gemm`` -- bf16 8192^3 forward + the two backward GEMMs of the
+  VJP; replicas at N > 1.  Metric: TFLOP/s.
+* ``gpt`` -- GPT training step (d1024 L24 H16 ff4096 V32000 s1024,
+  global batch 64, data-parallel over ranks with one NCCL gradient all-reduce,
+  AdamW), all kernels on the B200 path.  Metric: tokens/s.
+* ``prefill`` -- bucketed prefill of 8 prompts x 512 into the
+  static [24, 8, 16, 512, 64] KV cache through a captured CUDA graph.  Metric:
+  prefill tokens/s.
+
+Timing: W untimed warm-up steps, an untimed pre-roll (~0.6 s) while nvidia-smi
+starts sampling clocks, then exactly K steps between a barrier + synchronize on
+both sides, CUDA events on the launching stream, max over ranks.  ``e2e``
+repeats the measurement through the public API with pinned host inputs copied
+in and results copied out every step.
 
 ``--impl reference`` times the CPU restatement of the reference's path (the
-``oracle`` package, numpy, all host threads) on a bounded sample of the same
-workload; under torchrun only rank 0 runs it.
+``oracle`` package: JAX, the reference's runtime, cannot be installed here) on
+the host cores; under torchrun only rank 0 runs it.
 """
 
 from __future__ import annotations
@@ -40,12 +52,6 @@ sys.path.insert(0, os.path.join(ROOT, "ferrite-tpu_b200"))
 
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
-
-ROWS, DIM, EPS = 8192, 4096, 1e-6
-FWD_BYTES = 4 * ROWS * DIM * 2 + 4 * DIM  # read x, r; write h, y (bf16); read w (f32)
-BWD_BYTES = 4 * ROWS * DIM * 2 + 4 * DIM + 4 * DIM  # read h, dy, dh_direct; write dh; read w; write dw
-STEP_BYTES = FWD_BYTES + BWD_BYTES
-
 
 # ----------------------------------------------------------------------------- helpers
 
@@ -77,8 +83,7 @@ class ClockSampler:
     def __init__(self, device: torch.device):
         self.bus = None
         try:
-            props = torch.cuda.get_device_properties(device)
-            self.bus = int(getattr(props, "pci_bus_id"))
+            self.bus = int(getattr(torch.cuda.get_device_properties(device), "pci_bus_id"))
         except Exception:  # noqa: BLE001
             pass
         self.proc = None
@@ -139,7 +144,6 @@ class ClockSampler:
         out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
         if not sm:
             out["error"] = self.err or "no parsable samples"
-            out["raw"] = self.lines[:2]
         return out
 
 
@@ -152,79 +156,111 @@ def _load_traffic(kernel: str):
         return None
 
 
-# ----------------------------------------------------------------------------- norm workload (ours)
+def _events(n):
+    return [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+
+
+# ----------------------------------------------------------------------------- workloads
 
 
 class NormWorkload:
+    """fused add + RMSNorm fwd + bwd, 8192 x 4096 bf16 per rank."""
+
     name = "add_rmsnorm_fwd_bwd_bf16_8192x4096"
     metric = "add+RMSNorm fwd+bwd HBM GB/s"
     unit = "GB/s"
+    dtype = "bf16"
+    scaling = "weak"
+    bound = "hbm"
+    ROWS, DIM, EPS = 8192, 4096, 1e-6
+    FWD_BYTES = 4 * ROWS * DIM * 2 + 4 * DIM  # read x, r; write h, y (bf16); read w (f32)
+    BWD_BYTES = 4 * ROWS * DIM * 2 + 4 * DIM + 4 * DIM  # read h, dy, dh_direct; write dh; read w; write dw
+    kernels = ("add_rmsnorm_fwd", "rmsnorm_bwd+dw_reduce")
+    kernel_work = {"add_rmsnorm_fwd": FWD_BYTES, "rmsnorm_bwd+dw_reduce": BWD_BYTES}
+    launches_per_step = 3  # add_rmsnorm_fwd, rmsnorm_bwd, dw_reduce
+    n_events = 3
 
-    def __init__(self, device: torch.device):
+    def __init__(self, dev, ws, rank):
         from ferrite import _native as nat
 
-        self.nat = nat
-        self.lib = nat.lib()
-        self.dev = device
-        g = torch.Generator(device=device)
-        g.manual_seed(1234 + device.index if device.index is not None else 1234)
+        self.nat, self.lib, self.dev, self.ws = nat, nat.lib(), dev, ws
+        R, D = self.ROWS, self.DIM
+        g = torch.Generator(device=dev)
+        g.manual_seed(1234 + rank)
 
-        def rn(*shape, dtype=torch.bfloat16):
-            return torch.randn(*shape, generator=g, device=device, dtype=torch.float32).to(dtype)
+        def rn(*shape):
+            return torch.randn(*shape, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
 
         self.sets = []
         for _ in range(2):
-            s = {
-                "x": rn(ROWS, DIM), "r": rn(ROWS, DIM), "dy": rn(ROWS, DIM), "dhd": rn(ROWS, DIM),
-                "h": torch.empty(ROWS, DIM, dtype=torch.bfloat16, device=device),
-                "y": torch.empty(ROWS, DIM, dtype=torch.bfloat16, device=device),
-                "dh": torch.empty(ROWS, DIM, dtype=torch.bfloat16, device=device),
-            }
-            self.sets.append(s)
-        self.w = (1.0 + 0.1 * torch.randn(DIM, generator=g, device=device)).float()
-        self.dw = torch.empty(DIM, dtype=torch.float32, device=device)
-        ws = int(self.lib.ferrite_rmsnorm_bwd_workspace_size(ROWS, DIM))
-        self.ws = torch.empty(ws, dtype=torch.uint8, device=device)
-        # make every h valid before the first backward reads it
+            self.sets.append({
+                "x": rn(R, D), "r": rn(R, D), "dy": rn(R, D), "dhd": rn(R, D),
+                "h": torch.empty(R, D, dtype=torch.bfloat16, device=dev),
+                "y": torch.empty(R, D, dtype=torch.bfloat16, device=dev),
+                "dh": torch.empty(R, D, dtype=torch.bfloat16, device=dev),
+            })
+        self.w = (1.0 + 0.1 * torch.randn(D, generator=g, device=dev)).float()
+        self.dw = torch.empty(D, dtype=torch.float32, device=dev)
+        self.dw_sum = torch.empty_like(self.dw)
+        self.ws_buf = torch.empty(int(self.lib.ferrite_rmsnorm_bwd_workspace_size(R, D)), dtype=torch.uint8, device=dev)
         for s in self.sets:
-            self.fwd(s)
-        torch.cuda.synchronize(device)
+            self._fwd(s)
+        torch.cuda.synchronize(dev)
 
-    def fwd(self, s):
+    @property
+    def units_per_step(self):
+        return self.FWD_BYTES + self.BWD_BYTES
+
+    def _fwd(self, s):
         nat = self.nat
         nat.check(self.lib.ferrite_add_rmsnorm_fwd(
             nat.stream_ptr(self.dev), s["x"].data_ptr(), s["r"].data_ptr(), self.w.data_ptr(), s["h"].data_ptr(), s["y"].data_ptr(),
-            ROWS, DIM, EPS, nat.BF16, nat.F32))
+            self.ROWS, self.DIM, self.EPS, nat.BF16, nat.F32))
 
-    def bwd(self, s):
+    def _bwd(self, s):
         nat = self.nat
         nat.check(self.lib.ferrite_rmsnorm_bwd(
             nat.stream_ptr(self.dev), s["h"].data_ptr(), self.w.data_ptr(), s["dy"].data_ptr(), s["dhd"].data_ptr(), s["dh"].data_ptr(),
-            self.dw.data_ptr(), self.ws.data_ptr(), self.ws.numel(), ROWS, DIM, EPS, nat.BF16, nat.F32))
+            self.dw.data_ptr(), self.ws_buf.data_ptr(), self.ws_buf.numel(), self.ROWS, self.DIM, self.EPS, nat.BF16, nat.F32))
 
-    launches_per_step = 3  # add_rmsnorm_fwd, rmsnorm_bwd, dw_reduce
-
-    def step(self, i: int, events=None):
+    def step(self, i, ev=None):
         a, b = self.sets[i % 2], self.sets[(i + 1) % 2]
-        if events is not None:
-            events[0].record()
-        self.fwd(a)
-        if events is not None:
-            events[1].record()
-        self.bwd(b)
-        if events is not None:
-            events[2].record()
+        if ev:
+            ev[0].record()
+        self._fwd(a)
+        if ev:
+            ev[1].record()
+        self._bwd(b)
+        if ev:
+            ev[2].record()
+        if self.ws > 1:
+            import torch.distributed as dist
 
-    # ---- end to end through the public API, host buffers in and out
+            self.dw_sum.copy_(self.dw)
+            dist.all_reduce(self.dw_sum)
+
+    def breakdown(self, evs):
+        fwd = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+        bwd = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+        return {"add_rmsnorm_fwd": fwd, "rmsnorm_bwd+dw_reduce": bwd}
+
+    def config(self):
+        return {
+            "workload": self.name, "rows_per_gpu": self.ROWS, "dim": self.DIM, "eps": self.EPS,
+            "algorithmic_bytes_per_step_per_gpu": self.units_per_step,
+            "l2": "inputs larger than L2 (two 448 MiB buffer sets alternate)",
+            "parallelism": f"tokens sharded, {self.ws} rank(s), dw all-reduce" if self.ws > 1 else "single GPU",
+        }
+
     def e2e_setup(self):
-        pin = lambda t: t.cpu().pin_memory()  # noqa: E731
         s = self.sets[0]
-        self.host = {k: pin(s[k]) for k in ("x", "r", "dy", "dhd")}
-        self.host_w = pin(self.w)
-        self.out_host = {k: torch.empty(ROWS, DIM, dtype=torch.bfloat16).pin_memory() for k in ("h", "y", "dx")}
-        self.out_dw = torch.empty(DIM, dtype=torch.float32).pin_memory()
+        self.host = {k: s[k].cpu().pin_memory() for k in ("x", "r", "dy", "dhd")}
+        self.host_w = self.w.cpu().pin_memory()
+        self.out_host = {k: torch.empty(self.ROWS, self.DIM, dtype=torch.bfloat16).pin_memory() for k in ("h", "y", "dx")}
+        self.out_dw = torch.empty(self.DIM, dtype=torch.float32).pin_memory()
         self.h2d_bytes = sum(t.numel() * t.element_size() for t in self.host.values()) + self.host_w.numel() * 4
-        self.d2h_bytes = sum(t.numel() * t.element_size() for t in self.out_host.values()) + DIM * 4
+        self.d2h_bytes = sum(t.numel() * t.element_size() for t in self.out_host.values()) + self.DIM * 4
+        self.e2e_api = "ferrite.kernels.rmsnorm.rmsnorm(x, w, residual=r) + autograd backward, pinned host buffers"
 
     def e2e_step(self):
         from ferrite.kernels.rmsnorm import rmsnorm
@@ -235,63 +271,462 @@ class NormWorkload:
         w = self.host_w.to(d, non_blocking=True).requires_grad_(True)
         dy = self.host["dy"].to(d, non_blocking=True)
         dhd = self.host["dhd"].to(d, non_blocking=True)
-        h, y = rmsnorm(x, w, residual=r, eps=EPS)
+        h, y = rmsnorm(x, w, residual=r, eps=self.EPS)
         torch.autograd.backward([h, y], [dhd, dy])
         self.out_host["h"].copy_(h.detach(), non_blocking=True)
         self.out_host["y"].copy_(y.detach(), non_blocking=True)
         self.out_host["dx"].copy_(x.grad, non_blocking=True)
         self.out_dw.copy_(w.grad, non_blocking=True)
 
+    @classmethod
+    def cpu_baseline(cls, sample_rows=8192, repeats=5, threads=None):
+        """The oracle restatement (numpy, f32 statistics) of add+RMSNorm fwd+bwd on
+        ``sample_rows`` x 4096 bf16 rows, split over ``threads`` host threads."""
+        import concurrent.futures as cf
 
-# ----------------------------------------------------------------------------- CPU baseline / reference arm
+        import ml_dtypes
+
+        sys.path.insert(0, ROOT)
+        from oracle import rmsnorm as on
+
+        threads = threads or _host_cores()
+        rng = np.random.default_rng(0)
+        bf = ml_dtypes.bfloat16
+        D, E = cls.DIM, cls.EPS
+        x, r, dy, dhd = (rng.standard_normal((sample_rows, D), dtype=np.float32).astype(bf) for _ in range(4))
+        w = (1 + 0.1 * rng.standard_normal(D)).astype(np.float32)
+        chunks = np.array_split(np.arange(sample_rows), threads)
+
+        def work(idx):
+            h, _ = on.add_rmsnorm_fwd(x[idx], r[idx], w, E)
+            _, dw = on.rmsnorm_bwd(h, w, dy[idx], dhd[idx], E)
+            return dw
+
+        times = []
+        with cf.ThreadPoolExecutor(max_workers=threads) as ex:
+            list(ex.map(work, chunks))
+            for _ in range(repeats):
+                t0 = time.perf_counter()
+                parts = list(ex.map(work, chunks))
+                np.sum(parts, axis=0)  # the dw exchange across chunks
+                times.append(time.perf_counter() - t0)
+        t = statistics.median(times)
+        work_bytes = (cls.FWD_BYTES + cls.BWD_BYTES) * sample_rows / cls.ROWS
+        return {"value": work_bytes / t / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+                "sample": f"{sample_rows} of {cls.ROWS} rows x {D} (fwd+bwd), median of {repeats}, numpy oracle over {threads} threads",
+                "seconds_per_sample": t, "sample_fraction": sample_rows / cls.ROWS}
 
 
-def cpu_norm_baseline(sample_rows: int = 8192, repeats: int = 5, threads: int | None = None) -> dict:
-    """Time the oracle restatement (numpy, f32 statistics) of add+RMSNorm fwd+bwd on
-    ``sample_rows`` x 4096 bf16 rows, split over ``threads`` host threads."""
-    import concurrent.futures as cf
+class AttnWorkload:
+    """causal flash attention fwd + bwd, b8 h32 s8192 d128 bf16, heads sharded."""
 
-    import ml_dtypes
+    name = "flash_attention_causal_fwd_bwd_b8_h32_s8192_d128_bf16"
+    metric = "causal flash-attn fwd+bwd TFLOP/s"
+    unit = "TFLOP/s"
+    dtype = "bf16"
+    scaling = "strong"
+    bound = "tensor"
+    B, H, S, D = 8, 32, 8192, 128
+    kernels = ("attn_fwd", "attn_bwd_prep", "attn_bwd_dkv", "attn_bwd_dq")
+    launches_per_step = 4
+    n_events = 5
 
-    sys.path.insert(0, ROOT)
-    from oracle import rmsnorm as on
+    def __init__(self, dev, ws, rank):
+        from ferrite.kernels.flash_attention import attention_flops
 
-    threads = threads or _host_cores()
-    rng = np.random.default_rng(0)
-    bf = ml_dtypes.bfloat16
-    x = rng.standard_normal((sample_rows, DIM), dtype=np.float32).astype(bf)
-    r = rng.standard_normal((sample_rows, DIM), dtype=np.float32).astype(bf)
-    dy = rng.standard_normal((sample_rows, DIM), dtype=np.float32).astype(bf)
-    dhd = rng.standard_normal((sample_rows, DIM), dtype=np.float32).astype(bf)
-    w = (1 + 0.1 * rng.standard_normal(DIM)).astype(np.float32)
-    chunks = np.array_split(np.arange(sample_rows), threads)
+        self.dev, self.ws = dev, ws
+        bh = self.B * self.H
+        if bh % ws:
+            raise ValueError("batch*heads must divide over ranks")
+        self.bh_local = bh // ws
+        g = torch.Generator(device=dev)
+        g.manual_seed(rank)
+        shape = (1, self.bh_local, self.S, self.D)  # this rank's (b, h) slices as one batch row
+        self.q, self.k, self.v, self.do = (torch.randn(*shape, generator=g, device=dev).to(torch.bfloat16) for _ in range(4))
+        self.fwd_flops_local = attention_flops(1, self.bh_local, self.S, self.S, self.D, causal=True)
+        # tensor-core work each kernel issues, in units of one causal S*S*D/2 product: fwd 2, dkv 4, dq 3
+        unit = self.fwd_flops_local / 2
+        self.kernel_work = {"attn_fwd": 2 * unit, "attn_bwd_prep": 0, "attn_bwd_dkv": 4 * unit, "attn_bwd_dq": 3 * unit}
+        self.o = torch.empty_like(self.q)
+        self.lse = torch.empty(1, self.bh_local, self.S, device=dev)
+        self.delta = torch.empty_like(self.lse)
+        self.dq, self.dk, self.dv = (torch.empty_like(self.q) for _ in range(3))
 
-    def work(idx):
-        h, y = on.add_rmsnorm_fwd(x[idx], r[idx], w, EPS)
-        dh, dw = on.rmsnorm_bwd(h, w, dy[idx], dhd[idx], EPS)
-        return dw
+    @property
+    def units_per_step(self):
+        return 3.5 * self.fwd_flops_local  # per rank (bench_kernels.py:119)
 
-    times = []
-    with cf.ThreadPoolExecutor(max_workers=threads) as ex:
-        list(ex.map(work, chunks))  # warm-up
-        for _ in range(repeats):
+    def step(self, i, ev=None):
+        from ferrite import _native as nat
+
+        lib = nat.lib()
+        s = nat.stream_ptr(self.dev)
+        bh, S, D = self.bh_local, self.S, self.D
+        sc = 1.0 / np.sqrt(D)
+        if ev:
+            ev[0].record()
+        nat.check(lib.ferrite_attn_fwd(s, self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(), self.o.data_ptr(), self.lse.data_ptr(), 1, bh, S, S, D, sc, 1, 128, 128, nat.BF16))
+        if ev:
+            ev[1].record()
+        nat.check(lib.ferrite_attn_bwd_prep(s, self.do.data_ptr(), self.o.data_ptr(), self.delta.data_ptr(), 1, bh, S, D, nat.BF16))
+        if ev:
+            ev[2].record()
+        nat.check(lib.ferrite_attn_bwd_dkv(s, self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(), self.do.data_ptr(), self.lse.data_ptr(), self.delta.data_ptr(),
+                                           self.dk.data_ptr(), self.dv.data_ptr(), 1, bh, S, S, D, sc, 1, 128, 128, nat.BF16))
+        if ev:
+            ev[3].record()
+        nat.check(lib.ferrite_attn_bwd_dq(s, self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(), self.do.data_ptr(), self.lse.data_ptr(), self.delta.data_ptr(),
+                                          self.dq.data_ptr(), 1, bh, S, S, D, sc, 1, 128, 128, nat.BF16))
+        if ev:
+            ev[4].record()
+
+    def breakdown(self, evs):
+        return {k: statistics.mean(e[j].elapsed_time(e[j + 1]) for e in evs) for j, k in enumerate(self.kernels)}
+
+    def config(self):
+        return {"workload": self.name, "batch": self.B, "heads": self.H, "seq_len": self.S, "head_dim": self.D, "causal": True,
+                "block_q": 128, "block_k": 128, "heads_per_gpu": self.bh_local, "parallelism": f"batch*heads sharded over {self.ws} rank(s)",
+                "l2": "inputs larger than L2 (q, k, v, dO 512 MiB each at 1 GPU)"}
+
+    def e2e_setup(self):
+        self.host = {k: getattr(self, k).cpu().pin_memory() for k in ("q", "k", "v", "do")}
+        self.out_host = {k: torch.empty_like(self.host["q"]).pin_memory() for k in ("o", "dq", "dk", "dv")}
+        self.h2d_bytes = sum(t.numel() * 2 for t in self.host.values())
+        self.d2h_bytes = sum(t.numel() * 2 for t in self.out_host.values())
+        self.e2e_api = "ferrite.kernels.flash_attention.flash_attention(q, k, v, causal=True) + autograd backward, pinned host buffers"
+
+    def e2e_step(self):
+        from ferrite.kernels.flash_attention import flash_attention
+
+        d = self.dev
+        q, k, v = (self.host[n].to(d, non_blocking=True).requires_grad_(True) for n in ("q", "k", "v"))
+        do = self.host["do"].to(d, non_blocking=True)
+        o = flash_attention(q, k, v, causal=True)
+        o.backward(do)
+        for name, t in (("o", o.detach()), ("dq", q.grad), ("dk", k.grad), ("dv", v.grad)):
+            self.out_host[name].copy_(t, non_blocking=True)
+
+    @classmethod
+    def cpu_baseline(cls, slices=1, threads=None):
+        """The oracle's blockwise fwd + bwd (numpy) on ``slices`` of the 256 independent
+        (b, h) slices, extrapolated linearly to the whole config."""
+        import ml_dtypes
+
+        sys.path.insert(0, ROOT)
+        from oracle import attention as oa
+
+        rng = np.random.default_rng(0)
+        bf = ml_dtypes.bfloat16
+        q, k, v, do = (rng.standard_normal((1, slices, cls.S, cls.D), dtype=np.float32).astype(bf) for _ in range(4))
+        t0 = time.perf_counter()
+        o, lse = oa.flash_fwd(q, k, v, causal=True)
+        oa.flash_bwd(q, k, v, o, lse, do, causal=True)
+        t = time.perf_counter() - t0
+        flops = 3.5 * oa.attention_flops(1, slices, cls.S, cls.S, cls.D, causal=True)
+        return {"value": flops / t / 1e12, "unit": "TFLOP/s", "cores": threads or _host_cores(), "kind": "port",
+                "sample": f"{slices} of {cls.B * cls.H} (b,h) slices, numpy blockwise oracle (BLAS threads)", "seconds_per_sample": t,
+                "sample_fraction": slices / (cls.B * cls.H)}
+
+
+class GemmWorkload:
+    """bf16 8192^3 forward + the two backward GEMMs (replicas at N > 1)."""
+
+    name = "matmul_bf16_8192cubed_fwd_and_vjp"
+    metric = "matmul bf16 8192^3 fwd+2bwd TFLOP/s"
+    unit = "TFLOP/s"
+    dtype = "bf16"
+    scaling = "weak"
+    bound = "tensor"
+    M = N = K = 8192
+    kernels = ("gemm_fwd", "gemm_dA", "gemm_dB")
+    launches_per_step = 3
+    n_events = 4
+
+    def __init__(self, dev, ws, rank):
+        self.dev, self.ws = dev, ws
+        g = torch.Generator(device=dev)
+        g.manual_seed(rank)
+        sk = 1 / np.sqrt(self.K)
+        self.a = (torch.randn(self.M, self.K, generator=g, device=dev) * sk).to(torch.bfloat16)
+        self.b = (torch.randn(self.K, self.N, generator=g, device=dev) * sk).to(torch.bfloat16)
+        self.gout = torch.randn(self.M, self.N, generator=g, device=dev).to(torch.bfloat16)
+        self.c = torch.empty(self.M, self.N, dtype=torch.bfloat16, device=dev)
+        self.da = torch.empty_like(self.a)
+        self.db = torch.empty_like(self.b)
+        f = 2 * self.M * self.N * self.K
+        self.kernel_work = {"gemm_fwd": f, "gemm_dA": f, "gemm_dB": f}
+
+    @property
+    def units_per_step(self):
+        return 3 * 2 * self.M * self.N * self.K
+
+    def step(self, i, ev=None):
+        from ferrite.kernels.matmul import gemm
+
+        if ev:
+            ev[0].record()
+        gemm(self.a, self.b, out=self.c)
+        if ev:
+            ev[1].record()
+        gemm(self.gout, self.b, trans_b=True, out=self.da)
+        if ev:
+            ev[2].record()
+        gemm(self.a, self.gout, trans_a=True, out=self.db)
+        if ev:
+            ev[3].record()
+
+    def breakdown(self, evs):
+        return {k: statistics.mean(e[j].elapsed_time(e[j + 1]) for e in evs) for j, k in enumerate(self.kernels)}
+
+    def config(self):
+        return {"workload": self.name, "m": self.M, "n": self.N, "k": self.K, "parallelism": "independent replicas" if self.ws > 1 else "single GPU",
+                "l2": "operands 128 MiB each (larger than L2)"}
+
+    def e2e_setup(self):
+        self.host = {"a": self.a.cpu().pin_memory(), "b": self.b.cpu().pin_memory(), "g": self.gout.cpu().pin_memory()}
+        self.out_host = {k: torch.empty(self.M, self.N, dtype=torch.bfloat16).pin_memory() for k in ("c", "da", "db")}
+        self.h2d_bytes = sum(t.numel() * 2 for t in self.host.values())
+        self.d2h_bytes = sum(t.numel() * 2 for t in self.out_host.values())
+        self.e2e_api = "ferrite.kernels.matmul.matmul(x, y) + autograd backward, pinned host buffers"
+
+    def e2e_step(self):
+        from ferrite.kernels.matmul import matmul
+
+        d = self.dev
+        x = self.host["a"].to(d, non_blocking=True).requires_grad_(True)
+        y = self.host["b"].to(d, non_blocking=True).requires_grad_(True)
+        g = self.host["g"].to(d, non_blocking=True)
+        c = matmul(x, y)
+        c.backward(g)
+        self.out_host["c"].copy_(c.detach(), non_blocking=True)
+        self.out_host["da"].copy_(x.grad, non_blocking=True)
+        self.out_host["db"].copy_(y.grad, non_blocking=True)
+
+    @classmethod
+    def cpu_baseline(cls, rows=256, threads=None):
+        """numpy f32 (BLAS, all threads) on a ``rows``-row sample of A and G (the three
+        products scale linearly in the sampled rows)."""
+        rng = np.random.default_rng(0)
+        a = rng.standard_normal((rows, cls.K), dtype=np.float32)
+        b = rng.standard_normal((cls.K, cls.N), dtype=np.float32)
+        g = rng.standard_normal((rows, cls.N), dtype=np.float32)
+        a @ b  # warm-up
+        t0 = time.perf_counter()
+        a @ b
+        g @ b.T
+        a.T @ g
+        t = time.perf_counter() - t0
+        flops = 3 * 2 * rows * cls.N * cls.K
+        return {"value": flops / t / 1e12, "unit": "TFLOP/s", "cores": threads or _host_cores(), "kind": "port",
+                "sample": f"{rows} of {cls.M} rows, numpy f32 BLAS (oracle matmul_reference / matmul_vjp arithmetic)",
+                "seconds_per_sample": t, "sample_fraction": rows / cls.M}
+
+
+GPT_CFG = dict(vocab_size=32000, seq_len=1024, d_model=1024, n_head=16, n_layer=24, d_ff=4096)
+
+
+class GptWorkload:
+    """one data-parallel GPT training step, global batch 64 x 1024 tokens."""
+
+    name = "gpt_train_step_d1024_L24_H16_ff4096_V32000_s1024_b64"
+    metric = "GPT train tokens/s"
+    unit = "tokens/s"
+    dtype = "bf16"
+    scaling = "strong"
+    bound = "tensor"
+    GLOBAL_BATCH = 64
+    n_events = 2
+    kernels = ("train_step",)
+
+    def __init__(self, dev, ws, rank):
+        from ferrite import _native as nat
+        from ferrite.model.gpt import GPTConfig, flops_per_token, init_params, param_count, param_leaves
+        from ferrite.model.train import AdamW, FlatGrads, TrainConfig, build_train_step
+
+        self.dev, self.ws, self.rank = dev, ws, rank
+        self.cfg = GPTConfig(**GPT_CFG, attention="pallas", norm="pallas", linear="pallas", dtype=torch.bfloat16)
+        self.tcfg = TrainConfig(steps=1000, batch=self.GLOBAL_BATCH, lr=6e-4, warmup=20)
+        if self.GLOBAL_BATCH % ws:
+            raise ValueError("global batch must divide over ranks")
+        self.local_batch = self.GLOBAL_BATCH // ws
+        self.params = init_params(0, self.cfg, device=dev)
+        leaves = param_leaves(self.params)
+        for p in leaves:
+            p.requires_grad_(True)
+        n = param_count(self.params)
+        nonembed = n - self.params["tok_emb"].numel() - self.params["pos_emb"].numel()
+        self.flops_per_step_global = 3 * flops_per_token(self.cfg, nonembed)["total"] * self.GLOBAL_BATCH * self.cfg.seq_len
+        self.opt = AdamW(leaves, self.tcfg)
+        self.flat = FlatGrads(leaves)
+        self._step = build_train_step(self.cfg, self.tcfg, leaves, self.opt, self.flat, self.params)
+        rng = np.random.default_rng(rank)
+        ids = rng.integers(0, self.cfg.vocab_size, size=(self.local_batch, self.cfg.seq_len + 1))
+        self.x = torch.from_numpy(ids[:, :-1]).to(dev)
+        self.y = torch.from_numpy(ids[:, 1:]).to(dev)
+        self.kernel_work = {"train_step": self.flops_per_step_global / ws}
+        self._count_launches(nat)
+
+    def _count_launches(self, nat):
+        """Count native launches of one step (one C call = one kernel; rmsnorm_bwd = 2)."""
+        lib = nat.lib()
+        counts = {}
+        per_call = {"ferrite_rmsnorm_bwd": 2}
+        originals = {}
+        for name in ("ferrite_rmsnorm_fwd", "ferrite_add_rmsnorm_fwd", "ferrite_rmsnorm_bwd", "ferrite_gemm",
+                     "ferrite_attn_fwd", "ferrite_attn_bwd_prep", "ferrite_attn_bwd_dkv", "ferrite_attn_bwd_dq"):
+            fn = getattr(lib, name)
+            originals[name] = fn
+
+            def wrap(*a, _fn=fn, _n=name):
+                counts[_n] = counts.get(_n, 0) + 1
+                return _fn(*a)
+
+            setattr(lib, name, wrap)
+        try:
+            self._step(self.x, self.y)
+            torch.cuda.synchronize(self.dev)
+        finally:
+            for name, fn in originals.items():
+                setattr(lib, name, fn)
+        self.launches_per_step = sum(v * per_call.get(k, 1) for k, v in counts.items())
+        self.launch_counts = counts
+
+    @property
+    def units_per_step(self):
+        return self.local_batch * self.cfg.seq_len  # tokens this rank processes
+
+    def step(self, i, ev=None):
+        if ev:
+            ev[0].record()
+        self.loss, _ = self._step(self.x, self.y)
+        if ev:
+            ev[1].record()
+
+    def breakdown(self, evs):
+        return {"train_step": statistics.mean(e[0].elapsed_time(e[1]) for e in evs)}
+
+    def config(self):
+        return {"workload": self.name, "model": "ferrite GPT (pre-norm decoder)", **GPT_CFG, "global_batch": self.GLOBAL_BATCH,
+                "per_gpu_batch": self.local_batch, "parallelism": f"dp{self.ws}", "optimizer": "AdamW (reference formula), clip 1.0",
+                "init": "normal(0, 0.02), GPT-2 residual scaling", "data": "token ids uniform in [0, 32000)",
+                "train_flops_per_step": self.flops_per_step_global, "native_launch_counts": self.launch_counts}
+
+    def e2e_setup(self):
+        self.host_x = self.x.cpu().pin_memory()
+        self.host_y = self.y.cpu().pin_memory()
+        self.loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+        self.h2d_bytes = 2 * self.host_x.numel() * 8
+        self.d2h_bytes = 4
+        self.e2e_api = "ferrite.model.train step (forward, backward, NCCL all-reduce, AdamW) with host token batches in, loss out"
+
+    def e2e_step(self):
+        x = self.host_x.to(self.dev, non_blocking=True)
+        y = self.host_y.to(self.dev, non_blocking=True)
+        loss, _ = self._step(x, y)
+        self.loss_host.copy_(loss, non_blocking=True)
+
+    @classmethod
+    def cpu_baseline(cls, tokens=1024, threads=None):
+        """The reference's plain path restated in torch f32 on the CPU (oracle/gpt.py),
+        forward + backward of one 1024-token sequence of the full model."""
+        sys.path.insert(0, ROOT)
+        from oracle import gpt as og
+
+        threads = threads or _host_cores()
+        torch.set_num_threads(threads)
+        cfg = dict(GPT_CFG)
+        params = og.init(cfg)
+        rng = np.random.default_rng(0)
+        ids = torch.from_numpy(rng.integers(0, cfg["vocab_size"], size=(1, tokens + 1)))
+        t0 = time.perf_counter()
+        og.loss(params, ids[:, :-1], ids[:, 1:], cfg).backward()
+        t = time.perf_counter() - t0
+        return {"value": tokens / t, "unit": "tokens/s", "cores": threads, "kind": "port",
+                "sample": f"1 sequence x {tokens} tokens fwd+bwd (no optimizer), torch f32 CPU restatement (oracle/gpt.py)",
+                "seconds_per_sample": t, "sample_fraction": tokens / (cls.GLOBAL_BATCH * cfg["seq_len"])}
+
+
+class PrefillWorkload:
+    """configs[4] serving half: bucketed prefill of 8 prompts x 512 into [24, 8, 16, 512, 64]."""
+
+    name = "gpt_bucketed_prefill_8x512_into_kv_24x8x16x512x64"
+    metric = "GPT prefill tokens/s"
+    unit = "tokens/s"
+    dtype = "bf16"
+    scaling = "weak"
+    bound = "tensor"
+    n_events = 2
+    kernels = ("prefill_graph",)
+    PROMPTS, LEN = 8, 512
+
+    def __init__(self, dev, ws, rank):
+        from ferrite.model.gpt import GPTConfig, flops_per_token, init_params, param_count
+        from ferrite.serving.engine import Engine, ServeConfig
+
+        self.dev, self.ws = dev, ws
+        cfg = GPTConfig(**GPT_CFG, attention="pallas", norm="pallas", linear="pallas", dtype=torch.bfloat16)
+        self.params = init_params(0, cfg, device=dev)
+        self.engine = Engine(self.params, cfg, ServeConfig(batch=self.PROMPTS, max_len=512, buckets=(512,)))
+        rng = np.random.default_rng(rank)
+        self.prompts = [list(rng.integers(0, cfg.vocab_size, size=self.LEN)) for _ in range(self.PROMPTS)]
+        n = param_count(self.params)
+        nonembed = n - self.params["tok_emb"].numel() - self.params["pos_emb"].numel()
+        self.kernel_work = {"prefill_graph": flops_per_token(cfg, nonembed)["total"] * self.PROMPTS * self.LEN}
+        # one C call per kernel: per layer 2 norms, 4 GEMMs, 1 attention; final norm; LM head
+        self.launches_per_step = cfg.n_layer * 7 + 2
+        self.cfg = cfg
+
+    @property
+    def units_per_step(self):
+        return self.PROMPTS * self.LEN
+
+    def step(self, i, ev=None):
+        if ev:
+            ev[0].record()
+        self.tok, _, _, _ = self.engine.prefill(self.prompts)
+        if ev:
+            ev[1].record()
+
+    def breakdown(self, evs):
+        return {"prefill_graph": statistics.mean(e[0].elapsed_time(e[1]) for e in evs)}
+
+    def config(self):
+        return {"workload": self.name, "model": "ferrite GPT (pre-norm decoder)", **GPT_CFG, "prompts": self.PROMPTS, "prompt_len": self.LEN,
+                "bucket": 512, "kv_cache": [24, self.PROMPTS, 16, 512, 64], "parallelism": "replicas" if self.ws > 1 else "single GPU"}
+
+    def e2e_setup(self):
+        self.h2d_bytes = self.PROMPTS * self.LEN * 8 + self.PROMPTS * 8
+        self.d2h_bytes = self.PROMPTS * 8
+        self.e2e_api = "ferrite.serving.Engine.prefill(prompts) (host token lists in, first tokens out)"
+
+    def e2e_step(self):
+        tok, _, _, _ = self.engine.prefill(self.prompts)
+        tok.cpu()
+
+    @classmethod
+    def cpu_baseline(cls, threads=None):
+        """oracle/gpt.py forward on one 512-token prompt (torch f32, CPU)."""
+        sys.path.insert(0, ROOT)
+        from oracle import gpt as og
+
+        threads = threads or _host_cores()
+        torch.set_num_threads(threads)
+        cfg = dict(GPT_CFG)
+        params = og.init(cfg)
+        ids = torch.from_numpy(np.random.default_rng(0).integers(0, cfg["vocab_size"], size=(1, cls.LEN + 1)))
+        with torch.no_grad():
             t0 = time.perf_counter()
-            parts = list(ex.map(work, chunks))
-            np.sum(parts, axis=0)  # the dw exchange across chunks
-            times.append(time.perf_counter() - t0)
-    t = statistics.median(times)
-    bytes_sample = STEP_BYTES * sample_rows / ROWS
-    return {
-        "value": bytes_sample / t / 1e9,
-        "unit": "GB/s",
-        "cores": threads,
-        "kind": "port",
-        "sample": f"{sample_rows} of {ROWS} rows x {DIM} (fwd+bwd), median of {repeats}, numpy oracle over {threads} threads",
-        "seconds_per_sample": t,
-    }
+            og.loss(params, ids[:, :-1], ids[:, 1:], cfg)
+            t = time.perf_counter() - t0
+        return {"value": cls.LEN / t, "unit": "tokens/s", "cores": threads, "kind": "port",
+                "sample": f"1 prompt x {cls.LEN} tokens forward, torch f32 CPU restatement (oracle/gpt.py)", "seconds_per_sample": t,
+                "sample_fraction": 1 / cls.PROMPTS}
 
 
-# ----------------------------------------------------------------------------- main
+WORKLOADS = {"norm": NormWorkload, "attn": AttnWorkload, "gemm": GemmWorkload, "gpt": GptWorkload, "prefill": PrefillWorkload}
+
+
+# ----------------------------------------------------------------------------- runners
 
 
 def run_ours(args, ws, rank, local):
@@ -302,69 +737,60 @@ def run_ours(args, ws, rank, local):
     if ws > 1:
         from datetime import timedelta
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    wl = NormWorkload(dev)
-    dw_sum = torch.empty_like(wl.dw)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    W = WORKLOADS[args.workload]
+    wl = W(dev, ws, rank)
 
-    def one_step(i, ev=None):
-        wl.step(i, ev)
-        if ws > 1:
-            dw_sum.copy_(wl.dw)
-            dist.all_reduce(dw_sum)
-
-    for i in range(args.warmup):
-        one_step(i)
-    torch.cuda.synchronize(dev)
-    if ws > 1:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
-
-    # untimed pre-roll length (same on every rank): about 0.6 s of steps
-    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    p0.record()
-    for i in range(4):
-        wl.step(i)
-    p1.record()
-    torch.cuda.synchronize(dev)
-    n_pre = torch.tensor([max(1, int(600.0 / max(p0.elapsed_time(p1) / 4, 1e-3)))], device=dev)
-    if ws > 1:
-        dist.all_reduce(n_pre, op=dist.ReduceOp.MAX)
-    n_pre = int(min(n_pre.item(), 20000))
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(dev) as clk:
-        # nvidia-smi samples every 100 ms; keep the GPU under the same load (untimed
-        # steps) until the sampler is producing samples, so the clock record covers
-        # the loaded window that ends with the timed region.
-        for i in range(n_pre):
-            one_step(i)
+    def sync_all():
         torch.cuda.synchronize(dev)
         if ws > 1:
             dist.barrier()
         torch.cuda.synchronize(dev)
+
+    for i in range(args.warmup):
+        wl.step(i)
+    sync_all()
+
+    # untimed pre-roll length (same on every rank): about 0.6 s of steps
+    p0, p1 = _events(2)
+    p0.record()
+    wl.step(0)
+    p1.record()
+    torch.cuda.synchronize(dev)
+    n_pre = torch.tensor([max(1, int(600.0 / max(p0.elapsed_time(p1), 1e-3)))], device=dev)
+    if ws > 1:
+        dist.all_reduce(n_pre, op=dist.ReduceOp.MAX)
+    n_pre = int(min(n_pre.item(), 20000))
+
+    evs = [_events(wl.n_events) for _ in range(args.steps)]
+    start, stop = _events(2)
+    with ClockSampler(dev) as clk:
+        for i in range(n_pre):
+            wl.step(i)
+        sync_all()
         start.record()
         for i in range(args.steps):
-            one_step(i, evs[i])
+            wl.step(i, evs[i])
         stop.record()
         torch.cuda.synchronize(dev)
     ms = start.elapsed_time(stop)
-    fwd_ms = [e[0].elapsed_time(e[1]) for e in evs]
-    bwd_ms = [e[1].elapsed_time(e[2]) for e in evs]
-    t = torch.tensor([ms, statistics.mean(fwd_ms), statistics.mean(bwd_ms)], device=dev, dtype=torch.float64)
+    bd = wl.breakdown(evs)
+    names = list(bd)
+    t = torch.tensor([ms] + [bd[k] for k in names], device=dev, dtype=torch.float64)
     if ws > 1:
         dist.barrier()
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, fwd_avg, bwd_avg = (float(v) for v in t.tolist())
-    value = STEP_BYTES * ws * args.steps / (ms / 1e3) / 1e9
+    ms = float(t[0])
+    bd = {k: float(v) for k, v in zip(names, t[1:].tolist())}
+    scale = 1e9 if wl.unit == "GB/s" else (1e12 if wl.unit == "TFLOP/s" else 1.0)
+    value = wl.units_per_step * ws * args.steps / (ms / 1e3) / scale
 
-    # end-to-end through the public API with host buffers
+    # end to end through the public API with host buffers
     wl.e2e_setup()
-    for _ in range(max(1, args.warmup)):
+    for _ in range(max(1, min(args.warmup, 3))):
         wl.e2e_step()
-    torch.cuda.synchronize(dev)
-    if ws > 1:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sync_all()
+    e0, e1 = _events(2)
     e0.record()
     for _ in range(args.steps):
         wl.e2e_step()
@@ -373,63 +799,56 @@ def run_ours(args, ws, rank, local):
     e_ms = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
     if ws > 1:
         dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
-    e2e_value = STEP_BYTES * ws * args.steps / (float(e_ms.item()) / 1e3) / 1e9
+    e2e_value = wl.units_per_step * ws * args.steps / (float(e_ms.item()) / 1e3) / scale
 
     from ferrite import platform
 
     pk = platform.peaks()
-    dominant = ("add_rmsnorm_fwd", fwd_avg, FWD_BYTES) if fwd_avg >= bwd_avg else ("rmsnorm_bwd", bwd_avg, BWD_BYTES)
-    achieved = dominant[2] / (dominant[1] / 1e3) / 1e9
-    peak = pk.hbm_bytes_per_s / 1e9
+    dom = max((k for k in bd if wl.kernel_work.get(k)), key=lambda k: bd[k])
+    if wl.bound == "hbm":
+        achieved = wl.kernel_work[dom] / (bd[dom] / 1e3) / 1e9
+        peak, unit, psrc = pk.hbm_bytes_per_s / 1e9, "GB/s", "hbm_gbs"
+    else:
+        achieved = wl.kernel_work[dom] / (bd[dom] / 1e3) / 1e12
+        long_step = args.workload == "gpt"
+        peak = (pk.bf16_flops_sustained if long_step else pk.bf16_flops) / 1e12
+        unit, psrc = "TFLOP/s", "bf16_tflops_sustained" if long_step else "bf16_tflops"
     out = {
         "metric": wl.metric,
-        "value": round(value, 1),
+        "value": round(value, 3),
         "unit": wl.unit,
         "n_gpus": ws,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": round(ms / args.steps, 4),
+        "ms_per_step": round(ms / args.steps, 5),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": wl.scaling,
         "vs_baseline": None,
-        "dtype": "bf16",
+        "dtype": wl.dtype,
         "data": "synthetic",
-        "config": {
-            "workload": wl.name,
-            "rows_per_gpu": ROWS,
-            "dim": DIM,
-            "eps": EPS,
-            "algorithmic_bytes_per_step_per_gpu": STEP_BYTES,
-            "l2": "inputs larger than L2 (two 448 MiB buffer sets alternate)",
-            "parallelism": f"tokens sharded, {ws} rank(s), dw all-reduce" if ws > 1 else "single GPU",
-        },
+        "config": wl.config(),
         "roofline": {
-            "bound": "hbm",
-            "kernel": dominant[0],
-            "achieved": round(achieved, 1),
+            "bound": wl.bound,
+            "kernel": dom,
+            "achieved": round(achieved, 2),
             "peak": round(peak, 1),
-            "unit": "GB/s",
+            "unit": unit,
             "frac": round(achieved / peak, 4),
-            "peak_source": f"{pk.source} (MEASURED_PEAKS.json hbm_gbs)" if pk.source == "measured" else "fallback 6.65 TB/s",
-            "traffic": _load_traffic(dominant[0]),
-            "kernels_ms": {"add_rmsnorm_fwd": round(fwd_avg, 5), "rmsnorm_bwd+dw_reduce": round(bwd_avg, 5)},
-            "kernels_gbs": {
-                "add_rmsnorm_fwd": round(FWD_BYTES / (fwd_avg / 1e3) / 1e9, 1),
-                "rmsnorm_bwd+dw_reduce": round(BWD_BYTES / (bwd_avg / 1e3) / 1e9, 1),
-            },
+            "peak_source": f"{pk.source} (MEASURED_PEAKS.json {psrc})" if pk.source == "measured" else "fallback",
+            "traffic": _load_traffic(dom),
+            "kernels_ms": {k: round(v, 5) for k, v in bd.items()},
         },
-        "e2e": {
-            "value": round(e2e_value, 2),
-            "unit": wl.unit,
-            "h2d_bytes_per_step": wl.h2d_bytes,
-            "d2h_bytes_per_step": wl.d2h_bytes,
-            "api": "ferrite.kernels.rmsnorm.rmsnorm(x, w, residual=r) + autograd backward, pinned host buffers",
-        },
+        "e2e": {"value": round(e2e_value, 3), "unit": wl.unit, "h2d_bytes_per_step": wl.h2d_bytes, "d2h_bytes_per_step": wl.d2h_bytes, "api": wl.e2e_api},
         "gpu_launches": wl.launches_per_step * args.steps,
         "clocks": clk.summary(),
     }
+    if wl.bound == "hbm":
+        out["roofline"]["kernels_gbs"] = {k: round(wl.kernel_work[k] / (v / 1e3) / 1e9, 1) for k, v in bd.items() if wl.kernel_work.get(k)}
+    else:
+        out["roofline"]["kernels_tflops"] = {k: round(wl.kernel_work[k] / (v / 1e3) / 1e12, 1) for k, v in bd.items() if wl.kernel_work.get(k)}
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        out["cpu_baseline"] = cpu_norm_baseline(sample_rows=args.cpu_rows)
+        cb = W.cpu_baseline()
+        out["cpu_baseline"] = {k: (round(v, 4) if isinstance(v, float) else v) for k, v in cb.items()}
     if ws > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -440,31 +859,32 @@ def run_ours(args, ws, rank, local):
 def run_reference(args, ws, rank):
     if rank != 0:
         return
-    steps = []
-    for _ in range(args.warmup):
-        cpu_norm_baseline(sample_rows=args.cpu_rows, repeats=1)
-    for _ in range(args.steps):
-        steps.append(cpu_norm_baseline(sample_rows=args.cpu_rows, repeats=1))
-    v = statistics.median(s["value"] for s in steps)
-    base = steps[0]
+    W = WORKLOADS[args.workload]
+    heavy = args.workload in ("gpt", "attn", "prefill")
+    for _ in range(1 if heavy else min(args.warmup, 3)):
+        W.cpu_baseline()
+    runs = [W.cpu_baseline() for _ in range(min(args.steps, 3) if heavy else args.steps)]
+    v = statistics.median(r["value"] for r in runs)
+    base = runs[0]
+    per_step_s = statistics.median(r["seconds_per_sample"] for r in runs) / (base.get("sample_fraction") or 1.0)
     out = {
-        "metric": NormWorkload.metric,
-        "value": round(v, 3),
-        "unit": "GB/s",
+        "metric": W.metric,
+        "value": round(v, 4),
+        "unit": W.unit,
         "n_gpus": ws,
-        "steps": args.steps,
+        "steps": len(runs),
         "warmup": args.warmup,
-        "ms_per_step": round(statistics.median(s["seconds_per_sample"] for s in steps) * 1e3 * ROWS / args.cpu_rows, 2),
+        "ms_per_step": round(per_step_s * 1e3, 3),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": W.scaling,
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic",
         "impl": "reference",
-        "config": {"workload": NormWorkload.name, "rows_per_gpu": ROWS, "dim": DIM, "eps": EPS},
-        "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": base["cores"], "kind": "port", "sample": base["sample"]},
-        "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "note": "JAX (the reference's runtime) is not installable here; the reference's CPU path is timed as the numpy restatement in oracle/",
+        "config": {"workload": W.name},
+        "cpu_baseline": {"value": round(v, 4), "unit": W.unit, "cores": base["cores"], "kind": base["kind"], "sample": base["sample"]},
+        "e2e": {"value": round(v, 4), "unit": W.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "JAX (the reference's runtime) is not installable here; the reference's CPU path is timed as its restatement in oracle/",
     }
     print(json.dumps(out), flush=True)
 
@@ -472,11 +892,10 @@ def run_reference(args, ws, rank):
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["norm"], default="norm")
-    ap.add_argument("--cpu-rows", type=int, default=8192, help="rows in the bounded CPU-baseline sample")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="norm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)  # timing rule: at least 3 untimed warm-up steps

@@ -1,0 +1,206 @@
+"""Bucketed prefill on the B200 kernels into a static KV cache, plus greedy decode.
+
+Restates src/ferrite/serving/engine.py: ``ServeConfig`` (:35-40), ``bucket_for``
+(:43-47), ``prefill`` (:69-86: right-padded prompts, per-layer block on the
+kernels, K/V padded to ``max_len`` and stacked into ``[L, B, H, max_len, hd]``),
+``decode_step`` (:107-131), ``Engine`` (:137-209) and ``reference_greedy``
+(:231-242).
+
+B200 mapping of the reference's ahead-of-time compilation: each bucket's prefill
+is captured once into a CUDA graph over static input/output buffers at engine
+construction (the counterpart of ``jit(...).lower(...).compile()``), so serving
+a prompt replays a graph -- no Python-level launch overhead and no shape seen at
+serving time triggers new work.  Decode is one query row against the cache and,
+as in the reference (engine.py:12-15), stays on the plain (``xla``) path: it is
+out of this build's kernel scope.  ``jax.export`` of the decode step has no
+counterpart here.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+import time
+from typing import Any
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from ferrite.model.gpt import GPTConfig, _linear, _lm_head, _norm, block
+
+
+@dataclasses.dataclass(frozen=True)
+class ServeConfig:
+    batch: int = 1
+    max_len: int = 512
+    buckets: tuple[int, ...] = (128, 256, 512)
+    prefill_kernels: str = "pallas"  # "pallas" | "xla" for attention + norms in prefill
+    use_graphs: bool = True
+
+
+def bucket_for(length: int, buckets: tuple[int, ...]) -> int:
+    for b in buckets:
+        if length <= b:
+            return b
+    raise ValueError(f"prompt length {length} exceeds largest bucket {buckets[-1]}")
+
+
+@torch.no_grad()
+def prefill(params, tokens, lengths, cfg: GPTConfig, max_len: int):
+    """tokens [B, L] (right-padded), lengths [B] -> (next-token logits [B, V] f32, k_cache, v_cache).
+
+    Caches are [layers, B, H, max_len, hd]; positions >= length hold padding garbage
+    that decode never attends to and overwrites in order.
+    """
+    b, s = tokens.shape
+    h = (params["tok_emb"][tokens] + params["pos_emb"][:s]).to(cfg.dtype)
+    pending = None
+    kc = torch.zeros(cfg.n_layer, b, cfg.n_head, max_len, cfg.head_dim, dtype=cfg.dtype, device=tokens.device)
+    vc = torch.zeros_like(kc)
+    for i, layer in enumerate(params["layers"]):
+        h, pending, k, v = block(layer, h, pending, cfg)
+        kc[i, :, :, :s] = k
+        vc[i, :, :, :s] = v
+    _, y = _norm(pending, params["ln_f"], h, cfg)
+    last = y[torch.arange(b, device=y.device), (lengths - 1).long()]  # [B, D]
+    logits = _lm_head(last, params["tok_emb"], cfg)
+    return logits, kc, vc
+
+
+def _cache_attention(q, k_cache, v_cache, pos, scale):
+    """q [B, H, hd]; caches [B, H, max_len, hd]; pos [B] = index of the current token (engine.py:89-95)."""
+    s = torch.einsum("bhd,bhkd->bhk", q.float(), k_cache.float()) * scale
+    idx = torch.arange(k_cache.shape[2], device=q.device)[None, :]
+    s = torch.where((idx <= pos[:, None])[:, None, :], s, torch.tensor(-1e30, device=q.device))
+    p = torch.softmax(s, dim=-1)
+    return torch.einsum("bhk,bhkd->bhd", p, v_cache.float()).to(q.dtype)
+
+
+@torch.no_grad()
+def decode_step(params, token, pos, k_cache, v_cache, cfg: GPTConfig):
+    """One greedy decode step (engine.py:107-131); updates the caches in place."""
+    b = token.shape[0]
+    h = (params["tok_emb"][token] + params["pos_emb"][pos]).to(cfg.dtype)  # [B, D]
+    scale = 1.0 / np.sqrt(cfg.head_dim)
+    pending = None
+    ar = torch.arange(b, device=token.device)
+    for i, layer in enumerate(params["layers"]):
+        if pending is None:
+            y = _norm(h, layer["ln1"], None, cfg)
+        else:
+            h, y = _norm(pending, layer["ln1"], h, cfg)
+        qkv = _linear(y, layer["wqkv"], cfg).reshape(b, 3, cfg.n_head, cfg.head_dim)
+        q, k, v = qkv[:, 0], qkv[:, 1], qkv[:, 2]
+        k_cache[i, ar, :, pos] = k.to(k_cache.dtype)
+        v_cache[i, ar, :, pos] = v.to(v_cache.dtype)
+        a = _cache_attention(q, k_cache[i], v_cache[i], pos, scale).reshape(b, cfg.d_model)
+        a = _linear(a, layer["wo"], cfg)
+        h, y2 = _norm(a, layer["ln2"], h, cfg)
+        pending = _linear(F.gelu(_linear(y2, layer["w1"], cfg), approximate="tanh"), layer["w2"], cfg)
+    _, y = _norm(pending, params["ln_f"], h, cfg)
+    return torch.matmul(y.float(), params["tok_emb"].float().t())
+
+
+class Engine:
+    """Captures prefill per bucket (CUDA graphs) and generates greedily (engine.py:137-209)."""
+
+    def __init__(self, params, model_cfg: GPTConfig, serve_cfg: ServeConfig):
+        if max(serve_cfg.buckets) > model_cfg.seq_len or serve_cfg.max_len > model_cfg.seq_len:
+            raise ValueError("buckets and max_len must fit within the model's trained seq_len (positional table)")
+        self.params = params
+        self.cfg = model_cfg
+        self.serve = serve_cfg
+        self.prefill_cfg = model_cfg if serve_cfg.prefill_kernels == "pallas" else model_cfg.replace(attention="xla", norm="xla", linear="xla")
+        self.decode_cfg = model_cfg.replace(attention="xla", norm="xla", linear="xla")
+        self.device = params["tok_emb"].device
+        self.compile_seconds: dict[str, float] = {}
+        self._graphs: dict[int, Any] = {}
+        b = serve_cfg.batch
+        for bucket in serve_cfg.buckets:
+            t0 = time.perf_counter()
+            tok = torch.zeros(b, bucket, dtype=torch.long, device=self.device)
+            lens = torch.ones(b, dtype=torch.long, device=self.device)
+            if serve_cfg.use_graphs:
+                s = torch.cuda.Stream(self.device)
+                s.wait_stream(torch.cuda.current_stream(self.device))
+                with torch.cuda.stream(s):
+                    for _ in range(2):  # warm-up: module loading, allocator pools
+                        prefill(params, tok, lens, self.prefill_cfg, serve_cfg.max_len)
+                torch.cuda.current_stream(self.device).wait_stream(s)
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    out = prefill(params, tok, lens, self.prefill_cfg, serve_cfg.max_len)
+                self._graphs[bucket] = (g, tok, lens, out)
+            else:
+                self._graphs[bucket] = (None, tok, lens, None)
+            torch.cuda.synchronize(self.device)
+            self.compile_seconds[f"prefill_{bucket}"] = time.perf_counter() - t0
+        self.n_compiles = len(self.compile_seconds) + 1  # + decode (eager, plain path)
+
+    def prefill(self, prompts: list[list[int]]):
+        """Returns (first token [B], pos [B], caches). Prompts are right-padded to a bucket."""
+        b = self.serve.batch
+        if len(prompts) != b:
+            raise ValueError(f"engine built for batch {b}, got {len(prompts)} prompts")
+        lengths = np.array([len(p) for p in prompts], np.int64)
+        bucket = bucket_for(int(lengths.max()), self.serve.buckets)
+        tokens = np.zeros((b, bucket), np.int64)
+        for i, p in enumerate(prompts):
+            tokens[i, : len(p)] = p
+        g, tok, lens, out = self._graphs[bucket]
+        tok.copy_(torch.from_numpy(tokens), non_blocking=True)
+        lens.copy_(torch.from_numpy(lengths), non_blocking=True)
+        if g is not None:
+            g.replay()
+            logits, kc, vc = out
+            kc, vc = kc.clone(), vc.clone()  # the graph's buffers are reused by the next replay
+        else:
+            logits, kc, vc = prefill(self.params, tok, lens, self.prefill_cfg, self.serve.max_len)
+        return torch.argmax(logits, dim=-1), torch.from_numpy(lengths).to(self.device), kc, vc
+
+    def decode(self, token, pos, kc, vc):
+        logits = decode_step(self.params, token, pos, kc, vc, self.decode_cfg)
+        return torch.argmax(logits, dim=-1), kc, vc
+
+    def generate(self, prompts: list[list[int]], max_new_tokens: int) -> tuple[np.ndarray, dict]:
+        if max(len(p) for p in prompts) + max_new_tokens > self.serve.max_len:
+            raise ValueError("prompt + new tokens exceed max_len")
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        e0.record()
+        token, pos, kc, vc = self.prefill(prompts)
+        e1.record()
+        out = [token.cpu().numpy()]
+        ttft = e0.elapsed_time(e1)
+        step_times = []
+        for _ in range(max_new_tokens - 1):
+            t = time.perf_counter()
+            token, kc, vc = self.decode(token, pos, kc, vc)
+            out.append(token.cpu().numpy())
+            step_times.append(time.perf_counter() - t)
+            pos = pos + 1
+        total = time.perf_counter() - t0
+        stats = {
+            "ttft_ms": ttft,
+            "itl_ms_median": float(np.median(step_times)) * 1e3 if step_times else float("nan"),
+            "tokens_per_second": len(prompts) * max_new_tokens / total,
+            "total_s": total,
+            "n_compiles": self.n_compiles,
+        }
+        return np.stack(out, axis=1), stats
+
+
+@torch.no_grad()
+def reference_greedy(params, cfg: GPTConfig, prompt: list[int], max_new_tokens: int) -> np.ndarray:
+    """Slow but obviously-correct greedy decoding by re-running the full model each step."""
+    from ferrite.model.gpt import forward
+
+    toks = list(prompt)
+    out = []
+    dev = params["tok_emb"].device
+    for _ in range(max_new_tokens):
+        logits = forward(params, torch.tensor([toks], device=dev), cfg)
+        nxt = int(torch.argmax(logits[0, -1]))
+        out.append(nxt)
+        toks.append(nxt)
+    return np.array(out)

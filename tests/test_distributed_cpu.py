@@ -1,0 +1,119 @@
+"""Multi-rank host logic on CPU with ``gloo`` (world size 2): the data-parallel
+gradient all-reduce of the training step, the token-sharded RMSNorm backward's dw
+exchange (the only collective of the sharded bench), and failure detection when a
+rank leaves (a short process-group timeout turns the missing rank into an error
+on the survivor)."""
+
+import os
+import socket
+import sys
+import tempfile
+from datetime import timedelta
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _init(rank, ws, port, timeout_s=30):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    sys.path[:0] = [ROOT, os.path.join(ROOT, "ferrite-tpu_b200")]
+    dist.init_process_group("gloo", rank=rank, world_size=ws, timeout=timedelta(seconds=timeout_s))
+
+
+def _dp_worker(rank, ws, port, out):
+    _init(rank, ws, port)
+    from ferrite.model.train import FlatGrads
+
+    torch.manual_seed(0)
+    params = [torch.zeros(3, 4, requires_grad=True), torch.zeros(5, requires_grad=True)]
+    flat = FlatGrads(params)
+    flat.zero()
+    loss = (params[0] * (rank + 1)).sum() + (params[1] * (2.0 * rank)).sum()
+    loss.backward()
+    flat.all_reduce_mean()
+    torch.save([p.grad.clone() for p in params], os.path.join(out, f"g{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _norm_worker(rank, ws, port, out):
+    _init(rank, ws, port)
+    from oracle import rmsnorm as on
+
+    rng = np.random.default_rng(7)
+    rows, dim = 64, 48
+    h = rng.standard_normal((rows, dim)).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(dim)).astype(np.float32)
+    dy = rng.standard_normal((rows, dim)).astype(np.float32)
+    shard = slice(rank * rows // ws, (rank + 1) * rows // ws)
+    dh, dw = on.rmsnorm_bwd(h[shard], w, dy[shard])
+    t = torch.from_numpy(dw.copy())
+    dist.all_reduce(t)
+    np.save(os.path.join(out, f"dw{rank}.npy"), t.numpy())
+    np.save(os.path.join(out, f"dh{rank}.npy"), dh)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _leaver_worker(rank, ws, port, out):
+    _init(rank, ws, port, timeout_s=3)
+    if rank == 1:
+        return  # leaves between steps, never joins the next collective
+    t = torch.ones(4)
+    try:
+        dist.all_reduce(t)
+        status = "no-error"
+    except Exception as e:  # noqa: BLE001
+        status = "error:" + type(e).__name__
+    with open(os.path.join(out, "status.txt"), "w") as f:
+        f.write(status)
+
+
+def _run(fn, ws=2):
+    out = tempfile.mkdtemp()
+    mp.start_processes(fn, args=(ws, _free_port(), out), nprocs=ws, join=True, start_method="spawn")
+    return out
+
+
+def test_dp_gradient_all_reduce_is_the_mean():
+    out = _run(_dp_worker)
+    g0 = torch.load(os.path.join(out, "g0.pt"))
+    g1 = torch.load(os.path.join(out, "g1.pt"))
+    for a, b in zip(g0, g1):
+        assert torch.equal(a, b)
+    assert torch.allclose(g0[0], torch.full((3, 4), 1.5)) and torch.allclose(g0[1], torch.full((5,), 1.0))
+
+
+def test_token_sharded_rmsnorm_backward_exchange():
+    out = _run(_norm_worker)
+    sys.path.insert(0, ROOT)
+    from oracle import rmsnorm as on
+
+    rng = np.random.default_rng(7)
+    h = rng.standard_normal((64, 48)).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(48)).astype(np.float32)
+    dy = rng.standard_normal((64, 48)).astype(np.float32)
+    dh_full, dw_full = on.rmsnorm_bwd(h, w, dy)
+    for r in range(2):
+        np.testing.assert_allclose(np.load(os.path.join(out, f"dw{r}.npy")), dw_full, rtol=1e-5, atol=1e-5)
+    dh = np.concatenate([np.load(os.path.join(out, f"dh{r}.npy")) for r in range(2)])
+    np.testing.assert_array_equal(dh, dh_full)  # row-local: sharding changes nothing
+
+
+@pytest.mark.timeout(120)
+def test_missing_rank_surfaces_as_an_error():
+    out = _run(_leaver_worker)
+    status = open(os.path.join(out, "status.txt")).read()
+    assert status.startswith("error:"), status
