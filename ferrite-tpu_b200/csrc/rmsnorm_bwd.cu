@@ -1,5 +1,7 @@
 // RMSNorm backward kernels (dh and the deterministic dw reduction) and their
 // C-ABI entry points.
+#include <mutex>
+
 #include "rmsnorm_common.cuh"
 
 namespace ferrite {
@@ -347,6 +349,95 @@ static int run_bwd(cudaStream_t s, const void* h, const void* w, const void* dy,
   return check_launch("rmsnorm_dw_reduce");
 }
 
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant (ferrite_rmsnorm_bwd_noalloc)
+// ---------------------------------------------------------------------------
+//
+// Some callers cannot hand the backward a workspace: a host framework that owns
+// all device memory and gives its kernels no scratch allocator, or a runtime that
+// sizes its device arena once at start-up and allows no allocation afterwards
+// (cudaMalloc / cudaFree can synchronise the device and are not stream-ordered).
+// For them the dw partial sums live in a library-owned, file-scope device array
+// of fixed size instead of a caller workspace.  Every GPU that loads the library
+// holds this array (4 MiB) until the process exits.
+
+// Capacity of the library-owned dw partial buffer, in floats (4 MiB per device).
+constexpr int64_t kNoAllocPartialFloats = int64_t(1) << 20;
+// Largest row length the allocation-free variant accepts: its scalar plan needs
+// 8 partial rows per CTA and at least one CTA.
+constexpr int64_t kNoAllocMaxDim = kNoAllocPartialFloats / 8;
+
+static __device__ __align__(256) float g_noalloc_partials[kNoAllocPartialFloats];
+
+namespace {
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[64] = {nullptr};
+}  // namespace
+
+// Device address of g_noalloc_partials on `device` (which must be current).  In
+// host code the array's name is only a host-side stand-in, so the address is
+// looked up once per device with cudaGetSymbolAddress and cached.
+static int noalloc_partials(int device, float** out) {
+  if (device < 0 || device >= 64)
+    return fail(FERRITE_BAD_SHAPE, "rmsnorm_bwd_noalloc: device ordinal %d out of range", device);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[device] == nullptr) {
+    void* addr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&addr, g_noalloc_partials);
+    if (e != cudaSuccess || addr == nullptr)
+      return fail(FERRITE_LAUNCH_FAILED, "rmsnorm_bwd_noalloc: cudaGetSymbolAddress failed: %s",
+                  cudaGetErrorString(e));
+    g_noalloc_ptr[device] = static_cast<float*>(addr);
+  }
+  *out = g_noalloc_ptr[device];
+  return FERRITE_OK;
+}
+
+template <typename T, typename TW, bool HAS_DH>
+static int run_bwd_noalloc(cudaStream_t s, const void* h, const void* w, const void* dy,
+                           const void* dhd, void* dh, void* dw, int64_t rows, int64_t dim,
+                           float eps) {
+  const int dev = current_device();
+  float* part = nullptr;
+  if (int rc = noalloc_partials(dev, &part)) return rc;
+  const void* ptrs[5] = {h, dy, HAS_DH ? dhd : nullptr, dh, w};
+  BwdPlan p = plan_bwd<T, TW, HAS_DH>(rows, dim, ptrs, 5, dev);
+  // Fit the partial rows into the fixed buffer (the persistent kernels accept
+  // any grid size; a smaller grid only means more rows per CTA).
+  const int64_t max_rows = kNoAllocPartialFloats / dim;
+  if (p.c.vec) {
+    p.grid = (int)std::max<int64_t>(1, std::min<int64_t>(p.grid, max_rows));
+    p.nparts = p.grid;
+  } else {
+    p.grid = (int)std::max<int64_t>(1, std::min<int64_t>(p.grid, max_rows / 8));
+    p.nparts = p.grid * 8;
+  }
+  if ((int64_t)p.nparts * dim > kNoAllocPartialFloats)
+    return fail(FERRITE_BAD_SHAPE, "rmsnorm_bwd_noalloc: dim %lld needs more than the %lld-float buffer",
+                (long long)dim, (long long)kNoAllocPartialFloats);
+  if (p.c.vec) {
+    void* k = bwd_ptr<T, TW, HAS_DH>(p.c);
+    const int CTA = bwd_cta(p.c.tpr);
+    int dimi = (int)dim;
+    const T* hp = (const T*)h;
+    const TW* wp = (const TW*)w;
+    const T* dyp = (const T*)dy;
+    const T* dhdp = (const T*)dhd;
+    T* dhp = (T*)dh;
+    void* args[] = {&hp, &wp, &dyp, &dhdp, &dhp, &part, &rows, &dimi, &eps};
+    cudaError_t e = cudaLaunchKernel(k, dim3(p.grid), dim3(CTA), args, p.smem, s);
+    if (e != cudaSuccess)
+      return fail(FERRITE_LAUNCH_FAILED, "rmsnorm_bwd_noalloc: %s", cudaGetErrorString(e));
+  } else {
+    rmsnorm_bwd_scalar<T, TW, HAS_DH><<<p.grid, 256, 0, s>>>(
+        (const T*)h, (const TW*)w, (const T*)dy, (const T*)dhd, (T*)dh, part, rows, (int)dim, eps);
+  }
+  if (int rc = check_launch("rmsnorm_bwd_noalloc")) return rc;
+  dw_reduce_kernel<TW><<<(unsigned)((dim + 31) / 32), 1024, 0, s>>>(part, (TW*)dw, p.nparts, (int)dim);
+  return check_launch("rmsnorm_bwd_noalloc_dw_reduce");
+}
+
 }  // namespace norm
 }  // namespace ferrite
 
@@ -386,6 +477,39 @@ int ferrite_rmsnorm_bwd(void* stream, const void* h, const void* w,
   if (dtype == FERRITE_F16 && w_dtype == FERRITE_F32) return CALL(__half, float);
 #undef CALL
   return fail(FERRITE_UNSUPPORTED_DTYPE, "rmsnorm_bwd: dtype");
+}
+
+
+// Allocation-free RMSNorm backward; see the section comment above and the
+// declaration in ferrite_b200.h.  The first call on a device looks up the
+// buffer's device address (cudaGetSymbolAddress) with that device current;
+// make that first call before any stream capture.
+int ferrite_rmsnorm_bwd_noalloc(void* stream, const void* h, const void* w, const void* dy,
+                                const void* dh_direct, void* dh, void* dw, int64_t rows,
+                                int64_t dim, float eps, int dtype, int w_dtype) {
+  if (int rc = check_common("rmsnorm_bwd_noalloc", rows, dim, dtype, w_dtype)) return rc;
+  if (dim > kNoAllocMaxDim)
+    return fail(FERRITE_BAD_SHAPE,
+                "rmsnorm_bwd_noalloc: dim %lld exceeds the allocation-free maximum %lld",
+                (long long)dim, (long long)kNoAllocMaxDim);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (!dw) return fail(FERRITE_BAD_SHAPE, "rmsnorm_bwd_noalloc: null dw");
+  if (rows == 0) {
+    cudaError_t e = cudaMemsetAsync(dw, 0, dim * (w_dtype == FERRITE_F32 ? 4 : 2), s);
+    return e == cudaSuccess ? FERRITE_OK
+                            : fail(FERRITE_LAUNCH_FAILED, "rmsnorm_bwd_noalloc: memset");
+  }
+  if (!h || !w || !dy || !dh) return fail(FERRITE_BAD_SHAPE, "rmsnorm_bwd_noalloc: null pointer");
+  const bool has = dh_direct != nullptr;
+#define CALL(T, TW)                                                                         \
+  (has ? run_bwd_noalloc<T, TW, true>(s, h, w, dy, dh_direct, dh, dw, rows, dim, eps)       \
+       : run_bwd_noalloc<T, TW, false>(s, h, w, dy, dh_direct, dh, dw, rows, dim, eps))
+  if (dtype == FERRITE_BF16 && w_dtype == FERRITE_F32) return CALL(__nv_bfloat16, float);
+  if (dtype == FERRITE_BF16 && w_dtype == FERRITE_BF16) return CALL(__nv_bfloat16, __nv_bfloat16);
+  if (dtype == FERRITE_F32 && w_dtype == FERRITE_F32) return CALL(float, float);
+  if (dtype == FERRITE_F16 && w_dtype == FERRITE_F32) return CALL(__half, float);
+#undef CALL
+  return fail(FERRITE_UNSUPPORTED_DTYPE, "rmsnorm_bwd_noalloc: dtype");
 }
 
 }  // extern "C"

@@ -59,6 +59,7 @@ SIGNATURES: dict[str, tuple] = {
     "ferrite_add_rmsnorm_fwd": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f32, _i32, _i32]),
     "ferrite_rmsnorm_bwd_workspace_size": (_sz, [_i64, _i64]),
     "ferrite_rmsnorm_bwd": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _i64, _i64, _f32, _i32, _i32]),
+    "ferrite_rmsnorm_bwd_noalloc": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f32, _i32, _i32]),
     "ferrite_gemm": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _i32, _i32]),
     "ferrite_attn_fwd": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _i32, _i32, _i32]),
     "ferrite_attn_bwd_prep": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32]),

@@ -94,6 +94,23 @@ FERRITE_API int ferrite_rmsnorm_bwd(void* stream, const void* h, const void* w,
                         int64_t rows, int64_t dim, float eps, int dtype,
                         int w_dtype);
 
+/* Allocation-free variant of ferrite_rmsnorm_bwd (same arguments minus the
+ * workspace).  No counterpart in the reference: it exists for callers that cannot
+ * allocate device memory -- a host framework that owns all device memory and
+ * gives its kernels no scratch allocator, or a runtime that sizes its device
+ * arena once and allows no allocation afterwards (cudaMalloc/cudaFree can
+ * synchronise the device and are not stream-ordered).  The dw partial sums live
+ * in a library-owned device array of 2^20 floats (4 MiB, held on every GPU that
+ * loads the library until the process exits); dim above 131072 is rejected with
+ * FERRITE_BAD_SHAPE.  The first call on a device looks the array's address up
+ * (that device must be current); make it before any stream capture.  All calls
+ * share the array, so calls that overlap on the GPU (e.g. on two streams) race;
+ * nothing in it needs clearing between calls. */
+FERRITE_API int ferrite_rmsnorm_bwd_noalloc(void* stream, const void* h, const void* w,
+                        const void* dy, const void* dh_direct, void* dh,
+                        void* dw, int64_t rows, int64_t dim, float eps,
+                        int dtype, int w_dtype);
+
 /* ---- matmul ---------------------------------------------------------------- */
 
 /* C[M,N] = op(A)[M,K] @ op(B)[K,N] with an f32 accumulator, cast to c_dtype.
