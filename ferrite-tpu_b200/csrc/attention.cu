@@ -32,6 +32,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdlib>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -498,10 +499,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         tmem_ld32(t_s + 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[64]));
         tmem_ld32(t_s + 96, *reinterpret_cast<uint32_t(*)[32]>(&sv[96]));
         tmem_wait_ld();
+        if (diag || !(p.scale_log2 > 0.f)) {
 #pragma unroll
-        for (int i = 0; i < TK; ++i) {
-          const float x = (diag && i > kmax) ? kMaskValue : __uint_as_float(sv[i]) * p.scale_log2;
-          mx = fmaxf(mx, x);
+          for (int i = 0; i < TK; ++i)
+            mx = fmaxf(mx, (diag && i > kmax) ? kMaskValue : __uint_as_float(sv[i]) * p.scale_log2);
+        } else {
+#pragma unroll
+          for (int i = 0; i < TK; ++i) mx = fmaxf(mx, __uint_as_float(sv[i]));
+          mx *= p.scale_log2;  // scale > 0: max commutes with the scaling
         }
       }
       const float m_new = fmaxf(m_used, mx);
@@ -534,25 +539,35 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       // pass 2, two halves of 64 keys: p = 2^(x - m) rounded to the input dtype,
       // packed in pairs into S columns [0, 64) (already consumed).
       float rs = 0.f;
+      auto pass2 = [&](auto masked) {
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t sv[64];
-        tmem_ld32(t_s + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-        tmem_ld32(t_s + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
-        tmem_wait_ld();
-        uint32_t pk[32];
+        for (int half = 0; half < 2; ++half) {
+          uint32_t sv[64];
+          tmem_ld32(t_s + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+          tmem_ld32(t_s + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+          tmem_wait_ld();
+          uint32_t pk[32];
 #pragma unroll
-        for (int i = 0; i < 64; i += 2) {
-          const int col = half * 64 + i;
-          const float x0 = (diag && col > kmax) ? kMaskValue : __uint_as_float(sv[i]) * p.scale_log2;
-          const float x1 = (diag && col + 1 > kmax) ? kMaskValue : __uint_as_float(sv[i + 1]) * p.scale_log2;
-          const float p0 = ex2_approx(x0 - m_used);
-          const float p1 = ex2_approx(x1 - m_used);
-          rs += p0 + p1;
-          pk[i / 2] = BF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
+          for (int i = 0; i < 64; i += 2) {
+            float x0 = fmaf(__uint_as_float(sv[i]), p.scale_log2, -m_used);
+            float x1 = fmaf(__uint_as_float(sv[i + 1]), p.scale_log2, -m_used);
+            if constexpr (decltype(masked)::value) {
+              const int col = half * 64 + i;
+              x0 = col > kmax ? -INFINITY : x0;
+              x1 = col + 1 > kmax ? -INFINITY : x1;
+            }
+            const float p0 = ex2_approx(x0);
+            const float p1 = ex2_approx(x1);
+            rs += p0 + p1;
+            pk[i / 2] = BF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
+          }
+          tmem_st32(t_s + half * 32, pk);
         }
-        tmem_st32(t_s + half * 32, pk);
-      }
+      };
+      if (diag)
+        pass2(std::true_type{});
+      else
+        pass2(std::false_type{});
       l += rs;
       tmem_wait_st();
       tc_fence_before();
@@ -856,34 +871,49 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         st = reinterpret_cast<const float*>(smem + L::kYOff + s * L::kStageBytes + 2 * L::kYBytes);
       }
       tmem_wait_ld();
+      // Masking is tile-uniform except on the causal diagonal and past sq; the
+      // exponent input is set to -inf where masked (ex2.approx.ftz(-inf) = +0),
+      // so the loop has no per-element branches.
+      bool need_mask;
+      if constexpr (IS_DKV)
+        need_mask = (y0 + BY > p.sq) || (p.causal && x0 + BX - 1 > y0 + diag_shift);
+      else
+        need_mask = (x0 + BX > p.sq) || (p.causal && y0 + BY - 1 > x0 + diag_shift);
       uint32_t pp[BY / 2], dd[BY / 2];
+      auto body = [&](auto masked) {
 #pragma unroll
-      for (int e = 0; e < BY; e += 2) {
-        float pv[2], dv[2];
+        for (int e = 0; e < BY; e += 2) {
+          float pv[2], dv[2];
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const int c = e + u;  // streaming column
-          int key, qry;
-          float l2, dl;
-          if constexpr (IS_DKV) {
-            key = xrow;
-            qry = y0 + c;
-            l2 = st[c] * kLog2e;
-            dl = st[BY + c];
-          } else {
-            key = y0 + c;
-            qry = xrow;
-            l2 = row_lse2;
-            dl = row_delta;
+          for (int u = 0; u < 2; ++u) {
+            const int c = e + u;  // streaming column
+            float l2, dl;
+            if constexpr (IS_DKV) {
+              l2 = st[c] * kLog2e;
+              dl = st[BY + c];
+            } else {
+              l2 = row_lse2;
+              dl = row_delta;
+            }
+            float x = fmaf(__uint_as_float(a[c]), p.scale_log2, -l2);
+            if constexpr (decltype(masked)::value) {
+              const int key = IS_DKV ? xrow : y0 + c;
+              const int qry = IS_DKV ? y0 + c : xrow;
+              const bool valid = qry < p.sq && !(p.causal && key > qry + diag_shift);
+              x = valid ? x : -INFINITY;
+            }
+            const float pr = ex2_approx(x);
+            pv[u] = pr;
+            dv[u] = pr * (__uint_as_float(b[c]) - dl);
           }
-          const bool valid = qry < p.sq && !(p.causal && key > qry + diag_shift);
-          const float pr = valid ? ex2_approx(fmaf(__uint_as_float(a[c]), p.scale_log2, -l2)) : 0.f;
-          pv[u] = pr;
-          dv[u] = pr * (__uint_as_float(b[c]) - dl);
+          pp[e / 2] = BF16 ? pack_bf16x2(pv[0], pv[1]) : pack_f16x2(pv[0], pv[1]);
+          dd[e / 2] = BF16 ? pack_bf16x2(dv[0], dv[1]) : pack_f16x2(dv[0], dv[1]);
         }
-        pp[e / 2] = BF16 ? pack_bf16x2(pv[0], pv[1]) : pack_f16x2(pv[0], pv[1]);
-        dd[e / 2] = BF16 ? pack_bf16x2(dv[0], dv[1]) : pack_f16x2(dv[0], dv[1]);
-      }
+      };
+      if (need_mask)
+        body(std::true_type{});
+      else
+        body(std::false_type{});
       if constexpr (IS_DKV) tmem_st32(t_t1, pp);
       tmem_st32(t_t2, dd);
       tmem_wait_st();
