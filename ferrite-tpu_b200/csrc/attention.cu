@@ -428,25 +428,28 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       constexpr uint32_t idesc_o = make_idesc_f16(TQ, D, BF16, false, true);
       const uint32_t sq_ = smem_u32(smem + L::kQOff);
       bool ok = mbar_wait(q_full, 0, abort, 11) && mbar_wait(&kv_full[0], 0, abort, 12);
+      // Descriptors are built once; each MMA adds a compile-time byte offset.
+      const uint64_t dq_base = make_sdesc(sq_, 16, 1024);
+      const uint64_t dk_base = make_sdesc(smem_u32(smem + L::kKVOff), 16, 1024);
+      const uint64_t dv_base = make_sdesc(smem_u32(smem + L::kKVOff + L::kKBytes), TK * 128, 1024);
       auto issue_s = [&](int g, int j) {
-        const uint32_t sk_ = smem_u32(smem + L::kKVOff + (j & 1) * L::kStageBytes);
-        const uint32_t qa = sq_ + g * L::kQBytes;
+        const uint64_t dq = sdesc_at(dq_base, g * L::kQBytes);
+        const uint64_t dk = sdesc_at(dk_base, (j & 1) * L::kStageBytes);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t qo = (kk >> 2) * (TQ * 128) + (kk & 3) * 32;
           const uint32_t ko = (kk >> 2) * (TK * 128) + (kk & 3) * 32;
-          tc_mma_f16_ss(tmem + g * 128, make_sdesc(qa + qo, 16, 1024), make_sdesc(sk_ + ko, 16, 1024),
-                        idesc_s, kk != 0);
+          tc_mma_f16_ss(tmem + g * 128, sdesc_at(dq, qo), sdesc_at(dk, ko), idesc_s, kk != 0);
         }
         tc_commit(&s_full[g]);
       };
       auto issue_pv = [&](int g, int j) {
-        const uint32_t sv_ = smem_u32(smem + L::kKVOff + (j & 1) * L::kStageBytes + L::kKBytes);
+        const uint64_t dv = sdesc_at(dv_base, (j & 1) * L::kStageBytes);
         const uint32_t pa = tmem + g * 128;  // P_g: packed pairs in S columns [0, 64)
 #pragma unroll
         for (int kk = 0; kk < TK / 16; ++kk)
-          tc_mma_f16_ts(tmem + 256 + g * D, pa + kk * 8, make_sdesc(sv_ + kk * 2048, TK * 128, 1024),
-                        idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          tc_mma_f16_ts(tmem + 256 + g * D, pa + kk * 8, sdesc_at(dv, kk * 2048), idesc_o,
+                        (j > 0 || kk > 0) ? 1u : 0u);
         tc_commit(&pv_done[g]);
       };
       if (ok) {
@@ -661,8 +664,8 @@ struct BwdSmem {
   static constexpr int kX2Off = kXBytes;
   static constexpr int kYOff = 2 * kXBytes;
   static constexpr int kBarOff = kYOff + kYStages * kStageBytes;
-  // x_full, y_full[S], y_empty[S], t_full[2], e_full[2], acc_full
-  static constexpr int kNumBars = 2 * kYStages + 6;
+  // x_full, y_full[S], y_empty[S], t_full[2], e_full[2], acc_full, x_tmem
+  static constexpr int kNumBars = 2 * kYStages + 7;
   static constexpr int kTotal = 1024 + kBarOff + kNumBars * 8 + 16;
 };
 
@@ -696,11 +699,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint64_t* t_full = bars + 1 + 2 * kYStages;
   uint64_t* e_full = t_full + 2;
   uint64_t* acc_full = e_full + 2;
+  uint64_t* x_tmem = acc_full + 1;  // dQ: Q and dO copied into TMEM
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kNumBars);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int xt = p.n_x_tiles - 1 - (int)blockIdx.x;  // heaviest tiles first
+  // Heaviest tiles first: under a causal mask early key tiles (dK/dV) and late
+  // query tiles (dQ) see the most streaming tiles.
+  const int xt = IS_DKV ? (int)blockIdx.x : p.n_x_tiles - 1 - (int)blockIdx.x;
   const int bh = blockIdx.y;
   const int x0 = xt * BX;
   const int x_len = IS_DKV ? p.sk : p.sq;  // rows of the stationary operand
@@ -722,6 +728,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(x_full, 1);
     mbar_init(acc_full, 1);
+    mbar_init(x_tmem, 4);
     for (int i = 0; i < kYStages; ++i) {
       mbar_init(&y_full[i], 1);
       mbar_init(&y_empty[i], 1);
@@ -741,9 +748,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM columns: T1[2] at 0/64, T2[2] at 128/192, acc0 at 256, acc1 at 256 + D
+  // TMEM columns: T1[2] at 0/64, T2[2] at 128/192, acc0 at 256, then
+  //   dK/dV: acc1 at 256 + D;
+  //   dQ:    Q and dO as packed 16-bit pairs (A operands of the T MMAs, read from
+  //          TMEM so those small-N MMAs only stream the K/V tile from shared
+  //          memory) at 256 + D and 256 + D + D/2.
   const uint32_t t_acc0 = tmem + 256;
   const uint32_t t_acc1 = tmem + 256 + D;
+  const uint32_t t_xq = tmem + 256 + D;
+  const uint32_t t_xdo = tmem + 256 + D + D / 2;
 
   if (warp == 0) {
     if (lane == 0 && n_y > 0) {
@@ -783,18 +796,29 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const uint32_t sx1 = smem_u32(smem + L::kX1Off);
       const uint32_t sx2 = smem_u32(smem + L::kX2Off);
       bool ok = mbar_wait(x_full, 0, abort, 21);
+      if constexpr (!IS_DKV) ok = ok && mbar_wait(x_tmem, 0, abort, 29);
+      // Descriptors are built once; each MMA adds a compile-time byte offset.
+      const uint64_t dx1 = make_sdesc(sx1, 16, 1024);
+      const uint64_t dx2 = make_sdesc(sx2, 16, 1024);
+      const uint64_t dy_k = make_sdesc(smem_u32(smem + L::kYOff), 16, 1024);          // Y, K-major
+      const uint64_t dy_mn = make_sdesc(smem_u32(smem + L::kYOff), BY * 128, 1024);   // Y, MN-major
       auto issue_t = [&](int i) -> bool {
         const int s = i % kYStages, b = i & 1;
         if (!mbar_wait(&y_full[s], (i / kYStages) & 1, abort, 22)) return false;
         tc_fence_after();
-        const uint32_t sy1 = smem_u32(smem + L::kYOff + s * L::kStageBytes);
-        const uint32_t sy2 = sy1 + L::kYBytes;
+        const uint64_t dy1 = sdesc_at(dy_k, s * L::kStageBytes);
+        const uint64_t dy2 = sdesc_at(dy1, L::kYBytes);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t xo = (kk >> 2) * (BX * 128) + (kk & 3) * 32;
           const uint32_t yo = (kk >> 2) * (BY * 128) + (kk & 3) * 32;
-          tc_mma_f16_ss(tmem + b * 64, make_sdesc(sx1 + xo, 16, 1024), make_sdesc(sy1 + yo, 16, 1024), idesc_t, kk != 0);
-          tc_mma_f16_ss(tmem + 128 + b * 64, make_sdesc(sx2 + xo, 16, 1024), make_sdesc(sy2 + yo, 16, 1024), idesc_t, kk != 0);
+          if constexpr (IS_DKV) {
+            tc_mma_f16_ss(tmem + b * 64, sdesc_at(dx1, xo), sdesc_at(dy1, yo), idesc_t, kk != 0);
+            tc_mma_f16_ss(tmem + 128 + b * 64, sdesc_at(dx2, xo), sdesc_at(dy2, yo), idesc_t, kk != 0);
+          } else {
+            tc_mma_f16_ts(tmem + b * 64, t_xq + kk * 8, sdesc_at(dy1, yo), idesc_t, kk != 0);
+            tc_mma_f16_ts(tmem + 128 + b * 64, t_xdo + kk * 8, sdesc_at(dy2, yo), idesc_t, kk != 0);
+          }
         }
         tc_commit(&t_full[b]);
         return true;
@@ -803,8 +827,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int s = i % kYStages, b = i & 1;
         if (!mbar_wait(&e_full[b], (i >> 1) & 1, abort, 24)) return false;
         tc_fence_after();
-        const uint32_t sy1 = smem_u32(smem + L::kYOff + s * L::kStageBytes);
-        const uint32_t sy2 = sy1 + L::kYBytes;
+        const uint64_t dm1 = sdesc_at(dy_mn, s * L::kStageBytes);
+        const uint64_t dm2 = sdesc_at(dm1, L::kYBytes);
         const uint32_t tP = tmem + b * 64;         // P (dK/dV only): T1 columns [0, 32)
         const uint32_t tdS = tmem + 128 + b * 64;  // dS: T2 columns [0, 32)
 #pragma unroll
@@ -813,11 +837,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
           if constexpr (IS_DKV) {
             // dV += P^T dO   (acc1),   dK += dS^T Q  (acc0)
-            tc_mma_f16_ts(t_acc1, tP + kk * 8, make_sdesc(sy2 + yo, BY * 128, 1024), idesc_a, acc);
-            tc_mma_f16_ts(t_acc0, tdS + kk * 8, make_sdesc(sy1 + yo, BY * 128, 1024), idesc_a, acc);
+            tc_mma_f16_ts(t_acc1, tP + kk * 8, sdesc_at(dm2, yo), idesc_a, acc);
+            tc_mma_f16_ts(t_acc0, tdS + kk * 8, sdesc_at(dm1, yo), idesc_a, acc);
           } else {
             // dQ += dS K  (acc0)
-            tc_mma_f16_ts(t_acc0, tdS + kk * 8, make_sdesc(sy1 + yo, BY * 128, 1024), idesc_a, acc);
+            tc_mma_f16_ts(t_acc0, tdS + kk * 8, sdesc_at(dm1, yo), idesc_a, acc);
           }
         }
         tc_commit(&y_empty[s]);
@@ -840,6 +864,37 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
     const uint32_t t_t1 = tmem + lane_off + g * 64;
     const uint32_t t_t2 = tmem + lane_off + 128 + g * 64;
+    if constexpr (!IS_DKV) {
+      // Group 0 moves this CTA's Q and dO rows from the swizzled shared tiles into
+      // TMEM (one row per lane, 16-bit pairs along d) once, before any T MMA.
+      if (g == 0 && n_y > 0) {
+        if (mbar_wait(x_full, 0, abort, 30)) {
+#pragma unroll
+          for (int m = 0; m < 2; ++m) {
+            const uint8_t* xs = smem + (m == 0 ? L::kX1Off : L::kX2Off);
+            uint32_t w[D / 2];
+#pragma unroll
+            for (int ch = 0; ch < D / 64; ++ch)
+#pragma unroll
+              for (int gr = 0; gr < 8; ++gr) {
+                const uint4 v = *reinterpret_cast<const uint4*>(xs + ch * (BX * 128) + swz128(r, gr));
+                w[ch * 32 + gr * 4 + 0] = v.x;
+                w[ch * 32 + gr * 4 + 1] = v.y;
+                w[ch * 32 + gr * 4 + 2] = v.z;
+                w[ch * 32 + gr * 4 + 3] = v.w;
+              }
+            const uint32_t dst = (m == 0 ? t_xq : t_xdo) + lane_off;
+#pragma unroll
+            for (int c32 = 0; c32 < D / 64; ++c32)
+              tmem_st32(dst + c32 * 32, *reinterpret_cast<uint32_t(*)[32]>(&w[c32 * 32]));
+          }
+          tmem_wait_st();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(x_tmem);
+      }
+    }
     // dQ: this row's statistics (rows past sq are masked below)
     float row_lse2 = 0.f, row_delta = 0.f;
     if (!IS_DKV && xrow < p.sq) {

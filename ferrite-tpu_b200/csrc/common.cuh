@@ -379,6 +379,14 @@ __device__ __forceinline__ uint64_t make_sdesc(uint32_t saddr, uint32_t lbo,
   return d;
 }
 
+// Descriptor of the same layout `byte_off` bytes further into shared memory.
+// The start-address field holds addr >> 4 in 14 bits; shared-memory addresses
+// stay below 2^18 bytes, so adding (byte_off >> 4) never carries out of it.
+// Lets issuing code build a descriptor once and add compile-time offsets per MMA.
+__device__ __forceinline__ uint64_t sdesc_at(uint64_t desc, uint32_t byte_off) {
+  return desc + (uint64_t)(byte_off >> 4);
+}
+
 // Instruction descriptor for kind::f16 with f32 accumulation.
 //   bits 4-5 D format (1 = f32), 7-9 A format, 10-12 B format (0 f16, 1 bf16),
 //   bit 15 A major (0 K, 1 MN), bit 16 B major, bits 17-22 N>>3, 24-28 M>>4.

@@ -189,6 +189,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc = make_idesc_f16(BM, BN, BF16, A_MN, B_MN);
       int it = 0, local = 0;
       bool ok = true;
+      // Descriptors are built once; each MMA adds a byte offset (stage + K step).
+      const uint32_t s0 = smem_u32(tiles);
+      const uint64_t da_base = A_MN ? make_sdesc(s0, 8192, 1024) : make_sdesc(s0, 16, 1024);
+      const uint64_t db_base = B_MN ? make_sdesc(s0 + S::kABytes, 8192, 1024)
+                                    : make_sdesc(s0 + S::kABytes, 16, 1024);
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
         const int buf = local & 1;
         const uint32_t aph = (local >> 1) & 1;
@@ -203,16 +208,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_u32(tiles + s * S::kStageBytes);
-          const uint32_t sb = sa + S::kABytes;
+          const uint64_t da = sdesc_at(da_base, s * S::kStageBytes);
+          const uint64_t db = sdesc_at(db_base, s * S::kStageBytes);
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint64_t ad = A_MN ? make_sdesc(sa + kk * 2048, 8192, 1024)
-                                     : make_sdesc(sa + kk * 32, 16, 1024);
-            const uint64_t bd = B_MN ? make_sdesc(sb + kk * 2048, 8192, 1024)
-                                     : make_sdesc(sb + kk * 32, 16, 1024);
-            tc_mma_f16_ss(d_tmem, ad, bd, idesc, (kb | kk) != 0);
-          }
+          for (int kk = 0; kk < BK / 16; ++kk)
+            tc_mma_f16_ss(d_tmem, sdesc_at(da, A_MN ? kk * 2048 : kk * 32),
+                          sdesc_at(db, B_MN ? kk * 2048 : kk * 32), idesc, (kb | kk) != 0);
           tc_commit(&empty[s]);  // slot free once these MMAs retire
         }
         tc_commit(&acc_full[buf]);  // accumulator ready for the epilogue
