@@ -180,9 +180,14 @@ class NormWorkload:
     launches_per_step = 3  # add_rmsnorm_fwd, rmsnorm_bwd, dw_reduce
     n_events = 3
 
-    def __init__(self, dev, ws, rank):
+    def __init__(self, dev, ws, rank, shape=None):
         from ferrite import _native as nat
 
+        if shape:  # smaller cases for profiling captures: "rows,dim"
+            self.ROWS, self.DIM = shape
+            self.FWD_BYTES = 4 * self.ROWS * self.DIM * 2 + 4 * self.DIM
+            self.BWD_BYTES = 4 * self.ROWS * self.DIM * 2 + 8 * self.DIM
+            self.kernel_work = {"add_rmsnorm_fwd": self.FWD_BYTES, "rmsnorm_bwd+dw_reduce": self.BWD_BYTES}
         self.nat, self.lib, self.dev, self.ws = nat, nat.lib(), dev, ws
         R, D = self.ROWS, self.DIM
         g = torch.Generator(device=dev)
@@ -331,9 +336,11 @@ class AttnWorkload:
     launches_per_step = 4
     n_events = 5
 
-    def __init__(self, dev, ws, rank):
+    def __init__(self, dev, ws, rank, shape=None):
         from ferrite.kernels.flash_attention import attention_flops
 
+        if shape:  # smaller cases for profiling captures: "b,h,s,d"
+            self.B, self.H, self.S, self.D = shape
         self.dev, self.ws = dev, ws
         bh = self.B * self.H
         if bh % ws:
@@ -442,7 +449,9 @@ class GemmWorkload:
     launches_per_step = 3
     n_events = 4
 
-    def __init__(self, dev, ws, rank):
+    def __init__(self, dev, ws, rank, shape=None):
+        if shape:  # "m,n,k"
+            self.M, self.N, self.K = shape
         self.dev, self.ws = dev, ws
         g = torch.Generator(device=dev)
         g.manual_seed(rank)
@@ -538,7 +547,7 @@ class GptWorkload:
     n_events = 2
     kernels = ("train_step",)
 
-    def __init__(self, dev, ws, rank):
+    def __init__(self, dev, ws, rank, shape=None):
         from ferrite import _native as nat
         from ferrite.model.gpt import GPTConfig, flops_per_token, init_params, param_count, param_leaves
         from ferrite.model.train import AdamW, FlatGrads, TrainConfig, build_train_step
@@ -659,7 +668,7 @@ class PrefillWorkload:
     kernels = ("prefill_graph",)
     PROMPTS, LEN = 8, 512
 
-    def __init__(self, dev, ws, rank):
+    def __init__(self, dev, ws, rank, shape=None):
         from ferrite.model.gpt import GPTConfig, flops_per_token, init_params, param_count
         from ferrite.serving.engine import Engine, ServeConfig
 
@@ -739,7 +748,8 @@ def run_ours(args, ws, rank, local):
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     W = WORKLOADS[args.workload]
-    wl = W(dev, ws, rank)
+    shape = tuple(int(v) for v in args.shape.split(",")) if args.shape else None
+    wl = W(dev, ws, rank, shape)
 
     def sync_all():
         torch.cuda.synchronize(dev)
@@ -897,6 +907,7 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="norm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--shape", default=None, help="smaller case for profiling captures: norm rows,dim | attn b,h,s,d | gemm m,n,k")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)  # timing rule: at least 3 untimed warm-up steps
     ws, rank, local = _dist_env()

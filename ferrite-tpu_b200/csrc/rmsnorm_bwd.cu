@@ -156,6 +156,116 @@ __global__ void __launch_bounds__(CTA, CTA <= 512 ? 2 : 1)
   }
 }
 
+// TMA-fed backward for 16-bit rows of 256..4096 elements (dim = 8 x NC).  One
+// producer warp streams each row's h, dy (and dh_direct) into a STAGES-deep
+// shared-memory ring with 1-D bulk copies (cp.async.bulk, mbarrier
+// complete_tx), so every CTA keeps STAGES-1 rows of loads in flight without
+// spending registers on them; NC consumer threads each own 8 elements (one
+// 16-byte vector) of the row, reduce the two row sums with warp shuffles and one
+// named barrier, write dh and accumulate dw in registers.
+template <typename T, typename TW, bool HAS_DH, int NC, int STAGES>
+__global__ void __launch_bounds__(NC + 32, NC >= 512 ? 2 : 4)
+    rmsnorm_bwd_tma_kernel(const T* __restrict__ h, const TW* __restrict__ w,
+                           const T* __restrict__ dy, const T* __restrict__ dh_direct,
+                           T* __restrict__ dh, float* __restrict__ partial, int64_t rows,
+                           float eps) {
+  constexpr int DIM = NC * 8;
+  constexpr int ROW_BYTES = DIM * 2;
+  constexpr int NT = HAS_DH ? 3 : 2;  // streamed tensors per row
+  constexpr int NW = NC / 32;         // consumer warps
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * NT * ROW_BYTES);
+  uint64_t* empty = full + STAGES;
+  float* red = reinterpret_cast<float*>(empty + STAGES);  // [2][NW][2]
+  volatile int* abort = reinterpret_cast<volatile int*>(red + 2 * NW * 2);
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], NW);
+    }
+    *abort = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int64_t first = blockIdx.x, stride = gridDim.x;
+  const int64_t my_rows = first < rows ? (rows - first + stride - 1) / stride : 0;
+  auto stage = [&](int s, int t) { return smem + (s * NT + t) * ROW_BYTES; };
+
+  if (tid >= NC) {
+    // ---------------------------------------------------------------- producer
+    if (tid == NC) {
+      for (int64_t it = 0; it < my_rows; ++it) {
+        const int s = (int)(it % STAGES);
+        if (!mbar_wait(&empty[s], (uint32_t)((it / STAGES) & 1) ^ 1u, abort, 40)) break;
+        const int64_t off = (first + it * stride) * DIM;
+        mbar_arrive_expect_tx(&full[s], NT * ROW_BYTES);
+        bulk_load(stage(s, 0), h + off, ROW_BYTES, &full[s]);
+        bulk_load(stage(s, 1), dy + off, ROW_BYTES, &full[s]);
+        if constexpr (HAS_DH) bulk_load(stage(s, 2), dh_direct + off, ROW_BYTES, &full[s]);
+      }
+    }
+    return;
+  }
+  // ------------------------------------------------------------------ consumers
+  const int warp = tid >> 5, lane = tid & 31;
+  constexpr int VE = 8;
+  float wv[VE], dwp[VE];
+  load_w<TW, VE>(w, (int64_t)tid * VE, wv);
+#pragma unroll
+  for (int j = 0; j < VE; ++j) dwp[j] = 0.f;
+  const float inv_dim = 1.0f / (float)DIM;
+  for (int64_t it = 0; it < my_rows; ++it) {
+    const int s = (int)(it % STAGES);
+    if (!mbar_wait(&full[s], (uint32_t)((it / STAGES) & 1), abort, 41)) break;
+    float hv[VE], gv[VE], dd[VE];
+    Vec<T>::to_f(*reinterpret_cast<const uint4*>(stage(s, 0) + tid * 16), hv);
+    Vec<T>::to_f(*reinterpret_cast<const uint4*>(stage(s, 1) + tid * 16), gv);
+    if constexpr (HAS_DH) Vec<T>::to_f(*reinterpret_cast<const uint4*>(stage(s, 2) + tid * 16), dd);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with the slot
+    float a = 0.f, b = 0.f;  // sum h^2, sum dy*w*h
+#pragma unroll
+    for (int j = 0; j < VE; ++j) {
+      a = fmaf(hv[j], hv[j], a);
+      b = fmaf(gv[j] * wv[j], hv[j], b);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      a += __shfl_xor_sync(0xffffffffu, a, o);
+      b += __shfl_xor_sync(0xffffffffu, b, o);
+    }
+    float* rb = red + (it & 1) * NW * 2;
+    if (lane == 0) {
+      rb[warp * 2] = a;
+      rb[warp * 2 + 1] = b;
+    }
+    named_barrier(1, NC);
+    a = 0.f;
+    b = 0.f;
+#pragma unroll
+    for (int q = 0; q < NW; ++q) {
+      a += rb[q * 2];
+      b += rb[q * 2 + 1];
+    }
+    const float inv = rsqrtf(a * inv_dim + eps);
+    const float c = inv * b * inv_dim;  // mean(g * xhat)
+    float o[VE];
+#pragma unroll
+    for (int j = 0; j < VE; ++j) {
+      const float xhat = hv[j] * inv;
+      dwp[j] = fmaf(gv[j], xhat, dwp[j]);
+      float v = inv * (gv[j] * wv[j] - xhat * c);
+      if constexpr (HAS_DH) v += dd[j];
+      o[j] = v;
+    }
+    st_v4(dh + (first + it * stride) * DIM + (int64_t)tid * VE, Vec<T>::from_f(o));
+  }
+  float* p = partial + (int64_t)blockIdx.x * DIM + (int64_t)tid * VE;
+  *reinterpret_cast<float4*>(p) = make_float4(dwp[0], dwp[1], dwp[2], dwp[3]);
+  *reinterpret_cast<float4*>(p + 4) = make_float4(dwp[4], dwp[5], dwp[6], dwp[7]);
+}
+
 template <typename T, typename TW, bool HAS_DH>
 __global__ void __launch_bounds__(256)
     rmsnorm_bwd_scalar(const T* __restrict__ h, const TW* __restrict__ w,
@@ -238,6 +348,8 @@ struct BwdPlan {
   int grid;
   int nparts;  // rows of the partial-sum workspace
   int smem;    // dynamic shared memory bytes
+  void* tma_kernel = nullptr;  // TMA-fed kernel when set (16-bit rows of 256..4096)
+  int tma_threads = 0;
 };
 
 // Backward CTA size: at least 512 threads so that one CTA keeps enough loads in
@@ -275,10 +387,56 @@ static void* bwd_ptr(const Cfg& c) {
   return nullptr;
 }
 
+constexpr int kTmaStages = 4;
+
+template <typename T, typename TW, bool HAS_DH, int NC>
+static void* tma_kernel_ptr() {
+  return (void*)rmsnorm_bwd_tma_kernel<T, TW, HAS_DH, NC, kTmaStages>;
+}
+
+// TMA-fed plan for 16-bit rows whose length is 8 x {32, 64, 128, 256, 512}.
+template <typename T, typename TW, bool HAS_DH>
+static bool plan_bwd_tma(BwdPlan& p, int64_t rows, int64_t dim, const void* const* ptrs,
+                         int nptr, int device) {
+  if constexpr (sizeof(T) != 2) {
+    return false;
+  } else {
+    if (env_int("FERRITE_RMSNORM_BWD_TMA", 1) == 0) return false;
+    for (int i = 0; i < nptr; ++i)
+      if (ptrs[i] && (reinterpret_cast<uintptr_t>(ptrs[i]) & 15u)) return false;
+    void* k = nullptr;
+    switch (dim) {
+      case 256: k = tma_kernel_ptr<T, TW, HAS_DH, 32>(); break;
+      case 512: k = tma_kernel_ptr<T, TW, HAS_DH, 64>(); break;
+      case 1024: k = tma_kernel_ptr<T, TW, HAS_DH, 128>(); break;
+      case 2048: k = tma_kernel_ptr<T, TW, HAS_DH, 256>(); break;
+      case 4096: k = tma_kernel_ptr<T, TW, HAS_DH, 512>(); break;
+      default: return false;
+    }
+    const int nc = (int)(dim / 8);
+    const int nt = HAS_DH ? 3 : 2;
+    const int smem = kTmaStages * nt * (int)dim * 2 + 2 * kTmaStages * 8 + 2 * (nc / 32) * 2 * 4 + 16;
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return false;
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, nc + 32, smem) != cudaSuccess || occ < 1)
+      return false;
+    occ = std::min(occ, 8);
+    p.grid = (int)std::max<int64_t>(1, std::min<int64_t>(rows, (int64_t)num_sms(device) * occ));
+    p.nparts = p.grid;
+    p.smem = smem;
+    p.tma_kernel = k;
+    p.tma_threads = nc + 32;
+    return true;
+  }
+}
+
 template <typename T, typename TW, bool HAS_DH>
 static BwdPlan plan_bwd(int64_t rows, int64_t dim, const void* const* ptrs,
                         int nptr, int device) {
   BwdPlan p{};
+  if (plan_bwd_tma<T, TW, HAS_DH>(p, rows, dim, ptrs, nptr, device)) return p;
   p.c = pick(dim, sizeof(T), ptrs, nptr, true);
   const int sms = num_sms(device);
   if (p.c.vec) {
@@ -311,6 +469,16 @@ static BwdPlan plan_bwd(int64_t rows, int64_t dim, const void* const* ptrs,
   return p;
 }
 
+static int launch_tma(const BwdPlan& p, cudaStream_t s, const void* h, const void* w,
+                      const void* dy, const void* dhd, void* dh, float* part, int64_t rows,
+                      float eps) {
+  void* args[] = {&h, &w, &dy, &dhd, &dh, &part, &rows, &eps};
+  cudaError_t e = cudaLaunchKernel(p.tma_kernel, dim3(p.grid), dim3(p.tma_threads), args, p.smem, s);
+  if (e != cudaSuccess)
+    return fail(FERRITE_LAUNCH_FAILED, "rmsnorm_bwd (tma): %s", cudaGetErrorString(e));
+  return FERRITE_OK;
+}
+
 template <typename T, typename TW, bool HAS_DH>
 static int run_bwd(cudaStream_t s, const void* h, const void* w, const void* dy,
                    const void* dhd, void* dh, void* dw, void* ws,
@@ -324,7 +492,9 @@ static int run_bwd(cudaStream_t s, const void* h, const void* w, const void* dy,
                 "rmsnorm_bwd: workspace %zu bytes < %zu needed", ws_bytes, need);
   if ((reinterpret_cast<uintptr_t>(ws) & 15u) != 0)
     return fail(FERRITE_BAD_ALIGNMENT, "rmsnorm_bwd: workspace not 16-byte aligned");
-  if (p.c.vec) {
+  if (p.tma_kernel) {
+    if (int rc = launch_tma(p, s, h, w, dy, dhd, dh, (float*)ws, rows, eps)) return rc;
+  } else if (p.c.vec) {
     void* k = bwd_ptr<T, TW, HAS_DH>(p.c);
     const int CTA = bwd_cta(p.c.tpr);
     int dimi = (int)dim;
@@ -406,7 +576,10 @@ static int run_bwd_noalloc(cudaStream_t s, const void* h, const void* w, const v
   // Fit the partial rows into the fixed buffer (the persistent kernels accept
   // any grid size; a smaller grid only means more rows per CTA).
   const int64_t max_rows = kNoAllocPartialFloats / dim;
-  if (p.c.vec) {
+  if (p.tma_kernel) {
+    p.grid = (int)std::max<int64_t>(1, std::min<int64_t>(p.grid, max_rows));
+    p.nparts = p.grid;
+  } else if (p.c.vec) {
     p.grid = (int)std::max<int64_t>(1, std::min<int64_t>(p.grid, max_rows));
     p.nparts = p.grid;
   } else {
@@ -416,7 +589,9 @@ static int run_bwd_noalloc(cudaStream_t s, const void* h, const void* w, const v
   if ((int64_t)p.nparts * dim > kNoAllocPartialFloats)
     return fail(FERRITE_BAD_SHAPE, "rmsnorm_bwd_noalloc: dim %lld needs more than the %lld-float buffer",
                 (long long)dim, (long long)kNoAllocPartialFloats);
-  if (p.c.vec) {
+  if (p.tma_kernel) {
+    if (int rc = launch_tma(p, s, h, w, dy, dhd, dh, part, rows, eps)) return rc;
+  } else if (p.c.vec) {
     void* k = bwd_ptr<T, TW, HAS_DH>(p.c);
     const int CTA = bwd_cta(p.c.tpr);
     int dimi = (int)dim;

@@ -84,7 +84,10 @@ def test_golden_fixtures():
     np.testing.assert_allclose(to_numpy(dw), g["dw"], atol=1e-4, rtol=1e-5)
 
 
-@pytest.mark.parametrize("rows,dim", [(8192, 4096), (1, 4096), (7, 4096), (33, 1000), (5, 8), (3, 24), (1024, 8192), (64, 32768)])
+@pytest.mark.parametrize(
+    "rows,dim",
+    [(8192, 4096), (1, 4096), (7, 4096), (33, 1000), (5, 8), (3, 24), (1024, 8192), (64, 32768), (300, 256), (77, 512), (2048, 1024), (129, 2048)],
+)
 def test_add_rmsnorm_fwd_bwd_vs_oracle(rows, dim):
     """BASELINE config (8192 x 4096 bf16) plus ragged / odd / tiny / long rows."""
     rng = np.random.default_rng(rows * 7 + dim)
@@ -136,3 +139,19 @@ def test_zero_rows_is_a_no_op():
 
 def test_device_status_clean():
     nat.device_status(clear=True)
+
+
+@pytest.mark.parametrize("dim", [1024, 4096])
+def test_tma_backward_matches_register_backward(monkeypatch, dim):
+    """The TMA-fed backward (16-bit rows of 256..4096) and the register-prefetch
+    backward give bitwise-equal dh and dw within f32 summation order."""
+    rng = np.random.default_rng(dim)
+    rows = 1000
+    h = to_torch(normal(rng, (rows, dim), BF16))
+    w = to_torch((1.0 + 0.1 * rng.standard_normal(dim)).astype(np.float32))
+    dy, dhd = to_torch(normal(rng, (rows, dim), BF16)), to_torch(normal(rng, (rows, dim), BF16))
+    dh_a, dw_a = rmsnorm_backward(h, w, dy, dhd, 1e-6)
+    monkeypatch.setenv("FERRITE_RMSNORM_BWD_TMA", "0")
+    dh_b, dw_b = rmsnorm_backward(h, w, dy, dhd, 1e-6)
+    assert torch.equal(dh_a, dh_b)
+    torch.testing.assert_close(dw_a, dw_b, rtol=1e-5, atol=1e-4)
