@@ -45,6 +45,18 @@ constexpr float kMaskValue = -0.7f * 3.40282346638528859812e+38f;  // -0.7 * FLT
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
+// Element strides (batch, head, sequence) of a [b, h, s, d] operand whose d is
+// unit-stride, and the head count that splits the flattened batch*head index.
+// Contiguous [b, h, s, d] is {h*s*d, s*d, d}; the GPT block's packed
+// [b, s, 3, h, d] projection read in place is {3*h*s*d, d, 3*h*d} per slot.
+struct Bhsd {
+  int64_t b, h, s;
+  int nh;
+  __host__ __device__ __forceinline__ int64_t row(int64_t bh, int64_t r) const {
+    return (bh / nh) * b + (bh % nh) * h + r * s;
+  }
+};
+
 // ===========================================================================
 // delta = rowsum(dO * O) (flash_attention.py:328)
 // ===========================================================================
@@ -52,12 +64,13 @@ constexpr float kLn2 = 0.6931471805599453f;
 template <typename T>
 __global__ void __launch_bounds__(256)
     bwd_prep_kernel(const T* __restrict__ dout, const T* __restrict__ out,
-                    float* __restrict__ delta, int64_t rows, int d) {
+                    float* __restrict__ delta, Bhsd ld, Bhsd lo, int64_t rows, int s_len, int d) {
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   if (row >= rows) return;
-  const T* a = dout + row * d;
-  const T* b = out + row * d;
+  const int64_t bh = row / s_len, r = row % s_len;
+  const T* a = dout + ld.row(bh, r);
+  const T* b = out + lo.row(bh, r);
   float s = 0.f;
   for (int j = lane; j < d; j += 32) s = fmaf(DT<T>::to_f(a[j]), DT<T>::to_f(b[j]), s);
 #pragma unroll
@@ -83,15 +96,16 @@ template <typename T>
 __global__ void __launch_bounds__(kSimtWarps * 32)
     simt_fwd_kernel(const T* __restrict__ q, const T* __restrict__ k,
                     const T* __restrict__ v, T* __restrict__ o, float* __restrict__ lse,
-                    int sq, int sk, int d, float scale, int causal) {
+                    Bhsd lq, Bhsd lk, Bhsd lv, Bhsd lo, int sq, int sk, int d, float scale,
+                    int causal) {
   __shared__ float qs[kSimtWarps][kSimtMaxD];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t bh = blockIdx.y;
   const int row = blockIdx.x * kSimtWarps + warp;
   const bool active = row < sq;
-  const T* qr = q + (bh * sq + (active ? row : 0)) * (int64_t)d;
-  const T* kb = k + bh * sk * (int64_t)d;
-  const T* vb = v + bh * sk * (int64_t)d;
+  const T* qr = q + lq.row(bh, active ? row : 0);
+  const T* kb = k + lk.row(bh, 0);
+  const T* vb = v + lv.row(bh, 0);
   for (int j = lane; j < d; j += 32) qs[warp][j] = DT<T>::to_f(qr[j]);
   __syncwarp();
   constexpr int DPL = kSimtMaxD / 32;  // output dims per lane (max)
@@ -104,7 +118,7 @@ __global__ void __launch_bounds__(kSimtWarps * 32)
     const int key = k0 + lane;
     float s = kMaskValue;
     if (key < sk) {
-      const T* kr = kb + (int64_t)key * d;
+      const T* kr = kb + (int64_t)key * lk.s;
       float dot = 0.f;
       for (int j = 0; j < d; ++j) dot = fmaf(qs[warp][j], DT<T>::to_f(kr[j]), dot);
       s = dot * scale;
@@ -128,7 +142,7 @@ __global__ void __launch_bounds__(kSimtWarps * 32)
       const float pj = __shfl_sync(0xffffffffu, pr, jj);
       const int kk = k0 + jj;
       if (kk >= sk) break;
-      const T* vr = vb + (int64_t)kk * d;
+      const T* vr = vb + (int64_t)kk * lv.s;
 #pragma unroll
       for (int i = 0; i < DPL; ++i) {
         const int dd = lane + 32 * i;
@@ -138,7 +152,7 @@ __global__ void __launch_bounds__(kSimtWarps * 32)
   }
   if (!active) return;
   const float inv = 1.0f / l;
-  T* orow = o + (bh * sq + row) * (int64_t)d;
+  T* orow = o + lo.row(bh, row);
 #pragma unroll
   for (int i = 0; i < DPL; ++i) {
     const int dd = lane + 32 * i;
@@ -153,23 +167,24 @@ __global__ void __launch_bounds__(kSimtWarps * 32)
     simt_bwd_dq_kernel(const T* __restrict__ q, const T* __restrict__ k,
                        const T* __restrict__ v, const T* __restrict__ dout,
                        const float* __restrict__ lse, const float* __restrict__ delta,
-                       T* __restrict__ dq, int sq, int sk, int d, float scale, int causal) {
+                       T* __restrict__ dq, Bhsd lq, Bhsd lk, Bhsd lv, Bhsd ldo, Bhsd ldq,
+                       int sq, int sk, int d, float scale, int causal) {
   __shared__ float qs[kSimtWarps][kSimtMaxD];
   __shared__ float ds_[kSimtWarps][kSimtMaxD];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t bh = blockIdx.y;
   const int row = blockIdx.x * kSimtWarps + warp;
   if (row >= sq) return;
-  const T* qr = q + (bh * sq + row) * (int64_t)d;
-  const T* dor = dout + (bh * sq + row) * (int64_t)d;
+  const T* qr = q + lq.row(bh, row);
+  const T* dor = dout + ldo.row(bh, row);
   for (int j = lane; j < d; j += 32) {
     qs[warp][j] = DT<T>::to_f(qr[j]);
     ds_[warp][j] = DT<T>::to_f(dor[j]);
   }
   __syncwarp();
   const float lr = lse[bh * sq + row], dl = delta[bh * sq + row];
-  const T* kb = k + bh * sk * (int64_t)d;
-  const T* vb = v + bh * sk * (int64_t)d;
+  const T* kb = k + lk.row(bh, 0);
+  const T* vb = v + lv.row(bh, 0);
   constexpr int DPL = kSimtMaxD / 32;
   float acc[DPL];
 #pragma unroll
@@ -179,8 +194,8 @@ __global__ void __launch_bounds__(kSimtWarps * 32)
     const int key = k0 + lane;
     float dsv = 0.f;
     if (key < sk) {
-      const T* kr = kb + (int64_t)key * d;
-      const T* vr = vb + (int64_t)key * d;
+      const T* kr = kb + (int64_t)key * lk.s;
+      const T* vr = vb + (int64_t)key * lv.s;
       float sdot = 0.f, pdot = 0.f;
       for (int j = 0; j < d; ++j) {
         sdot = fmaf(qs[warp][j], DT<T>::to_f(kr[j]), sdot);
@@ -195,7 +210,7 @@ __global__ void __launch_bounds__(kSimtWarps * 32)
       const float dj = __shfl_sync(0xffffffffu, dsv, jj);
       const int kk = k0 + jj;
       if (kk >= sk) break;
-      const T* kr = kb + (int64_t)kk * d;
+      const T* kr = kb + (int64_t)kk * lk.s;
 #pragma unroll
       for (int i = 0; i < DPL; ++i) {
         const int dd = lane + 32 * i;
@@ -203,7 +218,7 @@ __global__ void __launch_bounds__(kSimtWarps * 32)
       }
     }
   }
-  T* out = dq + (bh * sq + row) * (int64_t)d;
+  T* out = dq + ldq.row(bh, row);
 #pragma unroll
   for (int i = 0; i < DPL; ++i) {
     const int dd = lane + 32 * i;
@@ -217,23 +232,24 @@ __global__ void __launch_bounds__(kSimtWarps * 32)
     simt_bwd_dkv_kernel(const T* __restrict__ q, const T* __restrict__ k,
                         const T* __restrict__ v, const T* __restrict__ dout,
                         const float* __restrict__ lse, const float* __restrict__ delta,
-                        T* __restrict__ dk, T* __restrict__ dv, int sq, int sk, int d,
-                        float scale, int causal) {
+                        T* __restrict__ dk, T* __restrict__ dv, Bhsd lq, Bhsd lk, Bhsd lv,
+                        Bhsd ldo, Bhsd ldk, Bhsd ldv, int sq, int sk, int d, float scale,
+                        int causal) {
   __shared__ float ks[kSimtWarps][kSimtMaxD];
   __shared__ float vs[kSimtWarps][kSimtMaxD];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t bh = blockIdx.y;
   const int key = blockIdx.x * kSimtWarps + warp;
   if (key >= sk) return;
-  const T* kr = k + (bh * sk + key) * (int64_t)d;
-  const T* vr = v + (bh * sk + key) * (int64_t)d;
+  const T* kr = k + lk.row(bh, key);
+  const T* vr = v + lv.row(bh, key);
   for (int j = lane; j < d; j += 32) {
     ks[warp][j] = DT<T>::to_f(kr[j]);
     vs[warp][j] = DT<T>::to_f(vr[j]);
   }
   __syncwarp();
-  const T* qb = q + bh * sq * (int64_t)d;
-  const T* db = dout + bh * sq * (int64_t)d;
+  const T* qb = q + lq.row(bh, 0);
+  const T* db = dout + ldo.row(bh, 0);
   constexpr int DPL = kSimtMaxD / 32;
   float ak[DPL], av[DPL];
 #pragma unroll
@@ -243,8 +259,8 @@ __global__ void __launch_bounds__(kSimtWarps * 32)
     const int qi = q0 + lane;
     float pv = 0.f, dsv = 0.f;
     if (qi < sq && qi >= qstart) {
-      const T* qr = qb + (int64_t)qi * d;
-      const T* dr = db + (int64_t)qi * d;
+      const T* qr = qb + (int64_t)qi * lq.s;
+      const T* dr = db + (int64_t)qi * ldo.s;
       float sdot = 0.f, pdot = 0.f;
       for (int j = 0; j < d; ++j) {
         sdot = fmaf(DT<T>::to_f(qr[j]), ks[warp][j], sdot);
@@ -261,8 +277,8 @@ __global__ void __launch_bounds__(kSimtWarps * 32)
       const float dj = __shfl_sync(0xffffffffu, dsv, jj);
       const int qq = q0 + jj;
       if (qq >= sq) break;
-      const T* qr = qb + (int64_t)qq * d;
-      const T* dr = db + (int64_t)qq * d;
+      const T* qr = qb + (int64_t)qq * lq.s;
+      const T* dr = db + (int64_t)qq * ldo.s;
 #pragma unroll
       for (int i = 0; i < DPL; ++i) {
         const int dd = lane + 32 * i;
@@ -273,8 +289,8 @@ __global__ void __launch_bounds__(kSimtWarps * 32)
       }
     }
   }
-  T* okr = dk + (bh * sk + key) * (int64_t)d;
-  T* ovr = dv + (bh * sk + key) * (int64_t)d;
+  T* okr = dk + ldk.row(bh, key);
+  T* ovr = dv + ldv.row(bh, key);
 #pragma unroll
   for (int i = 0; i < DPL; ++i) {
     const int dd = lane + 32 * i;
@@ -336,7 +352,8 @@ struct FwdParams {
   float scale_log2;  // scale * log2(e)
   int causal;
   void* o;
-  float* lse;
+  Bhsd lo;     // output layout
+  float* lse;  // [b*h, sq]
   int nq_blocks;  // 256-row query blocks
 };
 
@@ -369,6 +386,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   // Heaviest (last) query blocks first: causal work grows with the index.
   const int qb = p.nq_blocks - 1 - (int)blockIdx.x;
   const int bh = blockIdx.y;
+  const int hh = bh % p.lo.nh, bb = bh / p.lo.nh;  // TMA coordinates of the slice
   const int q0 = qb * 2 * TQ;
   const int diag_shift = p.sk - p.sq;  // causal: key <= query + diag_shift
   int n_kv = (p.sk + TK - 1) / TK;
@@ -407,8 +425,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       for (int g = 0; g < 2; ++g)
 #pragma unroll
         for (int c = 0; c < L::kChunks; ++c)
-          tma_load_3d(smem + L::kQOff + g * L::kQBytes + c * (TQ * 128), &tq, q_full, c * 64,
-                      q0 + g * TQ, bh);
+          tma_load_4d(smem + L::kQOff + g * L::kQBytes + c * (TQ * 128), &tq, q_full, c * 64,
+                      q0 + g * TQ, hh, bb);
       for (int j = 0; j < n_kv; ++j) {
         const int s = j & 1;
         if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, abort, 10)) break;
@@ -417,8 +435,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         mbar_arrive_expect_tx(&kv_full[s], L::kStageBytes);
 #pragma unroll
         for (int c = 0; c < L::kChunks; ++c) {
-          tma_load_3d(sk_ + c * (TK * 128), &tk, &kv_full[s], c * 64, j * TK, bh);
-          tma_load_3d(sv_ + c * (TK * 128), &tv, &kv_full[s], c * 64, j * TK, bh);
+          tma_load_4d(sk_ + c * (TK * 128), &tk, &kv_full[s], c * 64, j * TK, hh, bb);
+          tma_load_4d(sv_ + c * (TK * 128), &tv, &kv_full[s], c * 64, j * TK, hh, bb);
         }
       }
     }
@@ -582,7 +600,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       tc_fence_after();
       const float inv = 1.0f / l;
       typedef typename std::conditional<BF16, __nv_bfloat16, __half>::type T;
-      T* orow = reinterpret_cast<T*>(p.o) + ((int64_t)bh * p.sq + qrow) * D;
+      T* orow = reinterpret_cast<T*>(p.o) + p.lo.row(bh, qrow);
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t ov[32];
@@ -678,6 +696,7 @@ struct BwdParams {
   const float* delta;
   void* out0;  // dK/dV: dK; dQ: dQ
   void* out1;  // dK/dV: dV
+  Bhsd l0, l1;  // layouts of out0, out1
   int n_x_tiles;
 };
 
@@ -708,6 +727,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   // query tiles (dQ) see the most streaming tiles.
   const int xt = IS_DKV ? (int)blockIdx.x : p.n_x_tiles - 1 - (int)blockIdx.x;
   const int bh = blockIdx.y;
+  const int hh = bh % p.l0.nh, bb = bh / p.l0.nh;  // TMA coordinates of the slice
   const int x0 = xt * BX;
   const int x_len = IS_DKV ? p.sk : p.sq;  // rows of the stationary operand
   const int y_len = IS_DKV ? p.sq : p.sk;  // rows of the streaming operand
@@ -767,8 +787,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_arrive_expect_tx(x_full, 2 * L::kXBytes);
 #pragma unroll
       for (int c = 0; c < L::kChunks; ++c) {
-        tma_load_3d(smem + L::kX1Off + c * (BX * 128), &tx1, x_full, c * 64, x0, bh);
-        tma_load_3d(smem + L::kX2Off + c * (BX * 128), &tx2, x_full, c * 64, x0, bh);
+        tma_load_4d(smem + L::kX1Off + c * (BX * 128), &tx1, x_full, c * 64, x0, hh, bb);
+        tma_load_4d(smem + L::kX2Off + c * (BX * 128), &tx2, x_full, c * 64, x0, hh, bb);
       }
       for (int i = 0; i < n_y; ++i) {
         const int s = i % kYStages;
@@ -779,8 +799,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int yrow = (j0 + i) * BY;
 #pragma unroll
         for (int c = 0; c < L::kChunks; ++c) {
-          tma_load_3d(y1 + c * (BY * 128), &ty1, &y_full[s], c * 64, yrow, bh);
-          tma_load_3d(y2 + c * (BY * 128), &ty2, &y_full[s], c * 64, yrow, bh);
+          tma_load_4d(y1 + c * (BY * 128), &ty1, &y_full[s], c * 64, yrow, hh, bb);
+          tma_load_4d(y2 + c * (BY * 128), &ty2, &y_full[s], c * 64, yrow, hh, bb);
         }
         if constexpr (IS_DKV) {
           float* st = reinterpret_cast<float*>(y2 + L::kYBytes);
@@ -980,7 +1000,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     if (ok && n_y > 0 && mbar_wait(acc_full, 0, abort, 28)) {
       tc_fence_after();
       const bool row_ok = xrow < x_len;
-      const int64_t orow = ((int64_t)bh * x_len + xrow) * D;
+      const int64_t orow = ((IS_DKV && g == 1) ? p.l1 : p.l0).row(bh, xrow);
       T* out = reinterpret_cast<T*>((IS_DKV && g == 1) ? p.out1 : p.out0) + orow;
       const uint32_t src = (IS_DKV && g == 1) ? t_acc1 : t_acc0;
       const float mul = (IS_DKV && g == 1) ? 1.0f : p.scale;
@@ -1005,7 +1025,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
     } else if (ok && n_y == 0 && xrow < x_len) {
       // no streaming tile reaches these rows (not reachable for causal sq == sk): zeros
-      const int64_t orow = ((int64_t)bh * x_len + xrow) * D;
+      const int64_t orow = ((IS_DKV && g == 1) ? p.l1 : p.l0).row(bh, xrow);
       T* out = reinterpret_cast<T*>((IS_DKV && g == 1) ? p.out1 : p.out0) + orow;
       const int c_begin = IS_DKV ? 0 : g * (D / 2);
       const int c_end = IS_DKV ? D : (g + 1) * (D / 2);
@@ -1054,21 +1074,42 @@ static bool tc_fwd_ok(int64_t d, int64_t sk, int dtype) {
   return dtype != FERRITE_F32 && (d == 64 || d == 128) && sk % TK == 0;
 }
 
+// The tensor-core kernels read through TMA and store 16-byte vectors, so every
+// operand needs a 16-byte aligned base and strides that are positive multiples
+// of 8 (16-bit) elements; an extent-1 dimension's stride is never used.
+static bool tc_layout_ok(const void* ptr, const Bhsd& l, int64_t b, int64_t h, int64_t s) {
+  if (reinterpret_cast<uintptr_t>(ptr) & 15u) return false;
+  auto ok = [](int64_t st, int64_t n) {
+    return n == 1 || (st > 0 && st % 8 == 0 && st < (int64_t(1) << 38));
+  };
+  return ok(l.b, b) && ok(l.h, h) && ok(l.s, s);
+}
+
+// 4-D map of a [b, h, s, d] operand: dims (d, s, h, b), box (64, rows, 1, 1),
+// 128-byte swizzle.  The smem image of one box is the same [rows][64] K-major
+// tile a contiguous 3-D map gives.
+static int map_bhsd(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int D,
+                    const Bhsd& l, int64_t b, int64_t h, int64_t s, uint32_t rows) {
+  auto st = [&](int64_t stride, int64_t n) -> uint64_t {
+    return n == 1 ? (uint64_t)D * 2 : (uint64_t)stride * 2;
+  };
+  const uint64_t dims[4] = {(uint64_t)D, (uint64_t)s, (uint64_t)h, (uint64_t)b};
+  const uint64_t strides[3] = {st(l.s, s), st(l.h, h), st(l.b, b)};
+  const uint32_t box[4] = {64, rows, 1, 1};
+  return make_tmap_4d(m, base, dt, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 template <int D, bool BF16>
 static int launch_fwd_tc(cudaStream_t s, const void* q, const void* k, const void* v,
-                         void* o, float* lse, int64_t bh, int64_t sq, int64_t sk,
+                         void* o, float* lse, const Bhsd& lq, const Bhsd& lk, const Bhsd& lv,
+                         const Bhsd& lo, int64_t b, int64_t h, int64_t sq, int64_t sk,
                          float scale, int causal) {
   using L = FwdSmem<D>;
   const CUtensorMapDataType dt = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap tq, tk, tv;
-  int rc = make_tmap_3d(&tq, q, dt, 2, D, (uint64_t)sq, (uint64_t)bh, D * 2, (uint64_t)sq * D * 2,
-                        64, TQ, 1, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (!rc)
-    rc = make_tmap_3d(&tk, k, dt, 2, D, (uint64_t)sk, (uint64_t)bh, D * 2,
-                      (uint64_t)sk * D * 2, 64, TK, 1, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (!rc)
-    rc = make_tmap_3d(&tv, v, dt, 2, D, (uint64_t)sk, (uint64_t)bh, D * 2,
-                      (uint64_t)sk * D * 2, 64, TK, 1, CU_TENSOR_MAP_SWIZZLE_128B);
+  int rc = map_bhsd(&tq, q, dt, D, lq, b, h, sq, TQ);
+  if (!rc) rc = map_bhsd(&tk, k, dt, D, lk, b, h, sk, TK);
+  if (!rc) rc = map_bhsd(&tv, v, dt, D, lv, b, h, sk, TK);
   if (rc) return rc;
   FwdParams p;
   p.sq = (int)sq;
@@ -1076,38 +1117,42 @@ static int launch_fwd_tc(cudaStream_t s, const void* q, const void* k, const voi
   p.scale_log2 = scale * kLog2e;
   p.causal = causal;
   p.o = o;
+  p.lo = lo;
   p.lse = lse;
   p.nq_blocks = (int)((sq + 2 * TQ - 1) / (2 * TQ));
   auto kern = attn_fwd_tc_kernel<D, BF16>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
   if (e != cudaSuccess) return fail(FERRITE_LAUNCH_FAILED, "attn_fwd: smem attr: %s", cudaGetErrorString(e));
-  dim3 grid(p.nq_blocks, (unsigned)bh);
+  dim3 grid(p.nq_blocks, (unsigned)(b * h));
   kern<<<grid, kFwdThreads, L::kTotal, s>>>(tq, tk, tv, p);
   return check_launch("attn_fwd_tc");
 }
 
+// Operands of one backward call: the four inputs, the outputs and their layouts.
+struct BwdArgs {
+  const void *q, *k, *v, *dout;
+  const float *lse, *delta;
+  void *out0, *out1;  // dK, dV (dK/dV kernel) or dQ (dQ kernel)
+  Bhsd lq, lk, lv, ldo, l0, l1;
+};
+
 template <int D, bool BF16, bool IS_DKV>
-static int launch_bwd_tc(cudaStream_t s, const void* q, const void* k, const void* v,
-                         const void* dout, const float* lse, const float* delta, void* out0,
-                         void* out1, int64_t bh, int64_t sq, int64_t sk, float scale,
-                         int causal) {
+static int launch_bwd_tc(cudaStream_t s, const BwdArgs& a, int64_t b, int64_t h, int64_t sq,
+                         int64_t sk, float scale, int causal) {
   using L = BwdSmem<D>;
   const CUtensorMapDataType dt = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   // stationary pair (128-row boxes) and streaming pair (64-row boxes)
-  const void* x1 = IS_DKV ? k : q;
-  const void* x2 = IS_DKV ? v : dout;
-  const void* y1 = IS_DKV ? q : k;
-  const void* y2 = IS_DKV ? dout : v;
   const int64_t xs = IS_DKV ? sk : sq, ys = IS_DKV ? sq : sk;
   CUtensorMap tx1, tx2, ty1, ty2;
-  int rc = make_tmap_3d(&tx1, x1, dt, 2, D, (uint64_t)xs, (uint64_t)bh, D * 2, (uint64_t)xs * D * 2, 64, BX, 1, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (!rc) rc = make_tmap_3d(&tx2, x2, dt, 2, D, (uint64_t)xs, (uint64_t)bh, D * 2, (uint64_t)xs * D * 2, 64, BX, 1, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (!rc) rc = make_tmap_3d(&ty1, y1, dt, 2, D, (uint64_t)ys, (uint64_t)bh, D * 2, (uint64_t)ys * D * 2, 64, BY, 1, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (!rc) rc = make_tmap_3d(&ty2, y2, dt, 2, D, (uint64_t)ys, (uint64_t)bh, D * 2, (uint64_t)ys * D * 2, 64, BY, 1, CU_TENSOR_MAP_SWIZZLE_128B);
+  int rc = map_bhsd(&tx1, IS_DKV ? a.k : a.q, dt, D, IS_DKV ? a.lk : a.lq, b, h, xs, BX);
+  if (!rc) rc = map_bhsd(&tx2, IS_DKV ? a.v : a.dout, dt, D, IS_DKV ? a.lv : a.ldo, b, h, xs, BX);
+  if (!rc) rc = map_bhsd(&ty1, IS_DKV ? a.q : a.k, dt, D, IS_DKV ? a.lq : a.lk, b, h, ys, BY);
+  if (!rc) rc = map_bhsd(&ty2, IS_DKV ? a.dout : a.v, dt, D, IS_DKV ? a.ldo : a.lv, b, h, ys, BY);
   // lse / delta as [bh][sq] f32, 64-query boxes (zero-filled past sq)
+  const int64_t bh = b * h;
   CUtensorMap tl, td;
-  if (!rc) rc = make_tmap_2d(&tl, lse, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)sq, (uint64_t)bh, (uint64_t)sq * 4, BY, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
-  if (!rc) rc = make_tmap_2d(&td, delta, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)sq, (uint64_t)bh, (uint64_t)sq * 4, BY, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (!rc) rc = make_tmap_2d(&tl, a.lse, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)sq, (uint64_t)bh, (uint64_t)sq * 4, BY, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (!rc) rc = make_tmap_2d(&td, a.delta, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)sq, (uint64_t)bh, (uint64_t)sq * 4, BY, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
   BwdParams p;
   p.sq = (int)sq;
@@ -1115,10 +1160,12 @@ static int launch_bwd_tc(cudaStream_t s, const void* q, const void* k, const voi
   p.scale = scale;
   p.scale_log2 = scale * kLog2e;
   p.causal = causal;
-  p.lse = lse;
-  p.delta = delta;
-  p.out0 = out0;
-  p.out1 = out1;
+  p.lse = a.lse;
+  p.delta = a.delta;
+  p.out0 = a.out0;
+  p.out1 = a.out1;
+  p.l0 = a.l0;
+  p.l1 = a.l1;
   p.n_x_tiles = (int)((xs + BX - 1) / BX);
   auto kern = attn_bwd_tc_kernel<D, BF16, IS_DKV>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
@@ -1129,27 +1176,149 @@ static int launch_bwd_tc(cudaStream_t s, const void* q, const void* k, const voi
 }
 
 template <bool IS_DKV>
-static int dispatch_bwd_tc(cudaStream_t s, const void* q, const void* k, const void* v,
-                           const void* dout, const float* lse, const float* delta, void* out0,
-                           void* out1, int64_t bh, int64_t sq, int64_t sk, int64_t d,
-                           float scale, int causal, int dtype) {
+static int dispatch_bwd_tc(cudaStream_t s, const BwdArgs& a, int64_t b, int64_t h, int64_t sq,
+                           int64_t sk, int64_t d, float scale, int causal, int dtype) {
   const bool bf = dtype == FERRITE_BF16;
   if (d == 64)
-    return bf ? launch_bwd_tc<64, true, IS_DKV>(s, q, k, v, dout, lse, delta, out0, out1, bh, sq, sk, scale, causal)
-              : launch_bwd_tc<64, false, IS_DKV>(s, q, k, v, dout, lse, delta, out0, out1, bh, sq, sk, scale, causal);
-  return bf ? launch_bwd_tc<128, true, IS_DKV>(s, q, k, v, dout, lse, delta, out0, out1, bh, sq, sk, scale, causal)
-            : launch_bwd_tc<128, false, IS_DKV>(s, q, k, v, dout, lse, delta, out0, out1, bh, sq, sk, scale, causal);
+    return bf ? launch_bwd_tc<64, true, IS_DKV>(s, a, b, h, sq, sk, scale, causal)
+              : launch_bwd_tc<64, false, IS_DKV>(s, a, b, h, sq, sk, scale, causal);
+  return bf ? launch_bwd_tc<128, true, IS_DKV>(s, a, b, h, sq, sk, scale, causal)
+            : launch_bwd_tc<128, false, IS_DKV>(s, a, b, h, sq, sk, scale, causal);
 }
 
-template <typename T>
-static int launch_fwd_simt(cudaStream_t s, const void* q, const void* k, const void* v,
-                           void* o, float* lse, int64_t bh, int64_t sq, int64_t sk,
-                           int64_t d, float scale, int causal) {
-  dim3 grid((unsigned)((sq + kSimtWarps - 1) / kSimtWarps), (unsigned)bh);
-  simt_fwd_kernel<T><<<grid, kSimtWarps * 32, 0, s>>>((const T*)q, (const T*)k, (const T*)v,
-                                                       (T*)o, lse, (int)sq, (int)sk, (int)d,
-                                                       scale, causal);
+static Bhsd contiguous_bhsd(int64_t h, int64_t s, int64_t d) {
+  return Bhsd{h * s * d, s * d, d, (int)h};
+}
+
+static int strides_ok(const char* op, const ferrite_attn_strides* st) {
+  if (!st) return fail(FERRITE_BAD_SHAPE, "%s: null strides", op);
+  const int64_t* f = &st->q[0];
+  for (int i = 0; i < 24; ++i)
+    if (f[i] < 0) return fail(FERRITE_BAD_SHAPE, "%s: negative stride", op);
+  return FERRITE_OK;
+}
+
+static Bhsd bhsd_of(const int64_t st[3], int64_t h) { return Bhsd{st[0], st[1], st[2], (int)h}; }
+
+static int attn_fwd_impl(cudaStream_t s, const void* q, const void* k, const void* v, void* o,
+                         float* lse, const ferrite_attn_strides& st, int64_t b, int64_t h,
+                         int64_t sq, int64_t sk, int64_t d, float scale, int causal, int dtype) {
+  const Bhsd lq = bhsd_of(st.q, h), lk = bhsd_of(st.k, h), lv = bhsd_of(st.v, h), lo = bhsd_of(st.o, h);
+  if (tc_fwd_ok(d, sk, dtype) && tc_layout_ok(q, lq, b, h, sq) && tc_layout_ok(k, lk, b, h, sk) &&
+      tc_layout_ok(v, lv, b, h, sk) && tc_layout_ok(o, lo, b, h, sq)) {
+    const bool bf = dtype == FERRITE_BF16;
+    if (d == 64) return bf ? launch_fwd_tc<64, true>(s, q, k, v, o, lse, lq, lk, lv, lo, b, h, sq, sk, scale, causal)
+                           : launch_fwd_tc<64, false>(s, q, k, v, o, lse, lq, lk, lv, lo, b, h, sq, sk, scale, causal);
+    return bf ? launch_fwd_tc<128, true>(s, q, k, v, o, lse, lq, lk, lv, lo, b, h, sq, sk, scale, causal)
+              : launch_fwd_tc<128, false>(s, q, k, v, o, lse, lq, lk, lv, lo, b, h, sq, sk, scale, causal);
+  }
+  dim3 grid((unsigned)((sq + kSimtWarps - 1) / kSimtWarps), (unsigned)(b * h));
+#define FWD(T)                                                                                  \
+  simt_fwd_kernel<T><<<grid, kSimtWarps * 32, 0, s>>>((const T*)q, (const T*)k, (const T*)v,    \
+                                                       (T*)o, lse, lq, lk, lv, lo, (int)sq,     \
+                                                       (int)sk, (int)d, scale, causal)
+  if (dtype == FERRITE_F32) FWD(float);
+  else if (dtype == FERRITE_BF16) FWD(__nv_bfloat16);
+  else FWD(__half);
+#undef FWD
   return check_launch("attn_fwd_simt");
+}
+
+static int attn_bwd_prep_impl(cudaStream_t s, const void* dout, const void* out, float* delta,
+                              const ferrite_attn_strides& st, int64_t b, int64_t h, int64_t s_,
+                              int64_t d, int dtype) {
+  const Bhsd ld = bhsd_of(st.dout, h), lo = bhsd_of(st.o, h);
+  const int64_t rows = b * h * s_;
+  const unsigned grid = (unsigned)((rows + 7) / 8);
+#define PREP(T) \
+  bwd_prep_kernel<T><<<grid, 256, 0, s>>>((const T*)dout, (const T*)out, delta, ld, lo, rows, (int)s_, (int)d)
+  if (dtype == FERRITE_F32) PREP(float);
+  else if (dtype == FERRITE_BF16) PREP(__nv_bfloat16);
+  else if (dtype == FERRITE_F16) PREP(__half);
+  else return fail(FERRITE_UNSUPPORTED_DTYPE, "attn_bwd_prep: dtype %d", dtype);
+#undef PREP
+  return check_launch("attn_bwd_prep");
+}
+
+static bool tc_bwd_ok(const BwdArgs& a, int64_t b, int64_t h, int64_t sq, int64_t sk, int64_t d,
+                      int dtype, bool is_dkv) {
+  if (!tc_fwd_ok(d, sk, dtype) || env_int("FERRITE_ATTN_BWD_FORCE_SIMT", 0)) return false;
+  bool ok = tc_layout_ok(a.q, a.lq, b, h, sq) && tc_layout_ok(a.k, a.lk, b, h, sk) &&
+            tc_layout_ok(a.v, a.lv, b, h, sk) && tc_layout_ok(a.dout, a.ldo, b, h, sq);
+  if (is_dkv) return ok && tc_layout_ok(a.out0, a.l0, b, h, sk) && tc_layout_ok(a.out1, a.l1, b, h, sk);
+  return ok && tc_layout_ok(a.out0, a.l0, b, h, sq);
+}
+
+static int attn_bwd_dkv_impl(cudaStream_t s, const BwdArgs& a, int64_t b, int64_t h, int64_t sq,
+                             int64_t sk, int64_t d, float scale, int causal, int dtype) {
+  if (tc_bwd_ok(a, b, h, sq, sk, d, dtype, true))
+    return dispatch_bwd_tc<true>(s, a, b, h, sq, sk, d, scale, causal, dtype);
+  dim3 grid((unsigned)((sk + kSimtWarps - 1) / kSimtWarps), (unsigned)(b * h));
+#define DKV(T)                                                                                  \
+  simt_bwd_dkv_kernel<T><<<grid, kSimtWarps * 32, 0, s>>>(                                      \
+      (const T*)a.q, (const T*)a.k, (const T*)a.v, (const T*)a.dout, a.lse, a.delta,            \
+      (T*)a.out0, (T*)a.out1, a.lq, a.lk, a.lv, a.ldo, a.l0, a.l1, (int)sq, (int)sk, (int)d,    \
+      scale, causal)
+  if (dtype == FERRITE_F32) DKV(float);
+  else if (dtype == FERRITE_BF16) DKV(__nv_bfloat16);
+  else DKV(__half);
+#undef DKV
+  return check_launch("attn_bwd_dkv_simt");
+}
+
+static int attn_bwd_dq_impl(cudaStream_t s, const BwdArgs& a, int64_t b, int64_t h, int64_t sq,
+                            int64_t sk, int64_t d, float scale, int causal, int dtype) {
+  if (tc_bwd_ok(a, b, h, sq, sk, d, dtype, false))
+    return dispatch_bwd_tc<false>(s, a, b, h, sq, sk, d, scale, causal, dtype);
+  dim3 grid((unsigned)((sq + kSimtWarps - 1) / kSimtWarps), (unsigned)(b * h));
+#define DQ(T)                                                                                    \
+  simt_bwd_dq_kernel<T><<<grid, kSimtWarps * 32, 0, s>>>(                                        \
+      (const T*)a.q, (const T*)a.k, (const T*)a.v, (const T*)a.dout, a.lse, a.delta, (T*)a.out0, \
+      a.lq, a.lk, a.lv, a.ldo, a.l0, (int)sq, (int)sk, (int)d, scale, causal)
+  if (dtype == FERRITE_F32) DQ(float);
+  else if (dtype == FERRITE_BF16) DQ(__nv_bfloat16);
+  else DQ(__half);
+#undef DQ
+  return check_launch("attn_bwd_dq_simt");
+}
+
+static ferrite_attn_strides contiguous_strides(int64_t h, int64_t sq, int64_t sk, int64_t d) {
+  ferrite_attn_strides st;
+  auto set = [](int64_t* f, int64_t h_, int64_t s_, int64_t d_) {
+    f[0] = h_ * s_ * d_;
+    f[1] = s_ * d_;
+    f[2] = d_;
+  };
+  set(st.q, h, sq, d);
+  set(st.o, h, sq, d);
+  set(st.dout, h, sq, d);
+  set(st.dq, h, sq, d);
+  set(st.k, h, sk, d);
+  set(st.v, h, sk, d);
+  set(st.dk, h, sk, d);
+  set(st.dv, h, sk, d);
+  return st;
+}
+
+static BwdArgs bwd_args(const void* q, const void* k, const void* v, const void* dout,
+                        const float* lse, const float* delta, void* out0, void* out1,
+                        const ferrite_attn_strides& st, int64_t h, bool is_dkv) {
+  BwdArgs a;
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.dout = dout;
+  a.lse = lse;
+  a.delta = delta;
+  a.out0 = out0;
+  a.out1 = out1;
+  a.lq = bhsd_of(st.q, h);
+  a.lk = bhsd_of(st.k, h);
+  a.lv = bhsd_of(st.v, h);
+  a.ldo = bhsd_of(st.dout, h);
+  a.l0 = bhsd_of(is_dkv ? st.dk : st.dq, h);
+  a.l1 = bhsd_of(st.dv, h);
+  return a;
 }
 
 }  // namespace attn
@@ -1160,88 +1329,82 @@ using namespace ferrite::attn;
 
 extern "C" {
 
+int ferrite_attn_fwd_strided(void* stream, const void* q, const void* k, const void* v, void* o,
+                             float* lse, const ferrite_attn_strides* st, int64_t b, int64_t h,
+                             int64_t sq, int64_t sk, int64_t d, float scale, int causal,
+                             int block_q, int block_k, int dtype) {
+  if (int rc = validate("attn_fwd", b, h, sq, sk, d, causal, block_q, block_k, dtype)) return rc;
+  if (!q || !k || !v || !o || !lse) return fail(FERRITE_BAD_SHAPE, "attn_fwd: null pointer");
+  if (int rc = strides_ok("attn_fwd", st)) return rc;
+  return attn_fwd_impl((cudaStream_t)stream, q, k, v, o, lse, *st, b, h, sq, sk, d, scale, causal, dtype);
+}
+
 int ferrite_attn_fwd(void* stream, const void* q, const void* k, const void* v, void* o,
                      float* lse, int64_t b, int64_t h, int64_t sq, int64_t sk, int64_t d,
                      float scale, int causal, int block_q, int block_k, int dtype) {
-  if (int rc = validate("attn_fwd", b, h, sq, sk, d, causal, block_q, block_k, dtype)) return rc;
-  if (!q || !k || !v || !o || !lse) return fail(FERRITE_BAD_SHAPE, "attn_fwd: null pointer");
-  cudaStream_t s = (cudaStream_t)stream;
-  const int64_t bh = b * h;
-  if (tc_fwd_ok(d, sk, dtype)) {
-    const bool bf = dtype == FERRITE_BF16;
-    if (d == 64) return bf ? launch_fwd_tc<64, true>(s, q, k, v, o, lse, bh, sq, sk, scale, causal)
-                           : launch_fwd_tc<64, false>(s, q, k, v, o, lse, bh, sq, sk, scale, causal);
-    return bf ? launch_fwd_tc<128, true>(s, q, k, v, o, lse, bh, sq, sk, scale, causal)
-              : launch_fwd_tc<128, false>(s, q, k, v, o, lse, bh, sq, sk, scale, causal);
-  }
-  if (dtype == FERRITE_F32) return launch_fwd_simt<float>(s, q, k, v, o, lse, bh, sq, sk, d, scale, causal);
-  if (dtype == FERRITE_BF16) return launch_fwd_simt<__nv_bfloat16>(s, q, k, v, o, lse, bh, sq, sk, d, scale, causal);
-  return launch_fwd_simt<__half>(s, q, k, v, o, lse, bh, sq, sk, d, scale, causal);
+  const ferrite_attn_strides st = contiguous_strides(h, sq, sk, d);
+  return ferrite_attn_fwd_strided(stream, q, k, v, o, lse, &st, b, h, sq, sk, d, scale, causal,
+                                  block_q, block_k, dtype);
+}
+
+int ferrite_attn_bwd_prep_strided(void* stream, const void* dout, const void* out, float* delta,
+                                  const ferrite_attn_strides* st, int64_t b, int64_t h, int64_t s_,
+                                  int64_t d, int dtype) {
+  if (int rc = injected_fault("attn_bwd_prep")) return rc;
+  if (b <= 0 || h <= 0 || s_ <= 0 || d <= 0) return fail(FERRITE_BAD_SHAPE, "attn_bwd_prep: shape");
+  if (!dout || !out || !delta) return fail(FERRITE_BAD_SHAPE, "attn_bwd_prep: null pointer");
+  if (int rc = strides_ok("attn_bwd_prep", st)) return rc;
+  return attn_bwd_prep_impl((cudaStream_t)stream, dout, out, delta, *st, b, h, s_, d, dtype);
 }
 
 int ferrite_attn_bwd_prep(void* stream, const void* dout, const void* out, float* delta,
                           int64_t b, int64_t h, int64_t s_, int64_t d, int dtype) {
-  if (int rc = injected_fault("attn_bwd_prep")) return rc;
-  if (b <= 0 || h <= 0 || s_ <= 0 || d <= 0) return fail(FERRITE_BAD_SHAPE, "attn_bwd_prep: shape");
-  if (!dout || !out || !delta) return fail(FERRITE_BAD_SHAPE, "attn_bwd_prep: null pointer");
-  cudaStream_t s = (cudaStream_t)stream;
-  const int64_t rows = b * h * s_;
-  const unsigned grid = (unsigned)((rows + 7) / 8);
-  if (dtype == FERRITE_F32)
-    bwd_prep_kernel<float><<<grid, 256, 0, s>>>((const float*)dout, (const float*)out, delta, rows, (int)d);
-  else if (dtype == FERRITE_BF16)
-    bwd_prep_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)dout, (const __nv_bfloat16*)out, delta, rows, (int)d);
-  else if (dtype == FERRITE_F16)
-    bwd_prep_kernel<__half><<<grid, 256, 0, s>>>((const __half*)dout, (const __half*)out, delta, rows, (int)d);
-  else
-    return fail(FERRITE_UNSUPPORTED_DTYPE, "attn_bwd_prep: dtype %d", dtype);
-  return check_launch("attn_bwd_prep");
+  const ferrite_attn_strides st = contiguous_strides(h, s_, s_, d);
+  return ferrite_attn_bwd_prep_strided(stream, dout, out, delta, &st, b, h, s_, d, dtype);
+}
+
+int ferrite_attn_bwd_dkv_strided(void* stream, const void* q, const void* k, const void* v,
+                                 const void* dout, const float* lse, const float* delta, void* dk,
+                                 void* dv, const ferrite_attn_strides* st, int64_t b, int64_t h,
+                                 int64_t sq, int64_t sk, int64_t d, float scale, int causal,
+                                 int block_q, int block_k, int dtype) {
+  if (int rc = validate("attn_bwd_dkv", b, h, sq, sk, d, causal, block_q, block_k, dtype)) return rc;
+  if (!q || !k || !v || !dout || !lse || !delta || !dk || !dv)
+    return fail(FERRITE_BAD_SHAPE, "attn_bwd_dkv: null pointer");
+  if (int rc = strides_ok("attn_bwd_dkv", st)) return rc;
+  const BwdArgs a = bwd_args(q, k, v, dout, lse, delta, dk, dv, *st, h, true);
+  return attn_bwd_dkv_impl((cudaStream_t)stream, a, b, h, sq, sk, d, scale, causal, dtype);
 }
 
 int ferrite_attn_bwd_dkv(void* stream, const void* q, const void* k, const void* v,
                          const void* dout, const float* lse, const float* delta, void* dk,
                          void* dv, int64_t b, int64_t h, int64_t sq, int64_t sk, int64_t d,
                          float scale, int causal, int block_q, int block_k, int dtype) {
-  if (int rc = validate("attn_bwd_dkv", b, h, sq, sk, d, causal, block_q, block_k, dtype)) return rc;
-  if (!q || !k || !v || !dout || !lse || !delta || !dk || !dv)
-    return fail(FERRITE_BAD_SHAPE, "attn_bwd_dkv: null pointer");
-  cudaStream_t s = (cudaStream_t)stream;
-  const int64_t bh = b * h;
-  if (tc_fwd_ok(d, sk, dtype) && !env_int("FERRITE_ATTN_BWD_FORCE_SIMT", 0))
-    return dispatch_bwd_tc<true>(s, q, k, v, dout, lse, delta, dk, dv, bh, sq, sk, d, scale, causal, dtype);
-  dim3 grid((unsigned)((sk + kSimtWarps - 1) / kSimtWarps), (unsigned)bh);
-#define DKV(T)                                                                                  \
-  simt_bwd_dkv_kernel<T><<<grid, kSimtWarps * 32, 0, s>>>(                                      \
-      (const T*)q, (const T*)k, (const T*)v, (const T*)dout, lse, delta, (T*)dk, (T*)dv,        \
-      (int)sq, (int)sk, (int)d, scale, causal)
-  if (dtype == FERRITE_F32) DKV(float);
-  else if (dtype == FERRITE_BF16) DKV(__nv_bfloat16);
-  else DKV(__half);
-#undef DKV
-  return check_launch("attn_bwd_dkv_simt");
+  const ferrite_attn_strides st = contiguous_strides(h, sq, sk, d);
+  return ferrite_attn_bwd_dkv_strided(stream, q, k, v, dout, lse, delta, dk, dv, &st, b, h, sq, sk,
+                                      d, scale, causal, block_q, block_k, dtype);
+}
+
+int ferrite_attn_bwd_dq_strided(void* stream, const void* q, const void* k, const void* v,
+                                const void* dout, const float* lse, const float* delta, void* dq,
+                                const ferrite_attn_strides* st, int64_t b, int64_t h, int64_t sq,
+                                int64_t sk, int64_t d, float scale, int causal, int block_q,
+                                int block_k, int dtype) {
+  if (int rc = validate("attn_bwd_dq", b, h, sq, sk, d, causal, block_q, block_k, dtype)) return rc;
+  if (!q || !k || !v || !dout || !lse || !delta || !dq)
+    return fail(FERRITE_BAD_SHAPE, "attn_bwd_dq: null pointer");
+  if (int rc = strides_ok("attn_bwd_dq", st)) return rc;
+  const BwdArgs a = bwd_args(q, k, v, dout, lse, delta, dq, nullptr, *st, h, false);
+  return attn_bwd_dq_impl((cudaStream_t)stream, a, b, h, sq, sk, d, scale, causal, dtype);
 }
 
 int ferrite_attn_bwd_dq(void* stream, const void* q, const void* k, const void* v,
                         const void* dout, const float* lse, const float* delta, void* dq,
                         int64_t b, int64_t h, int64_t sq, int64_t sk, int64_t d, float scale,
                         int causal, int block_q, int block_k, int dtype) {
-  if (int rc = validate("attn_bwd_dq", b, h, sq, sk, d, causal, block_q, block_k, dtype)) return rc;
-  if (!q || !k || !v || !dout || !lse || !delta || !dq)
-    return fail(FERRITE_BAD_SHAPE, "attn_bwd_dq: null pointer");
-  cudaStream_t s = (cudaStream_t)stream;
-  const int64_t bh = b * h;
-  if (tc_fwd_ok(d, sk, dtype) && !env_int("FERRITE_ATTN_BWD_FORCE_SIMT", 0))
-    return dispatch_bwd_tc<false>(s, q, k, v, dout, lse, delta, dq, nullptr, bh, sq, sk, d, scale, causal, dtype);
-  dim3 grid((unsigned)((sq + kSimtWarps - 1) / kSimtWarps), (unsigned)bh);
-#define DQ(T)                                                                                    \
-  simt_bwd_dq_kernel<T><<<grid, kSimtWarps * 32, 0, s>>>(                                        \
-      (const T*)q, (const T*)k, (const T*)v, (const T*)dout, lse, delta, (T*)dq, (int)sq,        \
-      (int)sk, (int)d, scale, causal)
-  if (dtype == FERRITE_F32) DQ(float);
-  else if (dtype == FERRITE_BF16) DQ(__nv_bfloat16);
-  else DQ(__half);
-#undef DQ
-  return check_launch("attn_bwd_dq_simt");
+  const ferrite_attn_strides st = contiguous_strides(h, sq, sk, d);
+  return ferrite_attn_bwd_dq_strided(stream, q, k, v, dout, lse, delta, dq, &st, b, h, sq, sk, d,
+                                     scale, causal, block_q, block_k, dtype);
 }
 
 }  // extern "C"

@@ -150,6 +150,30 @@ int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
   return FERRITE_OK;
 }
 
+int make_tmap_4d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
+                 int elem_bytes, const uint64_t dims[4], const uint64_t strides_bytes[3],
+                 const uint32_t box[4], CUtensorMapSwizzle swizzle) {
+  if (int rc = load_encoder()) return rc;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
+    return fail(FERRITE_BAD_ALIGNMENT, "TMA base %p is not 16-byte aligned", base);
+  for (int i = 0; i < 3; ++i)
+    if (strides_bytes[i] % 16 != 0 || strides_bytes[i] == 0 || strides_bytes[i] >= (1ull << 40))
+      return fail(FERRITE_BAD_ALIGNMENT, "TMA stride %d (%llu bytes) must be a positive multiple of 16 below 2^40",
+                  i + 1, (unsigned long long)strides_bytes[i]);
+  if ((box[0] * (uint32_t)elem_bytes) % 16 != 0)
+    return fail(FERRITE_BAD_ALIGNMENT, "TMA box inner extent not 16-byte multiple");
+  cuuint64_t d[4] = {dims[0], dims[1], dims[2], dims[3]};
+  cuuint64_t st[3] = {strides_bytes[0], strides_bytes[1], strides_bytes[2]};
+  cuuint32_t bx[4] = {box[0], box[1], box[2], box[3]};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = g_encode_tiled(map, dtype, 4, const_cast<void*>(base), d, st, bx, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(FERRITE_BAD_SHAPE, "cuTensorMapEncodeTiled (4d) failed (%d)", (int)r);
+  return FERRITE_OK;
+}
+
 }  // namespace ferrite
 
 extern "C" {

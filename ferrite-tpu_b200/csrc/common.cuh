@@ -46,6 +46,10 @@ int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
                  uint64_t stride1_bytes, uint64_t stride2_bytes,
                  uint32_t box0, uint32_t box1, uint32_t box2,
                  CUtensorMapSwizzle swizzle);
+// 4-D map (dims d0 innermost .. d3, byte strides of dims 1..3).
+int make_tmap_4d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
+                 int elem_bytes, const uint64_t dims[4], const uint64_t strides_bytes[3],
+                 const uint32_t box[4], CUtensorMapSwizzle swizzle);
 
 // Device status word, one per translation unit and device (internal linkage,
 // so the translation units need no relocatable device code).  Set by bounded
@@ -218,6 +222,16 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map,
       "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::"
       "bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
       "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map,
+                                            uint64_t* bar, int c0, int c1, int c2,
+                                            int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::"
+      "bytes [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
 }
 

@@ -50,6 +50,27 @@ _i32 = ctypes.c_int
 _f32 = ctypes.c_float
 _sz = ctypes.c_size_t
 
+
+
+class AttnStrides(ctypes.Structure):
+    """``ferrite_attn_strides``: (batch, head, sequence) element strides of each
+    [b, h, s, d] attention operand (d unit-stride)."""
+
+    _fields_ = [(n, _i64 * 3) for n in ("q", "k", "v", "o", "dout", "dq", "dk", "dv")]
+
+
+def attn_strides(**tensors: torch.Tensor) -> AttnStrides:
+    """Strides of the named [b, h, s, d] views (``q=..., o=...``); unnamed fields are 0."""
+    st = AttnStrides()
+    for name, t in tensors.items():
+        if t.stride(3) != 1:
+            raise ValueError(f"{name}: head_dim must be unit-stride")
+        getattr(st, name)[:] = (t.stride(0), t.stride(1), t.stride(2))
+    return st
+
+
+_sp = ctypes.POINTER(AttnStrides)
+
 # name -> (restype, argtypes).  Must match include/ferrite_b200.h.
 SIGNATURES: dict[str, tuple] = {
     "ferrite_last_error": (ctypes.c_char_p, []),
@@ -65,6 +86,10 @@ SIGNATURES: dict[str, tuple] = {
     "ferrite_attn_bwd_prep": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32]),
     "ferrite_attn_bwd_dkv": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _i32, _i32, _i32]),
     "ferrite_attn_bwd_dq": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _i32, _i32, _i32]),
+    "ferrite_attn_fwd_strided": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _sp, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _i32, _i32, _i32]),
+    "ferrite_attn_bwd_prep_strided": (_i32, [_vp, _vp, _vp, _vp, _sp, _i64, _i64, _i64, _i64, _i32]),
+    "ferrite_attn_bwd_dkv_strided": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sp, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _i32, _i32, _i32]),
+    "ferrite_attn_bwd_dq_strided": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sp, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _i32, _i32, _i32]),
 }
 
 

@@ -27,6 +27,7 @@ internally (128 x 128 on the tensor cores).
 
 from __future__ import annotations
 
+import ctypes
 import dataclasses
 import math
 
@@ -81,45 +82,56 @@ def _validate(q, k, v, causal, bs: BlockSizes):
             raise ValueError(f"{name}={blk} must be a multiple of {mult} and divide the sequence length {dim}")
 
 
-def _forward(q, k, v, causal: bool, scale: float, bs: BlockSizes):
+def _unit_d(t):
+    """The kernels read any [b, h, s, d] view whose head_dim is unit-stride."""
+    return t if t.stride(3) == 1 else t.contiguous()
+
+
+def _forward(q, k, v, causal: bool, scale: float, bs: BlockSizes, out=None):
+    """``(out, lse)``; ``out`` may be a caller-provided strided [b, h, s, d] view."""
     nat.require_cuda(q, k, v)
     b, h, sq, d = q.shape
     sk = k.shape[2]
-    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
-    out = torch.empty_like(q)
+    q, k, v = _unit_d(q), _unit_d(k), _unit_d(v)
+    if out is None:
+        out = torch.empty((b, h, sq, d), dtype=q.dtype, device=q.device)
     lse = torch.empty((b, h, sq), dtype=torch.float32, device=q.device)
+    st = nat.attn_strides(q=q, k=k, v=v, o=out)
     nat.check(
-        nat.lib().ferrite_attn_fwd(
+        nat.lib().ferrite_attn_fwd_strided(
             nat.stream_ptr(q.device), q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), lse.data_ptr(),
-            b, h, sq, sk, d, scale, int(causal), bs.block_q, bs.block_k, nat.dtype_code(q.dtype),
+            ctypes.byref(st), b, h, sq, sk, d, scale, int(causal), bs.block_q, bs.block_k, nat.dtype_code(q.dtype),
         )
     )
     return out, lse
 
 
-def _backward(q, k, v, out, lse, do, causal: bool, scale: float, bs: BlockSizes):
+def _backward(q, k, v, out, lse, do, causal: bool, scale: float, bs: BlockSizes, dq=None, dk=None, dv=None):
+    """``(dq, dk, dv)``; the gradients may be caller-provided strided views."""
     nat.require_cuda(q, k, v, out, lse, do)
     b, h, sq, d = q.shape
     sk = k.shape[2]
-    do = do.to(q.dtype).contiguous()
+    q, k, v, out = _unit_d(q), _unit_d(k), _unit_d(v), _unit_d(out)
+    do = _unit_d(do.to(q.dtype))
     lib = nat.lib()
     s = nat.stream_ptr(q.device)
     code = nat.dtype_code(q.dtype)
+    dq = torch.empty((b, h, sq, d), dtype=q.dtype, device=q.device) if dq is None else dq
+    dk = torch.empty((b, h, sk, d), dtype=k.dtype, device=q.device) if dk is None else dk
+    dv = torch.empty((b, h, sk, d), dtype=v.dtype, device=q.device) if dv is None else dv
+    st = ctypes.byref(nat.attn_strides(q=q, k=k, v=v, o=out, dout=do, dq=dq, dk=dk, dv=dv))
     delta = torch.empty((b, h, sq), dtype=torch.float32, device=q.device)
-    nat.check(lib.ferrite_attn_bwd_prep(s, do.data_ptr(), out.data_ptr(), delta.data_ptr(), b, h, sq, d, code))
-    dq = torch.empty_like(q)
-    dk = torch.empty_like(k)
-    dv = torch.empty_like(v)
+    nat.check(lib.ferrite_attn_bwd_prep_strided(s, do.data_ptr(), out.data_ptr(), delta.data_ptr(), st, b, h, sq, d, code))
     nat.check(
-        lib.ferrite_attn_bwd_dkv(
+        lib.ferrite_attn_bwd_dkv_strided(
             s, q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), lse.data_ptr(), delta.data_ptr(),
-            dk.data_ptr(), dv.data_ptr(), b, h, sq, sk, d, scale, int(causal), bs.block_q_bwd, bs.block_k_bwd, code,
+            dk.data_ptr(), dv.data_ptr(), st, b, h, sq, sk, d, scale, int(causal), bs.block_q_bwd, bs.block_k_bwd, code,
         )
     )
     nat.check(
-        lib.ferrite_attn_bwd_dq(
+        lib.ferrite_attn_bwd_dq_strided(
             s, q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), lse.data_ptr(), delta.data_ptr(),
-            dq.data_ptr(), b, h, sq, sk, d, scale, int(causal), bs.block_q_bwd, bs.block_k_bwd, code,
+            dq.data_ptr(), st, b, h, sq, sk, d, scale, int(causal), bs.block_q_bwd, bs.block_k_bwd, code,
         )
     )
     return dq, dk, dv
@@ -154,6 +166,59 @@ def flash_attention(q, k, v, *, causal: bool = True, scale: float | None = None,
     if scale is None:
         scale = 1.0 / math.sqrt(q.shape[-1])
     return _Flash.apply(q, k, v, bool(causal), float(scale), bs)
+
+
+def _split_packed(qkv):
+    """[b, s, 3, h, d] -> q, k, v as [b, h, s, d] views (no copies)."""
+    return tuple(qkv[:, :, i].permute(0, 2, 1, 3) for i in range(3))
+
+
+class _FlashPacked(torch.autograd.Function):
+    """Attention over a packed [b, s, 3, h, d] projection, output [b, s, h, d].
+
+    The kernels read q, k and v in place through strided tensor maps and write
+    the output, and in the backward dq/dk/dv, straight into the layouts the
+    transformer block's linears use, so the head split and the transposes
+    around the reference's attention call (gpt.py:136-138) cost no copies."""
+
+    @staticmethod
+    def forward(ctx, qkv, causal, scale, bs):
+        b, s, _, h, d = qkv.shape
+        q, k, v = _split_packed(qkv)
+        out = torch.empty((b, s, h, d), dtype=qkv.dtype, device=qkv.device)
+        _, lse = _forward(q, k, v, causal, scale, bs, out=out.permute(0, 2, 1, 3))
+        ctx.save_for_backward(qkv, out, lse)
+        ctx.causal, ctx.scale, ctx.bs = causal, scale, bs
+        return out
+
+    @staticmethod
+    def backward(ctx, do):
+        qkv, out, lse = ctx.saved_tensors
+        q, k, v = _split_packed(qkv)
+        dqkv = torch.empty_like(qkv)
+        dq, dk, dv = _split_packed(dqkv)
+        do = do if do.stride(3) == 1 else do.contiguous()
+        _backward(q, k, v, out.permute(0, 2, 1, 3), lse, do.permute(0, 2, 1, 3), ctx.causal, ctx.scale, ctx.bs, dq=dq, dk=dk, dv=dv)
+        return dqkv, None, None, None
+
+
+def flash_attention_packed(qkv, *, causal: bool = True, scale: float | None = None, block_sizes: BlockSizes | None = None):
+    """``flash_attention`` on a packed ``[b, s, 3, h, d]`` q/k/v projection.
+
+    Returns ``[b, s, h, d]`` -- the same values as
+    ``flash_attention(q, k, v).transpose(1, 2)`` with ``q, k, v = qkv.unbind(2)``
+    transposed to ``[b, h, s, d]`` -- without materialising any transpose, in the
+    forward or the backward.
+    """
+    if qkv.ndim != 5 or qkv.shape[2] != 3:
+        raise ValueError(f"expected qkv as [b, s, 3, h, d]; got {tuple(qkv.shape)}")
+    qkv = qkv if qkv.is_contiguous() else qkv.contiguous()
+    bs = block_sizes or BlockSizes()
+    q, k, v = _split_packed(qkv)
+    _validate(q, k, v, causal, bs)
+    if scale is None:
+        scale = 1.0 / math.sqrt(qkv.shape[-1])
+    return _FlashPacked.apply(qkv, bool(causal), float(scale), bs)
 
 
 def flash_forward_with_lse(q, k, v, *, causal: bool = True, scale: float | None = None, block_sizes: BlockSizes | None = None):

@@ -11,7 +11,10 @@ default); softmax, RMS and loss statistics are f32.
 
 Differences from the reference, all on the ``pallas`` slot: the tied LM head also
 runs on the B200 GEMM when ``cfg.linear == "pallas"`` (the reference always leaves
-it to XLA), with the embedding passed as the transposed operand (no copy); the
+it to XLA), with the embedding passed as the transposed operand (no copy); attention reads
+q/k/v in place from the packed ``[B, S, 3, H, hd]`` projection and writes
+``[B, S, H, hd]`` (``flash_attention_packed``), so the head split and the
+transposes of gpt.py:136-138 are folded into the kernels' tensor maps; the
 ``xla`` slot is plain torch (cuBLAS matmuls, materialised attention).
 """
 
@@ -25,7 +28,7 @@ import torch
 import torch.nn.functional as F
 
 from ferrite import platform
-from ferrite.kernels.flash_attention import BlockSizes, flash_attention, flash_attention_reference
+from ferrite.kernels.flash_attention import BlockSizes, flash_attention, flash_attention_packed, flash_attention_reference
 from ferrite.kernels.matmul import gemm, matmul
 from ferrite.kernels.rmsnorm import rmsnorm, rmsnorm_reference
 
@@ -161,8 +164,13 @@ def block(layer, h, pending, cfg: GPTConfig):
     else:
         h, y = _norm(pending, layer["ln1"], h, cfg)
     qkv = _linear(y, layer["wqkv"], cfg).reshape(b, s, 3, cfg.n_head, cfg.head_dim)
-    q, k, v = (qkv[:, :, i].transpose(1, 2).contiguous() for i in range(3))  # [B, H, S, hd]
-    a = _attention(q, k, v, cfg).transpose(1, 2).reshape(b, s, cfg.d_model)
+    q, k, v = (qkv[:, :, i].transpose(1, 2) for i in range(3))  # [B, H, S, hd] views
+    blocks = cfg.attention_blocks(s) if cfg.attention == "pallas" else None
+    if blocks is not None:
+        # q/k/v read in place and the output written as [B, S, H, hd]: no transposes
+        a = flash_attention_packed(qkv, causal=True, block_sizes=blocks).reshape(b, s, cfg.d_model)
+    else:
+        a = _attention(q, k, v, cfg).transpose(1, 2).reshape(b, s, cfg.d_model)
     a = _linear(a, layer["wo"], cfg)
     h, y2 = _norm(a, layer["ln2"], h, cfg)
     pending = _linear(F.gelu(_linear(y2, layer["w1"], cfg), approximate="tanh"), layer["w2"], cfg)

@@ -131,7 +131,7 @@ FERRITE_API int ferrite_gemm(void* stream, const void* a, const void* b, void* c
 /* ---- causal flash attention ------------------------------------------------ */
 
 /* Shapes: q [b, h, sq, d], k/v [b, h, sk, d], all of dtype `dtype`, densely
- * packed.  lse/delta are f32 [b, h, sq] (the reference keeps them
+ * packed (the *_strided forms below take other layouts).  lse/delta are f32 [b, h, sq] (the reference keeps them
  * lane-replicated as [b, h, sq, 128]; that layout is internal to its custom_vjp
  * residuals, so the compact one is a drop-in).  block_q/block_k are the caller's
  * BlockSizes; the kernels validate them exactly like _validate
@@ -169,6 +169,47 @@ FERRITE_API int ferrite_attn_bwd_dq(void* stream, const void* q, const void* k,
                         const float* delta, void* dq, int64_t b, int64_t h,
                         int64_t sq, int64_t sk, int64_t d, float scale,
                         int causal, int block_q, int block_k, int dtype);
+
+/* ---- strided flash attention ----------------------------------------------- */
+
+/* Element strides (batch, head, sequence) of each [b, h, s, d] operand; d is
+ * unit-stride.  Each call reads the fields of the operands it takes:
+ * fwd q,k,v,o; bwd_prep dout,o; bwd_dkv q,k,v,dout,dk,dv; bwd_dq q,k,v,dout,dq.
+ * Contiguous [b, h, s, d] is {h*s*d, s*d, d}.  The packed projection of a
+ * transformer block, [b, s, 3, h, d] (q, k, v slots), is read in place with
+ * {3*s*h*d, d, 3*h*d} at base + slot*h*d, and an output written as [b, s, h, d]
+ * (ready for the output projection) has {s*h*d, d, h*d}.  The tensor-core path
+ * needs 16-byte aligned bases and strides that are multiples of 8 elements;
+ * other layouts run the CUDA-core path.  Strides must be non-negative. */
+typedef struct ferrite_attn_strides {
+  int64_t q[3], k[3], v[3], o[3], dout[3], dq[3], dk[3], dv[3];
+} ferrite_attn_strides;
+
+/* The four entry points above on strided operands.  They replace the same
+ * reference kernels; the strided forms fold the head split and q/k/v
+ * transposes of the reference's attention caller (gpt.py:136-138, which
+ * transposes [b, s, h, d] to [b, h, s, d] before flash_attention) into the
+ * kernels' tensor maps. */
+FERRITE_API int ferrite_attn_fwd_strided(void* stream, const void* q, const void* k,
+                             const void* v, void* o, float* lse,
+                             const ferrite_attn_strides* strides, int64_t b, int64_t h,
+                             int64_t sq, int64_t sk, int64_t d, float scale, int causal,
+                             int block_q, int block_k, int dtype);
+FERRITE_API int ferrite_attn_bwd_prep_strided(void* stream, const void* dout, const void* out,
+                                  float* delta, const ferrite_attn_strides* strides,
+                                  int64_t b, int64_t h, int64_t s, int64_t d, int dtype);
+FERRITE_API int ferrite_attn_bwd_dkv_strided(void* stream, const void* q, const void* k,
+                                 const void* v, const void* dout, const float* lse,
+                                 const float* delta, void* dk, void* dv,
+                                 const ferrite_attn_strides* strides, int64_t b, int64_t h,
+                                 int64_t sq, int64_t sk, int64_t d, float scale, int causal,
+                                 int block_q, int block_k, int dtype);
+FERRITE_API int ferrite_attn_bwd_dq_strided(void* stream, const void* q, const void* k,
+                                const void* v, const void* dout, const float* lse,
+                                const float* delta, void* dq,
+                                const ferrite_attn_strides* strides, int64_t b, int64_t h,
+                                int64_t sq, int64_t sk, int64_t d, float scale, int causal,
+                                int block_q, int block_k, int dtype);
 
 #ifdef __cplusplus
 }

@@ -43,6 +43,22 @@ def max_abs(a, b) -> float:
     return float(np.max(np.abs(f32(a) - f32(b)))) if np.size(a) else 0.0
 
 
+def bf16_ulp(x) -> np.ndarray:
+    """Spacing of bf16 values at |x|: 2^(e - 7) with e = floor(log2 |x|)."""
+    a = np.maximum(np.abs(f32(x)), np.float32(2.0**-126))
+    return np.ldexp(np.float32(1.0), np.floor(np.log2(a)).astype(np.int32) - 7)
+
+
+def assert_bf16_close(got, ref, atol: float = 2e-2) -> None:
+    """|got - ref| <= max(atol, one bf16 ulp of ref): the max-abs 2e-2 bound on bf16
+    results, widened to bf16's own rounding step where |ref| >= 4 (2^-5 there), since
+    two correct implementations may round a value near a tie to neighbouring bf16s."""
+    g, r = f32(got), f32(ref)
+    bound = np.maximum(np.float32(atol), bf16_ulp(r))
+    bad = np.abs(g - r) > bound
+    assert not bad.any(), f"{int(bad.sum())} elements off; worst {float(np.max(np.abs(g - r) - bound)):.3g} over the bound"
+
+
 def rel_l2(a, b) -> float:
     a, b = f32(a).astype(np.float64), f32(b).astype(np.float64)
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))

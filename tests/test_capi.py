@@ -65,6 +65,38 @@ def test_status_codes_without_a_gpu():
     assert e.value.status == nat.UNSUPPORTED_DTYPE
 
 
+def test_strided_attention_validation_without_a_gpu():
+    """The strided entry points check their stride block on the host, after the
+    shape checks and before any CUDA call."""
+    lib = nat.lib()
+    args = (1, 2, 256, 256, 64, 0.125, 1, 128, 128, nat.BF16)
+    rc = lib.ferrite_attn_fwd_strided(None, 1, 1, 1, 1, 1, None, *args)
+    assert rc == nat.BAD_SHAPE and "null strides" in nat.last_error()
+    st = nat.AttnStrides()
+    st.k[:] = (0, -64, 64)
+    rc = lib.ferrite_attn_fwd_strided(None, 1, 1, 1, 1, 1, ctypes.byref(st), *args)
+    assert rc == nat.BAD_SHAPE and "negative stride" in nat.last_error()
+    rc = lib.ferrite_attn_bwd_dq_strided(None, 1, 1, 1, 1, 1, 1, 1, ctypes.byref(st), *args)
+    assert rc == nat.BAD_SHAPE
+    rc = lib.ferrite_attn_bwd_dkv_strided(None, 1, 1, 1, 1, 1, 1, 1, 1, None, *args)
+    assert rc == nat.BAD_SHAPE
+    rc = lib.ferrite_attn_bwd_prep_strided(None, 1, 1, 1, None, 1, 2, 256, 64, nat.BF16)
+    assert rc == nat.BAD_SHAPE
+    # shape errors come first, as in the contiguous entry points
+    rc = lib.ferrite_attn_fwd_strided(None, 1, 1, 1, 1, 1, ctypes.byref(st), 1, 2, 256, 256, 64, 0.125, 1, 100, 128, nat.BF16)
+    assert rc == nat.BAD_SHAPE and "block_q" in nat.last_error()
+
+
+def test_attn_strides_struct_matches_views():
+    qkv = torch.zeros(2, 256, 3, 4, 64)
+    q = qkv[:, :, 0].permute(0, 2, 1, 3)
+    st = nat.attn_strides(q=q)
+    assert tuple(st.q) == (256 * 3 * 4 * 64, 64, 3 * 4 * 64) and tuple(st.k) == (0, 0, 0)
+    assert ctypes.sizeof(nat.AttnStrides) == 8 * 3 * 8
+    with pytest.raises(ValueError):
+        nat.attn_strides(q=q.transpose(2, 3))
+
+
 def test_host_fault_injection(monkeypatch):
     lib = nat.lib()
     monkeypatch.setenv("FERRITE_FAULT_INJECT", "rmsnorm_fwd,add_rmsnorm_fwd")

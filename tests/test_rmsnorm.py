@@ -14,7 +14,7 @@ import torch
 
 from ferrite import _native as nat
 from ferrite.kernels.rmsnorm import rmsnorm, rmsnorm_backward, rmsnorm_reference
-from helpers import BF16, load_arrays, max_abs, normal, to_numpy, to_torch
+from helpers import BF16, assert_bf16_close, load_arrays, max_abs, normal, to_numpy, to_torch
 from oracle import rmsnorm as on
 
 pytestmark = pytest.mark.gpu
@@ -74,7 +74,7 @@ def test_golden_fixtures():
     assert np.array_equal(to_numpy(h).view(np.uint16), g["h"].view(np.uint16))  # x+r rounding is exact
     assert max_abs(y, g["y"]) <= 2e-2
     dh, dw = rmsnorm_backward(to_torch(g["h"]), to_torch(g["w"]), to_torch(g["dy"]), to_torch(g["dh_direct"]), 1e-6)
-    assert max_abs(dh, g["dh"]) <= 2e-2
+    assert_bf16_close(dh, g["dh"])
     np.testing.assert_allclose(to_numpy(dw), g["dw"], rtol=1e-4, atol=1e-3)
     g = load_arrays(os.path.join(GOLDEN, "rmsnorm_f32_40x384.npz"))
     y = rmsnorm(to_torch(g["x"]), to_torch(g["w"]))
@@ -103,7 +103,7 @@ def test_add_rmsnorm_fwd_bwd_vs_oracle(rows, dim):
     assert np.all(np.abs(yg - yr) <= np.abs(yr) * 2**-7 + 1e-6)
     dh, dw = rmsnorm_backward(to_torch(h_ref), to_torch(w), to_torch(dy), to_torch(dhd), 1e-6)
     dh_ref, dw_ref = on.rmsnorm_bwd(h_ref, w, dy, dhd)
-    assert max_abs(dh, dh_ref) <= 2e-2
+    assert_bf16_close(dh, dh_ref)
     np.testing.assert_allclose(to_numpy(dw), dw_ref, rtol=2e-4, atol=2e-3 * np.sqrt(rows / 64 + 1))
 
 
@@ -144,14 +144,22 @@ def test_device_status_clean():
 @pytest.mark.parametrize("dim", [1024, 4096])
 def test_tma_backward_matches_register_backward(monkeypatch, dim):
     """The TMA-fed backward (16-bit rows of 256..4096) and the register-prefetch
-    backward give bitwise-equal dh and dw within f32 summation order."""
+    backward agree: the two sum a row in different orders, so dh may differ in the
+    last bf16 bit and dw within f32 summation order; both meet the oracle."""
     rng = np.random.default_rng(dim)
     rows = 1000
-    h = to_torch(normal(rng, (rows, dim), BF16))
-    w = to_torch((1.0 + 0.1 * rng.standard_normal(dim)).astype(np.float32))
-    dy, dhd = to_torch(normal(rng, (rows, dim), BF16)), to_torch(normal(rng, (rows, dim), BF16))
+    hn = normal(rng, (rows, dim), BF16)
+    wn = (1.0 + 0.1 * rng.standard_normal(dim)).astype(np.float32)
+    dyn, dhdn = normal(rng, (rows, dim), BF16), normal(rng, (rows, dim), BF16)
+    h, w, dy, dhd = to_torch(hn), to_torch(wn), to_torch(dyn), to_torch(dhdn)
     dh_a, dw_a = rmsnorm_backward(h, w, dy, dhd, 1e-6)
     monkeypatch.setenv("FERRITE_RMSNORM_BWD_TMA", "0")
     dh_b, dw_b = rmsnorm_backward(h, w, dy, dhd, 1e-6)
-    assert torch.equal(dh_a, dh_b)
+    a, b = dh_a.float(), dh_b.float()
+    assert torch.all((a - b).abs() <= b.abs() * 2**-7 + 1e-6)  # at most one bf16 ulp
+    assert (a != b).float().mean().item() < 0.01
     torch.testing.assert_close(dw_a, dw_b, rtol=1e-5, atol=1e-4)
+    dh_ref, dw_ref = on.rmsnorm_bwd(hn, wn, dyn, dhdn)
+    for dh, dw in ((dh_a, dw_a), (dh_b, dw_b)):
+        assert_bf16_close(dh, dh_ref)
+        np.testing.assert_allclose(to_numpy(dw), dw_ref, rtol=2e-4, atol=2e-3 * np.sqrt(rows / 64 + 1))
