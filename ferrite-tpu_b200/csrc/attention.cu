@@ -78,6 +78,44 @@ __global__ void __launch_bounds__(256)
   if (lane == 0) delta[row] = s;
 }
 
+// Vectorised delta: CTA (x, bh) covers prep_rows_per_cta(VPR) sequence rows of
+// slice bh; a row is read as VPR 16-byte vectors by VPR adjacent lanes (VPR =
+// d / (16 / sizeof(T)), a power of two <= 32) and reduced with xor shuffles
+// inside that lane group.  No integer division on the hot path.
+__host__ __device__ constexpr int prep_rows_per_cta(int vpr) {
+  return 256 / vpr > 128 ? 256 / vpr : 128;  // at least one full pass of 256 threads
+}
+
+template <typename T, int VPR>
+__global__ void __launch_bounds__(256)
+    bwd_prep_vec_kernel(const T* __restrict__ dout, const T* __restrict__ out,
+                        float* __restrict__ delta, Bhsd ld, Bhsd lo, int s_len) {
+  constexpr int kElems = 16 / sizeof(T);
+  constexpr int kRowsPerPass = 256 / VPR;
+  constexpr int kPasses = prep_rows_per_cta(VPR) / kRowsPerPass;
+  const int bh = blockIdx.y;
+  const int sub = threadIdx.x % VPR, rloc = threadIdx.x / VPR;
+  const T* db = dout + ld.row(bh, 0) + sub * kElems;
+  const T* ob = out + lo.row(bh, 0) + sub * kElems;
+  const int r_begin = blockIdx.x * prep_rows_per_cta(VPR);
+#pragma unroll 2
+  for (int pass = 0; pass < kPasses; ++pass) {
+    const int r = r_begin + pass * kRowsPerPass + rloc;
+    float acc = 0.f;
+    if (r < s_len) {
+      const uint4 a = ld_stream_v4(db + (int64_t)r * ld.s);
+      const uint4 b = ld_stream_v4(ob + (int64_t)r * lo.s);
+      const T* ea = reinterpret_cast<const T*>(&a);
+      const T* eb = reinterpret_cast<const T*>(&b);
+#pragma unroll
+      for (int e = 0; e < kElems; ++e) acc = fmaf(DT<T>::to_f(ea[e]), DT<T>::to_f(eb[e]), acc);
+    }
+#pragma unroll
+    for (int off = VPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (sub == 0 && r < s_len) delta[(int64_t)bh * s_len + r] = acc;
+  }
+}
+
 // ===========================================================================
 // CUDA-core path (any dtype, head_dim <= 256)
 // ===========================================================================
@@ -1224,20 +1262,49 @@ static int attn_fwd_impl(cudaStream_t s, const void* q, const void* k, const voi
   return check_launch("attn_fwd_simt");
 }
 
+template <typename T>
+static bool prep_vec_ok(const void* p, const Bhsd& l, int64_t b, int64_t h) {
+  constexpr int kElems = 16 / sizeof(T);
+  auto ok = [](int64_t st, int64_t n) { return n == 1 || st % kElems == 0; };
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0 && l.s % kElems == 0 && ok(l.b, b) && ok(l.h, h);
+}
+
+template <typename T>
+static int launch_prep(cudaStream_t s, const void* dout, const void* out, float* delta,
+                       const Bhsd& ld, const Bhsd& lo, int64_t b, int64_t h, int64_t s_, int64_t d) {
+  constexpr int kElems = 16 / sizeof(T);
+  const int64_t vpr = d / kElems;
+  const bool vec = d % kElems == 0 && vpr <= 32 && (vpr & (vpr - 1)) == 0 && b * h <= 65535 &&
+                   prep_vec_ok<T>(dout, ld, b, h) && prep_vec_ok<T>(out, lo, b, h);
+  if (vec) {
+    const int rpc = prep_rows_per_cta((int)vpr);
+    dim3 grid((unsigned)((s_ + rpc - 1) / rpc), (unsigned)(b * h));
+    const T* a = (const T*)dout;
+    const T* o = (const T*)out;
+    switch (vpr) {
+      case 1: bwd_prep_vec_kernel<T, 1><<<grid, 256, 0, s>>>(a, o, delta, ld, lo, (int)s_); break;
+      case 2: bwd_prep_vec_kernel<T, 2><<<grid, 256, 0, s>>>(a, o, delta, ld, lo, (int)s_); break;
+      case 4: bwd_prep_vec_kernel<T, 4><<<grid, 256, 0, s>>>(a, o, delta, ld, lo, (int)s_); break;
+      case 8: bwd_prep_vec_kernel<T, 8><<<grid, 256, 0, s>>>(a, o, delta, ld, lo, (int)s_); break;
+      case 16: bwd_prep_vec_kernel<T, 16><<<grid, 256, 0, s>>>(a, o, delta, ld, lo, (int)s_); break;
+      default: bwd_prep_vec_kernel<T, 32><<<grid, 256, 0, s>>>(a, o, delta, ld, lo, (int)s_); break;
+    }
+    return check_launch("attn_bwd_prep");
+  }
+  const int64_t rows = b * h * s_;
+  bwd_prep_kernel<T><<<(unsigned)((rows + 7) / 8), 256, 0, s>>>((const T*)dout, (const T*)out, delta, ld,
+                                                                 lo, rows, (int)s_, (int)d);
+  return check_launch("attn_bwd_prep");
+}
+
 static int attn_bwd_prep_impl(cudaStream_t s, const void* dout, const void* out, float* delta,
                               const ferrite_attn_strides& st, int64_t b, int64_t h, int64_t s_,
                               int64_t d, int dtype) {
   const Bhsd ld = bhsd_of(st.dout, h), lo = bhsd_of(st.o, h);
-  const int64_t rows = b * h * s_;
-  const unsigned grid = (unsigned)((rows + 7) / 8);
-#define PREP(T) \
-  bwd_prep_kernel<T><<<grid, 256, 0, s>>>((const T*)dout, (const T*)out, delta, ld, lo, rows, (int)s_, (int)d)
-  if (dtype == FERRITE_F32) PREP(float);
-  else if (dtype == FERRITE_BF16) PREP(__nv_bfloat16);
-  else if (dtype == FERRITE_F16) PREP(__half);
-  else return fail(FERRITE_UNSUPPORTED_DTYPE, "attn_bwd_prep: dtype %d", dtype);
-#undef PREP
-  return check_launch("attn_bwd_prep");
+  if (dtype == FERRITE_F32) return launch_prep<float>(s, dout, out, delta, ld, lo, b, h, s_, d);
+  if (dtype == FERRITE_BF16) return launch_prep<__nv_bfloat16>(s, dout, out, delta, ld, lo, b, h, s_, d);
+  if (dtype == FERRITE_F16) return launch_prep<__half>(s, dout, out, delta, ld, lo, b, h, s_, d);
+  return fail(FERRITE_UNSUPPORTED_DTYPE, "attn_bwd_prep: dtype %d", dtype);
 }
 
 static bool tc_bwd_ok(const BwdArgs& a, int64_t b, int64_t h, int64_t sq, int64_t sk, int64_t d,

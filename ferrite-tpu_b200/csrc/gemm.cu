@@ -14,6 +14,11 @@
 //   Operands may be K-major or MN-major in global memory (the transpose flags
 //   of the C ABI); the MN-major case uses MN-major shared-memory layouts and the
 //   instruction descriptor's transpose bits instead of materialised transposes.
+//   Split-K: when the output has too few tiles to fill the SMs (the weight
+//   gradients X^T G of a transformer: small M x N, K = tokens), each tile's K
+//   range is cut into `splits` slices that run as independent work units and
+//   write f32 partial tiles to a caller-provided workspace; a second kernel sums
+//   the slices in slice order (deterministic, no atomics) and rounds once.
 //
 // f32 operands (the reference's Precision.HIGHEST contract, _compat.py:17-26)
 // and shapes TMA cannot describe (row strides not a multiple of 16 bytes, tiny
@@ -54,6 +59,9 @@ struct Params {
   void* c;
   int tiles_m, tiles_n, k_blocks;
   int group_m;  // raster: groups of group_m M-tiles sweep all N-tiles
+  int splits;        // K slices per tile (1: no split)
+  int kb_per_split;  // k blocks per slice
+  float* ws;         // splits > 1: f32 partials [splits][m][n]
 };
 
 template <typename TC>
@@ -123,6 +131,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int num_tiles = p.tiles_m * p.tiles_n;
+  // Work unit u: tile u % num_tiles, K slice u / num_tiles (units of one slice
+  // share a K range, so concurrently running CTAs share A/B rows in L2).
+  const int num_units = num_tiles * p.splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -154,10 +165,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
         int mb, nb;
-        tile_coords(t, p, mb, nb);
-        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+        tile_coords(u % num_tiles, p, mb, nb);
+        const int kb0 = (u / num_tiles) * p.kb_per_split;
+        const int kb1 = min(kb0 + p.kb_per_split, p.k_blocks);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, abort, 1)) {
@@ -194,13 +207,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t da_base = A_MN ? make_sdesc(s0, 8192, 1024) : make_sdesc(s0, 16, 1024);
       const uint64_t db_base = B_MN ? make_sdesc(s0 + S::kABytes, 8192, 1024)
                                     : make_sdesc(s0 + S::kABytes, 16, 1024);
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++local) {
         const int buf = local & 1;
         const uint32_t aph = (local >> 1) & 1;
         if (!mbar_wait(&acc_empty[buf], aph ^ 1, abort, 2)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
-        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+        const int kb0 = (u / num_tiles) * p.kb_per_split;
+        const int kb1 = min(kb0 + p.kb_per_split, p.k_blocks);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(&full[s], ph, abort, 3)) {
@@ -213,7 +228,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
             tc_mma_f16_ss(d_tmem, sdesc_at(da, A_MN ? kk * 2048 : kk * 32),
-                          sdesc_at(db, B_MN ? kk * 2048 : kk * 32), idesc, (kb | kk) != 0);
+                          sdesc_at(db, B_MN ? kk * 2048 : kk * 32), idesc,
+                          (kb != kb0 || kk != 0) ? 1u : 0u);
           tc_commit(&empty[s]);  // slot free once these MMAs retire
         }
         tc_commit(&acc_full[buf]);  // accumulator ready for the epilogue
@@ -226,10 +242,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     TC* c = reinterpret_cast<TC*>(p.c);
     const bool vec_ok = ((reinterpret_cast<uintptr_t>(c) & 15u) == 0) &&
                         ((p.ldc * (int64_t)sizeof(TC)) % 16 == 0);
+    // partial slices are [m][n] f32 blocks of a 256-byte aligned workspace
+    const bool ws_vec_ok = (p.n % 4 == 0);
     int local = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++local) {
       int mb, nb;
-      tile_coords(t, p, mb, nb);
+      tile_coords(u % num_tiles, p, mb, nb);
+      const int split = u / num_tiles;
       const int buf = local & 1;
       const uint32_t aph = (local >> 1) & 1;
       if (!mbar_wait(&acc_full[buf], aph, abort, 4)) break;
@@ -241,7 +260,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t r[32];
         tmem_ld32(tbase + cc * 32, r);
         tmem_wait_ld();
-        store_row32<TC>(c, p.ldc, row, nb * BN + cc * 32, p.m, p.n, r, vec_ok);
+        if (p.splits > 1)
+          store_row32<float>(p.ws + (int64_t)split * p.m * p.n, p.n, row, nb * BN + cc * 32, p.m,
+                             p.n, r, ws_vec_ok);
+        else
+          store_row32<TC>(c, p.ldc, row, nb * BN + cc * 32, p.m, p.n, r, vec_ok);
       }
       tc_fence_before();
       __syncwarp();
@@ -254,6 +277,42 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+// Split-K reduction: C = sum over slices (in slice order) of the f32 partials,
+// rounded once to TC.  Four columns per thread (16-byte loads when n % 4 == 0).
+template <typename TC>
+__global__ void __launch_bounds__(256)
+    splitk_reduce_kernel(const float* __restrict__ ws, TC* __restrict__ c, int m, int n,
+                         int64_t ldc, int splits) {
+  const int64_t plane = (int64_t)m * n;
+  const int groups = (n + 3) / 4;
+  const int64_t total = (int64_t)m * groups;
+  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total;
+       g += (int64_t)gridDim.x * blockDim.x) {
+    const int row = (int)(g / groups);
+    const int col = (int)(g - (int64_t)row * groups) * 4;
+    const float* src = ws + (int64_t)row * n + col;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    if (n % 4 == 0) {
+      for (int sp = 0; sp < splits; ++sp) {
+        const float4 v = __ldcs(reinterpret_cast<const float4*>(src + sp * plane));
+        acc[0] += v.x;
+        acc[1] += v.y;
+        acc[2] += v.z;
+        acc[3] += v.w;
+      }
+    } else {
+      for (int sp = 0; sp < splits; ++sp)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (col + j < n) acc[j] += src[sp * plane + j];
+    }
+    TC* dst = c + (int64_t)row * ldc + col;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (col + j < n) dst[j] = DT<TC>::from_f(acc[j]);
   }
 }
 
@@ -400,19 +459,75 @@ static int dispatch_major(cudaStream_t s, bool a_mn, bool b_mn, const CUtensorMa
   return launch_tc<BN, true, true, BF16, TC>(s, ta, tb, p, grid);
 }
 
+// Tile width and K split.  Cost model in units of one 128x256x64 MMA block on
+// one SM: a 128-wide tile block costs 0.69 (half the FLOPs at ~72% of the
+// 256-wide rate, measured), waves are ceil(units / SMs), and a split adds the
+// f32 partial traffic (write + read of splits x M x N x 4 bytes, ~2.3 MB per
+// unit of time at HBM rate) plus the reduction launch.
+struct Plan {
+  int bn, splits, kb_per_split;
+};
+
+static Plan plan_tc(int64_t m, int64_t n, int64_t k, int sms, bool allow_split) {
+  const int64_t kb = (k + BK - 1) / BK;
+  const int64_t tm = (m + BM - 1) / BM;
+  Plan best{n < 256 ? 128 : 256, 1, (int)kb};
+  double best_cost = 1e300;
+  const int max_splits = allow_split ? (int)std::min<int64_t>(16, kb / 4) : 1;
+  for (int bn : {256, 128}) {
+    if (bn == 256 && n < 256) continue;
+    const int64_t tiles = tm * ((n + bn - 1) / bn);
+    const double unit = bn == 256 ? 1.0 : 0.69;
+    for (int sp = 1; sp <= std::max(1, max_splits); ++sp) {
+      const int64_t kbs = (kb + sp - 1) / sp;
+      const int64_t eff_splits = (kb + kbs - 1) / kbs;  // no empty slices
+      if (eff_splits != sp) continue;
+      const int64_t units = tiles * sp;
+      const double waves = (double)((units + sms - 1) / sms);
+      double cost = waves * (double)kbs * unit;
+      if (sp > 1) cost += 2.0 * sp * (double)m * (double)n * 4.0 / 2.3e6 + 13.0;
+      if (cost < best_cost * 0.97) {  // prefer fewer splits / wider tiles on near-ties
+        best_cost = cost;
+        best = Plan{bn, sp, (int)kbs};
+      }
+    }
+  }
+  const int forced = env_int("FERRITE_GEMM_BN", 0);
+  if ((forced == 128 || forced == 256) && n >= forced) best.bn = forced;
+  const int forced_split = env_int("FERRITE_GEMM_SPLITS", 0);
+  if (allow_split && forced_split >= 1) {
+    const int64_t kbs = (kb + forced_split - 1) / forced_split;
+    best.splits = (int)((kb + kbs - 1) / kbs);
+    best.kb_per_split = (int)kbs;
+  }
+  return best;
+}
+
+static size_t plan_workspace(const Plan& pl, int64_t m, int64_t n) {
+  return pl.splits > 1 ? (size_t)pl.splits * (size_t)m * (size_t)n * sizeof(float) : 0;
+}
+
+template <typename TC>
+static int launch_reduce(cudaStream_t s, const float* ws, void* c, int64_t m, int64_t n,
+                         int64_t ldc, int splits, int sms) {
+  const int64_t groups = m * ((n + 3) / 4);
+  const int64_t want = (groups + 255) / 256;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(want, (int64_t)sms * 8));
+  splitk_reduce_kernel<TC><<<grid, 256, 0, s>>>(ws, (TC*)c, (int)m, (int)n, ldc, splits);
+  return check_launch("gemm_splitk_reduce");
+}
+
 template <bool BF16, typename TC>
 static int run_tc(cudaStream_t s, const void* a, const void* b, void* c, int64_t m,
                   int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int trans_a,
-                  int trans_b) {
+                  int trans_b, void* workspace, size_t ws_bytes) {
   const int dev = current_device();
   const int sms = num_sms(dev);
-  // B tile width: 256 unless that leaves most SMs idle.
-  const int64_t tiles256 = ((m + BM - 1) / BM) * ((n + 255) / 256);
-  int BN = (tiles256 >= sms || n <= 128) ? 256 : 128;
-  if (n <= 128) BN = 128;
-  const int forced = env_int("FERRITE_GEMM_BN", 0);
-  if (forced == 128 || forced == 256) BN = forced;
-  if (n < BN) BN = 128;
+  Plan pl = plan_tc(m, n, k, sms, workspace != nullptr);
+  if (plan_workspace(pl, m, n) > ws_bytes || (reinterpret_cast<uintptr_t>(workspace) & 255u)) {
+    pl = plan_tc(m, n, k, sms, false);  // not enough scratch: no split
+  }
+  const int BN = pl.bn;
 
   const CUtensorMapDataType dt = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap ta, tb;
@@ -444,10 +559,15 @@ static int run_tc(cudaStream_t s, const void* a, const void* b, void* c, int64_t
   p.tiles_n = (int)((n + BN - 1) / BN);
   p.k_blocks = (int)((k + BK - 1) / BK);
   p.group_m = std::max(1, std::min(env_int("FERRITE_GEMM_GROUP_M", 16), p.tiles_m));
-  const int tiles = p.tiles_m * p.tiles_n;
-  const int grid = std::min(tiles, sms);
-  if (BN == 256) return dispatch_major<256, BF16, TC>(s, a_mn, b_mn, ta, tb, p, grid);
-  return dispatch_major<128, BF16, TC>(s, a_mn, b_mn, ta, tb, p, grid);
+  p.splits = pl.splits;
+  p.kb_per_split = pl.kb_per_split;
+  p.ws = pl.splits > 1 ? reinterpret_cast<float*>(workspace) : nullptr;
+  const int units = p.tiles_m * p.tiles_n * p.splits;
+  const int grid = std::min(units, sms);
+  rc = BN == 256 ? dispatch_major<256, BF16, TC>(s, a_mn, b_mn, ta, tb, p, grid)
+                 : dispatch_major<128, BF16, TC>(s, a_mn, b_mn, ta, tb, p, grid);
+  if (rc || pl.splits == 1) return rc;
+  return launch_reduce<TC>(s, p.ws, c, m, n, ldc, pl.splits, sms);
 }
 
 // True when every operand satisfies the TMA rules and the tile shapes fit.
@@ -470,9 +590,28 @@ static bool tc_eligible(const void* a, const void* b, int64_t m, int64_t n, int6
 using namespace ferrite;
 using namespace ferrite::gemm;
 
+extern "C" size_t ferrite_gemm_workspace_size(int64_t m, int64_t n, int64_t k, int64_t lda,
+                                              int64_t ldb, int trans_a, int trans_b,
+                                              int ab_dtype) {
+  if (m <= 0 || n <= 0 || k <= 0 || ab_dtype == FERRITE_F32) return 0;
+  if (m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff) return 0;
+  // Same eligibility rules as the launch, with aligned stand-in pointers.
+  const void* aligned = reinterpret_cast<const void*>(uintptr_t(256));
+  if (!tc_eligible(aligned, aligned, m, n, k, lda, ldb, trans_a, trans_b)) return 0;
+  return plan_workspace(plan_tc(m, n, k, num_sms(current_device()), true), m, n);
+}
+
 extern "C" int ferrite_gemm(void* stream, const void* a, const void* b, void* c, int64_t m,
                             int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc,
                             int trans_a, int trans_b, int ab_dtype, int c_dtype) {
+  return ferrite_gemm_ws(stream, a, b, c, m, n, k, lda, ldb, ldc, trans_a, trans_b, ab_dtype,
+                         c_dtype, nullptr, 0);
+}
+
+extern "C" int ferrite_gemm_ws(void* stream, const void* a, const void* b, void* c, int64_t m,
+                               int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc,
+                               int trans_a, int trans_b, int ab_dtype, int c_dtype,
+                               void* workspace, size_t workspace_bytes) {
   if (int rc = injected_fault("gemm")) return rc;
   if (m < 0 || n < 0 || k < 0)
     return fail(FERRITE_BAD_SHAPE, "gemm: negative size m=%lld n=%lld k=%lld", (long long)m,
@@ -502,13 +641,13 @@ extern "C" int ferrite_gemm(void* stream, const void* a, const void* b, void* c,
   if (ab_dtype != FERRITE_F32 && tc_eligible(a, b, m, n, k, lda, ldb, trans_a, trans_b)) {
     const bool bf = ab_dtype == FERRITE_BF16;
     if (bf) {
-      if (c_dtype == FERRITE_BF16) return run_tc<true, __nv_bfloat16>(s, a, b, c, m, n, k, lda, ldb, ldc, trans_a, trans_b);
-      if (c_dtype == FERRITE_F32) return run_tc<true, float>(s, a, b, c, m, n, k, lda, ldb, ldc, trans_a, trans_b);
-      return run_tc<true, __half>(s, a, b, c, m, n, k, lda, ldb, ldc, trans_a, trans_b);
+      if (c_dtype == FERRITE_BF16) return run_tc<true, __nv_bfloat16>(s, a, b, c, m, n, k, lda, ldb, ldc, trans_a, trans_b, workspace, workspace_bytes);
+      if (c_dtype == FERRITE_F32) return run_tc<true, float>(s, a, b, c, m, n, k, lda, ldb, ldc, trans_a, trans_b, workspace, workspace_bytes);
+      return run_tc<true, __half>(s, a, b, c, m, n, k, lda, ldb, ldc, trans_a, trans_b, workspace, workspace_bytes);
     }
-    if (c_dtype == FERRITE_BF16) return run_tc<false, __nv_bfloat16>(s, a, b, c, m, n, k, lda, ldb, ldc, trans_a, trans_b);
-    if (c_dtype == FERRITE_F32) return run_tc<false, float>(s, a, b, c, m, n, k, lda, ldb, ldc, trans_a, trans_b);
-    return run_tc<false, __half>(s, a, b, c, m, n, k, lda, ldb, ldc, trans_a, trans_b);
+    if (c_dtype == FERRITE_BF16) return run_tc<false, __nv_bfloat16>(s, a, b, c, m, n, k, lda, ldb, ldc, trans_a, trans_b, workspace, workspace_bytes);
+    if (c_dtype == FERRITE_F32) return run_tc<false, float>(s, a, b, c, m, n, k, lda, ldb, ldc, trans_a, trans_b, workspace, workspace_bytes);
+    return run_tc<false, __half>(s, a, b, c, m, n, k, lda, ldb, ldc, trans_a, trans_b, workspace, workspace_bytes);
   }
 #define SIMT(TA, TC) launch_simt<TA, TC>(s, a, b, c, m, n, k, lda, ldb, ldc, trans_a, trans_b)
   if (ab_dtype == FERRITE_F32) {

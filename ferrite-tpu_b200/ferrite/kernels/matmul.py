@@ -52,11 +52,16 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, trans_a: bool = False, trans_b: bo
     out_dtype = out_dtype or a.dtype
     if out is None:
         out = torch.empty((m, n), dtype=out_dtype, device=a.device)
+    lib = nat.lib()
+    code = nat.dtype_code(a.dtype)
+    # split-K scratch for few-tile outputs (weight gradients); 0 bytes otherwise
+    ws_bytes = lib.ferrite_gemm_workspace_size(m, n, ka, a.stride(0), b.stride(0), int(trans_a), int(trans_b), code) if m and n and ka else 0
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=a.device) if ws_bytes else None
     nat.check(
-        nat.lib().ferrite_gemm(
+        lib.ferrite_gemm_ws(
             nat.stream_ptr(a.device), a.data_ptr(), b.data_ptr(), out.data_ptr(), m, n, ka,
             a.stride(0), b.stride(0), out.stride(0), int(trans_a), int(trans_b),
-            nat.dtype_code(a.dtype), nat.dtype_code(out.dtype),
+            code, nat.dtype_code(out.dtype), None if ws is None else ws.data_ptr(), ws_bytes,
         )
     )
     return out

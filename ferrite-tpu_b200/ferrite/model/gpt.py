@@ -15,6 +15,8 @@ it to XLA), with the embedding passed as the transposed operand (no copy); atten
 q/k/v in place from the packed ``[B, S, 3, H, hd]`` projection and writes
 ``[B, S, H, hd]`` (``flash_attention_packed``), so the head split and the
 transposes of gpt.py:136-138 are folded into the kernels' tensor maps; the
+loss (gpt.py:147-152) runs on the native cross-entropy kernels, fused with the
+tied head into one autograd node (no f32 logit gradient is materialised); the
 ``xla`` slot is plain torch (cuBLAS matmuls, materialised attention).
 """
 
@@ -29,6 +31,7 @@ import torch.nn.functional as F
 
 from ferrite import platform
 from ferrite.kernels.flash_attention import BlockSizes, flash_attention, flash_attention_packed, flash_attention_reference
+from ferrite.kernels.cross_entropy import tied_head_cross_entropy
 from ferrite.kernels.matmul import gemm, matmul
 from ferrite.kernels.rmsnorm import rmsnorm, rmsnorm_reference
 
@@ -177,8 +180,8 @@ def block(layer, h, pending, cfg: GPTConfig):
     return h, pending, k, v
 
 
-def forward(params, tokens, cfg: GPTConfig):
-    """tokens [B, S] int -> logits [B, S, vocab] f32 (gpt.py:124-144)."""
+def hidden(params, tokens, cfg: GPTConfig):
+    """tokens [B, S] int -> final-norm output [B*S, d_model] (gpt.py:124-142)."""
     b, s = tokens.shape
     if s > cfg.seq_len:
         raise ValueError(f"sequence {s} longer than cfg.seq_len={cfg.seq_len}")
@@ -187,14 +190,27 @@ def forward(params, tokens, cfg: GPTConfig):
     for layer in params["layers"]:
         h, pending, _, _ = block(layer, h, pending, cfg)
     _, y = _norm(pending, params["ln_f"], h, cfg)
-    logits = _lm_head(y.reshape(-1, cfg.d_model), params["tok_emb"], cfg)
+    return y.reshape(-1, cfg.d_model)
+
+
+def forward(params, tokens, cfg: GPTConfig):
+    """tokens [B, S] int -> logits [B, S, vocab] f32 (gpt.py:124-144)."""
+    b, s = tokens.shape
+    logits = _lm_head(hidden(params, tokens, cfg), params["tok_emb"], cfg)
     return logits.reshape(b, s, cfg.vocab_size)
 
 
 def loss_fn(params, tokens, targets, cfg: GPTConfig):
-    """Mean next-token cross-entropy in f32 (gpt.py:147-152)."""
-    logits = forward(params, tokens, cfg)
-    return F.cross_entropy(logits.reshape(-1, cfg.vocab_size), targets.reshape(-1))
+    """Mean next-token cross-entropy in f32 (gpt.py:147-152).
+
+    On the ``pallas`` linear slot the tied LM head and the loss run as one
+    autograd node on the native kernels (f32 logits, ``log_softmax`` / gather
+    in two row passes, bf16 ``dlogits`` straight into the head's GEMMs)."""
+    y = hidden(params, tokens, cfg)
+    if cfg.linear == "pallas":
+        return tied_head_cross_entropy(y, params["tok_emb"].to(cfg.dtype), targets.reshape(-1))
+    logits = _lm_head(y, params["tok_emb"], cfg)
+    return F.cross_entropy(logits, targets.reshape(-1))
 
 
 def flops_per_token(cfg: GPTConfig, n_params_nonembed: int) -> dict:

@@ -128,6 +128,25 @@ FERRITE_API int ferrite_gemm(void* stream, const void* a, const void* b, void* c
                  int64_t ldc, int trans_a, int trans_b, int ab_dtype,
                  int c_dtype);
 
+/* Bytes of f32 scratch ferrite_gemm_ws can use for a split-K launch of this
+ * shape on the current device (0: the shape gets no split).  Splitting K helps
+ * when the output has fewer tiles than the GPU has SMs -- the weight gradients
+ * dW = X^T G of the reference's VJP (matmul.py:99-104) at transformer shapes
+ * (M x N = d_model x d_ff, K = tokens). */
+FERRITE_API size_t ferrite_gemm_workspace_size(int64_t m, int64_t n, int64_t k,
+                                   int64_t lda, int64_t ldb, int trans_a,
+                                   int trans_b, int ab_dtype);
+
+/* ferrite_gemm with caller-provided scratch (256-byte aligned): with at least
+ * ferrite_gemm_workspace_size() bytes the K range of each output tile is split
+ * over several SMs, the f32 partials are summed in a fixed order (results are
+ * run-to-run deterministic) and rounded once; with less, it behaves exactly
+ * like ferrite_gemm.  Replaces the same reference kernel as ferrite_gemm. */
+FERRITE_API int ferrite_gemm_ws(void* stream, const void* a, const void* b, void* c,
+                    int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
+                    int64_t ldc, int trans_a, int trans_b, int ab_dtype,
+                    int c_dtype, void* workspace, size_t workspace_bytes);
+
 /* ---- causal flash attention ------------------------------------------------ */
 
 /* Shapes: q [b, h, sq, d], k/v [b, h, sk, d], all of dtype `dtype`, densely
@@ -169,6 +188,28 @@ FERRITE_API int ferrite_attn_bwd_dq(void* stream, const void* q, const void* k,
                         const float* delta, void* dq, int64_t b, int64_t h,
                         int64_t sq, int64_t sk, int64_t d, float scale,
                         int causal, int block_q, int block_k, int dtype);
+
+/* ---- softmax cross-entropy (the GPT loss) --------------------------------- */
+
+/* lse[r] = log sum_c exp(logits[r, c]) and nll[r] = lse[r] - logits[r, t[r]] over
+ * f32 logits [rows, vocab] (row stride ld elements); targets int32
+ * (target_dtype 0) or int64 (1).  A target outside [0, vocab) gives nll = NaN.
+ * Replaces the loss of the reference's training step: jax.nn.log_softmax and
+ * the target gather in loss_fn, model/gpt.py:147-152 (the mean of nll is left
+ * to the caller).  No reference kernel counterpart: the reference runs this in
+ * XLA. */
+FERRITE_API int ferrite_xent_fwd(void* stream, const float* logits, const void* targets,
+                     float* lse, float* nll, int64_t rows, int64_t vocab, int64_t ld,
+                     int target_dtype);
+
+/* dlogits[r, c] = g * (exp(logits[r, c] - lse[r]) - [c == t[r]]) with
+ * g = (*dloss) * scale (dloss a device scalar, NULL meaning 1; scale = 1/rows
+ * for a mean), written as out_dtype (FERRITE_BF16 for the LM-head GEMMs) with
+ * row stride ld_out.  The backward of loss_fn (gpt.py:147-152) in one pass. */
+FERRITE_API int ferrite_xent_bwd(void* stream, const float* logits, const void* targets,
+                     const float* lse, const float* dloss, float scale, void* dlogits,
+                     int64_t rows, int64_t vocab, int64_t ld, int64_t ld_out,
+                     int target_dtype, int out_dtype);
 
 /* ---- strided flash attention ----------------------------------------------- */
 

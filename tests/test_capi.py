@@ -126,6 +126,9 @@ def test_last_error_is_thread_local():
 
 def test_workspace_query_is_bounded():
     lib = nat.lib()
+    # f32 operands never split (exact CUDA-core path); answered without a device
+    assert lib.ferrite_gemm_workspace_size(1024, 1024, 65536, 1024, 1024, 1, 0, nat.F32) == 0
+    assert lib.ferrite_gemm_workspace_size(0, 1024, 65536, 1024, 1024, 1, 0, nat.BF16) == 0
     ws = lib.ferrite_rmsnorm_bwd_workspace_size(8192, 4096)
     assert 0 < ws <= 8192 * 4096 * 4
     assert lib.ferrite_rmsnorm_bwd_workspace_size(1, 128) >= 8 * 128 * 4 or lib.ferrite_rmsnorm_bwd_workspace_size(1, 128) >= 128 * 4

@@ -141,12 +141,26 @@ def test_long_config_forward_sampled_heads():
         np.testing.assert_allclose(to_numpy(lse[bi, hi]), lse_ref[0, 0], atol=2e-4, rtol=1e-5)
 
 
-def test_delta_prep():
+@pytest.mark.parametrize("s,d,dtype", [(256, 64, BF16), (300, 128, BF16), (129, 256, BF16), (256, 64, np.float32), (77, 96, np.float16), (200, 8, BF16)])
+def test_delta_prep(s, d, dtype):
+    """Vectorised kernel (16-byte rows of up to 32 vectors) and the generic one (d = 96)."""
     rng = np.random.default_rng(2)
-    do, o = normal(rng, (2, 3, 256, 64), BF16), normal(rng, (2, 3, 256, 64), BF16)
-    delta = torch.empty(2, 3, 256, device="cuda")
+    do, o = normal(rng, (2, 3, s, d), dtype), normal(rng, (2, 3, s, d), dtype)
+    delta = torch.empty(2, 3, s, device="cuda")
     dot, ot = to_torch(do), to_torch(o)
-    nat.check(nat.lib().ferrite_attn_bwd_prep(nat.stream_ptr(), dot.data_ptr(), ot.data_ptr(), delta.data_ptr(), 2, 3, 256, 64, nat.BF16))
+    nat.check(nat.lib().ferrite_attn_bwd_prep(nat.stream_ptr(), dot.data_ptr(), ot.data_ptr(), delta.data_ptr(), 2, 3, s, d, nat.dtype_code(dot.dtype)))
+    np.testing.assert_allclose(to_numpy(delta), oa.delta(do, o), atol=1e-4, rtol=1e-5)
+
+
+def test_delta_prep_unaligned_takes_the_generic_kernel():
+    rng = np.random.default_rng(6)
+    do, o = normal(rng, (1, 2, 128, 64), BF16), normal(rng, (1, 2, 128, 64), BF16)
+    store = torch.empty(do.size + 1, dtype=torch.bfloat16, device="cuda")
+    dot = store[1:].view(1, 2, 128, 64)
+    dot.copy_(to_torch(do))
+    ot = to_torch(o)
+    delta = torch.empty(1, 2, 128, device="cuda")
+    nat.check(nat.lib().ferrite_attn_bwd_prep(nat.stream_ptr(), dot.data_ptr(), ot.data_ptr(), delta.data_ptr(), 1, 2, 128, 64, nat.BF16))
     np.testing.assert_allclose(to_numpy(delta), oa.delta(do, o), atol=1e-4, rtol=1e-5)
 
 

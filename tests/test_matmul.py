@@ -170,3 +170,63 @@ def test_device_status_clean_after_gemm():
     from ferrite import _native as nat
 
     nat.device_status(clear=True)
+
+
+# ---------------------------------------------------------------- split-K
+
+
+@pytest.mark.parametrize("ta", [False, True])
+@pytest.mark.parametrize("m,n,k", [(256, 256, 8192), (296, 520, 4000), (1024, 1024, 65536), (128, 384, 2048)])
+def test_split_k_matches_fp32_reference(ta, m, n, k):
+    """Few-tile outputs with long K (weight-gradient shapes) take the split-K
+    launch; the sum of the f32 slices is rounded once, like the unsplit kernel."""
+    from ferrite import _native as nat
+
+    g = torch.Generator(device="cuda").manual_seed(m + n + k)
+    a = (torch.randn((k, m) if ta else (m, k), device="cuda", generator=g) / k**0.5).to(torch.bfloat16)
+    b = torch.randn(k, n, device="cuda", generator=g).to(torch.bfloat16)
+    ws = nat.lib().ferrite_gemm_workspace_size(m, n, k, a.stride(0), b.stride(0), int(ta), 0, nat.BF16)
+    assert ws > 0, "shape expected to split"
+    ref = _ref32(a, b, ta=ta)
+    for out_dtype in (torch.bfloat16, torch.float32):
+        c = gemm(a, b, trans_a=ta, out_dtype=out_dtype)
+        if out_dtype == torch.float32:
+            torch.testing.assert_close(c, ref, rtol=1e-4, atol=1e-4)
+        else:
+            _assert_bf16_close(c, ref)
+        assert torch.equal(c, gemm(a, b, trans_a=ta, out_dtype=out_dtype))  # deterministic
+
+
+@pytest.mark.parametrize("splits", [2, 3, 7])
+def test_forced_split_counts_agree_with_unsplit(monkeypatch, splits):
+    """Uneven slices (k blocks not divisible by the split count) and the no-split
+    path agree to f32 summation order."""
+    g = torch.Generator(device="cuda").manual_seed(splits)
+    m, n, k = 512, 768, 64 * 29
+    a = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
+    b = torch.randn(k, n, device="cuda", generator=g).to(torch.bfloat16)
+    monkeypatch.setenv("FERRITE_GEMM_SPLITS", str(splits))
+    c_split = gemm(a, b, out_dtype=torch.float32)
+    monkeypatch.setenv("FERRITE_GEMM_SPLITS", "1")
+    c_one = gemm(a, b, out_dtype=torch.float32)
+    # N(0,1) operands, K = 1856: |c| ~ 43, f32 summation-order noise ~ 1e-4
+    torch.testing.assert_close(c_split, c_one, rtol=1e-5, atol=1e-3)
+    torch.testing.assert_close(c_split, _ref32(a, b), rtol=1e-4, atol=2e-3)
+
+
+def test_no_workspace_entry_point_never_splits():
+    """ferrite_gemm (no scratch) on a split-eligible shape runs the unsplit kernel."""
+    from ferrite import _native as nat
+
+    g = torch.Generator(device="cuda").manual_seed(7)
+    m, n, k = 256, 256, 8192
+    a = (torch.randn(m, k, device="cuda", generator=g) / k**0.5).to(torch.bfloat16)
+    b = torch.randn(k, n, device="cuda", generator=g).to(torch.bfloat16)
+    c = torch.empty(m, n, device="cuda", dtype=torch.float32)
+    nat.check(nat.lib().ferrite_gemm(nat.stream_ptr(), a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k, k, n, n, 0, 0, nat.BF16, nat.F32))
+    torch.testing.assert_close(c, _ref32(a, b), rtol=1e-4, atol=1e-4)
+    # too-small scratch: same as no scratch
+    ws = torch.empty(64, dtype=torch.uint8, device="cuda")
+    c2 = torch.empty_like(c)
+    nat.check(nat.lib().ferrite_gemm_ws(nat.stream_ptr(), a.data_ptr(), b.data_ptr(), c2.data_ptr(), m, n, k, k, n, n, 0, 0, nat.BF16, nat.F32, ws.data_ptr(), 64))
+    assert torch.equal(c, c2)

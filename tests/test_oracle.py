@@ -6,6 +6,7 @@ import os
 
 import numpy as np
 import pytest
+import torch
 
 from helpers import BF16, load_arrays, max_abs, normal, rel_l2
 from oracle import attention as oa
@@ -165,3 +166,23 @@ def test_matmul_golden_fixture_reproduces():
     g = load_arrays(os.path.join(GOLDEN, "matmul_ragged_bf16_77x130x203.npz"))
     assert np.array_equal(om.matmul_reference(g["x"], g["y"]).view(np.uint16), g["out"].view(np.uint16))
     np.testing.assert_array_equal(om.matmul_reference(g["x"], g["y"], out_dtype=np.float32), g["out_f32"])
+
+
+# ---------------------------------------------------------------- cross-entropy oracle
+
+
+def test_xent_oracle_against_torch_log_softmax():
+    """The loss restatement (gpt.py:147-152) against torch's f32 log_softmax/NLL on CPU."""
+    from oracle import xent as ox
+
+    rng = np.random.default_rng(0)
+    x = (3.0 * rng.standard_normal((64, 1000))).astype(np.float32)
+    t = rng.integers(0, 1000, 64)
+    xt = torch.from_numpy(x).requires_grad_(True)
+    ref = torch.nn.functional.cross_entropy(xt, torch.from_numpy(t))
+    ref.backward()
+    assert abs(ox.loss(x, t) - ref.item()) < 1e-5
+    np.testing.assert_allclose(ox.xent_bwd(x, t), xt.grad.numpy(), atol=1e-7, rtol=1e-4)
+    l, nll = ox.xent_fwd(x, t)
+    np.testing.assert_allclose(l, torch.logsumexp(torch.from_numpy(x), -1).numpy(), rtol=1e-6, atol=1e-6)
+    np.testing.assert_allclose(nll, ox.xent_fwd(x, t, acc=np.float64)[1], rtol=1e-5, atol=1e-5)
