@@ -39,6 +39,7 @@ the host cores; under torchrun only rank 0 runs it.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -351,13 +352,20 @@ class AttnWorkload:
         shape = (1, self.bh_local, self.S, self.D)  # this rank's (b, h) slices as one batch row
         self.q, self.k, self.v, self.do = (torch.randn(*shape, generator=g, device=dev).to(torch.bfloat16) for _ in range(4))
         self.fwd_flops_local = attention_flops(1, self.bh_local, self.S, self.S, self.D, causal=True)
-        # tensor-core work each kernel issues, in units of one causal S*S*D/2 product: fwd 2, dkv 4, dq 3
+        # tensor-core work each kernel issues, in units of one causal S*S*D/2 product:
+        # fwd 2 (S, PV), dK/dV 4 (S, dP, dV, dK, and it stores dS), dQ from dS 1
         unit = self.fwd_flops_local / 2
-        self.kernel_work = {"attn_fwd": 2 * unit, "attn_bwd_prep": 0, "attn_bwd_dkv": 4 * unit, "attn_bwd_dq": 3 * unit}
+        self.kernel_work = {"attn_fwd": 2 * unit, "attn_bwd_prep": 0, "attn_bwd_dkv": 4 * unit, "attn_bwd_dq": 1 * unit}
         self.o = torch.empty_like(self.q)
         self.lse = torch.empty(1, self.bh_local, self.S, device=dev)
         self.delta = torch.empty_like(self.lse)
         self.dq, self.dk, self.dv = (torch.empty_like(self.q) for _ in range(3))
+        from ferrite import _native as nat
+
+        # dS^T scratch of all local slices (bf16 [slice][S][S]), filled by the dK/dV kernel
+        ws = nat.lib().ferrite_attn_bwd_ds_workspace_size(1, self.bh_local, self.S, self.S, self.D, nat.BF16)
+        self.ds = torch.empty(ws, dtype=torch.uint8, device=dev)
+        self.strides = nat.attn_strides(q=self.q, k=self.k, v=self.v, o=self.o, dout=self.do, dq=self.dq, dk=self.dk, dv=self.dv)
 
     @property
     def units_per_step(self):
@@ -378,12 +386,12 @@ class AttnWorkload:
         nat.check(lib.ferrite_attn_bwd_prep(s, self.do.data_ptr(), self.o.data_ptr(), self.delta.data_ptr(), 1, bh, S, D, nat.BF16))
         if ev:
             ev[2].record()
-        nat.check(lib.ferrite_attn_bwd_dkv(s, self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(), self.do.data_ptr(), self.lse.data_ptr(), self.delta.data_ptr(),
-                                           self.dk.data_ptr(), self.dv.data_ptr(), 1, bh, S, S, D, sc, 1, 128, 128, nat.BF16))
+        st = ctypes.byref(self.strides)
+        nat.check(lib.ferrite_attn_bwd_dkv_ds(s, self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(), self.do.data_ptr(), self.lse.data_ptr(), self.delta.data_ptr(),
+                                              self.dk.data_ptr(), self.dv.data_ptr(), self.ds.data_ptr(), st, 0, bh, 1, bh, S, S, D, sc, 1, 128, 128, nat.BF16))
         if ev:
             ev[3].record()
-        nat.check(lib.ferrite_attn_bwd_dq(s, self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(), self.do.data_ptr(), self.lse.data_ptr(), self.delta.data_ptr(),
-                                          self.dq.data_ptr(), 1, bh, S, S, D, sc, 1, 128, 128, nat.BF16))
+        nat.check(lib.ferrite_attn_bwd_dq_ds(s, self.ds.data_ptr(), self.k.data_ptr(), self.dq.data_ptr(), st, 0, bh, 1, bh, S, S, D, sc, 1, 128, 128, nat.BF16))
         if ev:
             ev[4].record()
 

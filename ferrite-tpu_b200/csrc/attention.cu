@@ -719,9 +719,14 @@ struct BwdSmem {
   static constexpr int kX1Off = 0;
   static constexpr int kX2Off = kXBytes;
   static constexpr int kYOff = 2 * kXBytes;
-  static constexpr int kBarOff = kYOff + kYStages * kStageBytes;
-  // x_full, y_full[S], y_empty[S], t_full[2], e_full[2], acc_full, x_tmem
-  static constexpr int kNumBars = 2 * kYStages + 7;
+  // dK/dV with a dS output: one 128-key x 64-query bf16 staging tile (32 rows per
+  // elementwise warp, 128-byte swizzle) that the TMA store reads; the two
+  // elementwise groups hand it to each other tile by tile.
+  static constexpr int kStgOff = kYOff + kYStages * kStageBytes;
+  static constexpr int kStgBytes = BX * BY * 2;
+  static constexpr int kBarOff = kStgOff + kStgBytes;
+  // x_full, y_full[S], y_empty[S], t_full[2], e_full[2], acc_full, x_tmem, stg_free
+  static constexpr int kNumBars = 2 * kYStages + 8;
   static constexpr int kTotal = 1024 + kBarOff + kNumBars * 8 + 16;
 };
 
@@ -736,6 +741,10 @@ struct BwdParams {
   void* out1;  // dK/dV: dV
   Bhsd l0, l1;  // layouts of out0, out1
   int n_x_tiles;
+  int bh0;          // first batch*head slice of this launch (grid.y counts from it)
+  void* ds;         // dK/dV only, optional: dS^T [slice][key][ds_ld] in the input dtype
+  int64_t ds_ld;    // elements per key row (sq rounded up to 64)
+  int64_t ds_slice; // elements per slice
 };
 
 template <int D, bool BF16, bool IS_DKV>
@@ -743,7 +752,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tx1, const __grid_constant__ CUtensorMap tx2,
                        const __grid_constant__ CUtensorMap ty1, const __grid_constant__ CUtensorMap ty2,
                        const __grid_constant__ CUtensorMap tlse, const __grid_constant__ CUtensorMap tdelta,
-                       const BwdParams p) {
+                       const __grid_constant__ CUtensorMap tds, const BwdParams p) {
   using L = BwdSmem<D>;
   typedef typename std::conditional<BF16, __nv_bfloat16, __half>::type T;
   extern __shared__ uint8_t smem_raw[];
@@ -757,6 +766,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint64_t* e_full = t_full + 2;
   uint64_t* acc_full = e_full + 2;
   uint64_t* x_tmem = acc_full + 1;  // dQ: Q and dO copied into TMEM
+  uint64_t* stg_free = x_tmem + 1;  // dS staging tile released by the previous tile's warps
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kNumBars);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -764,7 +774,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   // Heaviest tiles first: under a causal mask early key tiles (dK/dV) and late
   // query tiles (dQ) see the most streaming tiles.
   const int xt = IS_DKV ? (int)blockIdx.x : p.n_x_tiles - 1 - (int)blockIdx.x;
-  const int bh = blockIdx.y;
+  const int bh = p.bh0 + (int)blockIdx.y;
   const int hh = bh % p.l0.nh, bb = bh / p.l0.nh;  // TMA coordinates of the slice
   const int x0 = xt * BX;
   const int x_len = IS_DKV ? p.sk : p.sq;  // rows of the stationary operand
@@ -787,6 +797,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(x_full, 1);
     mbar_init(acc_full, 1);
     mbar_init(x_tmem, 4);
+    mbar_init(stg_free, 4);
     for (int i = 0; i < kYStages; ++i) {
       mbar_init(&y_full[i], 1);
       mbar_init(&y_empty[i], 1);
@@ -1033,6 +1044,39 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&e_full[g]);
+      if constexpr (IS_DKV) {
+        // dS^T rows (these 32 keys x the tile's 64 queries) for the dQ-from-dS
+        // kernel, off the MMA's critical path: the accumulation MMAs of this
+        // tile are already released.  Staged in shared memory (swizzled rows,
+        // conflict-free) and written by one TMA store per warp.
+        if (p.ds != nullptr) {
+          if (i > 0 && !mbar_wait(stg_free, (i - 1) & 1, abort, 31)) {
+            ok = false;
+            break;
+          }
+          uint8_t* stg = smem + L::kStgOff + qw * 4096;
+          uint8_t* row = stg + lane * 128;
+#pragma unroll
+          for (int v = 0; v < BY / 8; ++v)
+            *reinterpret_cast<uint4*>(row + ((v ^ (lane & 7)) << 4)) =
+                make_uint4(dd[4 * v], dd[4 * v + 1], dd[4 * v + 2], dd[4 * v + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            // dS^T is stored in 64-key x 64-query blocks (8 KiB contiguous):
+            // coordinates (query in block, key in block, query block, key block)
+            const int key = x0 + qw * 32;
+            tma_store_4d(&tds, stg, 0, key & 63, y0 >> 6, (int)blockIdx.y * (p.sk >> 6) + (key >> 6));
+            bulk_commit_group();
+            bulk_wait_group_read0();  // staging read: hand it to the other group
+            mbar_arrive(stg_free);
+          }
+          __syncwarp();
+        }
+      }
+    }
+    if constexpr (IS_DKV) {
+      if (p.ds != nullptr && lane == 0) bulk_wait_group0();  // dS writes complete before exit
     }
     // epilogue: dK/dV -> group 0 stores dK, group 1 stores dV; dQ -> column halves
     if (ok && n_y > 0 && mbar_wait(acc_full, 0, abort, 28)) {
@@ -1075,6 +1119,202 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
+  }
+}
+
+// ===========================================================================
+// dQ from a materialised dS (tensor cores)
+// ===========================================================================
+//
+// dQ[q, :] = scale * sum_{k <= q} dS[q, k] K[k, :]: with the dK/dV kernel
+// writing its bf16 dS^T tiles ([key][query] per slice, the exact values the
+// reference rounds before its dQ product, flash_attention.py:234), dQ is a
+// batched GEMM  dQ_slice = (dS^T)^T K  -- one tensor-core product per tile
+// instead of recomputing S, P, dP and dS (three), and no atomics.  Per work unit
+// (128-query tile, slice) the K range stops at the causal diagonal.
+//   warp 0      TMA: dS^T boxes {64 queries, 64 keys} (MN-major A) and K boxes
+//               {64 d, 64 keys} (MN-major B) into a DQ_STAGES-slot ring;
+//   warp 1      TMEM (two D-column accumulators) + one MMA lane, M=128 N=D K=16;
+//   warps 2-5   epilogue: tcgen05.ld, x scale, round, 16-byte stores through the
+//               dQ layout.
+// Persistent: grid = min(units, SMs); slice by slice, heaviest query tile first.
+// The host launches it only where every query row sees at least one key (causal
+// implies sq == sk on this path), so every unit has K blocks.
+
+constexpr int kDqThreads = 192;
+
+template <int D>
+struct DqSmem {
+  static constexpr int kABytes = 128 * 64 * 2;  // dS^T: 2 boxes of 64 queries x 64 keys
+  static constexpr int kBBytes = 64 * D * 2;    // K: D/64 boxes of 64 d x 64 keys
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = D == 64 ? 8 : 6;
+  static constexpr int kBarOff = kStages * kStageBytes;
+  static constexpr int kNumBars = 2 * kStages + 4;
+  static constexpr int kTotal = 1024 + kBarOff + kNumBars * 8 + 16;
+};
+
+struct DqParams {
+  int sq, sk, causal, nh;
+  float scale;
+  int n_q_tiles, n_slices, bh0;
+  void* dq;
+  Bhsd ldq;
+};
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kDqThreads, 1)
+    attn_dq_ds_kernel(const __grid_constant__ CUtensorMap tds, const __grid_constant__ CUtensorMap tk,
+                      const DqParams p) {
+  using L = DqSmem<D>;
+  constexpr int STAGES = L::kStages;
+  typedef typename std::conditional<BF16, __nv_bfloat16, __half>::type T;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int units = p.n_q_tiles * p.n_slices;
+  const int diag_shift = p.sk - p.sq;
+  const int nkb_all = p.sk / 64;  // key blocks per slice in the dS layout
+  // unit u: slice u / n_q_tiles, query tile n_q_tiles - 1 - u % n_q_tiles (heaviest
+  // first within a slice).  CTAs running at the same time work on the same few
+  // slices, so each slice's K tiles are read from HBM once and then hit in L2.
+  auto unit_tile = [&](int u, int& qt, int& sl, int& nkb) {
+    sl = u / p.n_q_tiles;
+    qt = p.n_q_tiles - 1 - (u - sl * p.n_q_tiles);
+    int last_key = p.sk - 1;
+    if (p.causal) last_key = min(last_key, qt * 128 + 127 + diag_shift);
+    nkb = last_key < 0 ? 0 : last_key / 64 + 1;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);
+    }
+    *abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 2 * D);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tds);
+      tma_prefetch_desc(&tk);
+      int it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        int qt, sl, nkb;
+        unit_tile(u, qt, sl, nkb);
+        const int bh = p.bh0 + sl;
+        const int hh = bh % p.nh, bb = bh / p.nh;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int st = it % STAGES;
+          if (!mbar_wait(&empty[st], ((it / STAGES) & 1) ^ 1, abort, 40)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + st * L::kStageBytes;
+          uint8_t* sb = sa + L::kABytes;
+          mbar_arrive_expect_tx(&full[st], L::kStageBytes);
+          // two consecutive 64-query blocks of key block kb: 16 KiB contiguous
+          tma_load_4d(sa, &tds, &full[st], 0, 0, qt * 2, sl * nkb_all + kb);
+#pragma unroll
+          for (int c = 0; c < D / 64; ++c) tma_load_4d(sb + c * 8192, &tk, &full[st], c * 64, kb * 64, hh, bb);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_f16(128, D, BF16, true, true);
+      const uint32_t s0 = smem_u32(smem);
+      const uint64_t da_base = make_sdesc(s0, 8192, 1024);
+      const uint64_t db_base = make_sdesc(s0 + L::kABytes, 8192, 1024);
+      int it = 0, local = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++local) {
+        int qt, sl, nkb;
+        unit_tile(u, qt, sl, nkb);
+        const int buf = local & 1;
+        if (!mbar_wait(&acc_empty[buf], ((local >> 1) & 1) ^ 1, abort, 41)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + buf * D;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int st = it % STAGES;
+          if (!mbar_wait(&full[st], (it / STAGES) & 1, abort, 42)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = sdesc_at(da_base, st * L::kStageBytes);
+          const uint64_t db = sdesc_at(db_base, st * L::kStageBytes);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            tc_mma_f16_ss(d_tmem, sdesc_at(da, kk * 2048), sdesc_at(db, kk * 2048), idesc,
+                          (kb | kk) != 0 ? 1u : 0u);
+          tc_commit(&empty[st]);
+        }
+        tc_commit(&acc_full[buf]);
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    int local = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
+      int qt, sl, nkb;
+      unit_tile(u, qt, sl, nkb);
+      const int buf = local & 1;
+      if (!mbar_wait(&acc_full[buf], (local >> 1) & 1, abort, 43)) break;
+      tc_fence_after();
+      const int qrow = qt * 128 + r;
+      const uint32_t src = tmem + ((uint32_t)(q * 32) << 16) + buf * D;
+      T* out = reinterpret_cast<T*>(p.dq) + p.ldq.row(p.bh0 + sl, qrow);
+#pragma unroll 1
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(src + c0, v);
+        tmem_wait_ld();
+        if (qrow < p.sq) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 8) {
+            const float* f = reinterpret_cast<const float*>(&v[e]);
+            const float m = p.scale;
+            uint4 w;
+            w.x = BF16 ? pack_bf16x2(f[0] * m, f[1] * m) : pack_f16x2(f[0] * m, f[1] * m);
+            w.y = BF16 ? pack_bf16x2(f[2] * m, f[3] * m) : pack_f16x2(f[2] * m, f[3] * m);
+            w.z = BF16 ? pack_bf16x2(f[4] * m, f[5] * m) : pack_f16x2(f[4] * m, f[5] * m);
+            w.w = BF16 ? pack_bf16x2(f[6] * m, f[7] * m) : pack_f16x2(f[6] * m, f[7] * m);
+            *reinterpret_cast<uint4*>(out + c0 + e) = w;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 2 * D);
   }
 }
 
@@ -1172,7 +1412,28 @@ struct BwdArgs {
   const float *lse, *delta;
   void *out0, *out1;  // dK, dV (dK/dV kernel) or dQ (dQ kernel)
   Bhsd lq, lk, lv, ldo, l0, l1;
+  int64_t bh0 = 0, nbh = -1;  // slice range of the launch (nbh < 0: all)
+  void* ds = nullptr;         // dK/dV: optional dS^T output for the slice range
+  int64_t ds_ld = 0;
 };
+
+// dS^T workspace geometry: [slice][sk][ds_ld] in the input dtype, rows padded to
+// whole 64-query tiles.
+static int64_t ds_row_elems(int64_t sq) { return (sq + 63) / 64 * 64; }
+static int64_t ds_slice_bytes(int64_t sq, int64_t sk) { return ds_row_elems(sq) * sk * 2; }
+
+// dS^T workspace as 64-key x 64-query blocks: block (key block kb, query block
+// qb) of slice sl starts at ((sl * sk/64 + kb) * nqb + qb) * 4096 elements, rows
+// of 64 queries inside.  4-D tensor map (query, key, query block, slice*key
+// block); boxes of `key_rows` keys x `qblocks` query blocks.
+static int map_ds_blocks(CUtensorMap* m, const void* ds, CUtensorMapDataType dt, int64_t sq,
+                         int64_t sk, int64_t nbh, uint32_t key_rows, uint32_t qblocks) {
+  const int64_t nqb = ds_row_elems(sq) / 64;
+  const uint64_t dims[4] = {64, 64, (uint64_t)nqb, (uint64_t)(nbh * (sk / 64))};
+  const uint64_t strides[3] = {128, 8192, (uint64_t)nqb * 8192};
+  const uint32_t box[4] = {64, key_rows, qblocks, 1};
+  return make_tmap_4d(m, ds, dt, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
 
 template <int D, bool BF16, bool IS_DKV>
 static int launch_bwd_tc(cudaStream_t s, const BwdArgs& a, int64_t b, int64_t h, int64_t sq,
@@ -1205,11 +1466,23 @@ static int launch_bwd_tc(cudaStream_t s, const BwdArgs& a, int64_t b, int64_t h,
   p.l0 = a.l0;
   p.l1 = a.l1;
   p.n_x_tiles = (int)((xs + BX - 1) / BX);
+  p.bh0 = (int)a.bh0;
+  const int64_t nbh = a.nbh < 0 ? bh - a.bh0 : a.nbh;
+  p.ds = IS_DKV ? a.ds : nullptr;
+  p.ds_ld = a.ds_ld;
+  p.ds_slice = a.ds_ld * sk;
   auto kern = attn_bwd_tc_kernel<D, BF16, IS_DKV>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
   if (e != cudaSuccess) return fail(FERRITE_LAUNCH_FAILED, "attn_bwd: smem attr: %s", cudaGetErrorString(e));
-  dim3 grid(p.n_x_tiles, (unsigned)bh);
-  kern<<<grid, kBwdThreads, L::kTotal, s>>>(tx1, tx2, ty1, ty2, tl, td, p);
+  if (nbh <= 0) return FERRITE_OK;
+  // dS^T store map over the launch's slices: boxes of 64 queries x 32 keys
+  CUtensorMap tds = tl;  // placeholder when no dS is written (never dereferenced)
+  if (p.ds) {
+    rc = map_ds_blocks(&tds, p.ds, dt, sq, sk, nbh, 32, 1);
+    if (rc) return rc;
+  }
+  dim3 grid(p.n_x_tiles, (unsigned)nbh);
+  kern<<<grid, kBwdThreads, L::kTotal, s>>>(tx1, tx2, ty1, ty2, tl, td, tds, p);
   return check_launch(IS_DKV ? "attn_bwd_dkv_tc" : "attn_bwd_dq_tc");
 }
 
@@ -1222,6 +1495,47 @@ static int dispatch_bwd_tc(cudaStream_t s, const BwdArgs& a, int64_t b, int64_t 
               : launch_bwd_tc<64, false, IS_DKV>(s, a, b, h, sq, sk, scale, causal);
   return bf ? launch_bwd_tc<128, true, IS_DKV>(s, a, b, h, sq, sk, scale, causal)
             : launch_bwd_tc<128, false, IS_DKV>(s, a, b, h, sq, sk, scale, causal);
+}
+
+template <int D, bool BF16>
+static int launch_dq_ds(cudaStream_t s, const BwdArgs& a, int64_t b, int64_t h, int64_t sq,
+                        int64_t sk, float scale, int causal) {
+  using L = DqSmem<D>;
+  const CUtensorMapDataType dt = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const int64_t nbh = a.nbh < 0 ? b * h - a.bh0 : a.nbh;
+  if (nbh <= 0) return FERRITE_OK;
+  CUtensorMap tds, tk;
+  int rc = map_ds_blocks(&tds, a.ds, dt, sq, sk, nbh, 64, 2);
+  if (!rc) rc = map_bhsd(&tk, a.k, dt, D, a.lk, b, h, sk, 64);
+  if (rc) return rc;
+  DqParams p;
+  p.sq = (int)sq;
+  p.sk = (int)sk;
+  p.causal = causal;
+  p.nh = (int)h;
+  p.scale = scale;
+  p.n_q_tiles = (int)((sq + 127) / 128);
+  p.n_slices = (int)nbh;
+  p.bh0 = (int)a.bh0;
+  p.dq = a.out0;
+  p.ldq = a.l0;
+  auto kern = attn_dq_ds_kernel<D, BF16>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+  if (e != cudaSuccess) return fail(FERRITE_LAUNCH_FAILED, "attn_dq_ds: smem attr: %s", cudaGetErrorString(e));
+  const int64_t units = (int64_t)p.n_q_tiles * nbh;
+  const int grid = (int)std::min<int64_t>(units, num_sms(current_device()));
+  kern<<<grid, kDqThreads, L::kTotal, s>>>(tds, tk, p);
+  return check_launch("attn_dq_ds");
+}
+
+static int dispatch_dq_ds(cudaStream_t s, const BwdArgs& a, int64_t b, int64_t h, int64_t sq,
+                          int64_t sk, int64_t d, float scale, int causal, int dtype) {
+  const bool bf = dtype == FERRITE_BF16;
+  if (d == 64)
+    return bf ? launch_dq_ds<64, true>(s, a, b, h, sq, sk, scale, causal)
+              : launch_dq_ds<64, false>(s, a, b, h, sq, sk, scale, causal);
+  return bf ? launch_dq_ds<128, true>(s, a, b, h, sq, sk, scale, causal)
+            : launch_dq_ds<128, false>(s, a, b, h, sq, sk, scale, causal);
 }
 
 static Bhsd contiguous_bhsd(int64_t h, int64_t s, int64_t d) {
@@ -1472,6 +1786,96 @@ int ferrite_attn_bwd_dq(void* stream, const void* q, const void* k, const void* 
   const ferrite_attn_strides st = contiguous_strides(h, sq, sk, d);
   return ferrite_attn_bwd_dq_strided(stream, q, k, v, dout, lse, delta, dq, &st, b, h, sq, sk, d,
                                      scale, causal, block_q, block_k, dtype);
+}
+
+int ferrite_attn_bwd_dkv_ds(void* stream, const void* q, const void* k, const void* v,
+                            const void* dout, const float* lse, const float* delta, void* dk,
+                            void* dv, void* ds, const ferrite_attn_strides* st, int64_t bh_begin,
+                            int64_t bh_count, int64_t b, int64_t h, int64_t sq, int64_t sk,
+                            int64_t d, float scale, int causal, int block_q, int block_k,
+                            int dtype) {
+  if (int rc = validate("attn_bwd_dkv_ds", b, h, sq, sk, d, causal, block_q, block_k, dtype)) return rc;
+  if (!q || !k || !v || !dout || !lse || !delta || !dk || !dv || !ds)
+    return fail(FERRITE_BAD_SHAPE, "attn_bwd_dkv_ds: null pointer");
+  if (int rc = strides_ok("attn_bwd_dkv_ds", st)) return rc;
+  if (bh_begin < 0 || bh_count < 0 || bh_begin + bh_count > b * h)
+    return fail(FERRITE_BAD_SHAPE, "attn_bwd_dkv_ds: slice range [%lld, +%lld) outside b*h",
+                (long long)bh_begin, (long long)bh_count);
+  BwdArgs a = bwd_args(q, k, v, dout, lse, delta, dk, dv, *st, h, true);
+  if (!tc_bwd_ok(a, b, h, sq, sk, d, dtype, true) || (reinterpret_cast<uintptr_t>(ds) & 255u))
+    return fail(FERRITE_UNSUPPORTED_DTYPE,
+                "attn_bwd_dkv_ds: needs the tensor-core path (bf16/f16, d 64/128, sk %% 128 == 0, "
+                "16-byte aligned operands, 256-byte aligned dS)");
+  a.bh0 = bh_begin;
+  a.nbh = bh_count;
+  a.ds = ds;
+  a.ds_ld = ds_row_elems(sq);
+  return dispatch_bwd_tc<true>((cudaStream_t)stream, a, b, h, sq, sk, d, scale, causal, dtype);
+}
+
+int ferrite_attn_bwd_dq_ds(void* stream, const void* ds, const void* k, void* dq,
+                           const ferrite_attn_strides* st, int64_t bh_begin, int64_t bh_count,
+                           int64_t b, int64_t h, int64_t sq, int64_t sk, int64_t d, float scale,
+                           int causal, int block_q, int block_k, int dtype) {
+  if (int rc = validate("attn_bwd_dq_ds", b, h, sq, sk, d, causal, block_q, block_k, dtype)) return rc;
+  if (!ds || !k || !dq) return fail(FERRITE_BAD_SHAPE, "attn_bwd_dq_ds: null pointer");
+  if (int rc = strides_ok("attn_bwd_dq_ds", st)) return rc;
+  if (bh_begin < 0 || bh_count < 0 || bh_begin + bh_count > b * h)
+    return fail(FERRITE_BAD_SHAPE, "attn_bwd_dq_ds: slice range [%lld, +%lld) outside b*h",
+                (long long)bh_begin, (long long)bh_count);
+  BwdArgs a = bwd_args(nullptr, k, nullptr, nullptr, nullptr, nullptr, dq, nullptr, *st, h, false);
+  if (!tc_fwd_ok(d, sk, dtype) || !tc_layout_ok(k, a.lk, b, h, sk) ||
+      !tc_layout_ok(dq, a.l0, b, h, sq) || (reinterpret_cast<uintptr_t>(ds) & 255u))
+    return fail(FERRITE_UNSUPPORTED_DTYPE,
+                "attn_bwd_dq_ds: needs the tensor-core path (bf16/f16, d 64/128, sk %% 128 == 0, "
+                "16-byte aligned operands, 256-byte aligned dS)");
+  a.bh0 = bh_begin;
+  a.nbh = bh_count;
+  a.ds = const_cast<void*>(ds);
+  a.ds_ld = ds_row_elems(sq);
+  return dispatch_dq_ds((cudaStream_t)stream, a, b, h, sq, sk, d, scale, causal, dtype);
+}
+
+size_t ferrite_attn_bwd_ds_workspace_size(int64_t b, int64_t h, int64_t sq, int64_t sk,
+                                          int64_t d, int dtype) {
+  if (b <= 0 || h <= 0 || sq <= 0 || sk <= 0 || !tc_fwd_ok(d, sk, dtype)) return 0;
+  return (size_t)(b * h) * (size_t)ds_slice_bytes(sq, sk);
+}
+
+int ferrite_attn_bwd_ds(void* stream, const void* q, const void* k, const void* v,
+                        const void* dout, const float* lse, const float* delta, void* dq,
+                        void* dk, void* dv, const ferrite_attn_strides* st, void* workspace,
+                        size_t workspace_bytes, int64_t b, int64_t h, int64_t sq, int64_t sk,
+                        int64_t d, float scale, int causal, int block_q, int block_k,
+                        int dtype) {
+  if (int rc = validate("attn_bwd_ds", b, h, sq, sk, d, causal, block_q, block_k, dtype)) return rc;
+  if (!q || !k || !v || !dout || !lse || !delta || !dq || !dk || !dv)
+    return fail(FERRITE_BAD_SHAPE, "attn_bwd_ds: null pointer");
+  if (int rc = strides_ok("attn_bwd_ds", st)) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  BwdArgs kv = bwd_args(q, k, v, dout, lse, delta, dk, dv, *st, h, true);
+  BwdArgs qa = bwd_args(q, k, v, dout, lse, delta, dq, nullptr, *st, h, false);
+  const int64_t slice = ds_slice_bytes(sq, sk);
+  const int64_t per = workspace ? (int64_t)(workspace_bytes / (size_t)slice) : 0;
+  const bool use_ds = per >= 1 && (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0 &&
+                      env_int("FERRITE_ATTN_BWD_DS", 1) != 0 &&
+                      tc_bwd_ok(kv, b, h, sq, sk, d, dtype, true) &&
+                      tc_bwd_ok(qa, b, h, sq, sk, d, dtype, false);
+  if (!use_ds) {  // recompute path: dK/dV and dQ kernels over all slices
+    if (int rc = attn_bwd_dkv_impl(s, kv, b, h, sq, sk, d, scale, causal, dtype)) return rc;
+    return attn_bwd_dq_impl(s, qa, b, h, sq, sk, d, scale, causal, dtype);
+  }
+  const int64_t bh = b * h;
+  for (int64_t bh0 = 0; bh0 < bh; bh0 += per) {
+    const int64_t n = std::min<int64_t>(per, bh - bh0);
+    kv.bh0 = qa.bh0 = bh0;
+    kv.nbh = qa.nbh = n;
+    kv.ds = qa.ds = workspace;
+    kv.ds_ld = qa.ds_ld = ds_row_elems(sq);
+    if (int rc = dispatch_bwd_tc<true>(s, kv, b, h, sq, sk, d, scale, causal, dtype)) return rc;
+    if (int rc = dispatch_dq_ds(s, qa, b, h, sq, sk, d, scale, causal, dtype)) return rc;
+  }
+  return FERRITE_OK;
 }
 
 }  // extern "C"

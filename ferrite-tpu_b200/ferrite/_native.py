@@ -90,6 +90,10 @@ SIGNATURES: dict[str, tuple] = {
     "ferrite_attn_bwd_dq": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _i32, _i32, _i32]),
     "ferrite_xent_fwd": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32]),
     "ferrite_xent_bwd": (_i32, [_vp, _vp, _vp, _vp, _vp, _f32, _vp, _i64, _i64, _i64, _i64, _i32, _i32]),
+    "ferrite_attn_bwd_ds_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i64, _i32]),
+    "ferrite_attn_bwd_ds": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sp, _vp, _sz, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _i32, _i32, _i32]),
+    "ferrite_attn_bwd_dkv_ds": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _i32, _i32, _i32]),
+    "ferrite_attn_bwd_dq_ds": (_i32, [_vp, _vp, _vp, _vp, _sp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _i32, _i32, _i32]),
     "ferrite_attn_fwd_strided": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _sp, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _i32, _i32, _i32]),
     "ferrite_attn_bwd_prep_strided": (_i32, [_vp, _vp, _vp, _vp, _sp, _i64, _i64, _i64, _i64, _i32]),
     "ferrite_attn_bwd_dkv_strided": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sp, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _i32, _i32, _i32]),

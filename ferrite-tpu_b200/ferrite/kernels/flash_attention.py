@@ -13,9 +13,12 @@ Drop-in for the reference's ``ferrite.kernels.flash_attention``
   before the backward products (:210-211, :234), and the scale is applied to
   dK / dQ at the end (:220, :243);
 * backward = FlashAttention-2 recompute from ``lse`` and
-  ``delta = rowsum(dO * O)`` (:326-330) in two kernels without atomics: dK/dV with
-  one CTA per key tile sweeping query tiles, dQ with one CTA per query tile
-  sweeping key tiles.
+  ``delta = rowsum(dO * O)`` (:326-330) without atomics: dK/dV with one CTA per
+  key tile sweeping query tiles, which also writes the bf16 ``dS`` it forms to a
+  scratch buffer, then dQ = scale * dS K as one tensor-core GEMM per (batch,
+  head) slice -- the reference's dQ kernel recomputes S, P, dP and dS instead
+  (:224-243); both give the same rounded ``dS`` operand.  Without scratch (or on
+  the CUDA-core path) the recompute dQ kernel runs.
 
 The reference's ``jax.custom_vjp`` (:315-333) becomes a ``torch.autograd.Function``
 whose residuals are ``(q, k, v, out, lse)``; ``lse`` and ``delta`` are compact f32
@@ -30,6 +33,7 @@ from __future__ import annotations
 import ctypes
 import dataclasses
 import math
+import os
 
 import numpy as np
 import torch
@@ -122,19 +126,30 @@ def _backward(q, k, v, out, lse, do, causal: bool, scale: float, bs: BlockSizes,
     st = ctypes.byref(nat.attn_strides(q=q, k=k, v=v, o=out, dout=do, dq=dq, dk=dk, dv=dv))
     delta = torch.empty((b, h, sq), dtype=torch.float32, device=q.device)
     nat.check(lib.ferrite_attn_bwd_prep_strided(s, do.data_ptr(), out.data_ptr(), delta.data_ptr(), st, b, h, sq, d, code))
+    ws = _ds_workspace(lib, b, h, sq, sk, d, code, q.device)
     nat.check(
-        lib.ferrite_attn_bwd_dkv_strided(
+        lib.ferrite_attn_bwd_ds(
             s, q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), lse.data_ptr(), delta.data_ptr(),
-            dk.data_ptr(), dv.data_ptr(), st, b, h, sq, sk, d, scale, int(causal), bs.block_q_bwd, bs.block_k_bwd, code,
-        )
-    )
-    nat.check(
-        lib.ferrite_attn_bwd_dq_strided(
-            s, q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), lse.data_ptr(), delta.data_ptr(),
-            dq.data_ptr(), st, b, h, sq, sk, d, scale, int(causal), bs.block_q_bwd, bs.block_k_bwd, code,
+            dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), st, None if ws is None else ws.data_ptr(),
+            0 if ws is None else ws.numel(), b, h, sq, sk, d, scale, int(causal), bs.block_q_bwd, bs.block_k_bwd, code,
         )
     )
     return dq, dk, dv
+
+
+# Upper bound on the dS scratch of one backward call; slices beyond it are
+# processed in chunks (the kernels loop over them).
+DS_WORKSPACE_BUDGET = int(os.environ.get("FERRITE_ATTN_DS_BUDGET_MB", "4096")) << 20
+
+
+def _ds_workspace(lib, b, h, sq, sk, d, code, device):
+    """Scratch for the materialised-dS backward (None: the recompute path runs)."""
+    full = lib.ferrite_attn_bwd_ds_workspace_size(b, h, sq, sk, d, code)
+    if not full:
+        return None
+    per_slice = full // (b * h)
+    size = max(per_slice, min(full, DS_WORKSPACE_BUDGET // per_slice * per_slice))
+    return torch.empty(size, dtype=torch.uint8, device=device)
 
 
 class _Flash(torch.autograd.Function):

@@ -252,6 +252,51 @@ FERRITE_API int ferrite_attn_bwd_dq_strided(void* stream, const void* q, const v
                                 int64_t sq, int64_t sk, int64_t d, float scale, int causal,
                                 int block_q, int block_k, int dtype);
 
+/* ---- attention backward with a materialised dS ------------------------------ */
+
+/* Bytes of scratch that lets ferrite_attn_bwd_ds process all b*h slices in one
+ * pass: the bf16/f16 dS^T of every slice, [sk][sq rounded up to 64] (0 when the
+ * shape cannot take the tensor-core path). */
+FERRITE_API size_t ferrite_attn_bwd_ds_workspace_size(int64_t b, int64_t h, int64_t sq,
+                                          int64_t sk, int64_t d, int dtype);
+
+/* The whole attention backward after delta prep: dK, dV and dQ.  The dK/dV
+ * kernel also writes the dS it forms (rounded to the input dtype, the values the
+ * reference feeds its dQ product, flash_attention.py:234) into the workspace, and
+ * dQ = scale * dS K is then one tensor-core GEMM per slice instead of a second
+ * recomputation of S, P, dP and dS (flash_attention.py:224-243) -- still without
+ * atomics.  Slices are processed in chunks of as many as fit in workspace_bytes
+ * (256-byte aligned); with less than one slice, or layouts/dtypes the tensor
+ * cores cannot read, it runs ferrite_attn_bwd_dkv_strided +
+ * ferrite_attn_bwd_dq_strided.  Replaces the pair of backward pallas_calls of
+ * _flash_bwd, flash_attention.py:253-306. */
+FERRITE_API int ferrite_attn_bwd_ds(void* stream, const void* q, const void* k, const void* v,
+                        const void* dout, const float* lse, const float* delta, void* dq,
+                        void* dk, void* dv, const ferrite_attn_strides* strides,
+                        void* workspace, size_t workspace_bytes, int64_t b, int64_t h,
+                        int64_t sq, int64_t sk, int64_t d, float scale, int causal,
+                        int block_q, int block_k, int dtype);
+
+/* The two halves of ferrite_attn_bwd_ds, for callers that schedule them (or
+ * time them) separately, on the slice range [bh_begin, bh_begin + bh_count) of
+ * the flattened batch*head index.  ds is [bh_count][sk][sq rounded up to 64]
+ * (256-byte aligned); both need the tensor-core path and return
+ * FERRITE_UNSUPPORTED_DTYPE otherwise.  dkv_ds: dK, dV as ferrite_attn_bwd_dkv
+ * (flash_attention.py:197-221) plus dS^T; dq_ds: dQ = scale * dS K
+ * (replaces flash_attention.py:224-243). */
+FERRITE_API int ferrite_attn_bwd_dkv_ds(void* stream, const void* q, const void* k,
+                            const void* v, const void* dout, const float* lse,
+                            const float* delta, void* dk, void* dv, void* ds,
+                            const ferrite_attn_strides* strides, int64_t bh_begin,
+                            int64_t bh_count, int64_t b, int64_t h, int64_t sq,
+                            int64_t sk, int64_t d, float scale, int causal,
+                            int block_q, int block_k, int dtype);
+FERRITE_API int ferrite_attn_bwd_dq_ds(void* stream, const void* ds, const void* k, void* dq,
+                           const ferrite_attn_strides* strides, int64_t bh_begin,
+                           int64_t bh_count, int64_t b, int64_t h, int64_t sq,
+                           int64_t sk, int64_t d, float scale, int causal, int block_q,
+                           int block_k, int dtype);
+
 #ifdef __cplusplus
 }
 #endif

@@ -99,3 +99,102 @@ def test_unaligned_base_falls_back_to_cuda_cores():
     out = flash_attention(q, to_torch(kn), to_torch(vn), causal=True)
     ref = oa.reference_fwd(qn, kn, vn, causal=True)
     assert max_abs(out, ref) <= 2e-2
+
+
+# ---------------------------------------------------------------- materialised-dS backward
+
+
+def _bwd(q, k, v, do, causal):
+    from ferrite.kernels.flash_attention import flash_backward, flash_forward_with_lse
+
+    out, lse = flash_forward_with_lse(q, k, v, causal=causal)
+    return flash_backward(q, k, v, out, lse, do, causal=causal), out, lse
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("budget_slices", [1, 4, None])
+def test_ds_backward_matches_recompute_and_oracle(monkeypatch, d, causal, budget_slices):
+    """dQ from the stored dS (whole batch, or chunks of 1 / 4 of the 6 slices)
+    against the recompute dQ kernel and the blockwise oracle; dK/dV are the same
+    kernel either way, so bitwise equal."""
+    import importlib
+
+    from ferrite import _native as nat
+
+    fa = importlib.import_module("ferrite.kernels.flash_attention")  # the module, not the re-exported function
+
+    rng = np.random.default_rng(d + causal)
+    b, h, s = 2, 3, 512
+    qn, kn, vn, don = (normal(rng, (b, h, s, d), BF16) for _ in range(4))
+    q, k, v, do = (to_torch(a) for a in (qn, kn, vn, don))
+    per_slice = nat.lib().ferrite_attn_bwd_ds_workspace_size(1, 1, s, s, d, nat.BF16)
+    assert per_slice == s * s * 2
+    if budget_slices is not None:
+        monkeypatch.setattr(fa, "DS_WORKSPACE_BUDGET", budget_slices * per_slice)
+    (dq, dk, dv), out, lse = _bwd(q, k, v, do, causal)
+    monkeypatch.setenv("FERRITE_ATTN_BWD_DS", "0")
+    (dq0, dk0, dv0), _, _ = _bwd(q, k, v, do, causal)
+    assert torch.equal(dk, dk0) and torch.equal(dv, dv0)
+    assert_bf16_close(dq, dq0, atol=4e-3)
+    o_ref, lse_ref = oa.flash_fwd(qn, kn, vn, causal=causal)
+    g_ref = oa.flash_bwd(qn, kn, vn, o_ref, lse_ref, don, causal=causal)
+    for got, ref, name in zip((dq, dk, dv), g_ref, ("dq", "dk", "dv")):
+        assert max_abs(got, ref) <= 2e-2, name
+        assert rel_l2(got, ref) < 1e-2, name
+
+
+def test_ds_backward_ragged_noncausal_query_length():
+    """sq = 200 (not a multiple of the 64-query tile; dS rows padded to 256) with
+    sk = 384, non-causal."""
+    rng = np.random.default_rng(21)
+    qn = normal(rng, (1, 2, 200, 64), BF16)
+    kn, vn = normal(rng, (1, 2, 384, 64), BF16), normal(rng, (1, 2, 384, 64), BF16)
+    don = normal(rng, (1, 2, 200, 64), BF16)
+    from ferrite.kernels.flash_attention import flash_backward, flash_forward_with_lse
+
+    bs = BlockSizes(8, 128, 8, 128)
+    q, k, v, do = (to_torch(a) for a in (qn, kn, vn, don))
+    out, lse = flash_forward_with_lse(q, k, v, causal=False, block_sizes=bs)
+    dq, dk, dv = flash_backward(q, k, v, out, lse, do, causal=False, block_sizes=bs)
+    dq_r, dk_r, dv_r = oa.reference_bwd(qn, kn, vn, don, causal=False)
+    for got, ref, name in zip((dq, dk, dv), (dq_r, dk_r, dv_r), ("dq", "dk", "dv")):
+        assert max_abs(got, ref) <= 2e-2, name
+
+
+def test_ds_backward_is_deterministic():
+    g = torch.Generator(device="cuda").manual_seed(4)
+    q, k, v, do = (torch.randn(2, 4, 1024, 128, device="cuda", generator=g).to(torch.bfloat16) for _ in range(4))
+    a, _, _ = _bwd(q, k, v, do, True)
+    b_, _, _ = _bwd(q, k, v, do, True)
+    for x, y in zip(a, b_):
+        assert torch.equal(x, y)
+
+
+def test_split_dkv_ds_and_dq_ds_entry_points_over_slice_ranges():
+    """The two halves called separately on slice ranges [0, 2) and [2, 6) give
+    the same gradients as the one-call backward."""
+    import ctypes
+
+    from ferrite import _native as nat
+    from ferrite.kernels.flash_attention import flash_backward, flash_forward_with_lse
+
+    g = torch.Generator(device="cuda").manual_seed(8)
+    b, h, s, d = 2, 3, 256, 128
+    q, k, v, do = (torch.randn(b, h, s, d, device="cuda", generator=g).to(torch.bfloat16) for _ in range(4))
+    out, lse = flash_forward_with_lse(q, k, v, causal=True)
+    dq_ref, dk_ref, dv_ref = flash_backward(q, k, v, out, lse, do, causal=True)
+    lib = nat.lib()
+    sp = nat.stream_ptr()
+    delta = torch.empty(b, h, s, device="cuda")
+    nat.check(lib.ferrite_attn_bwd_prep(sp, do.data_ptr(), out.data_ptr(), delta.data_ptr(), b, h, s, d, nat.BF16))
+    dq, dk, dv = (torch.empty_like(q) for _ in range(3))
+    st = nat.attn_strides(q=q, k=k, v=v, o=out, dout=do, dq=dq, dk=dk, dv=dv)
+    ds = torch.empty(4 * s * s * 2, dtype=torch.uint8, device="cuda")  # room for 4 slices
+    for begin, count in ((0, 2), (2, 4)):
+        nat.check(lib.ferrite_attn_bwd_dkv_ds(sp, q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), lse.data_ptr(), delta.data_ptr(),
+                                              dk.data_ptr(), dv.data_ptr(), ds.data_ptr(), ctypes.byref(st), begin, count, b, h, s, s, d,
+                                              d**-0.5, 1, 128, 128, nat.BF16))
+        nat.check(lib.ferrite_attn_bwd_dq_ds(sp, ds.data_ptr(), k.data_ptr(), dq.data_ptr(), ctypes.byref(st), begin, count, b, h, s, s, d,
+                                             d**-0.5, 1, 128, 128, nat.BF16))
+    assert torch.equal(dq, dq_ref) and torch.equal(dk, dk_ref) and torch.equal(dv, dv_ref)

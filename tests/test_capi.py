@@ -87,6 +87,20 @@ def test_strided_attention_validation_without_a_gpu():
     assert rc == nat.BAD_SHAPE and "block_q" in nat.last_error()
 
 
+def test_ds_backward_host_checks_without_a_gpu():
+    lib = nat.lib()
+    assert lib.ferrite_attn_bwd_ds_workspace_size(2, 3, 512, 512, 64, nat.BF16) == 6 * 512 * 512 * 2
+    assert lib.ferrite_attn_bwd_ds_workspace_size(1, 1, 200, 384, 64, nat.BF16) == 256 * 384 * 2  # rows padded to 64
+    assert lib.ferrite_attn_bwd_ds_workspace_size(1, 1, 512, 512, 64, nat.F32) == 0  # CUDA-core path: no dS
+    assert lib.ferrite_attn_bwd_ds_workspace_size(1, 1, 512, 512, 96, nat.BF16) == 0
+    st = nat.AttnStrides()
+    args = (1, 2, 256, 256, 64, 0.125, 1, 128, 128, nat.BF16)
+    rc = lib.ferrite_attn_bwd_dkv_ds(None, 1, 1, 1, 1, 1, 1, 1, 1, 1, ctypes.byref(st), 1, 2, *args)
+    assert rc == nat.BAD_SHAPE and "slice range" in nat.last_error()
+    rc = lib.ferrite_attn_bwd_dq_ds(None, 1, 1, 1, ctypes.byref(st), -1, 1, *args)
+    assert rc == nat.BAD_SHAPE
+
+
 def test_attn_strides_struct_matches_views():
     qkv = torch.zeros(2, 256, 3, 4, 64)
     q = qkv[:, :, 0].permute(0, 2, 1, 3)
