@@ -206,8 +206,12 @@ class NormWorkload:
                 "dh": torch.empty(R, D, dtype=torch.bfloat16, device=dev),
             })
         self.w = (1.0 + 0.1 * torch.randn(D, generator=g, device=dev)).float()
-        self.dw = torch.empty(D, dtype=torch.float32, device=dev)
-        self.dw_sum = torch.empty_like(self.dw)
+        # dw of step i lands in dw_bufs[i % 2]; at N > 1 its all-reduce runs on NCCL's
+        # stream while the next step's kernels run (the next write of that buffer, two
+        # steps later, waits for it), like a gradient bucket reduced during backward.
+        self.dw_bufs = [torch.empty(D, dtype=torch.float32, device=dev) for _ in range(2)]
+        self.dw = self.dw_bufs[0]
+        self.pending = [None, None]
         self.ws_buf = torch.empty(int(self.lib.ferrite_rmsnorm_bwd_workspace_size(R, D)), dtype=torch.uint8, device=dev)
         for s in self.sets:
             self._fwd(s)
@@ -223,27 +227,30 @@ class NormWorkload:
             nat.stream_ptr(self.dev), s["x"].data_ptr(), s["r"].data_ptr(), self.w.data_ptr(), s["h"].data_ptr(), s["y"].data_ptr(),
             self.ROWS, self.DIM, self.EPS, nat.BF16, nat.F32))
 
-    def _bwd(self, s):
+    def _bwd(self, s, dw):
         nat = self.nat
         nat.check(self.lib.ferrite_rmsnorm_bwd(
             nat.stream_ptr(self.dev), s["h"].data_ptr(), self.w.data_ptr(), s["dy"].data_ptr(), s["dhd"].data_ptr(), s["dh"].data_ptr(),
-            self.dw.data_ptr(), self.ws_buf.data_ptr(), self.ws_buf.numel(), self.ROWS, self.DIM, self.EPS, nat.BF16, nat.F32))
+            dw.data_ptr(), self.ws_buf.data_ptr(), self.ws_buf.numel(), self.ROWS, self.DIM, self.EPS, nat.BF16, nat.F32))
 
     def step(self, i, ev=None):
         a, b = self.sets[i % 2], self.sets[(i + 1) % 2]
+        slot = i % 2
         if ev:
             ev[0].record()
         self._fwd(a)
         if ev:
             ev[1].record()
-        self._bwd(b)
+        if self.pending[slot] is not None:
+            self.pending[slot].wait()  # the stream waits for the all-reduce of step i - 2
+            self.pending[slot] = None
+        self._bwd(b, self.dw_bufs[slot])
         if ev:
             ev[2].record()
         if self.ws > 1:
             import torch.distributed as dist
 
-            self.dw_sum.copy_(self.dw)
-            dist.all_reduce(self.dw_sum)
+            self.pending[slot] = dist.all_reduce(self.dw_bufs[slot], async_op=True)
 
     def breakdown(self, evs):
         fwd = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
@@ -558,7 +565,7 @@ class GptWorkload:
     def __init__(self, dev, ws, rank, shape=None):
         from ferrite import _native as nat
         from ferrite.model.gpt import GPTConfig, flops_per_token, init_params, param_count, param_leaves
-        from ferrite.model.train import AdamW, FlatGrads, TrainConfig, build_train_step
+        from ferrite.model.train import TrainConfig, build_train_step, make_optimizer
 
         self.dev, self.ws, self.rank = dev, ws, rank
         self.cfg = GPTConfig(**GPT_CFG, attention="pallas", norm="pallas", linear="pallas", dtype=torch.bfloat16)
@@ -573,8 +580,9 @@ class GptWorkload:
         n = param_count(self.params)
         nonembed = n - self.params["tok_emb"].numel() - self.params["pos_emb"].numel()
         self.flops_per_step_global = 3 * flops_per_token(self.cfg, nonembed)["total"] * self.GLOBAL_BATCH * self.cfg.seq_len
-        self.opt = AdamW(leaves, self.tcfg)
-        self.flat = FlatGrads(leaves)
+        # native fused AdamW over flat buffers; at N > 1 the gradient all-reduce runs in
+        # buckets during backward (tied embedding and position table reduced last)
+        self.opt, self.flat = make_optimizer(leaves, self.tcfg, late=(self.params["tok_emb"], self.params["pos_emb"]))
         self._step = build_train_step(self.cfg, self.tcfg, leaves, self.opt, self.flat, self.params)
         rng = np.random.default_rng(rank)
         ids = rng.integers(0, self.cfg.vocab_size, size=(self.local_batch, self.cfg.seq_len + 1))
@@ -584,18 +592,34 @@ class GptWorkload:
         self._count_launches(nat)
 
     def _count_launches(self, nat):
-        """Count native launches of one step (one C call = one kernel; rmsnorm_bwd = 2)."""
+        """Count native kernel launches of one step by wrapping every launching entry
+        point of the C ABI (kernels per call: rmsnorm_bwd 2, adamw 2, a split-K gemm 2,
+        the dS attention backward 2 per chunk of slices, everything else 1)."""
         lib = nat.lib()
-        counts = {}
-        per_call = {"ferrite_rmsnorm_bwd": 2}
+        counts, kernels = {}, {}
+
+        def per_call(name, a):
+            if name in ("ferrite_rmsnorm_bwd", "ferrite_rmsnorm_bwd_noalloc", "ferrite_adamw_step"):
+                return 2
+            if name == "ferrite_gemm_ws":
+                return 2 if a[-1] else 1
+            if name == "ferrite_attn_bwd_ds":
+                ws_bytes, b, h, sq, sk = a[12], a[13], a[14], a[15], a[16]
+                per = ws_bytes // (((sq + 63) // 64) * 64 * sk * 2) if ws_bytes else 0
+                return 2 * -(-(b * h) // per) if per else 2
+            return 1
+
         originals = {}
-        for name in ("ferrite_rmsnorm_fwd", "ferrite_add_rmsnorm_fwd", "ferrite_rmsnorm_bwd", "ferrite_gemm",
-                     "ferrite_attn_fwd", "ferrite_attn_bwd_prep", "ferrite_attn_bwd_dkv", "ferrite_attn_bwd_dq"):
+        skip = ("ferrite_last_error", "ferrite_version", "ferrite_device_status")
+        for name in nat.SIGNATURES:
+            if name in skip or name.endswith("_workspace_size"):
+                continue
             fn = getattr(lib, name)
             originals[name] = fn
 
             def wrap(*a, _fn=fn, _n=name):
                 counts[_n] = counts.get(_n, 0) + 1
+                kernels[_n] = kernels.get(_n, 0) + per_call(_n, a)
                 return _fn(*a)
 
             setattr(lib, name, wrap)
@@ -605,7 +629,7 @@ class GptWorkload:
         finally:
             for name, fn in originals.items():
                 setattr(lib, name, fn)
-        self.launches_per_step = sum(v * per_call.get(k, 1) for k, v in counts.items())
+        self.launches_per_step = sum(kernels.values())
         self.launch_counts = counts
 
     @property

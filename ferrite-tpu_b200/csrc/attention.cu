@@ -380,8 +380,8 @@ struct FwdSmem {
   static constexpr int kQOff = 0;  // Q0, Q1
   static constexpr int kKVOff = 2 * kQBytes;
   static constexpr int kBarOff = kKVOff + 2 * kStageBytes;
-  // q_full, kv_full[2], kv_empty[2], s_full[2], p_full[2], pv_done[2]
-  static constexpr int kNumBars = 11;
+  // q_full, k_full[2], v_full[2], k_empty[2], v_empty[2], s_full[2], p_full[2], pv_done[2]
+  static constexpr int kNumBars = 15;
   static constexpr int kTotal = 1024 + kBarOff + kNumBars * 8 + 16;
 };
 
@@ -412,11 +412,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = bars + 3;
-  uint64_t* s_full = bars + 5;
-  uint64_t* p_full = bars + 7;
-  uint64_t* pv_done = bars + 9;
+  // K and V tiles have separate barriers: K_j is released as soon as both S_g(j)
+  // products are done, well before P V_j, so K_{j+2} streams in a full softmax
+  // period earlier than a combined K/V slot would allow.
+  uint64_t* k_full = bars + 1;
+  uint64_t* v_full = bars + 3;
+  uint64_t* k_empty = bars + 5;
+  uint64_t* v_empty = bars + 7;
+  uint64_t* s_full = bars + 9;
+  uint64_t* p_full = bars + 11;
+  uint64_t* pv_done = bars + 13;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kNumBars);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -436,8 +441,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&k_full[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 4);  // one arrival per softmax warp of the group
       mbar_init(&pv_done[i], 1);
@@ -465,16 +472,25 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         for (int c = 0; c < L::kChunks; ++c)
           tma_load_4d(smem + L::kQOff + g * L::kQBytes + c * (TQ * 128), &tq, q_full, c * 64,
                       q0 + g * TQ, hh, bb);
-      for (int j = 0; j < n_kv; ++j) {
-        const int s = j & 1;
-        if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, abort, 10)) break;
-        uint8_t* sk_ = smem + L::kKVOff + s * L::kStageBytes;
-        uint8_t* sv_ = sk_ + L::kKBytes;
-        mbar_arrive_expect_tx(&kv_full[s], L::kStageBytes);
+      // K runs one tile ahead of V: K0, K1, V0, K2, V1, ...
+      for (int i = 0; i <= n_kv; ++i) {
+        if (i < n_kv) {
+          const int s = i & 1;
+          if (!mbar_wait(&k_empty[s], ((i >> 1) & 1) ^ 1, abort, 10)) break;
+          uint8_t* sk_ = smem + L::kKVOff + s * L::kStageBytes;
+          mbar_arrive_expect_tx(&k_full[s], L::kKBytes);
 #pragma unroll
-        for (int c = 0; c < L::kChunks; ++c) {
-          tma_load_4d(sk_ + c * (TK * 128), &tk, &kv_full[s], c * 64, j * TK, hh, bb);
-          tma_load_4d(sv_ + c * (TK * 128), &tv, &kv_full[s], c * 64, j * TK, hh, bb);
+          for (int c = 0; c < L::kChunks; ++c)
+            tma_load_4d(sk_ + c * (TK * 128), &tk, &k_full[s], c * 64, i * TK, hh, bb);
+        }
+        if (i >= 1) {
+          const int j = i - 1, s = j & 1;
+          if (!mbar_wait(&v_empty[s], ((j >> 1) & 1) ^ 1, abort, 19)) break;
+          uint8_t* sv_ = smem + L::kKVOff + s * L::kStageBytes + L::kKBytes;
+          mbar_arrive_expect_tx(&v_full[s], L::kVBytes);
+#pragma unroll
+          for (int c = 0; c < L::kChunks; ++c)
+            tma_load_4d(sv_ + c * (TK * 128), &tv, &v_full[s], c * 64, j * TK, hh, bb);
         }
       }
     }
@@ -483,7 +499,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       constexpr uint32_t idesc_s = make_idesc_f16(TQ, TK, BF16, false, false);
       constexpr uint32_t idesc_o = make_idesc_f16(TQ, D, BF16, false, true);
       const uint32_t sq_ = smem_u32(smem + L::kQOff);
-      bool ok = mbar_wait(q_full, 0, abort, 11) && mbar_wait(&kv_full[0], 0, abort, 12);
+      bool ok = mbar_wait(q_full, 0, abort, 11) && mbar_wait(&k_full[0], 0, abort, 12);
       // Descriptors are built once; each MMA adds a compile-time byte offset.
       const uint64_t dq_base = make_sdesc(sq_, 16, 1024);
       const uint64_t dk_base = make_sdesc(smem_u32(smem + L::kKVOff), 16, 1024);
@@ -512,22 +528,27 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         tc_fence_after();
         issue_s(0, 0);
         issue_s(1, 0);
+        tc_commit(&k_empty[0]);  // K_0 no longer read once both S_g(0) complete
       }
       for (int j = 0; ok && j < n_kv; ++j) {
         const bool more = j + 1 < n_kv;
         if (!mbar_wait(&p_full[0], j & 1, abort, 13)) break;
+        if (!mbar_wait(&v_full[j & 1], (j >> 1) & 1, abort, 18)) break;
         tc_fence_after();
         issue_pv(0, j);
         if (more) {
-          if (!mbar_wait(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort, 14)) break;
+          if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort, 14)) break;
           tc_fence_after();
           issue_s(0, j + 1);
         }
         if (!mbar_wait(&p_full[1], j & 1, abort, 15)) break;
         tc_fence_after();
         issue_pv(1, j);
-        tc_commit(&kv_empty[j & 1]);  // K_j, V_j no longer read
-        if (more) issue_s(1, j + 1);
+        tc_commit(&v_empty[j & 1]);  // V_j no longer read
+        if (more) {
+          issue_s(1, j + 1);
+          tc_commit(&k_empty[(j + 1) & 1]);  // K_{j+1} no longer read
+        }
       }
     }
   } else if (warp >= 4) {

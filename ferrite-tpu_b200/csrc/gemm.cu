@@ -8,9 +8,10 @@
 //     (M=128, N=BN, K=16, kind::f16) into an f32 accumulator in TMEM; every slot
 //     is released with tcgen05.commit -> mbarrier, every finished tile with a
 //     commit to the accumulator's "full" barrier;
-//   * warps 2-5 are the epilogue: tcgen05.ld the accumulator (two TMEM buffers,
-//     so the epilogue of tile i overlaps the main loop of tile i+1), convert,
-//     and store with row/column masks.
+//   * warps 2-9 are the epilogue, two per TMEM lane quarter (each half of the
+//     tile's columns): tcgen05.ld the accumulator (two TMEM buffers, so the
+//     epilogue of tile i overlaps the main loop of tile i+1), convert (and apply
+//     the fused activation epilogues), and store with row/column masks.
 //   Operands may be K-major or MN-major in global memory (the transpose flags
 //   of the C ABI); the MN-major case uses MN-major shared-memory layouts and the
 //   instruction descriptor's transpose bits instead of materialised transposes.
@@ -28,6 +29,7 @@
 // Reference: src/ferrite/kernels/matmul.py of anxnd2211/ferrite-tpu
 // (_matmul_kernel :27-38, _matmul_impl :52-86, VJP :99-104).
 #include <algorithm>
+#include <type_traits>
 #include <cstdlib>
 
 #include "common.cuh"
@@ -39,7 +41,8 @@ namespace gemm {
 
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 x 16-bit = 128 bytes: one swizzle row
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;  // two warps per TMEM lane quarter, each half of the columns
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 
 template <int BN>
 struct Smem {
@@ -62,6 +65,8 @@ struct Params {
   int splits;        // K slices per tile (1: no split)
   int kb_per_split;  // k blocks per slice
   float* ws;         // splits > 1: f32 partials [splits][m][n]
+  void* aux;         // epilogue operand (GELU: the activation output / the pre-activation input)
+  int64_t ld_aux;
 };
 
 template <typename TC>
@@ -100,6 +105,80 @@ __device__ __forceinline__ void store_row32(TC* __restrict__ c, int64_t ldc, int
   }
 }
 
+// Epilogues (bf16/f16 outputs, unsplit K):
+//   kEpiNone     C = acc
+//   kEpiGelu     C = u = round(acc); aux = round(gelu_tanh(u))  (the MLP up-projection
+//                and its activation, gpt.py:141, in one pass)
+//   kEpiGeluBwd  C = round(round(acc) * gelu_tanh'(aux))        (the activation's
+//                backward folded into the dA = dP W2^T product; aux = u)
+constexpr int kEpiNone = 0, kEpiGelu = 1, kEpiGeluBwd = 2;
+
+// tanh-approximated GELU and its derivative in f32 (the formula of
+// jax.nn.gelu(approximate=True) / torch gelu(approximate="tanh")), evaluated via
+// the identity 1 + tanh(y) = 2 sigmoid(2y): with y = sqrt(2/pi) (x + 0.044715 x^3)
+// and s = 1 / (1 + e^(-2y)),
+//   gelu(x)  = x s
+//   gelu'(x) = s + 2 x s (1 - s) sqrt(2/pi) (1 + 3 * 0.044715 x^2)
+// (1 - tanh^2 = 4 s (1 - s)).  Two MUFU operations per element and no
+// cancellation for large |x|; agrees with the tanh form to ~1e-6 relative.
+__device__ __forceinline__ float gelu_sigmoid_arg(float x) {  // s
+  const float kBeta = 0.7978845608028654f;  // sqrt(2 / pi)
+  const float y = kBeta * fmaf(0.044715f * x, x * x, x);
+  float e;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-2.8853900817779268f * y));  // e^(-2y)
+  return __fdividef(1.0f, 1.0f + e);
+}
+__device__ __forceinline__ float gelu_tanh_f(float x) { return x * gelu_sigmoid_arg(x); }
+__device__ __forceinline__ float gelu_tanh_grad_f(float x) {
+  const float kBeta = 0.7978845608028654f;
+  const float s = gelu_sigmoid_arg(x);
+  return fmaf(2.0f * x * s * (1.0f - s), kBeta * fmaf(3.0f * 0.044715f * x, x, 1.0f), s);
+}
+
+// Rows of 32 accumulator columns through an epilogue: r holds f32 bits on entry.
+template <typename TC, int EPI>
+__device__ __forceinline__ void epilogue_row32(const Params& p, TC* c, int row, int col0,
+                                               uint32_t (&r)[32], bool vec_ok) {
+  if constexpr (EPI == kEpiNone) {
+    store_row32<TC>(c, p.ldc, row, col0, p.m, p.n, r, vec_ok);
+  } else {
+    if (row >= p.m) return;
+    TC* aux = reinterpret_cast<TC*>(p.aux) + (int64_t)row * p.ld_aux + col0;
+    const bool aux_vec = ((reinterpret_cast<uintptr_t>(p.aux) & 15u) == 0) &&
+                         ((p.ld_aux * (int64_t)sizeof(TC)) % 16 == 0);
+    if constexpr (EPI == kEpiGelu) {
+      uint32_t a[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float u = DT<TC>::to_f(DT<TC>::from_f(__uint_as_float(r[j])));
+        a[j] = __float_as_uint(gelu_tanh_f(u));
+      }
+      store_row32<TC>(c, p.ldc, row, col0, p.m, p.n, r, vec_ok);
+      store_row32<TC>(aux, 0, 0, 0, 1, p.n - col0, a, aux_vec);
+    } else {
+      float u[32];
+      if (aux_vec && col0 + 32 <= p.n) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          const uint4 v = *reinterpret_cast<const uint4*>(aux + j);
+          const TC* e = reinterpret_cast<const TC*>(&v);
+#pragma unroll
+          for (int t = 0; t < 8; ++t) u[j + t] = DT<TC>::to_f(e[t]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) u[j] = col0 + j < p.n ? DT<TC>::to_f(aux[j]) : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float da = DT<TC>::to_f(DT<TC>::from_f(__uint_as_float(r[j])));
+        r[j] = __float_as_uint(da * gelu_tanh_grad_f(u[j]));
+      }
+      store_row32<TC>(c, p.ldc, row, col0, p.m, p.n, r, vec_ok);
+    }
+  }
+}
+
 __device__ __forceinline__ void tile_coords(int t, const Params& p, int& mb, int& nb) {
   const int per_group = p.group_m * p.tiles_n;
   const int g = t / per_group;
@@ -111,7 +190,7 @@ __device__ __forceinline__ void tile_coords(int t, const Params& p, int& mb, int
 }
 
 // A_MN: A stored [K][M] (MN-major); B_MN: B stored [K][N] (MN-major).
-template <int BN, bool A_MN, bool B_MN, bool BF16, typename TC>
+template <int BN, bool A_MN, bool B_MN, bool BF16, typename TC, int EPI = kEpiNone>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a,
                    const __grid_constant__ CUtensorMap tma_b, const Params p) {
@@ -142,7 +221,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+      mbar_init(&acc_empty[b], kEpiWarps);  // one arrival per epilogue warp
     }
     *abort = 0;
     fence_mbar_init();
@@ -238,6 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;  // which half of the tile's columns
     const int row_in_tile = q * 32 + lane;
     TC* c = reinterpret_cast<TC*>(p.c);
     const bool vec_ok = ((reinterpret_cast<uintptr_t>(c) & 15u) == 0) &&
@@ -256,7 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
       const int row = mb * BM + row_in_tile;
 #pragma unroll 1
-      for (int cc = 0; cc < BN / 32; ++cc) {
+      for (int cc = half * (BN / 64); cc < (half + 1) * (BN / 64); ++cc) {
         uint32_t r[32];
         tmem_ld32(tbase + cc * 32, r);
         tmem_wait_ld();
@@ -264,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           store_row32<float>(p.ws + (int64_t)split * p.m * p.n, p.n, row, nb * BN + cc * 32, p.m,
                              p.n, r, ws_vec_ok);
         else
-          store_row32<TC>(c, p.ldc, row, nb * BN + cc * 32, p.m, p.n, r, vec_ok);
+          epilogue_row32<TC, EPI>(p, c, row, nb * BN + cc * 32, r, vec_ok);
       }
       tc_fence_before();
       __syncwarp();
@@ -438,10 +518,10 @@ static int launch_simt(cudaStream_t s, const void* a, const void* b, void* c, in
   return check_launch("gemm_simt");
 }
 
-template <int BN, bool A_MN, bool B_MN, bool BF16, typename TC>
+template <int BN, bool A_MN, bool B_MN, bool BF16, typename TC, int EPI = kEpiNone>
 static int launch_tc(cudaStream_t s, const CUtensorMap& ta, const CUtensorMap& tb,
                      const Params& p, int grid) {
-  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, BF16, TC>;
+  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, BF16, TC, EPI>;
   const int smem = Smem<BN>::kTotal;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess)
@@ -452,7 +532,16 @@ static int launch_tc(cudaStream_t s, const CUtensorMap& ta, const CUtensorMap& t
 
 template <int BN, bool BF16, typename TC>
 static int dispatch_major(cudaStream_t s, bool a_mn, bool b_mn, const CUtensorMap& ta,
-                          const CUtensorMap& tb, const Params& p, int grid) {
+                          const CUtensorMap& tb, const Params& p, int grid, int epi) {
+  if constexpr (BF16 && std::is_same<TC, __nv_bfloat16>::value) {
+    // the GPT MLP's fused epilogues: up-projection (A K-major, B MN-major) and
+    // dA = dP W2^T (both K-major)
+    if (epi == kEpiGelu && !a_mn && b_mn) return launch_tc<BN, false, true, true, TC, kEpiGelu>(s, ta, tb, p, grid);
+    if (epi == kEpiGeluBwd && !a_mn && !b_mn) return launch_tc<BN, false, false, true, TC, kEpiGeluBwd>(s, ta, tb, p, grid);
+  }
+  if (epi != kEpiNone)
+    return fail(FERRITE_UNSUPPORTED_DTYPE, "gemm: epilogue %d needs bf16 operands and output with %s", epi,
+                epi == kEpiGelu ? "A K-major, B [K][N]" : "A K-major, B [N][K] (trans_b)");
   if (!a_mn && !b_mn) return launch_tc<BN, false, false, BF16, TC>(s, ta, tb, p, grid);
   if (!a_mn && b_mn) return launch_tc<BN, false, true, BF16, TC>(s, ta, tb, p, grid);
   if (a_mn && !b_mn) return launch_tc<BN, true, false, BF16, TC>(s, ta, tb, p, grid);
@@ -520,10 +609,11 @@ static int launch_reduce(cudaStream_t s, const float* ws, void* c, int64_t m, in
 template <bool BF16, typename TC>
 static int run_tc(cudaStream_t s, const void* a, const void* b, void* c, int64_t m,
                   int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int trans_a,
-                  int trans_b, void* workspace, size_t ws_bytes) {
+                  int trans_b, void* workspace, size_t ws_bytes, int epi = kEpiNone,
+                  void* aux = nullptr, int64_t ld_aux = 0) {
   const int dev = current_device();
   const int sms = num_sms(dev);
-  Plan pl = plan_tc(m, n, k, sms, workspace != nullptr);
+  Plan pl = plan_tc(m, n, k, sms, workspace != nullptr && epi == kEpiNone);
   if (plan_workspace(pl, m, n) > ws_bytes || (reinterpret_cast<uintptr_t>(workspace) & 255u)) {
     pl = plan_tc(m, n, k, sms, false);  // not enough scratch: no split
   }
@@ -562,10 +652,12 @@ static int run_tc(cudaStream_t s, const void* a, const void* b, void* c, int64_t
   p.splits = pl.splits;
   p.kb_per_split = pl.kb_per_split;
   p.ws = pl.splits > 1 ? reinterpret_cast<float*>(workspace) : nullptr;
+  p.aux = aux;
+  p.ld_aux = ld_aux;
   const int units = p.tiles_m * p.tiles_n * p.splits;
   const int grid = std::min(units, sms);
-  rc = BN == 256 ? dispatch_major<256, BF16, TC>(s, a_mn, b_mn, ta, tb, p, grid)
-                 : dispatch_major<128, BF16, TC>(s, a_mn, b_mn, ta, tb, p, grid);
+  rc = BN == 256 ? dispatch_major<256, BF16, TC>(s, a_mn, b_mn, ta, tb, p, grid, epi)
+                 : dispatch_major<128, BF16, TC>(s, a_mn, b_mn, ta, tb, p, grid, epi);
   if (rc || pl.splits == 1) return rc;
   return launch_reduce<TC>(s, p.ws, c, m, n, ldc, pl.splits, sms);
 }
@@ -606,6 +698,26 @@ extern "C" int ferrite_gemm(void* stream, const void* a, const void* b, void* c,
                             int trans_a, int trans_b, int ab_dtype, int c_dtype) {
   return ferrite_gemm_ws(stream, a, b, c, m, n, k, lda, ldb, ldc, trans_a, trans_b, ab_dtype,
                          c_dtype, nullptr, 0);
+}
+
+extern "C" int ferrite_gemm_epilogue(void* stream, const void* a, const void* b, void* c,
+                                     int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
+                                     int64_t ldc, int trans_a, int trans_b, int epilogue,
+                                     void* aux, int64_t ld_aux) {
+  if (int rc = injected_fault("gemm")) return rc;
+  if (epilogue != kEpiGelu && epilogue != kEpiGeluBwd)
+    return fail(FERRITE_BAD_SHAPE, "gemm_epilogue: unknown epilogue %d", epilogue);
+  if (m < 0 || n < 0 || k < 0) return fail(FERRITE_BAD_SHAPE, "gemm_epilogue: negative size");
+  if (ld_aux < std::max<int64_t>(1, n) || ldc < std::max<int64_t>(1, n))
+    return fail(FERRITE_BAD_SHAPE, "gemm_epilogue: leading dimension too small");
+  if (m == 0 || n == 0) return FERRITE_OK;
+  if (!a || !b || !c || !aux) return fail(FERRITE_BAD_SHAPE, "gemm_epilogue: null pointer");
+  if (k == 0 || !tc_eligible(a, b, m, n, k, lda, ldb, trans_a, trans_b))
+    return fail(FERRITE_UNSUPPORTED_DTYPE,
+                "gemm_epilogue: needs the tensor-core path (16-byte aligned operands and strides, "
+                "m, n >= 128, k >= 64)");
+  return run_tc<true, __nv_bfloat16>((cudaStream_t)stream, a, b, c, m, n, k, lda, ldb, ldc, trans_a,
+                                     trans_b, nullptr, 0, epilogue, aux, ld_aux);
 }
 
 extern "C" int ferrite_gemm_ws(void* stream, const void* a, const void* b, void* c, int64_t m,

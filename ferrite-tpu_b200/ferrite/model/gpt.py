@@ -17,6 +17,7 @@ q/k/v in place from the packed ``[B, S, 3, H, hd]`` projection and writes
 transposes of gpt.py:136-138 are folded into the kernels' tensor maps; the
 loss (gpt.py:147-152) runs on the native cross-entropy kernels, fused with the
 tied head into one autograd node (no f32 logit gradient is materialised); the
+MLP's GELU runs in the epilogues of its GEMMs (forward and backward); the
 ``xla`` slot is plain torch (cuBLAS matmuls, materialised attention).
 """
 
@@ -159,6 +160,50 @@ class _TiedHead(torch.autograd.Function):
         return dy, de
 
 
+class _FusedMlp(torch.autograd.Function):
+    """``gelu_tanh(y W1) W2`` (gpt.py:141) with the activation in GEMM epilogues
+    (``ferrite_gemm_epilogue``): the forward's up-projection writes the
+    pre-activation u (kept for the backward) and a = gelu(u) in one pass; the
+    backward's dA = dP W2^T product writes dU = dA * gelu'(u) directly.  Same
+    rounding points as the unfused chain (u, a, dA and dU rounded to bf16)."""
+
+    @staticmethod
+    def forward(ctx, y, w1, w2):
+        from ferrite import _native as nat
+
+        t, d = y.shape
+        f = w1.shape[1]
+        u = torch.empty((t, f), dtype=y.dtype, device=y.device)
+        a = torch.empty_like(u)
+        nat.check(nat.lib().ferrite_gemm_epilogue(nat.stream_ptr(y.device), y.data_ptr(), w1.data_ptr(), u.data_ptr(),
+                                                  t, f, d, y.stride(0), w1.stride(0), u.stride(0), 0, 0, 1, a.data_ptr(), a.stride(0)))
+        ctx.save_for_backward(y, w1, w2, u, a)
+        return gemm(a, w2)
+
+    @staticmethod
+    def backward(ctx, dp):
+        from ferrite import _native as nat
+
+        y, w1, w2, u, a = ctx.saved_tensors
+        dp = dp.to(y.dtype).contiguous()
+        t, f = u.shape
+        du = torch.empty_like(u)
+        nat.check(nat.lib().ferrite_gemm_epilogue(nat.stream_ptr(y.device), dp.data_ptr(), w2.data_ptr(), du.data_ptr(),
+                                                  t, f, dp.shape[1], dp.stride(0), w2.stride(0), du.stride(0), 0, 1, 2, u.data_ptr(), u.stride(0)))
+        dw2 = gemm(a, dp, trans_a=True, out_dtype=w2.dtype)  # A^T dP
+        dy = gemm(du, w1, trans_b=True, out_dtype=y.dtype)  # dU W1^T
+        dw1 = gemm(y, du, trans_a=True, out_dtype=w1.dtype)  # Y^T dU
+        return dy, dw1, dw2
+
+
+def _mlp(y2, w1, w2, cfg: GPTConfig):
+    """The block's MLP, gelu(approximate=True) between the two linears (gpt.py:141)."""
+    b, s, d = y2.shape
+    if cfg.linear == "pallas" and cfg.dtype == torch.bfloat16 and d % 8 == 0 and w1.shape[1] % 8 == 0:
+        return _FusedMlp.apply(y2.reshape(-1, d).to(cfg.dtype), w1.to(cfg.dtype), w2.to(cfg.dtype)).reshape(b, s, -1)
+    return _linear(F.gelu(_linear(y2, w1, cfg), approximate="tanh"), w2, cfg)
+
+
 def block(layer, h, pending, cfg: GPTConfig):
     """One transformer block; returns (h, pending, k, v) (gpt.py:131-141, engine.py:53-66)."""
     b, s, _ = h.shape
@@ -176,7 +221,7 @@ def block(layer, h, pending, cfg: GPTConfig):
         a = _attention(q, k, v, cfg).transpose(1, 2).reshape(b, s, cfg.d_model)
     a = _linear(a, layer["wo"], cfg)
     h, y2 = _norm(a, layer["ln2"], h, cfg)
-    pending = _linear(F.gelu(_linear(y2, layer["w1"], cfg), approximate="tanh"), layer["w2"], cfg)
+    pending = _mlp(y2, layer["w1"], layer["w2"], cfg)
     return h, pending, k, v
 
 

@@ -104,42 +104,197 @@ def dist_env():
 
 class FlatGrads:
     """Points every parameter's ``.grad`` at a view of one flat f32 buffer, so the
-    data-parallel gradient exchange is a single all-reduce."""
+    data-parallel gradient exchange is one buffer's worth of all-reduce.
 
-    def __init__(self, params: list[torch.Tensor]):
+    With ``overlap=True`` (and a process group of more than one rank) the buffer
+    is cut into buckets of about ``bucket_mb`` MiB taken from its end -- the last
+    layers' gradients, which backward produces first -- and each bucket's
+    all-reduce (a sum) is launched on NCCL's stream from a post-accumulate hook as
+    soon as all of its gradients are final, so the exchange overlaps the rest of
+    the backward.  ``late`` parameters (e.g. a tied embedding, accumulated twice)
+    go in a final bucket reduced after backward.  :meth:`finish` waits for all
+    buckets; the caller divides by the world size (the fused AdamW does it in its
+    gradient pre-scale)."""
+
+    def __init__(self, params: list[torch.Tensor], *, overlap: bool = False, bucket_mb: float = 64.0, late=(), group=None):
         n = sum(p.numel() for p in params)
         self.flat = torch.zeros(n, dtype=torch.float32, device=params[0].device)
         self.views = []
+        self.offsets = []
         off = 0
         for p in params:
             v = self.flat[off : off + p.numel()].view_as(p)
             p.grad = v
             self.views.append(v)
+            self.offsets.append(off)
             off += p.numel()
         self.params = params
+        self.group = group
+        self.works = []
+        self.buckets = []
+        self.overlap = overlap and self._world() > 1
+        if self.overlap:
+            self._build_buckets(bucket_mb, {id(p) for p in late})
+
+    @staticmethod
+    def _dist():
+        import torch.distributed as dist
+
+        return dist
+
+    def _world(self) -> int:
+        dist = self._dist()
+        return dist.get_world_size(self.group) if dist.is_available() and dist.is_initialized() else 1
+
+    def _build_buckets(self, bucket_mb, late_ids):
+        limit = int(bucket_mb * (1 << 20) / 4)
+        order = [i for i in range(len(self.params)) if id(self.params[i]) not in late_ids][::-1]
+        cur, cur_n = [], 0
+        runs = []
+        for i in order:  # contiguous runs of the flat buffer, from its end
+            if cur and (cur_n >= limit or self.offsets[i] + self.params[i].numel() != self.offsets[cur[-1]]):
+                runs.append(cur)
+                cur, cur_n = [], 0
+            cur.append(i)
+            cur_n += self.params[i].numel()
+        if cur:
+            runs.append(cur)
+        for idx in runs:
+            lo = self.offsets[idx[-1]]
+            hi = self.offsets[idx[0]] + self.params[idx[0]].numel()
+            self.buckets.append({"lo": lo, "hi": hi, "members": set(idx), "expected": len(idx)})
+        for i in range(len(self.params)):
+            if id(self.params[i]) in late_ids:  # reduced after backward, not by a hook
+                self.buckets.append({"lo": self.offsets[i], "hi": self.offsets[i] + self.params[i].numel(), "members": {i}, "expected": None})
+        self.bucket_of = {i: b for b in self.buckets for i in b["members"]}
+        self._reset_buckets()
+        for i, p in enumerate(self.params):
+            if id(p) not in late_ids:
+                p.register_post_accumulate_grad_hook(self._hook(i))
+
+    def _reset_buckets(self):
+        for b in self.buckets:
+            b["left"] = b["expected"]
+            b["launched"] = False
+
+    def _hook(self, i):
+        def fire(_p):
+            b = self.bucket_of[i]
+            if b["expected"] is None or b["launched"]:
+                return
+            b["left"] -= 1
+            if b["left"] == 0:
+                self._launch(b)
+
+        return fire
+
+    def _launch(self, b):
+        b["launched"] = True
+        self.works.append(self._dist().all_reduce(self.flat[b["lo"] : b["hi"]], group=self.group, async_op=True))
 
     def zero(self):
         self.flat.zero_()
         for p, v in zip(self.params, self.views):
             p.grad = v
+        self._reset_buckets()
+
+    def finish(self):
+        """Overlap mode: launch the buckets still pending, then make the current
+        stream wait for every bucket's all-reduce (sums; divide by the world size)."""
+        for b in self.buckets:
+            if not b["launched"]:
+                self._launch(b)
+        for w in self.works:
+            w.wait()
+        self.works = []
 
     def all_reduce_mean(self, group=None):
-        import torch.distributed as dist
-
+        dist = self._dist()
         if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
             dist.all_reduce(self.flat, group=group)
             self.flat.div_(dist.get_world_size(group))
 
 
-def build_train_step(model_cfg: GPTConfig, train_cfg: TrainConfig, params_list, opt: AdamW, flat: FlatGrads, params):
+class FusedAdamW:
+    """adamw_update (train.py:59-74) as one native pass over flat f32 buffers
+    (``ferrite_adamw_step``: grad-norm clipping, bias-corrected Adam, decoupled
+    weight decay on ndim >= 2 parameters).
+
+    The parameters are moved into one flat buffer, decayed (ndim >= 2) ones first;
+    ``self.grads`` is a :class:`FlatGrads` with the same layout, and the moments
+    are flat.  ``grad_scale`` multiplies the gradients first (1 / world size after
+    a summed all-reduce)."""
+
+    def __init__(self, params: list[torch.Tensor], cfg: TrainConfig, b1=0.9, b2=0.95, eps=1e-8, *, overlap=False, late=(), bucket_mb=64.0):
+        from ferrite import _native as nat
+
+        self.nat, self.lib = nat, nat.lib()
+        decayed = [p for p in params if p.ndim >= 2]
+        self.order = decayed + [p for p in params if p.ndim < 2]
+        self.n_decay = sum(p.numel() for p in decayed)
+        self.n = sum(p.numel() for p in self.order)
+        dev = params[0].device
+        nat.require_cuda(params[0])
+        self.flat = torch.empty(self.n, dtype=torch.float32, device=dev)
+        off = 0
+        with torch.no_grad():
+            for p in self.order:
+                k = p.numel()
+                self.flat[off : off + k].copy_(p.reshape(-1))
+                p.data = self.flat[off : off + k].view_as(p)
+                off += k
+        self.grads = FlatGrads(self.order, overlap=overlap, late=late, bucket_mb=bucket_mb)
+        self.m = torch.zeros_like(self.flat)
+        self.v = torch.zeros_like(self.flat)
+        self.ws = torch.empty(int(self.lib.ferrite_adamw_workspace_size(self.n)), dtype=torch.uint8, device=dev)
+        self.gnorm = torch.zeros((), dtype=torch.float32, device=dev)
+        self.step = 0
+        self.cfg, self.b1, self.b2, self.eps = cfg, b1, b2, eps
+        self.params = self.order
+
+    @torch.no_grad()
+    def update(self, grads=None, grad_scale: float = 1.0) -> torch.Tensor:
+        self.step += 1
+        cfg, nat = self.cfg, self.nat
+        nat.check(
+            self.lib.ferrite_adamw_step(
+                nat.stream_ptr(self.flat.device), self.flat.data_ptr(), self.grads.flat.data_ptr(), self.m.data_ptr(),
+                self.v.data_ptr(), self.n, self.n_decay, lr_at(self.step, cfg), self.b1, self.b2, self.eps,
+                cfg.weight_decay, self.step, cfg.clip, grad_scale, self.gnorm.data_ptr(), self.ws.data_ptr(), self.ws.numel(),
+            )
+        )
+        return self.gnorm.clone()
+
+
+def make_optimizer(params: list[torch.Tensor], cfg: TrainConfig, *, fused: bool | None = None, late=()):
+    """(optimizer, FlatGrads): the native fused AdamW over flat buffers on CUDA
+    (with bucketed, backward-overlapped gradient all-reduce at more than one rank),
+    else the per-tensor reference AdamW."""
+    if fused is None:
+        fused = params[0].is_cuda
+    if fused:
+        opt = FusedAdamW(params, cfg, overlap=True, late=late)
+        return opt, opt.grads
+    return AdamW(params, cfg), FlatGrads(params)
+
+
+def build_train_step(model_cfg: GPTConfig, train_cfg: TrainConfig, params_list, opt, flat: FlatGrads, params):
     """One DP step: forward + backward on the local shard, gradient all-reduce, AdamW."""
 
     def step(x, y):
         flat.zero()
         loss = loss_fn(params, x, y, model_cfg)
         loss.backward()
-        flat.all_reduce_mean()
-        gnorm = opt.update(flat.views)
+        if isinstance(opt, FusedAdamW):
+            world = flat._world()
+            if flat.overlap:
+                flat.finish()  # bucket sums, launched during backward
+            elif world > 1:
+                flat._dist().all_reduce(flat.flat, group=flat.group)
+            gnorm = opt.update(grad_scale=1.0 / world)
+        else:
+            flat.all_reduce_mean()
+            gnorm = opt.update(flat.views)
         return loss.detach(), gnorm
 
     return step
@@ -165,8 +320,7 @@ def train(model_cfg: GPTConfig, train_cfg: TrainConfig, *, verbose: bool = True)
         p.requires_grad_(True)
     n_params = param_count(params)
     n_nonembed = n_params - params["tok_emb"].numel() - params["pos_emb"].numel()
-    opt = AdamW(leaves, train_cfg)
-    flat = FlatGrads(leaves)
+    opt, flat = make_optimizer(leaves, train_cfg, late=(params["tok_emb"], params["pos_emb"]))
     step_fn = build_train_step(model_cfg, train_cfg, leaves, opt, flat, params)
 
     def batch():

@@ -128,6 +128,20 @@ FERRITE_API int ferrite_gemm(void* stream, const void* a, const void* b, void* c
                  int64_t ldc, int trans_a, int trans_b, int ab_dtype,
                  int c_dtype);
 
+/* bf16 GEMM with the GPT MLP's activation fused into the epilogue (no
+ * reference kernel counterpart: the reference applies jax.nn.gelu(approximate=
+ * True) between two ferrite_matmul calls, gpt.py:141):
+ *   epilogue 1 (GELU):     c = u = A B rounded, aux = gelu_tanh(u) rounded
+ *                          (A [M][K], B [K][N]: trans_a = trans_b = 0);
+ *   epilogue 2 (GELU_BWD): c = round(round(A B^T) * gelu_tanh'(aux)), aux = u
+ *                          (dU from dA = dP W2^T: trans_a = 0, trans_b = 1).
+ * Both need the tensor-core path (16-byte aligned operands and strides, m, n >=
+ * 128, k >= 64); other shapes return FERRITE_UNSUPPORTED_DTYPE. */
+FERRITE_API int ferrite_gemm_epilogue(void* stream, const void* a, const void* b, void* c,
+                          int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
+                          int64_t ldc, int trans_a, int trans_b, int epilogue,
+                          void* aux, int64_t ld_aux);
+
 /* Bytes of f32 scratch ferrite_gemm_ws can use for a split-K launch of this
  * shape on the current device (0: the shape gets no split).  Splitting K helps
  * when the output has fewer tiles than the GPU has SMs -- the weight gradients
@@ -210,6 +224,27 @@ FERRITE_API int ferrite_xent_bwd(void* stream, const float* logits, const void* 
                      const float* lse, const float* dloss, float scale, void* dlogits,
                      int64_t rows, int64_t vocab, int64_t ld, int64_t ld_out,
                      int target_dtype, int out_dtype);
+
+/* ---- AdamW over flat parameters --------------------------------------------- */
+
+/* Bytes of scratch ferrite_adamw_step needs for n elements (the grad-norm
+ * partials). */
+FERRITE_API size_t ferrite_adamw_workspace_size(int64_t n);
+
+/* One AdamW step with global-norm clipping over flat f32 buffers of n elements
+ * (params, grads, m, v; 16-byte aligned), the reference's adamw_update
+ * (model/train.py:59-74) on the gradients g = grad_scale * grads (grad_scale =
+ * 1 / ranks turns a summed all-reduce into the mean): gnorm = ||g||_2,
+ * g' = g * min(1, clip / (gnorm + 1e-6)), m = b1 m + (1-b1) g', v = b2 v + (1-b2) g'^2,
+ * p -= lr ((m / (1-b1^step)) / (sqrt(v / (1-b2^step)) + eps) + wd p), with the
+ * decay term on elements [0, n_decay) only (the caller lays out the ndim >= 2
+ * parameters first).  gnorm is written to *gnorm_out (device, may be NULL).
+ * Deterministic (fixed-order norm reduction, no atomics). */
+FERRITE_API int ferrite_adamw_step(void* stream, float* params, const float* grads, float* m,
+                       float* v, int64_t n, int64_t n_decay, float lr, float b1, float b2,
+                       float eps, float weight_decay, int64_t step, float clip,
+                       float grad_scale, float* gnorm_out, void* workspace,
+                       size_t workspace_bytes);
 
 /* ---- strided flash attention ----------------------------------------------- */
 
