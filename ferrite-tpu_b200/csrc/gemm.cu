@@ -11,7 +11,10 @@
 //   * warps 2-9 are the epilogue, two per TMEM lane quarter (each half of the
 //     tile's columns): tcgen05.ld the accumulator (two TMEM buffers, so the
 //     epilogue of tile i overlaps the main loop of tile i+1), convert (and apply
-//     the fused activation epilogues), and store with row/column masks.
+//     the fused activation epilogues), and store: 16-bit outputs go through
+//     per-warp 32 x 32 shared-memory staging slots and TMA stores (one store
+//     instruction per chunk instead of 32 scattered row writes per warp store;
+//     the unit clips M / N edges), f32 outputs with masked vector stores.
 //   Operands may be K-major or MN-major in global memory (the transpose flags
 //   of the C ABI); the MN-major case uses MN-major shared-memory layouts and the
 //   instruction descriptor's transpose bits instead of materialised transposes.
@@ -51,9 +54,16 @@ struct Smem {
   static constexpr int kBBytes = BN * BK * 2;  // 16 or 32 KiB
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTileBytes = kStages * kStageBytes;
+  // 16-bit outputs leave through TMA stores: per epilogue warp two 32 x 32 staging
+  // slots (2 KiB each, 64-byte swizzle), alternating so the store of one chunk
+  // overlaps the conversion of the next.
+  static constexpr int kSlotBytes = 32 * 32 * 2;
+  static constexpr int kStgOff = kTileBytes;
+  static constexpr int kStgBytes = kEpiWarps * 2 * kSlotBytes;
   // barriers: full[S], empty[S], acc_full[2], acc_empty[2]; then tmem base, abort
+  static constexpr int kBarOff = kStgOff + kStgBytes;
   static constexpr int kBarBytes = (2 * kStages + 4) * 8 + 16;
-  static constexpr int kTotal = 1024 /*alignment slack*/ + kTileBytes + kBarBytes;
+  static constexpr int kTotal = 1024 /*alignment slack*/ + kBarOff + kBarBytes;
 };
 
 struct Params {
@@ -67,6 +77,7 @@ struct Params {
   float* ws;         // splits > 1: f32 partials [splits][m][n]
   void* aux;         // epilogue operand (GELU: the activation output / the pre-activation input)
   int64_t ld_aux;
+  int tma_store;     // 16-bit C (and aux output) written through tensor maps
 };
 
 template <typename TC>
@@ -179,6 +190,72 @@ __device__ __forceinline__ void epilogue_row32(const Params& p, TC* c, int row, 
   }
 }
 
+// Stage a warp's 32 rows x 32 columns (f32 bits in r, one row per lane) into
+// staging slot (count & 1) as 16-bit values with the 64-byte swizzle (16-byte
+// chunk c of row l at c ^ ((l >> 1) & 3): conflict-free), then lane 0 issues the
+// TMA store of the 32 x 32 box at (x, y).  Before a slot is rewritten, the
+// store issued from it two chunks earlier must have finished reading it.
+template <typename TC>
+__device__ __forceinline__ void stage_store_32x32(uint8_t* stg_base, int ew, int count, int lane,
+                                                  const uint32_t (&r)[32], const CUtensorMap* map,
+                                                  int x, int y) {
+  uint8_t* slot = stg_base + (ew * 2 + (count & 1)) * (32 * 32 * 2);
+  if (lane == 0) bulk_wait_group_read1();
+  __syncwarp();
+  uint8_t* row = slot + lane * 64;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint4 v;
+    const int j = c * 8;
+    if constexpr (std::is_same<TC, __nv_bfloat16>::value) {
+      v.x = pack_bf16x2(__uint_as_float(r[j]), __uint_as_float(r[j + 1]));
+      v.y = pack_bf16x2(__uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+      v.z = pack_bf16x2(__uint_as_float(r[j + 4]), __uint_as_float(r[j + 5]));
+      v.w = pack_bf16x2(__uint_as_float(r[j + 6]), __uint_as_float(r[j + 7]));
+    } else {
+      v.x = pack_f16x2(__uint_as_float(r[j]), __uint_as_float(r[j + 1]));
+      v.y = pack_f16x2(__uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+      v.z = pack_f16x2(__uint_as_float(r[j + 4]), __uint_as_float(r[j + 5]));
+      v.w = pack_f16x2(__uint_as_float(r[j + 6]), __uint_as_float(r[j + 7]));
+    }
+    *reinterpret_cast<uint4*>(row + ((c ^ ((lane >> 1) & 3)) << 4)) = v;
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(map, slot, x, y);
+    bulk_commit_group();
+  }
+}
+
+// GELU backward values for a 32-column chunk of one row: r (f32 bits of dA, in)
+// becomes round(dA) * gelu'(u) with u read from aux.
+template <typename TC>
+__device__ __forceinline__ void epilogue_gelu_bwd_vals(const Params& p, int row, int col0,
+                                                       uint32_t (&r)[32]) {
+  float u[32];
+  const TC* aux = reinterpret_cast<const TC*>(p.aux) + (int64_t)row * p.ld_aux + col0;
+  const bool aux_vec = ((reinterpret_cast<uintptr_t>(p.aux) & 15u) == 0) &&
+                       ((p.ld_aux * (int64_t)sizeof(TC)) % 16 == 0);
+  if (row < p.m && aux_vec && col0 + 32 <= p.n) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      const uint4 v = *reinterpret_cast<const uint4*>(aux + j);
+      const TC* e = reinterpret_cast<const TC*>(&v);
+#pragma unroll
+      for (int t = 0; t < 8; ++t) u[j + t] = DT<TC>::to_f(e[t]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) u[j] = (row < p.m && col0 + j < p.n) ? DT<TC>::to_f(aux[j]) : 0.f;
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const float da = DT<TC>::to_f(DT<TC>::from_f(__uint_as_float(r[j])));
+    r[j] = __float_as_uint(da * gelu_tanh_grad_f(u[j]));
+  }
+}
+
 __device__ __forceinline__ void tile_coords(int t, const Params& p, int& mb, int& nb) {
   const int per_group = p.group_m * p.tiles_n;
   const int g = t / per_group;
@@ -193,14 +270,16 @@ __device__ __forceinline__ void tile_coords(int t, const Params& p, int& mb, int
 template <int BN, bool A_MN, bool B_MN, bool BF16, typename TC, int EPI = kEpiNone>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a,
-                   const __grid_constant__ CUtensorMap tma_b, const Params p) {
+                   const __grid_constant__ CUtensorMap tma_b,
+                   const __grid_constant__ CUtensorMap tma_c,
+                   const __grid_constant__ CUtensorMap tma_aux, const Params p) {
   using S = Smem<BN>;
   constexpr int STAGES = S::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* tiles = smem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kTileBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOff);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
@@ -324,6 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ((p.ldc * (int64_t)sizeof(TC)) % 16 == 0);
     // partial slices are [m][n] f32 blocks of a 256-byte aligned workspace
     const bool ws_vec_ok = (p.n % 4 == 0);
+    int stg_count = 0;  // staging slot use counter (slot = count & 1)
     int local = 0;
     for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++local) {
       int mb, nb;
@@ -340,16 +420,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t r[32];
         tmem_ld32(tbase + cc * 32, r);
         tmem_wait_ld();
-        if (p.splits > 1)
+        if (p.splits > 1) {
           store_row32<float>(p.ws + (int64_t)split * p.m * p.n, p.n, row, nb * BN + cc * 32, p.m,
                              p.n, r, ws_vec_ok);
-        else
+        } else if constexpr (sizeof(TC) == 2) {
+          if (p.tma_store) {
+            // this warp's 32 rows x 32 columns through a staging slot and one TMA
+            // store (the unit clips rows / columns past M / N)
+            const int x = nb * BN + cc * 32, y = mb * BM + q * 32;
+            if constexpr (EPI == kEpiGeluBwd) epilogue_gelu_bwd_vals<TC>(p, row, x, r);
+            stage_store_32x32<TC>(smem + S::kStgOff, warp - 2, stg_count++, lane, r, &tma_c, x, y);
+            if constexpr (EPI == kEpiGelu) {
+              uint32_t a[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                a[j] = __float_as_uint(gelu_tanh_f(DT<TC>::to_f(DT<TC>::from_f(__uint_as_float(r[j])))));
+              stage_store_32x32<TC>(smem + S::kStgOff, warp - 2, stg_count++, lane, a, &tma_aux, x, y);
+            }
+          } else {
+            epilogue_row32<TC, EPI>(p, c, row, nb * BN + cc * 32, r, vec_ok);
+          }
+        } else {
           epilogue_row32<TC, EPI>(p, c, row, nb * BN + cc * 32, r, vec_ok);
+        }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
+    if (lane == 0) bulk_wait_group0();  // this warp's TMA stores complete before exit
   }
 
   // ------------------------------------------------------------ teardown
@@ -520,32 +619,33 @@ static int launch_simt(cudaStream_t s, const void* a, const void* b, void* c, in
 
 template <int BN, bool A_MN, bool B_MN, bool BF16, typename TC, int EPI = kEpiNone>
 static int launch_tc(cudaStream_t s, const CUtensorMap& ta, const CUtensorMap& tb,
-                     const Params& p, int grid) {
+                     const CUtensorMap& tc, const CUtensorMap& taux, const Params& p, int grid) {
   auto kern = gemm_tc_kernel<BN, A_MN, B_MN, BF16, TC, EPI>;
   const int smem = Smem<BN>::kTotal;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess)
     return fail(FERRITE_LAUNCH_FAILED, "gemm: smem attribute: %s", cudaGetErrorString(e));
-  kern<<<grid, kThreads, smem, s>>>(ta, tb, p);
+  kern<<<grid, kThreads, smem, s>>>(ta, tb, tc, taux, p);
   return check_launch("gemm_tc");
 }
 
 template <int BN, bool BF16, typename TC>
 static int dispatch_major(cudaStream_t s, bool a_mn, bool b_mn, const CUtensorMap& ta,
-                          const CUtensorMap& tb, const Params& p, int grid, int epi) {
+                          const CUtensorMap& tb, const CUtensorMap& tc, const CUtensorMap& taux,
+                          const Params& p, int grid, int epi) {
   if constexpr (BF16 && std::is_same<TC, __nv_bfloat16>::value) {
     // the GPT MLP's fused epilogues: up-projection (A K-major, B MN-major) and
     // dA = dP W2^T (both K-major)
-    if (epi == kEpiGelu && !a_mn && b_mn) return launch_tc<BN, false, true, true, TC, kEpiGelu>(s, ta, tb, p, grid);
-    if (epi == kEpiGeluBwd && !a_mn && !b_mn) return launch_tc<BN, false, false, true, TC, kEpiGeluBwd>(s, ta, tb, p, grid);
+    if (epi == kEpiGelu && !a_mn && b_mn) return launch_tc<BN, false, true, true, TC, kEpiGelu>(s, ta, tb, tc, taux, p, grid);
+    if (epi == kEpiGeluBwd && !a_mn && !b_mn) return launch_tc<BN, false, false, true, TC, kEpiGeluBwd>(s, ta, tb, tc, taux, p, grid);
   }
   if (epi != kEpiNone)
     return fail(FERRITE_UNSUPPORTED_DTYPE, "gemm: epilogue %d needs bf16 operands and output with %s", epi,
                 epi == kEpiGelu ? "A K-major, B [K][N]" : "A K-major, B [N][K] (trans_b)");
-  if (!a_mn && !b_mn) return launch_tc<BN, false, false, BF16, TC>(s, ta, tb, p, grid);
-  if (!a_mn && b_mn) return launch_tc<BN, false, true, BF16, TC>(s, ta, tb, p, grid);
-  if (a_mn && !b_mn) return launch_tc<BN, true, false, BF16, TC>(s, ta, tb, p, grid);
-  return launch_tc<BN, true, true, BF16, TC>(s, ta, tb, p, grid);
+  if (!a_mn && !b_mn) return launch_tc<BN, false, false, BF16, TC>(s, ta, tb, tc, taux, p, grid);
+  if (!a_mn && b_mn) return launch_tc<BN, false, true, BF16, TC>(s, ta, tb, tc, taux, p, grid);
+  if (a_mn && !b_mn) return launch_tc<BN, true, false, BF16, TC>(s, ta, tb, tc, taux, p, grid);
+  return launch_tc<BN, true, true, BF16, TC>(s, ta, tb, tc, taux, p, grid);
 }
 
 // Tile width and K split.  Cost model in units of one 128x256x64 MMA block on
@@ -656,8 +756,24 @@ static int run_tc(cudaStream_t s, const void* a, const void* b, void* c, int64_t
   p.ld_aux = ld_aux;
   const int units = p.tiles_m * p.tiles_n * p.splits;
   const int grid = std::min(units, sms);
-  rc = BN == 256 ? dispatch_major<256, BF16, TC>(s, a_mn, b_mn, ta, tb, p, grid, epi)
-                 : dispatch_major<128, BF16, TC>(s, a_mn, b_mn, ta, tb, p, grid, epi);
+  // 16-bit C (and the GELU epilogue's aux output) through TMA stores: 32 x 32
+  // boxes, 64-byte swizzle; a layout TMA cannot describe keeps direct stores
+  CUtensorMap tc = ta, taux = ta;  // placeholders when unused (never dereferenced)
+  p.tma_store = 0;
+  if (sizeof(TC) == 2 && pl.splits == 1 && env_int("FERRITE_GEMM_TMA_STORE", 1)) {
+    const CUtensorMapDataType ct = std::is_same<TC, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                                         : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const bool c_ok = (reinterpret_cast<uintptr_t>(c) & 15u) == 0 && (ldc * 2) % 16 == 0;
+    const bool aux_ok = epi != kEpiGelu || ((reinterpret_cast<uintptr_t>(aux) & 15u) == 0 && (ld_aux * 2) % 16 == 0);
+    if (c_ok && aux_ok &&
+        make_tmap_2d(&tc, c, ct, 2, (uint64_t)n, (uint64_t)m, (uint64_t)ldc * 2, 32, 32,
+                     CU_TENSOR_MAP_SWIZZLE_64B) == FERRITE_OK &&
+        (epi != kEpiGelu || make_tmap_2d(&taux, aux, ct, 2, (uint64_t)n, (uint64_t)m, (uint64_t)ld_aux * 2, 32, 32,
+                                         CU_TENSOR_MAP_SWIZZLE_64B) == FERRITE_OK))
+      p.tma_store = 1;
+  }
+  rc = BN == 256 ? dispatch_major<256, BF16, TC>(s, a_mn, b_mn, ta, tb, tc, taux, p, grid, epi)
+                 : dispatch_major<128, BF16, TC>(s, a_mn, b_mn, ta, tb, tc, taux, p, grid, epi);
   if (rc || pl.splits == 1) return rc;
   return launch_reduce<TC>(s, p.ws, c, m, n, ldc, pl.splits, sms);
 }
