@@ -451,6 +451,33 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
     *abort = 0;
     fence_mbar_init();
+    // The first loads (Q0, Q1, K0, K1, V0: every slot is still free) are issued
+    // before the TMEM allocation below, which waits for the SM's previous CTA to
+    // release its columns: the tiles then stream in under that CTA's tail.
+    if (n_kv > 0) {
+      tma_prefetch_desc(&tq);
+      tma_prefetch_desc(&tk);
+      tma_prefetch_desc(&tv);
+      mbar_arrive_expect_tx(q_full, 2 * L::kQBytes);
+#pragma unroll
+      for (int g = 0; g < 2; ++g)
+#pragma unroll
+        for (int c = 0; c < L::kChunks; ++c)
+          tma_load_4d(smem + L::kQOff + g * L::kQBytes + c * (TQ * 128), &tq, q_full, c * 64,
+                      q0 + g * TQ, hh, bb);
+      for (int i = 0; i < 2 && i < n_kv; ++i) {
+        uint8_t* sk_ = smem + L::kKVOff + i * L::kStageBytes;
+        mbar_arrive_expect_tx(&k_full[i], L::kKBytes);
+#pragma unroll
+        for (int c = 0; c < L::kChunks; ++c)
+          tma_load_4d(sk_ + c * (TK * 128), &tk, &k_full[i], c * 64, i * TK, hh, bb);
+      }
+      uint8_t* sv0 = smem + L::kKVOff + L::kKBytes;
+      mbar_arrive_expect_tx(&v_full[0], L::kVBytes);
+#pragma unroll
+      for (int c = 0; c < L::kChunks; ++c)
+        tma_load_4d(sv0 + c * (TK * 128), &tv, &v_full[0], c * 64, 0, hh, bb);
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -462,18 +489,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const uint32_t tmem = *tmem_slot;
   if (warp == 0) {
     if (lane == 0 && n_kv > 0) {
-      tma_prefetch_desc(&tq);
-      tma_prefetch_desc(&tk);
-      tma_prefetch_desc(&tv);
-      mbar_arrive_expect_tx(q_full, 2 * L::kQBytes);
-#pragma unroll
-      for (int g = 0; g < 2; ++g)
-#pragma unroll
-        for (int c = 0; c < L::kChunks; ++c)
-          tma_load_4d(smem + L::kQOff + g * L::kQBytes + c * (TQ * 128), &tq, q_full, c * 64,
-                      q0 + g * TQ, hh, bb);
-      // K runs one tile ahead of V: K0, K1, V0, K2, V1, ...
-      for (int i = 0; i <= n_kv; ++i) {
+      // K runs one tile ahead of V: K0, K1, V0 (issued above), K2, V1, K3, V2, ...
+      for (int i = 2; i <= n_kv; ++i) {
         if (i < n_kv) {
           const int s = i & 1;
           if (!mbar_wait(&k_empty[s], ((i >> 1) & 1) ^ 1, abort, 10)) break;
@@ -830,6 +847,40 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     *abort = 0;
     fence_mbar_init();
   }
+  // The stationary tiles and the first streaming stages (all slots still free)
+  // are requested before the TMEM allocation below, which waits for the SM's
+  // previous CTA to release its columns: they stream in under that CTA's tail.
+  auto load_y = [&](int i) {
+    const int s = i % kYStages;
+    uint8_t* y1 = smem + L::kYOff + s * L::kStageBytes;
+    uint8_t* y2 = y1 + L::kYBytes;
+    mbar_arrive_expect_tx(&y_full[s], 2 * L::kYBytes + (IS_DKV ? L::kStatBytes : 0));
+    const int yrow = (j0 + i) * BY;
+#pragma unroll
+    for (int c = 0; c < L::kChunks; ++c) {
+      tma_load_4d(y1 + c * (BY * 128), &ty1, &y_full[s], c * 64, yrow, hh, bb);
+      tma_load_4d(y2 + c * (BY * 128), &ty2, &y_full[s], c * 64, yrow, hh, bb);
+    }
+    if constexpr (IS_DKV) {
+      float* st = reinterpret_cast<float*>(y2 + L::kYBytes);
+      tma_load_2d(st, &tlse, &y_full[s], yrow, bh);
+      tma_load_2d(st + BY, &tdelta, &y_full[s], yrow, bh);
+    }
+  };
+  const int n_pre = min(n_y, kYStages);
+  if (threadIdx.x == 0 && n_y > 0) {
+    tma_prefetch_desc(&tx1);
+    tma_prefetch_desc(&tx2);
+    tma_prefetch_desc(&ty1);
+    tma_prefetch_desc(&ty2);
+    mbar_arrive_expect_tx(x_full, 2 * L::kXBytes);
+#pragma unroll
+    for (int c = 0; c < L::kChunks; ++c) {
+      tma_load_4d(smem + L::kX1Off + c * (BX * 128), &tx1, x_full, c * 64, x0, hh, bb);
+      tma_load_4d(smem + L::kX2Off + c * (BX * 128), &tx2, x_full, c * 64, x0, hh, bb);
+    }
+    for (int i = 0; i < n_pre; ++i) load_y(i);
+  }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
@@ -850,33 +901,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   if (warp == 0) {
     if (lane == 0 && n_y > 0) {
-      tma_prefetch_desc(&tx1);
-      tma_prefetch_desc(&tx2);
-      tma_prefetch_desc(&ty1);
-      tma_prefetch_desc(&ty2);
-      mbar_arrive_expect_tx(x_full, 2 * L::kXBytes);
-#pragma unroll
-      for (int c = 0; c < L::kChunks; ++c) {
-        tma_load_4d(smem + L::kX1Off + c * (BX * 128), &tx1, x_full, c * 64, x0, hh, bb);
-        tma_load_4d(smem + L::kX2Off + c * (BX * 128), &tx2, x_full, c * 64, x0, hh, bb);
-      }
-      for (int i = 0; i < n_y; ++i) {
-        const int s = i % kYStages;
-        if (!mbar_wait(&y_empty[s], ((i / kYStages) & 1) ^ 1, abort, 20)) break;
-        uint8_t* y1 = smem + L::kYOff + s * L::kStageBytes;
-        uint8_t* y2 = y1 + L::kYBytes;
-        mbar_arrive_expect_tx(&y_full[s], 2 * L::kYBytes + (IS_DKV ? L::kStatBytes : 0));
-        const int yrow = (j0 + i) * BY;
-#pragma unroll
-        for (int c = 0; c < L::kChunks; ++c) {
-          tma_load_4d(y1 + c * (BY * 128), &ty1, &y_full[s], c * 64, yrow, hh, bb);
-          tma_load_4d(y2 + c * (BY * 128), &ty2, &y_full[s], c * 64, yrow, hh, bb);
-        }
-        if constexpr (IS_DKV) {
-          float* st = reinterpret_cast<float*>(y2 + L::kYBytes);
-          tma_load_2d(st, &tlse, &y_full[s], yrow, bh);
-          tma_load_2d(st + BY, &tdelta, &y_full[s], yrow, bh);
-        }
+      for (int i = n_pre; i < n_y; ++i) {
+        if (!mbar_wait(&y_empty[i % kYStages], ((i / kYStages) & 1) ^ 1, abort, 20)) break;
+        load_y(i);
       }
     }
   } else if (warp == 1) {

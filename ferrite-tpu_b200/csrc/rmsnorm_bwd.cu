@@ -310,29 +310,33 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// dw[e] = sum_p partial[p][e] in a fixed order (bitwise deterministic).  A CTA
-// owns 32 columns; its 32 warps each sum every 32nd partial row (coalesced
-// 128-byte rows, four independent loads in flight per thread), then warp 0 adds
-// the 32 warp results in order.
+// dw = sum of the nparts partial rows, in a fixed order (bitwise deterministic).
+// CTA = 16 columns x 32 row groups; each thread issues all of its partial loads
+// (up to 16, rows ty, ty + 32, ...) before summing them in order, so the
+// reduction costs one round of L2 latency instead of one per load; the 32 row
+// groups are then added in order through shared memory.
+constexpr int kDwCols = 16;
 template <typename TW>
-__global__ void __launch_bounds__(1024)
+__global__ void __launch_bounds__(512)
     dw_reduce_kernel(const float* __restrict__ partial, TW* __restrict__ dw,
                      int nparts, int dim) {
-  __shared__ float sm[32][33];
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  const int e = blockIdx.x * 32 + tx;
-  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+  __shared__ float sm[32][kDwCols + 1];
+  const int tx = threadIdx.x % kDwCols, ty = threadIdx.x / kDwCols;
+  const int e = blockIdx.x * kDwCols + tx;
+  float acc = 0.f;
   if (e < dim) {
-    int p = ty;
-    for (; p + 96 < nparts; p += 128) {
-      a0 += partial[(int64_t)p * dim + e];
-      a1 += partial[(int64_t)(p + 32) * dim + e];
-      a2 += partial[(int64_t)(p + 64) * dim + e];
-      a3 += partial[(int64_t)(p + 96) * dim + e];
+    for (int p0 = 0; p0 < nparts; p0 += 32 * 16) {
+      float v[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const int p = p0 + ty + 32 * k;
+        v[k] = p < nparts ? partial[(int64_t)p * dim + e] : 0.f;
+      }
+#pragma unroll
+      for (int k = 0; k < 16; ++k) acc += v[k];
     }
-    for (; p < nparts; p += 32) a0 += partial[(int64_t)p * dim + e];
   }
-  sm[ty][tx] = (a0 + a1) + (a2 + a3);
+  sm[ty][tx] = acc;
   __syncthreads();
   if (ty == 0 && e < dim) {
     float t = 0.f;
@@ -514,7 +518,7 @@ static int run_bwd(cudaStream_t s, const void* h, const void* w, const void* dy,
         (float*)ws, rows, (int)dim, eps);
   }
   if (int rc = check_launch("rmsnorm_bwd")) return rc;
-  dw_reduce_kernel<TW><<<(unsigned)((dim + 31) / 32), 1024, 0, s>>>(
+  dw_reduce_kernel<TW><<<(unsigned)((dim + kDwCols - 1) / kDwCols), 512, 0, s>>>(
       (const float*)ws, (TW*)dw, p.nparts, (int)dim);
   return check_launch("rmsnorm_dw_reduce");
 }
@@ -609,7 +613,7 @@ static int run_bwd_noalloc(cudaStream_t s, const void* h, const void* w, const v
         (const T*)h, (const TW*)w, (const T*)dy, (const T*)dhd, (T*)dh, part, rows, (int)dim, eps);
   }
   if (int rc = check_launch("rmsnorm_bwd_noalloc")) return rc;
-  dw_reduce_kernel<TW><<<(unsigned)((dim + 31) / 32), 1024, 0, s>>>(part, (TW*)dw, p.nparts, (int)dim);
+  dw_reduce_kernel<TW><<<(unsigned)((dim + kDwCols - 1) / kDwCols), 512, 0, s>>>(part, (TW*)dw, p.nparts, (int)dim);
   return check_launch("rmsnorm_bwd_noalloc_dw_reduce");
 }
 
