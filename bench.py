@@ -27,7 +27,10 @@ Workloads (synthetic inputs, seeded):
 
 Timing: W untimed warm-up steps, an untimed pre-roll (~0.6 s) while nvidia-smi
 starts sampling clocks, then exactly K steps between a barrier + synchronize on
-both sides, CUDA events on the launching stream, max over ranks.  ``e2e``
+both sides, CUDA events on the launching stream around the region only, max over
+ranks.  The per-kernel times behind ``roofline`` come from a second pass of the same
+K steps with events recorded between the kernels (those events serialise the
+kernels, so they stay out of the headline region).  ``e2e``
 repeats the measurement through the public API with pinned host inputs copied
 in and results copied out every step.
 
@@ -810,10 +813,18 @@ def run_ours(args, ws, rank, local):
         for i in range(n_pre):
             wl.step(i)
         sync_all()
+        # value: the K steps back to back, with events only around the whole region
+        # (an event recorded between two kernels serialises them and costs ~5 us)
         start.record()
         for i in range(args.steps):
-            wl.step(i, evs[i])
+            wl.step(i)
         stop.record()
+        torch.cuda.synchronize(dev)
+        sync_all()
+        # per-kernel breakdown (roofline): a second pass of the same K steps with
+        # events between the kernels
+        for i in range(args.steps):
+            wl.step(i, evs[i])
         torch.cuda.synchronize(dev)
     ms = start.elapsed_time(stop)
     bd = wl.breakdown(evs)
@@ -878,6 +889,7 @@ def run_ours(args, ws, rank, local):
             "frac": round(achieved / peak, 4),
             "peak_source": f"{pk.source} (MEASURED_PEAKS.json {psrc})" if pk.source == "measured" else "fallback",
             "traffic": _load_traffic(dom),
+            "timing": "kernel times from a second pass of the same K steps with CUDA events between kernels",
             "kernels_ms": {k: round(v, 5) for k, v in bd.items()},
         },
         "e2e": {"value": round(e2e_value, 3), "unit": wl.unit, "h2d_bytes_per_step": wl.h2d_bytes, "d2h_bytes_per_step": wl.d2h_bytes, "api": wl.e2e_api},

@@ -39,6 +39,8 @@ __device__ __forceinline__ float block_sum(float v, float* sm) {
 
 __global__ void __launch_bounds__(kThreads)
     sumsq_partials_kernel(const float* __restrict__ g, int64_t n, float gs, float* __restrict__ partials) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ float sm[kThreads / 32];
   const int64_t nv = n / 4;
   const int64_t stride = (int64_t)gridDim.x * kThreads;
@@ -74,6 +76,8 @@ __global__ void __launch_bounds__(kThreads)
     adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
                  float* __restrict__ v, int64_t n, int64_t n_decay, const float* __restrict__ partials,
                  int n_partials, Hyper h, float* __restrict__ gnorm_out) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ float sm[kThreads / 32];
   __shared__ float s_scale;
   // identical fixed-order reduction of the partials in every CTA
@@ -142,7 +146,7 @@ int ferrite_adamw_step(void* stream, float* params, const float* grads, float* m
       return fail(FERRITE_BAD_ALIGNMENT, "adamw_step: buffers must be 16-byte aligned");
   cudaStream_t s = (cudaStream_t)stream;
   float* partials = static_cast<float*>(workspace);
-  sumsq_partials_kernel<<<np, kThreads, 0, s>>>(grads, n, grad_scale, partials);
+  (void)launch_pdl(sumsq_partials_kernel, dim3(np), dim3(kThreads), 0, s, grads, n, grad_scale, partials);
   if (int rc = check_launch("adamw_sumsq")) return rc;
   Hyper h;
   h.lr = lr;
@@ -155,7 +159,7 @@ int ferrite_adamw_step(void* stream, float* params, const float* grads, float* m
   h.clip = clip;
   h.gs = grad_scale;
   const int grid = std::min<int64_t>((n / 4 + kThreads - 1) / kThreads + 1, (int64_t)num_sms(current_device()) * 8);
-  adamw_kernel<<<grid, kThreads, 0, s>>>(params, grads, m, v, n, n_decay, partials, np, h, gnorm_out);
+  (void)launch_pdl(adamw_kernel, dim3(grid), dim3(kThreads), 0, s, params, grads, m, v, n, n_decay, partials, np, h, gnorm_out);
   return check_launch("adamw_update");
 }
 

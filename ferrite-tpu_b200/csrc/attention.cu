@@ -65,6 +65,8 @@ template <typename T>
 __global__ void __launch_bounds__(256)
     bwd_prep_kernel(const T* __restrict__ dout, const T* __restrict__ out,
                     float* __restrict__ delta, Bhsd ld, Bhsd lo, int64_t rows, int s_len, int d) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -90,6 +92,8 @@ template <typename T, int VPR>
 __global__ void __launch_bounds__(256)
     bwd_prep_vec_kernel(const T* __restrict__ dout, const T* __restrict__ out,
                         float* __restrict__ delta, Bhsd ld, Bhsd lo, int s_len) {
+  pdl_launch_dependents();
+  pdl_wait();
   constexpr int kElems = 16 / sizeof(T);
   constexpr int kRowsPerPass = 256 / VPR;
   constexpr int kPasses = prep_rows_per_cta(VPR) / kRowsPerPass;
@@ -136,6 +140,8 @@ __global__ void __launch_bounds__(kSimtWarps * 32)
                     const T* __restrict__ v, T* __restrict__ o, float* __restrict__ lse,
                     Bhsd lq, Bhsd lk, Bhsd lv, Bhsd lo, int sq, int sk, int d, float scale,
                     int causal) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ float qs[kSimtWarps][kSimtMaxD];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t bh = blockIdx.y;
@@ -207,6 +213,8 @@ __global__ void __launch_bounds__(kSimtWarps * 32)
                        const float* __restrict__ lse, const float* __restrict__ delta,
                        T* __restrict__ dq, Bhsd lq, Bhsd lk, Bhsd lv, Bhsd ldo, Bhsd ldq,
                        int sq, int sk, int d, float scale, int causal) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ float qs[kSimtWarps][kSimtMaxD];
   __shared__ float ds_[kSimtWarps][kSimtMaxD];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -273,6 +281,8 @@ __global__ void __launch_bounds__(kSimtWarps * 32)
                         T* __restrict__ dk, T* __restrict__ dv, Bhsd lq, Bhsd lk, Bhsd lv,
                         Bhsd ldo, Bhsd ldk, Bhsd ldv, int sq, int sk, int d, float scale,
                         int causal) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ float ks[kSimtWarps][kSimtMaxD];
   __shared__ float vs[kSimtWarps][kSimtMaxD];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -458,6 +468,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       tma_prefetch_desc(&tq);
       tma_prefetch_desc(&tk);
       tma_prefetch_desc(&tv);
+      pdl_wait();  // q, k, v may come from the previous kernel in the stream
       mbar_arrive_expect_tx(q_full, 2 * L::kQBytes);
 #pragma unroll
       for (int g = 0; g < 2; ++g)
@@ -487,6 +498,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_launch_dependents();  // every CTA holds its TMEM before the next kernel is scheduled
+  pdl_wait();
   if (warp == 0) {
     if (lane == 0 && n_kv > 0) {
       // K runs one tile ahead of V: K0, K1, V0 (issued above), K2, V1, K3, V2, ...
@@ -873,6 +886,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     tma_prefetch_desc(&tx2);
     tma_prefetch_desc(&ty1);
     tma_prefetch_desc(&ty2);
+    pdl_wait();  // the inputs may come from the previous kernel in the stream
     mbar_arrive_expect_tx(x_full, 2 * L::kXBytes);
 #pragma unroll
     for (int c = 0; c < L::kChunks; ++c) {
@@ -889,6 +903,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_launch_dependents();  // every CTA holds its TMEM before the next kernel is scheduled
+  pdl_wait();
   // TMEM columns: T1[2] at 0/64, T2[2] at 128/192, acc0 at 256, then
   //   dK/dV: acc1 at 256 + D;
   //   dQ:    Q and dO as packed 16-bit pairs (A operands of the T MMAs, read from
@@ -1261,6 +1277,8 @@ __global__ void __launch_bounds__(kDqThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_launch_dependents();  // every CTA holds its TMEM before the next kernel is scheduled
+  pdl_wait();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -1450,7 +1468,7 @@ static int launch_fwd_tc(cudaStream_t s, const void* q, const void* k, const voi
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
   if (e != cudaSuccess) return fail(FERRITE_LAUNCH_FAILED, "attn_fwd: smem attr: %s", cudaGetErrorString(e));
   dim3 grid(p.nq_blocks, (unsigned)(b * h));
-  kern<<<grid, kFwdThreads, L::kTotal, s>>>(tq, tk, tv, p);
+  (void)launch_pdl(kern, dim3(grid), dim3(kFwdThreads), L::kTotal, s, tq, tk, tv, p);
   return check_launch("attn_fwd_tc");
 }
 
@@ -1530,7 +1548,7 @@ static int launch_bwd_tc(cudaStream_t s, const BwdArgs& a, int64_t b, int64_t h,
     if (rc) return rc;
   }
   dim3 grid(p.n_x_tiles, (unsigned)nbh);
-  kern<<<grid, kBwdThreads, L::kTotal, s>>>(tx1, tx2, ty1, ty2, tl, td, tds, p);
+  (void)launch_pdl(kern, dim3(grid), dim3(kBwdThreads), L::kTotal, s, tx1, tx2, ty1, ty2, tl, td, tds, p);
   return check_launch(IS_DKV ? "attn_bwd_dkv_tc" : "attn_bwd_dq_tc");
 }
 
@@ -1572,7 +1590,7 @@ static int launch_dq_ds(cudaStream_t s, const BwdArgs& a, int64_t b, int64_t h, 
   if (e != cudaSuccess) return fail(FERRITE_LAUNCH_FAILED, "attn_dq_ds: smem attr: %s", cudaGetErrorString(e));
   const int64_t units = (int64_t)p.n_q_tiles * nbh;
   const int grid = (int)std::min<int64_t>(units, num_sms(current_device()));
-  kern<<<grid, kDqThreads, L::kTotal, s>>>(tds, tk, p);
+  (void)launch_pdl(kern, dim3(grid), dim3(kDqThreads), L::kTotal, s, tds, tk, p);
   return check_launch("attn_dq_ds");
 }
 
@@ -1614,7 +1632,7 @@ static int attn_fwd_impl(cudaStream_t s, const void* q, const void* k, const voi
   }
   dim3 grid((unsigned)((sq + kSimtWarps - 1) / kSimtWarps), (unsigned)(b * h));
 #define FWD(T)                                                                                  \
-  simt_fwd_kernel<T><<<grid, kSimtWarps * 32, 0, s>>>((const T*)q, (const T*)k, (const T*)v,    \
+  (void)launch_pdl(simt_fwd_kernel<T>, dim3(grid), dim3(kSimtWarps * 32), 0, s, (const T*)q, (const T*)k, (const T*)v,    \
                                                        (T*)o, lse, lq, lk, lv, lo, (int)sq,     \
                                                        (int)sk, (int)d, scale, causal)
   if (dtype == FERRITE_F32) FWD(float);
@@ -1644,17 +1662,17 @@ static int launch_prep(cudaStream_t s, const void* dout, const void* out, float*
     const T* a = (const T*)dout;
     const T* o = (const T*)out;
     switch (vpr) {
-      case 1: bwd_prep_vec_kernel<T, 1><<<grid, 256, 0, s>>>(a, o, delta, ld, lo, (int)s_); break;
-      case 2: bwd_prep_vec_kernel<T, 2><<<grid, 256, 0, s>>>(a, o, delta, ld, lo, (int)s_); break;
-      case 4: bwd_prep_vec_kernel<T, 4><<<grid, 256, 0, s>>>(a, o, delta, ld, lo, (int)s_); break;
-      case 8: bwd_prep_vec_kernel<T, 8><<<grid, 256, 0, s>>>(a, o, delta, ld, lo, (int)s_); break;
-      case 16: bwd_prep_vec_kernel<T, 16><<<grid, 256, 0, s>>>(a, o, delta, ld, lo, (int)s_); break;
-      default: bwd_prep_vec_kernel<T, 32><<<grid, 256, 0, s>>>(a, o, delta, ld, lo, (int)s_); break;
+      case 1: (void)launch_pdl(bwd_prep_vec_kernel<T, 1>, dim3(grid), dim3(256), 0, s, a, o, delta, ld, lo, (int)s_); break;
+      case 2: (void)launch_pdl(bwd_prep_vec_kernel<T, 2>, dim3(grid), dim3(256), 0, s, a, o, delta, ld, lo, (int)s_); break;
+      case 4: (void)launch_pdl(bwd_prep_vec_kernel<T, 4>, dim3(grid), dim3(256), 0, s, a, o, delta, ld, lo, (int)s_); break;
+      case 8: (void)launch_pdl(bwd_prep_vec_kernel<T, 8>, dim3(grid), dim3(256), 0, s, a, o, delta, ld, lo, (int)s_); break;
+      case 16: (void)launch_pdl(bwd_prep_vec_kernel<T, 16>, dim3(grid), dim3(256), 0, s, a, o, delta, ld, lo, (int)s_); break;
+      default: (void)launch_pdl(bwd_prep_vec_kernel<T, 32>, dim3(grid), dim3(256), 0, s, a, o, delta, ld, lo, (int)s_); break;
     }
     return check_launch("attn_bwd_prep");
   }
   const int64_t rows = b * h * s_;
-  bwd_prep_kernel<T><<<(unsigned)((rows + 7) / 8), 256, 0, s>>>((const T*)dout, (const T*)out, delta, ld,
+  (void)launch_pdl(bwd_prep_kernel<T>, dim3((unsigned)((rows + 7) / 8)), dim3(256), 0, s, (const T*)dout, (const T*)out, delta, ld,
                                                                  lo, rows, (int)s_, (int)d);
   return check_launch("attn_bwd_prep");
 }
@@ -1684,7 +1702,7 @@ static int attn_bwd_dkv_impl(cudaStream_t s, const BwdArgs& a, int64_t b, int64_
     return dispatch_bwd_tc<true>(s, a, b, h, sq, sk, d, scale, causal, dtype);
   dim3 grid((unsigned)((sk + kSimtWarps - 1) / kSimtWarps), (unsigned)(b * h));
 #define DKV(T)                                                                                  \
-  simt_bwd_dkv_kernel<T><<<grid, kSimtWarps * 32, 0, s>>>(                                      \
+  (void)launch_pdl(simt_bwd_dkv_kernel<T>, dim3(grid), dim3(kSimtWarps * 32), 0, s,                                       \
       (const T*)a.q, (const T*)a.k, (const T*)a.v, (const T*)a.dout, a.lse, a.delta,            \
       (T*)a.out0, (T*)a.out1, a.lq, a.lk, a.lv, a.ldo, a.l0, a.l1, (int)sq, (int)sk, (int)d,    \
       scale, causal)
@@ -1701,7 +1719,7 @@ static int attn_bwd_dq_impl(cudaStream_t s, const BwdArgs& a, int64_t b, int64_t
     return dispatch_bwd_tc<false>(s, a, b, h, sq, sk, d, scale, causal, dtype);
   dim3 grid((unsigned)((sq + kSimtWarps - 1) / kSimtWarps), (unsigned)(b * h));
 #define DQ(T)                                                                                    \
-  simt_bwd_dq_kernel<T><<<grid, kSimtWarps * 32, 0, s>>>(                                        \
+  (void)launch_pdl(simt_bwd_dq_kernel<T>, dim3(grid), dim3(kSimtWarps * 32), 0, s,                                         \
       (const T*)a.q, (const T*)a.k, (const T*)a.v, (const T*)a.dout, a.lse, a.delta, (T*)a.out0, \
       a.lq, a.lk, a.lv, a.ldo, a.l0, (int)sq, (int)sk, (int)d, scale, causal)
   if (dtype == FERRITE_F32) DQ(float);

@@ -82,6 +82,26 @@ int check_launch(const char* what) {
   return FERRITE_OK;
 }
 
+cudaError_t launch_k(const void* func, dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                     void** args) {
+  static const bool pdl = [] {
+    const char* e = std::getenv("FERRITE_PDL");
+    return !(e && *e && std::atoi(e) == 0);
+  }();
+  if (!pdl) return cudaLaunchKernel(func, grid, block, args, smem, s);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelExC(&cfg, func, args);
+}
+
 static int load_encoder() {
   std::lock_guard<std::mutex> lock(g_mu);
   if (g_encode_tiled) return FERRITE_OK;

@@ -34,6 +34,29 @@ int current_device();
 int injected_fault(const char* op);
 // Checks cudaGetLastError() after a launch.
 int check_launch(const char* what);
+
+// Kernel launch with programmatic dependent launch (PDL) allowed: the kernel may
+// be scheduled while the previous kernel in the stream is still finishing (its
+// CTAs run their set-up, then wait in pdl_wait() until that kernel has completed
+// and its memory is visible).  Hides the launch gap and the ramp-up between the
+// back-to-back kernels of a step.  FERRITE_PDL=0 launches plainly.  Returns the
+// launch's cudaError_t.
+cudaError_t launch_k(const void* func, dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                     void** args);
+
+template <typename... KP>
+inline cudaError_t launch_pdl_impl(void (*kern)(KP...), dim3 grid, dim3 block, size_t smem,
+                                   cudaStream_t s, KP... v) {
+  void* ptrs[sizeof...(KP) > 0 ? sizeof...(KP) : 1] = {(void*)&v...};
+  return launch_k((const void*)kern, grid, block, smem, s, ptrs);
+}
+// launch_pdl(kernel, grid, block, smem, stream, args...): arguments converted to
+// the kernel's parameter types.
+template <typename... KP, typename... A>
+inline cudaError_t launch_pdl(void (*kern)(KP...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t s, A&&... a) {
+  return launch_pdl_impl<KP...>(kern, grid, block, smem, s, static_cast<KP>(a)...);
+}
 // Encodes a 2-D tiled TMA descriptor (inner dimension first) with 128-byte
 // swizzle; returns 0 or a FERRITE_* code with the error set.
 int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
@@ -120,6 +143,16 @@ __device__ __forceinline__ void st_v4(void* p, uint4 v) {
 __device__ __forceinline__ void st_stream_v4(void* p, uint4 v) {
   __stcs(reinterpret_cast<uint4*>(p), v);
 }
+
+// Programmatic dependent launch, device side.  pdl_launch_dependents(): this CTA
+// lets the next kernel in the stream be scheduled (it runs once every CTA of this
+// grid has started or exited).  pdl_wait(): block until the previous kernel in the
+// stream has completed and its writes are visible; every thread calls it before
+// its first global-memory access.  Both are no-ops for a plain launch.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;

@@ -317,6 +317,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // PDL: every CTA holds its TMEM before the next kernel may be scheduled; no
+  // global memory is touched before the previous kernel has completed.
+  pdl_launch_dependents();
+  pdl_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -465,6 +469,8 @@ template <typename TC>
 __global__ void __launch_bounds__(256)
     splitk_reduce_kernel(const float* __restrict__ ws, TC* __restrict__ c, int m, int n,
                          int64_t ldc, int splits) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t plane = (int64_t)m * n;
   const int groups = (n + 3) / 4;
   const int64_t total = (int64_t)m * groups;
@@ -512,6 +518,8 @@ __global__ void __launch_bounds__(256)
     gemm_simt_kernel(const TA* __restrict__ a, const TA* __restrict__ b, TC* __restrict__ c,
                      int m, int n, int k, int64_t lda, int64_t ldb, int64_t ldc,
                      int trans_a, int trans_b) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ float As[2][SB_K][SB_M + 4];
   __shared__ float Bs[2][SB_K][SB_N + 4];
   const int tid = threadIdx.x;
@@ -612,7 +620,7 @@ static int launch_simt(cudaStream_t s, const void* a, const void* b, void* c, in
                        int ta, int tb) {
   dim3 grid((unsigned)((n + SB_N - 1) / SB_N), (unsigned)((m + SB_M - 1) / SB_M));
   if (grid.y > 65535) return fail(FERRITE_BAD_SHAPE, "gemm: M too large for the CUDA-core path");
-  gemm_simt_kernel<TA, TC><<<grid, 256, 0, s>>>((const TA*)a, (const TA*)b, (TC*)c, (int)m,
+  (void)launch_pdl(gemm_simt_kernel<TA, TC>, dim3(grid), dim3(256), 0, s, (const TA*)a, (const TA*)b, (TC*)c, (int)m,
                                                  (int)n, (int)k, lda, ldb, ldc, ta, tb);
   return check_launch("gemm_simt");
 }
@@ -625,7 +633,7 @@ static int launch_tc(cudaStream_t s, const CUtensorMap& ta, const CUtensorMap& t
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess)
     return fail(FERRITE_LAUNCH_FAILED, "gemm: smem attribute: %s", cudaGetErrorString(e));
-  kern<<<grid, kThreads, smem, s>>>(ta, tb, tc, taux, p);
+  (void)launch_pdl(kern, dim3(grid), dim3(kThreads), smem, s, ta, tb, tc, taux, p);
   return check_launch("gemm_tc");
 }
 
@@ -702,7 +710,7 @@ static int launch_reduce(cudaStream_t s, const float* ws, void* c, int64_t m, in
   const int64_t groups = m * ((n + 3) / 4);
   const int64_t want = (groups + 255) / 256;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(want, (int64_t)sms * 8));
-  splitk_reduce_kernel<TC><<<grid, 256, 0, s>>>(ws, (TC*)c, (int)m, (int)n, ldc, splits);
+  (void)launch_pdl(splitk_reduce_kernel<TC>, dim3(grid), dim3(256), 0, s, ws, (TC*)c, (int)m, (int)n, ldc, splits);
   return check_launch("gemm_splitk_reduce");
 }
 

@@ -29,6 +29,8 @@ __global__ void __launch_bounds__(CTA, CTA <= 512 ? 2 : 1)
   const int grp = threadIdx.x / TPR;
   const int nvec = dim / VE;
   const float inv_dim = 1.0f / (float)dim;
+  pdl_launch_dependents();
+  pdl_wait();
 
   float dwp[VPT][VE];
 #pragma unroll
@@ -188,6 +190,8 @@ __global__ void __launch_bounds__(NC + 32, NC >= 512 ? 2 : 4)
     fence_mbar_init();
   }
   __syncthreads();
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t first = blockIdx.x, stride = gridDim.x;
   const int64_t my_rows = first < rows ? (rows - first + stride - 1) / stride : 0;
   auto stage = [&](int s, int t) { return smem + (s * NT + t) * ROW_BYTES; };
@@ -278,6 +282,8 @@ __global__ void __launch_bounds__(256)
   const int wib = threadIdx.x >> 5;
   const int64_t gw = (int64_t)blockIdx.x * 8 + wib;
   const int64_t nw = (int64_t)gridDim.x * 8;
+  pdl_launch_dependents();
+  pdl_wait();
   float* my = partial + gw * dim;
   for (int j = lane; j < dim; j += 32) my[j] = 0.f;
   const float inv_dim = 1.0f / (float)dim;
@@ -323,6 +329,8 @@ __global__ void __launch_bounds__(512)
   __shared__ float sm[32][kDwCols + 1];
   const int tx = threadIdx.x % kDwCols, ty = threadIdx.x / kDwCols;
   const int e = blockIdx.x * kDwCols + tx;
+  pdl_launch_dependents();
+  pdl_wait();
   float acc = 0.f;
   if (e < dim) {
     for (int p0 = 0; p0 < nparts; p0 += 32 * 16) {
@@ -477,7 +485,7 @@ static int launch_tma(const BwdPlan& p, cudaStream_t s, const void* h, const voi
                       const void* dy, const void* dhd, void* dh, float* part, int64_t rows,
                       float eps) {
   void* args[] = {&h, &w, &dy, &dhd, &dh, &part, &rows, &eps};
-  cudaError_t e = cudaLaunchKernel(p.tma_kernel, dim3(p.grid), dim3(p.tma_threads), args, p.smem, s);
+  cudaError_t e = launch_k(p.tma_kernel, dim3(p.grid), dim3(p.tma_threads), p.smem, s, args);
   if (e != cudaSuccess)
     return fail(FERRITE_LAUNCH_FAILED, "rmsnorm_bwd (tma): %s", cudaGetErrorString(e));
   return FERRITE_OK;
@@ -509,17 +517,19 @@ static int run_bwd(cudaStream_t s, const void* h, const void* w, const void* dy,
     T* dhp = (T*)dh;
     float* part = (float*)ws;
     void* args[] = {&hp, &wp, &dyp, &dhdp, &dhp, &part, &rows, &dimi, &eps};
-    cudaError_t e = cudaLaunchKernel(k, dim3(p.grid), dim3(CTA), args, p.smem, s);
+    cudaError_t e = launch_k(k, dim3(p.grid), dim3(CTA), p.smem, s, args);
     if (e != cudaSuccess)
       return fail(FERRITE_LAUNCH_FAILED, "rmsnorm_bwd: %s", cudaGetErrorString(e));
   } else {
-    rmsnorm_bwd_scalar<T, TW, HAS_DH><<<p.grid, 256, 0, s>>>(
-        (const T*)h, (const TW*)w, (const T*)dy, (const T*)dhd, (T*)dh,
-        (float*)ws, rows, (int)dim, eps);
+    cudaError_t e = launch_pdl(rmsnorm_bwd_scalar<T, TW, HAS_DH>, dim3(p.grid), dim3(256), 0, s,
+                               (const T*)h, (const TW*)w, (const T*)dy, (const T*)dhd, (T*)dh,
+                               (float*)ws, rows, (int)dim, eps);
+    if (e != cudaSuccess) return fail(FERRITE_LAUNCH_FAILED, "rmsnorm_bwd: %s", cudaGetErrorString(e));
   }
   if (int rc = check_launch("rmsnorm_bwd")) return rc;
-  dw_reduce_kernel<TW><<<(unsigned)((dim + kDwCols - 1) / kDwCols), 512, 0, s>>>(
-      (const float*)ws, (TW*)dw, p.nparts, (int)dim);
+  cudaError_t e = launch_pdl(dw_reduce_kernel<TW>, dim3((unsigned)((dim + kDwCols - 1) / kDwCols)), dim3(512), 0, s,
+                             (const float*)ws, (TW*)dw, p.nparts, (int)dim);
+  if (e != cudaSuccess) return fail(FERRITE_LAUNCH_FAILED, "rmsnorm_dw_reduce: %s", cudaGetErrorString(e));
   return check_launch("rmsnorm_dw_reduce");
 }
 
@@ -605,15 +615,18 @@ static int run_bwd_noalloc(cudaStream_t s, const void* h, const void* w, const v
     const T* dhdp = (const T*)dhd;
     T* dhp = (T*)dh;
     void* args[] = {&hp, &wp, &dyp, &dhdp, &dhp, &part, &rows, &dimi, &eps};
-    cudaError_t e = cudaLaunchKernel(k, dim3(p.grid), dim3(CTA), args, p.smem, s);
+    cudaError_t e = launch_k(k, dim3(p.grid), dim3(CTA), p.smem, s, args);
     if (e != cudaSuccess)
       return fail(FERRITE_LAUNCH_FAILED, "rmsnorm_bwd_noalloc: %s", cudaGetErrorString(e));
   } else {
-    rmsnorm_bwd_scalar<T, TW, HAS_DH><<<p.grid, 256, 0, s>>>(
-        (const T*)h, (const TW*)w, (const T*)dy, (const T*)dhd, (T*)dh, part, rows, (int)dim, eps);
+    cudaError_t e = launch_pdl(rmsnorm_bwd_scalar<T, TW, HAS_DH>, dim3(p.grid), dim3(256), 0, s,
+                               (const T*)h, (const TW*)w, (const T*)dy, (const T*)dhd, (T*)dh, part, rows, (int)dim, eps);
+    if (e != cudaSuccess) return fail(FERRITE_LAUNCH_FAILED, "rmsnorm_bwd_noalloc: %s", cudaGetErrorString(e));
   }
   if (int rc = check_launch("rmsnorm_bwd_noalloc")) return rc;
-  dw_reduce_kernel<TW><<<(unsigned)((dim + kDwCols - 1) / kDwCols), 512, 0, s>>>(part, (TW*)dw, p.nparts, (int)dim);
+  cudaError_t e = launch_pdl(dw_reduce_kernel<TW>, dim3((unsigned)((dim + kDwCols - 1) / kDwCols)), dim3(512), 0, s,
+                             (const float*)part, (TW*)dw, p.nparts, (int)dim);
+  if (e != cudaSuccess) return fail(FERRITE_LAUNCH_FAILED, "rmsnorm_bwd_noalloc dw_reduce: %s", cudaGetErrorString(e));
   return check_launch("rmsnorm_bwd_noalloc_dw_reduce");
 }
 

@@ -21,6 +21,8 @@ __global__ void __launch_bounds__(CTA)
   const bool active = row < rows;
   const int nvec = dim / VE;
   const int64_t base = row * (int64_t)dim;
+  pdl_launch_dependents();
+  pdl_wait();
 
   float hv[VPT][VE];
   float ss = 0.f;
@@ -72,7 +74,9 @@ __global__ void __launch_bounds__(256)
                        T* __restrict__ y, int64_t rows, int dim, float eps) {
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  pdl_launch_dependents();
   if (row >= rows) return;
+  pdl_wait();
   const int64_t base = row * (int64_t)dim;
   float ss = 0.f;
   for (int j = lane; j < dim; j += 32) {
@@ -101,8 +105,9 @@ static int launch_fwd_t(cudaStream_t s, const void* x, const void* r,
   constexpr int RPC = CTA / TPR;
   const int64_t grid = (rows + RPC - 1) / RPC;
   if (grid > 0x7fffffff) return fail(FERRITE_BAD_SHAPE, "rmsnorm: too many rows");
-  rmsnorm_fwd_kernel<T, TW, ADD, VPT, TPR, CTA><<<(unsigned)grid, CTA, 0, s>>>(
-      (const T*)x, (const T*)r, (const TW*)w, (T*)h, (T*)y, rows, dim, eps);
+  cudaError_t e = launch_pdl(rmsnorm_fwd_kernel<T, TW, ADD, VPT, TPR, CTA>, dim3((unsigned)grid), dim3(CTA), 0, s,
+                             (const T*)x, (const T*)r, (const TW*)w, (T*)h, (T*)y, rows, dim, eps);
+  if (e != cudaSuccess) return fail(FERRITE_LAUNCH_FAILED, "rmsnorm_fwd: launch failed: %s", cudaGetErrorString(e));
   return check_launch("rmsnorm_fwd");
 }
 
@@ -130,8 +135,9 @@ static int run_fwd(cudaStream_t s, const void* x, const void* r, const void* w,
   Cfg c = pick(dim, sizeof(T), ptrs, 5, false);
   if (!c.vec) {
     const int64_t grid = (rows + 7) / 8;
-    rmsnorm_fwd_scalar<T, TW, ADD><<<(unsigned)grid, 256, 0, s>>>(
-        (const T*)x, (const T*)r, (const TW*)w, (T*)h, (T*)y, rows, (int)dim, eps);
+    cudaError_t e = launch_pdl(rmsnorm_fwd_scalar<T, TW, ADD>, dim3((unsigned)grid), dim3(256), 0, s,
+                               (const T*)x, (const T*)r, (const TW*)w, (T*)h, (T*)y, rows, (int)dim, eps);
+    if (e != cudaSuccess) return fail(FERRITE_LAUNCH_FAILED, "rmsnorm_fwd_scalar: launch failed: %s", cudaGetErrorString(e));
     return check_launch("rmsnorm_fwd_scalar");
   }
   switch (c.vpt) {

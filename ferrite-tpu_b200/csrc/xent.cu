@@ -41,6 +41,8 @@ __global__ void __launch_bounds__(kThreads)
     xent_fwd_kernel(const float* __restrict__ logits, const void* __restrict__ targets,
                     float* __restrict__ lse, float* __restrict__ nll, int64_t vocab, int64_t ld,
                     int is64) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ float sm[kWarps], ss[kWarps];
   const int64_t r = blockIdx.x;
   const float* x = logits + r * ld;
@@ -104,6 +106,8 @@ __global__ void __launch_bounds__(kThreads)
     xent_bwd_kernel(const float* __restrict__ logits, const void* __restrict__ targets,
                     const float* __restrict__ lse, const float* __restrict__ dloss, float scale,
                     TO* __restrict__ dx, int64_t vocab, int64_t ld, int64_t ld_out, int is64) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t r = blockIdx.x;
   const float* x = logits + r * ld;
   TO* o = dx + r * ld_out;
@@ -146,10 +150,10 @@ static int launch_bwd(cudaStream_t s, const float* logits, const void* targets, 
                    (reinterpret_cast<uintptr_t>(logits) & 15u) == 0 &&
                    (reinterpret_cast<uintptr_t>(dx) & (sizeof(TO) * 4 - 1)) == 0;
   if (vec)
-    xent_bwd_kernel<TO, true><<<(unsigned)rows, kThreads, 0, s>>>(logits, targets, lse, dloss, scale,
+    (void)launch_pdl(xent_bwd_kernel<TO, true>, dim3((unsigned)rows), dim3(kThreads), 0, s, logits, targets, lse, dloss, scale,
                                                                   (TO*)dx, vocab, ld, ld_out, is64);
   else
-    xent_bwd_kernel<TO, false><<<(unsigned)rows, kThreads, 0, s>>>(logits, targets, lse, dloss, scale,
+    (void)launch_pdl(xent_bwd_kernel<TO, false>, dim3((unsigned)rows), dim3(kThreads), 0, s, logits, targets, lse, dloss, scale,
                                                                    (TO*)dx, vocab, ld, ld_out, is64);
   return check_launch("xent_bwd");
 }
@@ -170,9 +174,9 @@ int ferrite_xent_fwd(void* stream, const float* logits, const void* targets, flo
   cudaStream_t s = (cudaStream_t)stream;
   const bool vec = vocab % 4 == 0 && ld % 4 == 0 && (reinterpret_cast<uintptr_t>(logits) & 15u) == 0;
   if (vec)
-    xent_fwd_kernel<true><<<(unsigned)rows, kThreads, 0, s>>>(logits, targets, lse, nll, vocab, ld, target_dtype);
+    (void)launch_pdl(xent_fwd_kernel<true>, dim3((unsigned)rows), dim3(kThreads), 0, s, logits, targets, lse, nll, vocab, ld, target_dtype);
   else
-    xent_fwd_kernel<false><<<(unsigned)rows, kThreads, 0, s>>>(logits, targets, lse, nll, vocab, ld, target_dtype);
+    (void)launch_pdl(xent_fwd_kernel<false>, dim3((unsigned)rows), dim3(kThreads), 0, s, logits, targets, lse, nll, vocab, ld, target_dtype);
   return check_launch("xent_fwd");
 }
 
