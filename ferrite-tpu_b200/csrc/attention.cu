@@ -371,24 +371,28 @@ __global__ void __launch_bounds__(kSimtWarps * 32)
 //                keeps using the stale max (l and O share it, so O / l is
 //                unchanged up to rounding).  After the last tile O / l is stored
 //                and lse = (m + log2 l) * ln 2.
-// TMEM: S0 [0,128), S1 [128,256), O0 [256, 256+D), O1 [256+D, 256+2D).
+// TMEM: S0 [0,128), S1 [128,256), O0 [256, 256+D), O1 [256+D, 256+2D);
+// with one query tile per CTA (NG = 1): S0 [0,128), O0 [128, 128+D).
 // MMAs issued by one thread execute in issue order, so S_g(j+1) (which
 // overwrites the P_g(j) columns) is issued only after PV_g(j).
 
 constexpr int TQ = 128;  // query rows per tile (TMEM lanes)
 constexpr int TK = 128;  // keys per KV tile
-constexpr int kFwdThreads = 384;  // 12 warps
 constexpr float kRescaleLog2 = 8.0f;
 
-template <int D>
+// NG: query tiles (softmax groups) per CTA.  NG = 2 ping-pongs two groups on one
+// tensor core; NG = 1 (d = 64) uses 256 TMEM columns and ~81 KB of shared memory,
+// so two CTAs share an SM and overlap each other's set-up and epilogue -- what
+// dominates at short sequence lengths.
+template <int D, int NG = 2>
 struct FwdSmem {
   static constexpr int kChunks = D / 64;      // 128-byte swizzle chunks along d
   static constexpr int kQBytes = TQ * D * 2;  // one Q tile (K-major)
   static constexpr int kKBytes = TK * D * 2;  // K tile (K-major)
   static constexpr int kVBytes = TK * D * 2;  // V tile (MN-major for the B operand)
   static constexpr int kStageBytes = kKBytes + kVBytes;
-  static constexpr int kQOff = 0;  // Q0, Q1
-  static constexpr int kKVOff = 2 * kQBytes;
+  static constexpr int kQOff = 0;  // Q0 (, Q1)
+  static constexpr int kKVOff = NG * kQBytes;
   static constexpr int kBarOff = kKVOff + 2 * kStageBytes;
   // q_full, k_full[2], v_full[2], k_empty[2], v_empty[2], s_full[2], p_full[2], pv_done[2]
   static constexpr int kNumBars = 15;
@@ -402,7 +406,7 @@ struct FwdParams {
   void* o;
   Bhsd lo;     // output layout
   float* lse;  // [b*h, sq]
-  int nq_blocks;  // 256-row query blocks
+  int nq_blocks;  // query blocks of NG * 128 rows
 };
 
 // Byte offset of 16-byte granule `col_granule` of row `row` in a [rows x 64]
@@ -411,12 +415,23 @@ __device__ __forceinline__ uint32_t swz128(int row, int col_granule) {
   return (uint32_t)(row * 128 + ((col_granule ^ (row & 7)) << 4));
 }
 
-template <int D, bool BF16>
-__global__ void __launch_bounds__(kFwdThreads, 1)
+// Warps: 0 TMA producer, 1 MMA issuer, then 4 softmax warps per query tile (the
+// first at warp kSoftWarp0; a softmax warp reads TMEM lanes 32 * (warp % 4) on).
+// NG = 1 has no idle warps, so 192 threads x 2 CTAs leave 168 registers a thread.
+template <int NG>
+constexpr int fwd_soft_warp0() { return NG == 1 ? 2 : 4; }
+template <int NG>
+constexpr int fwd_threads() { return 32 * (fwd_soft_warp0<NG>() + 4 * NG); }
+template <int NG>
+constexpr int fwd_tmem_cols() { return NG == 2 ? 512 : 256; }
+
+template <int D, bool BF16, int NG>
+__global__ void __launch_bounds__(fwd_threads<NG>(), NG == 1 ? 2 : 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq,
                        const __grid_constant__ CUtensorMap tk,
                        const __grid_constant__ CUtensorMap tv, const FwdParams p) {
-  using L = FwdSmem<D>;
+  using L = FwdSmem<D, NG>;
+  constexpr uint32_t kOCol = NG * 128;  // O_g at kOCol + g * D (S_g at g * 128)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -440,11 +455,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const int qb = p.nq_blocks - 1 - (int)blockIdx.x;
   const int bh = blockIdx.y;
   const int hh = bh % p.lo.nh, bb = bh / p.lo.nh;  // TMA coordinates of the slice
-  const int q0 = qb * 2 * TQ;
+  const int q0 = qb * NG * TQ;
   const int diag_shift = p.sk - p.sq;  // causal: key <= query + diag_shift
   int n_kv = (p.sk + TK - 1) / TK;
   if (p.causal) {
-    const int last_key = min(p.sk - 1, q0 + 2 * TQ - 1 + diag_shift);
+    const int last_key = min(p.sk - 1, q0 + NG * TQ - 1 + diag_shift);
     n_kv = last_key < 0 ? 0 : last_key / TK + 1;
   }
 
@@ -469,9 +484,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       tma_prefetch_desc(&tk);
       tma_prefetch_desc(&tv);
       pdl_wait();  // q, k, v may come from the previous kernel in the stream
-      mbar_arrive_expect_tx(q_full, 2 * L::kQBytes);
+      mbar_arrive_expect_tx(q_full, NG * L::kQBytes);
 #pragma unroll
-      for (int g = 0; g < 2; ++g)
+      for (int g = 0; g < NG; ++g)
 #pragma unroll
         for (int c = 0; c < L::kChunks; ++c)
           tma_load_4d(smem + L::kQOff + g * L::kQBytes + c * (TQ * 128), &tq, q_full, c * 64,
@@ -491,7 +506,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
+    tmem_alloc(tmem_slot, fwd_tmem_cols<NG>());
     tmem_relinquish();
   }
   tc_fence_before();
@@ -550,17 +565,32 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const uint32_t pa = tmem + g * 128;  // P_g: packed pairs in S columns [0, 64)
 #pragma unroll
         for (int kk = 0; kk < TK / 16; ++kk)
-          tc_mma_f16_ts(tmem + 256 + g * D, pa + kk * 8, sdesc_at(dv, kk * 2048), idesc_o,
+          tc_mma_f16_ts(tmem + kOCol + g * D, pa + kk * 8, sdesc_at(dv, kk * 2048), idesc_o,
                         (j > 0 || kk > 0) ? 1u : 0u);
         tc_commit(&pv_done[g]);
       };
       if (ok) {
         tc_fence_after();
         issue_s(0, 0);
-        issue_s(1, 0);
+        if constexpr (NG == 2) issue_s(1, 0);
         tc_commit(&k_empty[0]);  // K_0 no longer read once both S_g(0) complete
       }
-      for (int j = 0; ok && j < n_kv; ++j) {
+      if constexpr (NG == 1) {
+        for (int j = 0; ok && j < n_kv; ++j) {
+          if (!mbar_wait(&p_full[0], j & 1, abort, 13)) break;
+          if (!mbar_wait(&v_full[j & 1], (j >> 1) & 1, abort, 18)) break;
+          tc_fence_after();
+          issue_pv(0, j);
+          tc_commit(&v_empty[j & 1]);
+          if (j + 1 < n_kv) {
+            if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort, 14)) break;
+            tc_fence_after();
+            issue_s(0, j + 1);
+            tc_commit(&k_empty[(j + 1) & 1]);
+          }
+        }
+      }
+      for (int j = 0; NG == 2 && ok && j < n_kv; ++j) {
         const bool more = j + 1 < n_kv;
         if (!mbar_wait(&p_full[0], j & 1, abort, 13)) break;
         if (!mbar_wait(&v_full[j & 1], (j >> 1) & 1, abort, 18)) break;
@@ -581,15 +611,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
       }
     }
-  } else if (warp >= 4) {
+  } else if (warp >= fwd_soft_warp0<NG>()) {
     // ------------------------------------------------ softmax groups
-    const int g = (warp - 4) >> 2;
+    const int g = (warp - fwd_soft_warp0<NG>()) >> 2;
     const int qw = warp & 3;
     const int r = qw * 32 + lane;  // row within the query tile == TMEM lane
     const int qrow = q0 + g * TQ + r;
     const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
     const uint32_t t_s = tmem + lane_off + g * 128;
-    const uint32_t t_o = tmem + lane_off + 256 + g * D;
+    const uint32_t t_o = tmem + lane_off + kOCol + g * D;
     float m_used = -INFINITY, l = 0.f;
     bool ok = n_kv > 0;
     for (int j = 0; ok && j < n_kv; ++j) {
@@ -722,7 +752,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, fwd_tmem_cols<NG>());
   }
 }
 
@@ -774,7 +804,9 @@ struct BwdSmem {
   // elementwise warp, 128-byte swizzle) that the TMA store reads; the two
   // elementwise groups hand it to each other tile by tile.
   static constexpr int kStgOff = kYOff + kYStages * kStageBytes;
-  static constexpr int kStgBytes = BX * BY * 2;
+  // D = 64 leaves room for one staging tile per group (no hand-off wait)
+  static constexpr bool kOwnStg = D == 64;
+  static constexpr int kStgBytes = BX * BY * 2 * (kOwnStg ? 2 : 1);
   static constexpr int kBarOff = kStgOff + kStgBytes;
   // x_full, y_full[S], y_empty[S], t_full[2], e_full[2], acc_full, x_tmem, stg_free
   static constexpr int kNumBars = 2 * kYStages + 8;
@@ -1114,11 +1146,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         // tile are already released.  Staged in shared memory (swizzled rows,
         // conflict-free) and written by one TMA store per warp.
         if (p.ds != nullptr) {
-          if (i > 0 && !mbar_wait(stg_free, (i - 1) & 1, abort, 31)) {
+          if constexpr (L::kOwnStg) {
+            if (lane == 0) bulk_wait_group_read0();  // this warp's store of two tiles ago
+            __syncwarp();
+          } else if (i > 0 && !mbar_wait(stg_free, (i - 1) & 1, abort, 31)) {
             ok = false;
             break;
           }
-          uint8_t* stg = smem + L::kStgOff + qw * 4096;
+          uint8_t* stg = smem + L::kStgOff + (L::kOwnStg ? g * (BX * BY * 2) : 0) + qw * 4096;
           uint8_t* row = stg + lane * 128;
 #pragma unroll
           for (int v = 0; v < BY / 8; ++v)
@@ -1132,8 +1167,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             const int key = x0 + qw * 32;
             tma_store_4d(&tds, stg, 0, key & 63, y0 >> 6, (int)blockIdx.y * (p.sk >> 6) + (key >> 6));
             bulk_commit_group();
-            bulk_wait_group_read0();  // staging read: hand it to the other group
-            mbar_arrive(stg_free);
+            if constexpr (!L::kOwnStg) {
+              bulk_wait_group_read0();  // staging read: hand it to the other group
+              mbar_arrive(stg_free);
+            }
           }
           __syncwarp();
         }
@@ -1443,12 +1480,12 @@ static int map_bhsd(CUtensorMap* m, const void* base, CUtensorMapDataType dt, in
   return make_tmap_4d(m, base, dt, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-template <int D, bool BF16>
-static int launch_fwd_tc(cudaStream_t s, const void* q, const void* k, const void* v,
+template <int D, bool BF16, int NG>
+static int launch_fwd_tc_ng(cudaStream_t s, const void* q, const void* k, const void* v,
                          void* o, float* lse, const Bhsd& lq, const Bhsd& lk, const Bhsd& lv,
                          const Bhsd& lo, int64_t b, int64_t h, int64_t sq, int64_t sk,
                          float scale, int causal) {
-  using L = FwdSmem<D>;
+  using L = FwdSmem<D, NG>;
   const CUtensorMapDataType dt = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap tq, tk, tv;
   int rc = map_bhsd(&tq, q, dt, D, lq, b, h, sq, TQ);
@@ -1463,13 +1500,27 @@ static int launch_fwd_tc(cudaStream_t s, const void* q, const void* k, const voi
   p.o = o;
   p.lo = lo;
   p.lse = lse;
-  p.nq_blocks = (int)((sq + 2 * TQ - 1) / (2 * TQ));
-  auto kern = attn_fwd_tc_kernel<D, BF16>;
+  p.nq_blocks = (int)((sq + NG * TQ - 1) / (NG * TQ));
+  auto kern = attn_fwd_tc_kernel<D, BF16, NG>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
   if (e != cudaSuccess) return fail(FERRITE_LAUNCH_FAILED, "attn_fwd: smem attr: %s", cudaGetErrorString(e));
   dim3 grid(p.nq_blocks, (unsigned)(b * h));
-  (void)launch_pdl(kern, dim3(grid), dim3(kFwdThreads), L::kTotal, s, tq, tk, tv, p);
+  (void)launch_pdl(kern, dim3(grid), dim3(fwd_threads<NG>()), L::kTotal, s, tq, tk, tv, p);
   return check_launch("attn_fwd_tc");
+}
+
+// d = 64 runs one query tile per CTA (two CTAs per SM) unless FERRITE_ATTN_FWD_NG=2;
+// d = 128 always pairs two tiles in one CTA (its 1-tile CTA would not fit twice).
+template <int D, bool BF16>
+static int launch_fwd_tc(cudaStream_t s, const void* q, const void* k, const void* v, void* o,
+                         float* lse, const Bhsd& lq, const Bhsd& lk, const Bhsd& lv, const Bhsd& lo,
+                         int64_t b, int64_t h, int64_t sq, int64_t sk, float scale, int causal) {
+  if constexpr (D == 64) {
+    static const bool pair = env_int("FERRITE_ATTN_FWD_NG", 1) == 2;
+    if (!pair)
+      return launch_fwd_tc_ng<D, BF16, 1>(s, q, k, v, o, lse, lq, lk, lv, lo, b, h, sq, sk, scale, causal);
+  }
+  return launch_fwd_tc_ng<D, BF16, 2>(s, q, k, v, o, lse, lq, lk, lv, lo, b, h, sq, sk, scale, causal);
 }
 
 // Operands of one backward call: the four inputs, the outputs and their layouts.
