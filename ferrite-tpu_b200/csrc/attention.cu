@@ -639,14 +639,25 @@ __global__ void __launch_bounds__(fwd_threads<NG>(), NG == 1 ? 2 : 1)
         tmem_ld32(t_s + 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[64]));
         tmem_ld32(t_s + 96, *reinterpret_cast<uint32_t(*)[32]>(&sv[96]));
         tmem_wait_ld();
+        // Eight independent chains of 3-input maxima (a single fmaxf chain over 128
+        // columns is latency-bound with two softmax warps per scheduler).
+        auto row_max = [&](auto val) {
+          float m[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) m[k] = fmaxf(val(2 * k), val(2 * k + 1));
+#pragma unroll
+          for (int i = 16; i < TK; i += 16)
+#pragma unroll
+            for (int k = 0; k < 8; ++k) m[k] = fmax3(m[k], val(i + 2 * k), val(i + 2 * k + 1));
+          return fmaxf(fmax3(m[0], m[1], m[2]), fmax3(fmax3(m[3], m[4], m[5]), m[6], m[7]));
+        };
         if (diag || !(p.scale_log2 > 0.f)) {
-#pragma unroll
-          for (int i = 0; i < TK; ++i)
-            mx = fmaxf(mx, (diag && i > kmax) ? kMaskValue : __uint_as_float(sv[i]) * p.scale_log2);
+          mx = row_max([&](int i) {
+            return (diag && i > kmax) ? kMaskValue : __uint_as_float(sv[i]) * p.scale_log2;
+          });
         } else {
-#pragma unroll
-          for (int i = 0; i < TK; ++i) mx = fmaxf(mx, __uint_as_float(sv[i]));
-          mx *= p.scale_log2;  // scale > 0: max commutes with the scaling
+          // scale > 0: max commutes with the scaling
+          mx = row_max([&](int i) { return __uint_as_float(sv[i]); }) * p.scale_log2;
         }
       }
       const float m_new = fmaxf(m_used, mx);
@@ -665,8 +676,13 @@ __global__ void __launch_bounds__(fwd_threads<NG>(), NG == 1 ? 2 : 1)
             uint32_t ov[32];
             tmem_ld32(t_o + c * 32, ov);
             tmem_wait_ld();
+            const uint64_t a2 = f2_make(alpha, alpha);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+            for (int i = 0; i < 32; i += 2) {
+              const uint64_t o2 = f2_mul(f2_make_bits(ov[i], ov[i + 1]), a2);
+              ov[i] = (uint32_t)o2;
+              ov[i + 1] = (uint32_t)(o2 >> 32);
+            }
             tmem_st32(t_o + c * 32, ov);
           }
           tmem_wait_st();
@@ -678,7 +694,11 @@ __global__ void __launch_bounds__(fwd_threads<NG>(), NG == 1 ? 2 : 1)
       }
       // pass 2, two halves of 64 keys: p = 2^(x - m) rounded to the input dtype,
       // packed in pairs into S columns [0, 64) (already consumed).
-      float rs = 0.f;
+      // Column pairs go through the packed f32x2 pipe: x = s * scale - m (FFMA2)
+      // and two running pair sums (FADD2); exponentials stay scalar.
+      const uint64_t sc2 = f2_make(p.scale_log2, p.scale_log2);
+      const uint64_t nm2 = f2_make(-m_used, -m_used);
+      uint64_t rs2[2] = {f2_make(0.f, 0.f), f2_make(0.f, 0.f)};
       auto pass2 = [&](auto masked) {
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
@@ -689,8 +709,8 @@ __global__ void __launch_bounds__(fwd_threads<NG>(), NG == 1 ? 2 : 1)
           uint32_t pk[32];
 #pragma unroll
           for (int i = 0; i < 64; i += 2) {
-            float x0 = fmaf(__uint_as_float(sv[i]), p.scale_log2, -m_used);
-            float x1 = fmaf(__uint_as_float(sv[i + 1]), p.scale_log2, -m_used);
+            const uint64_t x2 = f2_fma(f2_make_bits(sv[i], sv[i + 1]), sc2, nm2);
+            float x0 = f2_lo(x2), x1 = f2_hi(x2);
             if constexpr (decltype(masked)::value) {
               const int col = half * 64 + i;
               x0 = col > kmax ? -INFINITY : x0;
@@ -698,7 +718,7 @@ __global__ void __launch_bounds__(fwd_threads<NG>(), NG == 1 ? 2 : 1)
             }
             const float p0 = ex2_approx(x0);
             const float p1 = ex2_approx(x1);
-            rs += p0 + p1;
+            rs2[(i >> 1) & 1] = f2_add(rs2[(i >> 1) & 1], f2_make(p0, p1));
             pk[i / 2] = BF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
           }
           tmem_st32(t_s + half * 32, pk);
@@ -708,7 +728,10 @@ __global__ void __launch_bounds__(fwd_threads<NG>(), NG == 1 ? 2 : 1)
         pass2(std::true_type{});
       else
         pass2(std::false_type{});
-      l += rs;
+      {
+        const uint64_t r2 = f2_add(rs2[0], rs2[1]);
+        l += f2_lo(r2) + f2_hi(r2);
+      }
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
