@@ -1247,6 +1247,412 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 }
 
 // ===========================================================================
+// dK/dV with 128-query streaming tiles (tensor cores, every product N >= 128)
+// ===========================================================================
+//
+// Same work as the dK/dV instance above (flash_attention.py:197-221, one CTA per
+// 128-key tile, no atomics) with 128-query streaming tiles, so that S^T = K Q^T
+// and dP^T = V dO^T are 128 x 128 products: a 128 x 64 tcgen05.mma takes as long
+// as a 128 x 128 one, so the 64-query tiles spent half the tensor time of their
+// two T products.  The 512 TMEM columns hold one S^T, one dP^T and the dK, dV
+// accumulators -- no room to double-buffer T -- so the two 128-column regions
+// R0, R1 swap roles every tile (S^T(i) in R(i % 2), dP^T(i) in the other) and
+// the elementwise work is split in two phases:
+//   EW-a(i): P = exp(scale S - lse) from S^T (registers, f32) -> P^T packed into
+//            its own S^T columns (TS operand of dV += P^T dO)
+//   EW-b(i): reads dP^T(i) (releasing its region), dS = P (dP - delta) -> bf16
+//            dS^T into a 128-byte-swizzled shared tile that is both the A operand
+//            of dK += dS^T Q and the source of the TMA store of dS^T for the
+//            dQ-from-dS kernel.
+// MMA order per tile:  S(i+1) | dV(i) | dK(i) | dP(i+1).  S(i+1) goes into dP(i)'s
+// region as soon as EW-b(i) holds dP(i) in registers, so EW-a(i+1) starts right
+// after EW-b(i); dP(i+1) overwrites S(i)'s region after dV(i) (issued before it,
+// tcgen05.mma executes in issue order) has read P(i).
+// Warps: 0 TMA producer, 1 TMEM owner + MMA lane, 2-9 elementwise: warp w
+// handles TMEM lanes 32 (w % 4) .. +31 (key rows) and query columns
+// [64 h, 64 h + 64) of each tile, h = (w - 2) / 4.
+// TMEM: R0 [0,128), R1 [128,256) (P^T packed at +[0,32) and +[64,96) of the S^T
+// region), dV [256, 256+D), dK [256+D, 256+2D).
+
+constexpr int kWideY = 128;                 // streaming rows (queries) per tile
+constexpr int kWideThreads = 320;           // 10 warps
+
+template <int D>
+struct WideSmem {
+  static constexpr int kChunks = D / 64;
+  static constexpr int kXBytes = BX * D * 2;            // K or V tile
+  static constexpr int kYBytes = kWideY * D * 2;        // Q or dO tile
+  static constexpr int kStages = D == 64 ? 3 : 2;
+  static constexpr int kStageBytes = 2 * kYBytes + 1024;  // Q, dO, lse + delta (128 f32 each)
+  static constexpr int kX1Off = 0;
+  static constexpr int kX2Off = kXBytes;
+  static constexpr int kYOff = 2 * kXBytes;
+  static constexpr int kStgOff = kYOff + kStages * kStageBytes;  // dS^T: 2 x [128 keys x 64 queries]
+  static constexpr int kDataBytes = kStgOff + BX * kWideY * 2;
+  // x_full, y_full[S], y_empty[S], s_full, dp_full, p_full, dp_free, ds_full, ds_free, acc_full
+  static constexpr int kNumBars = 2 * kStages + 8;
+  static constexpr int kBarBytes = kNumBars * 8 + 8;  // + TMEM slot + abort flag
+  static_assert(kBarBytes <= 128, "barrier block must fit the alignment slack rule");
+  // Data is placed at the first 1024-byte boundary; the barrier block goes into the
+  // slack before it when that is >= 128 bytes, else right after the data (the
+  // slack is then < 128, and 1024 extra bytes cover both cases).
+  static constexpr int kTotal = kDataBytes + 1024;
+};
+
+// Bounded wait that ignores the abort flag: used to drain this CTA's own MMAs
+// before TMEM is released on any path.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (!mbar_try_wait(bar, parity)) {
+    if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+      report_timeout(40);
+      return;
+    }
+  }
+}
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kWideThreads, 1)
+    attn_dkv_wide_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+                         const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdo,
+                         const __grid_constant__ CUtensorMap tlse, const __grid_constant__ CUtensorMap tdelta,
+                         const __grid_constant__ CUtensorMap tds, const BwdParams p) {
+  using L = WideSmem<D>;
+  constexpr int S = L::kStages;
+  typedef typename std::conditional<BF16, __nv_bfloat16, __half>::type T;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem - smem_raw >= 128 ? smem_raw : smem + L::kDataBytes);
+  uint64_t* x_full = bars + 0;
+  uint64_t* y_full = bars + 1;
+  uint64_t* y_empty = bars + 1 + S;
+  uint64_t* s_full = bars + 1 + 2 * S;
+  uint64_t* dp_full = s_full + 1;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* dp_free = s_full + 3;
+  uint64_t* ds_full = s_full + 4;
+  uint64_t* ds_free = s_full + 5;
+  uint64_t* acc_full = s_full + 6;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kNumBars);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = p.bh0 + (int)blockIdx.y;
+  const int hh = bh % p.l0.nh, bb = bh / p.l0.nh;
+  const int x0 = (int)blockIdx.x * BX;
+  const int diag_shift = p.sk - p.sq;
+  int j0 = 0;
+  const int j1 = (p.sq + kWideY - 1) / kWideY;
+  if (p.causal) j0 = max(0, x0 - diag_shift) / kWideY;
+  const int n_y = max(0, j1 - j0);
+
+  if (threadIdx.x == 0) {
+    mbar_init(x_full, 1);
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&y_full[i], 1);
+      mbar_init(&y_empty[i], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(dp_full, 1);
+    mbar_init(p_full, 8);   // one arrival per elementwise warp
+    mbar_init(dp_free, 8);
+    mbar_init(ds_full, 8);
+    mbar_init(ds_free, 1);
+    mbar_init(acc_full, 1);
+    *abort = 0;
+    fence_mbar_init();
+  }
+  auto load_y = [&](int i) {
+    const int s = i % S;
+    uint8_t* y1 = smem + L::kYOff + s * L::kStageBytes;
+    uint8_t* y2 = y1 + L::kYBytes;
+    mbar_arrive_expect_tx(&y_full[s], 2 * L::kYBytes + 2 * kWideY * 4);
+    const int yrow = (j0 + i) * kWideY;
+#pragma unroll
+    for (int c = 0; c < L::kChunks; ++c) {
+      tma_load_4d(y1 + c * (kWideY * 128), &tq, &y_full[s], c * 64, yrow, hh, bb);
+      tma_load_4d(y2 + c * (kWideY * 128), &tdo, &y_full[s], c * 64, yrow, hh, bb);
+    }
+    float* st = reinterpret_cast<float*>(y2 + L::kYBytes);
+    tma_load_2d(st, &tlse, &y_full[s], yrow, bh);
+    tma_load_2d(st + kWideY, &tdelta, &y_full[s], yrow, bh);
+  };
+  const int n_pre = min(n_y, S);
+  if (threadIdx.x == 0 && n_y > 0) {
+    tma_prefetch_desc(&tk);
+    tma_prefetch_desc(&tv);
+    tma_prefetch_desc(&tq);
+    tma_prefetch_desc(&tdo);
+    pdl_wait();
+    mbar_arrive_expect_tx(x_full, 2 * L::kXBytes);
+#pragma unroll
+    for (int c = 0; c < L::kChunks; ++c) {
+      tma_load_4d(smem + L::kX1Off + c * (BX * 128), &tk, x_full, c * 64, x0, hh, bb);
+      tma_load_4d(smem + L::kX2Off + c * (BX * 128), &tv, x_full, c * 64, x0, hh, bb);
+    }
+    for (int i = 0; i < n_pre; ++i) load_y(i);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_launch_dependents();
+  pdl_wait();
+  const uint32_t t_dv = tmem + 256;
+  const uint32_t t_dk = tmem + 256 + D;
+
+  if (warp == 0) {
+    if (lane == 0 && n_y > 0) {
+      for (int i = n_pre; i < n_y; ++i) {
+        if (!mbar_wait(&y_empty[i % S], ((i / S) & 1) ^ 1, abort, 41)) break;
+        load_y(i);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && n_y > 0) {
+      constexpr uint32_t idesc_t = make_idesc_f16(BX, kWideY, BF16, false, false);
+      constexpr uint32_t idesc_a = make_idesc_f16(BX, D, BF16, false, true);
+      const uint64_t dx1 = make_sdesc(smem_u32(smem + L::kX1Off), 16, 1024);
+      const uint64_t dx2 = make_sdesc(smem_u32(smem + L::kX2Off), 16, 1024);
+      const uint64_t dy_k = make_sdesc(smem_u32(smem + L::kYOff), 16, 1024);
+      const uint64_t dy_mn = make_sdesc(smem_u32(smem + L::kYOff), kWideY * 128, 1024);
+      const uint64_t dstg = make_sdesc(smem_u32(smem + L::kStgOff), 16, 1024);
+      bool ok = mbar_wait(x_full, 0, abort, 42);
+      // TMEM regions R0 = [0,128), R1 = [128,256) alternate roles: S^T(i) goes to
+      // R(i % 2), dP^T(i) to the other.  P^T(i) stays packed in S^T(i)'s region.
+      auto region = [&](int i, bool is_s) -> uint32_t { return (((i & 1) ^ (is_s ? 0 : 1)) ? 128u : 0u); };
+      auto issue_prod = [&](int i, bool is_s) {
+        const uint64_t dy = sdesc_at(dy_k, (i % S) * L::kStageBytes + (is_s ? 0 : L::kYBytes));
+        const uint64_t dx = is_s ? dx1 : dx2;
+        const uint32_t dst = tmem + region(i, is_s);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t xo = (kk >> 2) * (BX * 128) + (kk & 3) * 32;
+          const uint32_t yo = (kk >> 2) * (kWideY * 128) + (kk & 3) * 32;
+          tc_mma_f16_ss(dst, sdesc_at(dx, xo), sdesc_at(dy, yo), idesc_t, kk != 0);
+        }
+        tc_commit(is_s ? s_full : dp_full);
+      };
+      // dV += P^T(i) dO_i: A = P^T from TMEM, B = dO_i MN-major
+      auto issue_dv = [&](int i) {
+        const uint64_t dm2 = sdesc_at(dy_mn, (i % S) * L::kStageBytes + L::kYBytes);
+        const uint32_t pa = tmem + region(i, true);
+#pragma unroll
+        for (int kk = 0; kk < kWideY / 16; ++kk)
+          tc_mma_f16_ts(t_dv, pa + (kk >> 2) * 64 + (kk & 3) * 8, sdesc_at(dm2, kk * 2048), idesc_a,
+                        (i > 0 || kk > 0) ? 1u : 0u);
+      };
+      // dK += dS^T(i) Q_i: A = dS^T staging (K-major), B = Q_i MN-major
+      auto issue_dk = [&](int i) {
+        const uint64_t dm1 = sdesc_at(dy_mn, (i % S) * L::kStageBytes);
+#pragma unroll
+        for (int kk = 0; kk < kWideY / 16; ++kk)
+          tc_mma_f16_ss(t_dk, sdesc_at(dstg, (kk >> 2) * (BX * 128) + (kk & 3) * 32), sdesc_at(dm1, kk * 2048),
+                        idesc_a, (i > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(ds_free);          // staging may be rewritten
+        tc_commit(&y_empty[i % S]);  // Q_i, dO_i, stats no longer read
+      };
+      // Order per tile i: S(i+1) as soon as EW-b(i) holds dP(i) (its region), then
+      // dV(i), dK(i), and dP(i+1) into S(i)'s region after dV(i) has read P(i).
+      if (ok && (ok = mbar_wait(&y_full[0], 0, abort, 43))) {
+        tc_fence_after();
+        issue_prod(0, true);
+        issue_prod(0, false);
+      }
+      for (int i = 0; ok && i < n_y; ++i) {
+        const bool more = i + 1 < n_y;
+        if (!(ok = mbar_wait(p_full, i & 1, abort, 45))) break;
+        if (more) {
+          if (!(ok = mbar_wait(dp_free, i & 1, abort, 44))) break;
+          if (!(ok = mbar_wait(&y_full[(i + 1) % S], ((i + 1) / S) & 1, abort, 43))) break;
+        }
+        tc_fence_after();
+        if (more) issue_prod(i + 1, true);
+        issue_dv(i);
+        if (!(ok = mbar_wait(ds_full, i & 1, abort, 46))) break;
+        tc_fence_after();
+        issue_dk(i);
+        if (more) issue_prod(i + 1, false);
+      }
+      tc_commit(acc_full);
+      mbar_drain(acc_full, 0);  // every MMA of this CTA has completed
+    }
+  } else {
+    // ------------------------------------------------ elementwise warps
+    const int qw = warp & 3;
+    const int h = (warp - 2) >> 2;  // query columns [64 h, 64 h + 64)
+    const int r = qw * 32 + lane;   // key row == TMEM lane
+    const int xrow = x0 + r;
+    const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
+    const uint32_t t_col = tmem + lane_off + h * 64;  // + region: S^T (P^T packed in its first 32) / dP^T
+    uint8_t* stg = smem + L::kStgOff + h * (BX * 128) + qw * 4096;
+    bool ok = true;
+    for (int i = 0; ok && i < n_y; ++i) {
+      const int ph = i & 1;
+      const int y0 = (j0 + i) * kWideY;
+      const int s = i % S;
+      const uint32_t t_s = t_col + ((i & 1) ? 128u : 0u);
+      const uint32_t t_dp = t_col + ((i & 1) ? 0u : 128u);
+      const bool need_mask = (y0 + kWideY > p.sq) || (p.causal && x0 + BX - 1 > y0 + diag_shift);
+      // ---- EW-a: P = 2^(scale*log2e*S - lse*log2e)
+      if (!mbar_wait(s_full, ph, abort, 47) || !mbar_wait(&y_full[s], (i / S) & 1, abort, 48)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const float* st = reinterpret_cast<const float*>(smem + L::kYOff + s * L::kStageBytes + 2 * L::kYBytes) + h * 64;
+      uint32_t pf[64];
+      tmem_ld32(t_s, *reinterpret_cast<uint32_t(*)[32]>(&pf[0]));
+      tmem_ld32(t_s + 32, *reinterpret_cast<uint32_t(*)[32]>(&pf[32]));
+      tmem_wait_ld();
+      {
+        uint32_t pp[32];
+        // four columns per step: one 16-byte load of lse, packed f32x2 math
+        // (each lane rounds exactly like fmaf(s, scale*log2e, -(lse*log2e)))
+        const uint64_t sc2 = f2_make(p.scale_log2, p.scale_log2);
+        const uint64_t nlog2e2 = f2_make(-kLog2e, -kLog2e);
+        auto body_a = [&](auto masked) {
+#pragma unroll
+          for (int c = 0; c < 64; c += 4) {
+            const float4 l4 = *reinterpret_cast<const float4*>(st + c);
+            const uint64_t x01 = f2_fma(f2_make_bits(pf[c], pf[c + 1]), sc2, f2_mul(f2_make(l4.x, l4.y), nlog2e2));
+            const uint64_t x23 = f2_fma(f2_make_bits(pf[c + 2], pf[c + 3]), sc2, f2_mul(f2_make(l4.z, l4.w), nlog2e2));
+            float x[4] = {f2_lo(x01), f2_hi(x01), f2_lo(x23), f2_hi(x23)};
+            if constexpr (decltype(masked)::value) {
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const int qry = y0 + h * 64 + c + u;
+                const bool valid = qry < p.sq && !(p.causal && xrow > qry + diag_shift);
+                x[u] = valid ? x[u] : -INFINITY;
+              }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) pf[c + u] = __float_as_uint(ex2_approx(x[u]));
+          }
+        };
+        if (need_mask)
+          body_a(std::true_type{});
+        else
+          body_a(std::false_type{});
+#pragma unroll
+        for (int c = 0; c < 64; c += 2) {
+          const float a0 = __uint_as_float(pf[c]), a1 = __uint_as_float(pf[c + 1]);
+          pp[c / 2] = BF16 ? pack_bf16x2(a0, a1) : pack_f16x2(a0, a1);
+        }
+        tmem_st32(t_s, pp);
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+      // ---- EW-b: dS = P (dP - delta)
+      if (!mbar_wait(dp_full, ph, abort, 49)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      // dP^T(i) into registers first: its release (dp_free) lets S(i+1) into the region.
+      uint32_t b[64];
+      tmem_ld32(t_dp, *reinterpret_cast<uint32_t(*)[32]>(&b[0]));
+      tmem_ld32(t_dp + 32, *reinterpret_cast<uint32_t(*)[32]>(&b[32]));
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dp_free);
+      uint8_t* row = stg + lane * 128;
+#pragma unroll
+      for (int hb = 0; hb < 2; ++hb) {
+        uint32_t dd[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 4) {
+          const int c = hb * 32 + e;
+          const float4 d4 = *reinterpret_cast<const float4*>(st + kWideY + c);
+          const uint64_t d01 = f2_mul(f2_make_bits(pf[c], pf[c + 1]),
+                                      f2_sub(f2_make_bits(b[c], b[c + 1]), f2_make(d4.x, d4.y)));
+          const uint64_t d23 = f2_mul(f2_make_bits(pf[c + 2], pf[c + 3]),
+                                      f2_sub(f2_make_bits(b[c + 2], b[c + 3]), f2_make(d4.z, d4.w)));
+          dd[e / 2] = BF16 ? pack_bf16x2(f2_lo(d01), f2_hi(d01)) : pack_f16x2(f2_lo(d01), f2_hi(d01));
+          dd[e / 2 + 1] = BF16 ? pack_bf16x2(f2_lo(d23), f2_hi(d23)) : pack_f16x2(f2_lo(d23), f2_hi(d23));
+        }
+        if (hb == 0) {
+          // the staging tile is free once dK(i-1) has read it and this warp's TMA
+          // store of it has been read
+          if (i > 0 && !mbar_wait(ds_free, (i - 1) & 1, abort, 50)) {
+            ok = false;
+            break;
+          }
+          if (lane == 0) bulk_wait_group_read0();
+          __syncwarp();
+        }
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          const int g16 = hb * 4 + v;  // 16-byte granule of the 128-byte row
+          *reinterpret_cast<uint4*>(row + ((g16 ^ (lane & 7)) << 4)) =
+              make_uint4(dd[4 * v], dd[4 * v + 1], dd[4 * v + 2], dd[4 * v + 3]);
+        }
+      }
+      if (!ok) break;
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(ds_full);
+        if (p.ds != nullptr) {
+          // dS^T in 64-key x 64-query blocks: (query in block, key in block, query block, key block)
+          const int key = x0 + qw * 32;
+          tma_store_4d(&tds, stg, 0, key & 63, (y0 >> 6) + h, (int)blockIdx.y * (p.sk >> 6) + (key >> 6));
+          bulk_commit_group();
+        }
+      }
+      __syncwarp();
+    }
+    if (lane == 0) bulk_wait_group0();
+    // epilogue: warps with h = 0 store dK (x scale), h = 1 store dV
+    if (n_y > 0 && ok && mbar_wait(acc_full, 0, abort, 51)) {
+      tc_fence_after();
+      const bool row_ok = xrow < p.sk;
+      T* out = reinterpret_cast<T*>(h == 0 ? p.out0 : p.out1) + (h == 0 ? p.l0 : p.l1).row(bh, xrow);
+      const uint32_t src = (h == 0 ? t_dk : t_dv) + lane_off;
+      const float mul = h == 0 ? p.scale : 1.0f;
+#pragma unroll
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(src + c0, v);
+        tmem_wait_ld();
+        if (row_ok) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 8) {
+            uint4 w;
+            const float* f = reinterpret_cast<const float*>(&v[e]);
+            w.x = BF16 ? pack_bf16x2(f[0] * mul, f[1] * mul) : pack_f16x2(f[0] * mul, f[1] * mul);
+            w.y = BF16 ? pack_bf16x2(f[2] * mul, f[3] * mul) : pack_f16x2(f[2] * mul, f[3] * mul);
+            w.z = BF16 ? pack_bf16x2(f[4] * mul, f[5] * mul) : pack_f16x2(f[4] * mul, f[5] * mul);
+            w.w = BF16 ? pack_bf16x2(f[6] * mul, f[7] * mul) : pack_f16x2(f[6] * mul, f[7] * mul);
+            *reinterpret_cast<uint4*>(out + c0 + e) = w;
+          }
+        }
+      }
+    } else if (n_y == 0 && xrow < p.sk) {
+      // no query reaches these keys (not reachable when sk % 128 == 0): zeros
+      T* out = reinterpret_cast<T*>(h == 0 ? p.out0 : p.out1) + (h == 0 ? p.l0 : p.l1).row(bh, xrow);
+      for (int c = 0; c < D; ++c) out[c] = DT<T>::from_f(0.f);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ===========================================================================
 // dQ from a materialised dS (tensor cores)
 // ===========================================================================
 //
@@ -1626,10 +2032,67 @@ static int launch_bwd_tc(cudaStream_t s, const BwdArgs& a, int64_t b, int64_t h,
   return check_launch(IS_DKV ? "attn_bwd_dkv_tc" : "attn_bwd_dq_tc");
 }
 
+template <int D, bool BF16>
+static int launch_dkv_wide(cudaStream_t s, const BwdArgs& a, int64_t b, int64_t h, int64_t sq,
+                           int64_t sk, float scale, int causal) {
+  using L = WideSmem<D>;
+  const CUtensorMapDataType dt = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap tk, tv, tq, tdo;
+  int rc = map_bhsd(&tk, a.k, dt, D, a.lk, b, h, sk, BX);
+  if (!rc) rc = map_bhsd(&tv, a.v, dt, D, a.lv, b, h, sk, BX);
+  if (!rc) rc = map_bhsd(&tq, a.q, dt, D, a.lq, b, h, sq, kWideY);
+  if (!rc) rc = map_bhsd(&tdo, a.dout, dt, D, a.ldo, b, h, sq, kWideY);
+  // lse / delta as [bh][sq] f32, 128-query boxes (zero-filled past sq)
+  const int64_t bh = b * h;
+  CUtensorMap tl, td;
+  if (!rc) rc = make_tmap_2d(&tl, a.lse, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)sq, (uint64_t)bh, (uint64_t)sq * 4, kWideY, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (!rc) rc = make_tmap_2d(&td, a.delta, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)sq, (uint64_t)bh, (uint64_t)sq * 4, kWideY, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  BwdParams p;
+  p.sq = (int)sq;
+  p.sk = (int)sk;
+  p.scale = scale;
+  p.scale_log2 = scale * kLog2e;
+  p.causal = causal;
+  p.lse = a.lse;
+  p.delta = a.delta;
+  p.out0 = a.out0;
+  p.out1 = a.out1;
+  p.l0 = a.l0;
+  p.l1 = a.l1;
+  p.n_x_tiles = (int)((sk + BX - 1) / BX);
+  p.bh0 = (int)a.bh0;
+  const int64_t nbh = a.nbh < 0 ? bh - a.bh0 : a.nbh;
+  p.ds = a.ds;
+  p.ds_ld = a.ds_ld;
+  p.ds_slice = a.ds_ld * sk;
+  auto kern = attn_dkv_wide_kernel<D, BF16>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+  if (e != cudaSuccess) return fail(FERRITE_LAUNCH_FAILED, "attn_bwd_dkv: smem attr: %s", cudaGetErrorString(e));
+  if (nbh <= 0) return FERRITE_OK;
+  CUtensorMap tds = tl;  // placeholder when no dS is written (never dereferenced)
+  if (p.ds) {
+    rc = map_ds_blocks(&tds, p.ds, dt, sq, sk, nbh, 32, 1);
+    if (rc) return rc;
+  }
+  dim3 grid(p.n_x_tiles, (unsigned)nbh);
+  (void)launch_pdl(kern, dim3(grid), dim3(kWideThreads), L::kTotal, s, tk, tv, tq, tdo, tl, td, tds, p);
+  return check_launch("attn_bwd_dkv_wide");
+}
+
 template <bool IS_DKV>
 static int dispatch_bwd_tc(cudaStream_t s, const BwdArgs& a, int64_t b, int64_t h, int64_t sq,
                            int64_t sk, int64_t d, float scale, int causal, int dtype) {
   const bool bf = dtype == FERRITE_BF16;
+  // dK/dV: 128-query tiles (attn_dkv_wide_kernel) unless FERRITE_ATTN_DKV_WIDE=0
+  static const bool wide = env_int("FERRITE_ATTN_DKV_WIDE", 1) != 0;
+  if (IS_DKV && wide) {
+    if (d == 64)
+      return bf ? launch_dkv_wide<64, true>(s, a, b, h, sq, sk, scale, causal)
+                : launch_dkv_wide<64, false>(s, a, b, h, sq, sk, scale, causal);
+    return bf ? launch_dkv_wide<128, true>(s, a, b, h, sq, sk, scale, causal)
+              : launch_dkv_wide<128, false>(s, a, b, h, sq, sk, scale, causal);
+  }
   if (d == 64)
     return bf ? launch_bwd_tc<64, true, IS_DKV>(s, a, b, h, sq, sk, scale, causal)
               : launch_bwd_tc<64, false, IS_DKV>(s, a, b, h, sq, sk, scale, causal);
