@@ -1945,8 +1945,7 @@ static int launch_fwd_tc(cudaStream_t s, const void* q, const void* k, const voi
                          float* lse, const Bhsd& lq, const Bhsd& lk, const Bhsd& lv, const Bhsd& lo,
                          int64_t b, int64_t h, int64_t sq, int64_t sk, float scale, int causal) {
   if constexpr (D == 64) {
-    static const bool pair = env_int("FERRITE_ATTN_FWD_NG", 1) == 2;
-    if (!pair)
+    if (env_int("FERRITE_ATTN_FWD_NG", 1) != 2)
       return launch_fwd_tc_ng<D, BF16, 1>(s, q, k, v, o, lse, lq, lk, lv, lo, b, h, sq, sk, scale, causal);
   }
   return launch_fwd_tc_ng<D, BF16, 2>(s, q, k, v, o, lse, lq, lk, lv, lo, b, h, sq, sk, scale, causal);
@@ -2085,8 +2084,7 @@ static int dispatch_bwd_tc(cudaStream_t s, const BwdArgs& a, int64_t b, int64_t 
                            int64_t sk, int64_t d, float scale, int causal, int dtype) {
   const bool bf = dtype == FERRITE_BF16;
   // dK/dV: 128-query tiles (attn_dkv_wide_kernel) unless FERRITE_ATTN_DKV_WIDE=0
-  static const bool wide = env_int("FERRITE_ATTN_DKV_WIDE", 1) != 0;
-  if (IS_DKV && wide) {
+  if (IS_DKV && env_int("FERRITE_ATTN_DKV_WIDE", 1) != 0) {
     if (d == 64)
       return bf ? launch_dkv_wide<64, true>(s, a, b, h, sq, sk, scale, causal)
                 : launch_dkv_wide<64, false>(s, a, b, h, sq, sk, scale, causal);

@@ -198,3 +198,48 @@ def test_split_dkv_ds_and_dq_ds_entry_points_over_slice_ranges():
         nat.check(lib.ferrite_attn_bwd_dq_ds(sp, ds.data_ptr(), k.data_ptr(), dq.data_ptr(), ctypes.byref(st), begin, count, b, h, s, s, d,
                                              d**-0.5, 1, 128, 128, nat.BF16))
     assert torch.equal(dq, dq_ref) and torch.equal(dk, dk_ref) and torch.equal(dv, dv_ref)
+
+
+# ---------------------------------------------------------------- kernel variants
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("causal,sq,sk", [(True, 512, 512), (True, 384, 384), (False, 256, 384), (False, 640, 256)])
+def test_dkv_128_and_64_query_tiles_agree(monkeypatch, d, causal, sq, sk):
+    """The 128-query-tile dK/dV kernel (default) and the 64-query template
+    (FERRITE_ATTN_DKV_WIDE=0) form the same rounded P and dS; only the order of
+    the f32 accumulation differs.  Both meet the oracle; their dS-based dQ too."""
+    rng = np.random.default_rng(d * 7 + sq + sk + causal)
+    b, h = 1, 3
+    qn, don = normal(rng, (b, h, sq, d), BF16), normal(rng, (b, h, sq, d), BF16)
+    kn, vn = normal(rng, (b, h, sk, d), BF16), normal(rng, (b, h, sk, d), BF16)
+    q, k, v, do = (to_torch(a) for a in (qn, kn, vn, don))
+    (dq, dk, dv), out, lse = _bwd(q, k, v, do, causal)
+    monkeypatch.setenv("FERRITE_ATTN_DKV_WIDE", "0")
+    (dq0, dk0, dv0), _, _ = _bwd(q, k, v, do, causal)
+    for a, b_, name in ((dq, dq0, "dq"), (dk, dk0, "dk"), (dv, dv0, "dv")):
+        assert_bf16_close(a, b_, atol=4e-3)
+    o_ref, lse_ref = oa.flash_fwd(qn, kn, vn, causal=causal)
+    g_ref = oa.flash_bwd(qn, kn, vn, o_ref, lse_ref, don, causal=causal)
+    for got, ref, name in zip((dq, dk, dv), g_ref, ("dq", "dk", "dv")):
+        assert max_abs(got, ref) <= 2e-2, name
+        assert rel_l2(got, ref) < 1e-2, name
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_forward_one_and_two_query_tiles_per_cta_agree(monkeypatch, causal):
+    """d = 64 forward: one 128-row query tile per CTA (default, two CTAs per SM)
+    and two per CTA (FERRITE_ATTN_FWD_NG=2) run the same per-tile arithmetic."""
+    from ferrite.kernels.flash_attention import flash_forward_with_lse
+
+    rng = np.random.default_rng(11 + causal)
+    qn, kn, vn = (normal(rng, (2, 3, 640, 64), BF16) for _ in range(3))
+    q, k, v = (to_torch(a) for a in (qn, kn, vn))
+    out1, lse1 = flash_forward_with_lse(q, k, v, causal=causal)
+    monkeypatch.setenv("FERRITE_ATTN_FWD_NG", "2")
+    out2, lse2 = flash_forward_with_lse(q, k, v, causal=causal)
+    assert torch.equal(out1, out2)
+    assert torch.equal(lse1, lse2)
+    o_ref, lse_ref = oa.flash_fwd(qn, kn, vn, causal=causal)
+    assert max_abs(out1, o_ref) <= 2e-2
+    np.testing.assert_allclose(to_numpy(lse1), lse_ref, atol=2e-4, rtol=1e-5)
