@@ -858,12 +858,12 @@ def run_ours(args, ws, rank, local):
 
     pk = platform.peaks()
     dom = max((k for k in bd if wl.kernel_work.get(k)), key=lambda k: bd[k])
+    long_step = args.workload == "gpt"
     if wl.bound == "hbm":
         achieved = wl.kernel_work[dom] / (bd[dom] / 1e3) / 1e9
         peak, unit, psrc = pk.hbm_bytes_per_s / 1e9, "GB/s", "hbm_gbs"
     else:
         achieved = wl.kernel_work[dom] / (bd[dom] / 1e3) / 1e12
-        long_step = args.workload == "gpt"
         peak = (pk.bf16_flops_sustained if long_step else pk.bf16_flops) / 1e12
         unit, psrc = "TFLOP/s", "bf16_tflops_sustained" if long_step else "bf16_tflops"
     out = {
@@ -888,6 +888,7 @@ def run_ours(args, ws, rank, local):
             "unit": unit,
             "frac": round(achieved / peak, 4),
             "peak_source": f"{pk.source} (MEASURED_PEAKS.json {psrc})" if pk.source == "measured" else "fallback",
+            **({"frac_of_sustained": round(achieved / (pk.bf16_flops_sustained / 1e12), 4)} if wl.bound == "tensor" and not long_step else {}),
             "traffic": _load_traffic(dom),
             "timing": "kernel times from a second pass of the same K steps with CUDA events between kernels",
             "kernels_ms": {k: round(v, 5) for k, v in bd.items()},
