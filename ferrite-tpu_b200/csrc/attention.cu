@@ -2139,10 +2139,6 @@ static int dispatch_dq_ds(cudaStream_t s, const BwdArgs& a, int64_t b, int64_t h
             : launch_dq_ds<128, false>(s, a, b, h, sq, sk, scale, causal);
 }
 
-static Bhsd contiguous_bhsd(int64_t h, int64_t s, int64_t d) {
-  return Bhsd{h * s * d, s * d, d, (int)h};
-}
-
 static int strides_ok(const char* op, const ferrite_attn_strides* st) {
   if (!st) return fail(FERRITE_BAD_SHAPE, "%s: null strides", op);
   const int64_t* f = &st->q[0];
