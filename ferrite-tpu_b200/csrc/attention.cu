@@ -394,8 +394,9 @@ struct FwdSmem {
   static constexpr int kQOff = 0;  // Q0 (, Q1)
   static constexpr int kKVOff = NG * kQBytes;
   static constexpr int kBarOff = kKVOff + 2 * kStageBytes;
-  // q_full, k_full[2], v_full[2], k_empty[2], v_empty[2], s_full[2], p_full[2], pv_done[2]
-  static constexpr int kNumBars = 15;
+  // q_full, k_full[2], v_full[2], k_empty[2], v_empty[2], s_full[2], p_full[2], pv_done[2],
+  // p_half[2]
+  static constexpr int kNumBars = 17;
   static constexpr int kTotal = 1024 + kBarOff + kNumBars * 8 + 16;
 };
 
@@ -447,6 +448,8 @@ __global__ void __launch_bounds__(fwd_threads<NG>(), NG == 1 ? 2 : 1)
   uint64_t* s_full = bars + 9;
   uint64_t* p_full = bars + 11;
   uint64_t* pv_done = bars + 13;
+  // P columns of keys [0, 64) written: the first half of P V may start
+  uint64_t* p_half = bars + 15;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kNumBars);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -472,6 +475,7 @@ __global__ void __launch_bounds__(fwd_threads<NG>(), NG == 1 ? 2 : 1)
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 4);  // one arrival per softmax warp of the group
+      mbar_init(&p_half[i], 4);
       mbar_init(&pv_done[i], 1);
     }
     *abort = 0;
@@ -560,14 +564,17 @@ __global__ void __launch_bounds__(fwd_threads<NG>(), NG == 1 ? 2 : 1)
         }
         tc_commit(&s_full[g]);
       };
-      auto issue_pv = [&](int g, int j) {
+      // O_g += P_g V_j over keys [64 hh, 64 hh + 64): the first half is issued as
+      // soon as the softmax has written that half of P (p_half), the second with S
+      // of the next tile, so the group's next S waits for half a P V, not a whole one.
+      auto issue_pv = [&](int g, int j, int hh) {
         const uint64_t dv = sdesc_at(dv_base, (j & 1) * L::kStageBytes);
         const uint32_t pa = tmem + g * 128;  // P_g: packed pairs in S columns [0, 64)
 #pragma unroll
-        for (int kk = 0; kk < TK / 16; ++kk)
+        for (int kk = hh * 4; kk < hh * 4 + 4; ++kk)
           tc_mma_f16_ts(tmem + kOCol + g * D, pa + kk * 8, sdesc_at(dv, kk * 2048), idesc_o,
                         (j > 0 || kk > 0) ? 1u : 0u);
-        tc_commit(&pv_done[g]);
+        if (hh == 1) tc_commit(&pv_done[g]);
       };
       if (ok) {
         tc_fence_after();
@@ -577,10 +584,13 @@ __global__ void __launch_bounds__(fwd_threads<NG>(), NG == 1 ? 2 : 1)
       }
       if constexpr (NG == 1) {
         for (int j = 0; ok && j < n_kv; ++j) {
-          if (!mbar_wait(&p_full[0], j & 1, abort, 13)) break;
+          if (!mbar_wait(&p_half[0], j & 1, abort, 12)) break;
           if (!mbar_wait(&v_full[j & 1], (j >> 1) & 1, abort, 18)) break;
           tc_fence_after();
-          issue_pv(0, j);
+          issue_pv(0, j, 0);
+          if (!mbar_wait(&p_full[0], j & 1, abort, 13)) break;
+          tc_fence_after();
+          issue_pv(0, j, 1);
           tc_commit(&v_empty[j & 1]);
           if (j + 1 < n_kv) {
             if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort, 14)) break;
@@ -592,18 +602,24 @@ __global__ void __launch_bounds__(fwd_threads<NG>(), NG == 1 ? 2 : 1)
       }
       for (int j = 0; NG == 2 && ok && j < n_kv; ++j) {
         const bool more = j + 1 < n_kv;
-        if (!mbar_wait(&p_full[0], j & 1, abort, 13)) break;
+        if (!mbar_wait(&p_half[0], j & 1, abort, 12)) break;
         if (!mbar_wait(&v_full[j & 1], (j >> 1) & 1, abort, 18)) break;
         tc_fence_after();
-        issue_pv(0, j);
+        issue_pv(0, j, 0);
+        if (!mbar_wait(&p_full[0], j & 1, abort, 13)) break;
+        tc_fence_after();
+        issue_pv(0, j, 1);
         if (more) {
           if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort, 14)) break;
           tc_fence_after();
           issue_s(0, j + 1);
         }
+        if (!mbar_wait(&p_half[1], j & 1, abort, 19)) break;
+        tc_fence_after();
+        issue_pv(1, j, 0);
         if (!mbar_wait(&p_full[1], j & 1, abort, 15)) break;
         tc_fence_after();
-        issue_pv(1, j);
+        issue_pv(1, j, 1);
         tc_commit(&v_empty[j & 1]);  // V_j no longer read
         if (more) {
           issue_s(1, j + 1);
@@ -722,6 +738,12 @@ __global__ void __launch_bounds__(fwd_threads<NG>(), NG == 1 ? 2 : 1)
             pk[i / 2] = BF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
           }
           tmem_st32(t_s + half * 32, pk);
+          if (half == 0) {
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_half[g]);
+          }
         }
       };
       if (diag)
