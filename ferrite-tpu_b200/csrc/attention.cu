@@ -1311,8 +1311,9 @@ struct WideSmem {
   static constexpr int kYOff = 2 * kXBytes;
   static constexpr int kStgOff = kYOff + kStages * kStageBytes;  // dS^T: 2 x [128 keys x 64 queries]
   static constexpr int kDataBytes = kStgOff + BX * kWideY * 2;
-  // x_full, y_full[S], y_empty[S], s_full, dp_full, p_full, dp_free, ds_full, ds_free, acc_full
-  static constexpr int kNumBars = 2 * kStages + 8;
+  // x_full, y_full[S], y_empty[S], s_full, dp_full, p_full, dp_free, ds_full, ds_free, acc_full,
+  // p_half
+  static constexpr int kNumBars = 2 * kStages + 9;
   static constexpr int kBarBytes = kNumBars * 8 + 8;  // + TMEM slot + abort flag
   static_assert(kBarBytes <= 128, "barrier block must fit the alignment slack rule");
   // Data is placed at the first 1024-byte boundary; the barrier block goes into the
@@ -1357,6 +1358,7 @@ __global__ void __launch_bounds__(kWideThreads, 1)
   uint64_t* ds_full = s_full + 4;
   uint64_t* ds_free = s_full + 5;
   uint64_t* acc_full = s_full + 6;
+  uint64_t* p_half = s_full + 7;  // P^T of each warp's first 32 query columns written
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kNumBars);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -1379,6 +1381,7 @@ __global__ void __launch_bounds__(kWideThreads, 1)
     mbar_init(s_full, 1);
     mbar_init(dp_full, 1);
     mbar_init(p_full, 8);   // one arrival per elementwise warp
+    mbar_init(p_half, 8);
     mbar_init(dp_free, 8);
     mbar_init(ds_full, 8);
     mbar_init(ds_free, 1);
@@ -1462,13 +1465,17 @@ __global__ void __launch_bounds__(kWideThreads, 1)
         tc_commit(is_s ? s_full : dp_full);
       };
       // dV += P^T(i) dO_i: A = P^T from TMEM, B = dO_i MN-major
-      auto issue_dv = [&](int i) {
+      // part 0: query steps kk = 0, 1, 4, 5 (the warps' first 32 columns, p_half);
+      // part 1: kk = 2, 3, 6, 7 (p_full)
+      auto issue_dv = [&](int i, int part) {
         const uint64_t dm2 = sdesc_at(dy_mn, (i % S) * L::kStageBytes + L::kYBytes);
         const uint32_t pa = tmem + region(i, true);
 #pragma unroll
-        for (int kk = 0; kk < kWideY / 16; ++kk)
+        for (int q = 0; q < 4; ++q) {
+          const int kk = (q >> 1) * 4 + part * 2 + (q & 1);
           tc_mma_f16_ts(t_dv, pa + (kk >> 2) * 64 + (kk & 3) * 8, sdesc_at(dm2, kk * 2048), idesc_a,
                         (i > 0 || kk > 0) ? 1u : 0u);
+        }
       };
       // dK += dS^T(i) Q_i: A = dS^T staging (K-major), B = Q_i MN-major
       auto issue_dk = [&](int i) {
@@ -1489,6 +1496,9 @@ __global__ void __launch_bounds__(kWideThreads, 1)
       }
       for (int i = 0; ok && i < n_y; ++i) {
         const bool more = i + 1 < n_y;
+        if (!(ok = mbar_wait(p_half, i & 1, abort, 52))) break;
+        tc_fence_after();
+        issue_dv(i, 0);
         if (!(ok = mbar_wait(p_full, i & 1, abort, 45))) break;
         if (more) {
           if (!(ok = mbar_wait(dp_free, i & 1, abort, 44))) break;
@@ -1496,7 +1506,7 @@ __global__ void __launch_bounds__(kWideThreads, 1)
         }
         tc_fence_after();
         if (more) issue_prod(i + 1, true);
-        issue_dv(i);
+        issue_dv(i, 1);
         if (!(ok = mbar_wait(ds_full, i & 1, abort, 46))) break;
         tc_fence_after();
         issue_dk(i);
@@ -1534,14 +1544,13 @@ __global__ void __launch_bounds__(kWideThreads, 1)
       tmem_ld32(t_s + 32, *reinterpret_cast<uint32_t(*)[32]>(&pf[32]));
       tmem_wait_ld();
       {
-        uint32_t pp[32];
         // four columns per step: one 16-byte load of lse, packed f32x2 math
         // (each lane rounds exactly like fmaf(s, scale*log2e, -(lse*log2e)))
         const uint64_t sc2 = f2_make(p.scale_log2, p.scale_log2);
         const uint64_t nlog2e2 = f2_make(-kLog2e, -kLog2e);
-        auto body_a = [&](auto masked) {
+        auto body_a = [&](auto masked, auto c0) {
 #pragma unroll
-          for (int c = 0; c < 64; c += 4) {
+          for (int c = decltype(c0)::value; c < decltype(c0)::value + 32; c += 4) {
             const float4 l4 = *reinterpret_cast<const float4*>(st + c);
             const uint64_t x01 = f2_fma(f2_make_bits(pf[c], pf[c + 1]), sc2, f2_mul(f2_make(l4.x, l4.y), nlog2e2));
             const uint64_t x23 = f2_fma(f2_make_bits(pf[c + 2], pf[c + 3]), sc2, f2_mul(f2_make(l4.z, l4.w), nlog2e2));
@@ -1558,21 +1567,29 @@ __global__ void __launch_bounds__(kWideThreads, 1)
             for (int u = 0; u < 4; ++u) pf[c + u] = __float_as_uint(ex2_approx(x[u]));
           }
         };
-        if (need_mask)
-          body_a(std::true_type{});
-        else
-          body_a(std::false_type{});
+        // Two 32-column halves, each published on its own barrier: dV(i) takes the
+        // query steps of the first halves (p_half) while the second halves run.
+        auto half_a = [&](auto c0, uint64_t* bar) {
+          if (need_mask)
+            body_a(std::true_type{}, c0);
+          else
+            body_a(std::false_type{}, c0);
+          uint32_t pp[16];
 #pragma unroll
-        for (int c = 0; c < 64; c += 2) {
-          const float a0 = __uint_as_float(pf[c]), a1 = __uint_as_float(pf[c + 1]);
-          pp[c / 2] = BF16 ? pack_bf16x2(a0, a1) : pack_f16x2(a0, a1);
-        }
-        tmem_st32(t_s, pp);
-        tmem_wait_st();
+          for (int c = 0; c < 32; c += 2) {
+            const float a0 = __uint_as_float(pf[decltype(c0)::value + c]);
+            const float a1 = __uint_as_float(pf[decltype(c0)::value + c + 1]);
+            pp[c / 2] = BF16 ? pack_bf16x2(a0, a1) : pack_f16x2(a0, a1);
+          }
+          tmem_st16(t_s + decltype(c0)::value / 2, pp);
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar);
+        };
+        half_a(std::integral_constant<int, 0>{}, p_half);
+        half_a(std::integral_constant<int, 32>{}, p_full);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
       // ---- EW-b: dS = P (dP - delta)
       if (!mbar_wait(dp_full, ph, abort, 49)) {
         ok = false;
