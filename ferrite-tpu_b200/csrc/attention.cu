@@ -1283,9 +1283,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 //   EW-a(i): P = exp(scale S - lse) from S^T (registers, f32) -> P^T packed into
 //            its own S^T columns (TS operand of dV += P^T dO)
 //   EW-b(i): reads dP^T(i) (releasing its region), dS = P (dP - delta) -> bf16
-//            dS^T into a 128-byte-swizzled shared tile that is both the A operand
-//            of dK += dS^T Q and the source of the TMA store of dS^T for the
-//            dQ-from-dS kernel.
+//            dS^T packed into the other half of its S^T columns (TS operand of
+//            dK += dS^T Q), then into a 128-byte-swizzled shared tile that the TMA
+//            store of dS^T (for the dQ-from-dS kernel) reads -- after the dK
+//            operand is published, so the store is off the MMA's path.
 // MMA order per tile:  S(i+1) | dV(i) | dK(i) | dP(i+1).  S(i+1) goes into dP(i)'s
 // region as soon as EW-b(i) holds dP(i) in registers, so EW-a(i+1) starts right
 // after EW-b(i); dP(i+1) overwrites S(i)'s region after dV(i) (issued before it,
@@ -1294,7 +1295,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 // handles TMEM lanes 32 (w % 4) .. +31 (key rows) and query columns
 // [64 h, 64 h + 64) of each tile, h = (w - 2) / 4.
 // TMEM: R0 [0,128), R1 [128,256) (P^T packed at +[0,32) and +[64,96) of the S^T
-// region), dV [256, 256+D), dK [256+D, 256+2D).
+// region, dS^T at +[32,64) and +[96,128)), dV [256, 256+D), dK [256+D, 256+2D).
 
 constexpr int kWideY = 128;                 // streaming rows (queries) per tile
 constexpr int kWideThreads = 320;           // 10 warps
@@ -1311,9 +1312,8 @@ struct WideSmem {
   static constexpr int kYOff = 2 * kXBytes;
   static constexpr int kStgOff = kYOff + kStages * kStageBytes;  // dS^T: 2 x [128 keys x 64 queries]
   static constexpr int kDataBytes = kStgOff + BX * kWideY * 2;
-  // x_full, y_full[S], y_empty[S], s_full, dp_full, p_full, dp_free, ds_full, ds_free, acc_full,
-  // p_half
-  static constexpr int kNumBars = 2 * kStages + 9;
+  // x_full, y_full[S], y_empty[S], s_full, dp_full, p_full, dp_free, ds_full, acc_full, p_half
+  static constexpr int kNumBars = 2 * kStages + 8;
   static constexpr int kBarBytes = kNumBars * 8 + 8;  // + TMEM slot + abort flag
   static_assert(kBarBytes <= 128, "barrier block must fit the alignment slack rule");
   // Data is placed at the first 1024-byte boundary; the barrier block goes into the
@@ -1356,9 +1356,8 @@ __global__ void __launch_bounds__(kWideThreads, 1)
   uint64_t* p_full = s_full + 2;
   uint64_t* dp_free = s_full + 3;
   uint64_t* ds_full = s_full + 4;
-  uint64_t* ds_free = s_full + 5;
-  uint64_t* acc_full = s_full + 6;
-  uint64_t* p_half = s_full + 7;  // P^T of each warp's first 32 query columns written
+  uint64_t* acc_full = s_full + 5;
+  uint64_t* p_half = s_full + 6;  // P^T of each warp's first 32 query columns written
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kNumBars);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -1384,7 +1383,6 @@ __global__ void __launch_bounds__(kWideThreads, 1)
     mbar_init(p_half, 8);
     mbar_init(dp_free, 8);
     mbar_init(ds_full, 8);
-    mbar_init(ds_free, 1);
     mbar_init(acc_full, 1);
     *abort = 0;
     fence_mbar_init();
@@ -1447,7 +1445,6 @@ __global__ void __launch_bounds__(kWideThreads, 1)
       const uint64_t dx2 = make_sdesc(smem_u32(smem + L::kX2Off), 16, 1024);
       const uint64_t dy_k = make_sdesc(smem_u32(smem + L::kYOff), 16, 1024);
       const uint64_t dy_mn = make_sdesc(smem_u32(smem + L::kYOff), kWideY * 128, 1024);
-      const uint64_t dstg = make_sdesc(smem_u32(smem + L::kStgOff), 16, 1024);
       bool ok = mbar_wait(x_full, 0, abort, 42);
       // TMEM regions R0 = [0,128), R1 = [128,256) alternate roles: S^T(i) goes to
       // R(i % 2), dP^T(i) to the other.  P^T(i) stays packed in S^T(i)'s region.
@@ -1477,14 +1474,14 @@ __global__ void __launch_bounds__(kWideThreads, 1)
                         (i > 0 || kk > 0) ? 1u : 0u);
         }
       };
-      // dK += dS^T(i) Q_i: A = dS^T staging (K-major), B = Q_i MN-major
+      // dK += dS^T(i) Q_i: A = dS^T packed in S^T(i)'s region (TMEM), B = Q_i MN-major
       auto issue_dk = [&](int i) {
         const uint64_t dm1 = sdesc_at(dy_mn, (i % S) * L::kStageBytes);
+        const uint32_t da = tmem + region(i, true) + 32;
 #pragma unroll
         for (int kk = 0; kk < kWideY / 16; ++kk)
-          tc_mma_f16_ss(t_dk, sdesc_at(dstg, (kk >> 2) * (BX * 128) + (kk & 3) * 32), sdesc_at(dm1, kk * 2048),
-                        idesc_a, (i > 0 || kk > 0) ? 1u : 0u);
-        tc_commit(ds_free);          // staging may be rewritten
+          tc_mma_f16_ts(t_dk, da + (kk >> 2) * 64 + (kk & 3) * 8, sdesc_at(dm1, kk * 2048), idesc_a,
+                        (i > 0 || kk > 0) ? 1u : 0u);
         tc_commit(&y_empty[i % S]);  // Q_i, dO_i, stats no longer read
       };
       // Order per tile i: S(i+1) as soon as EW-b(i) holds dP(i) (its region), then
@@ -1604,6 +1601,14 @@ __global__ void __launch_bounds__(kWideThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(dp_free);
+      // dS(i) goes (a) packed into the free half of S^T(i)'s columns, [64 h + 32,
+      // 64 h + 64), where dK(i) reads it as a TMEM operand, and (b) into the shared
+      // staging tile for the TMA store of dS^T -- after ds_full, off the MMA's path.
+      const bool store_ds = p.ds != nullptr;
+      if (store_ds) {
+        if (lane == 0) bulk_wait_group_read0();  // this warp's previous store has read the tile
+        __syncwarp();
+      }
       uint8_t* row = stg + lane * 128;
 #pragma unroll
       for (int hb = 0; hb < 2; ++hb) {
@@ -1619,36 +1624,31 @@ __global__ void __launch_bounds__(kWideThreads, 1)
           dd[e / 2] = BF16 ? pack_bf16x2(f2_lo(d01), f2_hi(d01)) : pack_f16x2(f2_lo(d01), f2_hi(d01));
           dd[e / 2 + 1] = BF16 ? pack_bf16x2(f2_lo(d23), f2_hi(d23)) : pack_f16x2(f2_lo(d23), f2_hi(d23));
         }
-        if (hb == 0) {
-          // the staging tile is free once dK(i-1) has read it and this warp's TMA
-          // store of it has been read
-          if (i > 0 && !mbar_wait(ds_free, (i - 1) & 1, abort, 50)) {
-            ok = false;
-            break;
-          }
-          if (lane == 0) bulk_wait_group_read0();
-          __syncwarp();
-        }
+        tmem_st16(t_s + 32 + hb * 16, dd);
+        if (store_ds) {
 #pragma unroll
-        for (int v = 0; v < 4; ++v) {
-          const int g16 = hb * 4 + v;  // 16-byte granule of the 128-byte row
-          *reinterpret_cast<uint4*>(row + ((g16 ^ (lane & 7)) << 4)) =
-              make_uint4(dd[4 * v], dd[4 * v + 1], dd[4 * v + 2], dd[4 * v + 3]);
+          for (int v = 0; v < 4; ++v) {
+            const int g16 = hb * 4 + v;  // 16-byte granule of the 128-byte row
+            *reinterpret_cast<uint4*>(row + ((g16 ^ (lane & 7)) << 4)) =
+                make_uint4(dd[4 * v], dd[4 * v + 1], dd[4 * v + 2], dd[4 * v + 3]);
+          }
         }
       }
-      if (!ok) break;
-      fence_proxy_async_smem();
+      tmem_wait_st();
+      tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(ds_full);
-        if (p.ds != nullptr) {
+      if (lane == 0) mbar_arrive(ds_full);
+      if (store_ds) {
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
           // dS^T in 64-key x 64-query blocks: (query in block, key in block, query block, key block)
           const int key = x0 + qw * 32;
           tma_store_4d(&tds, stg, 0, key & 63, (y0 >> 6) + h, (int)blockIdx.y * (p.sk >> 6) + (key >> 6));
           bulk_commit_group();
         }
+        __syncwarp();
       }
-      __syncwarp();
     }
     if (lane == 0) bulk_wait_group0();
     // epilogue: warps with h = 0 store dK (x scale), h = 1 store dV
