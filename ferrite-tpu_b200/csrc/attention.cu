@@ -1287,10 +1287,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 //            dK += dS^T Q), then into a 128-byte-swizzled shared tile that the TMA
 //            store of dS^T (for the dQ-from-dS kernel) reads -- after the dK
 //            operand is published, so the store is off the MMA's path.
-// MMA order per tile:  S(i+1) | dV(i) | dK(i) | dP(i+1).  S(i+1) goes into dP(i)'s
-// region as soon as EW-b(i) holds dP(i) in registers, so EW-a(i+1) starts right
-// after EW-b(i); dP(i+1) overwrites S(i)'s region after dV(i) (issued before it,
-// tcgen05.mma executes in issue order) has read P(i).
+// MMA order per tile:  dV(i) part 0 | S(i+1) | dV(i) part 1 | dK(i) | dP(i+1).
+// S(i+1) goes into dP(i)'s region as soon as EW-b(i) holds dP(i) in registers, so
+// EW-a(i+1) starts right after EW-b(i); dP(i+1) overwrites S(i)'s region after dV(i)
+// and dK(i) (issued before it; tcgen05.mma executes in issue order) have read P(i)
+// and dS(i) there.
 // Warps: 0 TMA producer, 1 TMEM owner + MMA lane, 2-9 elementwise: warp w
 // handles TMEM lanes 32 (w % 4) .. +31 (key rows) and query columns
 // [64 h, 64 h + 64) of each tile, h = (w - 2) / 4.
@@ -1484,8 +1485,9 @@ __global__ void __launch_bounds__(kWideThreads, 1)
                         (i > 0 || kk > 0) ? 1u : 0u);
         tc_commit(&y_empty[i % S]);  // Q_i, dO_i, stats no longer read
       };
-      // Order per tile i: S(i+1) as soon as EW-b(i) holds dP(i) (its region), then
-      // dV(i), dK(i), and dP(i+1) into S(i)'s region after dV(i) has read P(i).
+      // Order per tile i: dV(i) part 0 once the first halves of P(i) are out; S(i+1)
+      // as soon as EW-b(i) holds dP(i) (its region); dV(i) part 1; dK(i); dP(i+1) into
+      // S(i)'s region after dV(i) and dK(i) (in issue order) have read P(i) and dS(i).
       if (ok && (ok = mbar_wait(&y_full[0], 0, abort, 43))) {
         tc_fence_after();
         issue_prod(0, true);
