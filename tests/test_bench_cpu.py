@@ -1,0 +1,36 @@
+"""bench.py's reference arm (the oracle timed on host cores) runs without a GPU: its
+one JSON line carries the fields the bench contract names."""
+
+import json
+import os
+import subprocess
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_reference_arm_json_line():
+    p = subprocess.run(
+        [sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "2", "--warmup", "1"],
+        capture_output=True, text=True, timeout=600, cwd=ROOT,
+    )
+    assert p.returncode == 0, p.stderr[-2000:]
+    lines = [ln for ln in p.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1, p.stdout
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference"
+    assert d["metric"] == "add+RMSNorm fwd+bwd HBM GB/s" and d["unit"] == "GB/s"
+    assert d["n_gpus"] == 1 and d["higher_is_better"] is True and d["scaling"] == "weak"
+    assert d["warmup"] >= 3  # the timing rule's minimum is enforced
+    assert d["value"] > 0 and d["ms_per_step"] > 0
+    cb = d["cpu_baseline"]
+    assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == d["value"] and cb["sample"]
+    assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    assert d["config"]["workload"] == "add_rmsnorm_fwd_bwd_bf16_8192x4096"
+
+
+def test_help_lists_the_workloads():
+    p = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--help"], capture_output=True, text=True, timeout=120, cwd=ROOT)
+    assert p.returncode == 0
+    for w in ("norm", "attn", "gemm", "gpt", "prefill"):
+        assert w in p.stdout
