@@ -3,7 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload norm|attn|gemm|gpt|prefill]
 
-Workloads (synthetic inputs, seeded):
+Workloads (the benchmark configs; synthetic inputs, seeded):
 
 * ``norm`` (default, configs[1]) -- fused residual-add + RMSNorm forward +
   backward, x/residual bf16 [8192, 4096] ~ N(0,1), weight f32 1 + 0.1 N(0,1),

@@ -103,7 +103,7 @@ def test_golden_fixture():
 @pytest.mark.parametrize("causal", [True, False])
 @pytest.mark.parametrize("d", [64, 128])
 def test_small_config_vs_blockwise_oracle(causal, d):
-    """b2 h4 s512 (d64; also d128), bf16 N(0,1) seed 0, block 128."""
+    """Small benchmark config: b2 h4 s512 (d64; also d128), bf16 N(0,1) seed 0, block 128."""
     rng = np.random.default_rng(0)
     q, k, v, do = _qkv(rng, 2, 4, 512, d, BF16, n=4)
     scale = 1 / np.sqrt(d)
@@ -128,7 +128,7 @@ def test_noncausal_unequal_lengths_and_short_query():
 
 @pytest.mark.slow
 def test_long_config_forward_sampled_heads():
-    """b8 h32 s8192 d128 bf16; full-size run on the GPU,
+    """Long-context benchmark config: b8 h32 s8192 d128 bf16; full-size run on the GPU,
     oracle on two (b, h) slices (heads are independent)."""
     b, h, s, d = 8, 32, 8192, 128
     g = torch.Generator(device="cuda").manual_seed(0)

@@ -100,7 +100,7 @@ def test_f16_operands():
 
 
 def test_bf16_8192_cubed_vs_oracle_rows():
-    """BASELINE config: bf16 8192^3, A, B ~ N(0,1)/sqrt(K), checked against the
+    """Benchmark config: bf16 8192^3, A, B ~ N(0,1)/sqrt(K), checked against the
     oracle on a sample of rows and against torch fp32 everywhere."""
     m = n = k = 8192
     rng = np.random.default_rng(0)

@@ -89,7 +89,7 @@ def test_golden_fixtures():
     [(8192, 4096), (1, 4096), (7, 4096), (33, 1000), (5, 8), (3, 24), (1024, 8192), (64, 32768), (300, 256), (77, 512), (2048, 1024), (129, 2048)],
 )
 def test_add_rmsnorm_fwd_bwd_vs_oracle(rows, dim):
-    """BASELINE config (8192 x 4096 bf16) plus ragged / odd / tiny / long rows."""
+    """Benchmark config (8192 x 4096 bf16) plus ragged / odd / tiny / long rows."""
     rng = np.random.default_rng(rows * 7 + dim)
     x, r = normal(rng, (rows, dim), BF16), normal(rng, (rows, dim), BF16)
     w = (1.0 + 0.1 * rng.standard_normal(dim)).astype(np.float32)
