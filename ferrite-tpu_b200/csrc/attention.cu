@@ -1756,6 +1756,15 @@ __global__ void __launch_bounds__(kDqThreads, 1)
   // unit u: slice u / n_q_tiles, query tile n_q_tiles - 1 - u % n_q_tiles (heaviest
   // first within a slice).  CTAs running at the same time work on the same few
   // slices, so each slice's K tiles are read from HBM once and then hit in L2.
+  // The CTA's r-th unit: rounds of gridDim.x consecutive units, taken left to right
+  // in even rounds and right to left in odd ones (boustrophedon), so the heavy and
+  // light query tiles of neighbouring units even out over a CTA's rounds (a plain
+  // stride gives one CTA only heavy tiles when gridDim.x is a multiple of n_q_tiles
+  // / 2, e.g. 148 CTAs over 8 tiles per slice: 30% idle at the tail).
+  auto unit_of = [&](int round) {
+    const int c = (round & 1) ? (int)gridDim.x - 1 - (int)blockIdx.x : (int)blockIdx.x;
+    return round * (int)gridDim.x + c;
+  };
   auto unit_tile = [&](int u, int& qt, int& sl, int& nkb) {
     sl = u / p.n_q_tiles;
     qt = p.n_q_tiles - 1 - (u - sl * p.n_q_tiles);
@@ -1793,7 +1802,7 @@ __global__ void __launch_bounds__(kDqThreads, 1)
       tma_prefetch_desc(&tk);
       int it = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      for (int rd = 0, u = unit_of(0); u < units && ok; u = unit_of(++rd)) {
         int qt, sl, nkb;
         unit_tile(u, qt, sl, nkb);
         const int bh = p.bh0 + sl;
@@ -1822,7 +1831,7 @@ __global__ void __launch_bounds__(kDqThreads, 1)
       const uint64_t db_base = make_sdesc(s0 + L::kABytes, 8192, 1024);
       int it = 0, local = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++local) {
+      for (int rd = 0, u = unit_of(0); u < units && ok; u = unit_of(++rd), ++local) {
         int qt, sl, nkb;
         unit_tile(u, qt, sl, nkb);
         const int buf = local & 1;
@@ -1851,7 +1860,7 @@ __global__ void __launch_bounds__(kDqThreads, 1)
     const int q = warp & 3;
     const int r = q * 32 + lane;
     int local = 0;
-    for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
+    for (int rd = 0, u = unit_of(0); u < units; u = unit_of(++rd), ++local) {
       int qt, sl, nkb;
       unit_tile(u, qt, sl, nkb);
       const int buf = local & 1;
