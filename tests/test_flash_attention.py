@@ -126,6 +126,23 @@ def test_noncausal_unequal_lengths_and_short_query():
     assert max_abs(out, oa.reference_fwd(q, k, v, causal=False)) <= 2e-2
 
 
+@pytest.mark.parametrize("d", [64, 128])
+def test_backward_ragged_query_length(d):
+    """sq = 200 against sk = 384 (non-causal): the last 128-query tile of the dK/dV
+    kernel and the last dS block of the dQ kernel are partly past sq."""
+    rng = np.random.default_rng(40 + d)
+    q, do = normal(rng, (1, 2, 200, d), BF16), normal(rng, (1, 2, 200, d), BF16)
+    k, v = normal(rng, (1, 2, 384, d), BF16), normal(rng, (1, 2, 384, d), BF16)
+    bs = BlockSizes(8, 128, 8, 128)
+    out, lse = flash_forward_with_lse(to_torch(q), to_torch(k), to_torch(v), causal=False, block_sizes=bs)
+    dq, dk, dv = flash_backward(to_torch(q), to_torch(k), to_torch(v), out, lse, to_torch(do), causal=False, block_sizes=bs)
+    o_ref, lse_ref = oa.flash_fwd(q, k, v, causal=False, bq=8, bk=128)
+    g_ref = oa.flash_bwd(q, k, v, o_ref, lse_ref, do, causal=False, bq=8, bk=128)
+    for got, ref, name in zip((dq, dk, dv), g_ref, ("dq", "dk", "dv")):
+        assert max_abs(got, ref) <= 2e-2, name
+        assert rel_l2(got, ref) < 1e-2, name
+
+
 @pytest.mark.slow
 def test_long_config_forward_sampled_heads():
     """Long-context benchmark config: b8 h32 s8192 d128 bf16; full-size run on the GPU,
