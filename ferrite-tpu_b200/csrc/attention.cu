@@ -416,6 +416,31 @@ __device__ __forceinline__ uint32_t swz128(int row, int col_granule) {
   return (uint32_t)(row * 128 + ((col_granule ^ (row & 7)) << 4));
 }
 
+// CTA order of the causal tensor-core kernels.  The grid is (tiles, slices); the
+// linear CTA index is mapped to (tile, slice) in batches of kOrderBatch slices with
+// the tile index running slowest inside a batch.  The callers number tiles heaviest
+// first, so a batch's heavy CTAs start before its light ones and the grid ends on
+// light CTAs (a plain (tile, slice) grid ended on the last slice's heaviest tile);
+// a batch's few slices keep the tiles they share in L2.
+// Short sequences (fewer than 16 tiles a slice) keep the plain order, which measured
+// 4% faster there.
+constexpr int kOrderBatch = 8;
+__device__ __forceinline__ void batched_order(int ntiles, int nslices, int& tile, int& slice) {
+  if (ntiles < 16) {
+    tile = (int)blockIdx.x;
+    slice = (int)blockIdx.y;
+    return;
+  }
+  const int lin = (int)blockIdx.x + (int)blockIdx.y * (int)gridDim.x;
+  const int per_batch = kOrderBatch * ntiles;
+  const int batch = lin / per_batch;
+  const int s0 = batch * kOrderBatch;
+  const int nb = min(kOrderBatch, nslices - s0);
+  const int idx = lin - batch * per_batch;
+  tile = idx / nb;
+  slice = s0 + idx % nb;
+}
+
 // Warps: 0 TMA producer, 1 MMA issuer, then 4 softmax warps per query tile (the
 // first at warp kSoftWarp0; a softmax warp reads TMEM lanes 32 * (warp % 4) on).
 // NG = 1 has no idle warps, so 192 threads x 2 CTAs leave 168 registers a thread.
@@ -455,8 +480,9 @@ __global__ void __launch_bounds__(fwd_threads<NG>(), NG == 1 ? 2 : 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // Heaviest (last) query blocks first: causal work grows with the index.
-  const int qb = p.nq_blocks - 1 - (int)blockIdx.x;
-  const int bh = blockIdx.y;
+  int qtile, bh;
+  batched_order(p.nq_blocks, (int)gridDim.y, qtile, bh);
+  const int qb = p.nq_blocks - 1 - qtile;  // heaviest (last) query blocks first
   const int hh = bh % p.lo.nh, bb = bh / p.lo.nh;  // TMA coordinates of the slice
   const int q0 = qb * NG * TQ;
   const int diag_shift = p.sk - p.sq;  // causal: key <= query + diag_shift
@@ -1363,9 +1389,11 @@ __global__ void __launch_bounds__(kWideThreads, 1)
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = p.bh0 + (int)blockIdx.y;
+  int ktile, slice;
+  batched_order(p.n_x_tiles, (int)gridDim.y, ktile, slice);  // key block 0 (most causal tiles) first
+  const int bh = p.bh0 + slice;
   const int hh = bh % p.l0.nh, bb = bh / p.l0.nh;
-  const int x0 = (int)blockIdx.x * BX;
+  const int x0 = ktile * BX;
   const int diag_shift = p.sk - p.sq;
   int j0 = 0;
   const int j1 = (p.sq + kWideY - 1) / kWideY;
@@ -1646,7 +1674,7 @@ __global__ void __launch_bounds__(kWideThreads, 1)
         if (lane == 0) {
           // dS^T in 64-key x 64-query blocks: (query in block, key in block, query block, key block)
           const int key = x0 + qw * 32;
-          tma_store_4d(&tds, stg, 0, key & 63, (y0 >> 6) + h, (int)blockIdx.y * (p.sk >> 6) + (key >> 6));
+          tma_store_4d(&tds, stg, 0, key & 63, (y0 >> 6) + h, slice * (p.sk >> 6) + (key >> 6));
           bulk_commit_group();
         }
         __syncwarp();
