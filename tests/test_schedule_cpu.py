@@ -38,3 +38,27 @@ def test_boustrophedon_balances_causal_tiles():
         stride = [sum(cost(u) for u in range(c, units, G)) for c in range(G)]
         assert max(snake) / np.mean(snake) < 1.03
         assert max(snake) / np.mean(snake) <= max(stride) / np.mean(stride)
+
+
+def batched_order(lin, ntiles, nslices, batch=8):
+    """CPU restatement of batched_order() in csrc/attention.cu for grids of at least
+    16 tiles a slice: linear CTA index -> (tile, slice), tile slowest inside a batch
+    of `batch` slices."""
+    per_batch = batch * ntiles
+    b = lin // per_batch
+    s0 = b * batch
+    nb = min(batch, nslices - s0)
+    idx = lin - b * per_batch
+    return idx // nb, s0 + idx % nb
+
+
+def test_batched_order_is_a_bijection_heaviest_first():
+    for ntiles, nslices in ((16, 1), (16, 7), (32, 256), (64, 32), (64, 33), (17, 9)):
+        pairs = [batched_order(lin, ntiles, nslices) for lin in range(ntiles * nslices)]
+        assert sorted(pairs) == [(t, s) for t in range(ntiles) for s in range(nslices)]
+        # inside each batch the tile index never decreases: heavy (low index) tiles first
+        for b0 in range(0, nslices, 8):
+            nb = min(8, nslices - b0)
+            lo = b0 * ntiles
+            tiles = [pairs[lin][0] for lin in range(lo, lo + nb * ntiles)]
+            assert tiles == sorted(tiles)
