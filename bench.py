@@ -1,7 +1,7 @@
 """Benchmark driver: one JSON line for one workload.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload norm|attn|gemm|gpt|prefill]
+                    [--workload norm|attn|gemm|gpt|prefill|decode]
 
 Workloads (the benchmark configs; synthetic inputs, seeded):
 
@@ -24,6 +24,11 @@ Workloads (the benchmark configs; synthetic inputs, seeded):
 * ``prefill`` -- bucketed prefill of 8 prompts x 512 into the
   static [24, 8, 16, 512, 64] KV cache through a captured CUDA graph.  Metric:
   prefill tokens/s.
+* ``decode`` (configs[4], decode) -- the attention of one greedy-decode step in all
+  24 layers: new K/V rows written into the static [24, 8, 16, 1024, 64] bf16 cache
+  and softmax(q K^T) V over positions 0..1023 (the last step of a 1024-token
+  context), one fused kernel per layer, the 24 launches replayed as one CUDA graph.
+  Metric: algorithmic HBM bytes / s (the cached K and V rows dominate).
 
 Timing: W untimed warm-up steps, an untimed pre-roll (~0.6 s) while nvidia-smi
 starts sampling clocks, then exactly K steps between a barrier + synchronize on
@@ -784,7 +789,128 @@ class PrefillWorkload:
                 "sample_fraction": 1 / cls.PROMPTS}
 
 
-WORKLOADS = {"norm": NormWorkload, "attn": AttnWorkload, "gemm": GemmWorkload, "gpt": GptWorkload, "prefill": PrefillWorkload}
+class DecodeWorkload:
+    """configs[4] serving half, decode: the attention of one greedy-decode step (cache
+    write + softmax(q K^T) V over the static cache) in all 24 layers, for 8 sequences at
+    the last position of a 1024-token context."""
+
+    name = "gpt_decode_attention_kv_24x8x16x1024x64_pos1023_bf16"
+    metric = "decode attention HBM GB/s"
+    unit = "GB/s"
+    dtype = "bf16"
+    scaling = "weak"
+    bound = "hbm"
+    n_events = 2
+    kernels = ("attn_decode",)
+    L, B, H, T, D = 24, 8, 16, 1024, 64
+
+    @classmethod
+    def step_bytes(cls, layers, b, h, pos, d, esz=2):
+        """Algorithmic bytes of one step: per (layer, b, h) the pos cached K and V rows,
+        q / k_new / v_new read, o written, the new K and V rows written."""
+        return layers * b * h * d * esz * (2 * pos + 3 + 1 + 2)
+
+    def __init__(self, dev, ws, rank, shape=None):
+        if shape:  # smaller cases: "layers,b,h,max_len,d"
+            self.L, self.B, self.H, self.T, self.D = shape
+        self.dev, self.ws = dev, ws
+        g = torch.Generator(device=dev)
+        g.manual_seed(77 + rank)
+        L, B, H, T, D = self.L, self.B, self.H, self.T, self.D
+        self.kc = torch.randn(L, B, H, T, D, generator=g, device=dev).to(torch.bfloat16)
+        self.vc = torch.randn(L, B, H, T, D, generator=g, device=dev).to(torch.bfloat16)
+        self.qkv = torch.randn(L, B, 3, H, D, generator=g, device=dev).to(torch.bfloat16)  # each layer's projection
+        self.pos = torch.full((B,), T - 1, dtype=torch.int64, device=dev)
+        self.o = torch.empty(L, B, H, D, dtype=torch.bfloat16, device=dev)
+        self.kernel_work = {"attn_decode": self.step_bytes(L, B, H, T - 1, D)}
+        self.launches_per_step = L
+        self._launch()  # first call: module load and per-device set-up, before the capture
+        torch.cuda.synchronize(dev)
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            self._launch()
+        torch.cuda.current_stream(dev).wait_stream(s)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._launch()
+
+    def _launch(self):
+        from ferrite import _native as nat
+
+        lib = nat.lib()
+        st = nat.stream_ptr(self.dev)
+        B, H, T, D = self.B, self.H, self.T, self.D
+        ld = 3 * H * D
+        for i in range(self.L):
+            base = self.qkv[i].data_ptr()
+            nat.check(lib.ferrite_attn_decode(st, base, base + H * D * 2, base + 2 * H * D * 2, self.kc[i].data_ptr(), self.vc[i].data_ptr(),
+                                              self.pos.data_ptr(), self.o[i].data_ptr(), B, H, T, D, ld, 1.0 / np.sqrt(D), nat.BF16))
+
+    @property
+    def units_per_step(self):
+        return self.kernel_work["attn_decode"]
+
+    def step(self, i, ev=None):
+        if ev:
+            ev[0].record()
+        self.graph.replay()
+        if ev:
+            ev[1].record()
+
+    def breakdown(self, evs):
+        return {"attn_decode": statistics.mean(e[0].elapsed_time(e[1]) for e in evs)}
+
+    def config(self):
+        return {"workload": self.name, "kv_cache": [self.L, self.B, self.H, self.T, self.D], "pos": self.T - 1, "layers": self.L,
+                "launches": "one ferrite_attn_decode per layer, the 24 captured in one CUDA graph",
+                "l2": f"caches {2 * self.kc.numel() * 2 / 2**20:.0f} MiB, larger than L2",
+                "parallelism": "replicas" if self.ws > 1 else "single GPU"}
+
+    def e2e_setup(self):
+        self.host_qkv = self.qkv.cpu().pin_memory()
+        self.host_pos = self.pos.cpu().pin_memory()
+        self.host_o = torch.empty(self.o.shape, dtype=self.o.dtype).pin_memory()
+        self.h2d_bytes = self.host_qkv.numel() * 2 + self.host_pos.numel() * 8
+        self.d2h_bytes = self.host_o.numel() * 2
+        self.e2e_api = ("ferrite.kernels.decode_attention.decode_attention(q, k_cache[l], v_cache[l], pos, k_new, v_new) per layer, "
+                        "eager; the new rows and positions copied in from pinned host memory and the outputs copied out every step, "
+                        "the caches resident in HBM as in a decode server")
+
+    def e2e_step(self):
+        from ferrite.kernels.decode_attention import decode_attention
+
+        qkv = self.host_qkv.to(self.dev, non_blocking=True)
+        pos = self.host_pos.to(self.dev, non_blocking=True)
+        for i in range(self.L):
+            o = decode_attention(qkv[i, :, 0], self.kc[i], self.vc[i], pos, k_new=qkv[i, :, 1], v_new=qkv[i, :, 2])
+            self.host_o[i].copy_(o, non_blocking=True)
+
+    @classmethod
+    def cpu_baseline(cls, layers=1, threads=None):
+        """The oracle's decode step (numpy, the reference's masked full-cache attention)
+        on ``layers`` of the 24 layers, extrapolated linearly."""
+        import ml_dtypes
+
+        sys.path.insert(0, ROOT)
+        from oracle import attention as oa
+
+        rng = np.random.default_rng(0)
+        bf = ml_dtypes.bfloat16
+        kc, vc = (rng.standard_normal((cls.B, cls.H, cls.T, cls.D), dtype=np.float32).astype(bf) for _ in range(2))
+        q, kn, vn = (rng.standard_normal((cls.B, cls.H, cls.D), dtype=np.float32).astype(bf) for _ in range(3))
+        pos = np.full(cls.B, cls.T - 1)
+        t0 = time.perf_counter()
+        for _ in range(layers):
+            oa.decode_reference(q, kc, vc, pos, 1.0 / np.sqrt(cls.D), kn, vn)
+        t = time.perf_counter() - t0
+        nbytes = cls.step_bytes(layers, cls.B, cls.H, cls.T - 1, cls.D)
+        return {"value": nbytes / t / 1e9, "unit": "GB/s", "cores": threads or _host_cores(), "kind": "port",
+                "sample": f"{layers} of {cls.L} layers, numpy oracle (BLAS threads)", "seconds_per_sample": t,
+                "sample_fraction": layers / cls.L}
+
+
+WORKLOADS = {"norm": NormWorkload, "attn": AttnWorkload, "gemm": GemmWorkload, "gpt": GptWorkload, "prefill": PrefillWorkload, "decode": DecodeWorkload}
 
 
 # ----------------------------------------------------------------------------- runners
@@ -932,7 +1058,7 @@ def run_reference(args, ws, rank):
     if rank != 0:
         return
     W = WORKLOADS[args.workload]
-    heavy = args.workload in ("gpt", "attn", "prefill")
+    heavy = args.workload in ("gpt", "attn", "prefill", "decode")
     for _ in range(1 if heavy else min(args.warmup, 3)):
         W.cpu_baseline()
     runs = [W.cpu_baseline() for _ in range(min(args.steps, 3) if heavy else args.steps)]
@@ -969,7 +1095,7 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="norm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--shape", default=None, help="smaller case for profiling captures: norm rows,dim | attn b,h,s,d | gemm m,n,k")
+    ap.add_argument("--shape", default=None, help="smaller case for profiling captures: norm rows,dim | attn b,h,s,d | gemm m,n,k | decode layers,b,h,max_len,d")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)  # timing rule: at least 3 untimed warm-up steps
     ws, rank, local = _dist_env()

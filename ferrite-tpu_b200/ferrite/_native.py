@@ -101,6 +101,7 @@ SIGNATURES: dict[str, tuple] = {
     "ferrite_attn_bwd_prep_strided": (_i32, [_vp, _vp, _vp, _vp, _sp, _i64, _i64, _i64, _i64, _i32]),
     "ferrite_attn_bwd_dkv_strided": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sp, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _i32, _i32, _i32]),
     "ferrite_attn_bwd_dq_strided": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sp, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _i32, _i32, _i32]),
+    "ferrite_attn_decode": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _f32, _i32]),
 }
 
 

@@ -262,7 +262,7 @@ def flash_attention_reference(q, k, v, *, causal: bool = True, scale: float | No
     if causal:
         sq, sk = q.shape[2], k.shape[2]
         mask = torch.tril(torch.ones((sq, sk), dtype=torch.bool, device=q.device), diagonal=sk - sq)
-        s = torch.where(mask, s, torch.tensor(MASK_VALUE, dtype=s.dtype, device=s.device))
+        s = torch.where(mask, s, MASK_VALUE)  # a Python scalar: no host-to-device copy (graph-capture safe)
     p = torch.softmax(s, dim=-1)
     return torch.einsum("bhqk,bhkd->bhqd", p, v.float()).to(q.dtype)
 

@@ -10,10 +10,12 @@ B200 mapping of the reference's ahead-of-time compilation: each bucket's prefill
 is captured once into a CUDA graph over static input/output buffers at engine
 construction (the counterpart of ``jit(...).lower(...).compile()``), so serving
 a prompt replays a graph -- no Python-level launch overhead and no shape seen at
-serving time triggers new work.  Decode is one query row against the cache and,
-as in the reference (engine.py:12-15), stays on the plain (``xla``) path: it is
-out of this build's kernel scope.  ``jax.export`` of the decode step has no
-counterpart here.
+serving time triggers new work.  Decode is one query row against the cache.  The
+reference keeps the whole decode step in XLA (engine.py:12-15); here its attention
+and cache write run as one kernel (``decode_attention``, selected by
+``ServeConfig.decode_attention="pallas"``, the default; ``"xla"`` gives the
+reference's plain path), while its norms and linears stay on the plain path.
+``jax.export`` of the decode step has no counterpart here.
 """
 
 from __future__ import annotations
@@ -26,6 +28,7 @@ import numpy as np
 import torch
 import torch.nn.functional as F
 
+from ferrite.kernels.decode_attention import decode_attention
 from ferrite.model.gpt import GPTConfig, _linear, _lm_head, _norm, block
 
 
@@ -35,6 +38,7 @@ class ServeConfig:
     max_len: int = 512
     buckets: tuple[int, ...] = (128, 256, 512)
     prefill_kernels: str = "pallas"  # "pallas" | "xla" for attention + norms in prefill
+    decode_attention: str = "pallas"  # "pallas": fused cache write + attention kernel; "xla": plain
     use_graphs: bool = True
 
 
@@ -71,14 +75,19 @@ def _cache_attention(q, k_cache, v_cache, pos, scale):
     """q [B, H, hd]; caches [B, H, max_len, hd]; pos [B] = index of the current token (engine.py:89-95)."""
     s = torch.einsum("bhd,bhkd->bhk", q.float(), k_cache.float()) * scale
     idx = torch.arange(k_cache.shape[2], device=q.device)[None, :]
-    s = torch.where((idx <= pos[:, None])[:, None, :], s, torch.tensor(-1e30, device=q.device))
+    s = torch.where((idx <= pos[:, None])[:, None, :], s, -1e30)
     p = torch.softmax(s, dim=-1)
     return torch.einsum("bhk,bhkd->bhd", p, v_cache.float()).to(q.dtype)
 
 
 @torch.no_grad()
 def decode_step(params, token, pos, k_cache, v_cache, cfg: GPTConfig):
-    """One greedy decode step (engine.py:107-131); updates the caches in place."""
+    """One greedy decode step (engine.py:107-131); updates the caches in place.
+
+    ``cfg.attention == "pallas"`` runs the cache write and the cache attention as one
+    kernel (:func:`ferrite.kernels.decode_attention.decode_attention`); otherwise
+    they run as the reference writes them (``_write_cache`` + ``_cache_attention``).
+    """
     b = token.shape[0]
     h = (params["tok_emb"][token] + params["pos_emb"][pos]).to(cfg.dtype)  # [B, D]
     scale = 1.0 / np.sqrt(cfg.head_dim)
@@ -91,9 +100,13 @@ def decode_step(params, token, pos, k_cache, v_cache, cfg: GPTConfig):
             h, y = _norm(pending, layer["ln1"], h, cfg)
         qkv = _linear(y, layer["wqkv"], cfg).reshape(b, 3, cfg.n_head, cfg.head_dim)
         q, k, v = qkv[:, 0], qkv[:, 1], qkv[:, 2]
-        k_cache[i, ar, :, pos] = k.to(k_cache.dtype)
-        v_cache[i, ar, :, pos] = v.to(v_cache.dtype)
-        a = _cache_attention(q, k_cache[i], v_cache[i], pos, scale).reshape(b, cfg.d_model)
+        if cfg.attention == "pallas":
+            a = decode_attention(q, k_cache[i], v_cache[i], pos, scale=scale, k_new=k.to(k_cache.dtype), v_new=v.to(v_cache.dtype))
+        else:
+            k_cache[i, ar, :, pos] = k.to(k_cache.dtype)
+            v_cache[i, ar, :, pos] = v.to(v_cache.dtype)
+            a = _cache_attention(q, k_cache[i], v_cache[i], pos, scale)
+        a = a.reshape(b, cfg.d_model)
         a = _linear(a, layer["wo"], cfg)
         h, y2 = _norm(a, layer["ln2"], h, cfg)
         pending = _linear(F.gelu(_linear(y2, layer["w1"], cfg), approximate="tanh"), layer["w2"], cfg)
@@ -111,7 +124,9 @@ class Engine:
         self.cfg = model_cfg
         self.serve = serve_cfg
         self.prefill_cfg = model_cfg if serve_cfg.prefill_kernels == "pallas" else model_cfg.replace(attention="xla", norm="xla", linear="xla")
-        self.decode_cfg = model_cfg.replace(attention="xla", norm="xla", linear="xla")
+        if serve_cfg.decode_attention not in ("pallas", "xla"):
+            raise ValueError(f"decode_attention must be 'pallas' or 'xla', got {serve_cfg.decode_attention!r}")
+        self.decode_cfg = model_cfg.replace(attention=serve_cfg.decode_attention, norm="xla", linear="xla")
         self.device = params["tok_emb"].device
         self.compile_seconds: dict[str, float] = {}
         self._graphs: dict[int, Any] = {}
@@ -135,7 +150,7 @@ class Engine:
                 self._graphs[bucket] = (None, tok, lens, None)
             torch.cuda.synchronize(self.device)
             self.compile_seconds[f"prefill_{bucket}"] = time.perf_counter() - t0
-        self.n_compiles = len(self.compile_seconds) + 1  # + decode (eager, plain path)
+        self.n_compiles = len(self.compile_seconds) + 1  # + decode (eager)
 
     def prefill(self, prompts: list[list[int]]):
         """Returns (first token [B], pos [B], caches). Prompts are right-padded to a bucket."""

@@ -332,6 +332,27 @@ FERRITE_API int ferrite_attn_bwd_dq_ds(void* stream, const void* ds, const void*
                            int64_t sk, int64_t d, float scale, int causal, int block_q,
                            int block_k, int dtype);
 
+/* ---- decode attention against a static KV cache ------------------------------ */
+
+/* One greedy-decode step of attention for a new token per batch row:
+ *   k_cache[b, h, pos[b], :] = k_new[b, h, :];  v_cache likewise      (if k_new != NULL)
+ *   o[b, h, :] = softmax_j(scale * q[b, h] . k_cache[b, h, j]) v_cache[b, h, j], j <= pos[b]
+ * in f32, cast to dtype.  q, k_new, v_new: row (b, h) at element b * ld_new + h * d (the
+ * [b, 3, h, d] qkv projection is read in place with ld_new = 3 * h * d); k_cache and
+ * v_cache: one layer of the cache, [b, h, max_len, d], densely packed; pos: int64
+ * [b] on the device; o: [b, h, d], densely packed.  k_new and v_new are both given
+ * or both NULL (NULL: the cache is only read).  dtype bf16 or f16 with d in {32, 64,
+ * 128, 256}, or f32 with d in {32, 64, 128}; all pointers 16-byte aligned and ld_new *
+ * element size a multiple of 16.  A pos[b] outside [0, max_len) writes nothing and
+ * gives o = NaN for that row.  Positions after pos[b] are never read (the reference
+ * masks them to -1e30, a softmax weight of exactly 0).  Replaces the reference's
+ * decode step attention, which runs in XLA: _write_cache (serving/engine.py:98-104)
+ * followed by _cache_attention (serving/engine.py:89-95). */
+FERRITE_API int ferrite_attn_decode(void* stream, const void* q, const void* k_new,
+                        const void* v_new, void* k_cache, void* v_cache, const int64_t* pos,
+                        void* o, int64_t b, int64_t h, int64_t max_len, int64_t d,
+                        int64_t ld_new, float scale, int dtype);
+
 #ifdef __cplusplus
 }
 #endif

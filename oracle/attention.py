@@ -14,6 +14,9 @@ Restates src/ferrite/kernels/flash_attention.py of anxnd2211/ferrite-tpu:
                         _bwd_dkv_kernel :197-221 and _bwd_dq_kernel :224-243
                         (P and dS rounded to the operand dtype before each
                         product, scale applied to dK/dQ at the end).
+and, from src/ferrite/serving/engine.py,
+  * ``decode_reference`` the decode step's cache write and cache attention
+                        (:89-104).
 Arrays are ``[b, h, s, d]``; bfloat16 is ``ml_dtypes.bfloat16``.  The (b, h)
 slices are independent, so callers may pass a subset of heads.
 """
@@ -181,3 +184,30 @@ def attention_flops(b, h, sq, sk, d, causal=True, backward=False) -> int:
     frac = 0.5 if causal else 1.0
     fwd = 4 * b * h * sq * sk * d * frac
     return int(fwd if not backward else fwd * 2.5)
+
+
+def decode_reference(q, k_cache, v_cache, pos, scale, k_new=None, v_new=None):
+    """One decode step against a static KV cache, src/ferrite/serving/engine.py of the
+    reference: ``_write_cache`` :98-104 (the new row stored at ``pos[b]``, cast to the
+    cache dtype) then ``_cache_attention`` :89-95 (f32 scores over every cache
+    position, positions after ``pos[b]`` set to -1e30, softmax, P V in f32, cast to
+    q's dtype).
+
+    q [b, h, d]; k_cache, v_cache [b, h, max_len, d]; pos [b] ints in [0, max_len);
+    k_new / v_new [b, h, d] or None.  Returns (o [b, h, d], k_cache, v_cache), the
+    caches as new arrays.
+    """
+    kc, vc = k_cache.copy(), v_cache.copy()
+    pos = np.asarray(pos, dtype=np.int64)
+    assert np.all((pos >= 0) & (pos < kc.shape[2])), "pos outside the cache"
+    if k_new is not None:
+        for bi, p in enumerate(pos):
+            kc[bi, :, p] = k_new[bi].astype(kc.dtype)
+            vc[bi, :, p] = v_new[bi].astype(vc.dtype)
+    s = np.einsum("bhd,bhkd->bhk", q.astype(F32), kc.astype(F32)) * F32(scale)
+    idx = np.arange(kc.shape[2])[None, :]
+    s = np.where((idx <= pos[:, None])[:, None, :], s, F32(-1e30))
+    s = s - s.max(-1, keepdims=True)
+    p = np.exp(s)
+    p = p / p.sum(-1, keepdims=True)
+    return np.einsum("bhk,bhkd->bhd", p, vc.astype(F32)).astype(q.dtype), kc, vc
