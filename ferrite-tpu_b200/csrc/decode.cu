@@ -14,8 +14,8 @@
 // there).  A row of d elements is read by d / EPV lanes, 16 bytes each (EPV = 8
 // elements for bf16/f16, 4 for f32), so a warp reads 32 / (d / EPV) rows at once.
 // Each such lane group keeps an online-softmax state (running max, sum, f32
-// accumulator) over its rows and takes kUnroll rows per step, so that 2 * kUnroll
-// 16-byte loads per lane are in flight.  The groups are merged in shared memory;
+// accumulator) over its rows, kUnroll rows per step, staged through a per-thread
+// shared-memory ring of cp.async copies kStages - 1 steps ahead.  The groups are merged in shared memory;
 // rank 0 of the cluster then merges the CTAs' states through distributed shared
 // memory and writes the output row: no global scratch and no second kernel.
 //
@@ -297,7 +297,11 @@ static int launch(cudaStream_t s, const void* q, const void* k_new, const void* 
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_attn_kernel<D, T>, kThreads, kRingBytes) != cudaSuccess || n < 1) n = 1;
     occ[dev] = n;
   }
-  const int c = pick_cluster(bh, max_len, G, (int64_t)num_sms(dev) * occ[dev]);
+  int c = pick_cluster(bh, max_len, G, (int64_t)num_sms(dev) * occ[dev]);
+  if (const char* e = std::getenv("FERRITE_DECODE_CLUSTER")) {  // A/B override: 1, 2, 4 or 8
+    const int v = std::atoi(e);
+    if (v == 1 || v == 2 || v == 4 || v == 8) c = v;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)bh, (unsigned)c, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
