@@ -10,12 +10,15 @@ B200 mapping of the reference's ahead-of-time compilation: each bucket's prefill
 is captured once into a CUDA graph over static input/output buffers at engine
 construction (the counterpart of ``jit(...).lower(...).compile()``), so serving
 a prompt replays a graph -- no Python-level launch overhead and no shape seen at
-serving time triggers new work.  Decode is one query row against the cache.  The
-reference keeps the whole decode step in XLA (engine.py:12-15); here its attention
-and cache write run as one kernel (``decode_attention``, selected by
-``ServeConfig.decode_attention="pallas"``, the default; ``"xla"`` gives the
-reference's plain path), while its norms and linears stay on the plain path.
-``jax.export`` of the decode step has no counterpart here.
+serving time triggers new work.  The decode step is captured the same way, once: its
+positions live on the device, so one graph serves every step.
+
+Decode is one query row against the cache.  The reference keeps the whole decode
+step in XLA (engine.py:12-15); here, with ``ServeConfig.decode_kernels="pallas"`` (the
+default), its attention and cache write run as one kernel (``decode_attention``) and
+its residual-add + RMSNorms on the fused norm kernel; its linears (one row per
+sequence) stay on the plain path.  ``"xla"`` gives the reference's plain path
+throughout.  ``jax.export`` of the decode step has no counterpart here.
 """
 
 from __future__ import annotations
@@ -38,7 +41,7 @@ class ServeConfig:
     max_len: int = 512
     buckets: tuple[int, ...] = (128, 256, 512)
     prefill_kernels: str = "pallas"  # "pallas" | "xla" for attention + norms in prefill
-    decode_attention: str = "pallas"  # "pallas": fused cache write + attention kernel; "xla": plain
+    decode_kernels: str = "pallas"  # "pallas": decode attention + norms on the B200 kernels; "xla": plain
     use_graphs: bool = True
 
 
@@ -111,11 +114,13 @@ def decode_step(params, token, pos, k_cache, v_cache, cfg: GPTConfig):
         h, y2 = _norm(a, layer["ln2"], h, cfg)
         pending = _linear(F.gelu(_linear(y2, layer["w1"], cfg), approximate="tanh"), layer["w2"], cfg)
     _, y = _norm(pending, params["ln_f"], h, cfg)
-    return torch.matmul(y.float(), params["tok_emb"].float().t())
+    # tied head in cfg.dtype with f32 accumulation (engine.py:130): the embedding is cast first
+    return _lm_head(y, params["tok_emb"], cfg.replace(linear="xla"))
 
 
 class Engine:
-    """Captures prefill per bucket (CUDA graphs) and generates greedily (engine.py:137-209)."""
+    """Captures prefill per bucket and the decode step (CUDA graphs) and generates greedily
+    (engine.py:137-209)."""
 
     def __init__(self, params, model_cfg: GPTConfig, serve_cfg: ServeConfig):
         if max(serve_cfg.buckets) > model_cfg.seq_len or serve_cfg.max_len > model_cfg.seq_len:
@@ -124,9 +129,10 @@ class Engine:
         self.cfg = model_cfg
         self.serve = serve_cfg
         self.prefill_cfg = model_cfg if serve_cfg.prefill_kernels == "pallas" else model_cfg.replace(attention="xla", norm="xla", linear="xla")
-        if serve_cfg.decode_attention not in ("pallas", "xla"):
-            raise ValueError(f"decode_attention must be 'pallas' or 'xla', got {serve_cfg.decode_attention!r}")
-        self.decode_cfg = model_cfg.replace(attention=serve_cfg.decode_attention, norm="xla", linear="xla")
+        if serve_cfg.decode_kernels not in ("pallas", "xla"):
+            raise ValueError(f"decode_kernels must be 'pallas' or 'xla', got {serve_cfg.decode_kernels!r}")
+        dk = serve_cfg.decode_kernels
+        self.decode_cfg = model_cfg.replace(attention=dk, norm=dk, linear="xla")
         self.device = params["tok_emb"].device
         self.compile_seconds: dict[str, float] = {}
         self._graphs: dict[int, Any] = {}
@@ -150,7 +156,39 @@ class Engine:
                 self._graphs[bucket] = (None, tok, lens, None)
             torch.cuda.synchronize(self.device)
             self.compile_seconds[f"prefill_{bucket}"] = time.perf_counter() - t0
-        self.n_compiles = len(self.compile_seconds) + 1  # + decode (eager)
+        self._decode_graph = None
+        if serve_cfg.use_graphs:
+            self._capture_decode()
+        # every bucket's prefill + the decode step (a captured graph, or one eager function)
+        self.n_compiles = len(self.compile_seconds) + (0 if self._decode_graph is not None else 1)
+
+    def _capture_decode(self):
+        """Captures one decode step into a CUDA graph over static buffers: the token and
+        position inputs, both caches and the next-token output (the counterpart of the
+        reference compiling its decode step once, engine.py:9-10).  Positions are read on
+        the device, so one graph serves every position."""
+        t0 = time.perf_counter()
+        cfg, b = self.cfg, self.serve.batch
+        shape = (cfg.n_layer, b, cfg.n_head, self.serve.max_len, cfg.head_dim)
+        self._dkc = torch.zeros(shape, dtype=cfg.dtype, device=self.device)
+        self._dvc = torch.zeros_like(self._dkc)
+        self._dtok = torch.zeros(b, dtype=torch.long, device=self.device)
+        self._dpos = torch.zeros(b, dtype=torch.long, device=self.device)
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for _ in range(2):  # warm-up: module loading, per-device kernel set-up, allocator pools
+                decode_step(self.params, self._dtok, self._dpos, self._dkc, self._dvc, self.decode_cfg)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            logits = decode_step(self.params, self._dtok, self._dpos, self._dkc, self._dvc, self.decode_cfg)
+            self._dnext = torch.argmax(logits, dim=-1)
+        self._decode_graph = g
+        self._dkc.zero_()  # the warm-up steps wrote rows at position 0
+        self._dvc.zero_()
+        torch.cuda.synchronize(self.device)
+        self.compile_seconds["decode"] = time.perf_counter() - t0
 
     def prefill(self, prompts: list[list[int]]):
         """Returns (first token [B], pos [B], caches). Prompts are right-padded to a bucket."""
@@ -174,6 +212,13 @@ class Engine:
         return torch.argmax(logits, dim=-1), torch.from_numpy(lengths).to(self.device), kc, vc
 
     def decode(self, token, pos, kc, vc):
+        """One greedy step; updates kc / vc in place.  Caches that are the engine's own decode
+        buffers (as ``generate`` passes them) replay the captured graph; others run eagerly."""
+        if self._decode_graph is not None and kc.data_ptr() == self._dkc.data_ptr() and vc.data_ptr() == self._dvc.data_ptr():
+            self._dtok.copy_(token)
+            self._dpos.copy_(pos)
+            self._decode_graph.replay()
+            return self._dnext.clone(), kc, vc
         logits = decode_step(self.params, token, pos, kc, vc, self.decode_cfg)
         return torch.argmax(logits, dim=-1), kc, vc
 
@@ -184,6 +229,10 @@ class Engine:
         t0 = time.perf_counter()
         e0.record()
         token, pos, kc, vc = self.prefill(prompts)
+        if self._decode_graph is not None:  # continue in the captured decode graph's own caches
+            self._dkc.copy_(kc)
+            self._dvc.copy_(vc)
+            kc, vc = self._dkc, self._dvc
         e1.record()
         out = [token.cpu().numpy()]
         ttft = e0.elapsed_time(e1)

@@ -215,7 +215,28 @@ def test_engine_decode_kernel_matches_plain_decode():
     prompts = [[1, 2, 3, 4, 5, 6, 7, 8, 9, 10], [42, 7, 99]]
     outs = []
     for mode in ("pallas", "xla"):
-        eng = Engine(params, cfg, ServeConfig(batch=2, max_len=256, buckets=(128,), decode_attention=mode))
+        eng = Engine(params, cfg, ServeConfig(batch=2, max_len=256, buckets=(128,), decode_kernels=mode))
         gen, _ = eng.generate(prompts, max_new_tokens=8)
+        outs.append(gen)
+    np.testing.assert_array_equal(outs[0], outs[1])
+
+
+@pytest.mark.gpu
+def test_engine_decode_graph_matches_eager_engine():
+    """The captured decode step (one CUDA graph for every position) generates the same
+    tokens as the eager engine, bf16 with the decode kernel at head_dim 64."""
+    from ferrite.model.gpt import GPTConfig, init_params
+    from ferrite.serving.engine import Engine, ServeConfig
+
+    cfg = GPTConfig(vocab_size=512, seq_len=512, d_model=256, n_head=4, n_layer=2, d_ff=1024, linear="pallas")
+    params = init_params(0, cfg)
+    rng = np.random.default_rng(0)
+    prompts = [list(rng.integers(0, 512, size=n)) for n in (100, 17, 128, 60)]
+    outs = []
+    for graphs in (True, False):
+        eng = Engine(params, cfg, ServeConfig(batch=4, max_len=256, buckets=(128,), use_graphs=graphs))
+        assert eng.n_compiles == 2
+        gen, stats = eng.generate(prompts, max_new_tokens=12)
+        assert stats["itl_ms_median"] > 0
         outs.append(gen)
     np.testing.assert_array_equal(outs[0], outs[1])
