@@ -24,6 +24,7 @@
 // so no CTA reads a cache row that this launch writes.
 #include <cooperative_groups.h>
 
+#include <atomic>
 #include <cmath>
 #include <cstdlib>
 #include <type_traits>
@@ -288,16 +289,18 @@ static int launch(cudaStream_t s, const void* q, const void* k_new, const void* 
   constexpr int G = kWarps * (32 / (D / EPV));
   const int64_t bh = b * h;
   const int dev = current_device();
-  static int occ[64] = {0};  // resident CTAs per SM of this instantiation, per device
+  // resident CTAs per SM of this instantiation, per device (set once; racing first calls
+  // store the same value)
+  static std::atomic<int> occ[64];
   if (dev < 0 || dev >= 64) return fail(FERRITE_LAUNCH_FAILED, "attn_decode: device ordinal %d", dev);
-  if (occ[dev] == 0) {
+  if (occ[dev].load(std::memory_order_relaxed) == 0) {
     cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<D, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRingBytes);
     if (e != cudaSuccess) return fail(FERRITE_LAUNCH_FAILED, "attn_decode: shared memory attribute: %s", cudaGetErrorString(e));
     int n = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_attn_kernel<D, T>, kThreads, kRingBytes) != cudaSuccess || n < 1) n = 1;
-    occ[dev] = n;
+    occ[dev].store(n, std::memory_order_relaxed);
   }
-  int c = pick_cluster(bh, max_len, G, (int64_t)num_sms(dev) * occ[dev]);
+  int c = pick_cluster(bh, max_len, G, (int64_t)num_sms(dev) * occ[dev].load(std::memory_order_relaxed));
   if (const char* e = std::getenv("FERRITE_DECODE_CLUSTER")) {  // A/B override: 1, 2, 4 or 8
     const int v = std::atoi(e);
     if (v == 1 || v == 2 || v == 4 || v == 8) c = v;

@@ -32,5 +32,5 @@ def test_reference_arm_json_line():
 def test_help_lists_the_workloads():
     p = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--help"], capture_output=True, text=True, timeout=120, cwd=ROOT)
     assert p.returncode == 0
-    for w in ("norm", "attn", "gemm", "gpt", "prefill"):
+    for w in ("norm", "attn", "gemm", "gpt", "prefill", "decode"):
         assert w in p.stdout

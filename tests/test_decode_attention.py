@@ -90,6 +90,36 @@ def test_decode_python_api_refuses_cpu_tensors():
         decode_attention(q, kc, kc.clone(), torch.zeros(1, dtype=torch.long))
 
 
+def pick_cluster(bh, max_len, groups, slots):
+    """CPU restatement of pick_cluster() in csrc/decode.cu: the largest C in {1, 2, 4, 8}
+    whose grid of bh * C CTAs fits in one wave of `slots` while every CTA keeps at least
+    one row per lane group of a full cache."""
+    c = 1
+    while c < 8 and bh * 2 * c <= slots and max_len // (2 * c) >= groups:
+        c *= 2
+    return c
+
+
+def test_cluster_rule_fills_one_wave():
+    # the bench shape: 8 x 16 slices, 1024 positions, 32 lane groups (d = 64, 16-bit),
+    # 148 SMs x 2 resident CTAs -> 2 CTAs per slice, 256 CTAs (measured best of 1/2/4/8)
+    assert pick_cluster(128, 1024, 32, 296) == 2
+    for bh in (1, 3, 16, 37, 128, 148, 300, 4096):
+        for max_len in (1, 31, 64, 512, 8192):
+            c = pick_cluster(bh, max_len, 32, 296)
+            assert c == 1 or (bh * c <= 296 and max_len // c >= 32)
+            assert c == 8 or bh * 2 * c > 296 or max_len // (2 * c) < 32  # maximal
+
+
+def test_decode_bench_bytes_per_step():
+    import bench
+
+    # 24 layers x 8 x 16 slices at pos 1023, d = 64 bf16: the 1023 cached K and V rows plus
+    # q / k_new / v_new / o and the two written rows, 128 bytes each
+    per_slice = (2 * 1023 + 6) * 64 * 2
+    assert bench.DecodeWorkload.step_bytes(24, 8, 16, 1023, 64) == 24 * 8 * 16 * per_slice == 806_879_232
+
+
 # --------------------------------------------------------------------------- GPU
 
 
