@@ -34,3 +34,15 @@ def test_help_lists_the_workloads():
     assert p.returncode == 0
     for w in ("norm", "attn", "gemm", "gpt", "prefill", "decode"):
         assert w in p.stdout
+
+
+def test_decode_reference_arm_json_line():
+    p = subprocess.run(
+        [sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--workload", "decode", "--steps", "1", "--warmup", "1"],
+        capture_output=True, text=True, timeout=600, cwd=ROOT,
+    )
+    assert p.returncode == 0, p.stderr[-2000:]
+    d = json.loads([ln for ln in p.stdout.splitlines() if ln.startswith("{")][-1])
+    assert d["impl"] == "reference" and d["metric"] == "decode attention HBM GB/s" and d["unit"] == "GB/s"
+    assert d["value"] > 0 and d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["value"] == d["value"]
+    assert d["config"]["workload"] == "gpt_decode_attention_kv_24x8x16x1024x64_pos1023_bf16"
