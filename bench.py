@@ -5,7 +5,12 @@
 
 Workloads (the benchmark configs; synthetic inputs, seeded):
 
-* ``norm`` (default, configs[1]) -- fused residual-add + RMSNorm forward +
+* ``attn`` (default, configs[3]) -- causal flash attention fwd + bwd, b8 h32 s8192
+  d128 bf16 (the north star's primary target), the 256 (batch, head) slices
+  sharded over ranks (strong scaling, no communication).  One step = forward,
+  delta prep, dK/dV (which stores dS) and dQ from dS.  Metric: algorithmic
+  TFLOP/s (fwd + bwd = 3.5 x fwd, flash_attention.py:383-390).
+* ``norm`` -- fused residual-add + RMSNorm forward +
   backward, x/residual bf16 [8192, 4096] ~ N(0,1), weight f32 1 + 0.1 N(0,1),
   eps 1e-6, upstream grads bf16 ~ N(0,1).  One step = ``add_rmsnorm_fwd`` on one
   buffer set + ``rmsnorm_bwd`` (dh and the deterministic dw reduction) on the
@@ -13,9 +18,6 @@ Workloads (the benchmark configs; synthetic inputs, seeded):
   L2-resident operands (L2 is 126 MB).  Metric: algorithmic HBM bytes / s.
   Multi-GPU: weak scaling, every rank normalises its own 8192-token shard; the
   only exchange is the backward's all-reduce of the f32 dw partial (16 KiB).
-* ``attn`` -- causal flash attention fwd + bwd, b8 h32 s8192 d128
-  bf16, heads sharded over ranks (strong scaling, no communication).  Metric:
-  algorithmic TFLOP/s (fwd + bwd = 3.5 x fwd, flash_attention.py:383-390).
 * ``gemm`` -- bf16 8192^3 forward + the two backward GEMMs of the
   VJP; replicas at N > 1.  Metric: TFLOP/s.
 * ``gpt`` -- GPT training step (d1024 L24 H16 ff4096 V32000 s1024,
@@ -169,6 +171,43 @@ def _events(n):
     return [torch.cuda.Event(enable_timing=True) for _ in range(n)]
 
 
+def _oracle_pool(workers: int):
+    """A process pool for the CPU oracle: spawned (never forked from a process that
+    holds a CUDA context) with single-threaded BLAS in every worker, so ``workers``
+    processes use ``workers`` cores."""
+    import concurrent.futures as cf
+    import multiprocessing as mp
+
+    keys = ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS")
+    saved = {k: os.environ.get(k) for k in keys}
+    os.environ.update({k: "1" for k in keys})
+    try:
+        ex = cf.ProcessPoolExecutor(max_workers=workers, mp_context=mp.get_context("spawn"))
+        list(ex.map(abs, range(workers)))  # start every worker while the variables are set
+    finally:
+        for k, v in saved.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
+    return ex
+
+
+def _attn_oracle_slice(args):
+    """One causal (b, h) slice through the oracle's blockwise forward and backward."""
+    seed, s, d = args
+    import ml_dtypes
+
+    sys.path.insert(0, ROOT)
+    from oracle import attention as oa
+
+    rng = np.random.default_rng(seed)
+    q, k, v, do = (rng.standard_normal((1, 1, s, d), dtype=np.float32).astype(ml_dtypes.bfloat16) for _ in range(4))
+    o, lse = oa.flash_fwd(q, k, v, causal=True)
+    oa.flash_bwd(q, k, v, o, lse, do, causal=True)
+    return s
+
+
 # ----------------------------------------------------------------------------- workloads
 
 
@@ -282,13 +321,19 @@ class NormWorkload:
         bwd = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
         return {"add_rmsnorm_fwd": fwd, "rmsnorm_bwd+dw_reduce": bwd}
 
-    def config(self):
+    @classmethod
+    def static_config(cls, ws):
+        """The config keys, from the class (the reference arm prints the same ones)."""
         return {
-            "workload": self.name, "rows_per_gpu": self.ROWS, "dim": self.DIM, "eps": self.EPS,
-            "algorithmic_bytes_per_step_per_gpu": self.units_per_step,
+            "workload": cls.name, "rows_per_gpu": cls.ROWS, "dim": cls.DIM, "eps": cls.EPS,
+            "algorithmic_bytes_per_step_per_gpu": cls.FWD_BYTES + cls.BWD_BYTES,
             "l2": "inputs larger than L2 (two 448 MiB buffer sets alternate)",
-            "parallelism": f"tokens sharded, {self.ws} rank(s), dw all-reduce" if self.ws > 1 else "single GPU",
+            "parallelism": f"tokens sharded, {ws} rank(s), dw all-reduce" if ws > 1 else "single GPU",
         }
+
+    def config(self):
+        return {**self.static_config(self.ws), "rows_per_gpu": self.ROWS, "dim": self.DIM,
+                "algorithmic_bytes_per_step_per_gpu": self.units_per_step}
 
     def e2e_setup(self):
         s = self.sets[0]
@@ -430,10 +475,16 @@ class AttnWorkload:
     def breakdown(self, evs):
         return {k: statistics.mean(e[j].elapsed_time(e[j + 1]) for e in evs) for j, k in enumerate(self.kernels)}
 
-    def config(self):
-        return {"workload": self.name, "batch": self.B, "heads": self.H, "seq_len": self.S, "head_dim": self.D, "causal": True,
-                "block_q": 128, "block_k": 128, "heads_per_gpu": self.bh_local, "parallelism": f"batch*heads sharded over {self.ws} rank(s)",
+    @classmethod
+    def static_config(cls, ws):
+        """The config keys, from the class (the reference arm prints the same ones)."""
+        return {"workload": cls.name, "batch": cls.B, "heads": cls.H, "seq_len": cls.S, "head_dim": cls.D, "causal": True,
+                "block_q": 128, "block_k": 128, "heads_per_gpu": cls.B * cls.H // ws, "parallelism": f"batch*heads sharded over {ws} rank(s)",
                 "l2": "inputs larger than L2 (q, k, v, dO 512 MiB each at 1 GPU)"}
+
+    def config(self):
+        return {**self.static_config(self.ws), "batch": self.B, "heads": self.H, "seq_len": self.S, "head_dim": self.D,
+                "heads_per_gpu": self.bh_local}
 
     def e2e_setup(self):
         self.host = {k: getattr(self, k).cpu().pin_memory() for k in ("q", "k", "v", "do")}
@@ -454,25 +505,26 @@ class AttnWorkload:
             self.out_host[name].copy_(t, non_blocking=True)
 
     @classmethod
-    def cpu_baseline(cls, slices=1, threads=None):
+    def cpu_baseline(cls, slices=None, threads=None):
         """The oracle's blockwise fwd + bwd (numpy) on ``slices`` of the 256 independent
-        (b, h) slices, extrapolated linearly to the whole config."""
-        import ml_dtypes
-
+        (b, h) slices (default: one per host core), one slice per process of a spawned
+        pool with single-threaded BLAS in each, extrapolated linearly to the whole
+        config (the slices are independent, so the work is linear in their number)."""
+        threads = threads or _host_cores()
+        slices = slices or threads
+        with _oracle_pool(threads) as ex:
+            list(ex.map(_attn_oracle_slice, [(i, 512, cls.D) for i in range(threads)]))  # warm-up: imports, BLAS
+            t0 = time.perf_counter()
+            list(ex.map(_attn_oracle_slice, [(i, cls.S, cls.D) for i in range(slices)]))
+            t = time.perf_counter() - t0
         sys.path.insert(0, ROOT)
         from oracle import attention as oa
 
-        rng = np.random.default_rng(0)
-        bf = ml_dtypes.bfloat16
-        q, k, v, do = (rng.standard_normal((1, slices, cls.S, cls.D), dtype=np.float32).astype(bf) for _ in range(4))
-        t0 = time.perf_counter()
-        o, lse = oa.flash_fwd(q, k, v, causal=True)
-        oa.flash_bwd(q, k, v, o, lse, do, causal=True)
-        t = time.perf_counter() - t0
         flops = 3.5 * oa.attention_flops(1, slices, cls.S, cls.S, cls.D, causal=True)
-        return {"value": flops / t / 1e12, "unit": "TFLOP/s", "cores": threads or _host_cores(), "kind": "port",
-                "sample": f"{slices} of {cls.B * cls.H} (b,h) slices, numpy blockwise oracle (BLAS threads)", "seconds_per_sample": t,
-                "sample_fraction": slices / (cls.B * cls.H)}
+        return {"value": flops / t / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                "sample": f"{slices} of {cls.B * cls.H} (b,h) slices of {cls.S} x {cls.D}, numpy blockwise oracle fwd+bwd, "
+                          f"{threads} spawned processes (one slice each, single-threaded BLAS); extrapolated linearly in slices",
+                "seconds_per_sample": t, "sample_fraction": slices / (cls.B * cls.H)}
 
 
 class GemmWorkload:
@@ -997,18 +1049,14 @@ def run_ours(args, ws, rank, local):
         dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
     e2e_value = wl.units_per_step * ws * args.steps / (float(e_ms.item()) / 1e3) / scale
 
-    from ferrite import platform
+    from ferrite.profiling import roofline as rl
 
-    pk = platform.peaks()
-    dom = max((k for k in bd if wl.kernel_work.get(k)), key=lambda k: bd[k])
-    long_step = args.workload == "gpt"
-    if wl.bound == "hbm":
-        achieved = wl.kernel_work[dom] / (bd[dom] / 1e3) / 1e9
-        peak, unit, psrc = pk.hbm_bytes_per_s / 1e9, "GB/s", "hbm_gbs"
-    else:
-        achieved = wl.kernel_work[dom] / (bd[dom] / 1e3) / 1e12
-        peak = (pk.bf16_flops_sustained if long_step else pk.bf16_flops) / 1e12
-        unit, psrc = "TFLOP/s", "bf16_tflops_sustained" if long_step else "bf16_tflops"
+    dom = rl.dominant(bd, wl.kernel_work)
+    # burst tensor peak for a sub-second timed region, sustained for a longer one
+    sustained = rl.Ceilings.from_platform().for_region(ms / 1e3)
+    work = wl.kernel_work[dom]
+    point = rl.analyze(dom, flops=work if wl.bound == "tensor" else 0.0, bytes_=work if wl.bound == "hbm" else 0.0,
+                       seconds=bd[dom] / 1e3, sustained=sustained)
     out = {
         "metric": wl.metric,
         "value": round(value, 3),
@@ -1024,15 +1072,7 @@ def run_ours(args, ws, rank, local):
         "data": "synthetic",
         "config": wl.config(),
         "roofline": {
-            "bound": wl.bound,
-            "kernel": dom,
-            "achieved": round(achieved, 2),
-            "peak": round(peak, 1),
-            "unit": unit,
-            "frac": round(achieved / peak, 4),
-            "peak_source": f"{pk.source} (MEASURED_PEAKS.json {psrc})" if pk.source == "measured" else "fallback",
-            **({"frac_of_sustained": round(achieved / (pk.bf16_flops_sustained / 1e12), 4)} if wl.bound == "tensor" and not long_step else {}),
-            "traffic": _load_traffic(dom),
+            **point.line(traffic=_load_traffic(dom)),
             "timing": "kernel times from a second pass of the same K steps with CUDA events between kernels",
             "kernels_ms": {k: round(v, 5) for k, v in bd.items()},
         },
@@ -1079,7 +1119,7 @@ def run_reference(args, ws, rank):
         "dtype": "bf16",
         "data": "synthetic",
         "impl": "reference",
-        "config": {"workload": W.name},
+        "config": W.static_config(ws) if hasattr(W, "static_config") else {"workload": W.name},
         "cpu_baseline": {"value": round(v, 4), "unit": W.unit, "cores": base["cores"], "kind": base["kind"], "sample": base["sample"]},
         "e2e": {"value": round(v, 4), "unit": W.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "JAX (the reference's runtime) is not installable here; the reference's CPU path is timed as its restatement in oracle/",
@@ -1093,7 +1133,7 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="norm")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="attn")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--shape", default=None, help="smaller case for profiling captures: norm rows,dim | attn b,h,s,d | gemm m,n,k | decode layers,b,h,max_len,d")
     args = ap.parse_args(argv)

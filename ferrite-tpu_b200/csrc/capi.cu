@@ -209,7 +209,8 @@ int ferrite_device_status(void* stream, int clear) {
     return ferrite::fail(FERRITE_LAUNCH_FAILED, "stream sync failed: %s",
                          cudaGetErrorString(e));
   int v = 0;
-  for (int st : {ferrite::status_gemm(clear), ferrite::status_attention(clear)})
+  for (int st : {ferrite::status_gemm(clear), ferrite::status_attention(clear),
+                 ferrite::status_rmsnorm(clear)})
     if (v == 0 && st != 0) v = st;
   if (v != 0)
     return ferrite::fail(v, "device reported status %d (a bounded wait expired)", v);

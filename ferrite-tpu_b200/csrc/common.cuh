@@ -94,6 +94,7 @@ static __device__ int g_device_status = 0;
   }
 int status_gemm(int clear);
 int status_attention(int clear);
+int status_rmsnorm(int clear);
 
 // --------------------------------------------------------------------------
 // device: dtype helpers
@@ -209,12 +210,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait for phase `parity` of `bar`.  Returns false (and records
-// FERRITE_DEVICE_TIMEOUT in the device status word) if the wait expired or if
-// *abort became non-zero while waiting; callers then skip their remaining work
-// and fall through to the CTA's teardown.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          volatile int* abort, int where) {
+// Bounded wait for phase `parity` of `bar`, at most `limit_ns` of %globaltimer.
+// Returns false (and records FERRITE_DEVICE_TIMEOUT in the device status word)
+// if the wait expired or if *abort became non-zero while waiting; callers then
+// skip their remaining work and fall through to the CTA's teardown.
+__device__ __forceinline__ bool mbar_wait_ns(uint64_t* bar, uint32_t parity,
+                                             volatile int* abort, int where,
+                                             uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   uint32_t spins = 0;
@@ -222,13 +224,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
     if (mbar_try_wait(bar, parity)) return true;
     if ((++spins & 255u) == 0) {
       if (*abort) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > limit_ns) {
         report_timeout(where);
         *abort = 1;
         return false;
       }
     }
   }
+}
+// The kernels' wait: the same, with the library-wide limit kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          volatile int* abort, int where) {
+  return mbar_wait_ns(bar, parity, abort, where, kWaitLimitNs);
 }
 
 // --------------------------------------------------------------------------

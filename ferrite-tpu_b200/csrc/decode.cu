@@ -386,4 +386,18 @@ int ferrite_attn_decode(void* stream, const void* q, const void* k_new, const vo
   return dispatch_d<float>(s, q, k_new, v_new, k_cache, v_cache, pos, out, b, h, max_len, d, ld_new, scale);
 }
 
+// The cluster size ferrite_attn_decode launches with for b*h slices, without
+// launching anything: the compiled rule above, with the lane groups of (d, dtype).
+int ferrite_attn_decode_cluster(int64_t bh, int64_t max_len, int64_t d, int dtype, int64_t slots) {
+  if (bh < 1 || max_len < 1 || slots < 1)
+    return fail(FERRITE_BAD_SHAPE, "attn_decode_cluster: bh, max_len and slots must be positive"), -1;
+  if (dtype != FERRITE_BF16 && dtype != FERRITE_F16 && dtype != FERRITE_F32)
+    return fail(FERRITE_UNSUPPORTED_DTYPE, "attn_decode_cluster: dtype %d", dtype), -1;
+  const int64_t epv = dtype == FERRITE_F32 ? 4 : 8;  // elements per 16-byte vector
+  if (d % epv != 0 || d / epv > 32 || 32 % (d / epv) != 0)
+    return fail(FERRITE_BAD_SHAPE, "attn_decode_cluster: head_dim %lld", (long long)d), -1;
+  const int groups = kWarps * (int)(32 / (d / epv));
+  return pick_cluster(bh, max_len, groups, slots);
+}
+
 }  // extern "C"

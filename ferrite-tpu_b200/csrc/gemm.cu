@@ -901,3 +901,80 @@ extern "C" int ferrite_gemm_ws(void* stream, const void* a, const void* b, void*
   return SIMT(__half, __half);
 #undef SIMT
 }
+
+// ---------------------------------------------------------------------------
+// Bounded-wait check: the failure path every tcgen05 kernel here takes when an
+// mbarrier wait runs out, exercised on purpose with a short limit.
+// ---------------------------------------------------------------------------
+namespace ferrite {
+namespace gemm {
+
+// One CTA of four warps, laid out like the tensor-core kernels: warp 1 holds a
+// TMEM allocation; lane 0 of warp 1 (the "MMA issuer") waits on an mbarrier that
+// nothing ever arrives on, for at most `limit_ns`; lane 0 of warps 0, 2 and 3
+// wait on a second such barrier and leave through the CTA's abort flag.  The
+// expired wait records FERRITE_DEVICE_TIMEOUT in the status word.  Teardown is
+// the kernels' own: __syncthreads, then the allocating warp frees TMEM.
+// out[0] = ns the issuer waited, out[1] = 1 if its wait reported a timeout,
+// out[2] = number of waiters that left (4), out[3] = 1 once TMEM was freed.
+__global__ void __launch_bounds__(128) wait_probe_kernel(uint64_t limit_ns,
+                                                         unsigned long long* out) {
+  __shared__ __align__(8) uint64_t bars[2];
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+  __shared__ int left;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  volatile int* abort = &abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    abort_flag = 0;
+    left = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_slot, 32);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_slot;
+  if (lane == 0) {
+    if (warp == 1) {
+      const uint64_t t0 = globaltimer_ns();
+      const bool ok = mbar_wait_ns(&bars[0], 0, abort, 90, limit_ns);
+      out[0] = globaltimer_ns() - t0;
+      out[1] = ok ? 0ull : 1ull;
+    } else {
+      // a bound 4x longer, so these leave through the abort flag the issuer raises
+      (void)mbar_wait_ns(&bars[1], 0, abort, 91, 4 * limit_ns);
+    }
+    atomicAdd(&left, 1);
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 32);
+    __syncwarp();
+    if (lane == 0) {
+      out[2] = (unsigned long long)left;
+      out[3] = 1ull;
+    }
+  }
+}
+
+}  // namespace gemm
+}  // namespace ferrite
+
+extern "C" FERRITE_API int ferrite_wait_probe(void* stream, uint64_t limit_ns, void* out) {
+  using namespace ferrite;
+  if (limit_ns == 0 || limit_ns > kWaitLimitNs)
+    return fail(FERRITE_BAD_SHAPE, "wait_probe: limit %llu ns outside (0, %llu]",
+                (unsigned long long)limit_ns, (unsigned long long)kWaitLimitNs);
+  if (!out || (reinterpret_cast<uintptr_t>(out) & 7u))
+    return fail(FERRITE_BAD_ALIGNMENT, "wait_probe: out must be an 8-byte aligned device pointer");
+  gemm::wait_probe_kernel<<<1, 128, 0, (cudaStream_t)stream>>>(limit_ns, (unsigned long long*)out);
+  return check_launch("wait_probe");
+}

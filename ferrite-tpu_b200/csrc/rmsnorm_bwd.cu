@@ -5,6 +5,10 @@
 #include "rmsnorm_common.cuh"
 
 namespace ferrite {
+// The TMA-ring backward bounds its mbarrier waits; an expired wait is recorded in
+// this translation unit's status word, which ferrite_device_status() polls.
+FERRITE_DEFINE_STATUS_READER(status_rmsnorm)
+
 namespace norm {
 
 // ---------------------------------------------------------------------------
@@ -559,22 +563,36 @@ std::mutex g_noalloc_mu;
 float* g_noalloc_ptr[64] = {nullptr};
 }  // namespace
 
-// Device address of g_noalloc_partials on `device` (which must be current).  In
-// host code the array's name is only a host-side stand-in, so the address is
-// looked up once per device with cudaGetSymbolAddress and cached.
-static int noalloc_partials(int device, float** out) {
-  if (device < 0 || device >= 64)
-    return fail(FERRITE_BAD_SHAPE, "rmsnorm_bwd_noalloc: device ordinal %d out of range", device);
-  std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_ptr[device] == nullptr) {
-    void* addr = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&addr, g_noalloc_partials);
-    if (e != cudaSuccess || addr == nullptr)
-      return fail(FERRITE_LAUNCH_FAILED, "rmsnorm_bwd_noalloc: cudaGetSymbolAddress failed: %s",
-                  cudaGetErrorString(e));
-    g_noalloc_ptr[device] = static_cast<float*>(addr);
+// Device address of g_noalloc_partials on the current device, and that device.
+// In host code the array's name is only a host-side stand-in, so the address is
+// looked up once per device with cudaGetSymbolAddress (that device current) and
+// cached.  The cache belongs to the device's primary context in this process: a
+// process that calls cudaDeviceReset must not call the allocation-free entry
+// point on that device afterwards.
+static int noalloc_partials(int* device, float** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess)
+    return fail(FERRITE_LAUNCH_FAILED, "rmsnorm_bwd_noalloc: cudaGetDevice failed: %s",
+                cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64)
+    return fail(FERRITE_LAUNCH_FAILED, "rmsnorm_bwd_noalloc: device ordinal %d beyond the 64 the address cache holds", dev);
+  *device = dev;
+  float* p = __atomic_load_n(&g_noalloc_ptr[dev], __ATOMIC_ACQUIRE);
+  if (p == nullptr) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    p = g_noalloc_ptr[dev];
+    if (p == nullptr) {
+      void* addr = nullptr;
+      e = cudaGetSymbolAddress(&addr, g_noalloc_partials);
+      if (e != cudaSuccess || addr == nullptr)
+        return fail(FERRITE_LAUNCH_FAILED, "rmsnorm_bwd_noalloc: cudaGetSymbolAddress failed: %s",
+                    cudaGetErrorString(e));
+      p = static_cast<float*>(addr);
+      __atomic_store_n(&g_noalloc_ptr[dev], p, __ATOMIC_RELEASE);
+    }
   }
-  *out = g_noalloc_ptr[device];
+  *out = p;
   return FERRITE_OK;
 }
 
@@ -582,9 +600,9 @@ template <typename T, typename TW, bool HAS_DH>
 static int run_bwd_noalloc(cudaStream_t s, const void* h, const void* w, const void* dy,
                            const void* dhd, void* dh, void* dw, int64_t rows, int64_t dim,
                            float eps) {
-  const int dev = current_device();
+  int dev = 0;
   float* part = nullptr;
-  if (int rc = noalloc_partials(dev, &part)) return rc;
+  if (int rc = noalloc_partials(&dev, &part)) return rc;
   const void* ptrs[5] = {h, dy, HAS_DH ? dhd : nullptr, dh, w};
   BwdPlan p = plan_bwd<T, TW, HAS_DH>(rows, dim, ptrs, 5, dev);
   // Fit the partial rows into the fixed buffer (the persistent kernels accept

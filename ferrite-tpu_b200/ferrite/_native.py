@@ -13,6 +13,8 @@ on a CUDA device, the call raises.  The library is built in-tree by
 from __future__ import annotations
 
 import ctypes
+import functools
+import itertools
 import os
 import threading
 
@@ -76,6 +78,7 @@ SIGNATURES: dict[str, tuple] = {
     "ferrite_last_error": (ctypes.c_char_p, []),
     "ferrite_version": (ctypes.c_char_p, []),
     "ferrite_device_status": (_i32, [_vp, _i32]),
+    "ferrite_wait_probe": (_i32, [_vp, ctypes.c_uint64, _vp]),
     "ferrite_rmsnorm_fwd": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _f32, _i32, _i32]),
     "ferrite_add_rmsnorm_fwd": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f32, _i32, _i32]),
     "ferrite_rmsnorm_bwd_workspace_size": (_sz, [_i64, _i64]),
@@ -102,6 +105,7 @@ SIGNATURES: dict[str, tuple] = {
     "ferrite_attn_bwd_dkv_strided": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sp, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _i32, _i32, _i32]),
     "ferrite_attn_bwd_dq_strided": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sp, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _i32, _i32, _i32]),
     "ferrite_attn_decode": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _f32, _i32]),
+    "ferrite_attn_decode_cluster": (_i32, [_i64, _i64, _i64, _i32, _i64]),
 }
 
 
@@ -171,6 +175,25 @@ def require_cuda(*tensors: torch.Tensor) -> None:
                 "ferrite kernels run on CUDA tensors only (got a tensor on "
                 f"{t.device}); there is no CPU fallback in the product path"
             )
+
+
+def on_tensor_device(fn):
+    """Decorator: run ``fn`` with the device of its first CUDA tensor argument
+    current.  The library plans and launches on the current device (SM count,
+    occupancy, kernel attributes, per-device caches) and the stream it is handed is
+    that device's, so a call on tensors of another GPU must switch to it first."""
+
+    @functools.wraps(fn)
+    def wrapper(*args, **kwargs):
+        for a in itertools.chain(args, kwargs.values()):
+            if isinstance(a, torch.Tensor) and a.is_cuda:
+                if a.device.index == torch.cuda.current_device():
+                    break
+                with torch.cuda.device(a.device):
+                    return fn(*args, **kwargs)
+        return fn(*args, **kwargs)
+
+    return wrapper
 
 
 def ptr(t: torch.Tensor | None) -> int | None:

@@ -31,6 +31,7 @@ def _target_code(t: torch.Tensor) -> int:
     raise TypeError(f"targets must be int32 or int64, got {t.dtype}")
 
 
+@nat.on_tensor_device
 def xent_forward(logits: torch.Tensor, targets: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """``(lse, nll)`` per row of f32 ``logits [rows, vocab]``."""
     nat.require_cuda(logits, targets)
@@ -51,6 +52,7 @@ def xent_forward(logits: torch.Tensor, targets: torch.Tensor) -> tuple[torch.Ten
     return lse, nll
 
 
+@nat.on_tensor_device
 def xent_backward(logits, targets, lse, dloss: torch.Tensor | None, scale: float, out_dtype=torch.float32) -> torch.Tensor:
     """``dlogits = dloss * scale * (softmax(logits) - onehot(targets))`` as ``out_dtype``."""
     nat.require_cuda(logits, targets, lse)

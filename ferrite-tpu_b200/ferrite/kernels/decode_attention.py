@@ -21,6 +21,7 @@ from ferrite import _native as nat
 _HEAD_DIMS = {torch.bfloat16: (32, 64, 128, 256), torch.float16: (32, 64, 128, 256), torch.float32: (32, 64, 128)}
 
 
+@nat.on_tensor_device
 def decode_attention(
     q: torch.Tensor,
     k_cache: torch.Tensor,

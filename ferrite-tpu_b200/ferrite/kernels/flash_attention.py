@@ -91,6 +91,7 @@ def _unit_d(t):
     return t if t.stride(3) == 1 else t.contiguous()
 
 
+@nat.on_tensor_device
 def _forward(q, k, v, causal: bool, scale: float, bs: BlockSizes, out=None):
     """``(out, lse)``; ``out`` may be a caller-provided strided [b, h, s, d] view."""
     nat.require_cuda(q, k, v)
@@ -110,6 +111,7 @@ def _forward(q, k, v, causal: bool, scale: float, bs: BlockSizes, out=None):
     return out, lse
 
 
+@nat.on_tensor_device
 def _backward(q, k, v, out, lse, do, causal: bool, scale: float, bs: BlockSizes, dq=None, dk=None, dv=None):
     """``(dq, dk, dv)``; the gradients may be caller-provided strided views."""
     nat.require_cuda(q, k, v, out, lse, do)

@@ -31,6 +31,7 @@ def _pick_blocks(m: int, n: int, k: int, bm, bn, bk):
     return bm, bn, bk
 
 
+@nat.on_tensor_device
 def gemm(a: torch.Tensor, b: torch.Tensor, *, trans_a: bool = False, trans_b: bool = False, out_dtype=None, out: torch.Tensor | None = None) -> torch.Tensor:
     """``op(a) @ op(b)`` through ``ferrite_gemm``; ``op`` transposes the stored 2-D tensor.
 

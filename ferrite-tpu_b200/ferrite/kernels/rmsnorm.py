@@ -27,6 +27,7 @@ def _check_block_rows(block_rows):
         raise ValueError(f"block_rows must be a multiple of {platform.SUBLANES}")
 
 
+@nat.on_tensor_device
 def _fwd(x2d: torch.Tensor, w: torch.Tensor, r2d: torch.Tensor | None, eps: float):
     nat.require_cuda(x2d, w, r2d)
     rows, dim = x2d.shape
@@ -45,6 +46,7 @@ def _fwd(x2d: torch.Tensor, w: torch.Tensor, r2d: torch.Tensor | None, eps: floa
     return h, y
 
 
+@nat.on_tensor_device
 def rmsnorm_backward(h: torch.Tensor, w: torch.Tensor, dy: torch.Tensor, dh_direct: torch.Tensor | None, eps: float):
     """Native backward: returns (dh, dw) with dh in h.dtype and dw in w.dtype."""
     nat.require_cuda(h, w, dy, dh_direct)

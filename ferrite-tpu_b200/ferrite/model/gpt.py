@@ -175,8 +175,9 @@ class _FusedMlp(torch.autograd.Function):
         f = w1.shape[1]
         u = torch.empty((t, f), dtype=y.dtype, device=y.device)
         a = torch.empty_like(u)
-        nat.check(nat.lib().ferrite_gemm_epilogue(nat.stream_ptr(y.device), y.data_ptr(), w1.data_ptr(), u.data_ptr(),
-                                                  t, f, d, y.stride(0), w1.stride(0), u.stride(0), 0, 0, 1, a.data_ptr(), a.stride(0)))
+        with torch.cuda.device(y.device):
+            nat.check(nat.lib().ferrite_gemm_epilogue(nat.stream_ptr(y.device), y.data_ptr(), w1.data_ptr(), u.data_ptr(),
+                                                      t, f, d, y.stride(0), w1.stride(0), u.stride(0), 0, 0, 1, a.data_ptr(), a.stride(0)))
         ctx.save_for_backward(y, w1, w2, u, a)
         return gemm(a, w2)
 
@@ -188,8 +189,9 @@ class _FusedMlp(torch.autograd.Function):
         dp = dp.to(y.dtype).contiguous()
         t, f = u.shape
         du = torch.empty_like(u)
-        nat.check(nat.lib().ferrite_gemm_epilogue(nat.stream_ptr(y.device), dp.data_ptr(), w2.data_ptr(), du.data_ptr(),
-                                                  t, f, dp.shape[1], dp.stride(0), w2.stride(0), du.stride(0), 0, 1, 2, u.data_ptr(), u.stride(0)))
+        with torch.cuda.device(y.device):
+            nat.check(nat.lib().ferrite_gemm_epilogue(nat.stream_ptr(y.device), dp.data_ptr(), w2.data_ptr(), du.data_ptr(),
+                                                      t, f, dp.shape[1], dp.stride(0), w2.stride(0), du.stride(0), 0, 1, 2, u.data_ptr(), u.stride(0)))
         dw2 = gemm(a, dp, trans_a=True, out_dtype=w2.dtype)  # A^T dP
         dy = gemm(du, w1, trans_b=True, out_dtype=y.dtype)  # dU W1^T
         dw1 = gemm(y, du, trans_a=True, out_dtype=w1.dtype)  # Y^T dU

@@ -256,13 +256,14 @@ class FusedAdamW:
     def update(self, grads=None, grad_scale: float = 1.0) -> torch.Tensor:
         self.step += 1
         cfg, nat = self.cfg, self.nat
-        nat.check(
-            self.lib.ferrite_adamw_step(
-                nat.stream_ptr(self.flat.device), self.flat.data_ptr(), self.grads.flat.data_ptr(), self.m.data_ptr(),
-                self.v.data_ptr(), self.n, self.n_decay, lr_at(self.step, cfg), self.b1, self.b2, self.eps,
-                cfg.weight_decay, self.step, cfg.clip, grad_scale, self.gnorm.data_ptr(), self.ws.data_ptr(), self.ws.numel(),
+        with torch.cuda.device(self.flat.device):
+            nat.check(
+                self.lib.ferrite_adamw_step(
+                    nat.stream_ptr(self.flat.device), self.flat.data_ptr(), self.grads.flat.data_ptr(), self.m.data_ptr(),
+                    self.v.data_ptr(), self.n, self.n_decay, lr_at(self.step, cfg), self.b1, self.b2, self.eps,
+                    cfg.weight_decay, self.step, cfg.clip, grad_scale, self.gnorm.data_ptr(), self.ws.data_ptr(), self.ws.numel(),
+                )
             )
-        )
         return self.gnorm.clone()
 
 

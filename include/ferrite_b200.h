@@ -60,6 +60,17 @@ FERRITE_API const char* ferrite_version(void);
  * (FERRITE_OK or FERRITE_DEVICE_TIMEOUT) and, if `clear` != 0, resets it. */
 FERRITE_API int ferrite_device_status(void* stream, int clear);
 
+/* Exercises the bounded-wait failure path of the tensor-core kernels: one CTA holds
+ * a TMEM allocation and waits on an mbarrier that nothing arrives on, for at most
+ * `limit_ns` (0 < limit_ns <= the library's 2 s bound).  The wait expires, the
+ * status word reads FERRITE_DEVICE_TIMEOUT, the other waiters leave through the
+ * CTA's abort flag and TMEM is freed before the CTA exits.  `out` is 4 u64 on the
+ * device: ns waited, 1 if the wait reported a timeout, waiters that left (4),
+ * 1 once TMEM was freed.  No counterpart kernel in the reference: its stand-in is
+ * the interpret-mode data-race detector run over the kernels
+ * (tests/test_flash_attention.py:79-85); Mosaic kernels have no device waits. */
+FERRITE_API int ferrite_wait_probe(void* stream, uint64_t limit_ns, void* out);
+
 /* ---- fused residual-add + RMSNorm ------------------------------------------- */
 
 /* y = x * rsqrt(mean(x^2) + eps) * w over the last axis of x[rows, dim].
@@ -352,6 +363,16 @@ FERRITE_API int ferrite_attn_decode(void* stream, const void* q, const void* k_n
                         const void* v_new, void* k_cache, void* v_cache, const int64_t* pos,
                         void* o, int64_t b, int64_t h, int64_t max_len, int64_t d,
                         int64_t ld_new, float scale, int dtype);
+
+/* The thread-block cluster size (1, 2, 4 or 8 CTAs per (batch, head) slice) that
+ * ferrite_attn_decode launches for `bh` = b * h slices of a `max_len`-row cache of
+ * head_dim `d` and dtype `dtype` on a GPU with `slots` resident CTAs (SMs x CTAs per
+ * SM): the largest C whose grid of bh * C CTAs fits in one wave while every CTA keeps
+ * at least one row per lane group.  Host-only (launches nothing); returns -1 with
+ * the error set for invalid arguments.  No counterpart in the reference, whose
+ * decode attention is an XLA fusion (serving/engine.py:89-95). */
+FERRITE_API int ferrite_attn_decode_cluster(int64_t bh, int64_t max_len, int64_t d, int dtype,
+                                            int64_t slots);
 
 #ifdef __cplusplus
 }

@@ -11,7 +11,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 def test_reference_arm_json_line():
     p = subprocess.run(
-        [sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "2", "--warmup", "1"],
+        [sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--workload", "norm", "--steps", "2", "--warmup", "1"],
         capture_output=True, text=True, timeout=600, cwd=ROOT,
     )
     assert p.returncode == 0, p.stderr[-2000:]
@@ -27,6 +27,24 @@ def test_reference_arm_json_line():
     assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == d["value"] and cb["sample"]
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     assert d["config"]["workload"] == "add_rmsnorm_fwd_bwd_bf16_8192x4096"
+    assert d["config"]["rows_per_gpu"] == 8192 and d["config"]["dim"] == 4096  # the same keys as the GPU arm's config
+
+
+def test_default_reference_arm_is_the_long_attention_config():
+    """The default workload is the north star's primary target; its reference arm times
+    the oracle on one (b, h) slice per host core in spawned processes."""
+    p = subprocess.run(
+        [sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "1", "--warmup", "1"],
+        capture_output=True, text=True, timeout=900, cwd=ROOT,
+    )
+    assert p.returncode == 0, p.stderr[-2000:]
+    d = json.loads([ln for ln in p.stdout.splitlines() if ln.startswith("{")][-1])
+    assert d["impl"] == "reference" and d["metric"] == "causal flash-attn fwd+bwd TFLOP/s" and d["unit"] == "TFLOP/s"
+    assert d["scaling"] == "strong" and d["value"] > 0
+    cfg = d["config"]
+    assert cfg["workload"] == "flash_attention_causal_fwd_bwd_b8_h32_s8192_d128_bf16"
+    assert (cfg["batch"], cfg["heads"], cfg["seq_len"], cfg["head_dim"]) == (8, 32, 8192, 128)
+    assert d["cpu_baseline"]["cores"] >= 1 and "spawned processes" in d["cpu_baseline"]["sample"]
 
 
 def test_help_lists_the_workloads():

@@ -90,25 +90,25 @@ def test_decode_python_api_refuses_cpu_tensors():
         decode_attention(q, kc, kc.clone(), torch.zeros(1, dtype=torch.long))
 
 
-def pick_cluster(bh, max_len, groups, slots):
-    """CPU restatement of pick_cluster() in csrc/decode.cu: the largest C in {1, 2, 4, 8}
-    whose grid of bh * C CTAs fits in one wave of `slots` while every CTA keeps at least
-    one row per lane group of a full cache."""
-    c = 1
-    while c < 8 and bh * 2 * c <= slots and max_len // (2 * c) >= groups:
-        c *= 2
-    return c
+def _cluster(bh, max_len, d=64, dtype=None, slots=296):
+    """The cluster size the compiled rule in csrc/decode.cu picks (host-only query)."""
+    return nat.lib().ferrite_attn_decode_cluster(bh, max_len, d, nat.BF16 if dtype is None else dtype, slots)
 
 
 def test_cluster_rule_fills_one_wave():
-    # the bench shape: 8 x 16 slices, 1024 positions, 32 lane groups (d = 64, 16-bit),
+    # the bench shape: 8 x 16 slices, 1024 positions, d = 64 bf16 (32 lane groups per CTA),
     # 148 SMs x 2 resident CTAs -> 2 CTAs per slice, 256 CTAs (measured best of 1/2/4/8)
-    assert pick_cluster(128, 1024, 32, 296) == 2
+    assert _cluster(128, 1024) == 2
+    groups = 32  # d = 64, 16-bit: 8 lanes a row, 4 rows a warp, 8 warps
     for bh in (1, 3, 16, 37, 128, 148, 300, 4096):
         for max_len in (1, 31, 64, 512, 8192):
-            c = pick_cluster(bh, max_len, 32, 296)
-            assert c == 1 or (bh * c <= 296 and max_len // c >= 32)
-            assert c == 8 or bh * 2 * c > 296 or max_len // (2 * c) < 32  # maximal
+            c = _cluster(bh, max_len)
+            assert c in (1, 2, 4, 8)
+            assert c == 1 or (bh * c <= 296 and max_len // c >= groups)
+            assert c == 8 or bh * 2 * c > 296 or max_len // (2 * c) < groups  # maximal
+    # lane groups follow (d, dtype): d = 128 bf16 has 16 per CTA, f32 d = 128 has 8
+    assert _cluster(1, 64, d=128) == 4 and _cluster(1, 64, d=128, dtype=nat.F32) == 8
+    assert _cluster(0, 64) == -1 and _cluster(4, 64, d=48) == -1
 
 
 def test_decode_bench_bytes_per_step():
