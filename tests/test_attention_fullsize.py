@@ -20,7 +20,7 @@ import numpy as np
 import pytest
 import torch
 
-from ferrite.kernels import flash_attention as fa
+from ferrite.kernels.flash_attention import DS_WORKSPACE_BUDGET, flash_attention, flash_attention_packed
 from helpers import max_abs, rel_l2, to_numpy
 from oracle import attention as oa
 
@@ -49,10 +49,10 @@ def test_long_config_backward_sampled_slices():
     b, h, s, d = 8, 32, 8192, 128
     q, k, v, do = _inputs((b, h, s, d), seed=0)
     per_slice = s * s * 2
-    chunk = fa.DS_WORKSPACE_BUDGET // per_slice  # slices per dS chunk
+    chunk = DS_WORKSPACE_BUDGET // per_slice  # slices per dS chunk
     assert 0 < chunk < b * h, "the test must cross at least one chunk boundary"
     qg, kg, vg = (t.clone().requires_grad_(True) for t in (q, k, v))
-    out = fa.flash_attention(qg, kg, vg, causal=True)
+    out = flash_attention(qg, kg, vg, causal=True)
     out.backward(do)
     torch.cuda.synchronize()
     flat = sorted({0, chunk - 1, chunk, 2 * chunk + 5, b * h - 1})
@@ -66,14 +66,14 @@ def test_gpt_shape_backward_sampled_slices(packed):
     q, k, v, do = _inputs((b, h, s, d), seed=3)
     if packed:
         qkv = torch.stack([t.transpose(1, 2) for t in (q, k, v)], dim=2).contiguous().requires_grad_(True)  # [b, s, 3, h, d]
-        out = fa.flash_attention_packed(qkv, causal=True)  # [b, s, h, d]
+        out = flash_attention_packed(qkv, causal=True)  # [b, s, h, d]
         out.backward(do.transpose(1, 2))
         torch.cuda.synchronize()
         out = out.detach().transpose(1, 2)
         grads = tuple(qkv.grad[:, :, i].transpose(1, 2) for i in range(3))
     else:
         qg, kg, vg = (t.clone().requires_grad_(True) for t in (q, k, v))
-        out = fa.flash_attention(qg, kg, vg, causal=True)
+        out = flash_attention(qg, kg, vg, causal=True)
         out.backward(do)
         torch.cuda.synchronize()
         out, grads = out.detach(), (qg.grad, kg.grad, vg.grad)
