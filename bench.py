@@ -253,13 +253,12 @@ class NormWorkload:
                 "dh": torch.empty(R, D, dtype=torch.bfloat16, device=dev),
             })
         self.w = (1.0 + 0.1 * torch.randn(D, generator=g, device=dev)).float()
-        # dw of step i lands in dw_bufs[i % 2]; at N > 1 its all-reduce runs on NCCL's
-        # stream while the next step's kernels run (the next write of that buffer, two
-        # steps later, waits for it), like a gradient bucket reduced during backward.
-        self.dw_bufs = [torch.empty(D, dtype=torch.float32, device=dev) for _ in range(2)]
-        self.dw = self.dw_bufs[0]
-        self.pending = [None, None]
-        self.dw_group = self._dw_group() if ws > 1 else None
+        # the sharded backward's one exchange (ferrite.sharding.DwExchange): dw of step i
+        # is summed over ranks on NCCL's stream (one-CTA communicator) while the next
+        # step's kernels run; its buffer is rewritten two steps later, after a wait
+        from ferrite.sharding import DwExchange, one_cta_nccl_group
+
+        self.exchange = DwExchange(D, dev, group=one_cta_nccl_group() if ws > 1 else None)
         self.ws_buf = torch.empty(int(self.lib.ferrite_rmsnorm_bwd_workspace_size(R, D)), dtype=torch.uint8, device=dev)
         for s in self.sets:
             self._fwd(s)
@@ -268,22 +267,6 @@ class NormWorkload:
     @property
     def units_per_step(self):
         return self.FWD_BYTES + self.BWD_BYTES
-
-    @staticmethod
-    def _dw_group():
-        """A communicator for the 16 KB dw all-reduce limited to one CTA: it overlaps
-        the next step's kernels, and a wide NCCL kernel spinning on its peers would hold
-        SMs that the persistent backward's CTAs are waiting for.  Measured at 4 GPUs with
-        NCCL limited to one channel: 3.6x one GPU, against 2.9x with NCCL's default."""
-        import torch.distributed as dist
-
-        try:
-            opts = dist.ProcessGroupNCCL.Options()
-            opts.config.min_ctas = 1
-            opts.config.max_ctas = 1
-            return dist.new_group(backend="nccl", pg_options=opts)
-        except (AttributeError, RuntimeError, TypeError):
-            return None  # the default group
 
     def _fwd(self, s):
         nat = self.nat
@@ -299,22 +282,15 @@ class NormWorkload:
 
     def step(self, i, ev=None):
         a, b = self.sets[i % 2], self.sets[(i + 1) % 2]
-        slot = i % 2
         if ev:
             ev[0].record()
         self._fwd(a)
         if ev:
             ev[1].record()
-        if self.pending[slot] is not None:
-            self.pending[slot].wait()  # the stream waits for the all-reduce of step i - 2
-            self.pending[slot] = None
-        self._bwd(b, self.dw_bufs[slot])
+        self._bwd(b, self.exchange.buffer(i))  # the stream first waits for step i - 2's all-reduce
         if ev:
             ev[2].record()
-        if self.ws > 1:
-            import torch.distributed as dist
-
-            self.pending[slot] = dist.all_reduce(self.dw_bufs[slot], group=self.dw_group, async_op=True)
+        self.exchange.start(i)
 
     def breakdown(self, evs):
         fwd = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
@@ -410,12 +386,12 @@ class AttnWorkload:
     scaling = "strong"
     bound = "tensor"
     B, H, S, D = 8, 32, 8192, 128
-    kernels = ("attn_fwd", "attn_bwd_prep", "attn_bwd_dkv", "attn_bwd_dq")
-    launches_per_step = 4
-    n_events = 5
+    kernels = ("attn_fwd", "attn_bwd_prep", "attn_bwd")
+    launches_per_step = 3
+    n_events = 4
 
     def __init__(self, dev, ws, rank, shape=None):
-        from ferrite.kernels.flash_attention import attention_flops
+        from ferrite.kernels.flash_attention import DS_WORKSPACE_BUDGET, attention_flops
 
         if shape:  # smaller cases for profiling captures: "b,h,s,d"
             self.B, self.H, self.S, self.D = shape
@@ -423,25 +399,29 @@ class AttnWorkload:
         bh = self.B * self.H
         if bh % ws:
             raise ValueError("batch*heads must divide over ranks")
-        self.bh_local = bh // ws
+        from ferrite.sharding import attention_slices
+
+        b0, b1 = attention_slices(self.B, self.H, ws, rank)  # this rank's (batch, head) slices
+        self.bh_local = b1 - b0
         g = torch.Generator(device=dev)
         g.manual_seed(rank)
         shape = (1, self.bh_local, self.S, self.D)  # this rank's (b, h) slices as one batch row
         self.q, self.k, self.v, self.do = (torch.randn(*shape, generator=g, device=dev).to(torch.bfloat16) for _ in range(4))
         self.fwd_flops_local = attention_flops(1, self.bh_local, self.S, self.S, self.D, causal=True)
         # tensor-core work each kernel issues, in units of one causal S*S*D/2 product:
-        # fwd 2 (S, PV), dK/dV 4 (S, dP, dV, dK, and it stores dS), dQ from dS 1
+        # fwd 2 (S, PV); the fused backward 5 (dK/dV units: S, dP, dV, dK; dQ units: dS K)
         unit = self.fwd_flops_local / 2
-        self.kernel_work = {"attn_fwd": 2 * unit, "attn_bwd_prep": 0, "attn_bwd_dkv": 4 * unit, "attn_bwd_dq": 1 * unit}
+        self.kernel_work = {"attn_fwd": 2 * unit, "attn_bwd_prep": 0, "attn_bwd": 5 * unit}
         self.o = torch.empty_like(self.q)
         self.lse = torch.empty(1, self.bh_local, self.S, device=dev)
         self.delta = torch.empty_like(self.lse)
         self.dq, self.dk, self.dv = (torch.empty_like(self.q) for _ in range(3))
         from ferrite import _native as nat
 
-        # dS^T scratch of all local slices (bf16 [slice][S][S]), filled by the dK/dV kernel
-        ws = nat.lib().ferrite_attn_bwd_ds_workspace_size(1, self.bh_local, self.S, self.S, self.D, nat.BF16)
-        self.ds = torch.empty(ws, dtype=torch.uint8, device=dev)
+        # dS scratch + scheduler state, sized like the Python API's (flash_attention.DS_WORKSPACE_BUDGET)
+        full = nat.lib().ferrite_attn_bwd_ds_workspace_size(1, self.bh_local, self.S, self.S, self.D, nat.BF16)
+        per = full // self.bh_local
+        self.ds = torch.empty(max(per, min(full, DS_WORKSPACE_BUDGET // per * per)), dtype=torch.uint8, device=dev)
         self.strides = nat.attn_strides(q=self.q, k=self.k, v=self.v, o=self.o, dout=self.do, dq=self.dq, dk=self.dk, dv=self.dv)
 
     @property
@@ -464,13 +444,11 @@ class AttnWorkload:
         if ev:
             ev[2].record()
         st = ctypes.byref(self.strides)
-        nat.check(lib.ferrite_attn_bwd_dkv_ds(s, self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(), self.do.data_ptr(), self.lse.data_ptr(), self.delta.data_ptr(),
-                                              self.dk.data_ptr(), self.dv.data_ptr(), self.ds.data_ptr(), st, 0, bh, 1, bh, S, S, D, sc, 1, 128, 128, nat.BF16))
+        nat.check(lib.ferrite_attn_bwd_ds(s, self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(), self.do.data_ptr(), self.lse.data_ptr(),
+                                          self.delta.data_ptr(), self.dq.data_ptr(), self.dk.data_ptr(), self.dv.data_ptr(), st, self.ds.data_ptr(),
+                                          self.ds.numel(), 1, bh, S, S, D, sc, 1, 128, 128, nat.BF16))
         if ev:
             ev[3].record()
-        nat.check(lib.ferrite_attn_bwd_dq_ds(s, self.ds.data_ptr(), self.k.data_ptr(), self.dq.data_ptr(), st, 0, bh, 1, bh, S, S, D, sc, 1, 128, 128, nat.BF16))
-        if ev:
-            ev[4].record()
 
     def breakdown(self, evs):
         return {k: statistics.mean(e[j].elapsed_time(e[j + 1]) for e in evs) for j, k in enumerate(self.kernels)}
@@ -1087,6 +1065,8 @@ def run_ours(args, ws, rank, local):
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         cb = W.cpu_baseline()
         out["cpu_baseline"] = {k: (round(v, 4) if isinstance(v, float) else v) for k, v in cb.items()}
+    if getattr(wl, "exchange", None) is not None:
+        wl.exchange.finish()
     if ws > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -1929,6 +1929,662 @@ __global__ void __launch_bounds__(kDqThreads, 1)
 }
 
 // ===========================================================================
+// Fused backward: dK/dV units and dQ-from-dS units in one persistent kernel
+// ===========================================================================
+//
+// The dK/dV work (one unit per (slice, 128-key tile), flash_attention.py:197-221)
+// and the dQ work (one unit per (slice, 128-query tile): dQ = scale * dS K, the
+// one tensor-core product that replaces the reference's second recompute,
+// :224-243) run as units of ONE persistent launch, so every dS tile is read back
+// while it is still in L2 and then dropped from L2 unwritten (discard.global.L2):
+// the dS round trip through HBM of the two-kernel path -- a write and a read of
+// 2 bytes per causal score, 34 GB per step at b8 h32 s8192 -- disappears, and with
+// it most of the energy that held the power-capped clock down.
+//
+// * A dK/dV unit walks its query tiles from the LAST to the first, so all units
+//   of a slice, which start close together, finish query tile i at about the
+//   same time, high tiles first.  Its eight elementwise warps hand each dS^T
+//   tile to a store warp (warp 10) through the shared staging tile; the store
+//   warp issues the TMA stores and, once they have completed (bulk wait_group,
+//   proxy fence), adds one to the query tile's counter (acquire-release).  The
+//   add that completes the count publishes the dQ unit of that tile in a ready
+//   queue.  The waits for store completion and the gpu-scope atomics stay off
+//   the elementwise and MMA warps' path.
+// * A dQ unit is handed out only once published, so a CTA never waits inside a
+//   unit for another CTA.  It streams the tile's dS^T blocks and the slice's K
+//   tiles through a ring (same MMA as attn_dq_ds_kernel), writes dQ, discards
+//   the dS lines it read and counts the slice's finished dQ units.
+// * Scheduling (thread 0, state in the workspace, zeroed per launch): a CTA takes
+//   a published dQ unit if there is one, else the next dK/dV unit in slice-major,
+//   heaviest-first order.  dS lives in `slots` slice-sized slots; slice s may
+//   start once every dQ unit of slice s - slots has finished (its slot is free).
+//   Every wait across CTAs happens in this claim loop, on work that was claimed
+//   earlier and is running, so there is no cycle; the loop is bounded by
+//   kWaitLimitNs and a global abort word stops every CTA after a timeout.
+// Numerics are those of the two-kernel path (same dS values, same products, same
+// summation order); no atomics touch any result.
+
+constexpr int kFusedMaxDqStages = 6;
+// warps 0 TMA loads, 1 TMEM + MMA, 2-9 elementwise / dQ epilogue, 10 dS stores + signals
+constexpr int kFusedThreads = 352;
+enum { kSchedNext = 0, kSchedHead = 1, kSchedTail = 2, kSchedAbort = 3, kSchedInts = 8 };
+
+struct FusedParams {
+  int nq, nkt;       // query tiles / key tiles (128 rows each) per slice
+  int n_slices;      // slices bh0 .. bh0 + n_slices - 1
+  int slots;         // dS slots (slice-sized)
+  int* sched;        // kSchedInts ints
+  int* ready;        // [n_slices * nq] published dQ unit ids (-1 = not yet written)
+  int* row_cnt;      // [n_slices * nq] dS producer-warp signals per query tile
+  int* dq_done;      // [n_slices] finished dQ units per slice
+  uint8_t* ds;       // slot 0 of the dS blocks
+  int64_t ds_slot_bytes;
+  void* dq;
+  Bhsd ldq;
+};
+
+template <int D>
+struct FusedSmem {
+  using W = WideSmem<D>;
+  static constexpr int kDataBytes = W::kDataBytes;
+  static constexpr int kDqABytes = 128 * 64 * 2;  // dS^T: 2 boxes of 64 queries x 64 keys
+  static constexpr int kDqBBytes = 64 * D * 2;    // K: D/64 boxes of 64 d x 64 keys
+  static constexpr int kDqStageBytes = kDqABytes + kDqBBytes;
+  static constexpr int kDqStages =
+      kDataBytes / kDqStageBytes < kFusedMaxDqStages ? kDataBytes / kDqStageBytes : kFusedMaxDqStages;
+  static_assert(kDqStages >= 2, "dQ ring needs two stages");
+  static constexpr int kNumDkvBars = W::kNumBars + 2;  // + stg_full, stg_free
+  static constexpr int kNumDqBars = 2 * kDqStages + 1;
+  // barriers, then TMEM slot, local abort, unit, kind, set-initialised flags
+  static constexpr int kBarBytes = (kNumDkvBars + kNumDqBars) * 8 + 32;
+  static_assert(kBarBytes <= 512, "barrier block must fit the alignment slack rule");
+  // Data at the first 1024-byte boundary; the barrier block in the slack before it
+  // when that holds 512 bytes, else right after the data (slack < 512 then).
+  static constexpr int kTotal = kDataBytes + 1024;
+};
+
+__device__ __forceinline__ int fused_producers(const FusedParams& fp, int causal, int qt) {
+  return causal ? min(qt + 1, fp.nkt) : fp.nkt;  // one signal per key tile
+}
+
+// Claim the next unit (thread 0 only).  Returns the unit id and sets kind (0 dK/dV,
+// 1 dQ), or -1 when every unit has been handed out or the launch aborted.
+// dQ units first: a CTA takes the oldest published one (compare-and-swap on the
+// queue head, retried with the value it returns).  Otherwise it draws a dK/dV
+// ticket with fetch-and-add (no retries however many CTAs draw at once) and keeps
+// it in `pending` until the ticket's dS slot is free, serving dQ units
+// meanwhile.  A ticket of slice s waits only for the dQ units of slice
+// s - slots, which depend only on dK/dV tickets drawn before it, so the oldest
+// waiting ticket can always start: no cycle.
+__device__ int fused_claim(const FusedParams& fp, int& kind, int& pending) {
+  int* s = fp.sched;
+  const int n_dkv = fp.n_slices * fp.nkt;
+  const int n_dq = fp.n_slices * fp.nq;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if ((spins & 15u) == 0 && ld_relaxed_gpu(&s[kSchedAbort])) return -1;
+    int h = ld_relaxed_gpu(&s[kSchedHead]);
+    const int t = ld_relaxed_gpu(&s[kSchedTail]);
+    while (h < t) {
+      const int old = atom_cas_gpu(&s[kSchedHead], h, h + 1);
+      if (old == h) {
+        int v;
+        while ((v = ld_acquire_gpu(&fp.ready[h])) < 0) {  // the publisher is between its two writes
+          if ((++spins & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+            report_timeout(61);
+            st_relaxed_gpu(&s[kSchedAbort], 1);
+            return -1;
+          }
+        }
+        kind = 1;
+        return v;
+      }
+      h = old;
+    }
+    if (h >= n_dq) return -1;  // every dQ unit handed out: every dK/dV unit ran
+    if (pending < 0) pending = atomicAdd(&s[kSchedNext], 1);
+    if (pending < n_dkv) {
+      const int sl = pending / fp.nkt;
+      if (sl < fp.slots || ld_acquire_gpu(&fp.dq_done[sl - fp.slots]) >= fp.nq) {
+        const int u = pending;
+        pending = -1;
+        kind = 0;
+        return u;
+      }
+    }
+    __nanosleep(200);
+    if ((++spins & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+      report_timeout(60);
+      st_relaxed_gpu(&s[kSchedAbort], 1);
+      return -1;
+    }
+  }
+}
+
+// Signal that the dS^T tile of one key tile for query tile `qt` of slice `sl` is in
+// global memory (the store warp, after the TMA stores of that tile completed).
+__device__ __forceinline__ void fused_signal(const FusedParams& fp, int causal, int sl, int qt) {
+  fence_proxy_async_global();
+  const int id = sl * fp.nq + qt;
+  const int old = atom_add_acq_rel_gpu(&fp.row_cnt[id], 1);
+  if (old + 1 == fused_producers(fp, causal, qt)) {
+    const int slot = atomicAdd(&fp.sched[kSchedTail], 1);
+    st_release_gpu(&fp.ready[slot], id);
+  }
+}
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kFusedThreads, 1)
+    attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+                          const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdo,
+                          const __grid_constant__ CUtensorMap tlse, const __grid_constant__ CUtensorMap tdelta,
+                          const __grid_constant__ CUtensorMap tds_st, const __grid_constant__ CUtensorMap tds_ld,
+                          const __grid_constant__ CUtensorMap tk64, const BwdParams p, const FusedParams fp) {
+  using W = WideSmem<D>;
+  using L = FusedSmem<D>;
+  constexpr int S = W::kStages;
+  constexpr int QS = L::kDqStages;
+  typedef typename std::conditional<BF16, __nv_bfloat16, __half>::type T;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem - smem_raw >= 512 ? smem_raw : smem + L::kDataBytes);
+  // dK/dV unit barriers (as in attn_dkv_wide_kernel)
+  uint64_t* x_full = bars + 0;
+  uint64_t* y_full = bars + 1;
+  uint64_t* y_empty = bars + 1 + S;
+  uint64_t* s_full = bars + 1 + 2 * S;
+  uint64_t* dp_full = s_full + 1;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* dp_free = s_full + 3;
+  uint64_t* ds_full = s_full + 4;
+  uint64_t* acc_full = s_full + 5;
+  uint64_t* p_half = s_full + 6;
+  uint64_t* stg_full = s_full + 7;  // the eight elementwise warps wrote the dS^T staging tile
+  uint64_t* stg_free = s_full + 8;  // the store warp's TMA stores have read it
+  // dQ unit barriers
+  uint64_t* q_full = bars + L::kNumDkvBars;
+  uint64_t* q_empty = q_full + QS;
+  uint64_t* q_acc = q_full + 2 * QS;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kNumDkvBars + L::kNumDqBars);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* s_unit = abort + 1;
+  volatile int* s_kind = abort + 2;
+  volatile int* s_inited = abort + 3;  // bit 0: dK/dV set, bit 1: dQ set
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int diag_shift = p.sk - p.sq;
+  const int nkb_all = p.sk / 64;
+
+  if (threadIdx.x == 0) {
+    *abort = 0;
+    *s_inited = 0;
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_launch_dependents();
+  pdl_wait();
+  const uint32_t t_dv = tmem + 256;
+  const uint32_t t_dk = tmem + 256 + D;
+
+  int pending = -1;  // thread 0: a dK/dV ticket whose dS slot is not free yet
+  while (true) {
+    // ---------------------------------------------------------------- claim
+    if (threadIdx.x == 0) {
+      int kind = 0;
+      const int u = *abort ? -1 : fused_claim(fp, kind, pending);
+      *s_unit = u;
+      *s_kind = kind;
+      if (u >= 0) {
+        fence_proxy_async_global();  // TMA traffic of this unit after the acquire of its inputs / slot
+        const int bit = kind ? 2 : 1;
+        if (kind == 0) {
+          if (*s_inited & 1) {
+            for (int i = 0; i < L::kNumDkvBars; ++i) mbar_inval(&bars[i]);
+          }
+          mbar_init(x_full, 1);
+          for (int i = 0; i < S; ++i) {
+            mbar_init(&y_full[i], 1);
+            mbar_init(&y_empty[i], 1);
+          }
+          mbar_init(s_full, 1);
+          mbar_init(dp_full, 1);
+          mbar_init(p_full, 8);
+          mbar_init(p_half, 8);
+          mbar_init(dp_free, 8);
+          mbar_init(ds_full, 8);
+          mbar_init(acc_full, 1);
+          mbar_init(stg_full, 8);
+          mbar_init(stg_free, 1);
+        } else {
+          if (*s_inited & 2) {
+            for (int i = 0; i < L::kNumDqBars; ++i) mbar_inval(&q_full[i]);
+          }
+          for (int i = 0; i < QS; ++i) {
+            mbar_init(&q_full[i], 1);
+            mbar_init(&q_empty[i], 1);
+          }
+          mbar_init(q_acc, 1);
+        }
+        *s_inited = *s_inited | bit;
+        fence_mbar_init();
+      }
+    }
+    __syncthreads();
+    const int unit = *s_unit;
+    if (unit < 0) break;
+
+    if (*s_kind == 0) {
+      // ============================================================ dK/dV unit
+      const int sl = unit / fp.nkt;
+      const int ktile = unit - sl * fp.nkt;
+      const int slot = sl % fp.slots;
+      const int bh = p.bh0 + sl;
+      const int hh = bh % p.l0.nh, bb = bh / p.l0.nh;
+      const int x0 = ktile * BX;
+      int j0 = 0;
+      const int j1 = (p.sq + kWideY - 1) / kWideY;
+      if (p.causal) j0 = max(0, x0 - diag_shift) / kWideY;
+      const int n_y = max(0, j1 - j0);
+      // query tile of the i-th step: last tile first
+      auto ytile = [&](int i) { return j1 - 1 - i; };
+      auto load_y = [&](int i) {
+        const int s = i % S;
+        uint8_t* y1 = smem + W::kYOff + s * W::kStageBytes;
+        uint8_t* y2 = y1 + W::kYBytes;
+        mbar_arrive_expect_tx(&y_full[s], 2 * W::kYBytes + 2 * kWideY * 4);
+        const int yrow = ytile(i) * kWideY;
+#pragma unroll
+        for (int c = 0; c < W::kChunks; ++c) {
+          tma_load_4d(y1 + c * (kWideY * 128), &tq, &y_full[s], c * 64, yrow, hh, bb);
+          tma_load_4d(y2 + c * (kWideY * 128), &tdo, &y_full[s], c * 64, yrow, hh, bb);
+        }
+        float* st = reinterpret_cast<float*>(y2 + W::kYBytes);
+        tma_load_2d(st, &tlse, &y_full[s], yrow, bh);
+        tma_load_2d(st + kWideY, &tdelta, &y_full[s], yrow, bh);
+      };
+      const int n_pre = min(n_y, S);
+      if (threadIdx.x == 0 && n_y > 0) {
+        mbar_arrive_expect_tx(x_full, 2 * W::kXBytes);
+#pragma unroll
+        for (int c = 0; c < W::kChunks; ++c) {
+          tma_load_4d(smem + W::kX1Off + c * (BX * 128), &tk, x_full, c * 64, x0, hh, bb);
+          tma_load_4d(smem + W::kX2Off + c * (BX * 128), &tv, x_full, c * 64, x0, hh, bb);
+        }
+        for (int i = 0; i < n_pre; ++i) load_y(i);
+      }
+      if (warp == 0) {
+        if (lane == 0 && n_y > 0) {
+          for (int i = n_pre; i < n_y; ++i) {
+            if (!mbar_wait(&y_empty[i % S], ((i / S) & 1) ^ 1, abort, 41)) break;
+            load_y(i);
+          }
+        }
+      } else if (warp == 1) {
+        if (lane == 0 && n_y > 0) {
+          constexpr uint32_t idesc_t = make_idesc_f16(BX, kWideY, BF16, false, false);
+          constexpr uint32_t idesc_a = make_idesc_f16(BX, D, BF16, false, true);
+          const uint64_t dx1 = make_sdesc(smem_u32(smem + W::kX1Off), 16, 1024);
+          const uint64_t dx2 = make_sdesc(smem_u32(smem + W::kX2Off), 16, 1024);
+          const uint64_t dy_k = make_sdesc(smem_u32(smem + W::kYOff), 16, 1024);
+          const uint64_t dy_mn = make_sdesc(smem_u32(smem + W::kYOff), kWideY * 128, 1024);
+          bool ok = mbar_wait(x_full, 0, abort, 42);
+          auto region = [&](int i, bool is_s) -> uint32_t { return (((i & 1) ^ (is_s ? 0 : 1)) ? 128u : 0u); };
+          auto issue_prod = [&](int i, bool is_s) {
+            const uint64_t dy = sdesc_at(dy_k, (i % S) * W::kStageBytes + (is_s ? 0 : W::kYBytes));
+            const uint64_t dx = is_s ? dx1 : dx2;
+            const uint32_t dst = tmem + region(i, is_s);
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint32_t xo = (kk >> 2) * (BX * 128) + (kk & 3) * 32;
+              const uint32_t yo = (kk >> 2) * (kWideY * 128) + (kk & 3) * 32;
+              tc_mma_f16_ss(dst, sdesc_at(dx, xo), sdesc_at(dy, yo), idesc_t, kk != 0);
+            }
+            tc_commit(is_s ? s_full : dp_full);
+          };
+          auto issue_dv = [&](int i, int part) {
+            const uint64_t dm2 = sdesc_at(dy_mn, (i % S) * W::kStageBytes + W::kYBytes);
+            const uint32_t pa = tmem + region(i, true);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int kk = (q >> 1) * 4 + part * 2 + (q & 1);
+              tc_mma_f16_ts(t_dv, pa + (kk >> 2) * 64 + (kk & 3) * 8, sdesc_at(dm2, kk * 2048), idesc_a,
+                            (i > 0 || kk > 0) ? 1u : 0u);
+            }
+          };
+          auto issue_dk = [&](int i) {
+            const uint64_t dm1 = sdesc_at(dy_mn, (i % S) * W::kStageBytes);
+            const uint32_t da = tmem + region(i, true) + 32;
+#pragma unroll
+            for (int kk = 0; kk < kWideY / 16; ++kk)
+              tc_mma_f16_ts(t_dk, da + (kk >> 2) * 64 + (kk & 3) * 8, sdesc_at(dm1, kk * 2048), idesc_a,
+                            (i > 0 || kk > 0) ? 1u : 0u);
+            tc_commit(&y_empty[i % S]);
+          };
+          if (ok && (ok = mbar_wait(&y_full[0], 0, abort, 43))) {
+            tc_fence_after();
+            issue_prod(0, true);
+            issue_prod(0, false);
+          }
+          for (int i = 0; ok && i < n_y; ++i) {
+            const bool more = i + 1 < n_y;
+            if (!(ok = mbar_wait(p_half, i & 1, abort, 52))) break;
+            tc_fence_after();
+            issue_dv(i, 0);
+            if (!(ok = mbar_wait(p_full, i & 1, abort, 45))) break;
+            if (more) {
+              if (!(ok = mbar_wait(dp_free, i & 1, abort, 44))) break;
+              if (!(ok = mbar_wait(&y_full[(i + 1) % S], ((i + 1) / S) & 1, abort, 43))) break;
+            }
+            tc_fence_after();
+            if (more) issue_prod(i + 1, true);
+            issue_dv(i, 1);
+            if (!(ok = mbar_wait(ds_full, i & 1, abort, 46))) break;
+            tc_fence_after();
+            issue_dk(i);
+            if (more) issue_prod(i + 1, false);
+          }
+          tc_commit(acc_full);
+          mbar_drain(acc_full, 0);
+        }
+      } else if (warp == 10) {
+        // ------------------------------------------------ dS^T stores + signals
+        // One TMA store per 32-key x 64-query staging block; the stg_free arrival
+        // lets the elementwise warps write the next tile while the stores drain to
+        // L2; a tile's query tile is signalled once its stores have completed (one
+        // tile later, so the wait is off every other warp's path).
+        if (lane == 0) {
+          bool ok = true;
+          int prev_qt = -1;
+          const uint64_t keep = l2_policy_evict_last();  // read back soon by a dQ unit
+          for (int i = 0; i < n_y; ++i) {
+            if (!mbar_wait(stg_full, i & 1, abort, 54)) {
+              ok = false;
+              break;
+            }
+            const int y0 = ytile(i) * kWideY;
+#pragma unroll
+            for (int hq = 0; hq < 8; ++hq) {
+              const int hb = hq >> 2, qw = hq & 3;
+              const int key = x0 + qw * 32;
+              tma_store_4d_hint(&tds_st, smem + W::kStgOff + hb * (BX * 128) + qw * 4096, 0, key & 63,
+                                (y0 >> 6) + hb, slot * nkb_all + (key >> 6), keep);
+            }
+            bulk_commit_group();
+            bulk_wait_group_read0();
+            mbar_arrive(stg_free);
+            if (prev_qt >= 0) {
+              bulk_wait_group1();
+              fused_signal(fp, p.causal, sl, prev_qt);
+            }
+            prev_qt = y0 / kWideY;
+          }
+          bulk_wait_group0();
+          if (ok && prev_qt >= 0) fused_signal(fp, p.causal, sl, prev_qt);
+        }
+      } else {
+        // ------------------------------------------------ elementwise warps
+        const int qw = warp & 3;
+        const int h = (warp - 2) >> 2;
+        const int r = qw * 32 + lane;
+        const int xrow = x0 + r;
+        const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
+        const uint32_t t_col = tmem + lane_off + h * 64;
+        uint8_t* stg = smem + W::kStgOff + h * (BX * 128) + qw * 4096;
+        bool ok = true;
+        for (int i = 0; ok && i < n_y; ++i) {
+          const int ph = i & 1;
+          const int y0 = ytile(i) * kWideY;
+          const int s = i % S;
+          const uint32_t t_s = t_col + ((i & 1) ? 128u : 0u);
+          const uint32_t t_dp = t_col + ((i & 1) ? 0u : 128u);
+          const bool need_mask = (y0 + kWideY > p.sq) || (p.causal && x0 + BX - 1 > y0 + diag_shift);
+          if (!mbar_wait(s_full, ph, abort, 47) || !mbar_wait(&y_full[s], (i / S) & 1, abort, 48)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const float* st = reinterpret_cast<const float*>(smem + W::kYOff + s * W::kStageBytes + 2 * W::kYBytes) + h * 64;
+          uint32_t pf[64];
+          tmem_ld32(t_s, *reinterpret_cast<uint32_t(*)[32]>(&pf[0]));
+          tmem_ld32(t_s + 32, *reinterpret_cast<uint32_t(*)[32]>(&pf[32]));
+          tmem_wait_ld();
+          {
+            const uint64_t sc2 = f2_make(p.scale_log2, p.scale_log2);
+            const uint64_t nlog2e2 = f2_make(-kLog2e, -kLog2e);
+            auto body_a = [&](auto masked, auto c0) {
+#pragma unroll
+              for (int c = decltype(c0)::value; c < decltype(c0)::value + 32; c += 4) {
+                const float4 l4 = *reinterpret_cast<const float4*>(st + c);
+                const uint64_t x01 = f2_fma(f2_make_bits(pf[c], pf[c + 1]), sc2, f2_mul(f2_make(l4.x, l4.y), nlog2e2));
+                const uint64_t x23 = f2_fma(f2_make_bits(pf[c + 2], pf[c + 3]), sc2, f2_mul(f2_make(l4.z, l4.w), nlog2e2));
+                float x[4] = {f2_lo(x01), f2_hi(x01), f2_lo(x23), f2_hi(x23)};
+                if constexpr (decltype(masked)::value) {
+#pragma unroll
+                  for (int u = 0; u < 4; ++u) {
+                    const int qry = y0 + h * 64 + c + u;
+                    const bool valid = qry < p.sq && !(p.causal && xrow > qry + diag_shift);
+                    x[u] = valid ? x[u] : -INFINITY;
+                  }
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) pf[c + u] = __float_as_uint(ex2_approx(x[u]));
+              }
+            };
+            auto half_a = [&](auto c0, uint64_t* bar) {
+              if (need_mask)
+                body_a(std::true_type{}, c0);
+              else
+                body_a(std::false_type{}, c0);
+              uint32_t pp[16];
+#pragma unroll
+              for (int c = 0; c < 32; c += 2) {
+                const float a0 = __uint_as_float(pf[decltype(c0)::value + c]);
+                const float a1 = __uint_as_float(pf[decltype(c0)::value + c + 1]);
+                pp[c / 2] = BF16 ? pack_bf16x2(a0, a1) : pack_f16x2(a0, a1);
+              }
+              tmem_st16(t_s + decltype(c0)::value / 2, pp);
+              tmem_wait_st();
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(bar);
+            };
+            half_a(std::integral_constant<int, 0>{}, p_half);
+            half_a(std::integral_constant<int, 32>{}, p_full);
+          }
+          if (!mbar_wait(dp_full, ph, abort, 49)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint32_t b[64];
+          tmem_ld32(t_dp, *reinterpret_cast<uint32_t(*)[32]>(&b[0]));
+          tmem_ld32(t_dp + 32, *reinterpret_cast<uint32_t(*)[32]>(&b[32]));
+          tmem_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(dp_free);
+          // the store warp's TMA stores of the previous tile have read the staging tile
+          if (i > 0 && !mbar_wait(stg_free, (i - 1) & 1, abort, 53)) {
+            ok = false;
+            break;
+          }
+          uint8_t* row = stg + lane * 128;
+#pragma unroll
+          for (int hb = 0; hb < 2; ++hb) {
+            uint32_t dd[16];
+#pragma unroll
+            for (int e = 0; e < 32; e += 4) {
+              const int c = hb * 32 + e;
+              const float4 d4 = *reinterpret_cast<const float4*>(st + kWideY + c);
+              const uint64_t d01 = f2_mul(f2_make_bits(pf[c], pf[c + 1]),
+                                          f2_sub(f2_make_bits(b[c], b[c + 1]), f2_make(d4.x, d4.y)));
+              const uint64_t d23 = f2_mul(f2_make_bits(pf[c + 2], pf[c + 3]),
+                                          f2_sub(f2_make_bits(b[c + 2], b[c + 3]), f2_make(d4.z, d4.w)));
+              dd[e / 2] = BF16 ? pack_bf16x2(f2_lo(d01), f2_hi(d01)) : pack_f16x2(f2_lo(d01), f2_hi(d01));
+              dd[e / 2 + 1] = BF16 ? pack_bf16x2(f2_lo(d23), f2_hi(d23)) : pack_f16x2(f2_lo(d23), f2_hi(d23));
+            }
+            tmem_st16(t_s + 32 + hb * 16, dd);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              const int g16 = hb * 4 + v;
+              *reinterpret_cast<uint4*>(row + ((g16 ^ (lane & 7)) << 4)) =
+                  make_uint4(dd[4 * v], dd[4 * v + 1], dd[4 * v + 2], dd[4 * v + 3]);
+            }
+          }
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(ds_full);
+          fence_proxy_async_smem();  // the staging writes, before the store warp's TMA reads them
+          __syncwarp();
+          if (lane == 0) mbar_arrive(stg_full);
+        }
+        if (n_y > 0 && ok && mbar_wait(acc_full, 0, abort, 51)) {
+          tc_fence_after();
+          const bool row_ok = xrow < p.sk;
+          T* out = reinterpret_cast<T*>(h == 0 ? p.out0 : p.out1) + (h == 0 ? p.l0 : p.l1).row(bh, xrow);
+          const uint32_t src = (h == 0 ? t_dk : t_dv) + lane_off;
+          const float mul = h == 0 ? p.scale : 1.0f;
+#pragma unroll
+          for (int c0 = 0; c0 < D; c0 += 32) {
+            uint32_t v[32];
+            tmem_ld32(src + c0, v);
+            tmem_wait_ld();
+            if (row_ok) {
+#pragma unroll
+              for (int e = 0; e < 32; e += 8) {
+                uint4 w;
+                const float* f = reinterpret_cast<const float*>(&v[e]);
+                w.x = BF16 ? pack_bf16x2(f[0] * mul, f[1] * mul) : pack_f16x2(f[0] * mul, f[1] * mul);
+                w.y = BF16 ? pack_bf16x2(f[2] * mul, f[3] * mul) : pack_f16x2(f[2] * mul, f[3] * mul);
+                w.z = BF16 ? pack_bf16x2(f[4] * mul, f[5] * mul) : pack_f16x2(f[4] * mul, f[5] * mul);
+                w.w = BF16 ? pack_bf16x2(f[6] * mul, f[7] * mul) : pack_f16x2(f[6] * mul, f[7] * mul);
+                *reinterpret_cast<uint4*>(out + c0 + e) = w;
+              }
+            }
+          }
+        } else if (n_y == 0 && xrow < p.sk) {
+          T* out = reinterpret_cast<T*>(h == 0 ? p.out0 : p.out1) + (h == 0 ? p.l0 : p.l1).row(bh, xrow);
+          for (int c = 0; c < D; ++c) out[c] = DT<T>::from_f(0.f);
+        }
+      }
+    } else {
+      // ============================================================ dQ unit
+      const int sl = unit / fp.nq;
+      const int qt = unit - sl * fp.nq;
+      const int slot = sl % fp.slots;
+      const int bh = p.bh0 + sl;
+      const int hh = bh % p.l0.nh, bb = bh / p.l0.nh;
+      int last_key = p.sk - 1;
+      if (p.causal) last_key = min(last_key, qt * 128 + 127 + diag_shift);
+      const int nkb = last_key < 0 ? 0 : last_key / 64 + 1;
+      const int nqb = p.sq / 64;  // query blocks per key block in the dS layout
+      if (warp == 0) {
+        if (lane == 0) {
+          const uint64_t last_use = l2_policy_evict_first();  // dS is read once, then discarded
+          for (int kb = 0; kb < nkb; ++kb) {
+            const int st = kb % QS;
+            if (!mbar_wait(&q_empty[st], ((kb / QS) & 1) ^ 1, abort, 62)) break;
+            uint8_t* sa = smem + st * L::kDqStageBytes;
+            uint8_t* sb = sa + L::kDqABytes;
+            mbar_arrive_expect_tx(&q_full[st], L::kDqStageBytes);
+            tma_load_4d_hint(sa, &tds_ld, &q_full[st], 0, 0, qt * 2, slot * nkb_all + kb, last_use);
+#pragma unroll
+            for (int c = 0; c < D / 64; ++c) tma_load_4d(sb + c * 8192, &tk64, &q_full[st], c * 64, kb * 64, hh, bb);
+          }
+        }
+      } else if (warp == 1) {
+        if (lane == 0) {
+          constexpr uint32_t idesc = make_idesc_f16(128, D, BF16, true, true);
+          const uint32_t s0 = smem_u32(smem);
+          const uint64_t da_base = make_sdesc(s0, 8192, 1024);
+          const uint64_t db_base = make_sdesc(s0 + L::kDqABytes, 8192, 1024);
+          bool ok = true;
+          for (int kb = 0; kb < nkb; ++kb) {
+            const int st = kb % QS;
+            if (!mbar_wait(&q_full[st], (kb / QS) & 1, abort, 63)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint64_t da = sdesc_at(da_base, st * L::kDqStageBytes);
+            const uint64_t db = sdesc_at(db_base, st * L::kDqStageBytes);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              tc_mma_f16_ss(tmem, sdesc_at(da, kk * 2048), sdesc_at(db, kk * 2048), idesc, (kb | kk) != 0 ? 1u : 0u);
+            tc_commit(&q_empty[st]);
+          }
+          (void)ok;
+          tc_commit(q_acc);
+          mbar_drain(q_acc, 0);
+        }
+      } else if (warp < 10) {
+        const int qw = warp & 3;
+        const int h = (warp - 2) >> 2;  // dQ columns [h D/2, (h + 1) D/2)
+        const int r = qw * 32 + lane;
+        if (nkb > 0 && mbar_wait(q_acc, 0, abort, 64)) {
+          tc_fence_after();
+          const int qrow = qt * 128 + r;
+          const uint32_t src = tmem + ((uint32_t)(qw * 32) << 16) + h * (D / 2);
+          T* out = reinterpret_cast<T*>(fp.dq) + fp.ldq.row(bh, qrow) + h * (D / 2);
+#pragma unroll 1
+          for (int c0 = 0; c0 < D / 2; c0 += 32) {
+            uint32_t v[32];
+            tmem_ld32(src + c0, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; e += 8) {
+              const float* f = reinterpret_cast<const float*>(&v[e]);
+              const float m = p.scale;
+              uint4 w;
+              w.x = BF16 ? pack_bf16x2(f[0] * m, f[1] * m) : pack_f16x2(f[0] * m, f[1] * m);
+              w.y = BF16 ? pack_bf16x2(f[2] * m, f[3] * m) : pack_f16x2(f[2] * m, f[3] * m);
+              w.z = BF16 ? pack_bf16x2(f[4] * m, f[5] * m) : pack_f16x2(f[4] * m, f[5] * m);
+              w.w = BF16 ? pack_bf16x2(f[6] * m, f[7] * m) : pack_f16x2(f[6] * m, f[7] * m);
+              *reinterpret_cast<uint4*>(out + c0 + e) = w;
+            }
+          }
+          // every load of this tile's dS has completed (its MMAs have): drop the lines
+          const uint8_t* base = fp.ds + (int64_t)slot * fp.ds_slot_bytes;
+          const int t = threadIdx.x - 64;  // 0 .. 255
+          for (int idx = t; idx < nkb * 128; idx += 256) {
+            const int kb = idx >> 7;
+            discard_l2_line(base + ((int64_t)kb * nqb + qt * 2) * 8192 + (idx & 127) * 128);
+          }
+        }
+      }
+    }
+
+    // ---------------------------------------------------------------- unit end
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (threadIdx.x == 0) {
+      if (*abort) {
+        st_relaxed_gpu(&fp.sched[kSchedAbort], 1);
+      } else if (*s_kind == 1) {
+        __threadfence();  // the discards above are ordered before the slot is handed on
+        red_add_release_gpu(&fp.dq_done[unit / fp.nq], 1);
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ===========================================================================
 // host
 // ===========================================================================
 
@@ -2215,6 +2871,99 @@ static int dispatch_dq_ds(cudaStream_t s, const BwdArgs& a, int64_t b, int64_t h
               : launch_dq_ds<64, false>(s, a, b, h, sq, sk, scale, causal);
   return bf ? launch_dq_ds<128, true>(s, a, b, h, sq, sk, scale, causal)
             : launch_dq_ds<128, false>(s, a, b, h, sq, sk, scale, causal);
+}
+
+// Fused backward workspace: `slots` dS slots (slice-sized, 8 KiB-aligned blocks)
+// followed by the scheduler state (sched ints, ready queue, per-tile producer
+// counts, per-slice finished dQ units), 256-byte aligned.
+static int64_t fused_sched_bytes(int64_t nslices, int64_t sq) {
+  const int64_t ndq = nslices * ((sq + 127) / 128);
+  return ((kSchedInts + 2 * ndq + nslices) * 4 + 255) / 256 * 256;
+}
+
+static bool fused_ok(int64_t sq, int64_t sk, int64_t d, int causal) {
+  if (env_int("FERRITE_ATTN_BWD_FUSED", 0) == 0) return false;
+  if (d != 64 && d != 128) return false;
+  if (sq % 128 != 0 || sk % 128 != 0) return false;
+  return !causal || sq == sk;
+}
+
+template <int D, bool BF16>
+static int launch_bwd_fused(cudaStream_t s, const BwdArgs& kv, const BwdArgs& qa, int64_t b, int64_t h,
+                            int64_t sq, int64_t sk, float scale, int causal, void* workspace,
+                            size_t workspace_bytes) {
+  using L = FusedSmem<D>;
+  const CUtensorMapDataType dt = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const int64_t bh = b * h;
+  const int64_t slot_bytes = ds_slice_bytes(sq, sk);
+  const int64_t sched_bytes = fused_sched_bytes(bh, sq);
+  const int64_t slots = std::min<int64_t>(bh, ((int64_t)workspace_bytes - sched_bytes) / slot_bytes);
+  if (slots < 1) return fail(FERRITE_WORKSPACE_TOO_SMALL, "attn_bwd_fused: workspace below one dS slice + scheduler state");
+  CUtensorMap tk, tv, tq, tdo, tl, td, tds_st, tds_ld, tk64;
+  int rc = map_bhsd(&tk, kv.k, dt, D, kv.lk, b, h, sk, BX);
+  if (!rc) rc = map_bhsd(&tv, kv.v, dt, D, kv.lv, b, h, sk, BX);
+  if (!rc) rc = map_bhsd(&tq, kv.q, dt, D, kv.lq, b, h, sq, kWideY);
+  if (!rc) rc = map_bhsd(&tdo, kv.dout, dt, D, kv.ldo, b, h, sq, kWideY);
+  if (!rc) rc = make_tmap_2d(&tl, kv.lse, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)sq, (uint64_t)bh, (uint64_t)sq * 4, kWideY, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (!rc) rc = make_tmap_2d(&td, kv.delta, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)sq, (uint64_t)bh, (uint64_t)sq * 4, kWideY, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (!rc) rc = map_ds_blocks(&tds_st, workspace, dt, sq, sk, slots, 32, 1);
+  if (!rc) rc = map_ds_blocks(&tds_ld, workspace, dt, sq, sk, slots, 64, 2);
+  if (!rc) rc = map_bhsd(&tk64, kv.k, dt, D, kv.lk, b, h, sk, 64);
+  if (rc) return rc;
+  BwdParams p;
+  p.sq = (int)sq;
+  p.sk = (int)sk;
+  p.scale = scale;
+  p.scale_log2 = scale * kLog2e;
+  p.causal = causal;
+  p.lse = kv.lse;
+  p.delta = kv.delta;
+  p.out0 = kv.out0;
+  p.out1 = kv.out1;
+  p.l0 = kv.l0;
+  p.l1 = kv.l1;
+  p.n_x_tiles = (int)(sk / BX);
+  p.bh0 = 0;
+  p.ds = workspace;
+  p.ds_ld = ds_row_elems(sq);
+  p.ds_slice = p.ds_ld * sk;
+  uint8_t* sched_base = reinterpret_cast<uint8_t*>(workspace) + slots * slot_bytes;
+  FusedParams fp;
+  fp.nq = (int)(sq / 128);
+  fp.nkt = (int)(sk / 128);
+  fp.n_slices = (int)bh;
+  fp.slots = (int)slots;
+  fp.sched = reinterpret_cast<int*>(sched_base);
+  fp.ready = fp.sched + kSchedInts;
+  fp.row_cnt = fp.ready + bh * fp.nq;
+  fp.dq_done = fp.row_cnt + bh * fp.nq;
+  fp.ds = reinterpret_cast<uint8_t*>(workspace);
+  fp.ds_slot_bytes = slot_bytes;
+  fp.dq = qa.out0;
+  fp.ldq = qa.l0;
+  // scheduler state: counters 0, ready queue -1
+  cudaError_t e = cudaMemsetAsync(sched_base, 0, sched_bytes, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(fp.ready, 0xff, (size_t)(bh * fp.nq) * 4, s);
+  if (e != cudaSuccess) return fail(FERRITE_LAUNCH_FAILED, "attn_bwd_fused: memset: %s", cudaGetErrorString(e));
+  auto kern = attn_bwd_fused_kernel<D, BF16>;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+  if (e != cudaSuccess) return fail(FERRITE_LAUNCH_FAILED, "attn_bwd_fused: smem attr: %s", cudaGetErrorString(e));
+  const int64_t units = bh * (fp.nq + fp.nkt);
+  const int grid = (int)std::min<int64_t>(units, num_sms(current_device()));
+  (void)launch_pdl(kern, dim3(grid), dim3(kFusedThreads), L::kTotal, s, tk, tv, tq, tdo, tl, td, tds_st, tds_ld,
+                   tk64, p, fp);
+  return check_launch("attn_bwd_fused");
+}
+
+static int dispatch_bwd_fused(cudaStream_t s, const BwdArgs& kv, const BwdArgs& qa, int64_t b, int64_t h,
+                              int64_t sq, int64_t sk, int64_t d, float scale, int causal, int dtype,
+                              void* workspace, size_t workspace_bytes) {
+  const bool bf = dtype == FERRITE_BF16;
+  if (d == 64)
+    return bf ? launch_bwd_fused<64, true>(s, kv, qa, b, h, sq, sk, scale, causal, workspace, workspace_bytes)
+              : launch_bwd_fused<64, false>(s, kv, qa, b, h, sq, sk, scale, causal, workspace, workspace_bytes);
+  return bf ? launch_bwd_fused<128, true>(s, kv, qa, b, h, sq, sk, scale, causal, workspace, workspace_bytes)
+            : launch_bwd_fused<128, false>(s, kv, qa, b, h, sq, sk, scale, causal, workspace, workspace_bytes);
 }
 
 static int strides_ok(const char* op, const ferrite_attn_strides* st) {
@@ -2514,7 +3263,7 @@ int ferrite_attn_bwd_dq_ds(void* stream, const void* ds, const void* k, void* dq
 size_t ferrite_attn_bwd_ds_workspace_size(int64_t b, int64_t h, int64_t sq, int64_t sk,
                                           int64_t d, int dtype) {
   if (b <= 0 || h <= 0 || sq <= 0 || sk <= 0 || !tc_fwd_ok(d, sk, dtype)) return 0;
-  return (size_t)(b * h) * (size_t)ds_slice_bytes(sq, sk);
+  return (size_t)(b * h) * (size_t)ds_slice_bytes(sq, sk) + (size_t)fused_sched_bytes(b * h, sq);
 }
 
 int ferrite_attn_bwd_ds(void* stream, const void* q, const void* k, const void* v,
@@ -2541,6 +3290,9 @@ int ferrite_attn_bwd_ds(void* stream, const void* q, const void* k, const void* 
     return attn_bwd_dq_impl(s, qa, b, h, sq, sk, d, scale, causal, dtype);
   }
   const int64_t bh = b * h;
+  if (fused_ok(sq, sk, d, causal) &&
+      (int64_t)workspace_bytes >= ds_slice_bytes(sq, sk) + fused_sched_bytes(bh, sq))
+    return dispatch_bwd_fused(s, kv, qa, b, h, sq, sk, d, scale, causal, dtype, workspace, workspace_bytes);
   for (int64_t bh0 = 0; bh0 < bh; bh0 += per) {
     const int64_t n = std::min<int64_t>(per, bh - bh0);
     kv.bh0 = qa.bh0 = bh0;

@@ -115,9 +115,11 @@ def _bwd(q, k, v, do, causal):
 @pytest.mark.parametrize("causal", [True, False])
 @pytest.mark.parametrize("budget_slices", [1, 4, None])
 def test_ds_backward_matches_recompute_and_oracle(monkeypatch, d, causal, budget_slices):
-    """dQ from the stored dS (whole batch, or chunks of 1 / 4 of the 6 slices)
-    against the recompute dQ kernel and the blockwise oracle; dK/dV are the same
-    kernel either way, so bitwise equal."""
+    """dQ from the stored dS (a workspace of the whole batch, or of 1 / 4 of the 6
+    slices: the fused backward then recycles its dS slots) against the recompute
+    path and the blockwise oracle.  The fused backward accumulates dK/dV over the
+    query tiles last-first, the recompute kernel first-last: equal up to f32
+    summation order, so compared at the dQ bound."""
     import importlib
 
     from ferrite import _native as nat
@@ -129,14 +131,14 @@ def test_ds_backward_matches_recompute_and_oracle(monkeypatch, d, causal, budget
     qn, kn, vn, don = (normal(rng, (b, h, s, d), BF16) for _ in range(4))
     q, k, v, do = (to_torch(a) for a in (qn, kn, vn, don))
     per_slice = nat.lib().ferrite_attn_bwd_ds_workspace_size(1, 1, s, s, d, nat.BF16)
-    assert per_slice == s * s * 2
+    assert per_slice >= s * s * 2  # one dS slice (+ the fused backward's scheduler state)
     if budget_slices is not None:
         monkeypatch.setattr(fa, "DS_WORKSPACE_BUDGET", budget_slices * per_slice)
     (dq, dk, dv), out, lse = _bwd(q, k, v, do, causal)
     monkeypatch.setenv("FERRITE_ATTN_BWD_DS", "0")
     (dq0, dk0, dv0), _, _ = _bwd(q, k, v, do, causal)
-    assert torch.equal(dk, dk0) and torch.equal(dv, dv0)
-    assert_bf16_close(dq, dq0, atol=4e-3)
+    for a, b_ in ((dq, dq0), (dk, dk0), (dv, dv0)):
+        assert_bf16_close(a, b_, atol=4e-3)
     o_ref, lse_ref = oa.flash_fwd(qn, kn, vn, causal=causal)
     g_ref = oa.flash_bwd(qn, kn, vn, o_ref, lse_ref, don, causal=causal)
     for got, ref, name in zip((dq, dk, dv), g_ref, ("dq", "dk", "dv")):
@@ -173,7 +175,8 @@ def test_ds_backward_is_deterministic():
 
 def test_split_dkv_ds_and_dq_ds_entry_points_over_slice_ranges():
     """The two halves called separately on slice ranges [0, 2) and [2, 6) give
-    the same gradients as the one-call backward."""
+    the same gradients as the one-call (fused) backward: dQ bitwise (same dS, same
+    product order), dK/dV up to the order of their f32 sums over query tiles."""
     import ctypes
 
     from ferrite import _native as nat
@@ -197,7 +200,9 @@ def test_split_dkv_ds_and_dq_ds_entry_points_over_slice_ranges():
                                               d**-0.5, 1, 128, 128, nat.BF16))
         nat.check(lib.ferrite_attn_bwd_dq_ds(sp, ds.data_ptr(), k.data_ptr(), dq.data_ptr(), ctypes.byref(st), begin, count, b, h, s, s, d,
                                              d**-0.5, 1, 128, 128, nat.BF16))
-    assert torch.equal(dq, dq_ref) and torch.equal(dk, dk_ref) and torch.equal(dv, dv_ref)
+    assert torch.equal(dq, dq_ref)
+    assert_bf16_close(dk, dk_ref, atol=4e-3)
+    assert_bf16_close(dv, dv_ref, atol=4e-3)
 
 
 # ---------------------------------------------------------------- kernel variants

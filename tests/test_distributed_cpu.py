@@ -76,20 +76,34 @@ def _bucket_worker(rank, ws, port, out):
 
 
 def _norm_worker(rank, ws, port, out):
+    """The token-sharded RMSNorm backward as the benchmark runs it: each rank takes
+    its row range (ferrite.sharding.norm_rows), writes its dw partial into the
+    exchange's buffer for the step and starts the overlapped all-reduce
+    (ferrite.sharding.DwExchange, two alternating buffers); four steps with
+    different upstream gradients, results read after later steps were started."""
     _init(rank, ws, port)
+    from ferrite.sharding import DwExchange, norm_rows
     from oracle import rmsnorm as on
 
     rng = np.random.default_rng(7)
-    rows, dim = 64, 48
+    rows, dim = 66, 48  # 33 rows a rank
     h = rng.standard_normal((rows, dim)).astype(np.float32)
     w = (1 + 0.1 * rng.standard_normal(dim)).astype(np.float32)
-    dy = rng.standard_normal((rows, dim)).astype(np.float32)
-    shard = slice(rank * rows // ws, (rank + 1) * rows // ws)
-    dh, dw = on.rmsnorm_bwd(h[shard], w, dy[shard])
-    t = torch.from_numpy(dw.copy())
-    dist.all_reduce(t)
-    np.save(os.path.join(out, f"dw{rank}.npy"), t.numpy())
-    np.save(os.path.join(out, f"dh{rank}.npy"), dh)
+    dys = [rng.standard_normal((rows, dim)).astype(np.float32) for _ in range(4)]
+    r0, r1 = norm_rows(rows, ws, rank)
+    ex = DwExchange(dim, "cpu")
+    dws = {}
+    for step, dy in enumerate(dys):
+        dh, dw = on.rmsnorm_bwd(h[r0:r1], w, dy[r0:r1])
+        ex.buffer(step).copy_(torch.from_numpy(dw))  # waits for step - 2's all-reduce first
+        ex.start(step)
+        if step >= 1:  # read the previous step's sum while this one is in flight
+            dws[step - 1] = ex.result(step - 1).clone()
+        np.save(os.path.join(out, f"dh{rank}_{step}.npy"), dh)
+    dws[3] = ex.result(3).clone()
+    ex.finish()
+    for step, t in dws.items():
+        np.save(os.path.join(out, f"dw{rank}_{step}.npy"), t.numpy())
     dist.barrier()
     dist.destroy_process_group()
 
@@ -129,14 +143,32 @@ def test_token_sharded_rmsnorm_backward_exchange():
     from oracle import rmsnorm as on
 
     rng = np.random.default_rng(7)
-    h = rng.standard_normal((64, 48)).astype(np.float32)
+    h = rng.standard_normal((66, 48)).astype(np.float32)
     w = (1 + 0.1 * rng.standard_normal(48)).astype(np.float32)
-    dy = rng.standard_normal((64, 48)).astype(np.float32)
-    dh_full, dw_full = on.rmsnorm_bwd(h, w, dy)
-    for r in range(2):
-        np.testing.assert_allclose(np.load(os.path.join(out, f"dw{r}.npy")), dw_full, rtol=1e-5, atol=1e-5)
-    dh = np.concatenate([np.load(os.path.join(out, f"dh{r}.npy")) for r in range(2)])
-    np.testing.assert_array_equal(dh, dh_full)  # row-local: sharding changes nothing
+    dys = [rng.standard_normal((66, 48)).astype(np.float32) for _ in range(4)]
+    for step, dy in enumerate(dys):
+        dh_full, dw_full = on.rmsnorm_bwd(h, w, dy)
+        for r in range(2):
+            np.testing.assert_allclose(np.load(os.path.join(out, f"dw{r}_{step}.npy")), dw_full, rtol=1e-5, atol=1e-5)
+        dh = np.concatenate([np.load(os.path.join(out, f"dh{r}_{step}.npy")) for r in range(2)])
+        np.testing.assert_array_equal(dh, dh_full)  # row-local: sharding changes nothing
+
+
+def test_shard_ranges_cover_every_unit_once():
+    sys.path[:0] = [os.path.join(ROOT, "ferrite-tpu_b200")]
+    from ferrite.sharding import attention_slices, norm_rows, shard_range
+
+    for n in (0, 1, 7, 256, 8192):
+        for world in (1, 2, 3, 4, 8):
+            ranges = [shard_range(n, world, r) for r in range(world)]
+            assert ranges[0][0] == 0 and ranges[-1][1] == n
+            assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
+            sizes = [e - b for b, e in ranges]
+            assert max(sizes) - min(sizes) <= 1
+    assert attention_slices(8, 32, 8, 3) == (96, 128)  # the long config at 8 GPUs: 32 slices a rank
+    assert norm_rows(8192, 4, 1) == (2048, 4096)
+    with pytest.raises(ValueError):
+        shard_range(10, 2, 2)
 
 
 @pytest.mark.timeout(120)
