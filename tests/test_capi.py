@@ -89,8 +89,11 @@ def test_strided_attention_validation_without_a_gpu():
 
 def test_ds_backward_host_checks_without_a_gpu():
     lib = nat.lib()
-    assert lib.ferrite_attn_bwd_ds_workspace_size(2, 3, 512, 512, 64, nat.BF16) == 6 * 512 * 512 * 2
-    assert lib.ferrite_attn_bwd_ds_workspace_size(1, 1, 200, 384, 64, nat.BF16) == 256 * 384 * 2  # rows padded to 64
+    def sched(slices, sq):  # the fused backward's scheduler state after the dS slots, 256-byte aligned
+        return -(-(8 + 2 * slices * -(-sq // 128) + slices) * 4 // 256) * 256
+
+    assert lib.ferrite_attn_bwd_ds_workspace_size(2, 3, 512, 512, 64, nat.BF16) == 6 * 512 * 512 * 2 + sched(6, 512)
+    assert lib.ferrite_attn_bwd_ds_workspace_size(1, 1, 200, 384, 64, nat.BF16) == 256 * 384 * 2 + sched(1, 200)  # rows padded to 64
     assert lib.ferrite_attn_bwd_ds_workspace_size(1, 1, 512, 512, 64, nat.F32) == 0  # CUDA-core path: no dS
     assert lib.ferrite_attn_bwd_ds_workspace_size(1, 1, 512, 512, 96, nat.BF16) == 0
     st = nat.AttnStrides()
