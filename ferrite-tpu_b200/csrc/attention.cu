@@ -1965,8 +1965,12 @@ __global__ void __launch_bounds__(kDqThreads, 1)
 // summation order); no atomics touch any result.
 
 constexpr int kFusedMaxDqStages = 6;
-// warps 0 TMA loads, 1 TMEM + MMA, 2-9 elementwise / dQ epilogue, 10 dS stores + signals
-constexpr int kFusedThreads = 352;
+// Warps: 0 TMA loads, 1 TMEM + MMA, 2 .. 2 + EW - 1 elementwise (dK/dV units) / dQ
+// epilogue (dQ units), then one warp of dS stores + signals.  EW = 8 (two warps per
+// TMEM lane quadrant, 64 query columns each; up to 168 registers a thread) or 16
+// (four per quadrant, 32 columns each; more warps per scheduler but 96 registers).
+template <int EW>
+constexpr int fused_threads() { return 32 * (EW + 3); }
 enum { kSchedNext = 0, kSchedHead = 1, kSchedTail = 2, kSchedAbort = 3, kSchedInts = 8 };
 
 struct FusedParams {
@@ -1974,8 +1978,8 @@ struct FusedParams {
   int n_slices;      // slices bh0 .. bh0 + n_slices - 1
   int slots;         // dS slots (slice-sized)
   int* sched;        // kSchedInts ints
-  int* ready;        // [n_slices * nq] published dQ unit ids (-1 = not yet written)
-  int* row_cnt;      // [n_slices * nq] dS producer-warp signals per query tile
+  int* ready;        // [n_slices * nq / 2] published dQ unit ids (-1 = not yet written)
+  int* row_cnt;      // [n_slices * nq / 2] dS tile signals per dQ unit
   int* dq_done;      // [n_slices] finished dQ units per slice
   uint8_t* ds;       // slot 0 of the dS blocks
   int64_t ds_slot_bytes;
@@ -1987,9 +1991,9 @@ template <int D>
 struct FusedSmem {
   using W = WideSmem<D>;
   static constexpr int kDataBytes = W::kDataBytes;
-  static constexpr int kDqABytes = 128 * 64 * 2;  // dS^T: 2 boxes of 64 queries x 64 keys
+  static constexpr int kDqABytes = 128 * 64 * 2;  // dS^T of one query tile: 2 boxes of 64 queries x 64 keys
   static constexpr int kDqBBytes = 64 * D * 2;    // K: D/64 boxes of 64 d x 64 keys
-  static constexpr int kDqStageBytes = kDqABytes + kDqBBytes;
+  static constexpr int kDqStageBytes = 2 * kDqABytes + kDqBBytes;  // two query tiles share the K block
   static constexpr int kDqStages =
       kDataBytes / kDqStageBytes < kFusedMaxDqStages ? kDataBytes / kDqStageBytes : kFusedMaxDqStages;
   static_assert(kDqStages >= 2, "dQ ring needs two stages");
@@ -2003,8 +2007,11 @@ struct FusedSmem {
   static constexpr int kTotal = kDataBytes + 1024;
 };
 
-__device__ __forceinline__ int fused_producers(const FusedParams& fp, int causal, int qt) {
-  return causal ? min(qt + 1, fp.nkt) : fp.nkt;  // one signal per key tile
+// A dQ unit covers the query tiles 2 u and 2 u + 1 of a slice (they share every K
+// block it loads).  Signals it waits for: one per key tile per query tile.
+__device__ __forceinline__ int fused_producers(const FusedParams& fp, int causal, int pair) {
+  const int q0 = 2 * pair, q1 = 2 * pair + 1;
+  return causal ? min(q0 + 1, fp.nkt) + min(q1 + 1, fp.nkt) : 2 * fp.nkt;
 }
 
 // Claim the next unit (thread 0 only).  Returns the unit id and sets kind (0 dK/dV,
@@ -2019,7 +2026,7 @@ __device__ __forceinline__ int fused_producers(const FusedParams& fp, int causal
 __device__ int fused_claim(const FusedParams& fp, int& kind, int& pending) {
   int* s = fp.sched;
   const int n_dkv = fp.n_slices * fp.nkt;
-  const int n_dq = fp.n_slices * fp.nq;
+  const int n_dq = fp.n_slices * (fp.nq / 2);
   const uint64_t t0 = globaltimer_ns();
   uint32_t spins = 0;
   while (true) {
@@ -2046,7 +2053,7 @@ __device__ int fused_claim(const FusedParams& fp, int& kind, int& pending) {
     if (pending < 0) pending = atomicAdd(&s[kSchedNext], 1);
     if (pending < n_dkv) {
       const int sl = pending / fp.nkt;
-      if (sl < fp.slots || ld_acquire_gpu(&fp.dq_done[sl - fp.slots]) >= fp.nq) {
+      if (sl < fp.slots || ld_acquire_gpu(&fp.dq_done[sl - fp.slots]) >= fp.nq / 2) {
         const int u = pending;
         pending = -1;
         kind = 0;
@@ -2066,16 +2073,16 @@ __device__ int fused_claim(const FusedParams& fp, int& kind, int& pending) {
 // global memory (the store warp, after the TMA stores of that tile completed).
 __device__ __forceinline__ void fused_signal(const FusedParams& fp, int causal, int sl, int qt) {
   fence_proxy_async_global();
-  const int id = sl * fp.nq + qt;
+  const int id = sl * (fp.nq / 2) + (qt >> 1);
   const int old = atom_add_acq_rel_gpu(&fp.row_cnt[id], 1);
-  if (old + 1 == fused_producers(fp, causal, qt)) {
+  if (old + 1 == fused_producers(fp, causal, qt >> 1)) {
     const int slot = atomicAdd(&fp.sched[kSchedTail], 1);
     st_release_gpu(&fp.ready[slot], id);
   }
 }
 
-template <int D, bool BF16>
-__global__ void __launch_bounds__(kFusedThreads, 1)
+template <int D, bool BF16, int EW>
+__global__ void __launch_bounds__(fused_threads<EW>(), 1)
     attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                           const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdo,
                           const __grid_constant__ CUtensorMap tlse, const __grid_constant__ CUtensorMap tdelta,
@@ -2085,6 +2092,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
   using L = FusedSmem<D>;
   constexpr int S = W::kStages;
   constexpr int QS = L::kDqStages;
+  constexpr int kStoreWarp = 2 + EW;
+  constexpr int CW = 128 * 4 / EW;  // query columns per elementwise warp (64 or 32)
+  constexpr int NG = EW / 4;        // elementwise warps per TMEM lane quadrant
   typedef typename std::conditional<BF16, __nv_bfloat16, __half>::type T;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -2156,12 +2166,12 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           }
           mbar_init(s_full, 1);
           mbar_init(dp_full, 1);
-          mbar_init(p_full, 8);
-          mbar_init(p_half, 8);
-          mbar_init(dp_free, 8);
-          mbar_init(ds_full, 8);
+          mbar_init(p_full, 8);  // one arrival per 32-query chunk 1, 3 (four lane quadrants each)
+          mbar_init(p_half, 8);  // one arrival per 32-query chunk 0, 2
+          mbar_init(dp_free, EW);
+          mbar_init(ds_full, EW);
           mbar_init(acc_full, 1);
-          mbar_init(stg_full, 8);
+          mbar_init(stg_full, EW);
           mbar_init(stg_free, 1);
         } else {
           if (*s_inited & 2) {
@@ -2249,23 +2259,26 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
             }
             tc_commit(is_s ? s_full : dp_full);
           };
+          // Query step kk (queries 16 kk .. 16 kk + 15) belongs to elementwise column
+          // group 16 kk / CW, which packs P^T into the first CW / 2 columns of its own
+          // CW and dS^T into the last CW / 2: P^T of step kk at CW g + (16 kk % CW) / 2,
+          // dS^T CW / 2 further.
+          auto packed = [](int kk) -> uint32_t { return (uint32_t)(CW * (16 * kk / CW) + (16 * kk % CW) / 2); };
           auto issue_dv = [&](int i, int part) {
             const uint64_t dm2 = sdesc_at(dy_mn, (i % S) * W::kStageBytes + W::kYBytes);
             const uint32_t pa = tmem + region(i, true);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-              const int kk = (q >> 1) * 4 + part * 2 + (q & 1);
-              tc_mma_f16_ts(t_dv, pa + (kk >> 2) * 64 + (kk & 3) * 8, sdesc_at(dm2, kk * 2048), idesc_a,
-                            (i > 0 || kk > 0) ? 1u : 0u);
+              const int kk = (q >> 1) * 4 + part * 2 + (q & 1);  // part 0: groups 0, 2; part 1: groups 1, 3
+              tc_mma_f16_ts(t_dv, pa + packed(kk), sdesc_at(dm2, kk * 2048), idesc_a, (i > 0 || kk > 0) ? 1u : 0u);
             }
           };
           auto issue_dk = [&](int i) {
             const uint64_t dm1 = sdesc_at(dy_mn, (i % S) * W::kStageBytes);
-            const uint32_t da = tmem + region(i, true) + 32;
+            const uint32_t da = tmem + region(i, true) + CW / 2;
 #pragma unroll
             for (int kk = 0; kk < kWideY / 16; ++kk)
-              tc_mma_f16_ts(t_dk, da + (kk >> 2) * 64 + (kk & 3) * 8, sdesc_at(dm1, kk * 2048), idesc_a,
-                            (i > 0 || kk > 0) ? 1u : 0u);
+              tc_mma_f16_ts(t_dk, da + packed(kk), sdesc_at(dm1, kk * 2048), idesc_a, (i > 0 || kk > 0) ? 1u : 0u);
             tc_commit(&y_empty[i % S]);
           };
           if (ok && (ok = mbar_wait(&y_full[0], 0, abort, 43))) {
@@ -2294,7 +2307,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           tc_commit(acc_full);
           mbar_drain(acc_full, 0);
         }
-      } else if (warp == 10) {
+      } else if (warp == kStoreWarp) {
         // ------------------------------------------------ dS^T stores + signals
         // One TMA store per 32-key x 64-query staging block; the stg_free arrival
         // lets the elementwise warps write the next tile while the stores drain to
@@ -2331,13 +2344,18 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         }
       } else {
         // ------------------------------------------------ elementwise warps
+        // warp w: TMEM lane quadrant w % 4 (key rows), query columns [CW cq, CW cq + CW)
+        // of each tile, cq = (w - 2) / 4; a warp reads and rewrites only its own CW
+        // columns of the S^T region (P^T packed into the first CW / 2, dS^T the rest)
         const int qw = warp & 3;
-        const int h = (warp - 2) >> 2;
+        const int cq = (warp - 2) >> 2;
         const int r = qw * 32 + lane;
         const int xrow = x0 + r;
         const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
-        const uint32_t t_col = tmem + lane_off + h * 64;
-        uint8_t* stg = smem + W::kStgOff + h * (BX * 128) + qw * 4096;
+        const uint32_t t_col = tmem + lane_off + CW * cq;
+        // staging tile: [64-query half][128 keys][128 B swizzled]; this warp's 2 CW bytes of each row
+        uint8_t* stg = smem + W::kStgOff + (CW * cq / 64) * (BX * 128) + qw * 4096;
+        const int g0 = (CW * cq % 64) / 8;  // first 16-byte granule of the row
         bool ok = true;
         for (int i = 0; ok && i < n_y; ++i) {
           const int ph = i & 1;
@@ -2351,62 +2369,67 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
             break;
           }
           tc_fence_after();
-          const float* st = reinterpret_cast<const float*>(smem + W::kYOff + s * W::kStageBytes + 2 * W::kYBytes) + h * 64;
-          uint32_t pf[64];
-          tmem_ld32(t_s, *reinterpret_cast<uint32_t(*)[32]>(&pf[0]));
-          tmem_ld32(t_s + 32, *reinterpret_cast<uint32_t(*)[32]>(&pf[32]));
+          const float* st = reinterpret_cast<const float*>(smem + W::kYOff + s * W::kStageBytes + 2 * W::kYBytes) + CW * cq;
+          uint32_t pf[CW];
+#pragma unroll
+          for (int c = 0; c < CW; c += 32) tmem_ld32(t_s + c, *reinterpret_cast<uint32_t(*)[32]>(&pf[c]));
           tmem_wait_ld();
           {
+            // four columns per step: one 16-byte load of lse, packed f32x2 math
+            // (each lane rounds exactly like fmaf(s, scale*log2e, -(lse*log2e)))
             const uint64_t sc2 = f2_make(p.scale_log2, p.scale_log2);
             const uint64_t nlog2e2 = f2_make(-kLog2e, -kLog2e);
-            auto body_a = [&](auto masked, auto c0) {
+            // 32-query chunks: P of chunk j is packed, published (p_half for even
+            // global chunks, p_full for odd) and dV's query steps on it can start
+            auto chunk_a = [&](auto c0) {
+              constexpr int C0 = decltype(c0)::value;
+              auto body = [&](auto masked) {
 #pragma unroll
-              for (int c = decltype(c0)::value; c < decltype(c0)::value + 32; c += 4) {
-                const float4 l4 = *reinterpret_cast<const float4*>(st + c);
-                const uint64_t x01 = f2_fma(f2_make_bits(pf[c], pf[c + 1]), sc2, f2_mul(f2_make(l4.x, l4.y), nlog2e2));
-                const uint64_t x23 = f2_fma(f2_make_bits(pf[c + 2], pf[c + 3]), sc2, f2_mul(f2_make(l4.z, l4.w), nlog2e2));
-                float x[4] = {f2_lo(x01), f2_hi(x01), f2_lo(x23), f2_hi(x23)};
-                if constexpr (decltype(masked)::value) {
+                for (int c = C0; c < C0 + 32; c += 4) {
+                  const float4 l4 = *reinterpret_cast<const float4*>(st + c);
+                  const uint64_t x01 = f2_fma(f2_make_bits(pf[c], pf[c + 1]), sc2, f2_mul(f2_make(l4.x, l4.y), nlog2e2));
+                  const uint64_t x23 = f2_fma(f2_make_bits(pf[c + 2], pf[c + 3]), sc2, f2_mul(f2_make(l4.z, l4.w), nlog2e2));
+                  float x[4] = {f2_lo(x01), f2_hi(x01), f2_lo(x23), f2_hi(x23)};
+                  if constexpr (decltype(masked)::value) {
 #pragma unroll
-                  for (int u = 0; u < 4; ++u) {
-                    const int qry = y0 + h * 64 + c + u;
-                    const bool valid = qry < p.sq && !(p.causal && xrow > qry + diag_shift);
-                    x[u] = valid ? x[u] : -INFINITY;
+                    for (int u = 0; u < 4; ++u) {
+                      const int qry = y0 + CW * cq + c + u;
+                      const bool valid = qry < p.sq && !(p.causal && xrow > qry + diag_shift);
+                      x[u] = valid ? x[u] : -INFINITY;
+                    }
                   }
-                }
 #pragma unroll
-                for (int u = 0; u < 4; ++u) pf[c + u] = __float_as_uint(ex2_approx(x[u]));
-              }
-            };
-            auto half_a = [&](auto c0, uint64_t* bar) {
+                  for (int u = 0; u < 4; ++u) pf[c + u] = __float_as_uint(ex2_approx(x[u]));
+                }
+              };
               if (need_mask)
-                body_a(std::true_type{}, c0);
+                body(std::true_type{});
               else
-                body_a(std::false_type{}, c0);
+                body(std::false_type{});
               uint32_t pp[16];
 #pragma unroll
               for (int c = 0; c < 32; c += 2) {
-                const float a0 = __uint_as_float(pf[decltype(c0)::value + c]);
-                const float a1 = __uint_as_float(pf[decltype(c0)::value + c + 1]);
+                const float a0 = __uint_as_float(pf[C0 + c]), a1 = __uint_as_float(pf[C0 + c + 1]);
                 pp[c / 2] = BF16 ? pack_bf16x2(a0, a1) : pack_f16x2(a0, a1);
               }
-              tmem_st16(t_s + decltype(c0)::value / 2, pp);
+              tmem_st16(t_s + C0 / 2, pp);
               tmem_wait_st();
               tc_fence_before();
               __syncwarp();
-              if (lane == 0) mbar_arrive(bar);
+              const int chunk = (CW * cq + C0) / 32;
+              if (lane == 0) mbar_arrive((chunk & 1) ? p_full : p_half);
             };
-            half_a(std::integral_constant<int, 0>{}, p_half);
-            half_a(std::integral_constant<int, 32>{}, p_full);
+            chunk_a(std::integral_constant<int, 0>{});
+            if constexpr (CW == 64) chunk_a(std::integral_constant<int, 32>{});
           }
           if (!mbar_wait(dp_full, ph, abort, 49)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          uint32_t b[64];
-          tmem_ld32(t_dp, *reinterpret_cast<uint32_t(*)[32]>(&b[0]));
-          tmem_ld32(t_dp + 32, *reinterpret_cast<uint32_t(*)[32]>(&b[32]));
+          uint32_t b[CW];
+#pragma unroll
+          for (int c = 0; c < CW; c += 32) tmem_ld32(t_dp + c, *reinterpret_cast<uint32_t(*)[32]>(&b[c]));
           tmem_wait_ld();
           tc_fence_before();
           __syncwarp();
@@ -2418,11 +2441,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           }
           uint8_t* row = stg + lane * 128;
 #pragma unroll
-          for (int hb = 0; hb < 2; ++hb) {
-            uint32_t dd[16];
+          for (int hb = 0; hb < CW / 16; ++hb) {  // 16 columns at a time (fewer live registers)
+            uint32_t dd[8];
 #pragma unroll
-            for (int e = 0; e < 32; e += 4) {
-              const int c = hb * 32 + e;
+            for (int e = 0; e < 16; e += 4) {
+              const int c = hb * 16 + e;
               const float4 d4 = *reinterpret_cast<const float4*>(st + kWideY + c);
               const uint64_t d01 = f2_mul(f2_make_bits(pf[c], pf[c + 1]),
                                           f2_sub(f2_make_bits(b[c], b[c + 1]), f2_make(d4.x, d4.y)));
@@ -2431,10 +2454,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
               dd[e / 2] = BF16 ? pack_bf16x2(f2_lo(d01), f2_hi(d01)) : pack_f16x2(f2_lo(d01), f2_hi(d01));
               dd[e / 2 + 1] = BF16 ? pack_bf16x2(f2_lo(d23), f2_hi(d23)) : pack_f16x2(f2_lo(d23), f2_hi(d23));
             }
-            tmem_st16(t_s + 32 + hb * 16, dd);
+            tmem_st8(t_s + CW / 2 + 8 * hb, dd);
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              const int g16 = hb * 4 + v;
+            for (int v = 0; v < 2; ++v) {
+              const int g16 = g0 + 2 * hb + v;
               *reinterpret_cast<uint4*>(row + ((g16 ^ (lane & 7)) << 4)) =
                   make_uint4(dd[4 * v], dd[4 * v + 1], dd[4 * v + 2], dd[4 * v + 3]);
             }
@@ -2447,14 +2470,18 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(stg_full);
         }
+        // epilogue: the first NG / 2 column groups store dK (x scale), the others dV,
+        // D / (NG / 2) columns each
+        constexpr int OC = D / (NG / 2);
+        const int hk = cq / (NG / 2), c_begin = (cq % (NG / 2)) * OC;
         if (n_y > 0 && ok && mbar_wait(acc_full, 0, abort, 51)) {
           tc_fence_after();
           const bool row_ok = xrow < p.sk;
-          T* out = reinterpret_cast<T*>(h == 0 ? p.out0 : p.out1) + (h == 0 ? p.l0 : p.l1).row(bh, xrow);
-          const uint32_t src = (h == 0 ? t_dk : t_dv) + lane_off;
-          const float mul = h == 0 ? p.scale : 1.0f;
+          T* out = reinterpret_cast<T*>(hk == 0 ? p.out0 : p.out1) + (hk == 0 ? p.l0 : p.l1).row(bh, xrow);
+          const uint32_t src = (hk == 0 ? t_dk : t_dv) + lane_off;
+          const float mul = hk == 0 ? p.scale : 1.0f;
 #pragma unroll
-          for (int c0 = 0; c0 < D; c0 += 32) {
+          for (int c0 = c_begin; c0 < c_begin + OC; c0 += 32) {
             uint32_t v[32];
             tmem_ld32(src + c0, v);
             tmem_wait_ld();
@@ -2472,21 +2499,26 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
             }
           }
         } else if (n_y == 0 && xrow < p.sk) {
-          T* out = reinterpret_cast<T*>(h == 0 ? p.out0 : p.out1) + (h == 0 ? p.l0 : p.l1).row(bh, xrow);
-          for (int c = 0; c < D; ++c) out[c] = DT<T>::from_f(0.f);
+          T* out = reinterpret_cast<T*>(hk == 0 ? p.out0 : p.out1) + (hk == 0 ? p.l0 : p.l1).row(bh, xrow);
+          for (int c = c_begin; c < c_begin + OC; ++c) out[c] = DT<T>::from_f(0.f);
         }
       }
     } else {
       // ============================================================ dQ unit
-      const int sl = unit / fp.nq;
-      const int qt = unit - sl * fp.nq;
+      // query tiles qt0 = 2 u' and qt0 + 1 of slice sl; K blocks up to the higher
+      // tile's diagonal, the lower tile's MMAs stop at its own
+      const int sl = unit / (fp.nq / 2);
+      const int qt0 = 2 * (unit - sl * (fp.nq / 2));
       const int slot = sl % fp.slots;
       const int bh = p.bh0 + sl;
       const int hh = bh % p.l0.nh, bb = bh / p.l0.nh;
-      int last_key = p.sk - 1;
-      if (p.causal) last_key = min(last_key, qt * 128 + 127 + diag_shift);
-      const int nkb = last_key < 0 ? 0 : last_key / 64 + 1;
-      const int nqb = p.sq / 64;  // query blocks per key block in the dS layout
+      auto kblocks = [&](int qt) {
+        int last_key = p.sk - 1;
+        if (p.causal) last_key = min(last_key, qt * 128 + 127 + diag_shift);
+        return last_key < 0 ? 0 : last_key / 64 + 1;
+      };
+      const int nkb0 = kblocks(qt0), nkb = kblocks(qt0 + 1);
+      const int nqb = (p.sq + 63) / 64;  // query blocks per key block in the dS layout
       if (warp == 0) {
         if (lane == 0) {
           const uint64_t last_use = l2_policy_evict_first();  // dS is read once, then discarded
@@ -2494,9 +2526,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
             const int st = kb % QS;
             if (!mbar_wait(&q_empty[st], ((kb / QS) & 1) ^ 1, abort, 62)) break;
             uint8_t* sa = smem + st * L::kDqStageBytes;
-            uint8_t* sb = sa + L::kDqABytes;
-            mbar_arrive_expect_tx(&q_full[st], L::kDqStageBytes);
-            tma_load_4d_hint(sa, &tds_ld, &q_full[st], 0, 0, qt * 2, slot * nkb_all + kb, last_use);
+            uint8_t* sb = sa + 2 * L::kDqABytes;
+            const bool both = kb < nkb0;
+            mbar_arrive_expect_tx(&q_full[st], (both ? 2 : 1) * L::kDqABytes + L::kDqBBytes);
+            tma_load_4d_hint(sa + L::kDqABytes, &tds_ld, &q_full[st], 0, 0, (qt0 + 1) * 2, slot * nkb_all + kb, last_use);
+            if (both) tma_load_4d_hint(sa, &tds_ld, &q_full[st], 0, 0, qt0 * 2, slot * nkb_all + kb, last_use);
 #pragma unroll
             for (int c = 0; c < D / 64; ++c) tma_load_4d(sb + c * 8192, &tk64, &q_full[st], c * 64, kb * 64, hh, bb);
           }
@@ -2506,44 +2540,50 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           constexpr uint32_t idesc = make_idesc_f16(128, D, BF16, true, true);
           const uint32_t s0 = smem_u32(smem);
           const uint64_t da_base = make_sdesc(s0, 8192, 1024);
-          const uint64_t db_base = make_sdesc(s0 + L::kDqABytes, 8192, 1024);
-          bool ok = true;
+          const uint64_t db_base = make_sdesc(s0 + 2 * L::kDqABytes, 8192, 1024);
           for (int kb = 0; kb < nkb; ++kb) {
             const int st = kb % QS;
-            if (!mbar_wait(&q_full[st], (kb / QS) & 1, abort, 63)) {
-              ok = false;
-              break;
-            }
+            if (!mbar_wait(&q_full[st], (kb / QS) & 1, abort, 63)) break;
             tc_fence_after();
             const uint64_t da = sdesc_at(da_base, st * L::kDqStageBytes);
             const uint64_t db = sdesc_at(db_base, st * L::kDqStageBytes);
+            // accumulators: tile qt0 at columns [0, D), qt0 + 1 at [D, 2 D)
+            if (kb < nkb0) {
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                tc_mma_f16_ss(tmem, sdesc_at(da, kk * 2048), sdesc_at(db, kk * 2048), idesc, (kb | kk) != 0 ? 1u : 0u);
+            }
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-              tc_mma_f16_ss(tmem, sdesc_at(da, kk * 2048), sdesc_at(db, kk * 2048), idesc, (kb | kk) != 0 ? 1u : 0u);
+              tc_mma_f16_ss(tmem + D, sdesc_at(da, L::kDqABytes + kk * 2048), sdesc_at(db, kk * 2048), idesc,
+                            (kb | kk) != 0 ? 1u : 0u);
             tc_commit(&q_empty[st]);
           }
-          (void)ok;
           tc_commit(q_acc);
           mbar_drain(q_acc, 0);
         }
-      } else if (warp < 10) {
+      } else if (warp < kStoreWarp) {
+        // the first NG / 2 column groups store tile qt0's dQ, the others tile qt0 + 1,
+        // D / (NG / 2) columns each
+        constexpr int OC = D / (NG / 2);
         const int qw = warp & 3;
-        const int h = (warp - 2) >> 2;  // dQ columns [h D/2, (h + 1) D/2)
+        const int cq = (warp - 2) >> 2;
+        const int tile = cq / (NG / 2), c_begin = (cq % (NG / 2)) * OC;
         const int r = qw * 32 + lane;
         if (nkb > 0 && mbar_wait(q_acc, 0, abort, 64)) {
           tc_fence_after();
-          const int qrow = qt * 128 + r;
-          const uint32_t src = tmem + ((uint32_t)(qw * 32) << 16) + h * (D / 2);
-          T* out = reinterpret_cast<T*>(fp.dq) + fp.ldq.row(bh, qrow) + h * (D / 2);
-#pragma unroll 1
-          for (int c0 = 0; c0 < D / 2; c0 += 32) {
+          const int qrow = (qt0 + tile) * 128 + r;
+          const uint32_t src = tmem + ((uint32_t)(qw * 32) << 16) + tile * D;
+          T* out = reinterpret_cast<T*>(fp.dq) + fp.ldq.row(bh, qrow);
+          const float m = p.scale;
+#pragma unroll
+          for (int c0 = c_begin; c0 < c_begin + OC; c0 += 32) {
             uint32_t v[32];
             tmem_ld32(src + c0, v);
             tmem_wait_ld();
 #pragma unroll
             for (int e = 0; e < 32; e += 8) {
               const float* f = reinterpret_cast<const float*>(&v[e]);
-              const float m = p.scale;
               uint4 w;
               w.x = BF16 ? pack_bf16x2(f[0] * m, f[1] * m) : pack_f16x2(f[0] * m, f[1] * m);
               w.y = BF16 ? pack_bf16x2(f[2] * m, f[3] * m) : pack_f16x2(f[2] * m, f[3] * m);
@@ -2552,12 +2592,14 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
               *reinterpret_cast<uint4*>(out + c0 + e) = w;
             }
           }
-          // every load of this tile's dS has completed (its MMAs have): drop the lines
+          // every load of these tiles' dS has completed (their MMAs have): drop the lines
           const uint8_t* base = fp.ds + (int64_t)slot * fp.ds_slot_bytes;
-          const int t = threadIdx.x - 64;  // 0 .. 255
-          for (int idx = t; idx < nkb * 128; idx += 256) {
-            const int kb = idx >> 7;
-            discard_l2_line(base + ((int64_t)kb * nqb + qt * 2) * 8192 + (idx & 127) * 128);
+          const int t = threadIdx.x - 64;  // 0 .. 32 EW - 1
+          const int lines0 = nkb0 * 128, lines = lines0 + nkb * 128;
+          for (int idx = t; idx < lines; idx += 32 * EW) {
+            const int j = idx < lines0 ? idx : idx - lines0;
+            const int qt = idx < lines0 ? qt0 : qt0 + 1;
+            discard_l2_line(base + ((int64_t)(j >> 7) * nqb + qt * 2) * 8192 + (j & 127) * 128);
           }
         }
       }
@@ -2572,7 +2614,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         st_relaxed_gpu(&fp.sched[kSchedAbort], 1);
       } else if (*s_kind == 1) {
         __threadfence();  // the discards above are ordered before the slot is handed on
-        red_add_release_gpu(&fp.dq_done[unit / fp.nq], 1);
+        red_add_release_gpu(&fp.dq_done[unit / (fp.nq / 2)], 1);
       }
     }
   }
@@ -2882,13 +2924,13 @@ static int64_t fused_sched_bytes(int64_t nslices, int64_t sq) {
 }
 
 static bool fused_ok(int64_t sq, int64_t sk, int64_t d, int causal) {
-  if (env_int("FERRITE_ATTN_BWD_FUSED", 0) == 0) return false;
+  if (env_int("FERRITE_ATTN_BWD_FUSED", 1) == 0) return false;
   if (d != 64 && d != 128) return false;
-  if (sq % 128 != 0 || sk % 128 != 0) return false;
+  if (sq % 256 != 0 || sk % 128 != 0) return false;  // dQ units pair the 128-query tiles
   return !causal || sq == sk;
 }
 
-template <int D, bool BF16>
+template <int D, bool BF16, int EW>
 static int launch_bwd_fused(cudaStream_t s, const BwdArgs& kv, const BwdArgs& qa, int64_t b, int64_t h,
                             int64_t sq, int64_t sk, float scale, int causal, void* workspace,
                             size_t workspace_bytes) {
@@ -2943,14 +2985,14 @@ static int launch_bwd_fused(cudaStream_t s, const BwdArgs& kv, const BwdArgs& qa
   fp.ldq = qa.l0;
   // scheduler state: counters 0, ready queue -1
   cudaError_t e = cudaMemsetAsync(sched_base, 0, sched_bytes, s);
-  if (e == cudaSuccess) e = cudaMemsetAsync(fp.ready, 0xff, (size_t)(bh * fp.nq) * 4, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(fp.ready, 0xff, (size_t)(bh * (fp.nq / 2)) * 4, s);
   if (e != cudaSuccess) return fail(FERRITE_LAUNCH_FAILED, "attn_bwd_fused: memset: %s", cudaGetErrorString(e));
-  auto kern = attn_bwd_fused_kernel<D, BF16>;
+  auto kern = attn_bwd_fused_kernel<D, BF16, EW>;
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
   if (e != cudaSuccess) return fail(FERRITE_LAUNCH_FAILED, "attn_bwd_fused: smem attr: %s", cudaGetErrorString(e));
-  const int64_t units = bh * (fp.nq + fp.nkt);
+  const int64_t units = bh * (fp.nq / 2 + fp.nkt);
   const int grid = (int)std::min<int64_t>(units, num_sms(current_device()));
-  (void)launch_pdl(kern, dim3(grid), dim3(kFusedThreads), L::kTotal, s, tk, tv, tq, tdo, tl, td, tds_st, tds_ld,
+  (void)launch_pdl(kern, dim3(grid), dim3(fused_threads<EW>()), L::kTotal, s, tk, tv, tq, tdo, tl, td, tds_st, tds_ld,
                    tk64, p, fp);
   return check_launch("attn_bwd_fused");
 }
@@ -2959,11 +3001,15 @@ static int dispatch_bwd_fused(cudaStream_t s, const BwdArgs& kv, const BwdArgs& 
                               int64_t sq, int64_t sk, int64_t d, float scale, int causal, int dtype,
                               void* workspace, size_t workspace_bytes) {
   const bool bf = dtype == FERRITE_BF16;
-  if (d == 64)
-    return bf ? launch_bwd_fused<64, true>(s, kv, qa, b, h, sq, sk, scale, causal, workspace, workspace_bytes)
-              : launch_bwd_fused<64, false>(s, kv, qa, b, h, sq, sk, scale, causal, workspace, workspace_bytes);
-  return bf ? launch_bwd_fused<128, true>(s, kv, qa, b, h, sq, sk, scale, causal, workspace, workspace_bytes)
-            : launch_bwd_fused<128, false>(s, kv, qa, b, h, sq, sk, scale, causal, workspace, workspace_bytes);
+  const bool ew16 = env_int("FERRITE_ATTN_BWD_FUSED_EW", 8) == 16;
+#define FUSED(DV, B, E) launch_bwd_fused<DV, B, E>(s, kv, qa, b, h, sq, sk, scale, causal, workspace, workspace_bytes)
+  if (d == 64) {
+    if (ew16) return bf ? FUSED(64, true, 16) : FUSED(64, false, 16);
+    return bf ? FUSED(64, true, 8) : FUSED(64, false, 8);
+  }
+  if (ew16) return bf ? FUSED(128, true, 16) : FUSED(128, false, 16);
+  return bf ? FUSED(128, true, 8) : FUSED(128, false, 8);
+#undef FUSED
 }
 
 static int strides_ok(const char* op, const ferrite_attn_strides* st) {
@@ -3293,8 +3339,12 @@ int ferrite_attn_bwd_ds(void* stream, const void* q, const void* k, const void* 
   if (fused_ok(sq, sk, d, causal) &&
       (int64_t)workspace_bytes >= ds_slice_bytes(sq, sk) + fused_sched_bytes(bh, sq))
     return dispatch_bwd_fused(s, kv, qa, b, h, sq, sk, d, scale, causal, dtype, workspace, workspace_bytes);
-  for (int64_t bh0 = 0; bh0 < bh; bh0 += per) {
-    const int64_t n = std::min<int64_t>(per, bh - bh0);
+  // two launches per chunk of slices; chunks of equal size (32 slices in a budget of 31
+  // run as 16 + 16, not 31 + 1, whose second launch would leave most SMs idle)
+  const int64_t nchunks = (bh + per - 1) / per;
+  const int64_t chunk = (bh + nchunks - 1) / nchunks;
+  for (int64_t bh0 = 0; bh0 < bh; bh0 += chunk) {
+    const int64_t n = std::min<int64_t>(chunk, bh - bh0);
     kv.bh0 = qa.bh0 = bh0;
     kv.nbh = qa.nbh = n;
     kv.ds = qa.ds = workspace;

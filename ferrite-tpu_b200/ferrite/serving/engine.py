@@ -192,6 +192,14 @@ class Engine:
 
     def prefill(self, prompts: list[list[int]]):
         """Returns (first token [B], pos [B], caches). Prompts are right-padded to a bucket."""
+        token, pos, kc, vc, graph_owned = self._run_prefill(prompts)
+        if graph_owned:  # the graph's buffers are reused by the next replay
+            kc, vc = kc.clone(), vc.clone()
+        return token, pos, kc, vc
+
+    def _run_prefill(self, prompts: list[list[int]]):
+        """prefill() without copying the caches out of a captured graph's buffers:
+        (token, pos, kc, vc, graph_owned), valid until the bucket's next replay."""
         b = self.serve.batch
         if len(prompts) != b:
             raise ValueError(f"engine built for batch {b}, got {len(prompts)} prompts")
@@ -206,10 +214,9 @@ class Engine:
         if g is not None:
             g.replay()
             logits, kc, vc = out
-            kc, vc = kc.clone(), vc.clone()  # the graph's buffers are reused by the next replay
         else:
             logits, kc, vc = prefill(self.params, tok, lens, self.prefill_cfg, self.serve.max_len)
-        return torch.argmax(logits, dim=-1), torch.from_numpy(lengths).to(self.device), kc, vc
+        return torch.argmax(logits, dim=-1), torch.from_numpy(lengths).to(self.device), kc, vc, g is not None
 
     def decode(self, token, pos, kc, vc):
         """One greedy step; updates kc / vc in place.  Caches that are the engine's own decode
@@ -228,11 +235,15 @@ class Engine:
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0 = time.perf_counter()
         e0.record()
-        token, pos, kc, vc = self.prefill(prompts)
-        if self._decode_graph is not None:  # continue in the captured decode graph's own caches
+        token, pos, kc, vc, graph_owned = self._run_prefill(prompts)
+        if self._decode_graph is not None:
+            # continue in the captured decode graph's own caches, copied straight from the
+            # prefill output (one copy of each cache, no intermediate clone)
             self._dkc.copy_(kc)
             self._dvc.copy_(vc)
             kc, vc = self._dkc, self._dvc
+        elif graph_owned:
+            kc, vc = kc.clone(), vc.clone()
         e1.record()
         out = [token.cpu().numpy()]
         ttft = e0.elapsed_time(e1)
