@@ -386,6 +386,7 @@ class AttnWorkload:
     scaling = "strong"
     bound = "tensor"
     B, H, S, D = 8, 32, 8192, 128
+    L2_NOTE = "inputs larger than L2 (q, k, v, dO 512 MiB each at 1 GPU)"
     kernels = ("attn_fwd", "attn_bwd_prep", "attn_bwd")
     launches_per_step = 3
     n_events = 4
@@ -458,7 +459,7 @@ class AttnWorkload:
         """The config keys, from the class (the reference arm prints the same ones)."""
         return {"workload": cls.name, "batch": cls.B, "heads": cls.H, "seq_len": cls.S, "head_dim": cls.D, "causal": True,
                 "block_q": 128, "block_k": 128, "heads_per_gpu": cls.B * cls.H // ws, "parallelism": f"batch*heads sharded over {ws} rank(s)",
-                "l2": "inputs larger than L2 (q, k, v, dO 512 MiB each at 1 GPU)"}
+                "l2": cls.L2_NOTE}
 
     def config(self):
         return {**self.static_config(self.ws), "batch": self.B, "heads": self.H, "seq_len": self.S, "head_dim": self.D,
@@ -505,6 +506,20 @@ class AttnWorkload:
                 "seconds_per_sample": t, "sample_fraction": slices / (cls.B * cls.H)}
 
 
+class AttnSmallWorkload(AttnWorkload):
+    """the reference's CPU-runnable attention case, causal fwd + bwd at
+    b2 h4 s512 d64 bf16 (blocks 128)."""
+
+    name = "flash_attention_causal_fwd_bwd_b2_h4_s512_d64_bf16"
+    metric = "causal flash-attn fwd+bwd TFLOP/s (b2 h4 s512 d64)"
+    B, H, S, D = 2, 4, 512, 64
+    L2_NOTE = "inputs 256 KiB each (L2-resident; launch-latency bound)"
+
+    @classmethod
+    def cpu_baseline(cls, slices=None, threads=None):
+        return super().cpu_baseline(slices=cls.B * cls.H, threads=min(threads or _host_cores(), cls.B * cls.H))
+
+
 class GemmWorkload:
     """bf16 8192^3 forward + the two backward GEMMs (replicas at N > 1)."""
 
@@ -515,6 +530,8 @@ class GemmWorkload:
     scaling = "weak"
     bound = "tensor"
     M = N = K = 8192
+    TORCH_DTYPE = torch.bfloat16
+    L2_NOTE = "operands 128 MiB each (larger than L2)"
     kernels = ("gemm_fwd", "gemm_dA", "gemm_dB")
     launches_per_step = 3
     n_events = 4
@@ -526,10 +543,11 @@ class GemmWorkload:
         g = torch.Generator(device=dev)
         g.manual_seed(rank)
         sk = 1 / np.sqrt(self.K)
-        self.a = (torch.randn(self.M, self.K, generator=g, device=dev) * sk).to(torch.bfloat16)
-        self.b = (torch.randn(self.K, self.N, generator=g, device=dev) * sk).to(torch.bfloat16)
-        self.gout = torch.randn(self.M, self.N, generator=g, device=dev).to(torch.bfloat16)
-        self.c = torch.empty(self.M, self.N, dtype=torch.bfloat16, device=dev)
+        dt = self.TORCH_DTYPE
+        self.a = (torch.randn(self.M, self.K, generator=g, device=dev) * sk).to(dt)
+        self.b = (torch.randn(self.K, self.N, generator=g, device=dev) * sk).to(dt)
+        self.gout = torch.randn(self.M, self.N, generator=g, device=dev).to(dt)
+        self.c = torch.empty(self.M, self.N, dtype=dt, device=dev)
         self.da = torch.empty_like(self.a)
         self.db = torch.empty_like(self.b)
         f = 2 * self.M * self.N * self.K
@@ -559,13 +577,15 @@ class GemmWorkload:
 
     def config(self):
         return {"workload": self.name, "m": self.M, "n": self.N, "k": self.K, "parallelism": "independent replicas" if self.ws > 1 else "single GPU",
-                "l2": "operands 128 MiB each (larger than L2)"}
+                "l2": self.L2_NOTE}
 
     def e2e_setup(self):
         self.host = {"a": self.a.cpu().pin_memory(), "b": self.b.cpu().pin_memory(), "g": self.gout.cpu().pin_memory()}
-        self.out_host = {k: torch.empty(self.M, self.N, dtype=torch.bfloat16).pin_memory() for k in ("c", "da", "db")}
-        self.h2d_bytes = sum(t.numel() * 2 for t in self.host.values())
-        self.d2h_bytes = sum(t.numel() * 2 for t in self.out_host.values())
+        self.out_host = {"c": torch.empty(self.M, self.N, dtype=self.TORCH_DTYPE).pin_memory(),
+                         "da": torch.empty(self.M, self.K, dtype=self.TORCH_DTYPE).pin_memory(),
+                         "db": torch.empty(self.K, self.N, dtype=self.TORCH_DTYPE).pin_memory()}
+        self.h2d_bytes = sum(t.numel() * t.element_size() for t in self.host.values())
+        self.d2h_bytes = sum(t.numel() * t.element_size() for t in self.out_host.values())
         self.e2e_api = "ferrite.kernels.matmul.matmul(x, y) + autograd backward, pinned host buffers"
 
     def e2e_step(self):
@@ -599,6 +619,28 @@ class GemmWorkload:
         return {"value": flops / t / 1e12, "unit": "TFLOP/s", "cores": threads or _host_cores(), "kind": "port",
                 "sample": f"{rows} of {cls.M} rows, numpy f32 BLAS (oracle matmul_reference / matmul_vjp arithmetic)",
                 "seconds_per_sample": t, "sample_fraction": rows / cls.M}
+
+
+class GemmRaggedWorkload(GemmWorkload):
+    """configs[2], ragged case: bf16 M=4000, N=3000, K=5000 forward + both VJP products
+    (no dimension a multiple of the 128 / 256 tiles: TMA zero-fills the edges)."""
+
+    name = "matmul_bf16_ragged_4000x3000x5000_fwd_and_vjp"
+    metric = "matmul bf16 4000x3000x5000 fwd+2bwd TFLOP/s"
+    M, N, K = 4000, 3000, 5000
+    L2_NOTE = "operands 30-40 MB each (inside L2; the shapes' edge tiles dominate)"
+
+
+class GemmF32Workload(GemmWorkload):
+    """configs[2], f32 case: 2048^3 at Precision.HIGHEST (exact f32 products on the CUDA
+    cores, _compat.py:17-26), forward + both VJP products."""
+
+    name = "matmul_f32_2048cubed_highest_fwd_and_vjp"
+    metric = "matmul f32 2048^3 HIGHEST fwd+2bwd TFLOP/s"
+    dtype = "f32"
+    M = N = K = 2048
+    TORCH_DTYPE = torch.float32
+    L2_NOTE = "operands 16 MiB each (inside L2)"
 
 
 GPT_CFG = dict(vocab_size=32000, seq_len=1024, d_model=1024, n_head=16, n_layer=24, d_ff=4096)
@@ -940,7 +982,13 @@ class DecodeWorkload:
                 "sample_fraction": layers / cls.L}
 
 
-WORKLOADS = {"norm": NormWorkload, "attn": AttnWorkload, "gemm": GemmWorkload, "gpt": GptWorkload, "prefill": PrefillWorkload, "decode": DecodeWorkload}
+WORKLOADS = {"norm": NormWorkload, "attn": AttnWorkload, "attn_small": AttnSmallWorkload, "gemm": GemmWorkload,
+             "gemm_ragged": GemmRaggedWorkload, "gemm_f32": GemmF32Workload, "gpt": GptWorkload, "prefill": PrefillWorkload,
+             "decode": DecodeWorkload}
+DEFAULT_WORKLOAD = "attn"
+# the other benchmark configs, measured after the default workload at N = 1 and reported
+# as compact lines inside its JSON line (so one driver run covers every config)
+OTHER_CONFIGS = ("attn_small", "norm", "gemm", "gemm_ragged", "gemm_f32", "gpt", "prefill", "decode")
 
 
 # ----------------------------------------------------------------------------- runners
@@ -957,6 +1005,31 @@ def run_ours(args, ws, rank, local):
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     W = WORKLOADS[args.workload]
     shape = tuple(int(v) for v in args.shape.split(",")) if args.shape else None
+    out = measure(W, args, ws, rank, dev, shape, cpu_baseline=rank == 0 and ws == 1 and not args.no_cpu_baseline)
+    if ws == 1 and shape is None and args.workload == DEFAULT_WORKLOAD and not args.no_other_configs:
+        # every other benchmark config on the same GPU, each with its own roofline,
+        # e2e and CPU baseline, reported inside this line
+        import gc
+
+        others = []
+        for name in OTHER_CONFIGS:
+            gc.collect()
+            torch.cuda.empty_cache()
+            sub = argparse.Namespace(**{**vars(args), "steps": min(args.steps, 10), "warmup": 3})
+            others.append(measure(WORKLOADS[name], sub, 1, rank, dev, None, cpu_baseline=not args.no_cpu_baseline))
+        out["other_configs"] = others
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
+def measure(W, args, ws, rank, dev, shape, cpu_baseline):
+    """One workload: warm-up, the timed K steps, the per-kernel pass, the end-to-end
+    pass through the public API and (optionally) the CPU baseline; returns its line."""
+    import torch.distributed as dist
+
     wl = W(dev, ws, rank, shape)
 
     def sync_all():
@@ -1062,23 +1135,20 @@ def run_ours(args, ws, rank, local):
         out["roofline"]["kernels_gbs"] = {k: round(wl.kernel_work[k] / (v / 1e3) / 1e9, 1) for k, v in bd.items() if wl.kernel_work.get(k)}
     else:
         out["roofline"]["kernels_tflops"] = {k: round(wl.kernel_work[k] / (v / 1e3) / 1e12, 1) for k, v in bd.items() if wl.kernel_work.get(k)}
-    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+    if cpu_baseline:
         cb = W.cpu_baseline()
         out["cpu_baseline"] = {k: (round(v, 4) if isinstance(v, float) else v) for k, v in cb.items()}
     if getattr(wl, "exchange", None) is not None:
         wl.exchange.finish()
-    if ws > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank == 0:
-        print(json.dumps(out), flush=True)
+    del wl
+    return out
 
 
 def run_reference(args, ws, rank):
     if rank != 0:
         return
     W = WORKLOADS[args.workload]
-    heavy = args.workload in ("gpt", "attn", "prefill", "decode")
+    heavy = args.workload in ("gpt", "attn", "attn_small", "prefill", "decode")
     for _ in range(1 if heavy else min(args.warmup, 3)):
         W.cpu_baseline()
     runs = [W.cpu_baseline() for _ in range(min(args.steps, 3) if heavy else args.steps)]
@@ -1113,8 +1183,9 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="attn")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-other-configs", action="store_true", help="default workload only (no sub-lines for the other configs)")
     ap.add_argument("--shape", default=None, help="smaller case for profiling captures: norm rows,dim | attn b,h,s,d | gemm m,n,k | decode layers,b,h,max_len,d")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)  # timing rule: at least 3 untimed warm-up steps

@@ -50,7 +50,7 @@ def test_default_reference_arm_is_the_long_attention_config():
 def test_help_lists_the_workloads():
     p = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--help"], capture_output=True, text=True, timeout=120, cwd=ROOT)
     assert p.returncode == 0
-    for w in ("norm", "attn", "gemm", "gpt", "prefill", "decode"):
+    for w in ("norm", "attn", "attn_small", "gemm", "gemm_ragged", "gemm_f32", "gpt", "prefill", "decode"):
         assert w in p.stdout
 
 
