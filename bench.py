@@ -171,6 +171,25 @@ def _events(n):
     return [torch.cuda.Event(enable_timing=True) for _ in range(n)]
 
 
+def _fp32_line(kernel: str, flops: float, seconds: float) -> dict:
+    """Roofline object for the exact-f32 CUDA-core GEMM: against the nominal FP32 FMA rate
+    (SMs x 128 lanes x 2 FLOP x the maximum SM clock), there being no measured figure."""
+    from ferrite import platform
+
+    sms = platform.sm_count()
+    mhz = 1965.0
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            mhz = float(json.load(f).get("sm_max_mhz", mhz))
+    except (OSError, ValueError):
+        pass
+    peak = sms * 128 * 2 * mhz * 1e6 / 1e12
+    achieved = flops / seconds / 1e12
+    return {"bound": "fp32", "kernel": kernel, "achieved": round(achieved, 2), "peak": round(peak, 1), "unit": "TFLOP/s",
+            "frac": round(achieved / peak, 4), "peak_source": f"nominal FP32 FMA rate ({sms} SMs x 128 lanes x 2 x {mhz:.0f} MHz)",
+            "traffic": None}
+
+
 def _oracle_pool(workers: int):
     """A process pool for the CPU oracle: spawned (never forked from a process that
     holds a CUDA context) with single-threaded BLAS in every worker, so ``workers``
@@ -638,6 +657,7 @@ class GemmF32Workload(GemmWorkload):
     name = "matmul_f32_2048cubed_highest_fwd_and_vjp"
     metric = "matmul f32 2048^3 HIGHEST fwd+2bwd TFLOP/s"
     dtype = "f32"
+    bound = "fp32"  # CUDA-core FMA rate, not the tensor cores
     M = N = K = 2048
     TORCH_DTYPE = torch.float32
     L2_NOTE = "operands 16 MiB each (inside L2)"
@@ -1106,7 +1126,7 @@ def measure(W, args, ws, rank, dev, shape, cpu_baseline):
     # burst tensor peak for a sub-second timed region, sustained for a longer one
     sustained = rl.Ceilings.from_platform().for_region(ms / 1e3)
     work = wl.kernel_work[dom]
-    point = rl.analyze(dom, flops=work if wl.bound == "tensor" else 0.0, bytes_=work if wl.bound == "hbm" else 0.0,
+    point = rl.analyze(dom, flops=work if wl.bound != "hbm" else 0.0, bytes_=work if wl.bound == "hbm" else 0.0,
                        seconds=bd[dom] / 1e3, sustained=sustained)
     out = {
         "metric": wl.metric,
@@ -1123,7 +1143,7 @@ def measure(W, args, ws, rank, dev, shape, cpu_baseline):
         "data": "synthetic",
         "config": wl.config(),
         "roofline": {
-            **point.line(traffic=_load_traffic(dom)),
+            **(point.line(traffic=_load_traffic(dom)) if wl.bound != "fp32" else _fp32_line(dom, work, bd[dom] / 1e3)),
             "timing": "kernel times from a second pass of the same K steps with CUDA events between kernels",
             "kernels_ms": {k: round(v, 5) for k, v in bd.items()},
         },
