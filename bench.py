@@ -685,6 +685,8 @@ class GptWorkload:
         from ferrite.model.train import TrainConfig, build_train_step, make_optimizer
 
         self.dev, self.ws, self.rank = dev, ws, rank
+        if shape:  # "global_batch": e.g. one GPU at the per-rank batch of a dp run
+            self.GLOBAL_BATCH = int(shape[0])
         self.cfg = GPTConfig(**GPT_CFG, attention="pallas", norm="pallas", linear="pallas", dtype=torch.bfloat16)
         self.tcfg = TrainConfig(steps=1000, batch=self.GLOBAL_BATCH, lr=6e-4, warmup=20)
         if self.GLOBAL_BATCH % ws:
@@ -1206,7 +1208,7 @@ def main(argv=None):
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-other-configs", action="store_true", help="default workload only (no sub-lines for the other configs)")
-    ap.add_argument("--shape", default=None, help="smaller case for profiling captures: norm rows,dim | attn b,h,s,d | gemm m,n,k | decode layers,b,h,max_len,d")
+    ap.add_argument("--shape", default=None, help="smaller case for profiling captures: norm rows,dim | attn b,h,s,d | gemm m,n,k | gpt global_batch | decode layers,b,h,max_len,d")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)  # timing rule: at least 3 untimed warm-up steps
     ws, rank, local = _dist_env()
