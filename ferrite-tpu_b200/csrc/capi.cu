@@ -102,6 +102,49 @@ cudaError_t launch_k(const void* func, dim3 grid, dim3 block, size_t smem, cudaS
   return cudaLaunchKernelExC(&cfg, func, args);
 }
 
+cudaError_t launch_k_cluster(const void* func, dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                             void** args, unsigned cluster_x) {
+  static const bool pdl = [] {
+    const char* e = std::getenv("FERRITE_PDL");
+    return !(e && *e && std::atoi(e) == 0);
+  }();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster_x;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  return cudaLaunchKernelExC(&cfg, func, args);
+}
+
+int max_active_clusters(const void* func, dim3 block, size_t smem, unsigned cluster_x) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(cluster_x, 1, 1);
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster_x;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, func, &cfg) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
 static int load_encoder() {
   std::lock_guard<std::mutex> lock(g_mu);
   if (g_encode_tiled) return FERRITE_OK;

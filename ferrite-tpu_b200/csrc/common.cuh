@@ -44,6 +44,25 @@ int check_launch(const char* what);
 cudaError_t launch_k(const void* func, dim3 grid, dim3 block, size_t smem, cudaStream_t s,
                      void** args);
 
+// The same with thread-block clusters of `cluster_x` CTAs along x (the grid's x a
+// multiple of it).
+cudaError_t launch_k_cluster(const void* func, dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                             void** args, unsigned cluster_x);
+// Clusters of `cluster_x` CTAs of `func` that fit on the device at once (0 on error).
+int max_active_clusters(const void* func, dim3 block, size_t smem, unsigned cluster_x);
+
+template <typename... KP>
+inline cudaError_t launch_cluster_impl(void (*kern)(KP...), dim3 grid, dim3 block, size_t smem,
+                                       cudaStream_t s, unsigned cluster_x, KP... v) {
+  void* ptrs[sizeof...(KP) > 0 ? sizeof...(KP) : 1] = {(void*)&v...};
+  return launch_k_cluster((const void*)kern, grid, block, smem, s, ptrs, cluster_x);
+}
+template <typename... KP, typename... A>
+inline cudaError_t launch_pdl_cluster(void (*kern)(KP...), dim3 grid, dim3 block, size_t smem,
+                                      cudaStream_t s, unsigned cluster_x, A&&... a) {
+  return launch_cluster_impl<KP...>(kern, grid, block, smem, s, cluster_x, static_cast<KP>(a)...);
+}
+
 template <typename... KP>
 inline cudaError_t launch_pdl_impl(void (*kern)(KP...), dim3 grid, dim3 block, size_t smem,
                                    cudaStream_t s, KP... v) {

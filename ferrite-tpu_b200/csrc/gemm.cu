@@ -266,6 +266,49 @@ __device__ __forceinline__ void tile_coords(int t, const Params& p, int& mb, int
   nb = r / gm;
 }
 
+// One epilogue warp's share of one accumulator tile: TMEM lanes q*32 .. q*32+31
+// (output rows row0 + q*32 + lane) and half `half` of the BN columns, read 32
+// columns at a time from `tbase` (this warp's lane quarter, the tile's buffer) and
+// written as f32 split-K partials, through the TMA staging slots (16-bit C, with
+// the fused activation epilogues) or with direct row stores.
+template <int BN, typename TC, int EPI>
+__device__ __forceinline__ void epilogue_tile(const Params& p, uint8_t* stg, const CUtensorMap* tma_c,
+                                              const CUtensorMap* tma_aux, uint32_t tbase, int row0, int nb,
+                                              int split, int ew, int lane, int q, int half, bool vec_ok,
+                                              bool ws_vec_ok, int& stg_count) {
+  TC* c = reinterpret_cast<TC*>(p.c);
+  const int row = row0 + q * 32 + lane;
+#pragma unroll 1
+  for (int cc = half * (BN / 64); cc < (half + 1) * (BN / 64); ++cc) {
+    uint32_t r[32];
+    tmem_ld32(tbase + cc * 32, r);
+    tmem_wait_ld();
+    if (p.splits > 1) {
+      store_row32<float>(p.ws + (int64_t)split * p.m * p.n, p.n, row, nb * BN + cc * 32, p.m, p.n, r,
+                         ws_vec_ok);
+    } else if constexpr (sizeof(TC) == 2) {
+      if (p.tma_store) {
+        // this warp's 32 rows x 32 columns through a staging slot and one TMA
+        // store (the unit clips rows / columns past M / N)
+        const int x = nb * BN + cc * 32, y = row0 + q * 32;
+        if constexpr (EPI == kEpiGeluBwd) epilogue_gelu_bwd_vals<TC>(p, row, x, r);
+        stage_store_32x32<TC>(stg, ew, stg_count++, lane, r, tma_c, x, y);
+        if constexpr (EPI == kEpiGelu) {
+          uint32_t a[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            a[j] = __float_as_uint(gelu_tanh_f(DT<TC>::to_f(DT<TC>::from_f(__uint_as_float(r[j])))));
+          stage_store_32x32<TC>(stg, ew, stg_count++, lane, a, tma_aux, x, y);
+        }
+      } else {
+        epilogue_row32<TC, EPI>(p, c, row, nb * BN + cc * 32, r, vec_ok);
+      }
+    } else {
+      epilogue_row32<TC, EPI>(p, c, row, nb * BN + cc * 32, r, vec_ok);
+    }
+  }
+}
+
 // A_MN: A stored [K][M] (MN-major); B_MN: B stored [K][N] (MN-major).
 template <int BN, bool A_MN, bool B_MN, bool BF16, typename TC, int EPI = kEpiNone>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -401,9 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int half = (warp - 2) >> 2;  // which half of the tile's columns
-    const int row_in_tile = q * 32 + lane;
-    TC* c = reinterpret_cast<TC*>(p.c);
-    const bool vec_ok = ((reinterpret_cast<uintptr_t>(c) & 15u) == 0) &&
+    const bool vec_ok = ((reinterpret_cast<uintptr_t>(p.c) & 15u) == 0) &&
                         ((p.ldc * (int64_t)sizeof(TC)) % 16 == 0);
     // partial slices are [m][n] f32 blocks of a 256-byte aligned workspace
     const bool ws_vec_ok = (p.n % 4 == 0);
@@ -418,36 +459,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&acc_full[buf], aph, abort, 4)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
-      const int row = mb * BM + row_in_tile;
-#pragma unroll 1
-      for (int cc = half * (BN / 64); cc < (half + 1) * (BN / 64); ++cc) {
-        uint32_t r[32];
-        tmem_ld32(tbase + cc * 32, r);
-        tmem_wait_ld();
-        if (p.splits > 1) {
-          store_row32<float>(p.ws + (int64_t)split * p.m * p.n, p.n, row, nb * BN + cc * 32, p.m,
-                             p.n, r, ws_vec_ok);
-        } else if constexpr (sizeof(TC) == 2) {
-          if (p.tma_store) {
-            // this warp's 32 rows x 32 columns through a staging slot and one TMA
-            // store (the unit clips rows / columns past M / N)
-            const int x = nb * BN + cc * 32, y = mb * BM + q * 32;
-            if constexpr (EPI == kEpiGeluBwd) epilogue_gelu_bwd_vals<TC>(p, row, x, r);
-            stage_store_32x32<TC>(smem + S::kStgOff, warp - 2, stg_count++, lane, r, &tma_c, x, y);
-            if constexpr (EPI == kEpiGelu) {
-              uint32_t a[32];
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                a[j] = __float_as_uint(gelu_tanh_f(DT<TC>::to_f(DT<TC>::from_f(__uint_as_float(r[j])))));
-              stage_store_32x32<TC>(smem + S::kStgOff, warp - 2, stg_count++, lane, a, &tma_aux, x, y);
-            }
-          } else {
-            epilogue_row32<TC, EPI>(p, c, row, nb * BN + cc * 32, r, vec_ok);
-          }
-        } else {
-          epilogue_row32<TC, EPI>(p, c, row, nb * BN + cc * 32, r, vec_ok);
-        }
-      }
+      epilogue_tile<BN, TC, EPI>(p, smem + S::kStgOff, &tma_c, &tma_aux, tbase, mb * BM, nb, split, warp - 2,
+                                 lane, q, half, vec_ok, ws_vec_ok, stg_count);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
@@ -460,6 +473,214 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// CTA-pair variant (unsplit K): a cluster of two CTAs on two SMs computes one
+// 256 x BN output tile with tcgen05.mma.cta_group::2 (M = 256).  Each CTA stages
+// its own 128 rows of A and its own BN/2 columns of B, so per SM a 128 x BN x 64
+// block of MMA work reads 16 KiB of A and BN*64 bytes of B from shared memory
+// (and from L2) instead of 16 KiB + BN*128 bytes: B's shared-memory and L2
+// traffic per FLOP halves, and the smaller stage leaves room for more stages.
+//   * both CTAs' warp 0 issue TMA loads (no multicast) into their own shared
+//     memory at the same offsets; the loads complete on the leader's (rank 0)
+//     "full" barrier, which expects the bytes of both CTAs;
+//   * the leader's warp 1 issues the pair MMAs; each MMA reads both CTAs'
+//     operand halves and writes rows 0-127 of the accumulator into the leader's
+//     TMEM and rows 128-255 into the peer's; its commits arrive on the "empty"
+//     and "accumulator full" barriers of both CTAs;
+//   * each CTA's epilogue drains its own TMEM rows and arrives on the leader's
+//     "accumulator empty" barrier (16 arrivals: 8 warps per CTA);
+//   * TMEM is allocated and freed by warp 1 of both CTAs together
+//     (cta_group::2); the clusters synchronise after set-up and before
+//     teardown, and each producer waits for the last release of every stage
+//     before its CTA may leave, so no arrival targets a CTA that has exited.
+// Every wait is bounded (kWaitLimitNs); an expired wait raises this CTA's abort
+// flag, and the peer's waits expire within the same bound.
+template <int BN>
+struct Smem2 {
+  static constexpr int kStages = BN == 256 ? 6 : 8;
+  static constexpr int kABytes = BM * BK * 2;         // this CTA's 128 rows of A: 16 KiB
+  static constexpr int kBBytes = (BN / 2) * BK * 2;   // this CTA's BN/2 columns of B
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTileBytes = kStages * kStageBytes;
+  static constexpr int kSlotBytes = 32 * 32 * 2;
+  static constexpr int kStgOff = kTileBytes;
+  static constexpr int kStgBytes = kEpiWarps * 2 * kSlotBytes;
+  static constexpr int kBarOff = kStgOff + kStgBytes;
+  static constexpr int kBarBytes = (2 * kStages + 4) * 8 + 16;
+  static constexpr int kTotal = 1024 + kBarOff + kBarBytes;
+  static_assert(kTotal <= 227 * 1024, "shared memory per CTA");
+};
+
+template <int BN, bool A_MN, bool B_MN, bool BF16, typename TC, int EPI = kEpiNone>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tma_a,
+                    const __grid_constant__ CUtensorMap tma_b,
+                    const __grid_constant__ CUtensorMap tma_c,
+                    const __grid_constant__ CUtensorMap tma_aux, const Params p) {
+  using S = Smem2<BN>;
+  constexpr int STAGES = S::kStages;
+  constexpr int BM2 = 2 * BM;  // rows of a pair tile
+  extern __shared__ uint8_t smem_raw[];
+  // Same kernel, same shared-memory size: the aligned base (and so every stage)
+  // sits at the same offset in both CTAs, as the pair MMA requires.
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* tiles = smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOff);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0: the leader, which issues the MMAs
+  const int pair = (int)(blockIdx.x >> 1);
+  const int num_pairs = (int)(gridDim.x >> 1);
+  const int num_units = p.tiles_m * p.tiles_n;  // pair tiles of 256 x BN
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);   // the leader's expect_tx arrival (+ both CTAs' bytes)
+      mbar_init(&empty[s], 1);  // the leader's MMA commit
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 2 * kEpiWarps);  // every epilogue warp of both CTAs
+    }
+    *abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tma_a);
+    tma_prefetch_desc(&tma_b);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, 2 * BN);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers initialised and TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_launch_dependents();
+  pdl_wait();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      const uint32_t full_leader = mapa_shared(full, 0);
+      int it = 0;
+      bool ok = true;
+      for (int u = pair; u < num_units && ok; u += num_pairs) {
+        int mb, nb;
+        tile_coords(u, p, mb, nb);
+        const int row = mb * BM2 + (int)rank * BM;         // this CTA's rows of A
+        const int col = nb * BN + (int)rank * (BN / 2);    // this CTA's columns of B
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, abort, 1)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = tiles + s * S::kStageBytes;
+          uint8_t* sb = sa + S::kABytes;
+          const uint32_t fb = full_leader + s * 8;
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * S::kStageBytes);
+          if constexpr (A_MN) {
+            tma_load_2d_pair(sa, &tma_a, fb, row, kb * BK);
+            tma_load_2d_pair(sa + 8192, &tma_a, fb, row + 64, kb * BK);
+          } else {
+            tma_load_2d_pair(sa, &tma_a, fb, kb * BK, row);
+          }
+          if constexpr (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 128; ++j)
+              tma_load_2d_pair(sb + j * 8192, &tma_b, fb, col + j * 64, kb * BK);
+          } else {
+            tma_load_2d_pair(sb, &tma_b, fb, kb * BK, col);
+          }
+        }
+      }
+      // Tail: the release of every stage's last use (the leader's commit, which
+      // arrives on this CTA's barrier) has landed before this CTA may leave.
+      for (int j = it; ok && j < it + STAGES; ++j)
+        if (j >= STAGES && !mbar_wait(&empty[j % STAGES], ((j / STAGES) & 1) ^ 1, abort, 5)) ok = false;
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader)
+    if (rank == 0 && lane == 0) {
+      constexpr uint32_t idesc = make_idesc_f16(BM2, BN, BF16, A_MN, B_MN);
+      int it = 0, local = 0;
+      bool ok = true;
+      const uint32_t s0 = smem_u32(tiles);
+      const uint64_t da_base = A_MN ? make_sdesc(s0, 8192, 1024) : make_sdesc(s0, 16, 1024);
+      const uint64_t db_base = B_MN ? make_sdesc(s0 + S::kABytes, 8192, 1024)
+                                    : make_sdesc(s0 + S::kABytes, 16, 1024);
+      for (int u = pair; u < num_units && ok; u += num_pairs, ++local) {
+        const int buf = local & 1;
+        const uint32_t aph = (local >> 1) & 1;
+        if (!mbar_wait(&acc_empty[buf], aph ^ 1, abort, 2)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, abort, 3)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = sdesc_at(da_base, s * S::kStageBytes);
+          const uint64_t db = sdesc_at(db_base, s * S::kStageBytes);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            tc_mma_pair_ss(d_tmem, sdesc_at(da, A_MN ? kk * 2048 : kk * 32),
+                           sdesc_at(db, B_MN ? kk * 2048 : kk * 32), idesc,
+                           (kb != 0 || kk != 0) ? 1u : 0u);
+          tc_commit_pair(&empty[s], 0x3);  // both CTAs' slots free once these MMAs retire
+        }
+        if (ok) tc_commit_pair(&acc_full[buf], 0x3);  // both accumulator halves ready
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const bool vec_ok = ((reinterpret_cast<uintptr_t>(p.c) & 15u) == 0) &&
+                        ((p.ldc * (int64_t)sizeof(TC)) % 16 == 0);
+    const uint32_t acc_empty_leader = mapa_shared(acc_empty, 0);
+    int stg_count = 0;
+    int local = 0;
+    for (int u = pair; u < num_units; u += num_pairs, ++local) {
+      int mb, nb;
+      tile_coords(u, p, mb, nb);
+      const int buf = local & 1;
+      const uint32_t aph = (local >> 1) & 1;
+      if (!mbar_wait(&acc_full[buf], aph, abort, 4)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
+      epilogue_tile<BN, TC, EPI>(p, smem + S::kStgOff, &tma_c, &tma_aux, tbase, mb * BM2 + (int)rank * BM, nb,
+                                 0, warp - 2, lane, q, half, vec_ok, false, stg_count);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc_empty_leader + buf * 8);
+    }
+    if (lane == 0) bulk_wait_group0();
+  }
+
+  // ------------------------------------------------------------ teardown
+  tc_fence_before();
+  __syncwarp();        // the warp reconverges before the aligned cluster barrier
+  cluster_sync_all();  // both CTAs done with TMEM, shared memory and each other's barriers
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, 2 * BN);
   }
 }
 
@@ -625,35 +846,62 @@ static int launch_simt(cudaStream_t s, const void* a, const void* b, void* c, in
   return check_launch("gemm_simt");
 }
 
-template <int BN, bool A_MN, bool B_MN, bool BF16, typename TC, int EPI = kEpiNone>
-static int launch_tc(cudaStream_t s, const CUtensorMap& ta, const CUtensorMap& tb,
-                     const CUtensorMap& tc, const CUtensorMap& taux, const Params& p, int grid) {
-  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, BF16, TC, EPI>;
-  const int smem = Smem<BN>::kTotal;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess)
-    return fail(FERRITE_LAUNCH_FAILED, "gemm: smem attribute: %s", cudaGetErrorString(e));
-  (void)launch_pdl(kern, dim3(grid), dim3(kThreads), smem, s, ta, tb, tc, taux, p);
-  return check_launch("gemm_tc");
+// Clusters of two gemm_tc2_kernel CTAs resident at once on `dev` (cached per
+// kernel instance and device; every instance has the same footprint).
+static int pair_slots(const void* kern, int dev, int sms) {
+  static int cache[64] = {0};
+  if (dev < 0 || dev >= 64) return sms / 2;
+  if (cache[dev] == 0) {
+    const int n = max_active_clusters(kern, dim3(kThreads), Smem2<256>::kTotal, 2);
+    cache[dev] = n > 0 ? n : sms / 2;
+  }
+  return cache[dev];
 }
 
-template <int BN, bool BF16, typename TC>
+// PAIR: the CTA-pair kernel (grid: two CTAs per cluster, at most the clusters
+// that fit at once); else the one-CTA kernel (grid: min(units, SMs)).
+template <bool PAIR, int BN, bool A_MN, bool B_MN, bool BF16, typename TC, int EPI = kEpiNone>
+static int launch_tc(cudaStream_t s, const CUtensorMap& ta, const CUtensorMap& tb,
+                     const CUtensorMap& tc, const CUtensorMap& taux, const Params& p, int units, int sms) {
+  if constexpr (PAIR) {
+    auto kern = gemm_tc2_kernel<BN, A_MN, B_MN, BF16, TC, EPI>;
+    const int smem = Smem2<BN>::kTotal;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess)
+      return fail(FERRITE_LAUNCH_FAILED, "gemm: smem attribute: %s", cudaGetErrorString(e));
+    const int clusters = std::min(units, pair_slots((const void*)kern, current_device(), sms));
+    (void)launch_pdl_cluster(kern, dim3(2 * clusters), dim3(kThreads), smem, s, 2u, ta, tb, tc, taux, p);
+    return check_launch("gemm_tc2");
+  } else {
+    auto kern = gemm_tc_kernel<BN, A_MN, B_MN, BF16, TC, EPI>;
+    const int smem = Smem<BN>::kTotal;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess)
+      return fail(FERRITE_LAUNCH_FAILED, "gemm: smem attribute: %s", cudaGetErrorString(e));
+    (void)launch_pdl(kern, dim3(std::min(units, sms)), dim3(kThreads), smem, s, ta, tb, tc, taux, p);
+    return check_launch("gemm_tc");
+  }
+}
+
+template <bool PAIR, int BN, bool BF16, typename TC>
 static int dispatch_major(cudaStream_t s, bool a_mn, bool b_mn, const CUtensorMap& ta,
                           const CUtensorMap& tb, const CUtensorMap& tc, const CUtensorMap& taux,
-                          const Params& p, int grid, int epi) {
+                          const Params& p, int units, int sms, int epi) {
   if constexpr (BF16 && std::is_same<TC, __nv_bfloat16>::value) {
     // the GPT MLP's fused epilogues: up-projection (A K-major, B MN-major) and
     // dA = dP W2^T (both K-major)
-    if (epi == kEpiGelu && !a_mn && b_mn) return launch_tc<BN, false, true, true, TC, kEpiGelu>(s, ta, tb, tc, taux, p, grid);
-    if (epi == kEpiGeluBwd && !a_mn && !b_mn) return launch_tc<BN, false, false, true, TC, kEpiGeluBwd>(s, ta, tb, tc, taux, p, grid);
+    if (epi == kEpiGelu && !a_mn && b_mn)
+      return launch_tc<PAIR, BN, false, true, true, TC, kEpiGelu>(s, ta, tb, tc, taux, p, units, sms);
+    if (epi == kEpiGeluBwd && !a_mn && !b_mn)
+      return launch_tc<PAIR, BN, false, false, true, TC, kEpiGeluBwd>(s, ta, tb, tc, taux, p, units, sms);
   }
   if (epi != kEpiNone)
     return fail(FERRITE_UNSUPPORTED_DTYPE, "gemm: epilogue %d needs bf16 operands and output with %s", epi,
                 epi == kEpiGelu ? "A K-major, B [K][N]" : "A K-major, B [N][K] (trans_b)");
-  if (!a_mn && !b_mn) return launch_tc<BN, false, false, BF16, TC>(s, ta, tb, tc, taux, p, grid);
-  if (!a_mn && b_mn) return launch_tc<BN, false, true, BF16, TC>(s, ta, tb, tc, taux, p, grid);
-  if (a_mn && !b_mn) return launch_tc<BN, true, false, BF16, TC>(s, ta, tb, tc, taux, p, grid);
-  return launch_tc<BN, true, true, BF16, TC>(s, ta, tb, tc, taux, p, grid);
+  if (!a_mn && !b_mn) return launch_tc<PAIR, BN, false, false, BF16, TC>(s, ta, tb, tc, taux, p, units, sms);
+  if (!a_mn && b_mn) return launch_tc<PAIR, BN, false, true, BF16, TC>(s, ta, tb, tc, taux, p, units, sms);
+  if (a_mn && !b_mn) return launch_tc<PAIR, BN, true, false, BF16, TC>(s, ta, tb, tc, taux, p, units, sms);
+  return launch_tc<PAIR, BN, true, true, BF16, TC>(s, ta, tb, tc, taux, p, units, sms);
 }
 
 // Tile width and K split.  Cost model in units of one 128x256x64 MMA block on
@@ -726,6 +974,9 @@ static int run_tc(cudaStream_t s, const void* a, const void* b, void* c, int64_t
     pl = plan_tc(m, n, k, sms, false);  // not enough scratch: no split
   }
   const int BN = pl.bn;
+  // 256 x 256 tiles on CTA pairs for unsplit plans with 256-wide tiles
+  // (FERRITE_GEMM_PAIR=0: one-CTA tiles only)
+  const bool pair = pl.splits == 1 && BN == 256 && m >= 2 * BM && env_int("FERRITE_GEMM_PAIR", 1) != 0;
 
   const CUtensorMapDataType dt = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap ta, tb;
@@ -744,7 +995,7 @@ static int run_tc(cudaStream_t s, const void* a, const void* b, void* c, int64_t
                       CU_TENSOR_MAP_SWIZZLE_128B);
   else
     rc = make_tmap_2d(&tb, b, dt, 2, (uint64_t)k, (uint64_t)n, (uint64_t)ldb * 2, 64,
-                      (uint32_t)BN, CU_TENSOR_MAP_SWIZZLE_128B);
+                      (uint32_t)(pair ? BN / 2 : BN), CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
 
   Params p;
@@ -753,7 +1004,8 @@ static int run_tc(cudaStream_t s, const void* a, const void* b, void* c, int64_t
   p.k = (int)k;
   p.ldc = ldc;
   p.c = c;
-  p.tiles_m = (int)((m + BM - 1) / BM);
+  const int64_t tile_rows = pair ? 2 * BM : BM;
+  p.tiles_m = (int)((m + tile_rows - 1) / tile_rows);
   p.tiles_n = (int)((n + BN - 1) / BN);
   p.k_blocks = (int)((k + BK - 1) / BK);
   p.group_m = std::max(1, std::min(env_int("FERRITE_GEMM_GROUP_M", 16), p.tiles_m));
@@ -763,7 +1015,6 @@ static int run_tc(cudaStream_t s, const void* a, const void* b, void* c, int64_t
   p.aux = aux;
   p.ld_aux = ld_aux;
   const int units = p.tiles_m * p.tiles_n * p.splits;
-  const int grid = std::min(units, sms);
   // 16-bit C (and the GELU epilogue's aux output) through TMA stores: 32 x 32
   // boxes, 64-byte swizzle; a layout TMA cannot describe keeps direct stores
   CUtensorMap tc = ta, taux = ta;  // placeholders when unused (never dereferenced)
@@ -780,8 +1031,9 @@ static int run_tc(cudaStream_t s, const void* a, const void* b, void* c, int64_t
                                          CU_TENSOR_MAP_SWIZZLE_64B) == FERRITE_OK))
       p.tma_store = 1;
   }
-  rc = BN == 256 ? dispatch_major<256, BF16, TC>(s, a_mn, b_mn, ta, tb, tc, taux, p, grid, epi)
-                 : dispatch_major<128, BF16, TC>(s, a_mn, b_mn, ta, tb, tc, taux, p, grid, epi);
+  rc = pair        ? dispatch_major<true, 256, BF16, TC>(s, a_mn, b_mn, ta, tb, tc, taux, p, units, sms, epi)
+       : BN == 256 ? dispatch_major<false, 256, BF16, TC>(s, a_mn, b_mn, ta, tb, tc, taux, p, units, sms, epi)
+                   : dispatch_major<false, 128, BF16, TC>(s, a_mn, b_mn, ta, tb, tc, taux, p, units, sms, epi);
   if (rc || pl.splits == 1) return rc;
   return launch_reduce<TC>(s, p.ws, c, m, n, ldc, pl.splits, sms);
 }
