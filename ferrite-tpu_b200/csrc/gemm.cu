@@ -477,7 +477,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
-// CTA-pair variant (unsplit K): a cluster of two CTAs on two SMs computes one
+// CTA-pair variant: a cluster of two CTAs on two SMs computes one
 // 256 x BN output tile with tcgen05.mma.cta_group::2 (M = 256).  Each CTA stages
 // its own 128 rows of A and its own BN/2 columns of B, so per SM a 128 x BN x 64
 // block of MMA work reads 16 KiB of A and BN*64 bytes of B from shared memory
@@ -541,7 +541,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t rank = cluster_ctarank();  // 0: the leader, which issues the MMAs
   const int pair = (int)(blockIdx.x >> 1);
   const int num_pairs = (int)(gridDim.x >> 1);
-  const int num_units = p.tiles_m * p.tiles_n;  // pair tiles of 256 x BN
+  const int num_tiles = p.tiles_m * p.tiles_n;  // pair tiles of 256 x BN
+  // Work unit u: tile u % num_tiles, K slice u / num_tiles (as in the one-CTA kernel).
+  const int num_units = num_tiles * p.splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -578,10 +580,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int u = pair; u < num_units && ok; u += num_pairs) {
         int mb, nb;
-        tile_coords(u, p, mb, nb);
+        tile_coords(u % num_tiles, p, mb, nb);
         const int row = mb * BM2 + (int)rank * BM;         // this CTA's rows of A
         const int col = nb * BN + (int)rank * (BN / 2);    // this CTA's columns of B
-        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+        const int kb0 = (u / num_tiles) * p.kb_per_split;
+        const int kb1 = min(kb0 + p.kb_per_split, p.k_blocks);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, abort, 1)) {
@@ -628,7 +632,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&acc_empty[buf], aph ^ 1, abort, 2)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
-        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+        const int kb0 = (u / num_tiles) * p.kb_per_split;
+        const int kb1 = min(kb0 + p.kb_per_split, p.k_blocks);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(&full[s], ph, abort, 3)) {
@@ -642,7 +648,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int kk = 0; kk < BK / 16; ++kk)
             tc_mma_pair_ss(d_tmem, sdesc_at(da, A_MN ? kk * 2048 : kk * 32),
                            sdesc_at(db, B_MN ? kk * 2048 : kk * 32), idesc,
-                           (kb != 0 || kk != 0) ? 1u : 0u);
+                           (kb != kb0 || kk != 0) ? 1u : 0u);
           tc_commit_pair(&empty[s], 0x3);  // both CTAs' slots free once these MMAs retire
         }
         if (ok) tc_commit_pair(&acc_full[buf], 0x3);  // both accumulator halves ready
@@ -654,19 +660,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int half = (warp - 2) >> 2;
     const bool vec_ok = ((reinterpret_cast<uintptr_t>(p.c) & 15u) == 0) &&
                         ((p.ldc * (int64_t)sizeof(TC)) % 16 == 0);
+    const bool ws_vec_ok = (p.n % 4 == 0);
     const uint32_t acc_empty_leader = mapa_shared(acc_empty, 0);
     int stg_count = 0;
     int local = 0;
     for (int u = pair; u < num_units; u += num_pairs, ++local) {
       int mb, nb;
-      tile_coords(u, p, mb, nb);
+      tile_coords(u % num_tiles, p, mb, nb);
       const int buf = local & 1;
       const uint32_t aph = (local >> 1) & 1;
       if (!mbar_wait(&acc_full[buf], aph, abort, 4)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
       epilogue_tile<BN, TC, EPI>(p, smem + S::kStgOff, &tma_c, &tma_aux, tbase, mb * BM2 + (int)rank * BM, nb,
-                                 0, warp - 2, lane, q, half, vec_ok, false, stg_count);
+                                 u / num_tiles, warp - 2, lane, q, half, vec_ok, ws_vec_ok, stg_count);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc_empty_leader + buf * 8);
@@ -847,12 +854,18 @@ static int launch_simt(cudaStream_t s, const void* a, const void* b, void* c, in
 }
 
 // Clusters of two gemm_tc2_kernel CTAs resident at once on `dev` (cached per
-// kernel instance and device; every instance has the same footprint).
-static int pair_slots(const void* kern, int dev, int sms) {
+// device; every instance has the same block size and shared memory, so one
+// representative instance answers for all).
+static int pair_slots(int dev, int sms) {
   static int cache[64] = {0};
   if (dev < 0 || dev >= 64) return sms / 2;
   if (cache[dev] == 0) {
-    const int n = max_active_clusters(kern, dim3(kThreads), Smem2<256>::kTotal, 2);
+    auto kern = gemm_tc2_kernel<256, false, false, true, __nv_bfloat16>;
+    int n = 0;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem2<256>::kTotal) == cudaSuccess)
+      n = max_active_clusters((const void*)kern, dim3(kThreads), Smem2<256>::kTotal, 2);
+    else
+      (void)cudaGetLastError();
     cache[dev] = n > 0 ? n : sms / 2;
   }
   return cache[dev];
@@ -869,7 +882,7 @@ static int launch_tc(cudaStream_t s, const CUtensorMap& ta, const CUtensorMap& t
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess)
       return fail(FERRITE_LAUNCH_FAILED, "gemm: smem attribute: %s", cudaGetErrorString(e));
-    const int clusters = std::min(units, pair_slots((const void*)kern, current_device(), sms));
+    const int clusters = std::min(units, pair_slots(current_device(), sms));
     (void)launch_pdl_cluster(kern, dim3(2 * clusters), dim3(kThreads), smem, s, 2u, ta, tb, tc, taux, p);
     return check_launch("gemm_tc2");
   } else {
@@ -904,47 +917,63 @@ static int dispatch_major(cudaStream_t s, bool a_mn, bool b_mn, const CUtensorMa
   return launch_tc<PAIR, BN, true, true, BF16, TC>(s, ta, tb, tc, taux, p, units, sms);
 }
 
-// Tile width and K split.  Cost model in units of one 128x256x64 MMA block on
+// Tile shape and K split.  Cost model in units of one 128x256x64 MMA block on
 // one SM: a 128-wide tile block costs 0.69 (half the FLOPs at ~72% of the
-// 256-wide rate, measured), waves are ceil(units / SMs), and a split adds the
-// f32 partial traffic (write + read of splits x M x N x 4 bytes, ~2.3 MB per
-// unit of time at HBM rate) plus the reduction launch.
+// 256-wide rate, measured) and a block of a CTA-pair tile 0.95 (the pair kernel
+// ran 5% faster than the one-CTA kernel on 8192^3); waves are ceil(units /
+// slots) with one slot per SM (one-CTA tiles) or per resident cluster of two
+// (pair tiles, 256 rows each); a split adds the f32 partial traffic (write +
+// read of splits x M x N x 4 bytes, ~2.3 MB per unit of time at HBM rate) plus
+// the reduction launch.
 struct Plan {
   int bn, splits, kb_per_split;
+  bool pair;
 };
 
-static Plan plan_tc(int64_t m, int64_t n, int64_t k, int sms, bool allow_split) {
+static Plan plan_tc(int64_t m, int64_t n, int64_t k, int sms, int pair_slots, bool allow_split) {
   const int64_t kb = (k + BK - 1) / BK;
-  const int64_t tm = (m + BM - 1) / BM;
-  Plan best{n < 256 ? 128 : 256, 1, (int)kb};
+  Plan best{n < 256 ? 128 : 256, 1, (int)kb, false};
   double best_cost = 1e300;
   const int max_splits = allow_split ? (int)std::min<int64_t>(16, kb / 4) : 1;
-  for (int bn : {256, 128}) {
-    if (bn == 256 && n < 256) continue;
-    const int64_t tiles = tm * ((n + bn - 1) / bn);
-    const double unit = bn == 256 ? 1.0 : 0.69;
+  const bool pair_ok = pair_slots > 0 && m >= 2 * BM && n >= 256 && env_int("FERRITE_GEMM_PAIR", 1) != 0;
+  struct Shape {
+    bool pair;
+    int bn;
+    double unit;
+  };
+  const Shape shapes[3] = {{true, 256, 0.95}, {false, 256, 1.0}, {false, 128, 0.69}};
+  for (const Shape& sh : shapes) {
+    if (sh.pair && !pair_ok) continue;
+    if (sh.bn == 256 && n < 256) continue;
+    const int64_t rows = sh.pair ? 2 * BM : BM;
+    const int64_t tiles = ((m + rows - 1) / rows) * ((n + sh.bn - 1) / sh.bn);
+    const int64_t slots = sh.pair ? pair_slots : sms;
     for (int sp = 1; sp <= std::max(1, max_splits); ++sp) {
       const int64_t kbs = (kb + sp - 1) / sp;
       const int64_t eff_splits = (kb + kbs - 1) / kbs;  // no empty slices
       if (eff_splits != sp) continue;
       const int64_t units = tiles * sp;
-      const double waves = (double)((units + sms - 1) / sms);
-      double cost = waves * (double)kbs * unit;
+      const double waves = (double)((units + slots - 1) / slots);
+      double cost = waves * (double)kbs * sh.unit;
       if (sp > 1) cost += 2.0 * sp * (double)m * (double)n * 4.0 / 2.3e6 + 13.0;
-      if (cost < best_cost * 0.97) {  // prefer fewer splits / wider tiles on near-ties
+      if (cost < best_cost * 0.97) {  // prefer the earlier shape / fewer splits on near-ties
         best_cost = cost;
-        best = Plan{bn, sp, (int)kbs};
+        best = Plan{sh.bn, sp, (int)kbs, sh.pair};
       }
     }
   }
   const int forced = env_int("FERRITE_GEMM_BN", 0);
-  if ((forced == 128 || forced == 256) && n >= forced) best.bn = forced;
+  if ((forced == 128 || forced == 256) && n >= forced) {
+    best.bn = forced;
+    if (forced == 128) best.pair = false;
+  }
   const int forced_split = env_int("FERRITE_GEMM_SPLITS", 0);
   if (allow_split && forced_split >= 1) {
     const int64_t kbs = (kb + forced_split - 1) / forced_split;
     best.splits = (int)((kb + kbs - 1) / kbs);
     best.kb_per_split = (int)kbs;
   }
+  if (env_int("FERRITE_GEMM_PAIR", -1) == 1 && pair_ok && best.bn == 256) best.pair = true;  // forced on
   return best;
 }
 
@@ -969,14 +998,13 @@ static int run_tc(cudaStream_t s, const void* a, const void* b, void* c, int64_t
                   void* aux = nullptr, int64_t ld_aux = 0) {
   const int dev = current_device();
   const int sms = num_sms(dev);
-  Plan pl = plan_tc(m, n, k, sms, workspace != nullptr && epi == kEpiNone);
+  const int pslots = pair_slots(dev, sms);
+  Plan pl = plan_tc(m, n, k, sms, pslots, workspace != nullptr && epi == kEpiNone);
   if (plan_workspace(pl, m, n) > ws_bytes || (reinterpret_cast<uintptr_t>(workspace) & 255u)) {
-    pl = plan_tc(m, n, k, sms, false);  // not enough scratch: no split
+    pl = plan_tc(m, n, k, sms, pslots, false);  // not enough scratch: no split
   }
   const int BN = pl.bn;
-  // 256 x 256 tiles on CTA pairs for unsplit plans with 256-wide tiles
-  // (FERRITE_GEMM_PAIR=0: one-CTA tiles only)
-  const bool pair = pl.splits == 1 && BN == 256 && m >= 2 * BM && env_int("FERRITE_GEMM_PAIR", 1) != 0;
+  const bool pair = pl.pair;  // 256 x 256 tiles on CTA pairs (FERRITE_GEMM_PAIR=0: never)
 
   const CUtensorMapDataType dt = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap ta, tb;
@@ -1066,7 +1094,9 @@ extern "C" size_t ferrite_gemm_workspace_size(int64_t m, int64_t n, int64_t k, i
   // Same eligibility rules as the launch, with aligned stand-in pointers.
   const void* aligned = reinterpret_cast<const void*>(uintptr_t(256));
   if (!tc_eligible(aligned, aligned, m, n, k, lda, ldb, trans_a, trans_b)) return 0;
-  return plan_workspace(plan_tc(m, n, k, num_sms(current_device()), true), m, n);
+  const int dev = current_device();
+  const int sms = num_sms(dev);
+  return plan_workspace(plan_tc(m, n, k, sms, pair_slots(dev, sms), true), m, n);
 }
 
 extern "C" int ferrite_gemm(void* stream, const void* a, const void* b, void* c, int64_t m,

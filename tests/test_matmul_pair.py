@@ -9,9 +9,10 @@ Cases: every transpose combination, ragged M (the last pair tile's second CTA
 entirely past M) and N, more pair tiles than resident clusters (several units
 per cluster), f32 and f16 outputs, the GPT MLP's fused GELU epilogues, and the
 reference's matmul sizes (src/ferrite/kernels/matmul.py:52-86 of
-anxnd2211/ferrite-tpu).  The calls go through ``ferrite_gemm`` (no split-K
-scratch) with 256-wide tiles forced (FERRITE_GEMM_BN=256), so every case runs
-unsplit on pairs; FERRITE_GEMM_PAIR=0 selects the one-CTA kernel.
+anxnd2211/ferrite-tpu).  The unsplit cases go through ``ferrite_gemm`` (no
+split-K scratch) and the split-K case through ``gemm`` with a forced split
+count; 256-wide tiles are forced (FERRITE_GEMM_BN=256) and FERRITE_GEMM_PAIR
+selects the pair (1) or the one-CTA (0) kernel.
 """
 
 import numpy as np
@@ -139,3 +140,25 @@ def test_gelu_epilogues(monkeypatch, t):
     torch.testing.assert_close(u.float(), _ref32(y, w1), atol=2e-2, rtol=1e-2)
     du, du1 = _both(monkeypatch, lambda: bwd(u))
     assert torch.equal(du, du1)
+
+
+@pytest.mark.parametrize("ta", [False, True])
+@pytest.mark.parametrize("splits", [2, 3])
+def test_pair_split_k_matches_one_cta(monkeypatch, ta, splits):
+    """Split-K on pairs (the weight gradients X^T G: few output tiles, long K): the
+    f32 partial slices and their ordered sum equal the one-CTA kernel's."""
+    from ferrite.kernels.matmul import gemm
+
+    g = torch.Generator(device="cuda").manual_seed(splits)
+    m, n, k = 768, 1024, 64 * 61
+    a = torch.randn((k, m) if ta else (m, k), device="cuda", generator=g).to(torch.bfloat16)
+    b = torch.randn(k, n, device="cuda", generator=g).to(torch.bfloat16)
+    monkeypatch.setenv("FERRITE_GEMM_SPLITS", str(splits))
+    for out_dtype in (torch.float32, torch.bfloat16):
+        got, one = _both(monkeypatch, lambda: gemm(a, b, trans_a=ta, out_dtype=out_dtype))
+        assert torch.equal(got, one)
+        ref = _ref32(a, b, ta)
+        if out_dtype == torch.float32:
+            torch.testing.assert_close(got, ref, atol=1e-3 * np.sqrt(k), rtol=1e-4)
+        else:
+            _bf16_close(got, ref, float(np.sqrt(k)))
