@@ -1036,7 +1036,13 @@ static int run_tc(cudaStream_t s, const void* a, const void* b, void* c, int64_t
   p.tiles_m = (int)((m + tile_rows - 1) / tile_rows);
   p.tiles_n = (int)((n + BN - 1) / BN);
   p.k_blocks = (int)((k + BK - 1) / BK);
-  p.group_m = std::max(1, std::min(env_int("FERRITE_GEMM_GROUP_M", 16), p.tiles_m));
+  // Raster group: the A rows of one group span about 32 MiB of bf16 over the whole K
+  // range (16 Mi elements), at most 16 tiles.  At 8192^3 that is 2048 rows: the group's
+  // A stays L2-resident while its units sweep N, and the kernel ran 3% faster (at a
+  // 3% higher clock under the power cap) than with 4096-row groups.
+  const int64_t group_rows = std::max<int64_t>(tile_rows, (int64_t(16) << 20) / std::max<int64_t>(k, 1));
+  const int gm_default = (int)std::min<int64_t>(16, std::max<int64_t>(1, group_rows / tile_rows));
+  p.group_m = std::max(1, std::min(env_int("FERRITE_GEMM_GROUP_M", gm_default), p.tiles_m));
   p.splits = pl.splits;
   p.kb_per_split = pl.kb_per_split;
   p.ws = pl.splits > 1 ? reinterpret_cast<float*>(workspace) : nullptr;
