@@ -2095,6 +2095,12 @@ __global__ void __launch_bounds__(fused_threads<EW>(), 1)
   constexpr int kStoreWarp = 2 + EW;
   constexpr int CW = 128 * 4 / EW;  // query columns per elementwise warp (64 or 32)
   constexpr int NG = EW / 4;        // elementwise warps per TMEM lane quadrant
+  // With 64 query columns a warp owns one whole 32-key x 64-query block of the dS^T
+  // staging tile: it stores the block itself (one TMA store) and, once that store has
+  // completed, arrives on st_done; the store warp then signals the tile to the dQ
+  // units.  No warp waits for the others' staging writes.  With 32 columns two warps
+  // share a block and the store warp stores the whole tile.
+  constexpr bool kWarpStores = CW == 64;
   typedef typename std::conditional<BF16, __nv_bfloat16, __half>::type T;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -2113,6 +2119,12 @@ __global__ void __launch_bounds__(fused_threads<EW>(), 1)
   uint64_t* p_half = s_full + 6;
   uint64_t* stg_full = s_full + 7;  // the eight elementwise warps wrote the dS^T staging tile
   uint64_t* stg_free = s_full + 8;  // the store warp's TMA stores have read it
+  // kWarpStores: every elementwise warp's store of tile t has completed, on st_done[t & 1].
+  // Two barriers alternate because arrivals carry no phase.  A warp arrives for tile t in
+  // iteration t + 1, after its dS of tile t + 1; the dP of tile t + 2 needs every warp's
+  // dS of tile t + 1, which each gives after finishing iteration t.  So a warp may arrive
+  // for tile t while a slower one has not arrived for t - 1, but never for t + 1.
+  uint64_t* st_done = stg_full;     // [2]: stg_full, stg_free (adjacent)
   // dQ unit barriers
   uint64_t* q_full = bars + L::kNumDkvBars;
   uint64_t* q_empty = q_full + QS;
@@ -2172,7 +2184,7 @@ __global__ void __launch_bounds__(fused_threads<EW>(), 1)
           mbar_init(ds_full, EW);
           mbar_init(acc_full, 1);
           mbar_init(stg_full, EW);
-          mbar_init(stg_free, 1);
+          mbar_init(stg_free, kWarpStores ? EW : 1);  // st_done[1] with per-warp stores
         } else {
           if (*s_inited & 2) {
             for (int i = 0; i < L::kNumDqBars; ++i) mbar_inval(&q_full[i]);
@@ -2313,7 +2325,12 @@ __global__ void __launch_bounds__(fused_threads<EW>(), 1)
         // lets the elementwise warps write the next tile while the stores drain to
         // L2; a tile's query tile is signalled once its stores have completed (one
         // tile later, so the wait is off every other warp's path).
-        if (lane == 0) {
+        if (kWarpStores && lane == 0) {
+          for (int i = 0; i < n_y; ++i) {
+            if (!mbar_wait(&st_done[i & 1], (i >> 1) & 1, abort, 55)) break;
+            fused_signal(fp, p.causal, sl, ytile(i));
+          }
+        } else if (lane == 0) {
           bool ok = true;
           int prev_qt = -1;
           const uint64_t keep = l2_policy_evict_last();  // read back soon by a dQ unit
@@ -2434,8 +2451,12 @@ __global__ void __launch_bounds__(fused_threads<EW>(), 1)
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(dp_free);
-          // the store warp's TMA stores of the previous tile have read the staging tile
-          if (i > 0 && !mbar_wait(stg_free, (i - 1) & 1, abort, 53)) {
+          if constexpr (kWarpStores) {
+            // this warp's own store of the previous tile has read its staging block
+            if (lane == 0) bulk_wait_group_read0();
+            __syncwarp();
+          } else if (i > 0 && !mbar_wait(stg_free, (i - 1) & 1, abort, 53)) {
+            // the store warp's TMA stores of the previous tile have read the staging tile
             ok = false;
             break;
           }
@@ -2466,9 +2487,33 @@ __global__ void __launch_bounds__(fused_threads<EW>(), 1)
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(ds_full);
-          fence_proxy_async_smem();  // the staging writes, before the store warp's TMA reads them
+          fence_proxy_async_smem();  // the staging writes, before the TMA store reads them
           __syncwarp();
-          if (lane == 0) mbar_arrive(stg_full);
+          if constexpr (kWarpStores) {
+            if (lane == 0) {
+              const int key = x0 + qw * 32;
+              // evict_last: dS^T is read back soon by a dQ unit
+              tma_store_4d_hint(&tds_st, stg, 0, key & 63, (y0 + CW * cq) >> 6, slot * nkb_all + (key >> 6),
+                                l2_policy_evict_last());
+              bulk_commit_group();
+              if (i > 0) {  // the previous tile's store has completed
+                bulk_wait_group1();
+                mbar_arrive(&st_done[(i - 1) & 1]);
+              }
+            }
+          } else if (lane == 0) {
+            mbar_arrive(stg_full);
+          }
+        }
+        if constexpr (kWarpStores) {
+          if (lane == 0) {
+            bulk_wait_group0();  // complete before the unit ends (the next unit reuses the smem)
+            // The last tile's arrival waits for the final dK commit, which needs every
+            // warp's last dS: all warps are then past their earlier arrivals, so this one
+            // cannot land in the phase of tile n_y - 3 (same barrier).
+            if (ok && n_y > 0 && mbar_wait(acc_full, 0, abort, 56)) mbar_arrive(&st_done[(n_y - 1) & 1]);
+          }
+          __syncwarp();
         }
         // epilogue: the first NG / 2 column groups store dK (x scale), the others dV,
         // D / (NG / 2) columns each
