@@ -1966,11 +1966,14 @@ __global__ void __launch_bounds__(kDqThreads, 1)
 
 constexpr int kFusedMaxDqStages = 6;
 // Warps: 0 TMA loads, 1 TMEM + MMA, 2 .. 2 + EW - 1 elementwise (dK/dV units) / dQ
-// epilogue (dQ units), then one warp of dS stores + signals.  EW = 8 (two warps per
-// TMEM lane quadrant, 64 query columns each; up to 168 registers a thread) or 16
-// (four per quadrant, 32 columns each; more warps per scheduler but 96 registers).
+// epilogue (dQ units), then one warp of dS stores + signals, then the scheduler warp,
+// which claims the CTA's next unit while the current one runs (at short sequences a
+// dK/dV unit is only a few tiles, and a claim is several gpu-scope atomics).  EW = 8
+// (two warps per TMEM lane quadrant, 64 query columns each; up to 168 registers a
+// thread) or 16 (four per quadrant, 32 columns each; more warps per scheduler but
+// ~100 registers).
 template <int EW>
-constexpr int fused_threads() { return 32 * (EW + 3); }
+constexpr int fused_threads() { return 32 * (EW + 4); }
 enum { kSchedNext = 0, kSchedHead = 1, kSchedTail = 2, kSchedAbort = 3, kSchedInts = 8 };
 
 struct FusedParams {
@@ -2000,7 +2003,8 @@ struct FusedSmem {
   static constexpr int kNumDkvBars = W::kNumBars + 2;  // + stg_full, stg_free
   static constexpr int kNumDqBars = 2 * kDqStages + 1;
   // barriers, then TMEM slot, local abort, unit, kind, set-initialised flags
-  static constexpr int kBarBytes = (kNumDkvBars + kNumDqBars) * 8 + 32;
+  // + TMEM slot and the CTA's scheduling words (32 bytes), per-warp store progress (32)
+  static constexpr int kBarBytes = (kNumDkvBars + kNumDqBars) * 8 + 64;
   static_assert(kBarBytes <= 512, "barrier block must fit the alignment slack rule");
   // Data at the first 1024-byte boundary; the barrier block in the slack before it
   // when that holds 512 bytes, else right after the data (slack < 512 then).
@@ -2023,7 +2027,7 @@ __device__ __forceinline__ int fused_producers(const FusedParams& fp, int causal
 // meanwhile.  A ticket of slice s waits only for the dQ units of slice
 // s - slots, which depend only on dK/dV tickets drawn before it, so the oldest
 // waiting ticket can always start: no cycle.
-__device__ int fused_claim(const FusedParams& fp, int& kind, int& pending) {
+__device__ __noinline__ int fused_claim(const FusedParams& fp, int& kind, int& pending) {
   int* s = fp.sched;
   const int n_dkv = fp.n_slices * fp.nkt;
   const int n_dq = fp.n_slices * (fp.nq / 2);
@@ -2097,9 +2101,10 @@ __global__ void __launch_bounds__(fused_threads<EW>(), 1)
   constexpr int NG = EW / 4;        // elementwise warps per TMEM lane quadrant
   // With 64 query columns a warp owns one whole 32-key x 64-query block of the dS^T
   // staging tile: it stores the block itself (one TMA store) and, once that store has
-  // completed, arrives on st_done; the store warp then signals the tile to the dQ
-  // units.  No warp waits for the others' staging writes.  With 32 columns two warps
-  // share a block and the store warp stores the whole tile.
+  // completed, publishes its progress; the store warp signals a tile to the dQ units
+  // when every warp's progress has passed it.  No warp waits for the others' staging
+  // writes.  With 32 columns two warps share a block and the store warp stores the
+  // whole tile.
   constexpr bool kWarpStores = CW == 64;
   typedef typename std::conditional<BF16, __nv_bfloat16, __half>::type T;
   extern __shared__ uint8_t smem_raw[];
@@ -2119,12 +2124,6 @@ __global__ void __launch_bounds__(fused_threads<EW>(), 1)
   uint64_t* p_half = s_full + 6;
   uint64_t* stg_full = s_full + 7;  // the eight elementwise warps wrote the dS^T staging tile
   uint64_t* stg_free = s_full + 8;  // the store warp's TMA stores have read it
-  // kWarpStores: every elementwise warp's store of tile t has completed, on st_done[t & 1].
-  // Two barriers alternate because arrivals carry no phase.  A warp arrives for tile t in
-  // iteration t + 1, after its dS of tile t + 1; the dP of tile t + 2 needs every warp's
-  // dS of tile t + 1, which each gives after finishing iteration t.  So a warp may arrive
-  // for tile t while a slower one has not arrived for t - 1, but never for t + 1.
-  uint64_t* st_done = stg_full;     // [2]: stg_full, stg_free (adjacent)
   // dQ unit barriers
   uint64_t* q_full = bars + L::kNumDkvBars;
   uint64_t* q_empty = q_full + QS;
@@ -2134,6 +2133,18 @@ __global__ void __launch_bounds__(fused_threads<EW>(), 1)
   volatile int* s_unit = abort + 1;
   volatile int* s_kind = abort + 2;
   volatile int* s_inited = abort + 3;  // bit 0: dK/dV set, bit 1: dQ set
+  volatile int* s_next = abort + 4;    // the scheduler warp's claim for the next unit
+  volatile int* s_next_kind = abort + 5;
+  // Work the current unit's MMA lane has not issued yet (query tiles of a dK/dV unit,
+  // key blocks of a dQ unit); 0 once it is done.  The scheduler claims the next unit
+  // when this drops to a few steps: early enough to hide the claim, late enough that
+  // a claimed unit does not sit idle in this CTA while other CTAs could run it.
+  volatile int* s_left = abort + 6;
+  // kWarpStores: tiles of the current dK/dV unit whose dS store has completed, per
+  // elementwise warp (monotonic counters: the store warp may fall any number of tiles
+  // behind without missing one, which an mbarrier phase could not guarantee)
+  int* s_prog = const_cast<int*>(abort + 7);
+  constexpr int kSchedWarp = 3 + EW;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int diag_shift = p.sk - p.sq;
@@ -2156,14 +2167,25 @@ __global__ void __launch_bounds__(fused_threads<EW>(), 1)
   const uint32_t t_dv = tmem + 256;
   const uint32_t t_dk = tmem + 256 + D;
 
-  int pending = -1;  // thread 0: a dK/dV ticket whose dS slot is not free yet
+  int pending = -1;  // scheduler lane: a dK/dV ticket whose dS slot is not free yet
+  // The scheduler warp's lane 0 makes every claim: the first one here, each next one
+  // as soon as the current unit has started.
+  auto claim_next = [&]() {
+    int kind = 0;
+    const int u = *abort ? -1 : fused_claim(fp, kind, pending);
+    *s_next = u;
+    *s_next_kind = kind;
+  };
+  if (warp == kSchedWarp && lane == 0) claim_next();
+  __syncthreads();
   while (true) {
-    // ---------------------------------------------------------------- claim
+    // ---------------------------------------------------------------- next unit
     if (threadIdx.x == 0) {
-      int kind = 0;
-      const int u = *abort ? -1 : fused_claim(fp, kind, pending);
+      const int kind = *s_next_kind;
+      const int u = *abort ? -1 : *s_next;
       *s_unit = u;
       *s_kind = kind;
+      *s_left = 0x7fffffff;
       if (u >= 0) {
         fence_proxy_async_global();  // TMA traffic of this unit after the acquire of its inputs / slot
         const int bit = kind ? 2 : 1;
@@ -2184,7 +2206,9 @@ __global__ void __launch_bounds__(fused_threads<EW>(), 1)
           mbar_init(ds_full, EW);
           mbar_init(acc_full, 1);
           mbar_init(stg_full, EW);
-          mbar_init(stg_free, kWarpStores ? EW : 1);  // st_done[1] with per-warp stores
+          mbar_init(stg_free, 1);
+          if constexpr (kWarpStores)
+            for (int w = 0; w < EW; ++w) s_prog[w] = 0;
         } else {
           if (*s_inited & 2) {
             for (int i = 0; i < L::kNumDqBars; ++i) mbar_inval(&q_full[i]);
@@ -2203,7 +2227,21 @@ __global__ void __launch_bounds__(fused_threads<EW>(), 1)
     const int unit = *s_unit;
     if (unit < 0) break;
 
-    if (*s_kind == 0) {
+    if (warp == kSchedWarp) {
+      if (lane == 0) {
+        const int thr = *s_kind == 0 ? 2 : 12;  // query tiles / key blocks still to issue
+        const uint64_t t0 = globaltimer_ns();
+        uint32_t spins = 0;
+        while (*s_left > thr && !*abort) {
+          __nanosleep(128);
+          if ((++spins & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+            report_timeout(65);
+            *abort = 1;
+          }
+        }
+        claim_next();  // read by thread 0 after the unit-end barrier
+      }
+    } else if (*s_kind == 0) {
       // ============================================================ dK/dV unit
       const int sl = unit / fp.nkt;
       const int ktile = unit - sl * fp.nkt;
@@ -2300,6 +2338,7 @@ __global__ void __launch_bounds__(fused_threads<EW>(), 1)
           }
           for (int i = 0; ok && i < n_y; ++i) {
             const bool more = i + 1 < n_y;
+            *s_left = n_y - i;
             if (!(ok = mbar_wait(p_half, i & 1, abort, 52))) break;
             tc_fence_after();
             issue_dv(i, 0);
@@ -2319,6 +2358,7 @@ __global__ void __launch_bounds__(fused_threads<EW>(), 1)
           tc_commit(acc_full);
           mbar_drain(acc_full, 0);
         }
+        if (lane == 0) *s_left = 0;
       } else if (warp == kStoreWarp) {
         // ------------------------------------------------ dS^T stores + signals
         // One TMA store per 32-key x 64-query staging block; the stg_free arrival
@@ -2326,8 +2366,21 @@ __global__ void __launch_bounds__(fused_threads<EW>(), 1)
         // L2; a tile's query tile is signalled once its stores have completed (one
         // tile later, so the wait is off every other warp's path).
         if (kWarpStores && lane == 0) {
-          for (int i = 0; i < n_y; ++i) {
-            if (!mbar_wait(&st_done[i & 1], (i >> 1) & 1, abort, 55)) break;
+          const uint64_t t0 = globaltimer_ns();
+          uint32_t spins = 0;
+          for (int i = 0; i < n_y && !*abort; ++i) {
+            // every warp's store of tile i has completed
+            while (true) {
+              int lo = n_y;
+#pragma unroll
+              for (int w = 0; w < EW; ++w) lo = min(lo, ld_acquire_cta_shared(&s_prog[w]));
+              if (lo > i || *abort) break;
+              if ((++spins & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+                report_timeout(55);
+                *abort = 1;
+              }
+            }
+            if (*abort) break;
             fused_signal(fp, p.causal, sl, ytile(i));
           }
         } else if (lane == 0) {
@@ -2498,7 +2551,7 @@ __global__ void __launch_bounds__(fused_threads<EW>(), 1)
               bulk_commit_group();
               if (i > 0) {  // the previous tile's store has completed
                 bulk_wait_group1();
-                mbar_arrive(&st_done[(i - 1) & 1]);
+                st_release_cta_shared(&s_prog[warp - 2], i);
               }
             }
           } else if (lane == 0) {
@@ -2508,10 +2561,7 @@ __global__ void __launch_bounds__(fused_threads<EW>(), 1)
         if constexpr (kWarpStores) {
           if (lane == 0) {
             bulk_wait_group0();  // complete before the unit ends (the next unit reuses the smem)
-            // The last tile's arrival waits for the final dK commit, which needs every
-            // warp's last dS: all warps are then past their earlier arrivals, so this one
-            // cannot land in the phase of tile n_y - 3 (same barrier).
-            if (ok && n_y > 0 && mbar_wait(acc_full, 0, abort, 56)) mbar_arrive(&st_done[(n_y - 1) & 1]);
+            if (ok) st_release_cta_shared(&s_prog[warp - 2], n_y);
           }
           __syncwarp();
         }
@@ -2588,6 +2638,7 @@ __global__ void __launch_bounds__(fused_threads<EW>(), 1)
           const uint64_t db_base = make_sdesc(s0 + 2 * L::kDqABytes, 8192, 1024);
           for (int kb = 0; kb < nkb; ++kb) {
             const int st = kb % QS;
+            *s_left = nkb - kb;
             if (!mbar_wait(&q_full[st], (kb / QS) & 1, abort, 63)) break;
             tc_fence_after();
             const uint64_t da = sdesc_at(da_base, st * L::kDqStageBytes);
@@ -2607,6 +2658,7 @@ __global__ void __launch_bounds__(fused_threads<EW>(), 1)
           tc_commit(q_acc);
           mbar_drain(q_acc, 0);
         }
+        if (lane == 0) *s_left = 0;
       } else if (warp < kStoreWarp) {
         // the first NG / 2 column groups store tile qt0's dQ, the others tile qt0 + 1,
         // D / (NG / 2) columns each
@@ -2651,17 +2703,23 @@ __global__ void __launch_bounds__(fused_threads<EW>(), 1)
     }
 
     // ---------------------------------------------------------------- unit end
+    // The workers meet first and a finished dQ unit is counted before the scheduler
+    // warp joins: its claim may be waiting for exactly that count (a ticket whose dS
+    // slot this unit frees).
     tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (threadIdx.x == 0) {
-      if (*abort) {
-        st_relaxed_gpu(&fp.sched[kSchedAbort], 1);
-      } else if (*s_kind == 1) {
-        __threadfence();  // the discards above are ordered before the slot is handed on
-        red_add_release_gpu(&fp.dq_done[unit / (fp.nq / 2)], 1);
+    if (warp != kSchedWarp) {
+      named_barrier(1, 32 * (EW + 3));
+      if (threadIdx.x == 0) {
+        if (*abort) {
+          st_relaxed_gpu(&fp.sched[kSchedAbort], 1);
+        } else if (*s_kind == 1) {
+          __threadfence();  // the discards above are ordered before the slot is handed on
+          red_add_release_gpu(&fp.dq_done[unit / (fp.nq / 2)], 1);
+        }
       }
     }
+    __syncthreads();
+    tc_fence_after();
   }
 
   __syncthreads();
