@@ -2240,6 +2240,22 @@ __global__ void __launch_bounds__(fused_threads<EW>(), 1)
           }
         }
         claim_next();  // read by thread 0 after the unit-end barrier
+        const int nu = *s_next;
+        if (nu >= 0 && *s_next_kind == 0) {
+          // warm L2 with the next dK/dV unit's K, V and first (last-index) Q, dO tiles
+          const int nsl = nu / fp.nkt;
+          const int nbh = p.bh0 + nsl;
+          const int nhh = nbh % p.l0.nh, nbb = nbh / p.l0.nh;
+          const int nx0 = (nu - nsl * fp.nkt) * BX;
+          const int ny = ((p.sq + kWideY - 1) / kWideY - 1) * kWideY;
+#pragma unroll
+          for (int c = 0; c < W::kChunks; ++c) {
+            tma_prefetch_4d(&tk, c * 64, nx0, nhh, nbb);
+            tma_prefetch_4d(&tv, c * 64, nx0, nhh, nbb);
+            tma_prefetch_4d(&tq, c * 64, ny, nhh, nbb);
+            tma_prefetch_4d(&tdo, c * 64, ny, nhh, nbb);
+          }
+        }
       }
     } else if (*s_kind == 0) {
       // ============================================================ dK/dV unit

@@ -294,6 +294,13 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map,
       : "memory");
 }
 
+// Prefetch of a 4-D box into L2 (no shared-memory destination, no completion).
+__device__ __forceinline__ void tma_prefetch_4d(const CUtensorMap* map, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(map), "r"(c0),
+               "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+
 // L2 cache policies for the .L2::cache_hint forms below: evict_last keeps lines
 // resident ahead of normal traffic (scratch that is read back soon), evict_first
 // lets them go first (data read for the last time).
