@@ -395,8 +395,8 @@ struct FwdSmem {
   static constexpr int kKVOff = NG * kQBytes;
   static constexpr int kBarOff = kKVOff + 2 * kStageBytes;
   // q_full, k_full[2], v_full[2], k_empty[2], v_empty[2], s_full[2], p_full[2], pv_done[2],
-  // p_half[2]
-  static constexpr int kNumBars = 17;
+  // p_half[2], s_free[2]
+  static constexpr int kNumBars = 19;
   static constexpr int kTotal = 1024 + kBarOff + kNumBars * 8 + 16;
 };
 
@@ -458,6 +458,11 @@ __global__ void __launch_bounds__(fwd_threads<NG>(), NG == 1 ? 2 : 1)
                        const __grid_constant__ CUtensorMap tv, const FwdParams p) {
   using L = FwdSmem<D, NG>;
   constexpr uint32_t kOCol = NG * 128;  // O_g at kOCol + g * D (S_g at g * 128)
+  // One query tile at d = 64 leaves TMEM columns [192, 256) free: P goes there instead of
+  // into S's own columns, so S(j + 1) is issued as soon as the softmax has read S(j)
+  // rather than after P V(j) -- the softmax of tile j + 1 no longer waits for S.
+  constexpr bool kSepP = NG == 1 && 128 + D + 64 <= fwd_tmem_cols<NG>();
+  constexpr uint32_t kPCol = 128 + D;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -475,6 +480,8 @@ __global__ void __launch_bounds__(fwd_threads<NG>(), NG == 1 ? 2 : 1)
   uint64_t* pv_done = bars + 13;
   // P columns of keys [0, 64) written: the first half of P V may start
   uint64_t* p_half = bars + 15;
+  // kSepP: the softmax has read all of S (the next S may overwrite it)
+  uint64_t* s_free = bars + 17;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kNumBars);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -503,6 +510,7 @@ __global__ void __launch_bounds__(fwd_threads<NG>(), NG == 1 ? 2 : 1)
       mbar_init(&p_full[i], 4);  // one arrival per softmax warp of the group
       mbar_init(&p_half[i], 4);
       mbar_init(&pv_done[i], 1);
+      mbar_init(&s_free[i], 4);
     }
     *abort = 0;
     fence_mbar_init();
@@ -595,7 +603,7 @@ __global__ void __launch_bounds__(fwd_threads<NG>(), NG == 1 ? 2 : 1)
       // of the next tile, so the group's next S waits for half a P V, not a whole one.
       auto issue_pv = [&](int g, int j, int hh) {
         const uint64_t dv = sdesc_at(dv_base, (j & 1) * L::kStageBytes);
-        const uint32_t pa = tmem + g * 128;  // P_g: packed pairs in S columns [0, 64)
+        const uint32_t pa = tmem + (kSepP ? kPCol : g * 128);  // P_g: packed pairs (S columns [0, 64) or kPCol)
 #pragma unroll
         for (int kk = hh * 4; kk < hh * 4 + 4; ++kk)
           tc_mma_f16_ts(tmem + kOCol + g * D, pa + kk * 8, sdesc_at(dv, kk * 2048), idesc_o,
@@ -614,11 +622,20 @@ __global__ void __launch_bounds__(fwd_threads<NG>(), NG == 1 ? 2 : 1)
           if (!mbar_wait(&v_full[j & 1], (j >> 1) & 1, abort, 18)) break;
           tc_fence_after();
           issue_pv(0, j, 0);
+          if constexpr (kSepP) {
+            if (j + 1 < n_kv) {
+              if (!mbar_wait(&s_free[0], j & 1, abort, 20)) break;
+              if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort, 14)) break;
+              tc_fence_after();
+              issue_s(0, j + 1);
+              tc_commit(&k_empty[(j + 1) & 1]);
+            }
+          }
           if (!mbar_wait(&p_full[0], j & 1, abort, 13)) break;
           tc_fence_after();
           issue_pv(0, j, 1);
           tc_commit(&v_empty[j & 1]);
-          if (j + 1 < n_kv) {
+          if (!kSepP && j + 1 < n_kv) {
             if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort, 14)) break;
             tc_fence_after();
             issue_s(0, j + 1);
@@ -662,6 +679,7 @@ __global__ void __launch_bounds__(fwd_threads<NG>(), NG == 1 ? 2 : 1)
     const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
     const uint32_t t_s = tmem + lane_off + g * 128;
     const uint32_t t_o = tmem + lane_off + kOCol + g * D;
+    const uint32_t t_p = kSepP ? tmem + lane_off + kPCol : t_s;  // packed P
     float m_used = -INFINITY, l = 0.f;
     bool ok = n_kv > 0;
     for (int j = 0; ok && j < n_kv; ++j) {
@@ -701,6 +719,15 @@ __global__ void __launch_bounds__(fwd_threads<NG>(), NG == 1 ? 2 : 1)
           // scale > 0: max commutes with the scaling
           mx = row_max([&](int i) { return __uint_as_float(sv[i]); }) * p.scale_log2;
         }
+      }
+      if (kSepP && j > 0) {
+        // P V(j - 1) has read P(j - 1) (its columns are rewritten below) and O is final
+        // for the rescale
+        if (!mbar_wait(&pv_done[g], (j - 1) & 1, abort, 21)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
       }
       const float m_new = fmaxf(m_used, mx);
       const bool need = m_new > m_used + kRescaleLog2;
@@ -748,6 +775,11 @@ __global__ void __launch_bounds__(fwd_threads<NG>(), NG == 1 ? 2 : 1)
           tmem_ld32(t_s + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
           tmem_ld32(t_s + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
           tmem_wait_ld();
+          if (kSepP && half == 1) {  // all of S(j) is in registers: S(j + 1) may overwrite it
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s_free[g]);
+          }
           uint32_t pk[32];
 #pragma unroll
           for (int i = 0; i < 64; i += 2) {
@@ -763,7 +795,7 @@ __global__ void __launch_bounds__(fwd_threads<NG>(), NG == 1 ? 2 : 1)
             rs2[(i >> 1) & 1] = f2_add(rs2[(i >> 1) & 1], f2_make(p0, p1));
             pk[i / 2] = BF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
           }
-          tmem_st32(t_s + half * 32, pk);
+          tmem_st32(t_p + half * 32, pk);
           if (half == 0) {
             tmem_wait_st();
             tc_fence_before();
