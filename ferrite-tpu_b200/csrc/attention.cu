@@ -2168,9 +2168,8 @@ __global__ void __launch_bounds__(fused_threads<EW>(), 1)
   volatile int* s_next = abort + 4;    // the scheduler warp's claim for the next unit
   volatile int* s_next_kind = abort + 5;
   // Work the current unit's MMA lane has not issued yet (query tiles of a dK/dV unit,
-  // key blocks of a dQ unit); 0 once it is done.  The scheduler claims the next unit
-  // when this drops to a few steps: early enough to hide the claim, late enough that
-  // a claimed unit does not sit idle in this CTA while other CTAs could run it.
+  // key blocks of a dQ unit); 0 once its MMAs have completed, when the scheduler claims
+  // the next unit.
   volatile int* s_left = abort + 6;
   // kWarpStores: tiles of the current dK/dV unit whose dS store has completed, per
   // elementwise warp (monotonic counters: the store warp may fall any number of tiles
@@ -2261,17 +2260,20 @@ __global__ void __launch_bounds__(fused_threads<EW>(), 1)
 
     if (warp == kSchedWarp) {
       if (lane == 0) {
-        const int thr = *s_kind == 0 ? 2 : 12;  // query tiles / key blocks still to issue
+        // Claim once this unit's MMAs have completed: the claim (several gpu-scope
+        // atomics) overlaps the unit's epilogue, and the claimed unit starts right after.
+        // Claiming earlier (two query tiles before the end) delayed the claimed dQ units
+        // by those tiles: their dS was read back later, and ~1/3 more DRAM traffic.
         const uint64_t t0 = globaltimer_ns();
         uint32_t spins = 0;
-        while (*s_left > thr && !*abort) {
+        while (*s_left > 0 && !*abort) {
           __nanosleep(128);
           if ((++spins & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
             report_timeout(65);
             *abort = 1;
           }
         }
-        claim_next();  // read by thread 0 after the unit-end barrier
+        claim_next();  // s_next is read by thread 0 after the unit-end barrier
         const int nu = *s_next;
         if (nu >= 0 && *s_next_kind == 0) {
           // warm L2 with the next dK/dV unit's K, V and first (last-index) Q, dO tiles
