@@ -3076,8 +3076,16 @@ static int64_t fused_sched_bytes(int64_t nslices, int64_t sq) {
   return ((kSchedInts + 2 * ndq + nslices) * 4 + 255) / 256 * 256;
 }
 
+// FERRITE_ATTN_BWD_FUSED: 0 never, 1 (default) from 4096 queries on, 2 whenever the
+// shape allows.  Below 4096 queries a dK/dV unit is only a few query tiles and the
+// unit's fixed costs (barrier set-up, first loads, epilogue) outweigh what the fused
+// launch saves: measured on one B200, the two-kernel path took the backward from 1.21
+// to 1.00 ms at b64 h16 s1024 d64 (the GPT shape) and from 1.45 to 1.31 ms at d128,
+// 3-6% at s2048; the fused kernel was 4% faster at s4096 d64 and level at s8192 d128,
+// where it moves less DRAM traffic and takes a rank's slices in one launch.
 static bool fused_ok(int64_t sq, int64_t sk, int64_t d, int causal) {
-  if (env_int("FERRITE_ATTN_BWD_FUSED", 1) == 0) return false;
+  const int mode = env_int("FERRITE_ATTN_BWD_FUSED", 1);
+  if (mode == 0 || (mode == 1 && sq < 4096)) return false;
   if (d != 64 && d != 128) return false;
   if (sq % 256 != 0 || sk % 128 != 0) return false;  // dQ units pair the 128-query tiles
   return !causal || sq == sk;

@@ -1,5 +1,7 @@
 """The fused persistent backward (dK/dV and dQ-from-dS units in one launch, dS kept
-in L2 between them) against the oracle and against the two-kernel path.
+in L2 between them) against the oracle and against the two-kernel path.  The product
+picks the fused kernel from 4096 queries on; these tests force it at small sizes
+(FERRITE_ATTN_BWD_FUSED=2).
 
 Both paths form the same rounded dS operand (flash_attention.py:184-194 of the
 reference) and compute dQ = scale * dS K with the same product order, so dQ is
@@ -35,7 +37,7 @@ def _bwd(q, k, v, o, lse, do, causal, ws_bytes=None, fused=True):
     full = lib.ferrite_attn_bwd_ds_workspace_size(b, h, sq, sk, d, code)
     ws = torch.empty(full if ws_bytes is None else ws_bytes, dtype=torch.uint8, device="cuda")
     old = os.environ.get("FERRITE_ATTN_BWD_FUSED")
-    os.environ["FERRITE_ATTN_BWD_FUSED"] = "1" if fused else "0"
+    os.environ["FERRITE_ATTN_BWD_FUSED"] = "2" if fused else "0"  # 2: the fused kernel at any eligible size
     try:
         nat.check(lib.ferrite_attn_bwd_ds(nat.stream_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), lse.data_ptr(),
                                           delta.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), ctypes.byref(st), ws.data_ptr(),
