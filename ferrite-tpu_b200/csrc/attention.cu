@@ -2200,7 +2200,7 @@ __global__ void __launch_bounds__(fused_threads<EW>(), 1)
 
   int pending = -1;  // scheduler lane: a dK/dV ticket whose dS slot is not free yet
   // The scheduler warp's lane 0 makes every claim: the first one here, each next one
-  // as soon as the current unit has started.
+  // once the current unit's MMAs have completed (below).
   auto claim_next = [&]() {
     int kind = 0;
     const int u = *abort ? -1 : fused_claim(fp, kind, pending);
@@ -2411,9 +2411,11 @@ __global__ void __launch_bounds__(fused_threads<EW>(), 1)
         if (lane == 0) *s_left = 0;
       } else if (warp == kStoreWarp) {
         // ------------------------------------------------ dS^T stores + signals
-        // One TMA store per 32-key x 64-query staging block; the stg_free arrival
-        // lets the elementwise warps write the next tile while the stores drain to
-        // L2; a tile's query tile is signalled once its stores have completed (one
+        // kWarpStores: the elementwise warps store their own blocks; this warp signals
+        // each tile once every warp's progress counter has passed it.  Otherwise this
+        // warp issues one TMA store per 32-key x 64-query staging block; the stg_free
+        // arrival lets the elementwise warps write the next tile while the stores drain
+        // to L2; a tile's query tile is signalled once its stores have completed (one
         // tile later, so the wait is off every other warp's path).
         if (kWarpStores && lane == 0) {
           const uint64_t t0 = globaltimer_ns();
