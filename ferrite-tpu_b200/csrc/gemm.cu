@@ -1,6 +1,9 @@
 // Matmul with an f32 accumulator for sm_100a.
 //
-// bf16/f16 operands: persistent, warp-specialised tcgen05 kernel.
+// bf16/f16 operands: persistent, warp-specialised tcgen05 kernels.  Plans with
+// 256-wide tiles and M >= 256 run on CTA pairs (gemm_tc2_kernel, below: one
+// 256 x 256 tile per cluster of two CTAs with cta_group::2 MMAs); the rest on
+// one CTA per 128-row tile (gemm_tc_kernel), described here:
 //   * warp 0 (one elected lane) issues TMA loads of A and B tiles into a ring of
 //     STAGES shared-memory slots (128-byte swizzle, no padding copies: ragged
 //     edges are zero-filled by TMA);
