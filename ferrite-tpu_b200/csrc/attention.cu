@@ -1,23 +1,22 @@
 // Causal flash attention for sm_100a: forward, delta prep, dK/dV and dQ.
 //
-// Tensor-core path (bf16/f16, head_dim 64 or 128, sk a multiple of 128): one CTA
-// per (128-row query tile, batch*head), warp-specialised:
-//   warp 0      TMA producer: Q once, then K/V tiles into a 2-slot ring; fully
-//               masked causal tiles are never requested (the KV loop stops at
-//               the diagonal), so they cost neither TMA traffic nor MMA time;
-//   warp 1      MMA issuer (one lane): S = Q K^T into one of two TMEM S buffers
-//               (SS form, both operands K-major), then O_j = P_j V_j into one of
-//               two TMEM PV buffers (P from shared memory, V MN-major), each
-//               completion published with tcgen05.commit -> mbarrier;
-//   warps 2-5   softmax warpgroup, one thread per query row (TMEM lane): reads S
-//               with tcgen05.ld, keeps the running max m and sum l in f32,
-//               writes P = exp(s - m) rounded to the input dtype into shared
-//               memory in the 128-byte-swizzled K-major layout the MMA reads,
-//               and folds each P_j V_j into an f32 register accumulator with the
-//               online-softmax rescale acc = acc * alpha + P_j V_j.  The output is
-//               normalised once at the end and lse = m + log(l) is written.
-// The S(j+1) MMA overlaps the softmax of tile j, and the P_j V_j MMA overlaps
-// the softmax of tile j+1 (the accumulator update lags one tile).
+// Tensor-core path (bf16/f16, head_dim 64 or 128, sk a multiple of 128), all
+// warp-specialised with TMA loads, tcgen05.mma into TMEM and bounded mbarrier waits:
+//   forward (attn_fwd_tc_kernel): a CTA holds two 128-row query tiles (d = 128) whose
+//     softmax warpgroups ping-pong on one tensor core, or one tile (d = 64, two CTAs
+//     per SM).  S = Q K^T lands in TMEM; the softmax writes P back into TMEM as packed
+//     pairs (into S's own columns, or at d = 64 into free columns so the next S need
+//     not wait for P V); O accumulates in TMEM through TS-form MMAs and is rescaled
+//     only when the running max grows by more than 2^8.  Fully masked causal tiles
+//     are never loaded.
+//   delta prep (bwd_prep_vec_kernel): rowsum(dO * O), vectorised.
+//   backward, two kernels: dK/dV per (128-key tile, slice) CTA over 128-query tiles
+//     (attn_dkv_wide_kernel), writing the rounded dS to a scratch slot; then dQ as a
+//     tensor-core GEMM over that dS (attn_dq_ds_kernel).
+//   backward, fused (attn_bwd_fused_kernel, from 4096 queries on): the same dK/dV work
+//     and the dQ-from-dS work as units of one persistent launch, dS read back from L2
+//     as soon as a query-tile pair is complete, with a scheduler warp claiming units.
+// The sections below describe each kernel in detail.
 //
 // Reference numerics (src/ferrite/kernels/flash_attention.py): scores
 // scale * q k^T in f32 (:103-105), finite MASK_VALUE on the causal diagonal
