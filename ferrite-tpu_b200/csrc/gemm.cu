@@ -837,6 +837,84 @@ __global__ void __launch_bounds__(256)
 }
 
 // ---------------------------------------------------------------------------
+// Skinny products: 16-bit A with at most kSkinnyM rows (K-major), B stored [N][K]
+// (trans_b), f32 accumulation -- the serving prefill's LM head over the last position
+// of each sequence (M = batch).  Below the tensor-core path's 128-row minimum these
+// would otherwise run the 128 x 128 CUDA-core tiles, 16x redundant at M = 8; here the
+// cost is reading B once.  A CTA stages all of A in shared memory; each warp takes four
+// output columns at a time, its lanes splitting K into 8-element vectors read straight
+// from B's rows, and reduces the f32 partial sums across the warp at the end.
+// ---------------------------------------------------------------------------
+constexpr int kSkinnyM = 16;
+constexpr int kSkinnyThreads = 256;
+constexpr int kSkinnyMaxSmem = 96 * 1024;
+
+template <typename TA, typename TC, int MR>
+__global__ void __launch_bounds__(kSkinnyThreads)
+    gemm_skinny_kernel(const TA* __restrict__ a, const TA* __restrict__ b, TC* __restrict__ c, int m,
+                       int n, int k, int64_t lda, int64_t ldb, int64_t ldc) {
+  extern __shared__ __align__(16) uint8_t skinny_smem[];
+  TA* sa = reinterpret_cast<TA*>(skinny_smem);  // [MR][k], rows past m zero
+  pdl_launch_dependents();
+  pdl_wait();
+  const int kv = k / 8;  // 16-byte vectors per row
+  for (int idx = threadIdx.x; idx < MR * kv; idx += blockDim.x) {
+    const int r = idx / kv, v = idx - r * kv;
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (r < m) val = ld_v4(a + (int64_t)r * lda + (int64_t)v * 8);
+    *reinterpret_cast<uint4*>(sa + (int64_t)r * k + (int64_t)v * 8) = val;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int quads = (n + 3) / 4;
+  for (int qd = blockIdx.x * (kSkinnyThreads / 32) + warp; qd < quads; qd += gridDim.x * (kSkinnyThreads / 32)) {
+    const int n0 = qd * 4;
+    float acc[MR][4];
+#pragma unroll
+    for (int r = 0; r < MR; ++r)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[r][j] = 0.f;
+    for (int v = lane; v < kv; v += 32) {
+      float bf[4][8];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint4 bv = make_uint4(0, 0, 0, 0);
+        if (n0 + j < n) bv = ld_v4(b + (int64_t)(n0 + j) * ldb + (int64_t)v * 8);
+        const TA* e = reinterpret_cast<const TA*>(&bv);
+#pragma unroll
+        for (int t = 0; t < 8; ++t) bf[j][t] = DT<TA>::to_f(e[t]);
+      }
+#pragma unroll
+      for (int r = 0; r < MR; ++r) {
+        const uint4 av = *reinterpret_cast<const uint4*>(sa + (int64_t)r * k + (int64_t)v * 8);
+        const TA* e = reinterpret_cast<const TA*>(&av);
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          const float x = DT<TA>::to_f(e[t]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[r][j] = fmaf(x, bf[j][t], acc[r][j]);
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < MR; ++r)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float s = acc[r][j];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+        acc[r][j] = s;
+      }
+    // lane (r * 4 + j) % 32 writes element (r, n0 + j)
+#pragma unroll
+    for (int r = 0; r < MR; ++r)
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (lane == ((r * 4 + j) & 31) && r < m && n0 + j < n) c[(int64_t)r * ldc + n0 + j] = DT<TC>::from_f(acc[r][j]);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // host
 // ---------------------------------------------------------------------------
 
@@ -872,6 +950,36 @@ static int pair_slots(int dev, int sms) {
     cache[dev] = n > 0 ? n : sms / 2;
   }
   return cache[dev];
+}
+
+// Skinny path: 16-bit A with at most kSkinnyM rows stored K-major, B stored [N][K],
+// 16-byte aligned rows, K a multiple of 8 whose A rows fit the shared-memory budget.
+static bool skinny_ok(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int64_t lda,
+                      int64_t ldb, int trans_a, int trans_b) {
+  if (env_int("FERRITE_GEMM_SKINNY", 1) == 0) return false;
+  if (trans_a || !trans_b || m < 1 || m > kSkinnyM || n < 1 || k < 8 || k % 8) return false;
+  if ((reinterpret_cast<uintptr_t>(a) & 15u) || (reinterpret_cast<uintptr_t>(b) & 15u)) return false;
+  if ((lda * 2) % 16 || (ldb * 2) % 16) return false;
+  const int mr = m <= 8 ? 8 : kSkinnyM;
+  return (int64_t)mr * k * 2 <= kSkinnyMaxSmem && n <= 0x7fffffff;
+}
+
+template <typename TA, typename TC>
+static int launch_skinny(cudaStream_t s, const void* a, const void* b, void* c, int64_t m, int64_t n,
+                         int64_t k, int64_t lda, int64_t ldb, int64_t ldc) {
+  const bool small = m <= 8;
+  auto kern = small ? gemm_skinny_kernel<TA, TC, 8> : gemm_skinny_kernel<TA, TC, kSkinnyM>;
+  const int smem = (small ? 8 : kSkinnyM) * (int)k * 2;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return fail(FERRITE_LAUNCH_FAILED, "gemm: skinny smem attribute: %s", cudaGetErrorString(e));
+  }
+  const int64_t quads = (n + 3) / 4;
+  const int64_t want = (quads + kSkinnyThreads / 32 - 1) / (kSkinnyThreads / 32);
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(want, 2 * (int64_t)num_sms(current_device())));
+  (void)launch_pdl(kern, dim3(grid), dim3(kSkinnyThreads), smem, s, (const TA*)a, (const TA*)b, (TC*)c, (int)m,
+                   (int)n, (int)k, lda, ldb, ldc);
+  return check_launch("gemm_skinny");
 }
 
 // PAIR: the CTA-pair kernel (grid: two CTAs per cluster, at most the clusters
@@ -1175,6 +1283,18 @@ extern "C" int ferrite_gemm_ws(void* stream, const void* a, const void* b, void*
     if (c_dtype == FERRITE_BF16) return run_tc<false, __nv_bfloat16>(s, a, b, c, m, n, k, lda, ldb, ldc, trans_a, trans_b, workspace, workspace_bytes);
     if (c_dtype == FERRITE_F32) return run_tc<false, float>(s, a, b, c, m, n, k, lda, ldb, ldc, trans_a, trans_b, workspace, workspace_bytes);
     return run_tc<false, __half>(s, a, b, c, m, n, k, lda, ldb, ldc, trans_a, trans_b, workspace, workspace_bytes);
+  }
+  if (ab_dtype != FERRITE_F32 && skinny_ok(a, b, m, n, k, lda, ldb, trans_a, trans_b)) {
+#define SKINNY(TA, TC) launch_skinny<TA, TC>(s, a, b, c, m, n, k, lda, ldb, ldc)
+    if (ab_dtype == FERRITE_BF16) {
+      if (c_dtype == FERRITE_F32) return SKINNY(__nv_bfloat16, float);
+      if (c_dtype == FERRITE_BF16) return SKINNY(__nv_bfloat16, __nv_bfloat16);
+      return SKINNY(__nv_bfloat16, __half);
+    }
+    if (c_dtype == FERRITE_F32) return SKINNY(__half, float);
+    if (c_dtype == FERRITE_BF16) return SKINNY(__half, __nv_bfloat16);
+    return SKINNY(__half, __half);
+#undef SKINNY
   }
 #define SIMT(TA, TC) launch_simt<TA, TC>(s, a, b, c, m, n, k, lda, ldb, ldc, trans_a, trans_b)
   if (ab_dtype == FERRITE_F32) {
