@@ -52,6 +52,22 @@ def bucket_for(length: int, buckets: tuple[int, ...]) -> int:
     raise ValueError(f"prompt length {length} exceeds largest bucket {buckets[-1]}")
 
 
+_MATRICES = ("wqkv", "wo", "w1", "w2")
+
+
+def cast_weights(params, dtype):
+    """The parameters with every layer matrix in the compute dtype, plus the tied embedding
+    in the compute dtype under ``lm_head`` for the output projection.  The model casts
+    these at every use (``w.to(cfg.dtype)``, gpt.py:95-104 and :143 of the reference);
+    casting once gives the same values, and inside a captured graph it saves re-reading
+    and re-writing every weight on each replay.  Norm weights and the f32 embedding
+    tables (the lookup adds them in f32 before casting) are shared, not copied."""
+    out = dict(params)
+    out["layers"] = [{k: (v.to(dtype) if k in _MATRICES else v) for k, v in layer.items()} for layer in params["layers"]]
+    out["lm_head"] = params["tok_emb"].to(dtype)
+    return out
+
+
 @torch.no_grad()
 def prefill(params, tokens, lengths, cfg: GPTConfig, max_len: int):
     """tokens [B, L] (right-padded), lengths [B] -> (next-token logits [B, V] f32, k_cache, v_cache).
@@ -70,7 +86,7 @@ def prefill(params, tokens, lengths, cfg: GPTConfig, max_len: int):
         vc[i, :, :, :s] = v
     _, y = _norm(pending, params["ln_f"], h, cfg)
     last = y[torch.arange(b, device=y.device), (lengths - 1).long()]  # [B, D]
-    logits = _lm_head(last, params["tok_emb"], cfg)
+    logits = _lm_head(last, params.get("lm_head", params["tok_emb"]), cfg)
     return logits, kc, vc
 
 
@@ -115,7 +131,7 @@ def decode_step(params, token, pos, k_cache, v_cache, cfg: GPTConfig):
         pending = _linear(F.gelu(_linear(y2, layer["w1"], cfg), approximate="tanh"), layer["w2"], cfg)
     _, y = _norm(pending, params["ln_f"], h, cfg)
     # tied head in cfg.dtype with f32 accumulation (engine.py:130): the embedding is cast first
-    return _lm_head(y, params["tok_emb"], cfg.replace(linear="xla"))
+    return _lm_head(y, params.get("lm_head", params["tok_emb"]), cfg.replace(linear="xla"))
 
 
 class Engine:
@@ -125,6 +141,8 @@ class Engine:
     def __init__(self, params, model_cfg: GPTConfig, serve_cfg: ServeConfig):
         if max(serve_cfg.buckets) > model_cfg.seq_len or serve_cfg.max_len > model_cfg.seq_len:
             raise ValueError("buckets and max_len must fit within the model's trained seq_len (positional table)")
+        # the weights as of construction, matrices cast once to the compute dtype
+        params = cast_weights(params, model_cfg.dtype)
         self.params = params
         self.cfg = model_cfg
         self.serve = serve_cfg
