@@ -915,6 +915,238 @@ __global__ void __launch_bounds__(kSkinnyThreads)
 }
 
 // ---------------------------------------------------------------------------
+// Skinny products with B stored [K][N] (no transpose): the decode step's linears,
+// y = x W with x [m <= 16, K] and W [K, N] row-major.  The cost is reading W once,
+// and at these sizes (2-8 MB per matrix) nearly all of W has to be in flight at
+// once.  A cluster of `cs` CTAs owns 64 output columns and splits K between its CTAs;
+// each CTA streams its rows of the 64-column strip (128 bytes per row) through a
+// two-stage shared-memory ring with 16-byte cp.async copies (kKnStageRows rows, 32 KB,
+// per stage: two stages hold the CTA's whole slice for K / cs <= 512), the 16-byte
+// chunks of a row XOR-swizzled by the row index.  The products run on mma.sync
+// m16n8k16 with the roles turned around, y^T = W^T x^T: W^T is the 16 x 16 A operand
+// (ldmatrix.trans straight from the [K][N] rows, conflict-free thanks to the
+// swizzle), x^T the 16 x 8 B operand (x kept 16-bit in shared memory, rows padded
+// by 16 bytes), f32 accumulators.  The arithmetic is negligible either way; one MMA
+// replaces 2048 FFMAs plus their conversions and shared-memory reads, which on CUDA
+// cores made these launches issue-bound.  Warps take interleaved 16-row steps; the
+// CTA sums its warps' tiles in shared memory, and the cluster's CTAs sum the partial
+// tiles through distributed shared memory in rank order, each CTA writing its share
+// of the outputs.  Fixed summation order (deterministic), no global scratch, one
+// launch.
+// ---------------------------------------------------------------------------
+constexpr int kKnTileN = 64;
+constexpr int kKnThreads = 256;
+constexpr int kKnWarps = kKnThreads / 32;
+constexpr int kKnStageRows = 256;  // rows of W per ring stage: 256 x 128 bytes
+constexpr int kKnStages = 2;
+constexpr int kKnMaxCluster = 8;
+constexpr int kKnMaxSmem = 160 * 1024;
+constexpr int kKnRowGrain = 64;  // rows per CTA are a multiple of this
+constexpr int kKnAUnits = 4;     // 16-byte units of x loaded per thread before they are stored
+
+// Shared memory of one CTA: the ring of W stages; x's rows [MR][kper + 8] (16-bit,
+// padded so that the eight rows of an MMA operand fall in distinct banks); the warps'
+// partial tiles [kKnWarps][MR][64] f32; the CTA's partial tile [MR][64] f32 that the
+// cluster reads.
+constexpr int kKnRingBytes = kKnStages * kKnStageRows * kKnTileN * 2;
+__host__ __device__ constexpr int kn_x_bytes(int kper, int mr) { return (mr * (kper + 8) * 2 + 15) / 16 * 16; }
+__host__ __device__ constexpr int kn_smem_bytes(int kper, int mr) {
+  return kKnRingBytes + kn_x_bytes(kper, mr) + (kKnWarps + 1) * mr * kKnTileN * 4;
+}
+
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+// 16-byte global -> shared asynchronous copy, L2 only; src_bytes = 0 fills zeros.
+__device__ __forceinline__ void cp_async16_zfill(void* smem, const void* gmem, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_group() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+// Four 8 x 8 16-bit matrices, transposed on the way (lane L gives the address of row
+// L % 8 of matrix L / 8).
+__device__ __forceinline__ void ldmatrix_x4_trans(const void* p, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+// d += a b, m16n8k16, 16-bit operands (A row-major, B column-major), f32 accumulators.
+template <typename TA>
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+  if constexpr (std::is_same<TA, __nv_bfloat16>::value)
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+                 "{%0, %1, %2, %3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+  else
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+                 "{%0, %1, %2, %3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+// EPI: kEpiNone (C = acc) or kEpiGelu (C = u = round(acc), aux = round(gelu_tanh(u))).
+template <typename TA, typename TC, int MR, int EPI>
+__global__ void __launch_bounds__(kKnThreads)
+    gemm_skinny_kn_kernel(const TA* __restrict__ a, const TA* __restrict__ b, TC* __restrict__ c, int m,
+                          int n, int k, int kper, int64_t lda, int64_t ldb, int64_t ldc, int a_vec,
+                          TC* __restrict__ aux, int64_t ld_aux) {
+  constexpr int NG = MR / 8;  // 8-row groups of x (MMA N = 8)
+  extern __shared__ __align__(128) uint8_t kn_smem[];
+  TA* ring = reinterpret_cast<TA*>(kn_smem);  // [kKnStages][kKnStageRows][64], chunks swizzled
+  TA* sx = reinterpret_cast<TA*>(kn_smem + kKnRingBytes);
+  float* red = reinterpret_cast<float*>(kn_smem + kKnRingBytes + kn_x_bytes(kper, MR));
+  float* part = red + kKnWarps * MR * kKnTileN;
+  const int ldx = kper + 8;
+  const int cs = (int)cluster_nctarank();
+  const int rank = (int)cluster_ctarank();
+  const int col0 = (int)(blockIdx.x / cs) * kKnTileN;
+  const int k0 = rank * kper;
+  const int kn = max(0, min(k - k0, kper));  // rows of W this CTA reads
+  const int nst = (kn + kKnStageRows - 1) / kKnStageRows;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, tig = lane & 3;
+  pdl_launch_dependents();
+  // Bring this CTA's strip of W into L2 while the previous kernel finishes (a launch
+  // that follows through programmatic dependent launch starts early).  A prefetch
+  // returns no data, so it is safe even if that kernel writes W: L2 keeps the newer lines.
+  if (col0 < n) {
+    const uint32_t bytes = (uint32_t)min(kKnTileN, n - col0) * 2;  // a multiple of 16
+    for (int r = threadIdx.x; r < kn; r += kKnThreads)
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(b + (int64_t)(k0 + r) * ldb + col0), "r"(bytes)
+                   : "memory");
+  }
+  pdl_wait();
+
+  // stage st <- rows [bt * kKnStageRows, +kKnStageRows) of this CTA's slice, 16 bytes
+  // (8 columns) per copy, chunk ch of row r at chunk ch ^ (r % 8); rows past the slice
+  // and columns past n are zero-filled
+  auto issue = [&](int st, int bt) {
+    TA* dst = ring + st * kKnStageRows * kKnTileN;
+#pragma unroll
+    for (int i = 0; i < kKnStageRows * 8 / kKnThreads; ++i) {
+      const int ci = i * kKnThreads + threadIdx.x;
+      const int r = ci >> 3, ch = ci & 7;
+      const int kk = bt * kKnStageRows + r, col = col0 + ch * 8;
+      const bool ok = kk < kn && col < n;  // n % 8 == 0: a chunk is all in or all out
+      const TA* src = ok ? b + (int64_t)(k0 + kk) * ldb + col : b;
+      cp_async16_zfill(dst + r * kKnTileN + ((ch ^ (r & 7)) << 3), src, ok ? 16 : 0);
+    }
+  };
+  if (nst > 0) issue(0, 0);
+  cp_async_commit_group();
+  if (nst > 1) issue(1, 1);
+  cp_async_commit_group();
+
+  // x's rows [k0, k0 + kper) -> sx (zero past m and past kn); a pass issues all its
+  // loads before its stores
+  {
+    const int vpr = kper / 8;
+    const int units = MR * vpr;
+    for (int base = 0; base < units; base += kKnThreads * kKnAUnits) {
+      uint4 xv[kKnAUnits];
+#pragma unroll
+      for (int u = 0; u < kKnAUnits; ++u) {
+        const int id = base + u * kKnThreads + threadIdx.x;
+        const int r = id / vpr, kk = (id - r * vpr) * 8;
+        const TA* src = a + (int64_t)r * lda + k0 + kk;
+        if (id < units && r < m && a_vec && kk + 8 <= kn) {
+          xv[u] = ld_v4(src);
+        } else {
+          uint4 v;
+          TA* e = reinterpret_cast<TA*>(&v);
+#pragma unroll
+          for (int t = 0; t < 8; ++t) e[t] = (id < units && r < m && kk + t < kn) ? src[t] : DT<TA>::from_f(0.f);
+          xv[u] = v;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kKnAUnits; ++u) {
+        const int id = base + u * kKnThreads + threadIdx.x;
+        const int r = id / vpr, kk = (id - r * vpr) * 8;
+        if (id < units) *reinterpret_cast<uint4*>(sx + r * ldx + kk) = xv[u];
+      }
+    }
+  }
+
+  float acc[4][NG][4];
+#pragma unroll
+  for (int s4 = 0; s4 < 4; ++s4)
+#pragma unroll
+    for (int ng = 0; ng < NG; ++ng)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[s4][ng][e] = 0.f;
+  for (int bt = 0; bt < nst; ++bt) {
+    cp_async_wait_1();  // this stage's group has landed (the newest may still fly)
+    __syncthreads();    // ... for every thread's copies, and x's rows are staged
+    const TA* st = ring + (bt & 1) * kKnStageRows * kKnTileN;
+    const int rows = min(kKnStageRows, kn - bt * kKnStageRows);
+    for (int ks = warp; ks * 16 < rows; ks += kKnWarps) {
+      const int kl = ks * 16;
+      const int kx = bt * kKnStageRows + kl;
+      uint32_t bx[NG][2];
+#pragma unroll
+      for (int ng = 0; ng < NG; ++ng) {
+        const TA* xp = sx + (ng * 8 + g) * ldx + kx + tig * 2;
+        bx[ng][0] = *reinterpret_cast<const uint32_t*>(xp);
+        bx[ng][1] = *reinterpret_cast<const uint32_t*>(xp + 8);
+      }
+      const int row = kl + (lane & 7) + ((lane >> 4) << 3);
+#pragma unroll
+      for (int s4 = 0; s4 < 4; ++s4) {
+        const int chunk = s4 * 2 + ((lane >> 3) & 1);
+        uint32_t wa[4];
+        ldmatrix_x4_trans(st + row * kKnTileN + ((chunk ^ (row & 7)) << 3), wa);
+#pragma unroll
+        for (int ng = 0; ng < NG; ++ng) mma_16816<TA>(acc[s4][ng], wa, bx[ng]);
+      }
+    }
+    __syncthreads();  // the stage is free again
+    if (bt + 2 < nst) issue(bt & 1, bt + 2);
+    cp_async_commit_group();
+  }
+
+  // accumulator (W column n0 + g [+8], x row tig*2 + e) -> the warp's tile, then the
+  // warps' tiles -> the CTA's partial tile
+#pragma unroll
+  for (int s4 = 0; s4 < 4; ++s4)
+#pragma unroll
+    for (int ng = 0; ng < NG; ++ng)
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int e = 0; e < 2; ++e)
+          red[(warp * MR + ng * 8 + tig * 2 + e) * kKnTileN + s4 * 16 + g + h * 8] = acc[s4][ng][h * 2 + e];
+  __syncthreads();
+  for (int v = threadIdx.x; v < MR * kKnTileN; v += kKnThreads) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < kKnWarps; ++w) s += red[w * MR * kKnTileN + v];
+    part[v] = s;
+  }
+  cluster_sync_all();  // every CTA's partial tile is visible to the cluster
+  const int per = MR * kKnTileN / cs;  // cs is a power of two <= 8
+  for (int v = rank * per + threadIdx.x; v < (rank + 1) * per; v += kKnThreads) {
+    const int r = v / kKnTileN, cc = col0 + v % kKnTileN;
+    if (r >= m || cc >= n) continue;
+    float s = 0.f;
+    for (int q = 0; q < cs; ++q) s += ld_shared_cluster_f32(mapa_shared(part + v, (uint32_t)q));
+    const TC u = DT<TC>::from_f(s);
+    c[(int64_t)r * ldc + cc] = u;
+    if constexpr (EPI == kEpiGelu) aux[(int64_t)r * ld_aux + cc] = DT<TC>::from_f(gelu_tanh_f(DT<TC>::to_f(u)));
+  }
+  cluster_sync_all();  // no CTA leaves while another still reads its partial tile
+}
+
+// ---------------------------------------------------------------------------
 // host
 // ---------------------------------------------------------------------------
 
@@ -980,6 +1212,55 @@ static int launch_skinny(cudaStream_t s, const void* a, const void* b, void* c, 
   (void)launch_pdl(kern, dim3(grid), dim3(kSkinnyThreads), smem, s, (const TA*)a, (const TA*)b, (TC*)c, (int)m,
                    (int)n, (int)k, lda, ldb, ldc);
   return check_launch("gemm_skinny");
+}
+
+// Cluster size and rows of W per CTA for the [K][N] skinny path: enough CTAs per
+// cluster that the ring holds a CTA's whole slice at once, then more (up to 8) while
+// the grid still fits the SMs once, so that most of W is in flight at once.
+struct KnPlan {
+  int cs, kper, smem;
+};
+static KnPlan kn_plan(int64_t m, int64_t n, int64_t k, int sms) {
+  const int mr = m <= 8 ? 8 : kSkinnyM;
+  const int chunk = kKnStages * kKnStageRows;  // rows the ring holds at once
+  const int64_t tiles = (n + kKnTileN - 1) / kKnTileN;
+  int cs = 1;
+  while (cs < kKnMaxCluster && (k + cs - 1) / cs > chunk) cs *= 2;
+  while (cs < kKnMaxCluster && tiles * cs * 2 <= sms && (k + 2 * cs - 1) / (2 * cs) >= kKnRowGrain) cs *= 2;
+  const int64_t rows = (k + cs - 1) / cs;
+  const int64_t kper = std::min<int64_t>((rows + kKnRowGrain - 1) / kKnRowGrain * kKnRowGrain, 1 << 20);
+  return {cs, (int)kper, kn_smem_bytes((int)kper, mr)};
+}
+
+// [K][N] skinny path: 16-bit operands, A K-major with at most kSkinnyM rows, B stored
+// [K][N] with 16-byte aligned rows and N a multiple of 8; K bounded by shared memory.
+static bool skinny_kn_ok(const void* b, int64_t m, int64_t n, int64_t k, int64_t ldb, int trans_a,
+                         int trans_b) {
+  if (env_int("FERRITE_GEMM_SKINNY", 1) == 0) return false;
+  if (trans_a || trans_b || m < 1 || m > kSkinnyM || n < 8 || n % 8 || k < 1) return false;
+  if ((reinterpret_cast<uintptr_t>(b) & 15u) || ldb % 8) return false;
+  if (n > 0x7fffffff || k > 0x7fffffff) return false;
+  return kn_plan(m, n, k, num_sms(current_device())).smem <= kKnMaxSmem;
+}
+
+template <typename TA, typename TC, int EPI = kEpiNone>
+static int launch_skinny_kn(cudaStream_t s, const void* a, const void* b, void* c, int64_t m, int64_t n,
+                            int64_t k, int64_t lda, int64_t ldb, int64_t ldc, void* aux = nullptr,
+                            int64_t ld_aux = 0) {
+  const KnPlan pl = kn_plan(m, n, k, num_sms(current_device()));
+  auto kern = m <= 8 ? gemm_skinny_kn_kernel<TA, TC, 8, EPI> : gemm_skinny_kn_kernel<TA, TC, kSkinnyM, EPI>;
+  if (pl.smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem);
+    if (e != cudaSuccess) return fail(FERRITE_LAUNCH_FAILED, "gemm: skinny [K][N] smem attribute: %s", cudaGetErrorString(e));
+  }
+  // x's rows as 16-byte vectors: aligned base and row stride (kper, hence k0, is a multiple of 16)
+  const int a_vec = (reinterpret_cast<uintptr_t>(a) & 15u) == 0 && lda % 8 == 0;
+  const int64_t tiles = (n + kKnTileN - 1) / kKnTileN;
+  if (tiles * pl.cs > 0x7fffffff) return fail(FERRITE_BAD_SHAPE, "gemm: N too large for the skinny path");
+  (void)launch_pdl_cluster(kern, dim3((unsigned)(tiles * pl.cs)), dim3(kKnThreads), (size_t)pl.smem, s,
+                           (unsigned)pl.cs, (const TA*)a, (const TA*)b, (TC*)c, (int)m, (int)n, (int)k,
+                           pl.kper, lda, ldb, ldc, a_vec, (TC*)aux, ld_aux);
+  return check_launch("gemm_skinny_kn");
 }
 
 // PAIR: the CTA-pair kernel (grid: two CTAs per cluster, at most the clusters
@@ -1235,10 +1516,16 @@ extern "C" int ferrite_gemm_epilogue(void* stream, const void* a, const void* b,
     return fail(FERRITE_BAD_SHAPE, "gemm_epilogue: leading dimension too small");
   if (m == 0 || n == 0) return FERRITE_OK;
   if (!a || !b || !c || !aux) return fail(FERRITE_BAD_SHAPE, "gemm_epilogue: null pointer");
+  // decode-sized up-projections (at most 16 rows, W stored [K][N]): the skinny kernel
+  if (epilogue == kEpiGelu && k > 0 && !tc_eligible(a, b, m, n, k, lda, ldb, trans_a, trans_b) &&
+      skinny_kn_ok(b, m, n, k, ldb, trans_a, trans_b))
+    return launch_skinny_kn<__nv_bfloat16, __nv_bfloat16, kEpiGelu>((cudaStream_t)stream, a, b, c, m, n, k, lda, ldb,
+                                                                     ldc, aux, ld_aux);
   if (k == 0 || !tc_eligible(a, b, m, n, k, lda, ldb, trans_a, trans_b))
     return fail(FERRITE_UNSUPPORTED_DTYPE,
                 "gemm_epilogue: needs the tensor-core path (16-byte aligned operands and strides, "
-                "m, n >= 128, k >= 64)");
+                "m, n >= 128, k >= 64) or, for the GELU epilogue, the skinny path (m <= 16, B stored "
+                "[K][N] 16-byte aligned, n and ldb multiples of 8)");
   return run_tc<true, __nv_bfloat16>((cudaStream_t)stream, a, b, c, m, n, k, lda, ldb, ldc, trans_a,
                                      trans_b, nullptr, 0, epilogue, aux, ld_aux);
 }
@@ -1295,6 +1582,18 @@ extern "C" int ferrite_gemm_ws(void* stream, const void* a, const void* b, void*
     if (c_dtype == FERRITE_BF16) return SKINNY(__half, __nv_bfloat16);
     return SKINNY(__half, __half);
 #undef SKINNY
+  }
+  if (ab_dtype != FERRITE_F32 && skinny_kn_ok(b, m, n, k, ldb, trans_a, trans_b)) {
+#define SKINNY_KN(TA, TC) launch_skinny_kn<TA, TC>(s, a, b, c, m, n, k, lda, ldb, ldc)
+    if (ab_dtype == FERRITE_BF16) {
+      if (c_dtype == FERRITE_F32) return SKINNY_KN(__nv_bfloat16, float);
+      if (c_dtype == FERRITE_BF16) return SKINNY_KN(__nv_bfloat16, __nv_bfloat16);
+      return SKINNY_KN(__nv_bfloat16, __half);
+    }
+    if (c_dtype == FERRITE_F32) return SKINNY_KN(__half, float);
+    if (c_dtype == FERRITE_BF16) return SKINNY_KN(__half, __nv_bfloat16);
+    return SKINNY_KN(__half, __half);
+#undef SKINNY_KN
   }
 #define SIMT(TA, TC) launch_simt<TA, TC>(s, a, b, c, m, n, k, lda, ldb, ldc, trans_a, trans_b)
   if (ab_dtype == FERRITE_F32) {

@@ -15,10 +15,12 @@ positions live on the device, so one graph serves every step.
 
 Decode is one query row against the cache.  The reference keeps the whole decode
 step in XLA (engine.py:12-15); here, with ``ServeConfig.decode_kernels="pallas"`` (the
-default), its attention and cache write run as one kernel (``decode_attention``) and
-its residual-add + RMSNorms on the fused norm kernel; its linears (one row per
-sequence) stay on the plain path.  ``"xla"`` gives the reference's plain path
-throughout.  ``jax.export`` of the decode step has no counterpart here.
+default), its attention and cache write run as one kernel (``decode_attention``), its
+residual-add + RMSNorms on the fused norm kernel, and for 16-bit models its linears
+(one row per sequence) and the tied LM head on the skinny GEMM kernels (B stored
+[K][N] for the layer matrices, the MLP's GELU fused into the up-projection; [N][K]
+for the embedding); f32 models keep the plain linears.  ``"xla"`` gives the reference's plain path throughout.  ``jax.export`` of
+the decode step has no counterpart here.
 """
 
 from __future__ import annotations
@@ -32,7 +34,7 @@ import torch
 import torch.nn.functional as F
 
 from ferrite.kernels.decode_attention import decode_attention
-from ferrite.model.gpt import GPTConfig, _linear, _lm_head, _norm, block
+from ferrite.model.gpt import GPTConfig, _linear, _lm_head, _mlp, _norm, block
 
 
 @dataclasses.dataclass(frozen=True)
@@ -128,10 +130,11 @@ def decode_step(params, token, pos, k_cache, v_cache, cfg: GPTConfig):
         a = a.reshape(b, cfg.d_model)
         a = _linear(a, layer["wo"], cfg)
         h, y2 = _norm(a, layer["ln2"], h, cfg)
-        pending = _linear(F.gelu(_linear(y2, layer["w1"], cfg), approximate="tanh"), layer["w2"], cfg)
+        pending = _mlp(y2[:, None], layer["w1"], layer["w2"], cfg)[:, 0]
     _, y = _norm(pending, params["ln_f"], h, cfg)
-    # tied head in cfg.dtype with f32 accumulation (engine.py:130): the embedding is cast first
-    return _lm_head(y, params.get("lm_head", params["tok_emb"]), cfg.replace(linear="xla"))
+    # tied head in cfg.dtype with f32 accumulation (engine.py:130): exact 16-bit products
+    # summed in f32 on either path, f32 logits
+    return _lm_head(y, params.get("lm_head", params["tok_emb"]), cfg)
 
 
 class Engine:
@@ -150,7 +153,9 @@ class Engine:
         if serve_cfg.decode_kernels not in ("pallas", "xla"):
             raise ValueError(f"decode_kernels must be 'pallas' or 'xla', got {serve_cfg.decode_kernels!r}")
         dk = serve_cfg.decode_kernels
-        self.decode_cfg = model_cfg.replace(attention=dk, norm=dk, linear="xla")
+        # the skinny GEMM kernels take 16-bit operands: f32 models keep the plain linears
+        dl = dk if model_cfg.dtype in (torch.bfloat16, torch.float16) else "xla"
+        self.decode_cfg = model_cfg.replace(attention=dk, norm=dk, linear=dl)
         self.device = params["tok_emb"].device
         self.compile_seconds: dict[str, float] = {}
         self._graphs: dict[int, Any] = {}

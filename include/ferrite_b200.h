@@ -146,8 +146,10 @@ FERRITE_API int ferrite_gemm(void* stream, const void* a, const void* b, void* c
  *                          (A [M][K], B [K][N]: trans_a = trans_b = 0);
  *   epilogue 2 (GELU_BWD): c = round(round(A B^T) * gelu_tanh'(aux)), aux = u
  *                          (dU from dA = dP W2^T: trans_a = 0, trans_b = 1).
- * Both need the tensor-core path (16-byte aligned operands and strides, m, n >=
- * 128, k >= 64); other shapes return FERRITE_UNSUPPORTED_DTYPE. */
+ * Both run on the tensor-core path (16-byte aligned operands and strides, m, n >=
+ * 128, k >= 64); epilogue 1 also runs for decode-sized products (m <= 16, B 16-byte
+ * aligned with n and ldb multiples of 8) on the skinny CUDA path.  Other shapes
+ * return FERRITE_UNSUPPORTED_DTYPE. */
 FERRITE_API int ferrite_gemm_epilogue(void* stream, const void* a, const void* b, void* c,
                           int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
                           int64_t ldc, int trans_a, int trans_b, int epilogue,

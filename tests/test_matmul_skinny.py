@@ -1,9 +1,12 @@
-"""The skinny 16-bit GEMM path (at most 16 rows of A, B stored [N][K]): the serving
-prefill's LM head over the last position of each sequence, y = h W^T with W the tied
-embedding (gpt.py:143 of anxnd2211/ferrite-tpu).  Checked against a torch fp32 reference
-and the oracle (f32 accumulation of exact 16-bit products: differences are summation
-order only), at the edges of the path (1 and 16 rows, N not a multiple of 4, K = 8) and
-just past them (17 rows, K not a multiple of 8), which take the other kernels.
+"""The skinny 16-bit GEMM paths (at most 16 rows of A).  B stored [N][K]: the serving
+LM head over the last position of each sequence, y = h W^T with W the tied embedding
+(gpt.py:143 of anxnd2211/ferrite-tpu).  B stored [K][N]: the decode step's linears,
+y = x W (gpt.py:95-104, engine.py:107-131), K split over a thread-block cluster.
+Checked against a torch fp32 reference and the oracle (f32 accumulation of exact 16-bit
+products: differences are summation order only), at the edges of each path (1, 8, 9 and
+16 rows, N not a multiple of 4 or of the 64-column tile, K = 8, K past one load batch
+per CTA) and just past them (17 rows, K or N not a multiple of 8), which take the
+other kernels.
 """
 
 import numpy as np
@@ -61,3 +64,93 @@ def test_strided_rows_and_deterministic():
     got = _gemm_tb(a, b, torch.float32)
     torch.testing.assert_close(got, ref, rtol=1e-4, atol=1e-4)
     assert torch.equal(got, _gemm_tb(a, b, torch.float32))
+
+
+def _gemm_kn(a, b, out_dtype):
+    """a [m, k], b [k, n] -> a b through ferrite_gemm (no transposes)."""
+    m, k = a.shape
+    n = b.shape[1]
+    c = torch.empty(m, n, dtype=out_dtype, device="cuda")
+    nat.check(nat.lib().ferrite_gemm(nat.stream_ptr(), a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k, a.stride(0), b.stride(0),
+                                     c.stride(0), 0, 0, nat.dtype_code(a.dtype), nat.dtype_code(c.dtype)))
+    torch.cuda.synchronize()
+    return c
+
+
+# decode linears of GPT d1024 (qkv, out, up, down), edges of the tile and of the cluster
+# split, K past one batch of loads per CTA (8192, 20000), and shapes that leave the path
+KN_SHAPES = [(8, 3072, 1024), (8, 1024, 1024), (8, 4096, 1024), (8, 1024, 4096), (1, 8, 8), (3, 1000, 1000),
+             (9, 200, 777), (16, 4096, 8192), (8, 136, 20000), (17, 256, 512), (8, 1002, 64)]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("m,n,k", KN_SHAPES)
+def test_skinny_kn_matches_fp32_reference(dtype, m, n, k):
+    g = torch.Generator(device="cuda").manual_seed(m * 7 + n * 3 + k)
+    a = torch.randn(m, k, device="cuda", generator=g).to(dtype)
+    b = (torch.randn(k, n, device="cuda", generator=g) / np.sqrt(k)).to(dtype)
+    ref = a.float() @ b.float()
+    got = _gemm_kn(a, b, torch.float32)
+    torch.testing.assert_close(got, ref, rtol=1e-4, atol=1e-4)
+    got16 = _gemm_kn(a, b, dtype)
+    torch.testing.assert_close(got16.float(), ref, rtol=2**-7, atol=1e-3)
+
+
+def test_skinny_kn_decode_shape_against_the_oracle():
+    """bf16 x [8, 1024] against the fused QKV weight [1024, 3072], bf16 out (the decode step)."""
+    rng = np.random.default_rng(11)
+    x = normal(rng, (8, 1024), BF16)
+    w = normal(rng, (1024, 3072), BF16, std=0.02)
+    got = to_numpy(_gemm_kn(to_torch(x), to_torch(w), torch.bfloat16)).astype(np.float32)
+    ref = om.matmul_reference(x, w, out_dtype=np.float32)
+    np.testing.assert_allclose(got, ref, rtol=2**-7, atol=1e-3)
+
+
+def test_skinny_kn_strided_and_deterministic():
+    """A and B as slices of larger buffers (lda > k, ldb > n); repeated calls agree bitwise."""
+    g = torch.Generator(device="cuda").manual_seed(4)
+    abuf = torch.randn(16, 5000, device="cuda", generator=g).to(torch.bfloat16)
+    bbuf = (torch.randn(4100, 1536, device="cuda", generator=g) / 64).to(torch.bfloat16)
+    a, b = abuf[:12, :4096], bbuf[:4096, 256:1280]
+    ref = a.float() @ b.float()
+    got = _gemm_kn(a, b, torch.float32)
+    torch.testing.assert_close(got, ref, rtol=1e-4, atol=1e-4)
+    for _ in range(3):
+        assert torch.equal(got, _gemm_kn(a, b, torch.float32))
+
+
+def test_matmul_api_routes_decode_rows():
+    """The reference-facing ``matmul`` on a decode-sized product: forward on the [K][N]
+    skinny path, backward products through their own paths, all against fp32."""
+    from ferrite.kernels.matmul import matmul
+
+    g = torch.Generator(device="cuda").manual_seed(8)
+    x = torch.randn(8, 1024, device="cuda", generator=g).to(torch.bfloat16).requires_grad_()
+    w = (torch.randn(1024, 4096, device="cuda", generator=g) / 32).to(torch.bfloat16).requires_grad_()
+    y = matmul(x, w)
+    ref = x.detach().float() @ w.detach().float()
+    torch.testing.assert_close(y.float(), ref, rtol=2**-7, atol=1e-3)
+    gy = torch.randn(8, 4096, device="cuda", generator=g).to(torch.bfloat16)
+    y.backward(gy)
+    torch.testing.assert_close(x.grad.float(), gy.float() @ w.detach().float().t(), rtol=2**-7, atol=2e-2)
+    torch.testing.assert_close(w.grad.float(), x.detach().float().t() @ gy.float(), rtol=2**-7, atol=2e-2)
+
+
+@pytest.mark.parametrize("m", [1, 8, 16])
+def test_skinny_kn_gelu_epilogue(m):
+    """ferrite_gemm_epilogue's GELU form on a decode-sized up-projection: u = x W1 rounded
+    to bf16 and a = gelu_tanh(u) rounded, the MLP's rounding points (gpt.py:141)."""
+    g = torch.Generator(device="cuda").manual_seed(20 + m)
+    d, f = 1024, 4096
+    x = torch.randn(m, d, device="cuda", generator=g).to(torch.bfloat16)
+    w1 = (torch.randn(d, f, device="cuda", generator=g) / 32).to(torch.bfloat16)
+    u = torch.empty(m, f, dtype=torch.bfloat16, device="cuda")
+    a = torch.empty_like(u)
+    nat.check(nat.lib().ferrite_gemm_epilogue(nat.stream_ptr(), x.data_ptr(), w1.data_ptr(), u.data_ptr(), m, f, d, d, f, f, 0, 0, 1,
+                                              a.data_ptr(), f))
+    torch.cuda.synchronize()
+    ref = x.float() @ w1.float()
+    torch.testing.assert_close(u.float(), ref, rtol=2**-7, atol=1e-3)
+    ga = torch.nn.functional.gelu(u.float(), approximate="tanh")
+    torch.testing.assert_close(a.float(), ga, rtol=2**-7, atol=1e-3)
+    assert torch.equal(u, _gemm_kn(x, w1, torch.bfloat16))  # same kernel, same sums as the plain product
