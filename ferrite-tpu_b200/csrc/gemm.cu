@@ -35,8 +35,10 @@
 // Reference: src/ferrite/kernels/matmul.py of anxnd2211/ferrite-tpu
 // (_matmul_kernel :27-38, _matmul_impl :52-86, VJP :99-104).
 #include <algorithm>
-#include <type_traits>
 #include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -836,97 +838,23 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// ---------------------------------------------------------------------------
-// Skinny products: 16-bit A with at most kSkinnyM rows (K-major), B stored [N][K]
-// (trans_b), f32 accumulation -- the serving prefill's LM head over the last position
-// of each sequence (M = batch).  Below the tensor-core path's 128-row minimum these
-// would otherwise run the 128 x 128 CUDA-core tiles, 16x redundant at M = 8; here the
-// cost is reading B once.  A CTA stages all of A in shared memory; each warp takes four
-// output columns at a time, its lanes splitting K into 8-element vectors read straight
-// from B's rows, and reduces the f32 partial sums across the warp at the end.
-// ---------------------------------------------------------------------------
-constexpr int kSkinnyM = 16;
-constexpr int kSkinnyThreads = 256;
-constexpr int kSkinnyMaxSmem = 96 * 1024;
-
-template <typename TA, typename TC, int MR>
-__global__ void __launch_bounds__(kSkinnyThreads)
-    gemm_skinny_kernel(const TA* __restrict__ a, const TA* __restrict__ b, TC* __restrict__ c, int m,
-                       int n, int k, int64_t lda, int64_t ldb, int64_t ldc) {
-  extern __shared__ __align__(16) uint8_t skinny_smem[];
-  TA* sa = reinterpret_cast<TA*>(skinny_smem);  // [MR][k], rows past m zero
-  pdl_launch_dependents();
-  pdl_wait();
-  const int kv = k / 8;  // 16-byte vectors per row
-  for (int idx = threadIdx.x; idx < MR * kv; idx += blockDim.x) {
-    const int r = idx / kv, v = idx - r * kv;
-    uint4 val = make_uint4(0, 0, 0, 0);
-    if (r < m) val = ld_v4(a + (int64_t)r * lda + (int64_t)v * 8);
-    *reinterpret_cast<uint4*>(sa + (int64_t)r * k + (int64_t)v * 8) = val;
-  }
-  __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int quads = (n + 3) / 4;
-  for (int qd = blockIdx.x * (kSkinnyThreads / 32) + warp; qd < quads; qd += gridDim.x * (kSkinnyThreads / 32)) {
-    const int n0 = qd * 4;
-    float acc[MR][4];
-#pragma unroll
-    for (int r = 0; r < MR; ++r)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) acc[r][j] = 0.f;
-    for (int v = lane; v < kv; v += 32) {
-      float bf[4][8];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint4 bv = make_uint4(0, 0, 0, 0);
-        if (n0 + j < n) bv = ld_v4(b + (int64_t)(n0 + j) * ldb + (int64_t)v * 8);
-        const TA* e = reinterpret_cast<const TA*>(&bv);
-#pragma unroll
-        for (int t = 0; t < 8; ++t) bf[j][t] = DT<TA>::to_f(e[t]);
-      }
-#pragma unroll
-      for (int r = 0; r < MR; ++r) {
-        const uint4 av = *reinterpret_cast<const uint4*>(sa + (int64_t)r * k + (int64_t)v * 8);
-        const TA* e = reinterpret_cast<const TA*>(&av);
-#pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          const float x = DT<TA>::to_f(e[t]);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) acc[r][j] = fmaf(x, bf[j][t], acc[r][j]);
-        }
-      }
-    }
-#pragma unroll
-    for (int r = 0; r < MR; ++r)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float s = acc[r][j];
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-        acc[r][j] = s;
-      }
-    // lane (r * 4 + j) % 32 writes element (r, n0 + j)
-#pragma unroll
-    for (int r = 0; r < MR; ++r)
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        if (lane == ((r * 4 + j) & 31) && r < m && n0 + j < n) c[(int64_t)r * ldc + n0 + j] = DT<TC>::from_f(acc[r][j]);
-  }
-}
+constexpr int kSkinnyM = 16;  // rows of A up to which the skinny kernel runs
 
 // ---------------------------------------------------------------------------
-// Skinny products with B stored [K][N] (no transpose): the decode step's linears,
-// y = x W with x [m <= 16, K] and W [K, N] row-major.  The cost is reading W once,
-// and at these sizes (2-8 MB per matrix) nearly all of W has to be in flight at
+// Skinny products, at most 16 rows of A (below the tensor-core path's 128-row tiles,
+// which would be 16x redundant at 8 rows): the decode step's linears, y = x W with x
+// [m <= 16, K] and W stored [K][N] row-major, and the tied LM head of decode and
+// prefill, y = h E^T with E stored [N][K] (trans_b).  The cost is reading W once, and
+// at these sizes (2-8 MB per layer matrix) nearly all of W has to be in flight at
 // once.  A cluster of `cs` CTAs owns 64 output columns and splits K between its CTAs;
-// each CTA streams its rows of the 64-column strip (128 bytes per row) through a
-// two-stage shared-memory ring with 16-byte cp.async copies (kKnStageRows rows, 32 KB,
-// per stage: two stages hold the CTA's whole slice for K / cs <= 512), the 16-byte
-// chunks of a row XOR-swizzled by the row index.  The products run on mma.sync
-// m16n8k16 with the roles turned around, y^T = W^T x^T: W^T is the 16 x 16 A operand
-// (ldmatrix.trans straight from the [K][N] rows, conflict-free thanks to the
-// swizzle), x^T the 16 x 8 B operand (x kept 16-bit in shared memory, rows padded
-// by 16 bytes), f32 accumulators.  The arithmetic is negligible either way; one MMA
+// each CTA streams its slice of the 64-column strip through a two-stage shared-memory
+// ring with 16-byte cp.async copies (32 KB per stage: two stages hold the CTA's whole
+// slice for K / cs <= 512), the 16-byte chunks of a row XOR-swizzled by the row
+// index.  The products run on mma.sync m16n8k16 with the roles turned around,
+// y^T = W^T x^T: W^T is the 16 x 16 A operand (ldmatrix.trans straight from [K][N]
+// rows, plain ldmatrix from [N][K] rows; conflict-free thanks to the swizzle), x^T
+// the 16 x 8 B operand (x kept 16-bit in shared memory, rows padded by 16 bytes),
+// f32 accumulators.  The arithmetic is negligible either way; one MMA
 // replaces 2048 FFMAs plus their conversions and shared-memory reads, which on CUDA
 // cores made these launches issue-bound.  Warps take interleaved 16-row steps; the
 // CTA sums its warps' tiles in shared memory, and the cluster's CTAs sum the partial
@@ -951,7 +879,7 @@ constexpr int kKnAUnits = 4;     // 16-byte units of x loaded per thread before 
 constexpr int kKnRingBytes = kKnStages * kKnStageRows * kKnTileN * 2;
 __host__ __device__ constexpr int kn_x_bytes(int kper, int mr) { return (mr * (kper + 8) * 2 + 15) / 16 * 16; }
 __host__ __device__ constexpr int kn_smem_bytes(int kper, int mr) {
-  return kKnRingBytes + kn_x_bytes(kper, mr) + (kKnWarps + 1) * mr * kKnTileN * 4;
+  return 1024 /*alignment slack*/ + kKnRingBytes + kn_x_bytes(kper, mr) + (kKnWarps + 1) * mr * kKnTileN * 4;
 }
 
 __device__ __forceinline__ uint32_t cluster_nctarank() {
@@ -978,6 +906,11 @@ __device__ __forceinline__ void ldmatrix_x4_trans(const void* p, uint32_t (&r)[4
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                : "r"(smem_u32(p)));
 }
+__device__ __forceinline__ void ldmatrix_x4(const void* p, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
 // d += a b, m16n8k16, 16-bit operands (A row-major, B column-major), f32 accumulators.
 template <typename TA>
 __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
@@ -994,31 +927,65 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4],
 }
 
 // EPI: kEpiNone (C = acc) or kEpiGelu (C = u = round(acc), aux = round(gelu_tanh(u))).
-template <typename TA, typename TC, int MR, int EPI>
-__global__ void __launch_bounds__(kKnThreads)
+// BNK: B stored [N][K] (trans_b) instead of [K][N]: a stage then holds the strip's 64
+// rows of N, kKnStageRows elements of K each, as four 64-element column blocks of 128-byte
+// rows (chunks swizzled by the row), and the W^T operand loads without the transpose.
+// TMA: stages arrive as 2-D tiled TMA copies (128-byte swizzle, which is the chunk ^
+// row % 8 layout above) completing on one mbarrier per stage -- a handful of
+// instructions per stage and no per-SM limit on 16-byte copies in flight; else as
+// 16-byte cp.async copies (shapes smaller than a TMA box).
+template <typename TA, typename TC, int MR, int EPI, bool BNK, bool TMA>
+__global__ void __launch_bounds__(kKnThreads, 2)
     gemm_skinny_kn_kernel(const TA* __restrict__ a, const TA* __restrict__ b, TC* __restrict__ c, int m,
                           int n, int k, int kper, int64_t lda, int64_t ldb, int64_t ldc, int a_vec,
-                          TC* __restrict__ aux, int64_t ld_aux) {
+                          TC* __restrict__ aux, int64_t ld_aux, const __grid_constant__ CUtensorMap tmap_b,
+                          int box_rows) {
   constexpr int NG = MR / 8;  // 8-row groups of x (MMA N = 8)
-  extern __shared__ __align__(128) uint8_t kn_smem[];
-  TA* ring = reinterpret_cast<TA*>(kn_smem);  // [kKnStages][kKnStageRows][64], chunks swizzled
+  extern __shared__ uint8_t kn_smem_raw[];
+  // 1024-byte aligned base: the 128-byte swizzle pattern repeats every 1024 bytes
+  uint8_t* kn_smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(kn_smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full_bar[kKnStages];
+  __shared__ int abort_flag;
+  volatile int* abort = &abort_flag;
+  TA* ring = reinterpret_cast<TA*>(kn_smem);  // [kKnStages][kKnStageRows * 64], chunks swizzled
   TA* sx = reinterpret_cast<TA*>(kn_smem + kKnRingBytes);
   float* red = reinterpret_cast<float*>(kn_smem + kKnRingBytes + kn_x_bytes(kper, MR));
   float* part = red + kKnWarps * MR * kKnTileN;
   const int ldx = kper + 8;
   const int cs = (int)cluster_nctarank();
   const int rank = (int)cluster_ctarank();
-  const int col0 = (int)(blockIdx.x / cs) * kKnTileN;
+  // persistent: cluster q takes the 64-column tiles q, q + clusters, ...; every CTA of
+  // a cluster walks the same tiles, so the cluster barriers below pair up
+  const int tiles = (n + kKnTileN - 1) / kKnTileN;
+  const int cluster_id = (int)(blockIdx.x / cs), clusters = (int)(gridDim.x / cs);
+  const int my_tiles = cluster_id < tiles ? (tiles - 1 - cluster_id) / clusters + 1 : 0;
+  int col0 = cluster_id * kKnTileN;
   const int k0 = rank * kper;
   const int kn = max(0, min(k - k0, kper));  // rows of W this CTA reads
   const int nst = (kn + kKnStageRows - 1) / kKnStageRows;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, tig = lane & 3;
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    if constexpr (TMA) {
+      mbar_init(&full_bar[0], 1);
+      mbar_init(&full_bar[1], 1);
+      fence_mbar_init();
+      tma_prefetch_desc(&tmap_b);
+    }
+  }
+  __syncthreads();
   pdl_launch_dependents();
   // Bring this CTA's strip of W into L2 while the previous kernel finishes (a launch
   // that follows through programmatic dependent launch starts early).  A prefetch
   // returns no data, so it is safe even if that kernel writes W: L2 keeps the newer lines.
-  if (col0 < n) {
+  if constexpr (BNK) {
+    if (kn > 0)  // one row of N per thread: kn elements of K (a multiple of 8)
+      for (int r = threadIdx.x; r < kKnTileN && col0 + r < n; r += kKnThreads)
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(b + (int64_t)(col0 + r) * ldb + k0),
+                     "r"((uint32_t)kn * 2)
+                     : "memory");
+  } else if (col0 < n) {
     const uint32_t bytes = (uint32_t)min(kKnTileN, n - col0) * 2;  // a multiple of 16
     for (int r = threadIdx.x; r < kn; r += kKnThreads)
       asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(b + (int64_t)(k0 + r) * ldb + col0), "r"(bytes)
@@ -1026,25 +993,62 @@ __global__ void __launch_bounds__(kKnThreads)
   }
   pdl_wait();
 
-  // stage st <- rows [bt * kKnStageRows, +kKnStageRows) of this CTA's slice, 16 bytes
-  // (8 columns) per copy, chunk ch of row r at chunk ch ^ (r % 8); rows past the slice
-  // and columns past n are zero-filled
-  auto issue = [&](int st, int bt) {
+  // stage st <- rows [bt * kKnStageRows, +kKnStageRows) of this CTA's slice of the
+  // strip at column c0, 16 bytes (8 columns) per copy, chunk ch of row r at chunk
+  // ch ^ (r % 8); rows past the slice and columns past n are zero-filled
+  auto issue = [&](int st, int bt, int c0) {
     TA* dst = ring + st * kKnStageRows * kKnTileN;
+    if constexpr (TMA) {
+      // one thread: the stage's box(es); the barrier expects every byte they write
+      // (zero fill past the tensor's edge included)
+      if (threadIdx.x == 0) {
+        if constexpr (BNK) {
+          const int boxes = min(kKnStageRows / 64, (kn - bt * kKnStageRows + 63) / 64);
+          mbar_arrive_expect_tx(&full_bar[st], (uint32_t)boxes * 64 * kKnTileN * 2);
+          for (int j = 0; j < boxes; ++j)
+            tma_load_2d(dst + j * 64 * kKnTileN, &tmap_b, &full_bar[st], k0 + bt * kKnStageRows + j * 64, c0);
+        } else {
+          mbar_arrive_expect_tx(&full_bar[st], (uint32_t)box_rows * kKnTileN * 2);
+          tma_load_2d(dst, &tmap_b, &full_bar[st], c0, k0 + bt * box_rows);
+        }
+      }
+      return;
+    }
 #pragma unroll
     for (int i = 0; i < kKnStageRows * 8 / kKnThreads; ++i) {
       const int ci = i * kKnThreads + threadIdx.x;
-      const int r = ci >> 3, ch = ci & 7;
-      const int kk = bt * kKnStageRows + r, col = col0 + ch * 8;
-      const bool ok = kk < kn && col < n;  // n % 8 == 0: a chunk is all in or all out
-      const TA* src = ok ? b + (int64_t)(k0 + kk) * ldb + col : b;
-      cp_async16_zfill(dst + r * kKnTileN + ((ch ^ (r & 7)) << 3), src, ok ? 16 : 0);
+      if constexpr (BNK) {
+        // row nl of the strip, chunk ch (8 elements of K) at chunk ch ^ (nl % 8);
+        // kn % 8 == 0: a chunk is all in or all out
+        const int nl = ci >> 5, ch = ci & 31;
+        const int kk = bt * kKnStageRows + ch * 8;
+        const bool ok = kk < kn && c0 + nl < n;
+        const TA* src = ok ? b + (int64_t)(c0 + nl) * ldb + k0 + kk : b;
+        cp_async16_zfill(dst + (ch >> 3) * 64 * kKnTileN + nl * 64 + (((ch & 7) ^ (nl & 7)) << 3), src, ok ? 16 : 0);
+      } else {
+        const int r = ci >> 3, ch = ci & 7;
+        const int kk = bt * kKnStageRows + r, col = c0 + ch * 8;
+        const bool ok = kk < kn && col < n;  // n % 8 == 0: a chunk is all in or all out
+        const TA* src = ok ? b + (int64_t)(k0 + kk) * ldb + col : b;
+        cp_async16_zfill(dst + r * kKnTileN + ((ch ^ (r & 7)) << 3), src, ok ? 16 : 0);
+      }
     }
   };
-  if (nst > 0) issue(0, 0);
-  cp_async_commit_group();
-  if (nst > 1) issue(1, 1);
-  cp_async_commit_group();
+  // the ring runs over the CTA's batches of all its tiles in one sequence: batch G is
+  // batch G % nst of tile G / nst, in stage G % 2, issued two batches ahead, so the next
+  // tile's copies fly while this tile is reduced
+  const int total = my_tiles * nst;
+  int issued = 0;  // batches whose copies were started (thread 0's count under TMA)
+  auto issue_g = [&](int gb) {
+    if (gb < total && !*abort) {
+      issue(gb & 1, gb % nst, (cluster_id + (gb / nst) * clusters) * kKnTileN);
+      issued = gb + 1;
+    }
+  };
+  issue_g(0);
+  if constexpr (!TMA) cp_async_commit_group();
+  issue_g(1);
+  if constexpr (!TMA) cp_async_commit_group();
 
   // x's rows [k0, k0 + kper) -> sx (zero past m and past kn); a pass issues all its
   // loads before its stores
@@ -1077,73 +1081,102 @@ __global__ void __launch_bounds__(kKnThreads)
     }
   }
 
-  float acc[4][NG][4];
+  int gb = 0;  // batches consumed
+  for (int tl = 0; tl < my_tiles; ++tl, col0 += clusters * kKnTileN) {
+    float acc[4][NG][4];
 #pragma unroll
-  for (int s4 = 0; s4 < 4; ++s4)
+    for (int s4 = 0; s4 < 4; ++s4)
 #pragma unroll
-    for (int ng = 0; ng < NG; ++ng)
+      for (int ng = 0; ng < NG; ++ng)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) acc[s4][ng][e] = 0.f;
-  for (int bt = 0; bt < nst; ++bt) {
-    cp_async_wait_1();  // this stage's group has landed (the newest may still fly)
-    __syncthreads();    // ... for every thread's copies, and x's rows are staged
-    const TA* st = ring + (bt & 1) * kKnStageRows * kKnTileN;
-    const int rows = min(kKnStageRows, kn - bt * kKnStageRows);
-    for (int ks = warp; ks * 16 < rows; ks += kKnWarps) {
-      const int kl = ks * 16;
-      const int kx = bt * kKnStageRows + kl;
-      uint32_t bx[NG][2];
-#pragma unroll
-      for (int ng = 0; ng < NG; ++ng) {
-        const TA* xp = sx + (ng * 8 + g) * ldx + kx + tig * 2;
-        bx[ng][0] = *reinterpret_cast<const uint32_t*>(xp);
-        bx[ng][1] = *reinterpret_cast<const uint32_t*>(xp + 8);
+        for (int e = 0; e < 4; ++e) acc[s4][ng][e] = 0.f;
+    for (int bt = 0; bt < nst; ++bt, ++gb) {
+      bool landed = true;
+      if constexpr (TMA) {
+        landed = !*abort && mbar_wait(&full_bar[gb & 1], (uint32_t)(gb >> 1) & 1u, abort, 130);
+      } else {
+        cp_async_wait_1();  // this stage's group has landed (the newest may still fly)
       }
-      const int row = kl + (lane & 7) + ((lane >> 4) << 3);
+      __syncthreads();  // ... for every thread's copies, and x's rows are staged
+      const TA* st = ring + (gb & 1) * kKnStageRows * kKnTileN;
+      const int rows = landed ? min(kKnStageRows, kn - bt * kKnStageRows) : 0;
+      for (int ks = warp; ks * 16 < rows; ks += kKnWarps) {
+        const int kl = ks * 16;
+        const int kx = bt * kKnStageRows + kl;
+        uint32_t bx[NG][2];
 #pragma unroll
-      for (int s4 = 0; s4 < 4; ++s4) {
-        const int chunk = s4 * 2 + ((lane >> 3) & 1);
-        uint32_t wa[4];
-        ldmatrix_x4_trans(st + row * kKnTileN + ((chunk ^ (row & 7)) << 3), wa);
+        for (int ng = 0; ng < NG; ++ng) {
+          const TA* xp = sx + (ng * 8 + g) * ldx + kx + tig * 2;
+          bx[ng][0] = *reinterpret_cast<const uint32_t*>(xp);
+          bx[ng][1] = *reinterpret_cast<const uint32_t*>(xp + 8);
+        }
 #pragma unroll
-        for (int ng = 0; ng < NG; ++ng) mma_16816<TA>(acc[s4][ng], wa, bx[ng]);
+        for (int s4 = 0; s4 < 4; ++s4) {
+          uint32_t wa[4];
+          if constexpr (BNK) {
+            // matrix q = lane / 8: rows of N s4*16 + (q & 1) * 8 + lane % 8, K chunk ks*2 + q / 2
+            const int nl = s4 * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+            const int chunk = ks * 2 + (lane >> 4);  // 8-element chunk of the stage's K
+            ldmatrix_x4(st + (chunk >> 3) * 64 * kKnTileN + nl * 64 + (((chunk & 7) ^ (nl & 7)) << 3), wa);
+          } else {
+            // matrix q = lane / 8: rows of K kl + (q / 2) * 8 + lane % 8, N chunk s4*2 + q % 2
+            const int row = kl + (lane & 7) + ((lane >> 4) << 3);
+            const int chunk = s4 * 2 + ((lane >> 3) & 1);
+            ldmatrix_x4_trans(st + row * kKnTileN + ((chunk ^ (row & 7)) << 3), wa);
+          }
+#pragma unroll
+          for (int ng = 0; ng < NG; ++ng) mma_16816<TA>(acc[s4][ng], wa, bx[ng]);
+        }
       }
+      __syncthreads();  // the stage is free again
+      issue_g(gb + 2);
+      if constexpr (!TMA) cp_async_commit_group();
     }
-    __syncthreads();  // the stage is free again
-    if (bt + 2 < nst) issue(bt & 1, bt + 2);
-    cp_async_commit_group();
-  }
 
-  // accumulator (W column n0 + g [+8], x row tig*2 + e) -> the warp's tile, then the
-  // warps' tiles -> the CTA's partial tile
+    // accumulator (W column n0 + g [+8], x row tig*2 + e) -> the warp's tile, then the
+    // warps' tiles -> the CTA's partial tile
 #pragma unroll
-  for (int s4 = 0; s4 < 4; ++s4)
+    for (int s4 = 0; s4 < 4; ++s4)
 #pragma unroll
-    for (int ng = 0; ng < NG; ++ng)
+      for (int ng = 0; ng < NG; ++ng)
 #pragma unroll
-      for (int h = 0; h < 2; ++h)
+        for (int h = 0; h < 2; ++h)
 #pragma unroll
-        for (int e = 0; e < 2; ++e)
-          red[(warp * MR + ng * 8 + tig * 2 + e) * kKnTileN + s4 * 16 + g + h * 8] = acc[s4][ng][h * 2 + e];
-  __syncthreads();
-  for (int v = threadIdx.x; v < MR * kKnTileN; v += kKnThreads) {
-    float s = 0.f;
+          for (int e = 0; e < 2; ++e)
+            red[(warp * MR + ng * 8 + tig * 2 + e) * kKnTileN + s4 * 16 + g + h * 8] = acc[s4][ng][h * 2 + e];
+    __syncthreads();
+    for (int v = threadIdx.x; v < MR * kKnTileN; v += kKnThreads) {
+      float s = 0.f;
 #pragma unroll
-    for (int w = 0; w < kKnWarps; ++w) s += red[w * MR * kKnTileN + v];
-    part[v] = s;
+      for (int w = 0; w < kKnWarps; ++w) s += red[w * MR * kKnTileN + v];
+      part[v] = s;
+    }
+    if (cs > 1) cluster_sync_all();  // every CTA's partial tile is visible to the cluster
+    else __syncthreads();
+    const int per = MR * kKnTileN / cs;  // cs is a power of two <= 8
+    for (int v = rank * per + threadIdx.x; v < (rank + 1) * per; v += kKnThreads) {
+      const int r = v / kKnTileN, cc = col0 + v % kKnTileN;
+      if (r >= m || cc >= n) continue;
+      float s = 0.f;
+      for (int q = 0; q < cs; ++q) s += ld_shared_cluster_f32(mapa_shared(part + v, (uint32_t)q));
+      const TC u = DT<TC>::from_f(s);
+      c[(int64_t)r * ldc + cc] = u;
+      if constexpr (EPI == kEpiGelu) aux[(int64_t)r * ld_aux + cc] = DT<TC>::from_f(gelu_tanh_f(DT<TC>::to_f(u)));
+    }
+    if (cs > 1) cluster_sync_all();  // no CTA rewrites (or leaves) its partial tile while another reads it
+    else __syncthreads();
   }
-  cluster_sync_all();  // every CTA's partial tile is visible to the cluster
-  const int per = MR * kKnTileN / cs;  // cs is a power of two <= 8
-  for (int v = rank * per + threadIdx.x; v < (rank + 1) * per; v += kKnThreads) {
-    const int r = v / kKnTileN, cc = col0 + v % kKnTileN;
-    if (r >= m || cc >= n) continue;
-    float s = 0.f;
-    for (int q = 0; q < cs; ++q) s += ld_shared_cluster_f32(mapa_shared(part + v, (uint32_t)q));
-    const TC u = DT<TC>::from_f(s);
-    c[(int64_t)r * ldc + cc] = u;
-    if constexpr (EPI == kEpiGelu) aux[(int64_t)r * ld_aux + cc] = DT<TC>::from_f(gelu_tanh_f(DT<TC>::to_f(u)));
+  // after an expired wait: let the copies still in flight land (bounded) before the
+  // shared memory they write is released.  No batch is issued after the abort, and at
+  // most two are in flight at once: the last two issued (a wait on a phase that has
+  // already completed returns at once).
+  if constexpr (TMA) {
+    if (threadIdx.x == 0 && *abort) {
+      int never = 0;
+      for (int q = max(0, issued - 2); q < issued; ++q)
+        (void)mbar_wait_ns(&full_bar[q & 1], (uint32_t)(q >> 1) & 1u, &never, 131, kWaitLimitNs);
+    }
   }
-  cluster_sync_all();  // no CTA leaves while another still reads its partial tile
 }
 
 // ---------------------------------------------------------------------------
@@ -1184,82 +1217,113 @@ static int pair_slots(int dev, int sms) {
   return cache[dev];
 }
 
-// Skinny path: 16-bit A with at most kSkinnyM rows stored K-major, B stored [N][K],
-// 16-byte aligned rows, K a multiple of 8 whose A rows fit the shared-memory budget.
-static bool skinny_ok(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int64_t lda,
-                      int64_t ldb, int trans_a, int trans_b) {
-  if (env_int("FERRITE_GEMM_SKINNY", 1) == 0) return false;
-  if (trans_a || !trans_b || m < 1 || m > kSkinnyM || n < 1 || k < 8 || k % 8) return false;
-  if ((reinterpret_cast<uintptr_t>(a) & 15u) || (reinterpret_cast<uintptr_t>(b) & 15u)) return false;
-  if ((lda * 2) % 16 || (ldb * 2) % 16) return false;
-  const int mr = m <= 8 ? 8 : kSkinnyM;
-  return (int64_t)mr * k * 2 <= kSkinnyMaxSmem && n <= 0x7fffffff;
-}
-
-template <typename TA, typename TC>
-static int launch_skinny(cudaStream_t s, const void* a, const void* b, void* c, int64_t m, int64_t n,
-                         int64_t k, int64_t lda, int64_t ldb, int64_t ldc) {
-  const bool small = m <= 8;
-  auto kern = small ? gemm_skinny_kernel<TA, TC, 8> : gemm_skinny_kernel<TA, TC, kSkinnyM>;
-  const int smem = (small ? 8 : kSkinnyM) * (int)k * 2;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return fail(FERRITE_LAUNCH_FAILED, "gemm: skinny smem attribute: %s", cudaGetErrorString(e));
-  }
-  const int64_t quads = (n + 3) / 4;
-  const int64_t want = (quads + kSkinnyThreads / 32 - 1) / (kSkinnyThreads / 32);
-  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(want, 2 * (int64_t)num_sms(current_device())));
-  (void)launch_pdl(kern, dim3(grid), dim3(kSkinnyThreads), smem, s, (const TA*)a, (const TA*)b, (TC*)c, (int)m,
-                   (int)n, (int)k, lda, ldb, ldc);
-  return check_launch("gemm_skinny");
-}
-
-// Cluster size and rows of W per CTA for the [K][N] skinny path: enough CTAs per
-// cluster that the ring holds a CTA's whole slice at once, then more (up to 8) while
-// the grid still fits the SMs once, so that most of W is in flight at once.
+// Cluster size and rows of K per CTA for the skinny path: K is split over a cluster
+// (up to 8 CTAs) while the grid of 64-column tiles would not cover half the SMs, so
+// that most of W is in flight at once, or while x's slice would not fit in shared
+// memory.  Wide outputs (the LM head's 32000 columns) keep whole K per CTA and are
+// covered by persistent clusters looping over their tiles.
 struct KnPlan {
   int cs, kper, smem;
 };
 static KnPlan kn_plan(int64_t m, int64_t n, int64_t k, int sms) {
   const int mr = m <= 8 ? 8 : kSkinnyM;
-  const int chunk = kKnStages * kKnStageRows;  // rows the ring holds at once
   const int64_t tiles = (n + kKnTileN - 1) / kKnTileN;
+  auto kper_for = [&](int c) {
+    const int64_t rows = (k + c - 1) / c;
+    return std::min<int64_t>((rows + kKnRowGrain - 1) / kKnRowGrain * kKnRowGrain, 1 << 20);
+  };
   int cs = 1;
-  while (cs < kKnMaxCluster && (k + cs - 1) / cs > chunk) cs *= 2;
-  while (cs < kKnMaxCluster && tiles * cs * 2 <= sms && (k + 2 * cs - 1) / (2 * cs) >= kKnRowGrain) cs *= 2;
-  const int64_t rows = (k + cs - 1) / cs;
-  const int64_t kper = std::min<int64_t>((rows + kKnRowGrain - 1) / kKnRowGrain * kKnRowGrain, 1 << 20);
-  return {cs, (int)kper, kn_smem_bytes((int)kper, mr)};
+  while (cs < kKnMaxCluster) {
+    const bool spread = tiles * cs * 2 <= sms && (k + 2 * cs - 1) / (2 * cs) >= kKnRowGrain;
+    const bool fits = kn_smem_bytes((int)kper_for(cs), mr) <= kKnMaxSmem;
+    if (!spread && fits) break;
+    cs *= 2;
+  }
+  const int kper = (int)kper_for(cs);
+  return {cs, kper, kn_smem_bytes(kper, mr)};
 }
 
-// [K][N] skinny path: 16-bit operands, A K-major with at most kSkinnyM rows, B stored
-// [K][N] with 16-byte aligned rows and N a multiple of 8; K bounded by shared memory.
+// Skinny path: 16-bit operands, A K-major with at most kSkinnyM rows; B with 16-byte
+// aligned rows (ldb a multiple of 8) stored [K][N] with N a multiple of 8, or [N][K]
+// (trans_b) with K a multiple of 8 (16-byte copies never straddle the edge); K bounded
+// by shared memory.
 static bool skinny_kn_ok(const void* b, int64_t m, int64_t n, int64_t k, int64_t ldb, int trans_a,
                          int trans_b) {
   if (env_int("FERRITE_GEMM_SKINNY", 1) == 0) return false;
-  if (trans_a || trans_b || m < 1 || m > kSkinnyM || n < 8 || n % 8 || k < 1) return false;
+  if (trans_a || m < 1 || m > kSkinnyM || n < 1 || k < 1) return false;
+  if (trans_b ? k % 8 != 0 : n % 8 != 0) return false;
   if ((reinterpret_cast<uintptr_t>(b) & 15u) || ldb % 8) return false;
   if (n > 0x7fffffff || k > 0x7fffffff) return false;
   return kn_plan(m, n, k, num_sms(current_device())).smem <= kKnMaxSmem;
 }
 
+// Clusters of `cs` CTAs of `kern` with `smem` bytes each that fit on the device at
+// once (cached per kernel, cluster size, shared memory and device).
+static int kn_cluster_slots(const void* kern, int cs, int smem) {
+  struct Entry {
+    const void* f;
+    int cs, smem, dev, n;
+  };
+  static std::mutex mu;
+  static Entry cache[64];
+  static int used = 0;
+  const int dev = current_device();
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < used; ++i)
+    if (cache[i].f == kern && cache[i].cs == cs && cache[i].smem == smem && cache[i].dev == dev) return cache[i].n;
+  int n = max_active_clusters(kern, dim3(kKnThreads), (size_t)smem, (unsigned)cs);
+  if (n <= 0) {
+    (void)cudaGetLastError();
+    n = std::max(1, num_sms(dev) / cs);
+  }
+  if (used < 64) cache[used++] = {kern, cs, smem, dev, n};
+  return n;
+}
+
 template <typename TA, typename TC, int EPI = kEpiNone>
 static int launch_skinny_kn(cudaStream_t s, const void* a, const void* b, void* c, int64_t m, int64_t n,
-                            int64_t k, int64_t lda, int64_t ldb, int64_t ldc, void* aux = nullptr,
-                            int64_t ld_aux = 0) {
+                            int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int trans_b,
+                            void* aux = nullptr, int64_t ld_aux = 0) {
   const KnPlan pl = kn_plan(m, n, k, num_sms(current_device()));
-  auto kern = m <= 8 ? gemm_skinny_kn_kernel<TA, TC, 8, EPI> : gemm_skinny_kn_kernel<TA, TC, kSkinnyM, EPI>;
-  if (pl.smem > 48 * 1024) {
+  // TMA stages when every box fits inside the tensor: [K][N] boxes are 64 columns x
+  // min(256, rows per CTA) rows, [N][K] boxes 64 x 64
+  const int box_rows = std::min(kKnStageRows, pl.kper);
+  const bool tma = trans_b ? (k >= 64 && n >= kKnTileN) : (n >= kKnTileN && k >= box_rows);
+  using Kern = void (*)(const TA*, const TA*, TC*, int, int, int, int, int64_t, int64_t, int64_t, int, TC*, int64_t,
+                        const CUtensorMap, int);
+  Kern kern;
+  if (trans_b) {
+    if (tma) kern = m <= 8 ? gemm_skinny_kn_kernel<TA, TC, 8, EPI, true, true> : gemm_skinny_kn_kernel<TA, TC, kSkinnyM, EPI, true, true>;
+    else kern = m <= 8 ? gemm_skinny_kn_kernel<TA, TC, 8, EPI, true, false> : gemm_skinny_kn_kernel<TA, TC, kSkinnyM, EPI, true, false>;
+  } else {
+    if (tma) kern = m <= 8 ? gemm_skinny_kn_kernel<TA, TC, 8, EPI, false, true> : gemm_skinny_kn_kernel<TA, TC, kSkinnyM, EPI, false, true>;
+    else kern = m <= 8 ? gemm_skinny_kn_kernel<TA, TC, 8, EPI, false, false> : gemm_skinny_kn_kernel<TA, TC, kSkinnyM, EPI, false, false>;
+  }
+  // (a runtime call first: it makes the device's primary context current on this
+  // thread -- e.g. an autograd worker -- which the tensor-map encoder needs)
+  {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem);
-    if (e != cudaSuccess) return fail(FERRITE_LAUNCH_FAILED, "gemm: skinny [K][N] smem attribute: %s", cudaGetErrorString(e));
+    if (e != cudaSuccess) return fail(FERRITE_LAUNCH_FAILED, "gemm: skinny smem attribute: %s", cudaGetErrorString(e));
+  }
+  CUtensorMap tmap;
+  std::memset(&tmap, 0, sizeof(tmap));
+  if (tma) {
+    const CUtensorMapDataType dt = std::is_same<TA, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                                         : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const int rc = trans_b ? make_tmap_2d(&tmap, b, dt, 2, (uint64_t)k, (uint64_t)n, (uint64_t)ldb * 2, 64, kKnTileN,
+                                          CU_TENSOR_MAP_SWIZZLE_128B)
+                           : make_tmap_2d(&tmap, b, dt, 2, (uint64_t)n, (uint64_t)k, (uint64_t)ldb * 2, kKnTileN,
+                                          (uint32_t)box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
   }
   // x's rows as 16-byte vectors: aligned base and row stride (kper, hence k0, is a multiple of 16)
   const int a_vec = (reinterpret_cast<uintptr_t>(a) & 15u) == 0 && lda % 8 == 0;
+  // persistent clusters: at most as many as fit at once, each looping over its tiles
   const int64_t tiles = (n + kKnTileN - 1) / kKnTileN;
-  if (tiles * pl.cs > 0x7fffffff) return fail(FERRITE_BAD_SHAPE, "gemm: N too large for the skinny path");
-  (void)launch_pdl_cluster(kern, dim3((unsigned)(tiles * pl.cs)), dim3(kKnThreads), (size_t)pl.smem, s,
+  const int64_t clusters = std::min<int64_t>(tiles, kn_cluster_slots((const void*)kern, pl.cs, pl.smem));
+  (void)launch_pdl_cluster(kern, dim3((unsigned)(clusters * pl.cs)), dim3(kKnThreads), (size_t)pl.smem, s,
                            (unsigned)pl.cs, (const TA*)a, (const TA*)b, (TC*)c, (int)m, (int)n, (int)k,
-                           pl.kper, lda, ldb, ldc, a_vec, (TC*)aux, ld_aux);
+                           pl.kper, lda, ldb, ldc, a_vec, (TC*)aux, ld_aux, tmap, box_rows);
   return check_launch("gemm_skinny_kn");
 }
 
@@ -1517,10 +1581,10 @@ extern "C" int ferrite_gemm_epilogue(void* stream, const void* a, const void* b,
   if (m == 0 || n == 0) return FERRITE_OK;
   if (!a || !b || !c || !aux) return fail(FERRITE_BAD_SHAPE, "gemm_epilogue: null pointer");
   // decode-sized up-projections (at most 16 rows, W stored [K][N]): the skinny kernel
-  if (epilogue == kEpiGelu && k > 0 && !tc_eligible(a, b, m, n, k, lda, ldb, trans_a, trans_b) &&
+  if (epilogue == kEpiGelu && !trans_b && k > 0 && !tc_eligible(a, b, m, n, k, lda, ldb, trans_a, trans_b) &&
       skinny_kn_ok(b, m, n, k, ldb, trans_a, trans_b))
     return launch_skinny_kn<__nv_bfloat16, __nv_bfloat16, kEpiGelu>((cudaStream_t)stream, a, b, c, m, n, k, lda, ldb,
-                                                                     ldc, aux, ld_aux);
+                                                                     ldc, 0, aux, ld_aux);
   if (k == 0 || !tc_eligible(a, b, m, n, k, lda, ldb, trans_a, trans_b))
     return fail(FERRITE_UNSUPPORTED_DTYPE,
                 "gemm_epilogue: needs the tensor-core path (16-byte aligned operands and strides, "
@@ -1571,20 +1635,8 @@ extern "C" int ferrite_gemm_ws(void* stream, const void* a, const void* b, void*
     if (c_dtype == FERRITE_F32) return run_tc<false, float>(s, a, b, c, m, n, k, lda, ldb, ldc, trans_a, trans_b, workspace, workspace_bytes);
     return run_tc<false, __half>(s, a, b, c, m, n, k, lda, ldb, ldc, trans_a, trans_b, workspace, workspace_bytes);
   }
-  if (ab_dtype != FERRITE_F32 && skinny_ok(a, b, m, n, k, lda, ldb, trans_a, trans_b)) {
-#define SKINNY(TA, TC) launch_skinny<TA, TC>(s, a, b, c, m, n, k, lda, ldb, ldc)
-    if (ab_dtype == FERRITE_BF16) {
-      if (c_dtype == FERRITE_F32) return SKINNY(__nv_bfloat16, float);
-      if (c_dtype == FERRITE_BF16) return SKINNY(__nv_bfloat16, __nv_bfloat16);
-      return SKINNY(__nv_bfloat16, __half);
-    }
-    if (c_dtype == FERRITE_F32) return SKINNY(__half, float);
-    if (c_dtype == FERRITE_BF16) return SKINNY(__half, __nv_bfloat16);
-    return SKINNY(__half, __half);
-#undef SKINNY
-  }
   if (ab_dtype != FERRITE_F32 && skinny_kn_ok(b, m, n, k, ldb, trans_a, trans_b)) {
-#define SKINNY_KN(TA, TC) launch_skinny_kn<TA, TC>(s, a, b, c, m, n, k, lda, ldb, ldc)
+#define SKINNY_KN(TA, TC) launch_skinny_kn<TA, TC>(s, a, b, c, m, n, k, lda, ldb, ldc, trans_b)
     if (ab_dtype == FERRITE_BF16) {
       if (c_dtype == FERRITE_F32) return SKINNY_KN(__nv_bfloat16, float);
       if (c_dtype == FERRITE_BF16) return SKINNY_KN(__nv_bfloat16, __nv_bfloat16);

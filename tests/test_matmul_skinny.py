@@ -32,7 +32,8 @@ def _gemm_tb(a, b, out_dtype):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("m,n,k", [(1, 5, 8), (3, 1000, 1024), (8, 32000, 1024), (9, 777, 2048), (16, 4099, 3072), (17, 300, 512), (8, 64, 1001)])
+@pytest.mark.parametrize("m,n,k", [(1, 5, 8), (3, 1000, 1024), (8, 32000, 1024), (9, 777, 2048), (16, 4099, 3072), (8, 100, 520),
+                                   (16, 300, 8192), (17, 300, 512), (8, 64, 1001)])
 def test_skinny_matches_fp32_reference(dtype, m, n, k):
     g = torch.Generator(device="cuda").manual_seed(m * 1000 + n + k)
     a = torch.randn(m, k, device="cuda", generator=g).to(dtype)
@@ -78,9 +79,12 @@ def _gemm_kn(a, b, out_dtype):
 
 
 # decode linears of GPT d1024 (qkv, out, up, down), edges of the tile and of the cluster
-# split, K past one batch of loads per CTA (8192, 20000), and shapes that leave the path
+# split, K past one batch of loads per CTA (8192, 20000), more 64-column tiles than
+# clusters fit at once (32768, 20000: each cluster loops over several), and shapes that
+# leave the path
 KN_SHAPES = [(8, 3072, 1024), (8, 1024, 1024), (8, 4096, 1024), (8, 1024, 4096), (1, 8, 8), (3, 1000, 1000),
-             (9, 200, 777), (16, 4096, 8192), (8, 136, 20000), (17, 256, 512), (8, 1002, 64)]
+             (9, 200, 777), (16, 4096, 8192), (8, 136, 20000), (8, 32768, 1024), (4, 20000, 256), (17, 256, 512),
+             (8, 1002, 64)]
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
