@@ -108,6 +108,23 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int grp = warp * RPW + row_in_warp;
 
   pdl_launch_dependents();
+  // Pull this CTA's cache rows into L2 while the previous kernel finishes (a launch that
+  // follows through programmatic dependent launch starts early).  pos may still be in
+  // flight from an earlier kernel of the stream, so this read (relaxed) only steers a
+  // prefetch, which returns no data; the rows themselves are read after pdl_wait().
+  if ((int)threadIdx.x < 2) {
+    int64_t p0;
+    asm volatile("ld.relaxed.gpu.global.s64 %0, [%1];" : "=l"(p0) : "l"(pos + bi) : "memory");
+    if (p0 >= 0 && p0 < max_len) {
+      const int64_t n0 = p0 + 1, chunk0 = (n0 + csize - 1) / csize;
+      const int64_t b0 = min((int64_t)rank * chunk0, n0), e0 = min(b0 + chunk0, n0);
+      if (e0 > b0) {
+        const T* base = (threadIdx.x == 0 ? k_cache : v_cache) + (slice * max_len + b0) * D;
+        const int64_t bytes = min((e0 - b0) * D * (int64_t)sizeof(T), (int64_t)1 << 30);  // a multiple of 16
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base), "r"((uint32_t)bytes) : "memory");
+      }
+    }
+  }
   pdl_wait();  // the previous kernel in the stream has finished (it may have written q or the cache)
   float qf[EPV], acc[EPV];
   unpack<T>(ld_v4(q + bi * ld_new + hi * D + sub * EPV), qf);

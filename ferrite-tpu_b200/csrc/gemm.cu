@@ -1218,9 +1218,10 @@ static int pair_slots(int dev, int sms) {
 }
 
 // Cluster size and rows of K per CTA for the skinny path: K is split over a cluster
-// (up to 8 CTAs) while the grid of 64-column tiles would not cover half the SMs, so
-// that most of W is in flight at once, or while x's slice would not fit in shared
-// memory.  Wide outputs (the LM head's 32000 columns) keep whole K per CTA and are
+// (up to 8 CTAs) while the grid of 64-column tiles would not cover half the SMs and
+// each CTA keeps at least one full stage of rows (below that the cluster's fixed costs
+// win: 1024 x 1024 ran 6% faster on 4 CTAs than on 8), so that most of W is in flight
+// at once; or while x's slice would not fit in shared memory.  Wide outputs (the LM head's 32000 columns) keep whole K per CTA and are
 // covered by persistent clusters looping over their tiles.
 struct KnPlan {
   int cs, kper, smem;
@@ -1234,7 +1235,7 @@ static KnPlan kn_plan(int64_t m, int64_t n, int64_t k, int sms) {
   };
   int cs = 1;
   while (cs < kKnMaxCluster) {
-    const bool spread = tiles * cs * 2 <= sms && (k + 2 * cs - 1) / (2 * cs) >= kKnRowGrain;
+    const bool spread = tiles * cs * 2 <= sms && (k + 2 * cs - 1) / (2 * cs) >= kKnStageRows;
     const bool fits = kn_smem_bytes((int)kper_for(cs), mr) <= kKnMaxSmem;
     if (!spread && fits) break;
     cs *= 2;
