@@ -9,6 +9,12 @@ the same seeded prompts (prefill bucket 512) and prints one JSON line: per mode 
 median inter-token latency, tokens/s and time to first token; whether the graph and
 eager engines produced identical tokens; and how far the kernel and plain paths'
 greedy tokens agree (they round differently in bf16).
+
+``--breakdown`` instead times, per call, the kernels one decode step of that model runs
+(graph-replayed back to back over 24 distinct weights or inputs, as the 24 layers
+do): the four layer linears and the tied LM head on the skinny GEMM against
+``torch.matmul`` (cuBLAS) on the same bf16 operands, the fused residual-add + RMSNorm,
+and the cache attention at the engine's shape (512-slot cache, position 400).
 """
 
 from __future__ import annotations
@@ -28,7 +34,11 @@ def main(argv=None) -> None:
     ap.add_argument("--prompts", type=int, default=8)
     ap.add_argument("--prompt-len", type=int, default=400)
     ap.add_argument("--new", type=int, default=64, help="tokens generated per prompt in the timed run")
+    ap.add_argument("--breakdown", action="store_true", help="per-call kernel times of one decode step instead")
     a = ap.parse_args(argv)
+    if a.breakdown:
+        print(json.dumps(breakdown(a.prompts)), flush=True)
+        return
     if a.prompt_len + a.new > 512:
         raise SystemExit("prompt-len + new must fit the 512-token cache")
     cfg = GPTConfig(vocab_size=32000, seq_len=1024, d_model=1024, n_head=16, n_layer=24, d_ff=4096,
@@ -57,6 +67,68 @@ def main(argv=None) -> None:
     out["token_agreement_pallas_vs_xla"] = round(float(np.mean(tokens[0] == tokens[2])), 4)
     out["first_divergence_pallas_vs_xla"] = [int(np.argmax(r)) if r.any() else None for r in (tokens[0] != tokens[2])]
     print(json.dumps(out), flush=True)
+
+
+def _graph_us(fn, reps: int = 30) -> float:
+    """Microseconds per replay of ``fn`` captured as one CUDA graph (CUDA events, after warm-up)."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            fn()
+    torch.cuda.current_stream().wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps * 1000.0
+
+
+@torch.no_grad()
+def breakdown(batch: int = 8) -> dict:
+    """Per-call times (us) of the kernels of one decode step of GPT d1024 L24 with ``batch``
+    sequences; each call class replayed 24 times back to back with distinct operands."""
+    from ferrite.kernels.decode_attention import decode_attention
+    from ferrite.kernels.matmul import gemm
+    from ferrite.kernels.rmsnorm import rmsnorm
+
+    dev, bf = torch.device("cuda"), torch.bfloat16
+    out = {"config": {"model": "GPT d1024 L24 H16 V32000 bf16", "batch": batch, "cache": [24, batch, 16, 512, 64], "pos": 400,
+                      "timing": "CUDA graph of 24 calls, us per call"}}
+    x = torch.randn(batch, 4096, device=dev).to(bf)
+    for name, (k, n) in {"qkv": (1024, 3072), "out": (1024, 1024), "up": (1024, 4096), "down": (4096, 1024)}.items():
+        ws = [torch.randn(k, n, device=dev).to(bf) for _ in range(24)]
+        xk = x[:, :k]
+        ours = _graph_us(lambda: [gemm(xk, w) for w in ws]) / 24
+        ref = _graph_us(lambda: [torch.matmul(xk, w) for w in ws]) / 24
+        out[f"linear_{name}_{k}x{n}"] = {"skinny_us": round(ours, 2), "cublas_us": round(ref, 2),
+                                         "skinny_GBps": round(k * n * 2 / ours / 1e3, 1)}
+        del ws
+    e = torch.randn(32000, 1024, device=dev).to(bf)
+    y = x[:, :1024]
+    ours = _graph_us(lambda: gemm(y, e, trans_b=True, out_dtype=torch.float32))
+    ref = _graph_us(lambda: torch.matmul(y.float(), e.float().t()))
+    out["lm_head_32000x1024_f32_logits"] = {"skinny_us": round(ours, 2), "torch_f32_us": round(ref, 2)}
+    del e
+    hs = [torch.randn(batch, 1024, device=dev).to(bf) for _ in range(24)]
+    rs = [torch.randn(batch, 1024, device=dev).to(bf) for _ in range(24)]
+    wn = torch.ones(1024, device=dev)
+    out["add_rmsnorm_us"] = round(_graph_us(lambda: [rmsnorm(hs[i], wn, residual=rs[i], eps=1e-5) for i in range(24)]) / 24, 2)
+    kc = torch.randn(24, batch, 16, 512, 64, device=dev).to(bf)
+    vc = torch.randn_like(kc)
+    q = torch.randn(batch, 3, 16, 64, device=dev).to(bf)
+    pos = torch.full((batch,), 400, dtype=torch.long, device=dev)
+    out["cache_attention_us"] = round(_graph_us(
+        lambda: [decode_attention(q[:, 0], kc[i], vc[i], pos, scale=0.125, k_new=q[:, 1], v_new=q[:, 2]) for i in range(24)]) / 24, 2)
+    return out
 
 
 if __name__ == "__main__":
