@@ -43,6 +43,7 @@ constexpr int kStages = 3;
 // K/V staging ring per CTA: kStages batches x kUnroll rows x (K, V) x 16 bytes per thread.
 constexpr int kRingBytes = kStages * kUnroll * 2 * kThreads * 16;
 constexpr int kMaxCluster = 8;
+constexpr int kPrefetchBytes = 16 * 1024;  // per CTA, of K and of V, ahead of the launch wait
 constexpr float kLog2e = 1.4426950408889634f;
 
 // 16-byte global -> shared asynchronous copy (cached in L2 only), and its group
@@ -108,10 +109,13 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int grp = warp * RPW + row_in_warp;
 
   pdl_launch_dependents();
-  // Pull this CTA's cache rows into L2 while the previous kernel finishes (a launch that
-  // follows through programmatic dependent launch starts early).  pos may still be in
-  // flight from an earlier kernel of the stream, so this read (relaxed) only steers a
-  // prefetch, which returns no data; the rows themselves are read after pdl_wait().
+  // Pull the first of this CTA's cache rows into L2 while the previous kernel finishes
+  // (a launch that follows through programmatic dependent launch starts early): up to
+  // kPrefetchBytes of K and of V, what its first copies ask for.  Prefetching the whole
+  // range was slower at a full cache (it competes with the previous launch's traffic);
+  // this cap measured best.  pos may still be in flight from an earlier kernel of the
+  // stream, so this read (relaxed) only steers a prefetch, which returns no data; the
+  // rows themselves are read after pdl_wait().
   if ((int)threadIdx.x < 2) {
     int64_t p0;
     asm volatile("ld.relaxed.gpu.global.s64 %0, [%1];" : "=l"(p0) : "l"(pos + bi) : "memory");
@@ -120,7 +124,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int64_t b0 = min((int64_t)rank * chunk0, n0), e0 = min(b0 + chunk0, n0);
       if (e0 > b0) {
         const T* base = (threadIdx.x == 0 ? k_cache : v_cache) + (slice * max_len + b0) * D;
-        const int64_t bytes = min((e0 - b0) * D * (int64_t)sizeof(T), (int64_t)1 << 30);  // a multiple of 16
+        const int64_t bytes = min((e0 - b0) * D * (int64_t)sizeof(T), (int64_t)kPrefetchBytes);  // a multiple of 16
         asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base), "r"((uint32_t)bytes) : "memory");
       }
     }
