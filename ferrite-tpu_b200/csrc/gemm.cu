@@ -934,12 +934,24 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4],
 // row % 8 layout above) completing on one mbarrier per stage -- a handful of
 // instructions per stage and no per-SM limit on 16-byte copies in flight; else as
 // 16-byte cp.async copies (shapes smaller than a TMA box).
-template <typename TA, typename TC, int MR, int EPI, bool BNK, bool TMA>
+// NORM: A is the normalised sum of two rows, the decode step's residual-add + RMSNorm
+// folded in front of its product (rmsnorm.py:52-56 of the reference): h = x + r in f32,
+// y = round(h * rsqrt(mean(h^2) + eps) * w) is the MMA operand.  Every CTA reads the
+// whole rows (at most 16 x K, from L2) for the statistics, one warp per row in a fixed
+// order, then stages its own K slice of y; CTA 0 alone writes round(h) to h_out.
+struct KnNorm {
+  const void* r;    // residual rows (row stride lda), or null: h = x
+  const float* w;   // norm weight [K]
+  void* h_out;      // round(h) (row stride lda), or null; never overlaps x or r
+  float eps;
+};
+
+template <typename TA, typename TC, int MR, int EPI, bool BNK, bool TMA, bool NORM = false>
 __global__ void __launch_bounds__(kKnThreads, 2)
     gemm_skinny_kn_kernel(const TA* __restrict__ a, const TA* __restrict__ b, TC* __restrict__ c, int m,
                           int n, int k, int kper, int64_t lda, int64_t ldb, int64_t ldc, int a_vec,
                           TC* __restrict__ aux, int64_t ld_aux, const __grid_constant__ CUtensorMap tmap_b,
-                          int box_rows) {
+                          int box_rows, const KnNorm nrm) {
   constexpr int NG = MR / 8;  // 8-row groups of x (MMA N = 8)
   extern __shared__ uint8_t kn_smem_raw[];
   // 1024-byte aligned base: the 128-byte swizzle pattern repeats every 1024 bytes
@@ -1050,8 +1062,47 @@ __global__ void __launch_bounds__(kKnThreads, 2)
   issue_g(1);
   if constexpr (!TMA) cp_async_commit_group();
 
+  // NORM: per-row 1 / rms over the whole row of h (x + r), one warp per row; CTA 0
+  // also writes round(h).  (k % 8 == 0 and 16-byte aligned rows: checked on the host.)
+  __shared__ float s_inv[MR];
+  if constexpr (NORM) {
+    const TA* rr = static_cast<const TA*>(nrm.r);
+    TA* ho = static_cast<TA*>(nrm.h_out);
+    for (int row = warp; row < MR; row += kKnWarps) {
+      float ss = 0.f;
+      if (row < m) {
+        for (int v = lane; v < k / 8; v += 32) {
+          const uint4 xv = ld_v4(a + (int64_t)row * lda + v * 8);
+          float h[8];
+          const TA* xe = reinterpret_cast<const TA*>(&xv);
+#pragma unroll
+          for (int t = 0; t < 8; ++t) h[t] = DT<TA>::to_f(xe[t]);
+          if (rr) {
+            const uint4 rv = ld_v4(rr + (int64_t)row * lda + v * 8);
+            const TA* re = reinterpret_cast<const TA*>(&rv);
+#pragma unroll
+            for (int t = 0; t < 8; ++t) h[t] += DT<TA>::to_f(re[t]);
+          }
+#pragma unroll
+          for (int t = 0; t < 8; ++t) ss = fmaf(h[t], h[t], ss);
+          if (ho && blockIdx.x == 0) {
+            uint4 hv;
+            TA* he = reinterpret_cast<TA*>(&hv);
+#pragma unroll
+            for (int t = 0; t < 8; ++t) he[t] = DT<TA>::from_f(h[t]);
+            *reinterpret_cast<uint4*>(ho + (int64_t)row * lda + v * 8) = hv;
+          }
+        }
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+      if (lane == 0) s_inv[row] = rsqrtf(ss / (float)k + nrm.eps);
+    }
+    __syncthreads();
+  }
+
   // x's rows [k0, k0 + kper) -> sx (zero past m and past kn); a pass issues all its
-  // loads before its stores
+  // loads before its stores.  NORM: y's rows instead, from x, r and the weight.
   {
     const int vpr = kper / 8;
     const int units = MR * vpr;
@@ -1062,7 +1113,31 @@ __global__ void __launch_bounds__(kKnThreads, 2)
         const int id = base + u * kKnThreads + threadIdx.x;
         const int r = id / vpr, kk = (id - r * vpr) * 8;
         const TA* src = a + (int64_t)r * lda + k0 + kk;
-        if (id < units && r < m && a_vec && kk + 8 <= kn) {
+        if constexpr (NORM) {
+          // kn % 8 == 0 here (k % 8 == 0, k0 a multiple of 64): whole vectors or none
+          uint4 v = make_uint4(0u, 0u, 0u, 0u);
+          if (id < units && r < m && kk < kn) {
+            const uint4 x8 = ld_v4(src);
+            const TA* xe = reinterpret_cast<const TA*>(&x8);
+            float h[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t) h[t] = DT<TA>::to_f(xe[t]);
+            if (nrm.r) {
+              const uint4 r8 = ld_v4(static_cast<const TA*>(nrm.r) + (int64_t)r * lda + k0 + kk);
+              const TA* re = reinterpret_cast<const TA*>(&r8);
+#pragma unroll
+              for (int t = 0; t < 8; ++t) h[t] += DT<TA>::to_f(re[t]);
+            }
+            const float4 w0 = *reinterpret_cast<const float4*>(nrm.w + k0 + kk);
+            const float4 w1 = *reinterpret_cast<const float4*>(nrm.w + k0 + kk + 4);
+            const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+            const float inv = s_inv[r];
+            TA* ye = reinterpret_cast<TA*>(&v);
+#pragma unroll
+            for (int t = 0; t < 8; ++t) ye[t] = DT<TA>::from_f(h[t] * inv * wv[t]);
+          }
+          xv[u] = v;
+        } else if (id < units && r < m && a_vec && kk + 8 <= kn) {
           xv[u] = ld_v4(src);
         } else {
           uint4 v;
@@ -1281,24 +1356,24 @@ static int kn_cluster_slots(const void* kern, int cs, int smem) {
   return n;
 }
 
-template <typename TA, typename TC, int EPI = kEpiNone>
+template <typename TA, typename TC, int EPI = kEpiNone, bool NORM = false>
 static int launch_skinny_kn(cudaStream_t s, const void* a, const void* b, void* c, int64_t m, int64_t n,
                             int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int trans_b,
-                            void* aux = nullptr, int64_t ld_aux = 0) {
+                            void* aux = nullptr, int64_t ld_aux = 0, KnNorm nrm = KnNorm{nullptr, nullptr, nullptr, 0.f}) {
   const KnPlan pl = kn_plan(m, n, k, num_sms(current_device()));
   // TMA stages when every box fits inside the tensor: [K][N] boxes are 64 columns x
   // min(256, rows per CTA) rows, [N][K] boxes 64 x 64
   const int box_rows = std::min(kKnStageRows, pl.kper);
   const bool tma = trans_b ? (k >= 64 && n >= kKnTileN) : (n >= kKnTileN && k >= box_rows);
   using Kern = void (*)(const TA*, const TA*, TC*, int, int, int, int, int64_t, int64_t, int64_t, int, TC*, int64_t,
-                        const CUtensorMap, int);
+                        const CUtensorMap, int, const KnNorm);
   Kern kern;
   if (trans_b) {
-    if (tma) kern = m <= 8 ? gemm_skinny_kn_kernel<TA, TC, 8, EPI, true, true> : gemm_skinny_kn_kernel<TA, TC, kSkinnyM, EPI, true, true>;
-    else kern = m <= 8 ? gemm_skinny_kn_kernel<TA, TC, 8, EPI, true, false> : gemm_skinny_kn_kernel<TA, TC, kSkinnyM, EPI, true, false>;
+    if (tma) kern = m <= 8 ? gemm_skinny_kn_kernel<TA, TC, 8, EPI, true, true, NORM> : gemm_skinny_kn_kernel<TA, TC, kSkinnyM, EPI, true, true, NORM>;
+    else kern = m <= 8 ? gemm_skinny_kn_kernel<TA, TC, 8, EPI, true, false, NORM> : gemm_skinny_kn_kernel<TA, TC, kSkinnyM, EPI, true, false, NORM>;
   } else {
-    if (tma) kern = m <= 8 ? gemm_skinny_kn_kernel<TA, TC, 8, EPI, false, true> : gemm_skinny_kn_kernel<TA, TC, kSkinnyM, EPI, false, true>;
-    else kern = m <= 8 ? gemm_skinny_kn_kernel<TA, TC, 8, EPI, false, false> : gemm_skinny_kn_kernel<TA, TC, kSkinnyM, EPI, false, false>;
+    if (tma) kern = m <= 8 ? gemm_skinny_kn_kernel<TA, TC, 8, EPI, false, true, NORM> : gemm_skinny_kn_kernel<TA, TC, kSkinnyM, EPI, false, true, NORM>;
+    else kern = m <= 8 ? gemm_skinny_kn_kernel<TA, TC, 8, EPI, false, false, NORM> : gemm_skinny_kn_kernel<TA, TC, kSkinnyM, EPI, false, false, NORM>;
   }
   // (a runtime call first: it makes the device's primary context current on this
   // thread -- e.g. an autograd worker -- which the tensor-map encoder needs)
@@ -1324,7 +1399,7 @@ static int launch_skinny_kn(cudaStream_t s, const void* a, const void* b, void* 
   const int64_t clusters = std::min<int64_t>(tiles, kn_cluster_slots((const void*)kern, pl.cs, pl.smem));
   (void)launch_pdl_cluster(kern, dim3((unsigned)(clusters * pl.cs)), dim3(kKnThreads), (size_t)pl.smem, s,
                            (unsigned)pl.cs, (const TA*)a, (const TA*)b, (TC*)c, (int)m, (int)n, (int)k,
-                           pl.kper, lda, ldb, ldc, a_vec, (TC*)aux, ld_aux, tmap, box_rows);
+                           pl.kper, lda, ldb, ldc, a_vec, (TC*)aux, ld_aux, tmap, box_rows, nrm);
   return check_launch("gemm_skinny_kn");
 }
 
@@ -1567,6 +1642,55 @@ extern "C" int ferrite_gemm(void* stream, const void* a, const void* b, void* c,
                             int trans_a, int trans_b, int ab_dtype, int c_dtype) {
   return ferrite_gemm_ws(stream, a, b, c, m, n, k, lda, ldb, ldc, trans_a, trans_b, ab_dtype,
                          c_dtype, nullptr, 0);
+}
+
+// Residual-add + RMSNorm in front of a skinny product (the decode step): see the header.
+extern "C" int ferrite_gemm_rmsnorm(void* stream, const void* x, const void* r, const float* w_norm, float eps,
+                                    void* h_out, const void* b, void* c, int64_t m, int64_t n, int64_t k,
+                                    int64_t ldx, int64_t ldb, int64_t ldc, int trans_b, int epilogue, void* aux,
+                                    int64_t ld_aux, int ab_dtype, int c_dtype) {
+  if (int rc = injected_fault("gemm")) return rc;
+  if (m < 0 || n < 0 || k < 0) return fail(FERRITE_BAD_SHAPE, "gemm_rmsnorm: negative size");
+  if (m == 0) return FERRITE_OK;
+  if (m > kSkinnyM) return fail(FERRITE_BAD_SHAPE, "gemm_rmsnorm: at most %d rows, got %lld", kSkinnyM, (long long)m);
+  if (n < 1 || k < 8 || k % 8) return fail(FERRITE_BAD_SHAPE, "gemm_rmsnorm: needs n >= 1 and k a positive multiple of 8");
+  if (ab_dtype != FERRITE_BF16 && ab_dtype != FERRITE_F16)
+    return fail(FERRITE_UNSUPPORTED_DTYPE, "gemm_rmsnorm: operands must be bf16 or f16");
+  if (c_dtype != ab_dtype && c_dtype != FERRITE_F32)
+    return fail(FERRITE_UNSUPPORTED_DTYPE, "gemm_rmsnorm: output dtype must be the operands' or f32");
+  if (epilogue != kEpiNone && epilogue != kEpiGelu) return fail(FERRITE_BAD_SHAPE, "gemm_rmsnorm: unknown epilogue %d", epilogue);
+  if (epilogue == kEpiGelu && (trans_b || ab_dtype != FERRITE_BF16 || c_dtype != FERRITE_BF16 || !aux || ld_aux < n))
+    return fail(FERRITE_BAD_SHAPE, "gemm_rmsnorm: the GELU epilogue needs bf16, B stored [K][N] and aux [m][>= n]");
+  if (!x || !w_norm || !b || !c) return fail(FERRITE_BAD_SHAPE, "gemm_rmsnorm: null pointer");
+  if (!r && h_out) return fail(FERRITE_BAD_SHAPE, "gemm_rmsnorm: h_out needs a residual");
+  if (ldx < k || ldx % 8 || ldc < n) return fail(FERRITE_BAD_SHAPE, "gemm_rmsnorm: leading dimension too small or not a multiple of 8");
+  auto misaligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) != 0; };
+  if (misaligned(x) || (r && misaligned(r)) || (h_out && misaligned(h_out)) || misaligned(w_norm))
+    return fail(FERRITE_BAD_ALIGNMENT, "gemm_rmsnorm: x, r, h_out and w_norm must be 16-byte aligned");
+  if (!(eps >= 0.f) || eps > 1.f) return fail(FERRITE_BAD_SHAPE, "gemm_rmsnorm: eps outside [0, 1]");
+  if (h_out) {  // h_out is written while every CTA still reads x and r
+    const uintptr_t span = (uintptr_t)(((m - 1) * ldx + k) * 2);
+    auto overlaps = [&](const void* p) {
+      const uintptr_t a0 = reinterpret_cast<uintptr_t>(p), b0 = reinterpret_cast<uintptr_t>(h_out);
+      return a0 < b0 + span && b0 < a0 + span;
+    };
+    if (overlaps(x) || overlaps(r)) return fail(FERRITE_BAD_SHAPE, "gemm_rmsnorm: h_out overlaps x or r");
+  }
+  if (!skinny_kn_ok(b, m, n, k, ldb, 0, trans_b))
+    return fail(FERRITE_UNSUPPORTED_DTYPE, "gemm_rmsnorm: B must be 16-byte aligned with ldb a multiple of 8 (and n a "
+                                           "multiple of 8 when stored [K][N]), K within shared memory");
+  cudaStream_t s = (cudaStream_t)stream;
+  const KnNorm nrm{r, w_norm, h_out, eps};
+  if (epilogue == kEpiGelu)
+    return launch_skinny_kn<__nv_bfloat16, __nv_bfloat16, kEpiGelu, true>(s, x, b, c, m, n, k, ldx, ldb, ldc, 0, aux, ld_aux, nrm);
+  if (ab_dtype == FERRITE_BF16) {
+    if (c_dtype == FERRITE_F32)
+      return launch_skinny_kn<__nv_bfloat16, float, kEpiNone, true>(s, x, b, c, m, n, k, ldx, ldb, ldc, trans_b, nullptr, 0, nrm);
+    return launch_skinny_kn<__nv_bfloat16, __nv_bfloat16, kEpiNone, true>(s, x, b, c, m, n, k, ldx, ldb, ldc, trans_b, nullptr, 0, nrm);
+  }
+  if (c_dtype == FERRITE_F32)
+    return launch_skinny_kn<__half, float, kEpiNone, true>(s, x, b, c, m, n, k, ldx, ldb, ldc, trans_b, nullptr, 0, nrm);
+  return launch_skinny_kn<__half, __half, kEpiNone, true>(s, x, b, c, m, n, k, ldx, ldb, ldc, trans_b, nullptr, 0, nrm);
 }
 
 extern "C" int ferrite_gemm_epilogue(void* stream, const void* a, const void* b, void* c,

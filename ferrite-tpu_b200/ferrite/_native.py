@@ -86,6 +86,8 @@ SIGNATURES: dict[str, tuple] = {
     "ferrite_rmsnorm_bwd_noalloc": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f32, _i32, _i32]),
     "ferrite_gemm": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _i32, _i32]),
     "ferrite_gemm_epilogue": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _i32, _vp, _i64]),
+    "ferrite_gemm_rmsnorm": (_i32, [_vp, _vp, _vp, _vp, _f32, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _vp,
+                                    _i64, _i32, _i32]),
     "ferrite_gemm_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i64, _i32, _i32, _i32]),
     "ferrite_gemm_ws": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _i32, _i32, _vp, _sz]),
     "ferrite_attn_fwd": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _i32, _i32, _i32]),

@@ -68,6 +68,60 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, trans_a: bool = False, trans_b: bo
     return out
 
 
+@nat.on_tensor_device
+def rmsnorm_matmul(x: torch.Tensor, w_norm: torch.Tensor, b: torch.Tensor, *, residual: torch.Tensor | None = None, eps: float = 1e-6,
+                   trans_b: bool = False, gelu: bool = False, out_dtype=None):
+    """Residual-add + RMSNorm folded in front of a product with at most 16 rows -- the
+    decode step's norm feeding its next linear -- in one launch (``ferrite_gemm_rmsnorm``).
+
+    ``h = x + residual`` (``x`` alone without one), ``y = rmsnorm(h) * w_norm`` (statistics
+    from the unrounded f32 sum, as ``rmsnorm`` with a residual), ``c = y @ op(b)`` with an f32
+    accumulator, ``op`` transposing ``b`` when ``trans_b``.  Returns ``(h, c)``, or with
+    ``gelu`` (the MLP up-projection) ``(h, u, gelu_tanh(u))``; ``h`` is ``x`` itself when no
+    residual is given.  Inference only (no autograd).  Shapes the fused kernel does not take
+    (more rows, misaligned or ragged operands) run the norm and the product as two launches.
+    """
+    from ferrite.kernels.rmsnorm import rmsnorm
+
+    m, k = x.shape
+    kb, n = (b.shape[1], b.shape[0]) if trans_b else (b.shape[0], b.shape[1])
+    if kb != k:
+        raise ValueError(f"inner dimensions differ: {k} vs {kb}")
+    if residual is not None and (residual.shape != x.shape or residual.dtype != x.dtype):
+        raise ValueError("residual must match x in shape and dtype")
+    out_dtype = out_dtype or x.dtype
+    w32 = w_norm.float().contiguous()
+    fits = (x.dtype in (torch.bfloat16, torch.float16) and b.dtype == x.dtype and 1 <= m <= 16 and k % 8 == 0
+            and out_dtype in (x.dtype, torch.float32) and (not gelu or (x.dtype == torch.bfloat16 and not trans_b and out_dtype == x.dtype)))
+    if fits:
+        x = x.contiguous()
+        residual = residual.contiguous() if residual is not None else None
+        bb = b if b.stride(1) == 1 else b.contiguous()
+        fits = all(t.data_ptr() % 16 == 0 for t in (x, bb, w32) + ((residual,) if residual is not None else ())) and bb.stride(0) % 8 == 0
+        fits = fits and (trans_b or n % 8 == 0)
+    if not fits:
+        if residual is None:
+            h, y = x, rmsnorm(x, w_norm, eps=eps)
+        else:
+            h, y = rmsnorm(x, w_norm, residual=residual, eps=eps)
+        if gelu:
+            u = gemm(y, b, trans_b=trans_b, out_dtype=out_dtype)
+            return h, u, torch.nn.functional.gelu(u.float(), approximate="tanh").to(u.dtype)
+        return h, gemm(y, b, trans_b=trans_b, out_dtype=out_dtype)
+    h = torch.empty_like(x) if residual is not None else x
+    c = torch.empty((m, n), dtype=out_dtype, device=x.device)
+    act = torch.empty_like(c) if gelu else None
+    nat.check(
+        nat.lib().ferrite_gemm_rmsnorm(
+            nat.stream_ptr(x.device), x.data_ptr(), nat.ptr(residual), w32.data_ptr(), float(eps),
+            h.data_ptr() if residual is not None else None, bb.data_ptr(), c.data_ptr(), m, n, k, x.stride(0), bb.stride(0),
+            c.stride(0), int(trans_b), 1 if gelu else 0, nat.ptr(act), act.stride(0) if gelu else 0,
+            nat.dtype_code(x.dtype), nat.dtype_code(out_dtype),
+        )
+    )
+    return (h, c, act) if gelu else (h, c)
+
+
 class _Matmul(torch.autograd.Function):
     """custom_vjp of ``_matmul_vjp`` (matmul.py:89-107)."""
 

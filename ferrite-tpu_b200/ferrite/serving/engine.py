@@ -19,7 +19,8 @@ default), its attention and cache write run as one kernel (``decode_attention``)
 residual-add + RMSNorms on the fused norm kernel, and for 16-bit models its linears
 (one row per sequence) and the tied LM head on the skinny GEMM kernels (B stored
 [K][N] for the layer matrices, the MLP's GELU fused into the up-projection; [N][K]
-for the embedding); f32 models keep the plain linears.  ``"xla"`` gives the reference's plain path throughout.  ``jax.export`` of
+for the embedding), each norm folded into the product it feeds; f32 models keep the
+plain linears.  ``"xla"`` gives the reference's plain path throughout.  ``jax.export`` of
 the decode step has no counterpart here.
 """
 
@@ -34,6 +35,7 @@ import torch
 import torch.nn.functional as F
 
 from ferrite.kernels.decode_attention import decode_attention
+from ferrite.kernels.matmul import rmsnorm_matmul
 from ferrite.model.gpt import GPTConfig, _linear, _lm_head, _mlp, _norm, block
 
 
@@ -108,18 +110,32 @@ def decode_step(params, token, pos, k_cache, v_cache, cfg: GPTConfig):
     ``cfg.attention == "pallas"`` runs the cache write and the cache attention as one
     kernel (:func:`ferrite.kernels.decode_attention.decode_attention`); otherwise
     they run as the reference writes them (``_write_cache`` + ``_cache_attention``).
+    With the norms and linears both on the kernels (16-bit, at most 16 sequences) each
+    residual-add + RMSNorm is folded into the product it feeds
+    (:func:`ferrite.kernels.matmul.rmsnorm_matmul`): ln1 into the QKV projection, ln2
+    into the MLP up-projection (with its GELU), ln_f into the tied head -- five launches
+    a layer instead of seven, same rounding points.
     """
     b = token.shape[0]
     h = (params["tok_emb"][token] + params["pos_emb"][pos]).to(cfg.dtype)  # [B, D]
     scale = 1.0 / np.sqrt(cfg.head_dim)
     pending = None
     ar = torch.arange(b, device=token.device)
+    fused = cfg.norm == "pallas" and cfg.linear == "pallas" and cfg.dtype in (torch.bfloat16, torch.float16) and b <= 16
     for i, layer in enumerate(params["layers"]):
-        if pending is None:
-            y = _norm(h, layer["ln1"], None, cfg)
+        if fused:
+            w = layer["wqkv"].to(cfg.dtype)
+            if pending is None:
+                _, qkv = rmsnorm_matmul(h, layer["ln1"], w, eps=cfg.eps)
+            else:
+                h, qkv = rmsnorm_matmul(pending, layer["ln1"], w, residual=h, eps=cfg.eps)
         else:
-            h, y = _norm(pending, layer["ln1"], h, cfg)
-        qkv = _linear(y, layer["wqkv"], cfg).reshape(b, 3, cfg.n_head, cfg.head_dim)
+            if pending is None:
+                y = _norm(h, layer["ln1"], None, cfg)
+            else:
+                h, y = _norm(pending, layer["ln1"], h, cfg)
+            qkv = _linear(y, layer["wqkv"], cfg)
+        qkv = qkv.reshape(b, 3, cfg.n_head, cfg.head_dim)
         q, k, v = qkv[:, 0], qkv[:, 1], qkv[:, 2]
         if cfg.attention == "pallas":
             a = decode_attention(q, k_cache[i], v_cache[i], pos, scale=scale, k_new=k.to(k_cache.dtype), v_new=v.to(v_cache.dtype))
@@ -129,12 +145,21 @@ def decode_step(params, token, pos, k_cache, v_cache, cfg: GPTConfig):
             a = _cache_attention(q, k_cache[i], v_cache[i], pos, scale)
         a = a.reshape(b, cfg.d_model)
         a = _linear(a, layer["wo"], cfg)
-        h, y2 = _norm(a, layer["ln2"], h, cfg)
-        pending = _mlp(y2[:, None], layer["w1"], layer["w2"], cfg)[:, 0]
-    _, y = _norm(pending, params["ln_f"], h, cfg)
+        if fused:
+            h, _, act = rmsnorm_matmul(a, layer["ln2"], layer["w1"].to(cfg.dtype), residual=h, eps=cfg.eps, gelu=True)
+            pending = _linear(act, layer["w2"], cfg)
+        else:
+            h, y2 = _norm(a, layer["ln2"], h, cfg)
+            pending = _mlp(y2[:, None], layer["w1"], layer["w2"], cfg)[:, 0]
     # tied head in cfg.dtype with f32 accumulation (engine.py:130): exact 16-bit products
     # summed in f32 on either path, f32 logits
-    return _lm_head(y, params.get("lm_head", params["tok_emb"]), cfg)
+    head = params.get("lm_head", params["tok_emb"])
+    if fused:
+        _, logits = rmsnorm_matmul(pending, params["ln_f"], head.to(cfg.dtype), residual=h, eps=cfg.eps, trans_b=True,
+                                   out_dtype=torch.float32)
+        return logits
+    _, y = _norm(pending, params["ln_f"], h, cfg)
+    return _lm_head(y, head, cfg)
 
 
 class Engine:

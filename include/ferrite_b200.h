@@ -155,6 +155,22 @@ FERRITE_API int ferrite_gemm_epilogue(void* stream, const void* a, const void* b
                           int64_t ldc, int trans_a, int trans_b, int epilogue,
                           void* aux, int64_t ld_aux);
 
+/* Residual-add + RMSNorm folded in front of a skinny product, one launch (the
+ * decode step's norm feeding its next linear; no reference kernel counterpart: the
+ * reference runs ferrite_rmsnorm -- rmsnorm.py:52-56, add_rmsnorm -- then a matmul,
+ * engine.py:107-131 / gpt.py:131-143):
+ *   h = x + r (f32; x alone when r is null), y = round(h * rsqrt(mean(h^2) + eps) * w),
+ *   c = y op(B) with an f32 accumulator (op as ferrite_gemm's trans_b), and h_out =
+ *   round(h) when given (it needs r, and must not overlap x or r).
+ * x, r, h_out: [m][k] with row stride ldx (a multiple of 8), 16-byte aligned; w_norm: f32
+ * [k], 16-byte aligned; m <= 16, k a multiple of 8; ab_dtype bf16 or f16, c_dtype the
+ * same or f32.  epilogue 1 (GELU, bf16, B stored [K][N]): c = u rounded, aux =
+ * gelu_tanh(u) rounded, as ferrite_gemm_epilogue. */
+FERRITE_API int ferrite_gemm_rmsnorm(void* stream, const void* x, const void* r, const float* w_norm, float eps,
+                          void* h_out, const void* b, void* c, int64_t m, int64_t n, int64_t k,
+                          int64_t ldx, int64_t ldb, int64_t ldc, int trans_b, int epilogue, void* aux,
+                          int64_t ld_aux, int ab_dtype, int c_dtype);
+
 /* Bytes of f32 scratch ferrite_gemm_ws can use for a split-K launch of this
  * shape on the current device (0: the shape gets no split).  Splitting K helps
  * when the output has fewer tiles than the GPU has SMs -- the weight gradients

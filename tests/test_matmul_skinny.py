@@ -158,3 +158,81 @@ def test_skinny_kn_gelu_epilogue(m):
     ga = torch.nn.functional.gelu(u.float(), approximate="tanh")
     torch.testing.assert_close(a.float(), ga, rtol=2**-7, atol=1e-3)
     assert torch.equal(u, _gemm_kn(x, w1, torch.bfloat16))  # same kernel, same sums as the plain product
+
+
+# ---------------------------------------------------------------------------
+# residual-add + RMSNorm folded in front of the skinny product (the decode step's norms)
+# ---------------------------------------------------------------------------
+
+def _norm_case(m, k, seed, residual=True):
+    rng = np.random.default_rng(seed)
+    x = normal(rng, (m, k), BF16)
+    r = normal(rng, (m, k), BF16) if residual else None
+    w = (1.0 + 0.1 * rng.standard_normal(k)).astype(np.float32)
+    return x, r, w
+
+
+@pytest.mark.parametrize("m,k,n", [(8, 1024, 3072), (1, 256, 768), (16, 1024, 1024), (5, 512, 200)])
+def test_gemm_rmsnorm_against_the_oracle(m, k, n):
+    """h = round(x + r) bitwise equal to the oracle's add_rmsnorm (rmsnorm.py:52-56 of the
+    reference); c = rmsnorm(h) w @ W within the bf16 tolerance (y may differ from the norm
+    kernel's by one rounding: another order of the same f32 statistics)."""
+    from ferrite.kernels.matmul import rmsnorm_matmul
+    from oracle import rmsnorm as orn
+
+    x, r, w = _norm_case(m, k, 30 + m)
+    wm = normal(np.random.default_rng(31), (k, n), BF16, std=k ** -0.5)
+    h, c = rmsnorm_matmul(to_torch(x), to_torch(w), to_torch(wm), residual=to_torch(r), eps=1e-6)
+    h_ref, y_ref = orn.add_rmsnorm_fwd(x, r, w, eps=1e-6)
+    np.testing.assert_array_equal(to_numpy(h), h_ref)
+    ref = om.matmul_reference(y_ref, wm, out_dtype=np.float32)
+    np.testing.assert_allclose(to_numpy(c).astype(np.float32), ref, rtol=2**-6, atol=2e-2)
+
+
+def test_gemm_rmsnorm_gelu_head_and_no_residual():
+    """The three decode forms: ln2 into the up-projection with its GELU (u and gelu(u)),
+    ln_f into the tied head (B stored [N][K], f32 logits), and the first layer's ln1
+    without a residual (h is x itself)."""
+    from ferrite.kernels.matmul import rmsnorm_matmul
+    from oracle import rmsnorm as orn
+
+    x, r, w = _norm_case(8, 1024, 40)
+    w1 = normal(np.random.default_rng(41), (1024, 4096), BF16, std=1 / 32)
+    h, u, a = rmsnorm_matmul(to_torch(x), to_torch(w), to_torch(w1), residual=to_torch(r), eps=1e-6, gelu=True)
+    _, y_ref = orn.add_rmsnorm_fwd(x, r, w, eps=1e-6)
+    u_ref = om.matmul_reference(y_ref, w1, out_dtype=np.float32)
+    np.testing.assert_allclose(to_numpy(u).astype(np.float32), u_ref, rtol=2**-6, atol=2e-2)
+    g = torch.nn.functional.gelu(u.float(), approximate="tanh")
+    torch.testing.assert_close(a.float(), g, rtol=2**-7, atol=1e-3)
+
+    e = normal(np.random.default_rng(42), (5000, 1024), BF16, std=0.02)
+    _, logits = rmsnorm_matmul(to_torch(x), to_torch(w), to_torch(e), residual=to_torch(r), eps=1e-6, trans_b=True,
+                               out_dtype=torch.float32)
+    assert logits.dtype == torch.float32
+    np.testing.assert_allclose(to_numpy(logits), om.matmul_reference(y_ref, np.ascontiguousarray(e.T), out_dtype=np.float32),
+                               rtol=2**-6, atol=5e-3)
+
+    xt = to_torch(x)
+    h0, c0 = rmsnorm_matmul(xt, to_torch(w), to_torch(w1), eps=1e-6)
+    assert h0 is xt
+    y0 = orn.rmsnorm_fwd(x, w, eps=1e-6)
+    np.testing.assert_allclose(to_numpy(c0).astype(np.float32), om.matmul_reference(y0, w1, out_dtype=np.float32), rtol=2**-6, atol=2e-2)
+
+
+def test_gemm_rmsnorm_fallback_and_errors():
+    """More than 16 rows take the norm kernel and the product as two launches (same
+    results within tolerance); the C entry rejects h_out overlapping its inputs."""
+    from ferrite.kernels.matmul import rmsnorm_matmul
+
+    x, r, w = _norm_case(20, 512, 50)
+    wm = to_torch(normal(np.random.default_rng(51), (512, 256), BF16, std=512 ** -0.5))
+    h, c = rmsnorm_matmul(to_torch(x), to_torch(w), wm, residual=to_torch(r), eps=1e-6)
+    h8, c8 = rmsnorm_matmul(to_torch(x[:8]), to_torch(w), wm, residual=to_torch(r[:8]), eps=1e-6)
+    assert torch.equal(h[:8], h8)
+    torch.testing.assert_close(c[:8].float(), c8.float(), rtol=2**-6, atol=2e-2)
+
+    xt, rt, wt = to_torch(x[:8]), to_torch(r[:8]), to_torch(w)
+    out = torch.empty(8, 256, dtype=torch.bfloat16, device="cuda")
+    rc = nat.lib().ferrite_gemm_rmsnorm(nat.stream_ptr(), xt.data_ptr(), rt.data_ptr(), wt.data_ptr(), 1e-6, rt.data_ptr(),
+                                        wm.data_ptr(), out.data_ptr(), 8, 256, 512, 512, 256, 256, 0, 0, None, 0, nat.BF16, nat.BF16)
+    assert rc == nat.BAD_SHAPE
