@@ -43,7 +43,7 @@ constexpr int kStages = 3;
 // K/V staging ring per CTA: kStages batches x kUnroll rows x (K, V) x 16 bytes per thread.
 constexpr int kRingBytes = kStages * kUnroll * 2 * kThreads * 16;
 constexpr int kMaxCluster = 8;
-constexpr int kPrefetchBytes = 16 * 1024;  // per CTA, of K and of V, ahead of the launch wait
+constexpr int kPrefetchBytes = 32 * 1024;  // per CTA, of K and of V, ahead of the launch wait
 constexpr float kLog2e = 1.4426950408889634f;
 
 // 16-byte global -> shared asynchronous copy (cached in L2 only), and its group
